@@ -1,0 +1,291 @@
+"""ctypes bindings for the CPU oracle (TEST INFRASTRUCTURE ONLY).
+
+The oracle is a plain-C restatement of the reference's CPU arithmetic
+(``rnn_oracle.c``).  Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU
+baseline legs of ``bench.py`` may import this module; the product package
+``rustnn_b200`` never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "librnn_oracle.so")
+
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_u32p = np.ctypeslib.ndpointer(dtype=np.uint32, flags="C_CONTIGUOUS")
+_i64p = np.ctypeslib.ndpointer(dtype=np.int64, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+
+
+def build(force: bool = False) -> str:
+    """Compile the oracle with the recipe in ``oracle/Makefile``."""
+    if force or not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < max(
+        os.path.getmtime(os.path.join(HERE, f)) for f in ("rnn_oracle.c", "rnn_oracle.h")
+    ):
+        subprocess.check_call(["make", "-s", "-C", HERE])
+    return LIB_PATH
+
+
+class _Rng(C.Structure):
+    _fields_ = [("s", C.c_uint64 * 4)]
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is not None:
+        return _lib
+    build()
+    L = C.CDLL(LIB_PATH)
+    V, I, F, Z, U64 = None, C.c_int, C.c_float, C.c_size_t, C.c_uint64
+    P = C.c_void_p
+    sig = {
+        "orc_rng_new": (V, [C.POINTER(_Rng), U64]),
+        "orc_rng_next_u64": (U64, [C.POINTER(_Rng)]),
+        "orc_rng_uniform": (F, [C.POINTER(_Rng)]),
+        "orc_rng_normal": (F, [C.POINTER(_Rng)]),
+        "orc_rng_below": (U64, [C.POINTER(_Rng), U64]),
+        "orc_rand_vec": (V, [_f32p, Z, C.POINTER(_Rng)]),
+        "orc_matmul": (V, [I, I, I, _f32p, I, _f32p, I, _f32p, I]),
+        "orc_matmul_dw": (V, [I, I, I, _f32p, _f32p, _f32p]),
+        "orc_naive_matmul": (V, [I, I, I, _f32p, I, _f32p, I, _f32p]),
+        "orc_conv2d_fwd": (V, [_f32p, I, I, I, I, _f32p, I, I, I, I, _f32p]),
+        "orc_conv2d_dgrad": (V, [_f32p, I, I, I, I, _f32p, I, I, I, I, _f32p]),
+        "orc_conv2d_wgrad": (V, [_f32p, _f32p, I, I, I, I, I, I, I, I, _f32p]),
+        "orc_bn_fwd_train": (V, [_f32p, I, I, I, _f32p, _f32p, _f32p, _f32p, F, F, I, _f32p, _f32p]),
+        "orc_bn_fwd_eval": (V, [_f32p, I, I, I, _f32p, _f32p, _f32p, _f32p, F, I]),
+        "orc_bn_bwd": (V, [_f32p, _f32p, I, I, I, _f32p, _f32p, _f32p, _f32p, _f32p]),
+        "orc_relu_back": (V, [_f32p, _f32p, Z]),
+        "orc_add": (V, [_f32p, _f32p, Z]),
+        "orc_add_relu": (V, [_f32p, _f32p, Z]),
+        "orc_gap_fwd": (V, [_f32p, I, I, _f32p]),
+        "orc_gap_bwd": (V, [_f32p, I, I, _f32p]),
+        "orc_fc_fwd": (V, [_f32p, I, I, I, _f32p, _f32p, _f32p]),
+        "orc_fc_bwd": (V, [_f32p, _f32p, I, I, I, _f32p, _f32p, _f32p, _f32p]),
+        "orc_softmax_ce": (F, [_f32p, _u32p, I, I, F, _f32p, C.POINTER(C.c_int)]),
+        "orc_sgd_step": (V, [_f32p, _f32p, _f32p, Z, F, F, F, I]),
+        "orc_resnet_new": (P, [I, I, I, U64]),
+        "orc_resnet_free": (V, [P]),
+        "orc_resnet_num_params": (Z, [P]),
+        "orc_resnet_num_tensors": (I, [P]),
+        "orc_resnet_get_params": (V, [P, _f32p]),
+        "orc_resnet_set_params": (V, [P, _f32p]),
+        "orc_resnet_get_grads": (V, [P, _f32p]),
+        "orc_resnet_get_moments": (V, [P, _f32p]),
+        "orc_resnet_zero_grads": (V, [P]),
+        "orc_resnet_num_buffers": (Z, [P]),
+        "orc_resnet_get_buffers": (V, [P, _f32p]),
+        "orc_resnet_param_info": (V, [P, _i64p, _i32p]),
+        "orc_resnet_forward": (V, [P, _f32p, I, I, I, I, _f32p]),
+        "orc_resnet_backward": (V, [P, _f32p]),
+        "orc_resnet_step": (V, [P, F, F, F]),
+        "orc_resnet_train_step": (F, [P, _f32p, _u32p, I, F, F, F, F, C.POINTER(C.c_int)]),
+        "orc_resnet_flops": (U64, [P, I, I]),
+        "orc_set_threads": (V, [I]),
+        "orc_get_threads": (I, []),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+# ---------------------------------------------------------------- rng.rs
+
+
+class Rng:
+    """rng.rs Rng: SplitMix64-seeded xoshiro256++ (bit exact)."""
+
+    def __init__(self, seed: int):
+        self._s = _Rng()
+        lib().orc_rng_new(C.byref(self._s), C.c_uint64(seed & (2**64 - 1)))
+
+    def next_u64(self) -> int:
+        return lib().orc_rng_next_u64(C.byref(self._s))
+
+    def uniform(self) -> float:
+        return lib().orc_rng_uniform(C.byref(self._s))
+
+    def normal(self) -> float:
+        return lib().orc_rng_normal(C.byref(self._s))
+
+    def below(self, n: int) -> int:
+        return lib().orc_rng_below(C.byref(self._s), n)
+
+    def rand_vec(self, n: int) -> np.ndarray:
+        out = np.empty(n, np.float32)
+        lib().orc_rand_vec(out, n, C.byref(self._s))
+        return out
+
+
+# ---------------------------------------------------------------- gemm.rs
+
+
+def matmul(m, n, k, a, at, b, bt, c=None, acc=False):
+    if c is None:
+        c = np.zeros(m * n, np.float32)
+    lib().orc_matmul(m, n, k, _f32(a).ravel(), int(at), _f32(b).ravel(), int(bt), c, int(acc))
+    return c
+
+
+def matmul_dw(m, n, k, a, b, c):
+    lib().orc_matmul_dw(m, n, k, _f32(a).ravel(), _f32(b).ravel(), c)
+    return c
+
+
+def naive_matmul(m, n, k, a, at, b, bt):
+    c = np.zeros(m * n, np.float32)
+    lib().orc_naive_matmul(m, n, k, _f32(a).ravel(), int(at), _f32(b).ravel(), int(bt), c)
+    return c
+
+
+# ---------------------------------------------------------------- conv
+
+
+def out_dim(h, k, stride, pad):
+    return (h + 2 * pad - k) // stride + 1
+
+
+def conv2d_fwd(x, n, cin, h, w, wt, cout, k, stride, pad):
+    oh, ow = out_dim(h, k, stride, pad), out_dim(w, k, stride, pad)
+    y = np.empty(n * cout * oh * ow, np.float32)
+    lib().orc_conv2d_fwd(_f32(x).ravel(), n, cin, h, w, _f32(wt).ravel(), cout, k, stride, pad, y)
+    return y
+
+
+def conv2d_dgrad(dy, n, cin, h, w, wt, cout, k, stride, pad):
+    dx = np.empty(n * cin * h * w, np.float32)
+    lib().orc_conv2d_dgrad(_f32(dy).ravel(), n, cin, h, w, _f32(wt).ravel(), cout, k, stride, pad, dx)
+    return dx
+
+
+def conv2d_wgrad(x, dy, n, cin, h, w, cout, k, stride, pad, dw=None):
+    if dw is None:
+        dw = np.zeros(cout * cin * k * k, np.float32)
+    lib().orc_conv2d_wgrad(_f32(x).ravel(), _f32(dy).ravel(), n, cin, h, w, cout, k, stride, pad, dw)
+    return dw
+
+
+# ---------------------------------------------------------------- BN / glue
+
+
+def bn_fwd_train(y, n, c, hw, gamma, beta, rmean, rvar, relu, mom=0.1, eps=1e-5):
+    """In place on a copy of y; returns (out, xhat, invstd); rmean/rvar updated."""
+    out = _f32(y).ravel().copy()
+    xhat = np.empty_like(out)
+    invstd = np.empty(c, np.float32)
+    lib().orc_bn_fwd_train(out, n, c, hw, _f32(gamma), _f32(beta), rmean, rvar, mom, eps, int(relu), xhat, invstd)
+    return out, xhat, invstd
+
+
+def bn_bwd(dy, xhat, n, c, hw, gamma, invstd, dgamma, dbeta):
+    dx = np.empty(n * c * hw, np.float32)
+    lib().orc_bn_bwd(_f32(dy).ravel(), _f32(xhat).ravel(), n, c, hw, _f32(gamma), _f32(invstd), dx, dgamma, dbeta)
+    return dx
+
+
+def softmax_ce(logits, labels, nclass, smooth):
+    logits = _f32(logits).ravel()
+    labels = np.ascontiguousarray(labels, dtype=np.uint32)
+    d = np.empty_like(logits)
+    corr = C.c_int(0)
+    loss = lib().orc_softmax_ce(logits, labels, len(labels), nclass, smooth, d, C.byref(corr))
+    return loss, d, corr.value
+
+
+# ---------------------------------------------------------------- model.rs
+
+
+class ResNet:
+    """model.rs ResNet restated in C."""
+
+    def __init__(self, depth_n, width, nclass, seed):
+        self.h = lib().orc_resnet_new(depth_n, width, nclass, seed)
+        self.nclass = nclass
+        self.width = width
+        self.depth_n = depth_n
+
+    def __del__(self):
+        if getattr(self, "h", None) and _lib is not None:
+            _lib.orc_resnet_free(self.h)
+            self.h = None
+
+    def num_params(self):
+        return lib().orc_resnet_num_params(self.h)
+
+    def num_tensors(self):
+        return lib().orc_resnet_num_tensors(self.h)
+
+    def param_info(self):
+        k = self.num_tensors()
+        sizes = np.zeros(k, np.int64)
+        decay = np.zeros(k, np.int32)
+        lib().orc_resnet_param_info(self.h, sizes, decay)
+        return sizes, decay
+
+    def params(self):
+        out = np.empty(self.num_params(), np.float32)
+        lib().orc_resnet_get_params(self.h, out)
+        return out
+
+    def set_params(self, v):
+        lib().orc_resnet_set_params(self.h, _f32(v).ravel())
+
+    def grads(self):
+        out = np.empty(self.num_params(), np.float32)
+        lib().orc_resnet_get_grads(self.h, out)
+        return out
+
+    def moments(self):
+        out = np.empty(self.num_params(), np.float32)
+        lib().orc_resnet_get_moments(self.h, out)
+        return out
+
+    def buffers(self):
+        out = np.empty(lib().orc_resnet_num_buffers(self.h), np.float32)
+        lib().orc_resnet_get_buffers(self.h, out)
+        return out
+
+    def zero_grads(self):
+        lib().orc_resnet_zero_grads(self.h)
+
+    def forward(self, x, n, hw=32, train=True):
+        logits = np.empty(n * self.nclass, np.float32)
+        lib().orc_resnet_forward(self.h, _f32(x).ravel(), n, hw, hw, int(train), logits)
+        return logits
+
+    def backward(self, dlogits):
+        lib().orc_resnet_backward(self.h, _f32(dlogits).ravel())
+
+    def step(self, lr, mom, wd):
+        lib().orc_resnet_step(self.h, lr, mom, wd)
+
+    def train_step(self, x, labels, smooth=0.1, lr=0.2, mom=0.9, wd=5e-4):
+        labels = np.ascontiguousarray(labels, dtype=np.uint32)
+        corr = C.c_int(0)
+        loss = lib().orc_resnet_train_step(self.h, _f32(x).ravel(), labels, len(labels), smooth, lr, mom, wd, C.byref(corr))
+        return loss, corr.value
+
+    def flops(self, h=32, w=32):
+        return lib().orc_resnet_flops(self.h, h, w)
+
+
+def set_threads(n: int):
+    lib().orc_set_threads(n)
+
+
+def get_threads() -> int:
+    return lib().orc_get_threads()

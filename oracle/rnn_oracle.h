@@ -1,0 +1,135 @@
+/*
+ * CPU oracle for the rustnn dense-contraction path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is a plain-C restatement of the
+ * reference's own CPU arithmetic (lsiddd/rustnn, Rust).  It exists to check
+ * the CUDA library and to time a CPU baseline.  Only tests/, the smoke check
+ * in __graft_entry__.py and the cpu_baseline / --impl reference legs of
+ * bench.py may load it.  The product library (rustnn_b200) never calls it.
+ *
+ * Every function names the reference file:line it restates.  All arithmetic
+ * is f32 except where the reference itself accumulates in f64 (BatchNorm and
+ * LayerNorm statistics, the global-norm clip).
+ *
+ * Pinning: the reference is Rust and no Rust toolchain exists on this
+ * machine, so it cannot be run to produce golden tensors.  The reference ships
+ * no stored tensors either.  The oracle is pinned to what the reference's own
+ * tests hold: the naive-GEMM check (check.rs:105-161), the directional
+ * derivative gradchecks (check.rs:19-40, 503-770) and the published parameter
+ * and MAC counts (README.md:116-117).  tests/test_oracle.py runs all of them.
+ */
+#ifndef RNN_ORACLE_H
+#define RNN_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- rng.rs ------------------------------------------------------------ */
+typedef struct { uint64_t s[4]; } orc_rng;
+void     orc_rng_new(orc_rng *r, uint64_t seed);          /* rng.rs:8-20  */
+uint64_t orc_rng_next_u64(orc_rng *r);                     /* rng.rs:23-36 */
+float    orc_rng_uniform(orc_rng *r);                      /* rng.rs:50-52 */
+float    orc_rng_normal(orc_rng *r);                       /* rng.rs:55-59 */
+uint64_t orc_rng_below(orc_rng *r, uint64_t n);            /* rng.rs:45-47 */
+void     orc_rand_vec(float *out, size_t n, orc_rng *r);   /* rng.rs:70-72 */
+
+/* ---- gemm.rs ----------------------------------------------------------- */
+/* C[m x n] (+)= op(A) op(B); at: A is [k x m]; bt: B is [n x k]. gemm.rs:434 */
+void orc_matmul(int m, int n, int k, const float *a, int at, const float *b,
+                int bt, float *c, int acc);
+/* C[m x n] += A^T B, A [k x m], B [k x n].  gemm.rs:555-598 */
+void orc_matmul_dw(int m, int n, int k, const float *a, const float *b, float *c);
+/* naive triple loop, check.rs:105-122 */
+void orc_naive_matmul(int m, int n, int k, const float *a, int at,
+                      const float *b, int bt, float *c);
+
+/* ---- conv.rs / nn.rs Conv2d -------------------------------------------- */
+/* NCHW x [n,cin,h,w]; W [cout, cin*k*k]; y [n,cout,oh,ow].  nn.rs:166-185 */
+void orc_conv2d_fwd(const float *x, int n, int cin, int h, int w,
+                    const float *wt, int cout, int k, int stride, int pad,
+                    float *y);
+/* dX = col2im(W^T dY), overwrites dx.  nn.rs:230-250, conv.rs:207-246 */
+void orc_conv2d_dgrad(const float *dy, int n, int cin, int h, int w,
+                      const float *wt, int cout, int k, int stride, int pad,
+                      float *dx);
+/* dW += dY im2col(X)^T.  nn.rs:193-227, conv.rs:283-322 */
+void orc_conv2d_wgrad(const float *x, const float *dy, int n, int cin, int h,
+                      int w, int cout, int k, int stride, int pad, float *dw);
+
+/* ---- nn.rs BatchNorm2d -------------------------------------------------- */
+/* Train-mode forward in place on y [n,c,hw] (nn.rs:326-354).  Writes xhat,
+ * invstd; updates running mean/var (mom, unbiased var). */
+void orc_bn_fwd_train(float *y, int n, int c, int hw, const float *gamma,
+                      const float *beta, float *rmean, float *rvar, float mom,
+                      float eps, int relu, float *xhat, float *invstd);
+/* Eval-mode forward in place (nn.rs:358-369). */
+void orc_bn_fwd_eval(float *y, int n, int c, int hw, const float *gamma,
+                     const float *beta, const float *rmean, const float *rvar,
+                     float eps, int relu);
+/* Backward (nn.rs:384-427): dx written, dgamma/dbeta accumulated. */
+void orc_bn_bwd(const float *dy, const float *xhat, int n, int c, int hw,
+                const float *gamma, const float *invstd, float *dx,
+                float *dgamma, float *dbeta);
+
+/* ---- nn.rs glue --------------------------------------------------------- */
+void orc_relu_back(float *d, const float *y, size_t len);         /* nn.rs:433 */
+void orc_add(float *a, const float *b, size_t len);               /* nn.rs:441 */
+void orc_add_relu(float *a, const float *b, size_t len);          /* nn.rs:446 */
+void orc_gap_fwd(const float *x, int nc, int hw, float *y);       /* nn.rs:455 */
+void orc_gap_bwd(const float *dy, int nc, int hw, float *dx);     /* nn.rs:465 */
+/* scalar classifier nn::Linear (nn.rs:501-563) */
+void orc_fc_fwd(const float *x, int n, int fin, int fout, const float *w,
+                const float *b, float *y);
+void orc_fc_bwd(const float *x, const float *dy, int n, int fin, int fout,
+                const float *w, float *dw, float *db, float *dx);
+/* softmax + CE with smoothing; returns mean loss, writes dlogits (/n).
+ * nn.rs:573-637 */
+float orc_softmax_ce(const float *logits, const uint32_t *labels, int n,
+                     int nclass, float smooth, float *dlogits, int *correct);
+/* Param::step, SGD-Nesterov with decoupled wd.  nn.rs:102-110 */
+void orc_sgd_step(float *v, float *g, float *m, size_t len, float lr,
+                  float mom, float wd, int decay);
+
+/* ---- model.rs ResNet ---------------------------------------------------- */
+typedef struct orc_resnet orc_resnet;
+orc_resnet *orc_resnet_new(int depth_n, int width, int nclass, uint64_t seed);
+void   orc_resnet_free(orc_resnet *net);
+size_t orc_resnet_num_params(const orc_resnet *net);
+int    orc_resnet_num_tensors(const orc_resnet *net);
+/* flat copies in for_each_param order (model.rs:159-168) */
+void   orc_resnet_get_params(const orc_resnet *net, float *out);
+void   orc_resnet_set_params(orc_resnet *net, const float *in);
+void   orc_resnet_get_grads(const orc_resnet *net, float *out);
+void   orc_resnet_get_moments(const orc_resnet *net, float *out);
+void   orc_resnet_zero_grads(orc_resnet *net);
+/* running mean/var of every BN, for_each_buffer order (model.rs:170-176) */
+size_t orc_resnet_num_buffers(const orc_resnet *net);
+void   orc_resnet_get_buffers(const orc_resnet *net, float *out);
+/* per-tensor sizes and decay flags, for_each_param order */
+void   orc_resnet_param_info(const orc_resnet *net, int64_t *sizes, int *decay);
+/* model.rs:135-146; logits [n, nclass] */
+void   orc_resnet_forward(orc_resnet *net, const float *x, int n, int h,
+                          int w, int train, float *logits);
+/* model.rs:148-157 */
+void   orc_resnet_backward(orc_resnet *net, const float *dlogits);
+/* model.rs:206-208 */
+void   orc_resnet_step(orc_resnet *net, float lr, float mom, float wd);
+/* forward + softmax_ce + backward + step (train.rs:684-699) */
+float  orc_resnet_train_step(orc_resnet *net, const float *x,
+                             const uint32_t *labels, int n, float smooth,
+                             float lr, float mom, float wd, int *correct);
+/* model.rs:179-198 */
+uint64_t orc_resnet_flops(const orc_resnet *net, int h, int w);
+
+/* ---- threads ------------------------------------------------------------ */
+void orc_set_threads(int n);
+int  orc_get_threads(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,233 @@
+"""Pins the CPU oracle to the reference's own known-answer checks.
+
+The reference ships no stored tensors, so the oracle is pinned to what its
+tests hold:
+
+* the naive-GEMM check, check.rs:124-161 (3 shapes x 4 transposes);
+* the directional-derivative gradchecks, check.rs:19-40 (dircheck),
+  check.rs:503-724 (layercheck) and check.rs:727-770 (full ResNet);
+* the published parameter/MAC counts, README.md:116-117, and the rng
+  contract of rng.rs:74-118.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+TOL = 5e-3  # check.rs:42-44
+EPS = 3e-4  # check.rs:55-60
+
+
+def dircheck(base, grad, eps, rng, lossf):
+    """check.rs:19-40."""
+    base = np.asarray(base, np.float32)
+    v = rng.rand_vec(base.size)
+    lp = lossf((base + np.float32(eps) * v).astype(np.float32))
+    lm = lossf((base - np.float32(eps) * v).astype(np.float32))
+    num = (lp - lm) / (2.0 * eps)
+    ana = float(np.dot(np.asarray(grad, np.float64), v.astype(np.float64)))
+    return abs(num - ana) / (abs(num) + abs(ana) + 1e-6)
+
+
+def max_rel(want, got):
+    """check.rs:135-141."""
+    return float(np.max(np.abs(want - got)) / max(1e-6, float(np.max(np.abs(want)))))
+
+
+# ------------------------------------------------------------------ rng.rs
+
+
+def test_rng_contract():
+    a, b = O.Rng(1234), O.Rng(1234)
+    assert all(a.next_u64() == b.next_u64() for _ in range(1000))
+    assert O.Rng(1).next_u64() != O.Rng(2).next_u64()
+    r = O.Rng(7)
+    xs = [r.uniform() for _ in range(10000)]
+    assert min(xs) >= 0.0 and max(xs) < 1.0
+    r = O.Rng(9)
+    for n in (1, 2, 7, 100):
+        assert all(r.below(n) < n for _ in range(1000))
+
+
+def test_rng_xoshiro_known_answer():
+    """SplitMix64 seeding + xoshiro256++, written out independently in Python."""
+    M = 2**64 - 1
+
+    def rotl(x, k):
+        return ((x << k) | (x >> (64 - k))) & M
+
+    z = (5 + 0x9E3779B97F4A7C15) & M
+    s = []
+    for _ in range(4):
+        z = (z + 0x9E3779B97F4A7C15) & M
+        x = z
+        x = ((x ^ (x >> 30)) * 0xBF58476D1CE4E5B9) & M
+        x = ((x ^ (x >> 27)) * 0x94D049BB133111EB) & M
+        s.append(x ^ (x >> 31))
+    r = O.Rng(5)
+    for _ in range(64):
+        res = (rotl((s[0] + s[3]) & M, 23) + s[0]) & M
+        t = (s[1] << 17) & M
+        s[2] ^= s[0]
+        s[3] ^= s[1]
+        s[1] ^= s[2]
+        s[0] ^= s[3]
+        s[2] ^= t
+        s[3] = rotl(s[3], 45)
+        assert r.next_u64() == res
+
+
+def test_normal_moments():
+    v = O.Rng(0).rand_vec(200000)
+    assert abs(v.mean()) < 0.01 and abs(v.std() - 1.0) < 0.01
+
+
+# ------------------------------------------------------------------ gemm
+
+
+@pytest.mark.parametrize("m,n,k", [(23, 37, 19), (64, 48, 96), (7, 16, 259)])
+@pytest.mark.parametrize("at", [False, True])
+@pytest.mark.parametrize("bt", [False, True])
+def test_gemmcheck(m, n, k, at, bt):
+    """check.rs:124-161, with a much tighter bar than the reference's 5e-3."""
+    rng = O.Rng(1234 ^ m ^ (n << 8) ^ (k << 16))
+    a = rng.rand_vec(m * k)
+    b = rng.rand_vec(k * n)
+    want = O.naive_matmul(m, n, k, a, at, b, bt)
+    got = O.matmul(m, n, k, a, at, b, bt)
+    assert max_rel(want, got) < 1e-5
+    # acc = true adds on top of C
+    got2 = O.matmul(m, n, k, a, at, b, bt, c=got.copy(), acc=True)
+    assert max_rel(2 * want, got2) < 1e-5
+
+
+def test_matmul_dw_against_naive():
+    rng = O.Rng(3)
+    m, n, k = 37, 29, 1000
+    a = rng.rand_vec(k * m)
+    b = rng.rand_vec(k * n)
+    c0 = rng.rand_vec(m * n)
+    want = c0 + O.naive_matmul(m, n, k, a, True, b, False)
+    got = O.matmul_dw(m, n, k, a, b, c0.copy())
+    assert max_rel(want, got) < 1e-5
+
+
+# ------------------------------------------------------------------ layers
+
+
+def kaiming(rng, fan_in, n):
+    s = np.float32(np.sqrt(np.float32(2.0) / np.float32(fan_in)))
+    return (rng.rand_vec(n) * s).astype(np.float32)
+
+
+@pytest.mark.parametrize(
+    "cin,cout,k,stride,pad,hh",
+    [(3, 4, 3, 1, 1, 6), (4, 6, 1, 2, 0, 8), (4, 5, 3, 2, 1, 7)],  # check.rs:509-513
+)
+def test_conv_gradcheck(cin, cout, k, stride, pad, hh):
+    rng = O.Rng(1234)
+    w = kaiming(rng, cin * k * k, cout * cin * k * k)
+    x = rng.rand_vec(2 * cin * hh * hh)
+    y0 = O.conv2d_fwd(x, 2, cin, hh, hh, w, cout, k, stride, pad)
+    r = rng.rand_vec(y0.size)
+    dw = O.conv2d_wgrad(x, r, 2, cin, hh, hh, cout, k, stride, pad)
+    dx = O.conv2d_dgrad(r, 2, cin, hh, hh, w, cout, k, stride, pad)
+    e = dircheck(x, dx, EPS, rng, lambda c: float(np.dot(O.conv2d_fwd(c, 2, cin, hh, hh, w, cout, k, stride, pad), r)))
+    assert e < TOL, e
+    e = dircheck(w, dw, EPS, rng, lambda c: float(np.dot(O.conv2d_fwd(x, 2, cin, hh, hh, c, cout, k, stride, pad), r)))
+    assert e < TOL, e
+
+
+def test_batchnorm_gradcheck():
+    """check.rs:546-596."""
+    rng = O.Rng(99)
+    c, n, hw = 4, 3, 25
+    g = np.array([0.5 + rng.uniform() for _ in range(c)], np.float32)
+    b = rng.rand_vec(c)
+    x = (rng.rand_vec(n * c * hw) * 2.0 + 1.0).astype(np.float32)
+
+    def fwd(xx, gg, bb):
+        rm, rv = np.zeros(c, np.float32), np.ones(c, np.float32)
+        return O.bn_fwd_train(xx, n, c, hw, gg, bb, rm, rv, relu=False)
+
+    y0, xhat, invstd = fwd(x, g, b)
+    r = rng.rand_vec(y0.size)
+    dg, db = np.zeros(c, np.float32), np.zeros(c, np.float32)
+    dx = O.bn_bwd(r, xhat, n, c, hw, g, invstd, dg, db)
+    assert dircheck(x, dx, EPS, rng, lambda cc: float(np.dot(fwd(cc, g, b)[0], r))) < TOL
+    assert dircheck(g, dg, EPS, rng, lambda cc: float(np.dot(fwd(x, cc, b)[0], r))) < TOL
+    assert dircheck(b, db, EPS, rng, lambda cc: float(np.dot(fwd(x, g, cc)[0], r))) < TOL
+
+
+def test_fc_gradcheck():
+    """check.rs:598-623 (nn::Linear)."""
+    import ctypes as C
+
+    L = O.lib()
+    rng = O.Rng(5)
+    fin, fout, n = 6, 5, 3
+    w = (kaiming(rng, fin, fin * fout) * np.float32(0.5)).astype(np.float32)
+    b = rng.rand_vec(fout)
+    x = rng.rand_vec(n * fin)
+
+    def fwd(xx, ww):
+        y = np.empty(n * fout, np.float32)
+        L.orc_fc_fwd(np.ascontiguousarray(xx, np.float32), n, fin, fout, np.ascontiguousarray(ww, np.float32), b, y)
+        return y
+
+    r = rng.rand_vec(n * fout)
+    dw, db, dx = np.zeros(fin * fout, np.float32), np.zeros(fout, np.float32), np.zeros(n * fin, np.float32)
+    L.orc_fc_bwd(x, r, n, fin, fout, w, dw, db, dx)
+    assert dircheck(x, dx, EPS, rng, lambda c: float(np.dot(fwd(c, w), r))) < TOL
+    assert dircheck(w, dw, EPS, rng, lambda c: float(np.dot(fwd(x, c), r))) < TOL
+    del C
+
+
+def test_softmax_ce_gradcheck():
+    """check.rs:665-676."""
+    rng = O.Rng(11)
+    n, nc = 4, 7
+    z = rng.rand_vec(n * nc)
+    labels = np.array([rng.below(nc) for _ in range(n)], np.uint32)
+    _, d, _ = O.softmax_ce(z, labels, nc, 0.1)
+    e = dircheck(z, d, EPS, rng, lambda c: O.softmax_ce(c, labels, nc, 0.1)[0])
+    assert e < TOL, e
+
+
+# ------------------------------------------------------------------ model
+
+
+def test_resnet_param_and_mac_counts():
+    """README.md:116-117 (resnet14 w32: 708,228 params, 105.8 MMAC/img)."""
+    net = O.ResNet(2, 32, 100, 1234)
+    assert net.num_params() == 708228
+    assert round(net.flops() / 2e6, 1) == 105.8
+    # ResNet-56 W=64, the data-parallel config: 13,651,364 params
+    assert O.ResNet(9, 64, 100, 0).num_params() == 13651364
+
+
+def test_resnet_full_gradcheck():
+    """check.rs:727-770: ResNet-8 w4, 16x16, batch 8, all parameters."""
+    NC, BS, seed = 10, 8, 1234
+    net = O.ResNet(1, 4, NC, seed)
+    rng = O.Rng(seed ^ 0x5EED)
+    sizes, _ = net.param_info()
+    p = net.params()
+    p = (p + np.float32(0.3) * rng.rand_vec(p.size)).astype(np.float32)
+    net.set_params(p)
+    x = rng.rand_vec(BS * 3 * 16 * 16)
+    labels = np.array([rng.below(NC) for _ in range(BS)], np.uint32)
+    logits = net.forward(x, BS, hw=16, train=True)
+    _, dl, _ = O.softmax_ce(logits, labels, NC, 0.0)
+    net.zero_grads()
+    net.backward(dl)
+    g = net.grads()
+
+    def lossf(c):
+        net.set_params(c)
+        lg = net.forward(x, BS, hw=16, train=True)
+        return O.softmax_ce(lg, labels, NC, 0.0)[0]
+
+    e = dircheck(p, g, EPS, rng, lossf)
+    net.set_params(p)
+    assert e < TOL, e
