@@ -1,0 +1,353 @@
+#!/usr/bin/env python
+"""Training-throughput benchmark of the rustnn B200 backend.
+
+Default workload: ResNet --depth 9 (56 layers),
+width 64, global batch 1024 split over N GPUs (one process per GPU,
+data-parallel with an NCCL gradient allreduce, SyncBN so every rank
+normalises with whole-batch statistics like the single-process reference),
+synthetic CIFAR-shaped data (uniform bytes normalised to mean 0 / std 1),
+random init, f32 arithmetic (3xTF32 on the tensor cores).  One step =
+forward + softmax_ce + backward + allreduce + SGD-Nesterov (train.rs:684-699).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config resnet56|resnet20]
+    python bench.py --impl reference ...   # the CPU reference arm
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # name: (depth_n, width, global batch, BASELINE config index)
+    "resnet56": (9, 64, 1024, 5),
+    "resnet20": (3, 32, 128, 2),
+}
+NCLASS = 100
+METRIC = "train images/sec (fwd+bwd+optimizer step)"
+
+
+def synthetic_batch(n: int, seed: int):
+    """Uniform bytes 0-255 normalised per channel to mean 0 / std 1 (BASELINE
+    configs 2 and 5); labels uniform over 0..99."""
+    rs = np.random.default_rng(seed)
+    u = rs.integers(0, 256, size=(n, 3, 32, 32)).astype(np.float32)
+    x = ((u - 127.5) / 73.9).astype(np.float32)
+    labels = rs.integers(0, NCLASS, size=n).astype(np.uint32)
+    return x.ravel(), labels
+
+
+# ---------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sms.append(float(f[1]))
+                maxes.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        load = [s for s in sms if s > 0.5 * max(sms)] or sms
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+# ---------------------------------------------------------------- CPU legs
+
+
+def cpu_oracle_images_per_sec(depth_n, width, n_img, steps, threads=None):
+    """Times the C restatement of the reference (oracle) on the host cores."""
+    from oracle import oracle as O
+
+    if threads:
+        O.set_threads(threads)
+    cores = O.get_threads()
+    net = O.ResNet(depth_n, width, NCLASS, 0)
+    x, labels = synthetic_batch(n_img, 1)
+    net.train_step(x, labels)  # warm-up (allocations)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        net.train_step(x, labels, smooth=0.1, lr=0.2, mom=0.9, wd=5e-4)
+    dt = time.perf_counter() - t0
+    return n_img * steps / dt, cores, dt
+
+
+def run_reference(args, cfg_name):
+    depth_n, width, gbatch, cfg_idx = CONFIGS[cfg_name]
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    # bounded per-step sample of the same workload, all host threads
+    sample = int(os.environ.get("RNN_REF_SAMPLE", "8" if cfg_name == "resnet56" else "32"))
+    ips, cores, dt = cpu_oracle_images_per_sec(depth_n, width, sample, max(1, args.steps))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(ips, 3), "unit": "images/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * dt / max(1, args.steps), 2),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{cfg_name}-w{width} train step (BASELINE config {cfg_idx})", "global_batch": gbatch,
+                   "sample_batch": sample, "parallelism": "cpu-threads"},
+        "cpu_baseline": {"value": round(ips, 3), "unit": "images/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} steps of a {sample}-image batch of the {cfg_name}-w{width} step "
+                                   "(C restatement of the reference, OpenMP; the Rust reference cannot be built: "
+                                   "no cargo/rustc in the image)"},
+        "e2e": {"value": round(ips, 3), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- GPU arm
+
+
+def conv_kernel_roofline(ctx_ops, torch, n_local, peaks, reps=5):
+    """Times the stage-1 3x3 64->64 convolution kernels (the step's dominant
+    tcgen05 kernels) with CUDA events on the launching stream."""
+    from rustnn_b200 import ops
+
+    c, h = 64, 32
+    dev = torch.device("cuda")
+    x = torch.randn(n_local * c * h * h, device=dev)
+    w = torch.randn(c * c * 9, device=dev) * 0.05
+    dy = torch.randn(n_local * c * h * h, device=dev)
+    y = torch.empty_like(x)
+    dx = torch.empty_like(x)
+    dw = torch.zeros_like(w)
+    flops = 2.0 * n_local * h * h * c * c * 9
+    res = {}
+    s = torch.cuda.current_stream()
+    for name, fn in (("conv_fwd", lambda: ops.conv2d_forward(x, w, n_local, c, h, h, c, 3, 1, 1, y=y)),
+                     ("conv_dgrad", lambda: ops.conv2d_dgrad(dy, w, n_local, c, h, h, c, 3, 1, 1, dx=dx)),
+                     ("conv_wgrad", lambda: ops.conv2d_wgrad(x, dy, n_local, c, h, h, c, 3, 1, 1, dw=dw))):
+        for _ in range(2):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(s)
+        for _ in range(reps):
+            fn()
+        e1.record(s)
+        torch.cuda.synchronize()
+        res[name] = e0.elapsed_time(e1) / reps / 1e3  # seconds per launch
+    return flops, res
+
+
+def read_traffic(name):
+    """Per-launch DRAM bytes from a committed ncu summary (profiles/*.txt),
+    scaled to the bench launch size; None if absent."""
+    p = os.path.join(ROOT, "profiles", "conv_traffic.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith(name + " bytes_per_image_fullscale:"):
+            try:
+                return float(line.split(":")[1])
+            except ValueError:
+                return None
+    return None
+
+
+def run_ours(args, cfg_name):
+    import torch
+    import torch.distributed as dist
+
+    depth_n, width, gbatch, cfg_idx = CONFIGS[cfg_name]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and world > 1:
+        print(f"warning: WORLD_SIZE {world} != --gpus {args.gpus}", file=sys.stderr)
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+    if gbatch % world:
+        raise SystemExit(f"global batch {gbatch} not divisible by {world}")
+    n_local = gbatch // world
+
+    from rustnn_b200 import _lib, model
+
+    net = model.ResNet(depth_n, width, NCLASS, 0)
+    if world > 1:
+        uid = [model.dp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        net.dp_init(rank, world, uid[0], sync_bn=not args.local_bn)
+
+    x_np, lab_np = synthetic_batch(n_local, 100 + rank)
+    x = torch.from_numpy(x_np).cuda()
+    labels = torch.from_numpy(lab_np.astype(np.int32)).cuda()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- device-resident step (value)
+    for _ in range(args.warmup):
+        net.train_step(x, labels)
+    barrier()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    s = torch.cuda.current_stream()
+    l0 = _lib.lib().rnn_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(s)
+    for _ in range(args.steps):
+        net.train_step(x, labels)
+    e1.record(s)
+    barrier()
+    launches = _lib.lib().rnn_launch_count() - l0
+    clocks = sampler.stop()
+    t = e0.elapsed_time(e1) / 1e3
+    loss = float(net._loss.item())
+
+    # ---- end to end through the host tier (pinned host inputs, loss read back)
+    xp = torch.from_numpy(x_np).pin_memory()
+    lp = torch.from_numpy(lab_np).pin_memory()
+    xh = xp.numpy()
+    lh = lp.numpy()
+    for _ in range(max(1, args.warmup // 2)):
+        net.train_step_host(xh, lh)
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(s)
+    for _ in range(args.steps):
+        net.train_step_host(xh, lh)
+    e3.record(s)
+    barrier()
+    t_e2e = e2.elapsed_time(e3) / 1e3
+
+    # ---- dominant-kernel roofline (stage-1 conv at the local batch)
+    peaks = {}
+    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pk):
+        peaks = json.load(open(pk))
+    flops, ktimes = conv_kernel_roofline(None, torch, n_local, peaks)
+
+    times = torch.tensor([t, t_e2e], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    t, t_e2e = times.tolist()
+
+    if rank == 0:
+        value = gbatch * args.steps / t
+        e2e = gbatch * args.steps / t_e2e
+        top = max(ktimes, key=ktimes.get)
+        achieved = flops / ktimes[top] / 1e12
+        bf16 = peaks.get("bf16_tflops")
+        peak_src = "measured bf16 (MEASURED_PEAKS.json)"
+        if bf16 is None:
+            bf16, peak_src = 1590.0, "fallback bf16 1.59 PF/s"
+        tf32 = bf16 / 2.0
+        trafb = read_traffic(top)
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "images/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(1000 * t / args.steps, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"resnet{6 * depth_n + 2}-w{width} train step (BASELINE config {cfg_idx})",
+                       "global_batch": gbatch, "per_gpu_batch": n_local, "image": "3x32x32", "nclass": NCLASS,
+                       "optimizer": "sgd-nesterov lr0.2 mom0.9 wd5e-4, smooth 0.1",
+                       "parallelism": f"dp{world}" + ("" if world == 1 else (" localbn" if args.local_bn else " syncbn")),
+                       "l2": "no flush: one step moves tens of GB of activations, far beyond the 126 MB L2"},
+            "e2e": {"value": round(e2e, 2), "unit": "images/s", "h2d_bytes_per_step": int(x_np.nbytes + lab_np.nbytes),
+                    "d2h_bytes_per_step": 8},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor", "kernel": f"tc3_gemm {top} stage-1 3x3 64->64, batch {n_local}",
+                         "achieved": round(achieved, 2), "peak": round(bf16, 1), "unit": "TFLOP/s",
+                         "frac": round(achieved / bf16, 4),
+                         "peak_note": f"{peak_src}; achieved counts algorithmic 2MNK flops; 3xTF32 issues 3x "
+                                      f"that at TF32 rate (= bf16/2 = {tf32:.0f})",
+                         "frac_issued_vs_tf32": round(3 * achieved / tf32, 4),
+                         "traffic": None if trafb is None else round(trafb * n_local),
+                         "kernel_ms": {k: round(v * 1e3, 4) for k, v in ktimes.items()}},
+            "clocks": clocks,
+            "loss": round(loss, 5),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            sample = 8 if cfg_name == "resnet56" else 32
+            ips, cores, dt = cpu_oracle_images_per_sec(depth_n, width, sample, 2)
+            line["cpu_baseline"] = {"value": round(ips, 3), "unit": "images/s", "cores": cores, "kind": "port",
+                                    "sample": f"2 steps x {sample} images of the same step (C restatement)"}
+        print(json.dumps(line), flush=True)
+    net.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="resnet56", choices=sorted(CONFIGS))
+    ap.add_argument("--local-bn", action="store_true", help="per-rank BN statistics instead of SyncBN")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args, args.config)
+    return run_ours(args, args.config)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,190 @@
+/*
+ * librnn_b200 -- C ABI of the B200 (sm_100a) backend for rustnn's
+ * dense-contraction path.
+ *
+ * Every entry point returns RNN_OK (0) or a negative RNN_ERR_* code; nothing
+ * unwinds across the boundary.  rnn_last_error() gives the message of the
+ * last failure on the calling thread.
+ *
+ * Two tiers:
+ *   - "_dev" entry points take DEVICE pointers and enqueue on the context's
+ *     stream (asynchronous; call rnn_ctx_synchronize to wait and to collect
+ *     device-side error flags);
+ *   - the plain-named entry points take HOST pointers, mirror the reference's
+ *     Rust signatures, copy in, run, copy out and synchronise.
+ * All tensors are f32, row-major / NCHW exactly as in the reference.
+ * Gradients accumulate (+=) wherever the reference accumulates.
+ *
+ * A context owns one CUDA stream and a growable device workspace.  Calls on
+ * one context must come from one host thread at a time.
+ */
+#ifndef RNN_B200_H
+#define RNN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RNN_OK 0
+#define RNN_ERR_ARG -1     /* bad shape, stride, alignment or pointer */
+#define RNN_ERR_CUDA -2    /* CUDA runtime error */
+#define RNN_ERR_NCCL -3    /* NCCL error */
+#define RNN_ERR_DEVICE -4  /* a kernel raised its device error word (timeout) */
+#define RNN_ERR_UNSUPPORTED -5
+
+typedef struct rnn_ctx rnn_ctx;
+typedef struct rnn_resnet rnn_resnet;
+
+const char *rnn_last_error(void);
+/* Number of kernels this library has launched in this process. */
+unsigned long long rnn_launch_count(void);
+/* 1 when the library was built for sm_100a and a B200-class device is present */
+int rnn_device_ok(int device);
+
+/* ---- context ------------------------------------------------------------ */
+int rnn_ctx_create(rnn_ctx **out, int device);
+int rnn_ctx_destroy(rnn_ctx *ctx);
+/* Use an external stream (e.g. the caller's framework stream) instead of the
+ * context's own; pass NULL to go back to the context's stream. */
+int rnn_ctx_set_stream(rnn_ctx *ctx, void *cuda_stream);
+void *rnn_ctx_stream(rnn_ctx *ctx);
+/* Waits for the stream and reports kernel timeouts as RNN_ERR_DEVICE. */
+int rnn_ctx_synchronize(rnn_ctx *ctx);
+
+/* ---- GEMM (gemm.rs) ----------------------------------------------------- */
+/* C[m x n] (+)= op(A) op(B).  at: A is [k x m]; bt: B is [n x k]; acc: add to
+ * C instead of overwriting.  Replaces gemm::matmul (gemm.rs:434-444) and
+ * gemm::gemm_small (gemm.rs:500-512; the PackedA/PackedB scratch arguments
+ * have no counterpart: packing happens in shared memory). */
+int rnn_gemm_dev(rnn_ctx *ctx, int m, int n, int k, const float *a, int at,
+                 const float *b, int bt, float *c, int acc);
+int rnn_gemm(rnn_ctx *ctx, int m, int n, int k, const float *a, int at,
+             const float *b, int bt, float *c, int acc);
+/* C[m x n] += A^T B, A [k x m], B [k x n]: gemm::matmul_dw (gemm.rs:555).
+ * Split over K with a deterministic fixed-order reduction. */
+int rnn_gemm_dw_dev(rnn_ctx *ctx, int m, int n, int k, const float *a,
+                    const float *b, float *c);
+int rnn_gemm_dw(rnn_ctx *ctx, int m, int n, int k, const float *a,
+                const float *b, float *c);
+
+/* ---- Conv2d (nn.rs:115-251, conv.rs) ------------------------------------ */
+/* x [n,cin,h,w], w [cout, cin*k*k] in (ci,kh,kw) order, y [n,cout,oh,ow]
+ * with oh = (h + 2 pad - k)/stride + 1.  acc: y += conv(x) instead of =.
+ * Replaces Conv2d::forward (nn.rs:166) / conv::forward_image (conv.rs:169). */
+int rnn_conv2d_fwd_dev(rnn_ctx *ctx, const float *x, int n, int cin, int h,
+                       int w, const float *wt, int cout, int k, int stride,
+                       int pad, float *y, int acc);
+int rnn_conv2d_fwd(rnn_ctx *ctx, const float *x, int n, int cin, int h, int w,
+                   const float *wt, int cout, int k, int stride, int pad,
+                   float *y);
+/* dx (+)= col2im(W^T dy).  Replaces the dX half of Conv2d::backward
+ * (nn.rs:230-250) / conv::dx_image (conv.rs:207).  acc=0 overwrites dx like
+ * the reference (conv.rs:218); acc=1 adds (fuses the residual add_). */
+int rnn_conv2d_dgrad_dev(rnn_ctx *ctx, const float *dy, int n, int cin, int h,
+                         int w, const float *wt, int cout, int k, int stride,
+                         int pad, float *dx, int acc);
+int rnn_conv2d_dgrad(rnn_ctx *ctx, const float *dy, int n, int cin, int h,
+                     int w, const float *wt, int cout, int k, int stride,
+                     int pad, float *dx);
+/* dw += dy im2col(x)^T.  Replaces Conv2d::backward_w (nn.rs:193-227) /
+ * conv::dw_image (conv.rs:283).  Deterministic split-K reduction. */
+int rnn_conv2d_wgrad_dev(rnn_ctx *ctx, const float *x, const float *dy, int n,
+                         int cin, int h, int w, int cout, int k, int stride,
+                         int pad, float *dw);
+int rnn_conv2d_wgrad(rnn_ctx *ctx, const float *x, const float *dy, int n,
+                     int cin, int h, int w, int cout, int k, int stride,
+                     int pad, float *dw);
+
+/* ---- BatchNorm2d (nn.rs:255-428) ---------------------------------------- */
+/* Train-mode forward over y [n,c,hw]: per-channel batch statistics in f64
+ * (nn.rs:301-322), running mean/var update with momentum `mom` and unbiased
+ * variance (nn.rs:330-336), out = gamma*xhat + beta, optionally ReLU
+ * (nn.rs:326-354).  Writes mean[c] and invstd[c]; xhat is not stored (the
+ * backward recomputes it from y).  out may alias y. */
+int rnn_batchnorm_fwd_dev(rnn_ctx *ctx, const float *y, int n, int c, int hw,
+                          const float *gamma, const float *beta, float *rmean,
+                          float *rvar, float mom, float eps, int relu,
+                          float *mean, float *invstd, float *out);
+/* Eval-mode forward (nn.rs:358-369). */
+int rnn_batchnorm_eval_dev(rnn_ctx *ctx, const float *y, int n, int c, int hw,
+                           const float *gamma, const float *beta,
+                           const float *rmean, const float *rvar, float eps,
+                           int relu, float *out);
+/* Backward (nn.rs:384-427) with xhat = (y - mean) * invstd.  When
+ * relu_out != NULL the incoming gradient is first masked by relu_out > 0
+ * (relu_back_, nn.rs:433).  dgamma/dbeta accumulate; dx is written. */
+int rnn_batchnorm_bwd_dev(rnn_ctx *ctx, const float *dy, const float *y, int n,
+                          int c, int hw, const float *gamma, const float *mean,
+                          const float *invstd, const float *relu_out,
+                          float *dx, float *dgamma, float *dbeta);
+
+/* ---- elementwise / loss / optimiser (nn.rs) ----------------------------- */
+int rnn_relu_back_dev(rnn_ctx *ctx, float *d, const float *y, size_t len);   /* nn.rs:433 */
+int rnn_add_dev(rnn_ctx *ctx, float *a, const float *b, size_t len);         /* nn.rs:441 */
+int rnn_add_relu_dev(rnn_ctx *ctx, float *a, const float *b, size_t len);    /* nn.rs:446 */
+int rnn_gap_fwd_dev(rnn_ctx *ctx, const float *x, int nc, int hw, float *y); /* nn.rs:455 */
+int rnn_gap_bwd_dev(rnn_ctx *ctx, const float *dy, int nc, int hw, float *dx); /* nn.rs:465 */
+/* softmax + cross-entropy with label smoothing (nn.rs:615-637): writes
+ * dlogits (already divided by n), loss_out[0] = mean loss, correct_out[0] =
+ * number of argmax hits.  Deterministic. */
+int rnn_softmax_ce_dev(rnn_ctx *ctx, const float *logits, const uint32_t *labels,
+                       int n, int nclass, float smooth, float *dlogits,
+                       float *loss_out, int *correct_out);
+/* Param::step (nn.rs:102-110) over `len` elements; g is zeroed. */
+int rnn_sgd_nesterov_dev(rnn_ctx *ctx, float *v, float *g, float *m, size_t len,
+                         float lr, float mom, float wd, int decay);
+
+/* ---- ResNet training step (model.rs, train.rs:684-699) ------------------ */
+/* ResNet::new(depth_n, width, nclass, seed) (model.rs:112-133), with the
+ * reference's initialisation drawn from the same xoshiro256++ stream, so
+ * parameters are bit-identical to the reference's at creation. */
+int rnn_resnet_create(rnn_ctx *ctx, int depth_n, int width, int nclass,
+                      uint64_t seed, rnn_resnet **out);
+int rnn_resnet_destroy(rnn_resnet *net);
+int rnn_resnet_num_params(rnn_resnet *net, size_t *out);
+int rnn_resnet_num_buffers(rnn_resnet *net, size_t *out);
+/* flat host copies in for_each_param order (model.rs:159-168) */
+int rnn_resnet_get_params(rnn_resnet *net, float *out);
+int rnn_resnet_set_params(rnn_resnet *net, const float *in);
+int rnn_resnet_get_grads(rnn_resnet *net, float *out);
+int rnn_resnet_get_moments(rnn_resnet *net, float *out);
+/* running mean/var, for_each_buffer order (model.rs:170-176) */
+int rnn_resnet_get_buffers(rnn_resnet *net, float *out);
+/* device pointer to the flat gradient buffer (for external collectives) */
+int rnn_resnet_grad_buffer(rnn_resnet *net, float **out, size_t *len);
+/* ResNet::forward (model.rs:135): x [n,3,h,w] device, logits [n,nclass] */
+int rnn_resnet_forward_dev(rnn_resnet *net, const float *x, int n, int h, int w,
+                           int train, float *logits);
+/* ResNet::backward (model.rs:148): gradients accumulate */
+int rnn_resnet_backward_dev(rnn_resnet *net, const float *dlogits);
+/* ResNet::step (model.rs:206) */
+int rnn_resnet_step(rnn_resnet *net, float lr, float mom, float wd);
+/* forward + softmax_ce + backward (+ gradient allreduce when data-parallel)
+ * + step, on device inputs.  loss/correct are device pointers (1 element). */
+int rnn_resnet_train_step_dev(rnn_resnet *net, const float *x,
+                              const uint32_t *labels, int n, float smooth,
+                              float lr, float mom, float wd, float *loss,
+                              int *correct);
+/* Same from host inputs: copies x/labels in and loss/correct out. */
+int rnn_resnet_train_step(rnn_resnet *net, const float *x,
+                          const uint32_t *labels, int n, float smooth, float lr,
+                          float mom, float wd, float *loss, int *correct);
+
+/* ---- data parallel (no reference counterpart: the reference is one process) */
+#define RNN_UID_BYTES 128
+int rnn_dp_unique_id(unsigned char *uid_out);
+/* Joins an NCCL communicator (one rank per GPU).  The train step then sums
+ * gradients across ranks and divides by world (each rank's softmax_ce divides
+ * by its local batch), and, when sync_bn != 0, BatchNorm statistics are
+ * reduced across ranks so every rank normalises with whole-batch statistics
+ * like the single-process reference. */
+int rnn_resnet_dp_init(rnn_resnet *net, int rank, int world,
+                       const unsigned char *uid, int sync_bn);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,119 @@
+"""Loads librnn_b200.so and declares its C ABI (include/rnn_b200.h).
+
+The product path has no fallback: if the library is missing or the device is
+not an sm_100a part, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "librnn_b200.so")
+
+RNN_OK = 0
+ERRORS = {-1: "RNN_ERR_ARG", -2: "RNN_ERR_CUDA", -3: "RNN_ERR_NCCL", -4: "RNN_ERR_DEVICE", -5: "RNN_ERR_UNSUPPORTED"}
+
+_lock = threading.Lock()
+_lib = None
+
+I, F, Z, U64, P = C.c_int, C.c_float, C.c_size_t, C.c_uint64, C.c_void_p
+FP = C.c_void_p  # device or host float pointer, passed as an integer address
+
+
+class _CtxS(C.Structure):
+    """opaque rnn_ctx"""
+
+
+class _NetS(C.Structure):
+    """opaque rnn_resnet"""
+
+
+# distinct handle types: ctypes rejects a context where a network is expected
+CTX = C.POINTER(_CtxS)
+NET = C.POINTER(_NetS)
+
+# name -> argtypes; every function returns int unless listed in _RESTYPE
+SIGS = {
+    "rnn_device_ok": [I],
+    "rnn_launch_count": [],
+    "rnn_ctx_create": [C.POINTER(CTX), I],
+    "rnn_ctx_destroy": [CTX],
+    "rnn_ctx_set_stream": [CTX, P],
+    "rnn_ctx_stream": [CTX],
+    "rnn_ctx_synchronize": [CTX],
+    "rnn_gemm_dev": [CTX, I, I, I, FP, I, FP, I, FP, I],
+    "rnn_gemm": [CTX, I, I, I, FP, I, FP, I, FP, I],
+    "rnn_gemm_dw_dev": [CTX, I, I, I, FP, FP, FP],
+    "rnn_gemm_dw": [CTX, I, I, I, FP, FP, FP],
+    "rnn_conv2d_fwd_dev": [CTX, FP, I, I, I, I, FP, I, I, I, I, FP, I],
+    "rnn_conv2d_fwd": [CTX, FP, I, I, I, I, FP, I, I, I, I, FP],
+    "rnn_conv2d_dgrad_dev": [CTX, FP, I, I, I, I, FP, I, I, I, I, FP, I],
+    "rnn_conv2d_dgrad": [CTX, FP, I, I, I, I, FP, I, I, I, I, FP],
+    "rnn_conv2d_wgrad_dev": [CTX, FP, FP, I, I, I, I, I, I, I, I, FP],
+    "rnn_conv2d_wgrad": [CTX, FP, FP, I, I, I, I, I, I, I, I, FP],
+    "rnn_batchnorm_fwd_dev": [CTX, FP, I, I, I, FP, FP, FP, FP, F, F, I, FP, FP, FP],
+    "rnn_batchnorm_eval_dev": [CTX, FP, I, I, I, FP, FP, FP, FP, F, I, FP],
+    "rnn_batchnorm_bwd_dev": [CTX, FP, FP, I, I, I, FP, FP, FP, FP, FP, FP, FP],
+    "rnn_relu_back_dev": [CTX, FP, FP, Z],
+    "rnn_add_dev": [CTX, FP, FP, Z],
+    "rnn_add_relu_dev": [CTX, FP, FP, Z],
+    "rnn_gap_fwd_dev": [CTX, FP, I, I, FP],
+    "rnn_gap_bwd_dev": [CTX, FP, I, I, FP],
+    "rnn_softmax_ce_dev": [CTX, FP, FP, I, I, F, FP, FP, FP],
+    "rnn_sgd_nesterov_dev": [CTX, FP, FP, FP, Z, F, F, F, I],
+    "rnn_resnet_create": [CTX, I, I, I, U64, C.POINTER(NET)],
+    "rnn_resnet_destroy": [NET],
+    "rnn_resnet_num_params": [NET, C.POINTER(Z)],
+    "rnn_resnet_num_buffers": [NET, C.POINTER(Z)],
+    "rnn_resnet_get_params": [NET, FP],
+    "rnn_resnet_set_params": [NET, FP],
+    "rnn_resnet_get_grads": [NET, FP],
+    "rnn_resnet_get_moments": [NET, FP],
+    "rnn_resnet_get_buffers": [NET, FP],
+    "rnn_resnet_grad_buffer": [NET, C.POINTER(P), C.POINTER(Z)],
+    "rnn_resnet_forward_dev": [NET, FP, I, I, I, I, FP],
+    "rnn_resnet_backward_dev": [NET, FP],
+    "rnn_resnet_step": [NET, F, F, F],
+    "rnn_resnet_train_step_dev": [NET, FP, FP, I, F, F, F, F, FP, FP],
+    "rnn_resnet_train_step": [NET, FP, FP, I, F, F, F, F, FP, FP],
+    "rnn_dp_unique_id": [FP],
+    "rnn_resnet_dp_init": [NET, I, I, FP, I],
+}
+_RESTYPE = {"rnn_ctx_stream": P, "rnn_launch_count": C.c_ulonglong}
+
+
+class RnnError(RuntimeError):
+    pass
+
+
+def lib():
+    """The loaded library; raises if it was not built."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise RnnError(
+                f"{LIB_PATH} is missing: build it with `python -m rustnn_b200.build` (there is no CPU fallback)"
+            )
+        L = C.CDLL(LIB_PATH)
+        L.rnn_last_error.restype = C.c_char_p
+        L.rnn_last_error.argtypes = []
+        for name, args in SIGS.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = _RESTYPE.get(name, C.c_int)
+        _lib = L
+        return L
+
+
+def check(code: int, what: str = "") -> None:
+    if code != RNN_OK:
+        msg = lib().rnn_last_error().decode(errors="replace")
+        raise RnnError(f"{what}: {ERRORS.get(code, code)}: {msg}")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args), name)

@@ -1,0 +1,213 @@
+// Dense GEMM entry points on the tcgen05 3xTF32 engine.
+//
+//   rnn_gemm_dev     C (+)= op(A) op(B)           gemm.rs:434 matmul / :500 gemm_small
+//   rnn_gemm_dw_dev  C  += A^T B  (split over K)  gemm.rs:555 matmul_dw
+//
+// Operand A rows are the M index and operand B rows the N index of the
+// engine; K-contiguous operands use the K-major producer mapping (lanes walk
+// K, 16-byte loads when K is a multiple of 4), M/N-contiguous operands the
+// MN-major mapping (lanes walk rows, each warp load covers 32 consecutive
+// floats).
+#include "tc_launch.cuh"
+
+namespace rnn {
+namespace tc {
+
+template <bool AT, bool BT>
+struct DenseProb {
+  static constexpr bool A_KMAJOR = !AT;  // A [m x k] row-major: K contiguous
+  static constexpr bool B_KMAJOR = BT;   // B [n x k] row-major: K contiguous
+  const float* a;
+  const float* b;
+  float* c;
+  float* ws;  // split-K partials [splits][M][N] (splits > 1)
+  int M, N, K;
+  int acc;
+  int splits;
+  bool a_vec, b_vec, c_vec;
+
+  __device__ __forceinline__ void load_a(int row, int k4, float (&v)[4]) const {
+    if (!AT) {
+      if (row < M && a_vec && k4 + 3 < K) {
+        float4 t = __ldg(reinterpret_cast<const float4*>(a + (size_t)row * K + k4));
+        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+          v[i] = (row < M && k4 + i < K) ? __ldg(a + (size_t)row * K + k4 + i) : 0.0f;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+        v[i] = (row < M && k4 + i < K) ? __ldg(a + (size_t)(k4 + i) * M + row) : 0.0f;
+    }
+  }
+
+  __device__ __forceinline__ void load_b(int row, int k4, float (&v)[4]) const {
+    if (BT) {
+      if (row < N && b_vec && k4 + 3 < K) {
+        float4 t = __ldg(reinterpret_cast<const float4*>(b + (size_t)row * K + k4));
+        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+          v[i] = (row < N && k4 + i < K) ? __ldg(b + (size_t)row * K + k4 + i) : 0.0f;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+        v[i] = (row < N && k4 + i < K) ? __ldg(b + (size_t)(k4 + i) * N + row) : 0.0f;
+    }
+  }
+
+  __device__ __forceinline__ void store(int row, int col0, int split, const float (&v)[32]) const {
+    if (row >= M || col0 >= N) return;
+    const int nvalid = N - col0;
+    if (splits > 1) {
+      store_row32(ws + ((size_t)split * M + row) * N + col0, nvalid, v, false, c_vec);
+    } else {
+      store_row32(c + (size_t)row * N + col0, nvalid, v, acc != 0, c_vec);
+    }
+  }
+};
+
+template <int BN>
+struct DenseLauncher {
+  template <class P>
+  static int run(rnn_ctx* ctx, P prob, int splits) {
+    Sched s = make_sched(prob.M, prob.N, prob.K, BN, splits);
+    prob.splits = s.splits;
+    if (s.splits > 1) {
+      RNN_TRY(ensure_ws(ctx, sizeof(float) * (size_t)s.splits * prob.M * prob.N));
+      prob.ws = static_cast<float*>(ctx->ws);
+    }
+    RNN_TRY(launch<BN>(ctx, prob, s));
+    if (s.splits > 1)
+      RNN_TRY(launch_splitk_reduce(ctx, prob.ws, prob.c, prob.M, prob.N, s.splits, prob.acc != 0,
+                                   false));
+    return RNN_OK;
+  }
+};
+
+static inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+template <bool AT, bool BT>
+static int gemm_typed(rnn_ctx* ctx, int m, int n, int k, const float* a, const float* b, float* c,
+                      bool acc, bool force_split) {
+  DenseProb<AT, BT> p;
+  p.a = a; p.b = b; p.c = c; p.ws = nullptr;
+  p.M = m; p.N = n; p.K = k; p.acc = acc ? 1 : 0; p.splits = 1;
+  p.a_vec = (k % 4 == 0) && al16(a);
+  p.b_vec = (k % 4 == 0) && al16(b);
+  p.c_vec = (n % 4 == 0) && al16(c);
+  const int m_tiles = (m + BM - 1) / BM;
+  const int bn = pick_bn(n, m_tiles, ctx->num_sms);
+  int splits = pick_splits(m, n, k, bn, ctx->num_sms);
+  if (!force_split && splits > 1 && (long)m * n * k < (1L << 22)) splits = 1;
+  switch (bn) {
+    case 32: return DenseLauncher<32>::run(ctx, p, splits);
+    case 64: return DenseLauncher<64>::run(ctx, p, splits);
+    case 128: return DenseLauncher<128>::run(ctx, p, splits);
+    default: return DenseLauncher<256>::run(ctx, p, splits);
+  }
+}
+
+__global__ void zero_kernel(float* c, size_t len) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (; i < len; i += stride) c[i] = 0.0f;
+}
+
+int gemm_dev(rnn_ctx* ctx, int m, int n, int k, const float* a, bool at, const float* b, bool bt,
+             float* c, bool acc, bool force_split) {
+  RNN_REQUIRE(m >= 0 && n >= 0 && k >= 0, "gemm: negative size m=%d n=%d k=%d", m, n, k);
+  if (m == 0 || n == 0) return RNN_OK;
+  RNN_REQUIRE(c != nullptr, "gemm: null C");
+  if (k == 0) {  // gemm.rs:449-453
+    if (!acc) {
+      size_t len = (size_t)m * n;
+      zero_kernel<<<(unsigned)std::min<size_t>((len + 255) / 256, 4096), 256, 0, ctx->stream>>>(c, len);
+      RNN_CHECK_LAUNCH();
+    }
+    return RNN_OK;
+  }
+  RNN_REQUIRE(a != nullptr && b != nullptr, "gemm: null operand");
+  if (!at && !bt) return gemm_typed<false, false>(ctx, m, n, k, a, b, c, acc, force_split);
+  if (!at && bt) return gemm_typed<false, true>(ctx, m, n, k, a, b, c, acc, force_split);
+  if (at && !bt) return gemm_typed<true, false>(ctx, m, n, k, a, b, c, acc, force_split);
+  return gemm_typed<true, true>(ctx, m, n, k, a, b, c, acc, force_split);
+}
+
+// ---------------------------------------------------------------- split-K
+
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, float* __restrict__ out, int rows,
+                                     int cols, int splits, int acc, int transpose) {
+  const size_t total = (size_t)rows * cols;
+  const size_t plane = total;
+  if (!transpose) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+         i += (size_t)gridDim.x * blockDim.x) {
+      float s = 0.0f;
+      for (int p = 0; p < splits; p++) s += ws[p * plane + i];
+      out[i] = acc ? out[i] + s : s;
+    }
+  } else {
+    // 32x32 tiles through shared memory so that both the partial reads
+    // (row-major [rows][cols]) and the transposed writes are coalesced.
+    __shared__ float tile[32][33];
+    const int tr = (rows + 31) / 32, tcn = (cols + 31) / 32;
+    for (int t = blockIdx.x; t < tr * tcn; t += gridDim.x) {
+      const int r0 = (t % tr) * 32, c0 = (t / tr) * 32;
+      for (int e = threadIdx.x; e < 1024; e += blockDim.x) {
+        const int rr = e / 32, cc = e % 32;
+        const int r = r0 + rr, c = c0 + cc;
+        float s = 0.0f;
+        if (r < rows && c < cols)
+          for (int p = 0; p < splits; p++) s += ws[p * plane + (size_t)r * cols + c];
+        tile[rr][cc] = s;
+      }
+      __syncthreads();
+      for (int e = threadIdx.x; e < 1024; e += blockDim.x) {
+        const int cc = e / 32, rr = e % 32;
+        const int r = r0 + rr, c = c0 + cc;
+        if (r < rows && c < cols) {
+          float* o = out + (size_t)c * rows + r;
+          *o = acc ? *o + tile[rr][cc] : tile[rr][cc];
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+int launch_splitk_reduce(rnn_ctx* ctx, const float* ws, float* out, int rows, int cols, int splits,
+                         bool acc, bool transpose) {
+  size_t total = (size_t)rows * cols;
+  unsigned grid;
+  if (transpose) grid = (unsigned)std::min<size_t>(((rows + 31) / 32) * (size_t)((cols + 31) / 32), 4096);
+  else grid = (unsigned)std::min<size_t>((total + 255) / 256, (size_t)ctx->num_sms * 8);
+  if (grid == 0) return RNN_OK;
+  splitk_reduce_kernel<<<grid, 256, 0, ctx->stream>>>(ws, out, rows, cols, splits, acc ? 1 : 0,
+                                                      transpose ? 1 : 0);
+  RNN_CHECK_LAUNCH();
+  return RNN_OK;
+}
+
+}  // namespace tc
+}  // namespace rnn
+
+using namespace rnn;
+
+extern "C" int rnn_gemm_dev(rnn_ctx* ctx, int m, int n, int k, const float* a, int at,
+                            const float* b, int bt, float* c, int acc) {
+  RNN_REQUIRE(ctx != nullptr, "null context");
+  return tc::gemm_dev(ctx, m, n, k, a, at != 0, b, bt != 0, c, acc != 0, false);
+}
+
+extern "C" int rnn_gemm_dw_dev(rnn_ctx* ctx, int m, int n, int k, const float* a, const float* b,
+                               float* c) {
+  RNN_REQUIRE(ctx != nullptr, "null context");
+  if (m == 0 || n == 0 || k == 0) return RNN_OK;  // gemm.rs:556-558
+  // C[m x n] += A^T B with A [k x m], B [k x n]: op(A) = A^T (at), op(B) = B
+  return tc::gemm_dev(ctx, m, n, k, a, true, b, false, c, true, true);
+}

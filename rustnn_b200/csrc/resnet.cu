@@ -1,0 +1,632 @@
+// Device-resident CIFAR ResNet training step (model.rs, nn.rs, train.rs).
+//
+// Parameters, gradients and momenta live in three flat device buffers in the
+// reference's for_each_param order (model.rs:159-168), so the SGD update is
+// one launch and the data-parallel gradient allreduce is one NCCL call.
+// Activations are preallocated for the batch capacity and reused each step:
+// per block x_in (the previous block's output), y1 = conv1(x), h1 =
+// relu(bn1(y1)), y2 = conv2(h1), yd = convd(x) (down-sampling blocks) and
+// out = relu(bn2(y2) + shortcut), which is exactly what model.rs:39-55 keeps
+// alive for its backward.  BatchNorm keeps its input y and recomputes xhat.
+#include <nccl.h>
+#include <string.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "bn.cuh"
+#include "ew.cuh"
+#include "rng.h"
+
+namespace rnn {
+
+struct ConvL {
+  int cin, cout, k, stride, pad;
+  size_t w_off;  // offset into the flat parameter buffer
+};
+
+struct BNL {
+  int c;
+  size_t g_off, b_off;  // gamma, beta offsets in the flat buffer
+  size_t rm_off;        // running mean offset in the buffer array; rv follows
+  float* mean = nullptr;
+  float* invstd = nullptr;
+};
+
+struct Block {
+  ConvL c1, c2, cd;
+  BNL b1, b2, bd;
+  bool down = false;
+  int cin, cout, stride;
+  float *y1 = nullptr, *h1 = nullptr, *y2 = nullptr, *yd = nullptr, *out = nullptr;
+  const float* x_in = nullptr;
+  int n = 0, h = 0, w = 0, oh = 0, ow = 0;
+};
+
+}  // namespace rnn
+
+using namespace rnn;
+
+struct rnn_resnet {
+  rnn_ctx* ctx = nullptr;
+  int depth_n = 0, width = 0, nclass = 0;
+  ConvL stem{};
+  BNL stem_bn{};
+  std::vector<Block> blocks;
+  size_t fcw_off = 0, fcb_off = 0;
+  int fin = 0, fout = 0;
+  // flat parameter state
+  size_t nparams = 0;
+  float *v = nullptr, *g = nullptr, *m = nullptr;
+  uint8_t* decay = nullptr;
+  std::vector<uint8_t> decay_host;
+  // BN running statistics (for_each_buffer order: [rm, rv] per BN)
+  size_t nbuf = 0;
+  float* bnbuf = nullptr;
+  float* bnstat = nullptr;  // mean/invstd arrays of every BN
+  // activations
+  int cap_n = 0, cap_h = 0, cap_w = 0;
+  float *stem_y = nullptr, *stem_out = nullptr, *pooled = nullptr, *logits = nullptr, *dlogits = nullptr,
+        *dpool = nullptr;
+  float* gbuf[4] = {nullptr, nullptr, nullptr, nullptr};
+  size_t gbuf_elems = 0;
+  void* scratch = nullptr;  // BN partials/sums, CE row buffers
+  size_t scratch_bytes = 0;
+  float* x_stage = nullptr;
+  uint32_t* lab_stage = nullptr;
+  float* loss_dev = nullptr;
+  int* correct_dev = nullptr;
+  std::vector<void*> act_allocs;
+  // last forward
+  int n = 0, h = 0, w = 0, fh = 0, fw = 0;
+  const float* x_in = nullptr;
+  // data parallel
+  ncclComm_t comm = nullptr;
+  int rank = 0, world = 1;
+  bool sync_bn = false;
+};
+
+namespace rnn {
+
+static size_t bn_scratch_need(rnn_resnet* net, int n) {
+  size_t a = 0;
+  for (int c : {net->width, net->width * 2, net->width * 4})
+    a = std::max(a, bn_scratch_bytes(n, c, net->ctx->num_sms));
+  size_t ce = (((size_t)n * 4 + 255) & ~(size_t)255) * 2;
+  return a + ce + 4096;
+}
+
+static void free_acts(rnn_resnet* net) {
+  for (void* p : net->act_allocs) cudaFree(p);
+  net->act_allocs.clear();
+  for (auto& b : net->blocks) b.y1 = b.h1 = b.y2 = b.yd = b.out = nullptr;
+  net->stem_y = net->stem_out = net->pooled = net->logits = net->dlogits = net->dpool = nullptr;
+  for (auto& p : net->gbuf) p = nullptr;
+  net->scratch = nullptr;
+  net->x_stage = nullptr;
+  net->lab_stage = nullptr;
+  net->cap_n = net->cap_h = net->cap_w = 0;
+}
+
+static int alloc_f(rnn_resnet* net, float** p, size_t n) {
+  void* q = nullptr;
+  RNN_CUDA(cudaMalloc(&q, std::max<size_t>(n, 1) * sizeof(float)));
+  net->act_allocs.push_back(q);
+  *p = static_cast<float*>(q);
+  return RNN_OK;
+}
+
+// (Re)allocates every activation for batch n at h x w input.
+static int ensure_acts(rnn_resnet* net, int n, int h, int w) {
+  if (n <= net->cap_n && h == net->cap_h && w == net->cap_w) return RNN_OK;
+  RNN_CUDA(cudaStreamSynchronize(net->ctx->stream));
+  free_acts(net);
+  const int W = net->width;
+  size_t stem = (size_t)n * W * h * w;
+  RNN_TRY(alloc_f(net, &net->stem_y, stem));
+  RNN_TRY(alloc_f(net, &net->stem_out, stem));
+  size_t gmax = stem;
+  int ch = h, cw = w;
+  for (auto& b : net->blocks) {
+    const int oh = (ch + 2 - 3) / b.stride + 1, ow = (cw + 2 - 3) / b.stride + 1;
+    const size_t no = (size_t)n * b.cout * oh * ow;
+    RNN_TRY(alloc_f(net, &b.y1, no));
+    RNN_TRY(alloc_f(net, &b.h1, no));
+    RNN_TRY(alloc_f(net, &b.y2, no));
+    RNN_TRY(alloc_f(net, &b.out, no));
+    if (b.down) RNN_TRY(alloc_f(net, &b.yd, no));
+    gmax = std::max(gmax, no);
+    gmax = std::max(gmax, (size_t)n * b.cin * ch * cw);
+    ch = oh;
+    cw = ow;
+  }
+  for (auto& p : net->gbuf) RNN_TRY(alloc_f(net, &p, gmax));
+  net->gbuf_elems = gmax;
+  RNN_TRY(alloc_f(net, &net->pooled, (size_t)n * net->fin));
+  RNN_TRY(alloc_f(net, &net->dpool, (size_t)n * net->fin));
+  RNN_TRY(alloc_f(net, &net->logits, (size_t)n * net->fout));
+  RNN_TRY(alloc_f(net, &net->dlogits, (size_t)n * net->fout));
+  RNN_TRY(alloc_f(net, &net->x_stage, (size_t)n * 3 * h * w));
+  float* lab = nullptr;
+  RNN_TRY(alloc_f(net, &lab, (size_t)n));
+  net->lab_stage = reinterpret_cast<uint32_t*>(lab);
+  net->scratch_bytes = bn_scratch_need(net, n);
+  float* scr = nullptr;
+  RNN_TRY(alloc_f(net, &scr, net->scratch_bytes / sizeof(float) + 1));
+  net->scratch = scr;
+  net->cap_n = n;
+  net->cap_h = h;
+  net->cap_w = w;
+  return RNN_OK;
+}
+
+// BN scratch layout inside net->scratch
+struct BnScratch {
+  double* part;
+  double* sums;
+  float* dgb;
+  float* row_loss;
+  int* hit;
+};
+
+static BnScratch bn_scratch(rnn_resnet* net, int n, int C) {
+  BnScratch s;
+  char* base = static_cast<char*>(net->scratch);
+  const int P = std::max(1, std::min(n, (4 * net->ctx->num_sms + C - 1) / C));
+  size_t a = ((size_t)C * P * 2 * sizeof(double) + 255) & ~(size_t)255;
+  size_t b = ((size_t)C * 2 * sizeof(double) + 255) & ~(size_t)255;
+  s.part = reinterpret_cast<double*>(base);
+  s.sums = reinterpret_cast<double*>(base + a);
+  s.dgb = reinterpret_cast<float*>(base + a + b);
+  // CE buffers live at the end of the scratch block
+  size_t ce = ((size_t)n * 4 + 255) & ~(size_t)255;
+  char* tail = base + net->scratch_bytes - 2 * ce - 1024;
+  s.row_loss = reinterpret_cast<float*>(tail);
+  s.hit = reinterpret_cast<int*>(tail + ce);
+  return s;
+}
+
+static int allreduce_sums(rnn_resnet* net, double* sums, int C) {
+  if (!net->comm || !net->sync_bn) return RNN_OK;
+  ncclResult_t r = ncclAllReduce(sums, sums, (size_t)C * 2, ncclDouble, ncclSum, net->comm, net->ctx->stream);
+  if (r != ncclSuccess) return set_error(RNN_ERR_NCCL, "SyncBN allreduce: %s", ncclGetErrorString(r));
+  return RNN_OK;
+}
+
+static int bn_forward(rnn_resnet* net, BNL& bn, const float* y, int n, int hw, bool train, bool relu,
+                      float* out) {
+  rnn_ctx* ctx = net->ctx;
+  float* gamma = net->v + bn.g_off;
+  float* beta = net->v + bn.b_off;
+  float* rm = net->bnbuf + bn.rm_off;
+  float* rv = rm + bn.c;
+  if (!train) return rnn_batchnorm_eval_dev(ctx, y, n, bn.c, hw, gamma, beta, rm, rv, 1e-5f, relu, out);
+  BnScratch s = bn_scratch(net, n, bn.c);
+  RNN_TRY(bn_fwd_sums(ctx, y, n, bn.c, hw, s.part, s.sums));
+  RNN_TRY(allreduce_sums(net, s.sums, bn.c));
+  const double count = (double)n * hw * (net->sync_bn ? net->world : 1);
+  return bn_fwd_finish(ctx, y, n, bn.c, hw, count, s.sums, gamma, beta, rm, rv, 0.1f, 1e-5f, relu ? 1 : 0,
+                       bn.mean, bn.invstd, out);
+}
+
+static int bn_backward(rnn_resnet* net, BNL& bn, const float* dy, const float* y, const float* relu_out, int n,
+                       int hw, float* dx) {
+  rnn_ctx* ctx = net->ctx;
+  BnScratch s = bn_scratch(net, n, bn.c);
+  RNN_TRY(bn_bwd_sums(ctx, dy, y, relu_out, n, bn.c, hw, bn.mean, bn.invstd, s.part, s.sums));
+  RNN_TRY(allreduce_sums(net, s.sums, bn.c));
+  const bool sb = net->sync_bn && net->comm;
+  const double count = (double)n * hw * (sb ? net->world : 1);
+  const float pscale = sb ? 1.0f / (float)net->world : 1.0f;
+  return bn_bwd_finish(ctx, dy, y, relu_out, n, bn.c, hw, count, s.sums, net->v + bn.g_off, bn.mean, bn.invstd,
+                       s.dgb, dx, net->g + bn.g_off, net->g + bn.b_off, pscale);
+}
+
+static int conv_forward(rnn_resnet* net, const ConvL& c, const float* x, int n, int h, int w, float* y) {
+  return tc::conv_fwd(net->ctx, x, n, c.cin, h, w, net->v + c.w_off, c.cout, c.k, c.stride, c.pad, y, false);
+}
+
+static int conv_backward(rnn_resnet* net, const ConvL& c, const float* x, const float* dy, int n, int h, int w,
+                         float* dx, bool dx_acc) {
+  // nn.rs:230-250: backward_w then dX
+  RNN_TRY(tc::conv_wgrad(net->ctx, x, dy, n, c.cin, h, w, c.cout, c.k, c.stride, c.pad, net->g + c.w_off, 0));
+  if (dx)
+    RNN_TRY(tc::conv_dgrad(net->ctx, dy, n, c.cin, h, w, net->v + c.w_off, c.cout, c.k, c.stride, c.pad, dx,
+                           dx_acc));
+  return RNN_OK;
+}
+
+static int resnet_forward(rnn_resnet* net, const float* x, int n, int h, int w, bool train, float* logits) {
+  RNN_TRY(ensure_acts(net, n, h, w));
+  // stem conv + BN + ReLU (model.rs:136)
+  RNN_TRY(conv_forward(net, net->stem, x, n, h, w, net->stem_y));
+  RNN_TRY(bn_forward(net, net->stem_bn, net->stem_y, n, h * w, train, true, net->stem_out));
+  const float* cur = net->stem_out;
+  int ch = h, cw = w;
+  for (auto& b : net->blocks) {
+    // model.rs:39-55
+    const int oh = (ch + 2 - 3) / b.stride + 1, ow = (cw + 2 - 3) / b.stride + 1;
+    const int ohw = oh * ow;
+    const size_t no = (size_t)n * b.cout * ohw;
+    b.x_in = cur;
+    b.n = n; b.h = ch; b.w = cw; b.oh = oh; b.ow = ow;
+    RNN_TRY(conv_forward(net, b.c1, cur, n, ch, cw, b.y1));
+    RNN_TRY(bn_forward(net, b.b1, b.y1, n, ohw, train, true, b.h1));
+    RNN_TRY(conv_forward(net, b.c2, b.h1, n, oh, ow, b.y2));
+    RNN_TRY(bn_forward(net, b.b2, b.y2, n, ohw, train, false, b.out));
+    if (b.down) {
+      RNN_TRY(conv_forward(net, b.cd, cur, n, ch, cw, b.yd));
+      float* s = net->gbuf[0];
+      RNN_TRY(bn_forward(net, b.bd, b.yd, n, ohw, train, false, s));
+      RNN_TRY(add(net->ctx, b.out, s, no, true));
+    } else {
+      RNN_TRY(add(net->ctx, b.out, cur, no, true));
+    }
+    cur = b.out;
+    ch = oh;
+    cw = ow;
+  }
+  net->n = n; net->h = h; net->w = w; net->fh = ch; net->fw = cw;
+  net->x_in = x;
+  RNN_TRY(gap_fwd(net->ctx, cur, n * net->fin, ch * cw, net->pooled));
+  RNN_TRY(fc_fwd(net->ctx, net->pooled, n, net->fin, net->fout, net->v + net->fcw_off, net->v + net->fcb_off,
+                 logits));
+  return RNN_OK;
+}
+
+static int resnet_backward(rnn_resnet* net, const float* dlogits) {
+  rnn_ctx* ctx = net->ctx;
+  const int n = net->n;
+  // model.rs:148-157
+  RNN_TRY(fc_bwd(ctx, net->pooled, dlogits, n, net->fin, net->fout, net->v + net->fcw_off, net->g + net->fcw_off,
+                 net->g + net->fcb_off, net->dpool));
+  int id = 0, it = 1, idm = 2, idx = 3;
+  float** G = net->gbuf;
+  RNN_TRY(gap_bwd(ctx, net->dpool, n * net->fin, net->fh * net->fw, G[id]));
+  for (int bi = (int)net->blocks.size() - 1; bi >= 0; bi--) {
+    Block& b = net->blocks[bi];
+    const int ohw = b.oh * b.ow;
+    const size_t no = (size_t)n * b.cout * ohw, ni = (size_t)n * b.cin * b.h * b.w;
+    float *d = G[id], *t = G[it], *dmain = G[idm], *dx = G[idx];
+    // model.rs:57-72
+    RNN_TRY(relu_back(ctx, d, b.out, no));
+    RNN_TRY(bn_backward(net, b.b2, d, b.y2, nullptr, n, ohw, t));
+    RNN_TRY(conv_backward(net, b.c2, b.h1, t, n, b.oh, b.ow, dmain, false));
+    RNN_TRY(bn_backward(net, b.b1, dmain, b.y1, b.h1, n, ohw, t));
+    RNN_TRY(conv_backward(net, b.c1, b.x_in, t, n, b.h, b.w, dx, false));
+    if (b.down) {
+      RNN_TRY(bn_backward(net, b.bd, d, b.yd, nullptr, n, ohw, t));
+      RNN_TRY(conv_backward(net, b.cd, b.x_in, t, n, b.h, b.w, dx, true));
+    } else {
+      RNN_TRY(add(ctx, dx, d, ni, false));
+    }
+    std::swap(id, idx);
+  }
+  // stem: relu_back, BN backward, dW only (model.rs:154-156)
+  const int hw = net->h * net->w;
+  float *d = G[id], *t = G[it];
+  RNN_TRY(bn_backward(net, net->stem_bn, d, net->stem_y, net->stem_out, n, hw, t));
+  RNN_TRY(conv_backward(net, net->stem, net->x_in, t, n, net->h, net->w, nullptr, false));
+  return RNN_OK;
+}
+
+static int resnet_step(rnn_resnet* net, float lr, float mom, float wd) {
+  const float gscale = net->comm ? 1.0f / (float)net->world : 1.0f;
+  return sgd_nesterov(net->ctx, net->v, net->g, net->m, net->decay, 0, net->nparams, lr, mom, wd, gscale);
+}
+
+static int allreduce_grads(rnn_resnet* net) {
+  if (!net->comm || net->world <= 1) return RNN_OK;
+  ncclResult_t r = ncclAllReduce(net->g, net->g, net->nparams, ncclFloat, ncclSum, net->comm, net->ctx->stream);
+  if (r != ncclSuccess) return set_error(RNN_ERR_NCCL, "gradient allreduce: %s", ncclGetErrorString(r));
+  return RNN_OK;
+}
+
+static int train_step(rnn_resnet* net, const float* x, const uint32_t* labels, int n, float smooth, float lr,
+                      float mom, float wd, float* loss, int* correct) {
+  RNN_TRY(resnet_forward(net, x, n, 32, 32, true, net->logits));
+  BnScratch s = bn_scratch(net, n, 1);
+  RNN_TRY(softmax_ce(net->ctx, net->logits, labels, n, net->fout, smooth, net->dlogits, s.row_loss, s.hit, loss,
+                     correct));
+  RNN_TRY(resnet_backward(net, net->dlogits));
+  RNN_TRY(allreduce_grads(net));
+  return resnet_step(net, lr, mom, wd);
+}
+
+}  // namespace rnn
+
+// ==================================================================== C ABI
+
+extern "C" int rnn_resnet_create(rnn_ctx* ctx, int depth_n, int width, int nclass, uint64_t seed,
+                                 rnn_resnet** out) {
+  RNN_REQUIRE(ctx && out, "resnet_create: null argument");
+  RNN_REQUIRE(depth_n >= 1 && width >= 1 && nclass >= 1, "resnet_create: bad config");
+  *out = nullptr;
+  rnn_resnet* net = new rnn_resnet();
+  net->ctx = ctx;
+  net->depth_n = depth_n;
+  net->width = width;
+  net->nclass = nclass;
+
+  // ---- layout in for_each_param order (model.rs:159-168, :74-86)
+  size_t off = 0, boff = 0;
+  std::vector<size_t> sizes;
+  std::vector<uint8_t> dec;
+  auto take = [&](size_t n, bool decay) {
+    size_t o = off;
+    off += n;
+    sizes.push_back(n);
+    dec.push_back(decay ? 1 : 0);
+    return o;
+  };
+  auto mk_conv = [&](ConvL& c, int cin, int cout, int k, int stride, int pad) {
+    c.cin = cin; c.cout = cout; c.k = k; c.stride = stride; c.pad = pad;
+    c.w_off = take((size_t)cout * cin * k * k, true);  // Param::kaiming: decay
+  };
+  auto mk_bn = [&](BNL& b, int c) {
+    b.c = c;
+    b.g_off = take(c, false);
+    b.b_off = take(c, false);
+    b.rm_off = boff;
+    boff += 2 * (size_t)c;
+  };
+  mk_conv(net->stem, 3, width, 3, 1, 1);
+  mk_bn(net->stem_bn, width);
+  const int widths[3] = {width, width * 2, width * 4};
+  int cin = width;
+  for (int s = 0; s < 3; s++)
+    for (int bb = 0; bb < depth_n; bb++) {
+      Block b;
+      b.stride = (s > 0 && bb == 0) ? 2 : 1;
+      b.cin = cin;
+      b.cout = widths[s];
+      b.down = b.stride != 1 || cin != b.cout;
+      mk_conv(b.c1, cin, b.cout, 3, b.stride, 1);
+      mk_bn(b.b1, b.cout);
+      mk_conv(b.c2, b.cout, b.cout, 3, 1, 1);
+      mk_bn(b.b2, b.cout);
+      if (b.down) {
+        mk_conv(b.cd, cin, b.cout, 1, b.stride, 0);
+        mk_bn(b.bd, b.cout);
+      }
+      net->blocks.push_back(b);
+      cin = b.cout;
+    }
+  net->fin = width * 4;
+  net->fout = nclass;
+  net->fcw_off = take((size_t)net->fin * nclass, true);
+  net->fcb_off = take(nclass, false);
+  net->nparams = off;
+  net->nbuf = boff;
+
+  // ---- initial values, drawn in ResNet::new order (model.rs:112-133):
+  // every block (c1, c2, shortcut conv) first, then the stem, then the
+  // classifier (nn.rs:487-498, halved); BN gamma 1 (0 for each block's bn2,
+  // model.rs:22-23), beta 0.
+  std::vector<float> hv(net->nparams, 0.0f);
+  Rng rng(seed);
+  auto kaiming = [&](const ConvL& c) {
+    const float s = sqrtf(2.0f / (float)(c.cin * c.k * c.k));
+    const size_t n = (size_t)c.cout * c.cin * c.k * c.k;
+    for (size_t i = 0; i < n; i++) hv[c.w_off + i] = rng.normal() * s;
+  };
+  auto bn_init = [&](const BNL& b, float gamma) {
+    for (int i = 0; i < b.c; i++) hv[b.g_off + i] = gamma;
+  };
+  for (auto& b : net->blocks) {
+    kaiming(b.c1);
+    kaiming(b.c2);
+    if (b.down) kaiming(b.cd);
+    bn_init(b.b1, 1.0f);
+    bn_init(b.b2, 0.0f);
+    if (b.down) bn_init(b.bd, 1.0f);
+  }
+  kaiming(net->stem);
+  bn_init(net->stem_bn, 1.0f);
+  {
+    const float s = sqrtf(2.0f / (float)net->fin);
+    for (size_t i = 0; i < (size_t)net->fin * nclass; i++) hv[net->fcw_off + i] = rng.normal() * s * 0.5f;
+  }
+
+  // ---- device state
+  net->decay_host.resize(net->nparams);
+  {
+    size_t o = 0;
+    for (size_t i = 0; i < sizes.size(); i++) {
+      memset(net->decay_host.data() + o, dec[i], sizes[i]);
+      o += sizes[i];
+    }
+  }
+  auto fail = [&](int code) {
+    rnn_resnet_destroy(net);
+    return code;
+  };
+  if (cudaMalloc(&net->v, net->nparams * 4) != cudaSuccess || cudaMalloc(&net->g, net->nparams * 4) != cudaSuccess ||
+      cudaMalloc(&net->m, net->nparams * 4) != cudaSuccess || cudaMalloc(&net->decay, net->nparams) != cudaSuccess ||
+      cudaMalloc(&net->bnbuf, net->nbuf * 4) != cudaSuccess)
+    return fail(set_error(RNN_ERR_CUDA, "resnet_create: out of device memory"));
+  // mean/invstd of every BN
+  size_t nstat = 0;
+  nstat += 2 * (size_t)net->stem_bn.c;
+  for (auto& b : net->blocks) nstat += 2 * (size_t)(b.b1.c + b.b2.c + (b.down ? b.bd.c : 0));
+  if (cudaMalloc(&net->bnstat, nstat * 4) != cudaSuccess)
+    return fail(set_error(RNN_ERR_CUDA, "resnet_create: out of device memory"));
+  {
+    float* p = net->bnstat;
+    auto assign = [&](BNL& b) {
+      b.mean = p;
+      b.invstd = p + b.c;
+      p += 2 * b.c;
+    };
+    assign(net->stem_bn);
+    for (auto& b : net->blocks) {
+      assign(b.b1);
+      assign(b.b2);
+      if (b.down) assign(b.bd);
+    }
+  }
+  std::vector<float> hb(net->nbuf);
+  {
+    // running mean 0, running var 1 (nn.rs:271-272)
+    auto fillb = [&](const BNL& b) {
+      for (int i = 0; i < b.c; i++) {
+        hb[b.rm_off + i] = 0.0f;
+        hb[b.rm_off + b.c + i] = 1.0f;
+      }
+    };
+    fillb(net->stem_bn);
+    for (auto& b : net->blocks) {
+      fillb(b.b1);
+      fillb(b.b2);
+      if (b.down) fillb(b.bd);
+    }
+  }
+  if (cudaMemcpy(net->v, hv.data(), net->nparams * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemset(net->g, 0, net->nparams * 4) != cudaSuccess || cudaMemset(net->m, 0, net->nparams * 4) != cudaSuccess ||
+      cudaMemcpy(net->decay, net->decay_host.data(), net->nparams, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(net->bnbuf, hb.data(), net->nbuf * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+    return fail(set_error(RNN_ERR_CUDA, "resnet_create: upload failed"));
+  if (cudaMalloc(&net->loss_dev, 4) != cudaSuccess || cudaMalloc(&net->correct_dev, 4) != cudaSuccess)
+    return fail(set_error(RNN_ERR_CUDA, "resnet_create: out of device memory"));
+  *out = net;
+  return RNN_OK;
+}
+
+extern "C" int rnn_resnet_destroy(rnn_resnet* net) {
+  if (!net) return RNN_OK;
+  if (net->ctx) cudaStreamSynchronize(net->ctx->stream);
+  free_acts(net);
+  cudaFree(net->v);
+  cudaFree(net->g);
+  cudaFree(net->m);
+  cudaFree(net->decay);
+  cudaFree(net->bnbuf);
+  cudaFree(net->bnstat);
+  cudaFree(net->loss_dev);
+  cudaFree(net->correct_dev);
+  if (net->comm) ncclCommDestroy(net->comm);
+  delete net;
+  return RNN_OK;
+}
+
+extern "C" int rnn_resnet_num_params(rnn_resnet* net, size_t* out) {
+  RNN_REQUIRE(net && out, "null argument");
+  *out = net->nparams;
+  return RNN_OK;
+}
+
+extern "C" int rnn_resnet_num_buffers(rnn_resnet* net, size_t* out) {
+  RNN_REQUIRE(net && out, "null argument");
+  *out = net->nbuf;
+  return RNN_OK;
+}
+
+static int copy_out(rnn_resnet* net, float* dst, const float* src, size_t n) {
+  RNN_CUDA(cudaStreamSynchronize(net->ctx->stream));
+  RNN_CUDA(cudaMemcpy(dst, src, n * 4, cudaMemcpyDeviceToHost));
+  return RNN_OK;
+}
+
+extern "C" int rnn_resnet_get_params(rnn_resnet* net, float* out) {
+  RNN_REQUIRE(net && out, "null argument");
+  return copy_out(net, out, net->v, net->nparams);
+}
+extern "C" int rnn_resnet_get_grads(rnn_resnet* net, float* out) {
+  RNN_REQUIRE(net && out, "null argument");
+  return copy_out(net, out, net->g, net->nparams);
+}
+extern "C" int rnn_resnet_get_moments(rnn_resnet* net, float* out) {
+  RNN_REQUIRE(net && out, "null argument");
+  return copy_out(net, out, net->m, net->nparams);
+}
+extern "C" int rnn_resnet_get_buffers(rnn_resnet* net, float* out) {
+  RNN_REQUIRE(net && out, "null argument");
+  return copy_out(net, out, net->bnbuf, net->nbuf);
+}
+extern "C" int rnn_resnet_set_params(rnn_resnet* net, const float* in) {
+  RNN_REQUIRE(net && in, "null argument");
+  RNN_CUDA(cudaStreamSynchronize(net->ctx->stream));
+  RNN_CUDA(cudaMemcpy(net->v, in, net->nparams * 4, cudaMemcpyHostToDevice));
+  return RNN_OK;
+}
+extern "C" int rnn_resnet_grad_buffer(rnn_resnet* net, float** out, size_t* len) {
+  RNN_REQUIRE(net && out && len, "null argument");
+  *out = net->g;
+  *len = net->nparams;
+  return RNN_OK;
+}
+
+extern "C" int rnn_resnet_forward_dev(rnn_resnet* net, const float* x, int n, int h, int w, int train,
+                                      float* logits) {
+  RNN_REQUIRE(net && x && logits, "resnet_forward: null argument");
+  RNN_REQUIRE(n > 0 && h > 0 && w > 0, "resnet_forward: bad shape");
+  return resnet_forward(net, x, n, h, w, train != 0, logits);
+}
+
+extern "C" int rnn_resnet_backward_dev(rnn_resnet* net, const float* dlogits) {
+  RNN_REQUIRE(net && dlogits, "resnet_backward: null argument");
+  RNN_REQUIRE(net->n > 0, "resnet_backward: no forward pass recorded");
+  return resnet_backward(net, dlogits);
+}
+
+extern "C" int rnn_resnet_step(rnn_resnet* net, float lr, float mom, float wd) {
+  RNN_REQUIRE(net, "null argument");
+  return resnet_step(net, lr, mom, wd);
+}
+
+extern "C" int rnn_resnet_train_step_dev(rnn_resnet* net, const float* x, const uint32_t* labels, int n,
+                                         float smooth, float lr, float mom, float wd, float* loss, int* correct) {
+  RNN_REQUIRE(net && x && labels, "train_step: null argument");
+  RNN_REQUIRE(n > 0, "train_step: empty batch");
+  return train_step(net, x, labels, n, smooth, lr, mom, wd, loss ? loss : net->loss_dev,
+                    correct ? correct : net->correct_dev);
+}
+
+extern "C" int rnn_resnet_train_step(rnn_resnet* net, const float* x, const uint32_t* labels, int n, float smooth,
+                                     float lr, float mom, float wd, float* loss, int* correct) {
+  RNN_REQUIRE(net && x && labels, "train_step: null argument");
+  RNN_REQUIRE(n > 0, "train_step: empty batch");
+  rnn_ctx* ctx = net->ctx;
+  RNN_TRY(ensure_acts(net, n, 32, 32));
+  RNN_CUDA(cudaMemcpyAsync(net->x_stage, x, (size_t)n * 3 * 32 * 32 * 4, cudaMemcpyHostToDevice, ctx->stream));
+  RNN_CUDA(cudaMemcpyAsync(net->lab_stage, labels, (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream));
+  RNN_TRY(train_step(net, net->x_stage, net->lab_stage, n, smooth, lr, mom, wd, net->loss_dev, net->correct_dev));
+  float l = 0.0f;
+  int c = 0;
+  RNN_CUDA(cudaMemcpyAsync(&l, net->loss_dev, 4, cudaMemcpyDeviceToHost, ctx->stream));
+  RNN_CUDA(cudaMemcpyAsync(&c, net->correct_dev, 4, cudaMemcpyDeviceToHost, ctx->stream));
+  RNN_TRY(rnn_ctx_synchronize(ctx));
+  if (loss) *loss = l;
+  if (correct) *correct = c;
+  return RNN_OK;
+}
+
+// ---------------------------------------------------------------- DP
+
+extern "C" int rnn_dp_unique_id(unsigned char* uid_out) {
+  RNN_REQUIRE(uid_out, "null argument");
+  static_assert(sizeof(ncclUniqueId) == RNN_UID_BYTES, "uid size");
+  ncclUniqueId id;
+  ncclResult_t r = ncclGetUniqueId(&id);
+  if (r != ncclSuccess) return set_error(RNN_ERR_NCCL, "ncclGetUniqueId: %s", ncclGetErrorString(r));
+  memcpy(uid_out, &id, sizeof(id));
+  return RNN_OK;
+}
+
+extern "C" int rnn_resnet_dp_init(rnn_resnet* net, int rank, int world, const unsigned char* uid, int sync_bn) {
+  RNN_REQUIRE(net && uid, "null argument");
+  RNN_REQUIRE(world >= 1 && rank >= 0 && rank < world, "dp_init: bad rank/world");
+  if (net->comm) {
+    ncclCommDestroy(net->comm);
+    net->comm = nullptr;
+  }
+  ncclUniqueId id;
+  memcpy(&id, uid, sizeof(id));
+  RNN_CUDA(cudaSetDevice(net->ctx->device));
+  ncclResult_t r = ncclCommInitRank(&net->comm, world, id, rank);
+  if (r != ncclSuccess) return set_error(RNN_ERR_NCCL, "ncclCommInitRank: %s", ncclGetErrorString(r));
+  net->rank = rank;
+  net->world = world;
+  net->sync_bn = sync_bn != 0;
+  return RNN_OK;
+}

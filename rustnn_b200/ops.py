@@ -1,0 +1,220 @@
+"""Operator-level API over the C ABI, mirroring the reference's Rust calls.
+
+Tensors are torch CUDA float32 tensors (torch is used only for device memory
+and streams).  Every op runs on the current torch stream, through a context
+bound to it, and raises ``RnnError`` on any failure; there is no CPU path.
+
+Reference interfaces mirrored here:
+  matmul      gemm.rs:434-444 (C (+)= op(A) op(B))
+  gemm_small  gemm.rs:500-512 (same contract; no packing scratch needed)
+  matmul_dw   gemm.rs:555     (C += A^T B)
+  conv2d_*    nn.rs:166/193/230 (Conv2d forward / backward_w / backward)
+  batchnorm_* nn.rs:290-427
+  softmax_ce  nn.rs:615-637
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from ._lib import CTX, RnnError, call, check, lib
+
+__all__ = [
+    "Context", "default_context", "matmul", "gemm_small", "matmul_dw", "conv2d_forward", "conv2d_dgrad",
+    "conv2d_wgrad", "batchnorm_forward", "batchnorm_eval", "batchnorm_backward", "relu_back_", "add_",
+    "add_relu_", "gap_forward", "gap_backward", "softmax_ce", "sgd_nesterov_", "out_dim", "RnnError",
+]
+
+
+class Context:
+    """An rnn_ctx on one device (its stream follows torch's current stream)."""
+
+    def __init__(self, device: int = 0):
+        if not torch.cuda.is_available():
+            raise RnnError("rustnn_b200 needs a CUDA device (sm_100a); there is no CPU fallback")
+        self.device = device
+        h = CTX()
+        with torch.cuda.device(device):
+            check(lib().rnn_ctx_create(C.byref(h), device), "rnn_ctx_create")
+        self.h = h
+        self._stream = None
+
+    def bind(self):
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        if s != self._stream:
+            call("rnn_ctx_set_stream", self.h, C.c_void_p(s))
+            self._stream = s
+        return self.h
+
+    def synchronize(self):
+        call("rnn_ctx_synchronize", self.h)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().rnn_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_ctx = {}
+
+
+def default_context(device=None) -> Context:
+    if device is None:
+        device = torch.cuda.current_device()
+    if device not in _ctx:
+        _ctx[device] = Context(device)
+    return _ctx[device]
+
+
+def _ptr(t: torch.Tensor, name: str):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dtype != torch.float32 and t.dtype != torch.int32:
+        raise RnnError(f"{name}: expected a CUDA float32 tensor")
+    if not t.is_contiguous():
+        raise RnnError(f"{name}: tensor must be contiguous")
+    return C.c_void_p(t.data_ptr())
+
+
+def _ctx_of(t: torch.Tensor, ctx):
+    c = ctx or default_context(t.device.index)
+    return c.bind()
+
+
+def out_dim(h: int, k: int, stride: int, pad: int) -> int:
+    """nn.rs:148-150."""
+    return (h + 2 * pad - k) // stride + 1
+
+
+# ---------------------------------------------------------------- gemm.rs
+
+
+def matmul(m, n, k, a, at, b, bt, c, acc=False, ctx=None):
+    """C[m x n] (+)= op(A) op(B) (gemm.rs:434)."""
+    call("rnn_gemm_dev", _ctx_of(c, ctx), m, n, k, _ptr(a, "a"), int(bool(at)), _ptr(b, "b"), int(bool(bt)),
+         _ptr(c, "c"), int(bool(acc)))
+    return c
+
+
+gemm_small = matmul  # gemm.rs:500: same contract; batching happens inside the engine
+
+
+def matmul_dw(m, n, k, a, b, c, ctx=None):
+    """C[m x n] += A^T B, A [k x m], B [k x n] (gemm.rs:555)."""
+    call("rnn_gemm_dw_dev", _ctx_of(c, ctx), m, n, k, _ptr(a, "a"), _ptr(b, "b"), _ptr(c, "c"))
+    return c
+
+
+# ---------------------------------------------------------------- conv
+
+
+def conv2d_forward(x, w, n, cin, h, wd, cout, k, stride, pad, y=None, acc=False, ctx=None):
+    oh, ow = out_dim(h, k, stride, pad), out_dim(wd, k, stride, pad)
+    if y is None:
+        y = torch.empty(n * cout * oh * ow, device=x.device, dtype=torch.float32)
+    call("rnn_conv2d_fwd_dev", _ctx_of(x, ctx), _ptr(x, "x"), n, cin, h, wd, _ptr(w, "w"), cout, k, stride, pad,
+         _ptr(y, "y"), int(bool(acc)))
+    return y
+
+
+def conv2d_dgrad(dy, w, n, cin, h, wd, cout, k, stride, pad, dx=None, acc=False, ctx=None):
+    if dx is None:
+        dx = torch.empty(n * cin * h * wd, device=dy.device, dtype=torch.float32)
+    call("rnn_conv2d_dgrad_dev", _ctx_of(dy, ctx), _ptr(dy, "dy"), n, cin, h, wd, _ptr(w, "w"), cout, k, stride,
+         pad, _ptr(dx, "dx"), int(bool(acc)))
+    return dx
+
+
+def conv2d_wgrad(x, dy, n, cin, h, wd, cout, k, stride, pad, dw=None, ctx=None):
+    """dw += dy im2col(x)^T (accumulates, like nn.rs:226)."""
+    if dw is None:
+        dw = torch.zeros(cout * cin * k * k, device=x.device, dtype=torch.float32)
+    call("rnn_conv2d_wgrad_dev", _ctx_of(x, ctx), _ptr(x, "x"), _ptr(dy, "dy"), n, cin, h, wd, cout, k, stride,
+         pad, _ptr(dw, "dw"))
+    return dw
+
+
+# ---------------------------------------------------------------- BatchNorm
+
+
+def batchnorm_forward(y, n, c, hw, gamma, beta, rmean, rvar, relu, mom=0.1, eps=1e-5, out=None, ctx=None):
+    """Returns (out, mean, invstd); rmean/rvar updated in place."""
+    if out is None:
+        out = torch.empty_like(y)
+    mean = torch.empty(c, device=y.device, dtype=torch.float32)
+    invstd = torch.empty(c, device=y.device, dtype=torch.float32)
+    call("rnn_batchnorm_fwd_dev", _ctx_of(y, ctx), _ptr(y, "y"), n, c, hw, _ptr(gamma, "gamma"),
+         _ptr(beta, "beta"), _ptr(rmean, "rmean"), _ptr(rvar, "rvar"), mom, eps, int(bool(relu)), _ptr(mean, "mean"),
+         _ptr(invstd, "invstd"), _ptr(out, "out"))
+    return out, mean, invstd
+
+
+def batchnorm_eval(y, n, c, hw, gamma, beta, rmean, rvar, relu, eps=1e-5, out=None, ctx=None):
+    if out is None:
+        out = torch.empty_like(y)
+    call("rnn_batchnorm_eval_dev", _ctx_of(y, ctx), _ptr(y, "y"), n, c, hw, _ptr(gamma, "gamma"), _ptr(beta, "beta"),
+         _ptr(rmean, "rmean"), _ptr(rvar, "rvar"), eps, int(bool(relu)), _ptr(out, "out"))
+    return out
+
+
+def batchnorm_backward(dy, y, n, c, hw, gamma, mean, invstd, dgamma, dbeta, relu_out=None, dx=None, ctx=None):
+    if dx is None:
+        dx = torch.empty_like(dy)
+    ro = _ptr(relu_out, "relu_out") if relu_out is not None else None
+    call("rnn_batchnorm_bwd_dev", _ctx_of(dy, ctx), _ptr(dy, "dy"), _ptr(y, "y"), n, c, hw, _ptr(gamma, "gamma"),
+         _ptr(mean, "mean"), _ptr(invstd, "invstd"), ro, _ptr(dx, "dx"), _ptr(dgamma, "dgamma"), _ptr(dbeta, "dbeta"))
+    return dx
+
+
+# ---------------------------------------------------------------- glue
+
+
+def relu_back_(d, y, ctx=None):
+    call("rnn_relu_back_dev", _ctx_of(d, ctx), _ptr(d, "d"), _ptr(y, "y"), d.numel())
+    return d
+
+
+def add_(a, b, ctx=None):
+    call("rnn_add_dev", _ctx_of(a, ctx), _ptr(a, "a"), _ptr(b, "b"), a.numel())
+    return a
+
+
+def add_relu_(a, b, ctx=None):
+    call("rnn_add_relu_dev", _ctx_of(a, ctx), _ptr(a, "a"), _ptr(b, "b"), a.numel())
+    return a
+
+
+def gap_forward(x, nc, hw, ctx=None):
+    y = torch.empty(nc, device=x.device, dtype=torch.float32)
+    call("rnn_gap_fwd_dev", _ctx_of(x, ctx), _ptr(x, "x"), nc, hw, _ptr(y, "y"))
+    return y
+
+
+def gap_backward(dy, nc, hw, ctx=None):
+    dx = torch.empty(nc * hw, device=dy.device, dtype=torch.float32)
+    call("rnn_gap_bwd_dev", _ctx_of(dy, ctx), _ptr(dy, "dy"), nc, hw, _ptr(dx, "dx"))
+    return dx
+
+
+def softmax_ce(logits, labels, nclass, smooth, ctx=None):
+    """Returns (loss tensor[1], dlogits, correct tensor[1]) (nn.rs:615-637)."""
+    n = labels.numel()
+    lab = labels.to(torch.int32).contiguous()
+    d = torch.empty_like(logits)
+    loss = torch.empty(1, device=logits.device, dtype=torch.float32)
+    corr = torch.empty(1, device=logits.device, dtype=torch.int32)
+    call("rnn_softmax_ce_dev", _ctx_of(logits, ctx), _ptr(logits, "logits"), _ptr(lab, "labels"), n, nclass, smooth,
+         _ptr(d, "dlogits"), _ptr(loss, "loss"), _ptr(corr, "correct"))
+    return loss, d, corr
+
+
+def sgd_nesterov_(v, g, m, lr, mom, wd, decay, ctx=None):
+    """Param::step (nn.rs:102-110); g is zeroed."""
+    call("rnn_sgd_nesterov_dev", _ctx_of(v, ctx), _ptr(v, "v"), _ptr(g, "g"), _ptr(m, "m"), v.numel(), lr, mom, wd,
+         int(bool(decay)))
+    return v

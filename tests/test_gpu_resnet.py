@@ -1,0 +1,143 @@
+"""GPU parity of the whole ResNet training step against the CPU oracle, plus
+the reference's gradcheck (check.rs:727-770) run against the GPU backend."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-4
+
+
+def rel(got, want):
+    got = np.asarray(got, np.float64).ravel()
+    want = np.asarray(want, np.float64).ravel()
+    den = np.linalg.norm(want)
+    return float(np.linalg.norm(got - want) / (den if den > 0 else 1.0))
+
+
+def dev(a, dtype=np.float32):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype)).cuda()
+
+
+@pytest.fixture(scope="module")
+def M():
+    from rustnn_b200 import model
+
+    return model
+
+
+def images(rng, n, hw=32):
+    """Uniform bytes normalised like the BASELINE synthetic data."""
+    u = np.array([rng.below(256) for _ in range(n * 3 * hw * hw)], np.float32)
+    return ((u - 127.5) / 73.9).astype(np.float32)
+
+
+@pytest.mark.parametrize("depth_n,width,nclass,seed", [(1, 4, 10, 1234), (3, 32, 100, 0), (2, 16, 100, 7)])
+def test_init_bit_exact(M, depth_n, width, nclass, seed):
+    """ResNet::new draws (model.rs:112-133) reproduce the reference's init."""
+    g = M.ResNet(depth_n, width, nclass, seed)
+    o = O.ResNet(depth_n, width, nclass, seed)
+    assert g.nparams == o.num_params()
+    assert np.array_equal(g.params(), o.params())
+    assert np.array_equal(g.buffers(), o.buffers())
+
+
+def _tensor_slices(o):
+    sizes, _ = o.param_info()
+    offs = np.concatenate([[0], np.cumsum(sizes)])
+    return [(int(offs[i]), int(offs[i + 1])) for i in range(len(sizes))]
+
+
+def test_resnet8_forward_backward(M):
+    """The gradcheck fixture (check.rs:731-750): ResNet-8 w4, 16x16, batch 8."""
+    NC, BS, seed = 10, 8, 1234
+    g = M.ResNet(1, 4, NC, seed)
+    o = O.ResNet(1, 4, NC, seed)
+    rng = O.Rng(seed ^ 0x5EED)
+    p = (o.params() + np.float32(0.3) * rng.rand_vec(o.num_params())).astype(np.float32)
+    o.set_params(p)
+    g.set_params(p)
+    x = rng.rand_vec(BS * 3 * 16 * 16)
+    labels = np.array([rng.below(NC) for _ in range(BS)], np.uint32)
+    lo = o.forward(x, BS, hw=16, train=True)
+    xd = dev(x)
+    lg = g.forward(xd, BS, hw=16, train=True)
+    torch.cuda.synchronize()
+    assert rel(lg.cpu().numpy(), lo) < TOL
+    _, dl, _ = O.softmax_ce(lo, labels, NC, 0.0)
+    o.zero_grads()
+    o.backward(dl)
+    g.backward(dev(dl))
+    gg, go = g.grads(), o.grads()
+    assert rel(gg, go) < TOL
+    for a, b in _tensor_slices(o):
+        if np.linalg.norm(go[a:b]) > 1e-3:
+            assert rel(gg[a:b], go[a:b]) < 1e-3, (a, b, rel(gg[a:b], go[a:b]))
+    assert rel(g.buffers(), o.buffers()) < 1e-5
+
+
+def test_resnet20_train_steps(M):
+    """BASELINE config 2 geometry (ResNet-20 W=32) at batch 16, two SGD steps."""
+    n, seed = 16, 0
+    g = M.ResNet(3, 32, 100, seed)
+    o = O.ResNet(3, 32, 100, seed)
+    rng = O.Rng(42)
+    for step in range(2):
+        x = images(rng, n)
+        labels = np.array([rng.below(100) for _ in range(n)], np.uint32)
+        lo, co = o.train_step(x, labels, smooth=0.1, lr=0.2, mom=0.9, wd=5e-4)
+        loss, corr = g.train_step(dev(x), dev(labels.astype(np.int32), np.int32), smooth=0.1, lr=0.2, mom=0.9,
+                                  wd=5e-4)
+        torch.cuda.synchronize()
+        assert abs(float(loss.item()) - lo) <= 1e-4 * abs(lo)
+    assert rel(g.params(), o.params()) < TOL
+    assert rel(g.moments(), o.moments()) < TOL
+    assert rel(g.buffers(), o.buffers()) < TOL
+    assert np.all(g.grads() == 0)  # Param::step zeroes the gradient
+
+
+def test_host_tier_train_step_matches_device_tier(M):
+    n = 8
+    a = M.ResNet(1, 8, 10, 3)
+    b = M.ResNet(1, 8, 10, 3)
+    rng = O.Rng(1)
+    x = images(rng, n)
+    labels = np.array([rng.below(10) for _ in range(n)], np.uint32)
+    la, _ = a.train_step_host(x, labels)
+    lb, _ = b.train_step(dev(x), dev(labels.astype(np.int32), np.int32))
+    torch.cuda.synchronize()
+    assert la == pytest.approx(float(lb.item()), rel=1e-6)
+    assert np.array_equal(a.params(), b.params())
+
+
+def test_resnet_gradcheck_on_gpu(M):
+    """check.rs:727-770 with the GPU backend computing every loss and grad."""
+    from rustnn_b200 import ops
+
+    NC, BS, seed, eps = 10, 8, 1234, 3e-4
+    net = M.ResNet(1, 4, NC, seed)
+    rng = O.Rng(seed ^ 0x5EED)
+    p = (net.params() + np.float32(0.3) * rng.rand_vec(net.nparams)).astype(np.float32)
+    net.set_params(p)
+    x = dev(rng.rand_vec(BS * 3 * 16 * 16))
+    labels = dev(np.array([rng.below(NC) for _ in range(BS)], np.int32), np.int32)
+    logits = net.forward(x, BS, hw=16, train=True)
+    _, dl, _ = ops.softmax_ce(logits, labels, NC, 0.0)
+    net.backward(dl)
+    grad = net.grads()
+
+    def lossf(c):
+        net.set_params(c)
+        lg = net.forward(x, BS, hw=16, train=True)
+        return float(ops.softmax_ce(lg, labels, NC, 0.0)[0].item())
+
+    v = rng.rand_vec(p.size)
+    lp = lossf((p + np.float32(eps) * v).astype(np.float32))
+    lm = lossf((p - np.float32(eps) * v).astype(np.float32))
+    num = (lp - lm) / (2 * eps)
+    ana = float(np.dot(grad.astype(np.float64), v.astype(np.float64)))
+    err = abs(num - ana) / (abs(num) + abs(ana) + 1e-6)
+    assert err < 5e-3, err  # check.rs:42-44
