@@ -47,9 +47,12 @@ int rnn_device_ok(int device);
 /* ---- context ------------------------------------------------------------ */
 int rnn_ctx_create(rnn_ctx **out, int device);
 int rnn_ctx_destroy(rnn_ctx *ctx);
-/* Use an external stream (e.g. the caller's framework stream) instead of the
- * context's own; pass NULL to go back to the context's stream. */
+/* Enqueue on `cuda_stream` (e.g. the caller's framework stream; NULL is the
+ * legacy default stream) instead of the context's own stream.  Work already
+ * queued on the previous stream is waited for first. */
 int rnn_ctx_set_stream(rnn_ctx *ctx, void *cuda_stream);
+/* Go back to the context's own (non-blocking) stream. */
+int rnn_ctx_use_own_stream(rnn_ctx *ctx);
 void *rnn_ctx_stream(rnn_ctx *ctx);
 /* Waits for the stream and reports kernel timeouts as RNN_ERR_DEVICE. */
 int rnn_ctx_synchronize(rnn_ctx *ctx);

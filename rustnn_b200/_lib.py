@@ -41,6 +41,7 @@ SIGS = {
     "rnn_ctx_create": [C.POINTER(CTX), I],
     "rnn_ctx_destroy": [CTX],
     "rnn_ctx_set_stream": [CTX, P],
+    "rnn_ctx_use_own_stream": [CTX],
     "rnn_ctx_stream": [CTX],
     "rnn_ctx_synchronize": [CTX],
     "rnn_gemm_dev": [CTX, I, I, I, FP, I, FP, I, FP, I],

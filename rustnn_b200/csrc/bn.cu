@@ -199,6 +199,9 @@ static unsigned ew_grid(size_t total, int num_sms) {
 
 int bn_fwd_sums(rnn_ctx* ctx, const float* y, int n, int C, int hw, double* part, double* sums) {
   const int P = bn_parts(n, C, ctx->num_sms);
+  RNN_RANGE(y, sizeof(float) * (size_t)n * C * hw);
+  RNN_RANGE(part, sizeof(double) * (size_t)C * P * 2);
+  RNN_RANGE(sums, sizeof(double) * (size_t)C * 2);
   bn_fwd_partial_kernel<<<dim3(C, P), BN_NT, 0, ctx->stream>>>(y, n, C, hw, P, part);
   RNN_CHECK_LAUNCH();
   bn_combine_kernel<<<(C + 127) / 128, 128, 0, ctx->stream>>>(part, C, P, sums);
@@ -209,6 +212,15 @@ int bn_fwd_sums(rnn_ctx* ctx, const float* y, int n, int C, int hw, double* part
 int bn_fwd_finish(rnn_ctx* ctx, const float* y, int n, int C, int hw, double count, const double* sums,
                   const float* gamma, const float* beta, float* rmean, float* rvar, float mom, float eps,
                   int relu, float* mean, float* invstd, float* out) {
+  RNN_RANGE(sums, sizeof(double) * (size_t)C * 2);
+  RNN_RANGE(mean, sizeof(float) * C);
+  RNN_RANGE(invstd, sizeof(float) * C);
+  if (rmean) RNN_RANGE(rmean, sizeof(float) * C);
+  if (rvar) RNN_RANGE(rvar, sizeof(float) * C);
+  RNN_RANGE(gamma, sizeof(float) * C);
+  RNN_RANGE(beta, sizeof(float) * C);
+  RNN_RANGE(y, sizeof(float) * (size_t)n * C * hw);
+  RNN_RANGE(out, sizeof(float) * (size_t)n * C * hw);
   bn_finalize_kernel<<<(C + 127) / 128, 128, 0, ctx->stream>>>(sums, C, count, mom, eps, mean, invstd,
                                                                 rmean, rvar);
   RNN_CHECK_LAUNCH();
@@ -222,6 +234,13 @@ int bn_fwd_finish(rnn_ctx* ctx, const float* y, int n, int C, int hw, double cou
 int bn_bwd_sums(rnn_ctx* ctx, const float* dy, const float* y, const float* relu_out, int n, int C, int hw,
                 const float* mean, const float* invstd, double* part, double* sums) {
   const int P = bn_parts(n, C, ctx->num_sms);
+  RNN_RANGE(dy, sizeof(float) * (size_t)n * C * hw);
+  RNN_RANGE(y, sizeof(float) * (size_t)n * C * hw);
+  if (relu_out) RNN_RANGE(relu_out, sizeof(float) * (size_t)n * C * hw);
+  RNN_RANGE(mean, sizeof(float) * C);
+  RNN_RANGE(invstd, sizeof(float) * C);
+  RNN_RANGE(part, sizeof(double) * (size_t)C * P * 2);
+  RNN_RANGE(sums, sizeof(double) * (size_t)C * 2);
   bn_bwd_partial_kernel<<<dim3(C, P), BN_NT, 0, ctx->stream>>>(dy, y, relu_out, n, C, hw, P, mean,
                                                                invstd, part);
   RNN_CHECK_LAUNCH();
@@ -234,6 +253,12 @@ int bn_bwd_finish(rnn_ctx* ctx, const float* dy, const float* y, const float* re
                   double count, const double* sums, const float* gamma, const float* mean,
                   const float* invstd, float* dgb /* [2C] scratch */, float* dx, float* dgamma,
                   float* dbeta, float pscale) {
+  RNN_RANGE(sums, sizeof(double) * (size_t)C * 2);
+  RNN_RANGE(dgb, sizeof(float) * (size_t)C * 2);
+  if (dgamma) RNN_RANGE(dgamma, sizeof(float) * C);
+  if (dbeta) RNN_RANGE(dbeta, sizeof(float) * C);
+  RNN_RANGE(gamma, sizeof(float) * C);
+  RNN_RANGE(dx, sizeof(float) * (size_t)n * C * hw);
   bn_bwd_finalize_kernel<<<(C + 127) / 128, 128, 0, ctx->stream>>>(sums, C, dgb, dgb + C, dgamma, dbeta,
                                                                     pscale);
   RNN_CHECK_LAUNCH();
@@ -278,6 +303,10 @@ extern "C" int rnn_batchnorm_eval_dev(rnn_ctx* ctx, const float* y, int n, int c
   RNN_REQUIRE(ctx && y && gamma && beta && rmean && rvar && out, "batchnorm_eval: null argument");
   const size_t total = (size_t)n * c * hw;
   if (total == 0) return RNN_OK;
+  RNN_RANGE(y, total * sizeof(float));
+  RNN_RANGE(out, total * sizeof(float));
+  RNN_RANGE(rmean, c * sizeof(float));
+  RNN_RANGE(rvar, c * sizeof(float));
   bn_eval_kernel<<<ew_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(y, c, hw, total, gamma, beta, rmean,
                                                                          rvar, eps, relu, out);
   RNN_CHECK_LAUNCH();

@@ -1,5 +1,7 @@
 // Context, error reporting and the host-pointer tier of the C ABI.
+#include <cuda.h>
 #include <stdarg.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -10,6 +12,61 @@ namespace rnn {
 
 static thread_local char g_err[1024] = "";
 unsigned long long g_launches = 0;
+
+static int env_flag(const char* name) {
+  const char* v = getenv(name);
+  return v && v[0] && v[0] != '0';
+}
+
+bool range_checks_enabled() {
+  static const int on = env_flag("RNN_CHECK_RANGES");
+  return on != 0;
+}
+
+bool debug_sync_enabled() {
+  static const int on = env_flag("RNN_DEBUG_SYNC");
+  return on != 0;
+}
+
+typedef CUresult (*GetRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+static GetRangeFn get_range_fn() {
+  static GetRangeFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<GetRangeFn>(p);
+  }
+  return fn;
+}
+
+int check_range(const void* p, size_t bytes, const char* what, const char* file, int line) {
+  if (bytes == 0) return RNN_OK;
+  if (p == nullptr) return set_error(RNN_ERR_ARG, "%s:%d: %s is null but %zu bytes are accessed", file, line, what, bytes);
+  GetRangeFn fn = get_range_fn();
+  if (!fn) return set_error(RNN_ERR_CUDA, "range check: cuMemGetAddressRange unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  CUresult r = fn(&base, &size, reinterpret_cast<CUdeviceptr>(p));
+  if (r != CUDA_SUCCESS)
+    return set_error(RNN_ERR_ARG, "%s:%d: %s = %p is not in a device allocation (CUresult %d)", file, line, what, p,
+                     (int)r);
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  if (a + bytes > (uintptr_t)base + size)
+    return set_error(RNN_ERR_ARG, "%s:%d: %s = %p + %zu bytes overruns its allocation [%p, +%zu)", file, line, what,
+                     p, bytes, (void*)base, size);
+  return RNN_OK;
+}
+
+int debug_sync_check(const char* file, int line) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return set_error(RNN_ERR_CUDA, "%s:%d: kernel failed: %s", file, line, cudaGetErrorString(e));
+  return RNN_OK;
+}
 
 int set_error(int code, const char* fmt, ...) {
   va_list ap;
@@ -75,16 +132,16 @@ extern "C" int rnn_ctx_create(rnn_ctx** out, int device) {
   rnn_ctx* ctx = new rnn_ctx();
   ctx->device = device;
   ctx->num_sms = p.multiProcessorCount;
-  cudaError_t e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+  cudaError_t e = cudaStreamCreateWithFlags(&ctx->own, cudaStreamNonBlocking);
   if (e != cudaSuccess) {
     delete ctx;
     return set_error(RNN_ERR_CUDA, "stream create: %s", cudaGetErrorString(e));
   }
-  ctx->own_stream = true;
+  ctx->stream = ctx->own;
   e = cudaMalloc(&ctx->dev_error, sizeof(int));
   if (e == cudaSuccess) e = cudaMemset(ctx->dev_error, 0, sizeof(int));
   if (e != cudaSuccess) {
-    cudaStreamDestroy(ctx->stream);
+    cudaStreamDestroy(ctx->own);
     delete ctx;
     return set_error(RNN_ERR_CUDA, "ctx alloc: %s", cudaGetErrorString(e));
   }
@@ -95,31 +152,28 @@ extern "C" int rnn_ctx_create(rnn_ctx** out, int device) {
 extern "C" int rnn_ctx_destroy(rnn_ctx* ctx) {
   if (!ctx) return RNN_OK;
   cudaSetDevice(ctx->device);
-  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  cudaStreamSynchronize(ctx->stream);
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->stage) cudaFree(ctx->stage);
   if (ctx->dev_error) cudaFree(ctx->dev_error);
-  if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
+  if (ctx->own) cudaStreamDestroy(ctx->own);
   delete ctx;
   return RNN_OK;
 }
 
 extern "C" int rnn_ctx_set_stream(rnn_ctx* ctx, void* stream) {
   RNN_REQUIRE(ctx != nullptr, "null context");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (s == ctx->stream) return RNN_OK;
+  // work already queued on the old stream finishes before the switch
   RNN_CUDA(cudaStreamSynchronize(ctx->stream));
-  if (stream == nullptr) {
-    if (!ctx->own_stream) {
-      RNN_CUDA(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
-      ctx->own_stream = true;
-    }
-    return RNN_OK;
-  }
-  if (ctx->own_stream) {
-    RNN_CUDA(cudaStreamDestroy(ctx->stream));
-    ctx->own_stream = false;
-  }
-  ctx->stream = static_cast<cudaStream_t>(stream);
+  ctx->stream = s;
   return RNN_OK;
+}
+
+extern "C" int rnn_ctx_use_own_stream(rnn_ctx* ctx) {
+  RNN_REQUIRE(ctx != nullptr, "null context");
+  return rnn_ctx_set_stream(ctx, ctx->own);
 }
 
 extern "C" void* rnn_ctx_stream(rnn_ctx* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
@@ -131,7 +185,9 @@ extern "C" int rnn_ctx_synchronize(rnn_ctx* ctx) {
   RNN_CUDA(cudaMemcpy(&err, ctx->dev_error, sizeof(int), cudaMemcpyDeviceToHost));
   if (err) {
     RNN_CUDA(cudaMemset(ctx->dev_error, 0, sizeof(int)));
-    return set_error(RNN_ERR_DEVICE, "a kernel gave up waiting on a pipeline barrier (device error 0x%x)", err);
+    return set_error(RNN_ERR_DEVICE, "device error 0x%x (%s%s)", err,
+                     (err & 1) ? "a kernel gave up waiting on a pipeline barrier " : "",
+                     (err & 2) ? "a label is >= nclass" : "");
   }
   return RNN_OK;
 }

@@ -25,16 +25,37 @@ int set_error(int code, const char* fmt, ...);
 
 // Every kernel launch of the library is followed by RNN_CHECK_LAUNCH(), which
 // also counts it (rnn_launch_count()).
+// With RNN_DEBUG_SYNC=1 it also waits for the kernel and names the launch
+// site of a failing kernel.
 extern unsigned long long g_launches;
-#define RNN_CHECK_LAUNCH()                                   \
-  do {                                                       \
-    __atomic_add_fetch(&::rnn::g_launches, 1ull, __ATOMIC_RELAXED); \
-    RNN_CUDA(cudaGetLastError());                            \
+bool debug_sync_enabled();
+int debug_sync_check(const char* file, int line);
+#define RNN_CHECK_LAUNCH()                                                \
+  do {                                                                    \
+    __atomic_add_fetch(&::rnn::g_launches, 1ull, __ATOMIC_RELAXED);       \
+    RNN_CUDA(cudaGetLastError());                                         \
+    if (::rnn::debug_sync_enabled()) {                                    \
+      int d__ = ::rnn::debug_sync_check(__FILE__, __LINE__);             \
+      if (d__ != RNN_OK) return d__;                                      \
+    }                                                                     \
   } while (0)
 
 #define RNN_REQUIRE(cond, ...)                                  \
   do {                                                          \
     if (!(cond)) return ::rnn::set_error(RNN_ERR_ARG, __VA_ARGS__); \
+  } while (0)
+
+// Launch-argument validation (enabled with RNN_CHECK_RANGES=1): every device
+// range a launch will touch must lie inside one live device allocation; a
+// violation is reported as RNN_ERR_ARG and the launch is not made.
+bool range_checks_enabled();
+int check_range(const void* p, size_t bytes, const char* what, const char* file, int line);
+#define RNN_RANGE(p, bytes)                                                          \
+  do {                                                                               \
+    if (::rnn::range_checks_enabled()) {                                             \
+      int r__ = ::rnn::check_range((const void*)(p), (size_t)(bytes), #p, __FILE__, __LINE__); \
+      if (r__ != RNN_OK) return r__;                                                 \
+    }                                                                                \
   } while (0)
 
 #define RNN_TRY(expr)          \
@@ -46,7 +67,8 @@ extern unsigned long long g_launches;
 // Device-side error word.  Kernels with bounded waits OR in a code instead of
 // hanging; the host reads it at rnn_ctx_synchronize().
 enum DeviceError : int {
-  DEV_ERR_TIMEOUT = 1,
+  DEV_ERR_TIMEOUT = 1,  // a pipeline wait gave up
+  DEV_ERR_LABEL = 2,    // softmax_ce saw a label >= nclass
 };
 
 }  // namespace rnn
@@ -54,8 +76,8 @@ enum DeviceError : int {
 struct rnn_ctx {
   int device = 0;
   int num_sms = 148;
-  cudaStream_t stream = nullptr;
-  bool own_stream = false;
+  cudaStream_t stream = nullptr;  // stream every call enqueues on
+  cudaStream_t own = nullptr;     // the context's own stream
   // growable device workspace (split-K partials, BN partial sums, host-API
   // staging).  Reused across calls: all users run in stream order.
   void* ws = nullptr;

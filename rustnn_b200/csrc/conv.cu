@@ -255,6 +255,15 @@ struct ConvWgradProb {
 
 // ---------------------------------------------------------------- launch
 
+// Device bytes each conv operand spans (range checks).
+struct ConvSpans {
+  size_t x, w, y;
+};
+static inline ConvSpans spans(const ConvGeom& g, int k) {
+  return {sizeof(float) * (size_t)g.n * g.cin * g.h * g.w, sizeof(float) * (size_t)g.cout * g.cin * k * k,
+          sizeof(float) * (size_t)g.n * g.cout * g.oh * g.ow};
+}
+
 template <int BN>
 struct ConvLauncher {
   template <class P>
@@ -274,6 +283,7 @@ struct WgradLauncher {
     if (s.splits > 1) {
       RNN_TRY(ensure_ws(ctx, sizeof(float) * (size_t)s.splits * prob.M * prob.N));
       prob.ws = static_cast<float*>(ctx->ws);
+      RNN_RANGE(prob.ws, sizeof(float) * (size_t)s.splits * prob.M * prob.N);
     }
     RNN_TRY(launch<BN>(ctx, prob, s));
     if (s.splits > 1)
@@ -311,6 +321,10 @@ int conv_fwd(rnn_ctx* ctx, const float* x, int n, int cin, int h, int w, const f
   ConvGeom g;
   RNN_TRY(check_geom(n, cin, h, w, cout, k, stride, pad, &g));
   if (n == 0) return RNN_OK;
+  const ConvSpans sp = spans(g, k);
+  RNN_RANGE(x, sp.x);
+  RNN_RANGE(wt, sp.w);
+  RNN_RANGE(y, sp.y);
   const int M = n * g.oh * g.ow, N = cout, K = cin * k * k;
   const int bn = pick_bn(N, (M + BM - 1) / BM, ctx->num_sms);
   auto fill = [&](auto& p) {
@@ -331,6 +345,10 @@ int conv_dgrad(rnn_ctx* ctx, const float* dy, int n, int cin, int h, int w, cons
   ConvGeom g;
   RNN_TRY(check_geom(n, cin, h, w, cout, k, stride, pad, &g));
   if (n == 0) return RNN_OK;
+  const ConvSpans sp = spans(g, k);
+  RNN_RANGE(dy, sp.y);
+  RNN_RANGE(wt, sp.w);
+  RNN_RANGE(dx, sp.x);
   const int M = n * h * w, N = cin, K = cout * k * k;
   const int bn = pick_bn(N, (M + BM - 1) / BM, ctx->num_sms);
   auto fill = [&](auto& p) {
@@ -350,6 +368,10 @@ int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, in
   ConvGeom g;
   RNN_TRY(check_geom(n, cin, h, w, cout, k, stride, pad, &g));
   if (n == 0) return RNN_OK;
+  const ConvSpans sp = spans(g, k);
+  RNN_RANGE(x, sp.x);
+  RNN_RANGE(dy, sp.y);
+  RNN_RANGE(dw, sp.w);
   const int M = cin * k * k, N = cout, K = n * g.oh * g.ow;
   const int bn = pick_bn(N, (M + BM - 1) / BM, ctx->num_sms);
   const int splits = force_splits > 0 ? force_splits : pick_splits(M, N, K, bn, ctx->num_sms);

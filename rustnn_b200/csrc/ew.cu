@@ -57,6 +57,8 @@ static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) =
 int relu_back(rnn_ctx* ctx, float* d, const float* y, size_t n) {
   if (n == 0) return RNN_OK;
   RNN_REQUIRE(al16(d) && al16(y), "relu_back: pointers must be 16-byte aligned");
+  RNN_RANGE(d, n * sizeof(float));
+  RNN_RANGE(y, n * sizeof(float));
   relu_back_kernel<<<grid_for(n / 4 + 1, ctx->num_sms), 256, 0, ctx->stream>>>(d, y, n);
   RNN_CHECK_LAUNCH();
   return RNN_OK;
@@ -65,6 +67,8 @@ int relu_back(rnn_ctx* ctx, float* d, const float* y, size_t n) {
 int add(rnn_ctx* ctx, float* a, const float* b, size_t n, bool relu) {
   if (n == 0) return RNN_OK;
   RNN_REQUIRE(al16(a) && al16(b), "add: pointers must be 16-byte aligned");
+  RNN_RANGE(a, n * sizeof(float));
+  RNN_RANGE(b, n * sizeof(float));
   add_kernel<<<grid_for(n / 4 + 1, ctx->num_sms), 256, 0, ctx->stream>>>(a, b, n, relu ? 1 : 0);
   RNN_CHECK_LAUNCH();
   return RNN_OK;
@@ -93,6 +97,8 @@ __global__ void gap_bwd_kernel(const float* __restrict__ dy, int nc, int hw, flo
 
 int gap_fwd(rnn_ctx* ctx, const float* x, int nc, int hw, float* y) {
   if (nc == 0) return RNN_OK;
+  RNN_RANGE(x, sizeof(float) * (size_t)nc * hw);
+  RNN_RANGE(y, sizeof(float) * (size_t)nc);
   gap_fwd_kernel<<<(nc * 32 + 255) / 256, 256, 0, ctx->stream>>>(x, nc, hw, y);
   RNN_CHECK_LAUNCH();
   return RNN_OK;
@@ -100,6 +106,8 @@ int gap_fwd(rnn_ctx* ctx, const float* x, int nc, int hw, float* y) {
 
 int gap_bwd(rnn_ctx* ctx, const float* dy, int nc, int hw, float* dx) {
   if (nc == 0) return RNN_OK;
+  RNN_RANGE(dy, sizeof(float) * (size_t)nc);
+  RNN_RANGE(dx, sizeof(float) * (size_t)nc * hw);
   gap_bwd_kernel<<<grid_for((size_t)nc * hw, ctx->num_sms), 256, 0, ctx->stream>>>(dy, nc, hw, dx);
   RNN_CHECK_LAUNCH();
   return RNN_OK;
@@ -153,6 +161,10 @@ __global__ void fc_bwd_x_kernel(const float* __restrict__ dy, int n, int fin, in
 int fc_fwd(rnn_ctx* ctx, const float* x, int n, int fin, int fout, const float* w, const float* b, float* y) {
   const long warps = (long)n * fout;
   if (warps == 0) return RNN_OK;
+  RNN_RANGE(x, sizeof(float) * (size_t)n * fin);
+  RNN_RANGE(w, sizeof(float) * (size_t)fout * fin);
+  RNN_RANGE(b, sizeof(float) * (size_t)fout);
+  RNN_RANGE(y, sizeof(float) * (size_t)n * fout);
   fc_fwd_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, ctx->stream>>>(x, n, fin, fout, w, b, y);
   RNN_CHECK_LAUNCH();
   return RNN_OK;
@@ -161,6 +173,12 @@ int fc_fwd(rnn_ctx* ctx, const float* x, int n, int fin, int fout, const float* 
 int fc_bwd(rnn_ctx* ctx, const float* x, const float* dy, int n, int fin, int fout, const float* w, float* dw,
            float* db, float* dx) {
   const int nw = std::max(fout * fin, fout);
+  RNN_RANGE(x, sizeof(float) * (size_t)n * fin);
+  RNN_RANGE(dy, sizeof(float) * (size_t)n * fout);
+  RNN_RANGE(w, sizeof(float) * (size_t)fout * fin);
+  RNN_RANGE(dw, sizeof(float) * (size_t)fout * fin);
+  RNN_RANGE(db, sizeof(float) * (size_t)fout);
+  if (dx) RNN_RANGE(dx, sizeof(float) * (size_t)n * fin);
   fc_bwd_w_kernel<<<(nw + 255) / 256, 256, 0, ctx->stream>>>(x, dy, n, fin, fout, dw, db);
   RNN_CHECK_LAUNCH();
   if (dx) {
@@ -175,12 +193,24 @@ int fc_bwd(rnn_ctx* ctx, const float* x, const float* dy, int n, int fin, int fo
 // one warp per example; nn.rs:588-613.  row_loss[i], hit[i] written.
 __global__ void softmax_ce_rows_kernel(const float* __restrict__ logits, const uint32_t* __restrict__ labels,
                                        int n, int nclass, float smooth, float inv, float* __restrict__ d,
-                                       float* __restrict__ row_loss, int* __restrict__ hit) {
+                                       float* __restrict__ row_loss, int* __restrict__ hit, int* dev_error) {
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, l = threadIdx.x & 31;
   if (i >= n) return;
   const float* z = logits + (size_t)i * nclass;
   float* dr = d + (size_t)i * nclass;
-  const int y = (int)labels[i];
+  const uint32_t yl = labels[i];
+  if (yl >= (uint32_t)nclass) {
+    // out-of-range label: the reference panics on the slice index; flag it
+    // (RNN_ERR_DEVICE at the next synchronise) and contribute nothing
+    if (l == 0) {
+      atomicOr(dev_error, 2);
+      row_loss[i] = NAN;
+      hit[i] = 0;
+    }
+    for (int j = l; j < nclass; j += 32) dr[j] = NAN;
+    return;
+  }
+  const int y = (int)yl;
   // argmax with the lowest index on ties (nn.rs:573-583 keeps the first max)
   float mx = -INFINITY;
   int arg = 0x7fffffff;
@@ -249,9 +279,16 @@ __global__ void softmax_ce_total_kernel(const float* __restrict__ row_loss, cons
 int softmax_ce(rnn_ctx* ctx, const float* logits, const uint32_t* labels, int n, int nclass, float smooth,
                float* dlogits, float* row_loss, int* hit, float* loss_out, int* correct_out) {
   if (n == 0) return RNN_OK;
+  RNN_RANGE(logits, sizeof(float) * (size_t)n * nclass);
+  RNN_RANGE(labels, sizeof(uint32_t) * (size_t)n);
+  RNN_RANGE(dlogits, sizeof(float) * (size_t)n * nclass);
+  RNN_RANGE(row_loss, sizeof(float) * (size_t)n);
+  RNN_RANGE(hit, sizeof(int) * (size_t)n);
+  if (loss_out) RNN_RANGE(loss_out, sizeof(float));
+  if (correct_out) RNN_RANGE(correct_out, sizeof(int));
   const float inv = 1.0f / (float)n;
   softmax_ce_rows_kernel<<<(n * 32 + 255) / 256, 256, 0, ctx->stream>>>(logits, labels, n, nclass, smooth, inv,
-                                                                        dlogits, row_loss, hit);
+                                                                        dlogits, row_loss, hit, ctx->dev_error);
   RNN_CHECK_LAUNCH();
   softmax_ce_total_kernel<<<1, 256, 0, ctx->stream>>>(row_loss, hit, n, inv, loss_out, correct_out);
   RNN_CHECK_LAUNCH();
@@ -280,6 +317,10 @@ __global__ void sgd_kernel(float* __restrict__ v, float* __restrict__ g, float* 
 int sgd_nesterov(rnn_ctx* ctx, float* v, float* g, float* m, const uint8_t* decay_mask, int decay_all, size_t n,
                  float lr, float mom, float wd, float gscale) {
   if (n == 0) return RNN_OK;
+  RNN_RANGE(v, n * sizeof(float));
+  RNN_RANGE(g, n * sizeof(float));
+  RNN_RANGE(m, n * sizeof(float));
+  if (decay_mask) RNN_RANGE(decay_mask, n);
   sgd_kernel<<<grid_for(n, ctx->num_sms, 8), 256, 0, ctx->stream>>>(v, g, m, decay_mask, decay_all, n, lr, mom,
                                                                      wd, gscale);
   RNN_CHECK_LAUNCH();

@@ -80,7 +80,11 @@ struct DenseLauncher {
     if (s.splits > 1) {
       RNN_TRY(ensure_ws(ctx, sizeof(float) * (size_t)s.splits * prob.M * prob.N));
       prob.ws = static_cast<float*>(ctx->ws);
+      RNN_RANGE(prob.ws, sizeof(float) * (size_t)s.splits * prob.M * prob.N);
     }
+    RNN_RANGE(prob.a, sizeof(float) * (size_t)prob.M * prob.K);
+    RNN_RANGE(prob.b, sizeof(float) * (size_t)prob.N * prob.K);
+    RNN_RANGE(prob.c, sizeof(float) * (size_t)prob.M * prob.N);
     RNN_TRY(launch<BN>(ctx, prob, s));
     if (s.splits > 1)
       RNN_TRY(launch_splitk_reduce(ctx, prob.ws, prob.c, prob.M, prob.N, s.splits, prob.acc != 0,
@@ -126,6 +130,7 @@ int gemm_dev(rnn_ctx* ctx, int m, int n, int k, const float* a, bool at, const f
   if (k == 0) {  // gemm.rs:449-453
     if (!acc) {
       size_t len = (size_t)m * n;
+      RNN_RANGE(c, len * sizeof(float));
       zero_kernel<<<(unsigned)std::min<size_t>((len + 255) / 256, 4096), 256, 0, ctx->stream>>>(c, len);
       RNN_CHECK_LAUNCH();
     }
@@ -183,6 +188,8 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, float* __rest
 int launch_splitk_reduce(rnn_ctx* ctx, const float* ws, float* out, int rows, int cols, int splits,
                          bool acc, bool transpose) {
   size_t total = (size_t)rows * cols;
+  RNN_RANGE(ws, total * splits * sizeof(float));
+  RNN_RANGE(out, total * sizeof(float));
   unsigned grid;
   if (transpose) grid = (unsigned)std::min<size_t>(((rows + 31) / 32) * (size_t)((cols + 31) / 32), 4096);
   else grid = (unsigned)std::min<size_t>((total + 255) / 256, (size_t)ctx->num_sms * 8);

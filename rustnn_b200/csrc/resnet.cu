@@ -324,6 +324,8 @@ static int allreduce_grads(rnn_resnet* net) {
 
 static int train_step(rnn_resnet* net, const float* x, const uint32_t* labels, int n, float smooth, float lr,
                       float mom, float wd, float* loss, int* correct) {
+  // allocate first: net->logits / dlogits / scratch exist only after this
+  RNN_TRY(ensure_acts(net, n, 32, 32));
   RNN_TRY(resnet_forward(net, x, n, 32, 32, true, net->logits));
   BnScratch s = bn_scratch(net, n, 1);
   RNN_TRY(softmax_ce(net->ctx, net->logits, labels, n, net->fout, smooth, net->dlogits, s.row_loss, s.hit, loss,

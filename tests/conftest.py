@@ -4,6 +4,9 @@ import sys
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+# Every launch made by the tests validates its device ranges on the host first
+# (an extent bug is refused with RNN_ERR_ARG instead of faulting the GPU).
+os.environ.setdefault("RNN_CHECK_RANGES", "1")
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
