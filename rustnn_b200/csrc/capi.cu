@@ -106,6 +106,21 @@ int ensure_stage(rnn_ctx* ctx, size_t bytes) {
   return RNN_OK;
 }
 
+int ensure_pack(rnn_ctx* ctx, size_t bytes) {
+  if (bytes <= ctx->pack_bytes) return RNN_OK;
+  size_t want = std::max(bytes, ctx->pack_bytes * 2);
+  want = (want + (1 << 20) - 1) & ~(size_t)((1 << 20) - 1);
+  if (ctx->pack) {
+    RNN_CUDA(cudaStreamSynchronize(ctx->stream));
+    RNN_CUDA(cudaFree(ctx->pack));
+    ctx->pack = nullptr;
+    ctx->pack_bytes = 0;
+  }
+  RNN_CUDA(cudaMalloc(&ctx->pack, want));
+  ctx->pack_bytes = want;
+  return RNN_OK;
+}
+
 }  // namespace rnn
 
 using namespace rnn;
@@ -155,6 +170,7 @@ extern "C" int rnn_ctx_destroy(rnn_ctx* ctx) {
   cudaStreamSynchronize(ctx->stream);
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->stage) cudaFree(ctx->stage);
+  if (ctx->pack) cudaFree(ctx->pack);
   if (ctx->dev_error) cudaFree(ctx->dev_error);
   if (ctx->own) cudaStreamDestroy(ctx->own);
   delete ctx;

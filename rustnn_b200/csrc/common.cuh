@@ -86,6 +86,9 @@ struct rnn_ctx {
   // host-API staging buffer
   void* stage = nullptr;
   size_t stage_bytes = 0;
+  // packed B-operand images (weights in the MMA's shared-memory layout)
+  void* pack = nullptr;
+  size_t pack_bytes = 0;
 };
 
 namespace rnn {
@@ -93,4 +96,5 @@ namespace rnn {
 // growing so no in-flight kernel still reads the old buffer.
 int ensure_ws(rnn_ctx* ctx, size_t bytes);
 int ensure_stage(rnn_ctx* ctx, size_t bytes);
+int ensure_pack(rnn_ctx* ctx, size_t bytes);
 }  // namespace rnn

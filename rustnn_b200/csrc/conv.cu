@@ -253,6 +253,268 @@ struct ConvWgradProb {
   }
 };
 
+// ---------------------------------------------------------------- fast paths
+//
+// When the contracted channel count is a multiple of 32, fwd and dgrad order
+// K tap-major: k = tap * C + c, so one 32-wide K block is one (kh, kw) tap
+// over 32 consecutive channels.  A producer thread owns one output row
+// (pixel); per K block it resolves the tap's input position and validity
+// once and then issues 32 loads strided by one channel plane (each warp load
+// covers 32 consecutive pixels).  The weights go through pack_b_kernel into
+// the MMA's shared-memory image and are streamed with cp.async.bulk.
+
+template <int KS, int BN>
+struct FastConvFwd {
+  static constexpr bool B_BULK = true;
+  static constexpr int KK = KS * KS;
+  const float* x;
+  float* y;
+  const float* bpack;
+  ConvGeom g;
+  int M, N;
+  int CB;  // channel blocks of 32 per tap
+  int kblocks;
+  int acc;
+  int splits;
+
+  struct TS {
+    const float* xb;
+    int iy0, ix0;
+    bool ok;
+  };
+  __device__ __forceinline__ void tile_begin(TS& ts, int m0, int, int gt) const {
+    const int row = m0 + gt;
+    ts.ok = row < M;
+    const int ohw = g.oh * g.ow;
+    const int r = ts.ok ? row : 0;
+    const int img = r / ohw, rem = r - img * ohw;
+    const int oy = rem / g.ow, ox = rem - oy * g.ow;
+    ts.iy0 = oy * g.stride - g.pad;
+    ts.ix0 = ox * g.stride - g.pad;
+    ts.xb = x + (size_t)img * g.cin * g.h * g.w;
+  }
+  static __device__ __forceinline__ void a_slot(int gt, int j, int& r, int& c) { r = gt; c = j; }
+  __device__ __forceinline__ void load_a(const TS& ts, int kb, int, float (&v)[32]) const {
+    const int tap = kb / CB, cb = kb - tap * CB;
+    const int kh = tap / KS, kw = tap - kh * KS;
+    const int iy = ts.iy0 + kh, ix = ts.ix0 + kw;
+    const bool valid = ts.ok && iy >= 0 && iy < g.h && ix >= 0 && ix < g.w;
+    const int hw = g.h * g.w;
+    const float* p = ts.xb + (size_t)(cb * 32) * hw + (valid ? iy * g.w + ix : 0);
+#pragma unroll
+    for (int j = 0; j < 32; j++) v[j] = valid ? __ldg(p + (size_t)j * hw) : 0.0f;
+  }
+  __device__ __forceinline__ const void* b_src(int nt, int kb) const {
+    return bpack + ((size_t)nt * kblocks + kb) * (2 * BN * BK);
+  }
+  __device__ __forceinline__ void store(int row, int col0, int, const float (&v)[32]) const {
+    if (row >= M) return;
+    const int ohw = g.oh * g.ow;
+    const int img = row / ohw, rem = row - img * ohw;
+    float* yp = y + ((size_t)img * g.cout) * ohw + rem;
+#pragma unroll
+    for (int j = 0; j < 32; j++) {
+      const int co = col0 + j;
+      if (co < N) {
+        float* q = yp + (size_t)co * ohw;
+        *q = acc ? *q + v[j] : v[j];
+      }
+    }
+  }
+};
+
+// B(co, k = tap*cin + ci) = W[co][ci][tap]
+struct PackFwdSrc {
+  const float* w;
+  int cout, cin, kk;
+  __device__ __forceinline__ float operator()(int co, int k) const {
+    const int tap = k / cin, ci = k - tap * cin;
+    return (co < cout && tap < kk) ? __ldg(w + ((size_t)co * cin + ci) * kk + tap) : 0.0f;
+  }
+};
+
+template <int KS, int BN>
+struct FastConvDgrad {
+  static constexpr bool B_BULK = true;
+  static constexpr int KK = KS * KS;
+  const float* dy;
+  float* dx;
+  const float* bpack;
+  ConvGeom g;
+  int M, N;
+  int CB;  // cout blocks of 32 per tap
+  int kblocks;
+  int acc;
+  int splits;
+
+  struct TS {
+    const float* dyb;
+    int ty0, tx0;  // iy + pad, ix + pad
+    bool ok;
+  };
+  __device__ __forceinline__ void tile_begin(TS& ts, int m0, int, int gt) const {
+    const int row = m0 + gt;
+    ts.ok = row < M;
+    const int hw = g.h * g.w;
+    const int r = ts.ok ? row : 0;
+    const int img = r / hw, rem = r - img * hw;
+    const int iy = rem / g.w, ix = rem - iy * g.w;
+    ts.ty0 = iy + g.pad;
+    ts.tx0 = ix + g.pad;
+    ts.dyb = dy + (size_t)img * g.cout * g.oh * g.ow;
+  }
+  static __device__ __forceinline__ void a_slot(int gt, int j, int& r, int& c) { r = gt; c = j; }
+  __device__ __forceinline__ void load_a(const TS& ts, int kb, int, float (&v)[32]) const {
+    const int tap = kb / CB, cb = kb - tap * CB;
+    const int kh = tap / KS, kw = tap - kh * KS;
+    const int ty = ts.ty0 - kh, tx = ts.tx0 - kw;
+    int oy, ox;
+    bool valid = ts.ok && ty >= 0 && tx >= 0;
+    if (g.stride == 1) {
+      oy = ty; ox = tx;
+    } else {
+      oy = ty / g.stride; ox = tx / g.stride;
+      valid = valid && oy * g.stride == ty && ox * g.stride == tx;
+    }
+    valid = valid && oy < g.oh && ox < g.ow;
+    const int ohw = g.oh * g.ow;
+    const float* p = ts.dyb + (size_t)(cb * 32) * ohw + (valid ? oy * g.ow + ox : 0);
+#pragma unroll
+    for (int j = 0; j < 32; j++) v[j] = valid ? __ldg(p + (size_t)j * ohw) : 0.0f;
+  }
+  __device__ __forceinline__ const void* b_src(int nt, int kb) const {
+    return bpack + ((size_t)nt * kblocks + kb) * (2 * BN * BK);
+  }
+  __device__ __forceinline__ void store(int row, int col0, int, const float (&v)[32]) const {
+    if (row >= M) return;
+    const int hw = g.h * g.w;
+    const int img = row / hw, rem = row - img * hw;
+    float* xp = dx + ((size_t)img * g.cin) * hw + rem;
+#pragma unroll
+    for (int j = 0; j < 32; j++) {
+      const int ci = col0 + j;
+      if (ci < N) {
+        float* q = xp + (size_t)ci * hw;
+        *q = acc ? *q + v[j] : v[j];
+      }
+    }
+  }
+};
+
+// B(ci, k = tap*cout + co) = W[co][ci][tap]
+struct PackDgradSrc {
+  const float* w;
+  int cout, cin, kk;
+  __device__ __forceinline__ float operator()(int ci, int k) const {
+    const int tap = k / cout, co = k - tap * cout;
+    return (ci < cin && tap < kk) ? __ldg(w + ((size_t)co * cin + ci) * kk + tap) : 0.0f;
+  }
+};
+
+// wgrad: M = (ci, kh, kw) rows, N = cout, K = pixels, when every group of 4
+// consecutive pixels lies in one output row (ow % 4 == 0).  A producer
+// thread owns 4 consecutive pixels of 8 rows; it decodes the pixel block once
+// per K block and the 8 rows once per tile.  dY is read with 16-byte loads.
+template <int KS>
+struct FastConvWgrad {
+  static constexpr bool B_BULK = false;
+  static constexpr int KK = KS * KS;
+  const float* x;
+  const float* dy;
+  float* dw;
+  float* ws;
+  ConvGeom g;
+  int M, N, K;
+  int splits;
+
+  struct TS {
+    int rowoff[8];  // ci*H*W + (kh-pad)*W + (kw-pad)
+    int dkh[8], dkw[8];
+    uint32_t rok;   // bit j: row j in range
+    int n0;
+  };
+  __device__ __forceinline__ void tile_begin(TS& ts, int m0, int n0, int gt) const {
+    ts.rok = 0;
+    ts.n0 = n0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int row = m0 + (gt >> 3) + 16 * j;
+      const int r = row < M ? row : 0;
+      const int ci = r / KK, kk = r - ci * KK;
+      const int kh = kk / KS, kw = kk - kh * KS;
+      ts.dkh[j] = kh - g.pad;
+      ts.dkw[j] = kw - g.pad;
+      ts.rowoff[j] = ci * g.h * g.w + ts.dkh[j] * g.w + ts.dkw[j];
+      if (row < M) ts.rok |= 1u << j;
+    }
+  }
+  static __device__ __forceinline__ void a_slot(int gt, int j, int& r, int& c) {
+    r = (gt >> 3) + 16 * j;
+    c = gt & 7;
+  }
+  static __device__ __forceinline__ void b_slot(int gt, int j, int& r, int& c) {
+    const int idx = gt + 128 * j;
+    r = idx >> 3;
+    c = idx & 7;
+  }
+  __device__ __forceinline__ void load_a(const TS& ts, int kb, int gt, float (&v)[32]) const {
+    const int p0 = kb * BK + 4 * (gt & 7);
+    const int ohw = g.oh * g.ow;
+    if (p0 >= K) {
+#pragma unroll
+      for (int j = 0; j < 32; j++) v[j] = 0.0f;
+      return;
+    }
+    const int img = p0 / ohw, rem = p0 - img * ohw;
+    const int oy = rem / g.ow, ox = rem - oy * g.ow;
+    const int ys = oy * g.stride, xs = ox * g.stride;
+    const float* base = x + (size_t)img * g.cin * g.h * g.w + ys * g.w + xs;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int iy = ys + ts.dkh[j];
+      const bool rv = ((ts.rok >> j) & 1u) && iy >= 0 && iy < g.h;
+      const float* p = base + (rv ? ts.rowoff[j] : 0);
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int ix = xs + i * g.stride + ts.dkw[j];
+        const bool ok = rv && ix >= 0 && ix < g.w;
+        v[4 * j + i] = ok ? __ldg(p + i * g.stride) : 0.0f;
+      }
+    }
+  }
+  template <int NB>
+  __device__ __forceinline__ void load_b(const TS& ts, int kb, int gt, float (&v)[NB]) const {
+    const int p0 = kb * BK + 4 * (gt & 7);
+    const int ohw = g.oh * g.ow;
+    const bool pin = p0 < K;
+    const int img = pin ? p0 / ohw : 0, rem = pin ? p0 - img * ohw : 0;
+    const float* base = dy + ((size_t)img * g.cout) * ohw + rem;
+#pragma unroll
+    for (int j = 0; j < NB / 4; j++) {
+      const int co = ts.n0 + ((gt + 128 * j) >> 3);
+      if (pin && co < N) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(base + (size_t)co * ohw));
+        v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+      } else {
+        v[4 * j] = v[4 * j + 1] = v[4 * j + 2] = v[4 * j + 3] = 0.0f;
+      }
+    }
+  }
+  __device__ __forceinline__ const void* b_src(int, int) const { return nullptr; }
+  __device__ __forceinline__ void store(int row, int col0, int split, const float (&v)[32]) const {
+    if (row >= M || col0 >= N) return;
+    if (splits > 1) {
+      store_row32(ws + ((size_t)split * M + row) * N + col0, N - col0, v, false, (N % 4) == 0);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j++) {
+        const int co = col0 + j;
+        if (co < N) dw[(size_t)co * M + row] += v[j];
+      }
+    }
+  }
+};
+
 // ---------------------------------------------------------------- launch
 
 // Device bytes each conv operand spans (range checks).
@@ -316,6 +578,42 @@ static int check_geom(int n, int cin, int h, int w, int cout, int k, int stride,
   return RNN_OK;
 }
 
+template <int KS, int BN>
+static int fast_fwd(rnn_ctx* ctx, const float* x, const float* wt, float* y, const ConvGeom& g, bool acc) {
+  constexpr int KK = KS * KS;
+  FastConvFwd<KS, BN> p;
+  p.x = x; p.y = y; p.g = g; p.acc = acc ? 1 : 0; p.splits = 1;
+  p.M = g.n * g.oh * g.ow; p.N = g.cout;
+  p.CB = g.cin / 32;
+  p.kblocks = KK * p.CB;
+  Sched s = make_sched(p.M, p.N, p.kblocks * BK, BN, 1);
+  const size_t bytes = (size_t)s.n_tiles * p.kblocks * 2 * BN * BK * sizeof(float);
+  RNN_TRY(ensure_pack(ctx, bytes));
+  p.bpack = static_cast<const float*>(ctx->pack);
+  RNN_RANGE(ctx->pack, bytes);
+  PackFwdSrc src{wt, g.cout, g.cin, KK};
+  RNN_TRY(launch_pack<BN>(ctx, src, s.n_tiles, p.kblocks, static_cast<float*>(ctx->pack)));
+  return launch<BN>(ctx, p, s);
+}
+
+template <int KS, int BN>
+static int fast_dgrad(rnn_ctx* ctx, const float* dy, const float* wt, float* dx, const ConvGeom& g, bool acc) {
+  constexpr int KK = KS * KS;
+  FastConvDgrad<KS, BN> p;
+  p.dy = dy; p.dx = dx; p.g = g; p.acc = acc ? 1 : 0; p.splits = 1;
+  p.M = g.n * g.h * g.w; p.N = g.cin;
+  p.CB = g.cout / 32;
+  p.kblocks = KK * p.CB;
+  Sched s = make_sched(p.M, p.N, p.kblocks * BK, BN, 1);
+  const size_t bytes = (size_t)s.n_tiles * p.kblocks * 2 * BN * BK * sizeof(float);
+  RNN_TRY(ensure_pack(ctx, bytes));
+  p.bpack = static_cast<const float*>(ctx->pack);
+  RNN_RANGE(ctx->pack, bytes);
+  PackDgradSrc src{wt, g.cout, g.cin, KK};
+  RNN_TRY(launch_pack<BN>(ctx, src, s.n_tiles, p.kblocks, static_cast<float*>(ctx->pack)));
+  return launch<BN>(ctx, p, s);
+}
+
 int conv_fwd(rnn_ctx* ctx, const float* x, int n, int cin, int h, int w, const float* wt, int cout,
              int k, int stride, int pad, float* y, bool acc) {
   ConvGeom g;
@@ -332,6 +630,14 @@ int conv_fwd(rnn_ctx* ctx, const float* x, int n, int cin, int h, int w, const f
     p.splits = 1;
     p.w_vec = (K % 4 == 0) && ((reinterpret_cast<uintptr_t>(wt) & 15) == 0);
   };
+  if (cin % 32 == 0) {
+    switch (bn) {
+      case 32: return k == 3 ? fast_fwd<3, 32>(ctx, x, wt, y, g, acc) : fast_fwd<1, 32>(ctx, x, wt, y, g, acc);
+      case 64: return k == 3 ? fast_fwd<3, 64>(ctx, x, wt, y, g, acc) : fast_fwd<1, 64>(ctx, x, wt, y, g, acc);
+      case 128: return k == 3 ? fast_fwd<3, 128>(ctx, x, wt, y, g, acc) : fast_fwd<1, 128>(ctx, x, wt, y, g, acc);
+      default: return k == 3 ? fast_fwd<3, 256>(ctx, x, wt, y, g, acc) : fast_fwd<1, 256>(ctx, x, wt, y, g, acc);
+    }
+  }
   if (k == 3) {
     ConvFwdProb<3> p; fill(p);
     return run_bn<ConvLauncher>(ctx, bn, p, 1);
@@ -355,6 +661,16 @@ int conv_dgrad(rnn_ctx* ctx, const float* dy, int n, int cin, int h, int w, cons
     p.dy = dy; p.w = wt; p.dx = dx; p.g = g; p.M = M; p.N = N; p.K = K; p.acc = acc ? 1 : 0;
     p.splits = 1;
   };
+  if (cout % 32 == 0) {
+    switch (bn) {
+      case 32: return k == 3 ? fast_dgrad<3, 32>(ctx, dy, wt, dx, g, acc) : fast_dgrad<1, 32>(ctx, dy, wt, dx, g, acc);
+      case 64: return k == 3 ? fast_dgrad<3, 64>(ctx, dy, wt, dx, g, acc) : fast_dgrad<1, 64>(ctx, dy, wt, dx, g, acc);
+      case 128:
+        return k == 3 ? fast_dgrad<3, 128>(ctx, dy, wt, dx, g, acc) : fast_dgrad<1, 128>(ctx, dy, wt, dx, g, acc);
+      default:
+        return k == 3 ? fast_dgrad<3, 256>(ctx, dy, wt, dx, g, acc) : fast_dgrad<1, 256>(ctx, dy, wt, dx, g, acc);
+    }
+  }
   if (k == 3) {
     ConvDgradProb<3> p; fill(p);
     return run_bn<ConvLauncher>(ctx, bn, p, 1);
@@ -373,13 +689,27 @@ int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, in
   RNN_RANGE(dy, sp.y);
   RNN_RANGE(dw, sp.w);
   const int M = cin * k * k, N = cout, K = n * g.oh * g.ow;
-  const int bn = pick_bn(N, (M + BM - 1) / BM, ctx->num_sms);
+  // The im2col operand (A) is the expensive one to gather; each gathered
+  // element feeds BN multiply-adds, so use the widest tile that covers cout
+  // and let split-K supply the parallelism.
+  const int bn = N <= 32 ? 32 : N <= 64 ? 64 : N <= 128 ? 128 : 256;
   const int splits = force_splits > 0 ? force_splits : pick_splits(M, N, K, bn, ctx->num_sms);
   auto fill = [&](auto& p) {
     p.x = x; p.dy = dy; p.dw = dw; p.ws = nullptr; p.g = g; p.M = M; p.N = N; p.K = K;
     p.splits = 1;
     p.dy_vec = ((g.oh * g.ow) % 4 == 0) && ((reinterpret_cast<uintptr_t>(dy) & 15) == 0);
   };
+  if (g.ow % 4 == 0) {
+    auto ffill = [&](auto& p) {
+      p.x = x; p.dy = dy; p.dw = dw; p.ws = nullptr; p.g = g; p.M = M; p.N = N; p.K = K; p.splits = 1;
+    };
+    if (k == 3) {
+      FastConvWgrad<3> p; ffill(p);
+      return run_bn<WgradLauncher>(ctx, bn, p, splits);
+    }
+    FastConvWgrad<1> p; ffill(p);
+    return run_bn<WgradLauncher>(ctx, bn, p, splits);
+  }
   if (k == 3) {
     ConvWgradProb<3> p; fill(p);
     return run_bn<WgradLauncher>(ctx, bn, p, splits);

@@ -14,11 +14,16 @@
 // f32 TMEM accumulator (the lo*lo term, ~2^-22 relative, is dropped).  This
 // is the split-TF32 scheme of Ootomo & Yokota (2022).
 //
-// CTA layout (288 threads, one CTA per SM, persistent over output tiles):
-//   warps 0-3  producers: global -> registers -> hi/lo split -> shared memory
-//              in the canonical K-major SWIZZLE_128B layout, STAGES-deep ring
-//   warp  4    TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 5-8  epilogue: tcgen05.ld from a double-buffered TMEM accumulator
+// CTA layout (416 threads, one CTA per SM, persistent over output tiles):
+//   warps 0-7  producers in two groups of four that take alternate K blocks,
+//              so two blocks' global loads are in flight at once:
+//              global -> registers -> hi/lo split -> shared memory in the
+//              canonical K-major SWIZZLE_128B layout, STAGES-deep ring.  When
+//              the B operand is a weight tensor it is pre-packed once per call
+//              into that exact shared-memory image (hi and lo) and one thread
+//              streams it with cp.async.bulk instead (no register traffic)
+//   warp  8    TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 9-12 epilogue: tcgen05.ld from a double-buffered TMEM accumulator
 //              (2 x BN columns), so the epilogue of tile i overlaps the
 //              main loop of tile i+1
 // Tiles are BM=128 rows (TMEM lanes) x BN columns, BK=32 f32 (128 bytes) of K
@@ -34,10 +39,11 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 32;  // f32 elements of K per stage = one 128-byte swizzle row
-constexpr int NUM_PRODUCER_WARPS = 4;
-constexpr int MMA_WARP = 4;
-constexpr int FIRST_EPI_WARP = 5;
-constexpr int NUM_THREADS = 9 * 32;
+constexpr int NUM_PRODUCER_WARPS = 8;  // two groups of four
+constexpr int GROUP_THREADS = 128;
+constexpr int MMA_WARP = 8;
+constexpr int FIRST_EPI_WARP = 9;
+constexpr int NUM_THREADS = 13 * 32;
 constexpr unsigned long long WAIT_TIMEOUT_NS = 2000000000ull;  // 2 s
 
 // ------------------------------------------------------------------ PTX
@@ -58,6 +64,22 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// One arrival that also announces `bytes` of incoming bulk-copy traffic.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+// 1-D bulk copy global -> shared (TMA engine, no tensor map, no multicast);
+// completes `bytes` of transaction count on `bar`.  16-byte aligned, size a
+// multiple of 16.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst_smem, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst_smem),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
@@ -218,6 +240,7 @@ struct Cfg {
   // 1024 bytes of alignment slack + barriers
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
   static constexpr uint32_t IDESC = idesc_tf32(BM, BN);
+  static constexpr int BCH = BN / 16;  // B chunks (4 K values) per producer thread
 };
 
 // Work decomposition shared by the host launcher and the kernel.
@@ -228,19 +251,71 @@ struct Sched {
   int num_tiles;       // m_tiles * n_tiles * splits
 };
 
+// ------------------------------------------------------------------ Prob
+//
+// A problem type supplies, for one producer thread `gt` (0..127 within its
+// group):
+//   static constexpr bool B_BULK;          B arrives pre-packed by bulk copy
+//   struct TS;                             per-thread tile state
+//   void tile_begin(TS&, int m0, int n0, int gt) const;
+//   void load_a(const TS&, int kb, int gt, float (&v)[32]) const;
+//        the thread's 8 A chunks; chunk j = K values 4c..4c+3 of row r with
+//        (r, c) = a_slot(gt, j); zero outside the problem
+//   static void a_slot(int gt, int j, int& r, int& c);
+//   void load_b(const TS&, int kb, int gt, float (&v)[BCH*4]) const;   (!B_BULK)
+//   static void b_slot(int gt, int j, int& r, int& c);                   (!B_BULK)
+//   const void* b_src(int n_tile, int kb) const;  packed (hi, lo) image (B_BULK)
+//   void store(int row, int col0, int split, const float (&v)[32]) const;
+//        epilogue: 32 consecutive accumulator columns of one row
+//   int M, N;
+
+// Adapter for problems written against the per-chunk interface
+//   A_KMAJOR / B_KMAJOR, load_a(row, k4, v4), load_b(row, k4, v4), store.
+template <class P, int BN>
+struct ChunkProb : P {
+  static constexpr bool B_BULK = false;
+  struct TS {
+    int m0, n0;
+  };
+  __device__ __forceinline__ void tile_begin(TS& ts, int m0, int n0, int) const {
+    ts.m0 = m0;
+    ts.n0 = n0;
+  }
+  static __device__ __forceinline__ void a_slot(int gt, int j, int& r, int& c) {
+    if (P::A_KMAJOR) { r = (gt >> 3) + 16 * j; c = gt & 7; }
+    else { r = gt; c = j; }
+  }
+  static __device__ __forceinline__ void b_slot(int gt, int j, int& r, int& c) {
+    const int idx = gt + 128 * j;
+    if (P::B_KMAJOR) { r = idx >> 3; c = idx & 7; }
+    else { r = idx % BN; c = idx / BN; }
+  }
+  __device__ __forceinline__ void load_a(const TS& ts, int kb, int gt, float (&v)[32]) const {
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      int r, c;
+      a_slot(gt, j, r, c);
+      float t[4];
+      P::load_a(ts.m0 + r, kb * BK + 4 * c, t);
+      v[4 * j] = t[0]; v[4 * j + 1] = t[1]; v[4 * j + 2] = t[2]; v[4 * j + 3] = t[3];
+    }
+  }
+  template <int NB>
+  __device__ __forceinline__ void load_b(const TS& ts, int kb, int gt, float (&v)[NB]) const {
+#pragma unroll
+    for (int j = 0; j < NB / 4; j++) {
+      int r, c;
+      b_slot(gt, j, r, c);
+      float t[4];
+      P::load_b(ts.n0 + r, kb * BK + 4 * c, t);
+      v[4 * j] = t[0]; v[4 * j + 1] = t[1]; v[4 * j + 2] = t[2]; v[4 * j + 3] = t[3];
+    }
+  }
+  __device__ __forceinline__ const void* b_src(int, int) const { return nullptr; }
+};
+
 // ------------------------------------------------------------------ kernel
 
-// Prob concept:
-//   static constexpr bool A_KMAJOR, B_KMAJOR;   producer thread mapping
-//   int M, N;                                  problem rows / columns
-//   __device__ void begin_tile(int m0, int n0, int split, TileState&) (optional
-//       per-thread precomputation; see the Prob types)
-//   __device__ void load_a(int row, int k4, float (&v)[4]) const
-//   __device__ void load_b(int row, int k4, float (&v)[4]) const
-//       rows are global row indices, k4 the first of 4 consecutive K indices;
-//       must return 0 for out-of-range rows / K
-//   __device__ void store(int row, int col0, int split, const float (&v)[32]) const
-//       col0 is a multiple of 32; row may be >= M (ignore), cols may exceed N
 template <int BN, class Prob>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc3_gemm_kernel(const Prob prob, const Sched sched, int* dev_error) {
@@ -264,7 +339,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; s++) {
-      mbar_init(&full[s], NUM_PRODUCER_WARPS * 32);
+      // one group's 128 threads, plus the bulk-copy thread's expect_tx arrival
+      mbar_init(&full[s], GROUP_THREADS + (Prob::B_BULK ? 1 : 0));
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; b++) {
@@ -288,63 +364,60 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (warp < NUM_PRODUCER_WARPS) {
     // ---------------------------------------------------------- producers
-    const int t = threadIdx.x;  // 0..127
+    const int group = warp >> 2;                 // 0 or 1
+    const int gt = threadIdx.x & (GROUP_THREADS - 1);
     uint32_t it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < sched.num_tiles && ok; tile += gridDim.x) {
       const int split = tile / tiles_mn;
       const int mn = tile - split * tiles_mn;
       const int mt = mn % sched.m_tiles, nt = mn / sched.m_tiles;
-      const int m0 = mt * BM, n0 = nt * BN;
       const int kb0 = split * sched.kb_per_split;
       int kb1 = kb0 + sched.kb_per_split;
       if (kb1 > sched.kblocks) kb1 = sched.kblocks;
+      typename Prob::TS ts;
+      prob.tile_begin(ts, mt * BM, nt * BN, gt);
       for (int kb = kb0; kb < kb1; kb++, it++) {
+        if ((int)(it & 1) != group) continue;
         const int stage = it % C::STAGES;
         const uint32_t phase = (it / C::STAGES) & 1;
-        const int k0 = kb * BK;
-        // A: 128 rows x 8 chunks, 8 chunks per thread
-        float va[8][4];
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-          int r, c;
-          if (Prob::A_KMAJOR) { r = (t >> 3) + 16 * j; c = t & 7; }
-          else { r = t; c = j; }
-          prob.load_a(m0 + r, k0 + 4 * c, va[j]);
-        }
-        // B: BN rows x 8 chunks, BN/16 chunks per thread
-        constexpr int BJ = BN / 16;
-        float vb[BJ][4];
-#pragma unroll
-        for (int j = 0; j < BJ; j++) {
-          int idx = t + 128 * j, r, c;
-          if (Prob::B_KMAJOR) { r = idx >> 3; c = idx & 7; }
-          else { r = idx % BN; c = idx / BN; }
-          prob.load_b(n0 + r, k0 + 4 * c, vb[j]);
-        }
+        float va[32];
+        prob.load_a(ts, kb, gt, va);
+        constexpr int NB = Prob::B_BULK ? 4 : C::BCH * 4;
+        float vb[NB];
+        if constexpr (!Prob::B_BULK) prob.template load_b<NB>(ts, kb, gt, vb);
         if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, dev_error)) { ok = false; break; }
         const uint32_t a_hi = ring + stage * C::STAGE_BYTES;
         const uint32_t a_lo = a_hi + C::A_BYTES;
         const uint32_t b_hi = a_lo + C::A_BYTES;
         const uint32_t b_lo = b_hi + C::B_BYTES;
+        if constexpr (Prob::B_BULK) {
+          if (gt == 0) {
+            mbar_arrive_expect_tx(&full[stage], 2 * C::B_BYTES);
+            bulk_g2s(b_hi, prob.b_src(nt, kb), 2 * C::B_BYTES, &full[stage]);
+          }
+        }
 #pragma unroll
         for (int j = 0; j < 8; j++) {
           int r, c;
-          if (Prob::A_KMAJOR) { r = (t >> 3) + 16 * j; c = t & 7; }
-          else { r = t; c = j; }
-          store_split(a_hi, a_lo, sw128_offset(r, c), va[j]);
+          Prob::a_slot(gt, j, r, c);
+          const float t[4] = {va[4 * j], va[4 * j + 1], va[4 * j + 2], va[4 * j + 3]};
+          store_split(a_hi, a_lo, sw128_offset(r, c), t);
         }
+        if constexpr (!Prob::B_BULK) {
 #pragma unroll
-        for (int j = 0; j < BJ; j++) {
-          int idx = t + 128 * j, r, c;
-          if (Prob::B_KMAJOR) { r = idx >> 3; c = idx & 7; }
-          else { r = idx % BN; c = idx / BN; }
-          store_split(b_hi, b_lo, sw128_offset(r, c), vb[j]);
+          for (int j = 0; j < NB / 4; j++) {
+            int r, c;
+            Prob::b_slot(gt, j, r, c);
+            const float t[4] = {vb[4 * j], vb[4 * j + 1], vb[4 * j + 2], vb[4 * j + 3]};
+            store_split(b_hi, b_lo, sw128_offset(r, c), t);
+          }
         }
         fence_async_smem();
         mbar_arrive(&full[stage]);
       }
     }
+    (void)lane;
   } else if (warp == MMA_WARP) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
@@ -425,6 +498,37 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == MMA_WARP) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+// ------------------------------------------------------------------ packing
+//
+// Writes the B operand of every (n tile, K block) as the shared-memory image
+// the MMA reads: [hi tile | lo tile], each BN rows x 128 bytes in the
+// K-major SWIZZLE_128B layout.  `Src` maps (row, k) of the B operand to a
+// value (zero outside).  One thread per 16-byte chunk.
+template <int BN, class Src>
+__global__ void pack_b_kernel(const Src src, int n_tiles, int kblocks, float* __restrict__ out) {
+  const long total = (long)n_tiles * kblocks * BN * 8;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int c = (int)(i & 7);
+    const long rest = i >> 3;
+    const int r = (int)(rest % BN);
+    const long tk = rest / BN;  // n_tile * kblocks + kb
+    const int kb = (int)(tk % kblocks), nt = (int)(tk / kblocks);
+    float v[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) v[e] = src(nt * BN + r, kb * BK + 4 * c + e);
+    float h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      h[e] = tf32_round(v[e]);
+      l[e] = v[e] - h[e];
+    }
+    char* img = reinterpret_cast<char*>(out) + tk * (2L * BN * BK * 4);
+    const uint32_t off = static_cast<uint32_t>((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+    *reinterpret_cast<float4*>(img + off) = make_float4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<float4*>(img + BN * BK * 4 + off) = make_float4(l[0], l[1], l[2], l[3]);
+  }
 }
 
 }  // namespace tc

@@ -4,6 +4,7 @@
 #pragma once
 
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 #include "tc_gemm.cuh"
@@ -83,19 +84,47 @@ inline int pick_splits(int M, int N, int K, int bn, int num_sms) {
   return (int)std::max<long>(s, 1);
 }
 
+// True for problem types written against the engine's native interface
+// (they define a per-thread tile state TS); others go through ChunkProb.
+template <class P, class = void>
+struct has_ts : std::false_type {};
+template <class P>
+struct has_ts<P, std::void_t<typename P::TS>> : std::true_type {};
+
 template <int BN, class Prob>
-int launch(rnn_ctx* ctx, const Prob& prob, const Sched& sched) {
+int launch_native(rnn_ctx* ctx, const Prob& prob, const Sched& sched) {
   using C = Cfg<BN>;
   static bool attr_set = false;  // per instantiation; set once per process
   if (!attr_set) {
-    RNN_CUDA(cudaFuncSetAttribute(tc3_gemm_kernel<BN, Prob>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    RNN_CUDA(cudaFuncSetAttribute(tc3_gemm_kernel<BN, Prob>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  C::SMEM_BYTES));
     attr_set = true;
   }
   if (sched.num_tiles <= 0) return RNN_OK;
   int grid = std::min(sched.num_tiles, ctx->num_sms);
-  tc3_gemm_kernel<BN, Prob><<<grid, NUM_THREADS, C::SMEM_BYTES, ctx->stream>>>(prob, sched,
-                                                                               ctx->dev_error);
+  tc3_gemm_kernel<BN, Prob><<<grid, NUM_THREADS, C::SMEM_BYTES, ctx->stream>>>(prob, sched, ctx->dev_error);
+  RNN_CHECK_LAUNCH();
+  return RNN_OK;
+}
+
+template <int BN, class Prob>
+int launch(rnn_ctx* ctx, const Prob& prob, const Sched& sched) {
+  if constexpr (has_ts<Prob>::value) {
+    return launch_native<BN>(ctx, prob, sched);
+  } else {
+    ChunkProb<Prob, BN> w;
+    static_cast<Prob&>(w) = prob;
+    return launch_native<BN>(ctx, w, sched);
+  }
+}
+
+// Packs the B operand image for every (n tile, K block) into `out`
+// (ensure_pack must have sized it: n_tiles * kblocks * 2 * BN * BK floats).
+template <int BN, class Src>
+int launch_pack(rnn_ctx* ctx, const Src& src, int n_tiles, int kblocks, float* out) {
+  const long chunks = (long)n_tiles * kblocks * BN * 8;
+  const unsigned grid = (unsigned)std::min<long>((chunks + 255) / 256, (long)ctx->num_sms * 8);
+  pack_b_kernel<BN, Src><<<grid, 256, 0, ctx->stream>>>(src, n_tiles, kblocks, out);
   RNN_CHECK_LAUNCH();
   return RNN_OK;
 }
