@@ -72,6 +72,17 @@ int rnn_gemm_dw_dev(rnn_ctx *ctx, int m, int n, int k, const float *a,
                     const float *b, float *c);
 int rnn_gemm_dw(rnn_ctx *ctx, int m, int n, int k, const float *a,
                 const float *b, float *c);
+/* No counterpart in the reference.  The same C += A^T B for callers that may
+ * not allocate device memory (a framework that keeps all device memory in its
+ * own pool, a loop that cannot pay cudaMalloc's implicit synchronisation): no
+ * context, device pointers, enqueued on `cuda_stream` (NULL = legacy default
+ * stream).  Split-K partials live in a fixed 16-MiB device array inside the
+ * library, held by every GPU that loads it until exit; m*n may not exceed
+ * 2,097,152 (RNN_ERR_ARG otherwise).  The first call on a device looks up the
+ * array's device address, so make that first call before any stream capture.
+ * All calls share the array: calls that overlap on a GPU race. */
+int rnn_gemm_dw_noalloc_dev(int m, int n, int k, const float *a,
+                            const float *b, float *c, void *cuda_stream);
 
 /* ---- Conv2d (nn.rs:115-251, conv.rs) ------------------------------------ */
 /* x [n,cin,h,w], w [cout, cin*k*k] in (ci,kh,kw) order, y [n,cout,oh,ow]

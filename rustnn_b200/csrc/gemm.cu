@@ -218,3 +218,114 @@ extern "C" int rnn_gemm_dw_dev(rnn_ctx* ctx, int m, int n, int k, const float* a
   // C[m x n] += A^T B with A [k x m], B [k x n]: op(A) = A^T (at), op(B) = B
   return tc::gemm_dev(ctx, m, n, k, a, true, b, false, c, true, true);
 }
+
+// ---------------------------------------------------------------- no-alloc variant
+//
+// rnn_gemm_dw_noalloc_dev is matmul_dw (C += A^T B) for callers that must not
+// allocate device memory at all: for example a host framework that has
+// reserved the device's memory for its own caching pool (a cudaMalloc from a
+// library could fail or fragment that pool), or a latency-critical loop that
+// cannot pay cudaMalloc's implicit device synchronisation.  It needs no
+// context: the split-K partial sums go to a fixed file-scope device array of
+// NOALLOC_SCRATCH_BYTES (16 MiB), which every GPU that loads this library
+// holds until the process exits.  All calls share that array, so two calls
+// whose kernels overlap on a GPU race; issue them on one stream or order them.
+// The partials it holds are fully rewritten by each call before they are read,
+// so nothing in it has to start at zero.
+#include <mutex>
+
+namespace rnn {
+namespace tc {
+
+constexpr size_t NOALLOC_SCRATCH_BYTES = size_t(16) << 20;
+constexpr size_t NOALLOC_SCRATCH_FLOATS = NOALLOC_SCRATCH_BYTES / sizeof(float);
+constexpr int NOALLOC_MAX_DEVICES = 64;
+
+static __device__ __align__(256) float g_noalloc_scratch[NOALLOC_SCRATCH_FLOATS];
+static __device__ int g_noalloc_error;  // pipeline-wait timeouts of these launches
+
+struct NoAllocDevice {
+  float* scratch = nullptr;  // device address of g_noalloc_scratch on this device
+  int* error = nullptr;
+  int num_sms = 0;
+  bool ready = false;
+};
+static NoAllocDevice g_noalloc_devices[NOALLOC_MAX_DEVICES];
+static std::mutex g_noalloc_mutex;
+
+// Once per device, with that device current: host code only holds a
+// stand-in for the array's name, so the device address has to be looked up.
+static int noalloc_setup(int device, NoAllocDevice** out) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  RNN_REQUIRE(device >= 0 && device < NOALLOC_MAX_DEVICES, "gemm_dw_noalloc: device %d out of range", device);
+  NoAllocDevice& d = g_noalloc_devices[device];
+  if (!d.ready) {
+    RNN_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&d.scratch), g_noalloc_scratch));
+    RNN_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&d.error), g_noalloc_error));
+    RNN_CUDA(cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, device));
+    d.ready = true;
+  }
+  *out = &d;
+  return RNN_OK;
+}
+
+template <int BN>
+static int noalloc_run(rnn_ctx* ctx, DenseProb<true, false> p, int splits) {
+  Sched s = make_sched(p.M, p.N, p.K, BN, splits);
+  p.splits = s.splits;
+  p.ws = s.splits > 1 ? static_cast<float*>(ctx->ws) : nullptr;
+  RNN_TRY(launch<BN>(ctx, p, s));
+  if (s.splits > 1) {
+    const size_t total = (size_t)p.M * p.N;
+    const unsigned grid = (unsigned)std::min<size_t>((total + 255) / 256, (size_t)ctx->num_sms * 8);
+    splitk_reduce_kernel<<<grid, 256, 0, ctx->stream>>>(p.ws, p.c, p.M, p.N, s.splits, 1, 0);
+    RNN_CHECK_LAUNCH();
+  }
+  return RNN_OK;
+}
+
+}  // namespace tc
+}  // namespace rnn
+
+extern "C" int rnn_gemm_dw_noalloc_dev(int m, int n, int k, const float* a, const float* b, float* c,
+                                       void* stream) {
+  using namespace rnn::tc;
+  RNN_REQUIRE(m >= 0 && n >= 0 && k >= 0, "gemm_dw_noalloc: negative size m=%d n=%d k=%d", m, n, k);
+  if (m == 0 || n == 0 || k == 0) return RNN_OK;
+  RNN_REQUIRE(a && b && c, "gemm_dw_noalloc: null operand");
+  // at least two partial planes must fit: m*n <= scratch / 2
+  RNN_REQUIRE((size_t)m * n <= NOALLOC_SCRATCH_FLOATS / 2,
+              "gemm_dw_noalloc: m*n = %zu exceeds this entry point's limit of %zu elements (its fixed %zu-MiB "
+              "scratch holds at least two partial results); use rnn_gemm_dw_dev",
+              (size_t)m * n, NOALLOC_SCRATCH_FLOATS / 2, NOALLOC_SCRATCH_BYTES >> 20);
+  RNN_RANGE(a, sizeof(float) * (size_t)k * m);
+  RNN_RANGE(b, sizeof(float) * (size_t)k * n);
+  RNN_RANGE(c, sizeof(float) * (size_t)m * n);
+  int device = 0;
+  RNN_CUDA(cudaGetDevice(&device));
+  NoAllocDevice* d = nullptr;
+  RNN_TRY(noalloc_setup(device, &d));
+  rnn_ctx ctx;  // on the stack: nothing is allocated
+  ctx.device = device;
+  ctx.num_sms = d->num_sms;
+  ctx.stream = static_cast<cudaStream_t>(stream);
+  ctx.ws = d->scratch;
+  ctx.ws_bytes = NOALLOC_SCRATCH_BYTES;
+  ctx.dev_error = d->error;
+  DenseProb<true, false> p;
+  p.a = a; p.b = b; p.c = c; p.ws = nullptr;
+  p.M = m; p.N = n; p.K = k; p.acc = 1; p.splits = 1;
+  p.a_vec = false;
+  p.b_vec = false;
+  p.c_vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(c) & 15) == 0);
+  const int bn = pick_bn(n, (m + BM - 1) / BM, ctx.num_sms);
+  int splits = pick_splits(m, n, k, bn, ctx.num_sms);
+  const int cap = (int)std::min<size_t>(NOALLOC_SCRATCH_FLOATS / ((size_t)m * n), 1 << 20);
+  if (splits > cap) splits = cap;
+  switch (bn) {
+    case 32: return noalloc_run<32>(&ctx, p, splits);
+    case 64: return noalloc_run<64>(&ctx, p, splits);
+    case 128: return noalloc_run<128>(&ctx, p, splits);
+    default: return noalloc_run<256>(&ctx, p, splits);
+  }
+}
