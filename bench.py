@@ -216,17 +216,13 @@ def run_ours(args, cfg_name):
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
-    if gbatch % world:
-        raise SystemExit(f"global batch {gbatch} not divisible by {world}")
-    n_local = gbatch // world
+    from rustnn_b200 import _lib, dp, model
 
-    from rustnn_b200 import _lib, model
-
+    _, n_local = dp.shard(gbatch, world, rank)
     net = model.ResNet(depth_n, width, NCLASS, 0)
     if world > 1:
-        uid = [model.dp_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        net.dp_init(rank, world, uid[0], sync_bn=not args.local_bn)
+        uid = dp.share_unique_id(model.dp_unique_id)
+        net.dp_init(rank, world, uid, sync_bn=not args.local_bn)
 
     x_np, lab_np = synthetic_batch(n_local, 100 + rank)
     x = torch.from_numpy(x_np).cuda()
@@ -281,10 +277,7 @@ def run_ours(args, cfg_name):
         peaks = json.load(open(pk))
     flops, ktimes = conv_kernel_roofline(None, torch, n_local, peaks)
 
-    times = torch.tensor([t, t_e2e], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    t, t_e2e = times.tolist()
+    t, t_e2e = dp.max_over_ranks([t, t_e2e], device="cuda")
 
     if rank == 0:
         value = gbatch * args.steps / t
