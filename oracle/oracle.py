@@ -88,6 +88,19 @@ def lib():
         "orc_resnet_step": (V, [P, F, F, F]),
         "orc_resnet_train_step": (F, [P, _f32p, _u32p, I, F, F, F, F, C.POINTER(C.c_int)]),
         "orc_resnet_flops": (U64, [P, I, I]),
+        "orc_rel_index": (I, [I, I, I, I, C.c_void_p]),
+        "orc_attn_fwd": (V, [I, I, I, I, I, I, _u32p, I, _f32p, I, I, _f32p, I, I, I, _f32p, _f32p, _f32p, _f32p]),
+        "orc_attn_bwd": (V, [I, I, I, I, I, _u32p, I, _f32p, I, I, _f32p, I, I, I, _f32p, _f32p, _f32p,
+                             _f32p, _f32p, _f32p, _f32p]),
+        "orc_layernorm_fwd": (V, [_f32p, I, I, _f32p, _f32p, F, _f32p, _f32p, _f32p]),
+        "orc_layernorm_bwd": (V, [_f32p, _f32p, _f32p, I, I, _f32p, _f32p, _f32p, _f32p]),
+        "orc_linear_fwd": (V, [_f32p, I, I, I, _f32p, C.c_void_p, _f32p]),
+        "orc_linear_bwd": (V, [_f32p, _f32p, I, I, I, _f32p, _f32p, C.c_void_p, _f32p]),
+        "orc_newton_schulz": (V, [_f32p, I, I, I]),
+        "orc_muon_step": (V, [_f32p, _f32p, _f32p, I, I, I, F, F, F, I]),
+        "orc_adamw_step": (V, [_f32p, _f32p, _f32p, _f32p, Z, F, F, I, F, F, F, I]),
+        "orc_clip": (F, [_f32p, Z, F]),
+        "orc_ema_update": (V, [_f32p, _f32p, Z, F, I]),
         "orc_set_threads": (V, [I]),
         "orc_get_threads": (I, []),
     }
@@ -281,6 +294,70 @@ class ResNet:
 
     def flops(self, h=32, w=32):
         return lib().orc_resnet_flops(self.h, h, w)
+
+
+# ---------------------------------------------------------------- attn.rs
+
+
+def rel_index(th, tw, mh, mw):
+    """(relidx [th*tw*mh*mw] u32, nrel), attn.rs:53-72."""
+    idx = np.empty(th * tw * mh * mw, np.uint32)
+    nrel = lib().orc_rel_index(th, tw, mh, mw, C.c_void_p(idx.ctypes.data))
+    return idx, nrel
+
+
+def attn_fwd(n, h, dh, tq, tk, mask_diag, relidx, nrel, q, qstride, qoff, kv, kvstride, koff, voff, tau, rel):
+    p = np.empty(n * h * tq * tk, np.float32)
+    o = np.empty(n * tq * h * dh, np.float32)
+    lib().orc_attn_fwd(n, h, dh, tq, tk, int(mask_diag), np.ascontiguousarray(relidx, np.uint32), nrel,
+                       _f32(q).ravel(), qstride, qoff, _f32(kv).ravel(), kvstride, koff, voff, _f32(tau), _f32(rel),
+                       p, o)
+    return p, o
+
+
+def attn_bwd(n, h, dh, tq, tk, relidx, nrel, q, qstride, qoff, kv, kvstride, koff, voff, tau, p, dout,
+             dq, dkv, dtau, drel):
+    """dq, dkv, dtau, drel are float32 arrays that accumulate."""
+    lib().orc_attn_bwd(n, h, dh, tq, tk, np.ascontiguousarray(relidx, np.uint32), nrel, _f32(q).ravel(), qstride,
+                       qoff, _f32(kv).ravel(), kvstride, koff, voff, _f32(tau), _f32(p).ravel(), _f32(dout).ravel(),
+                       dq, dkv, dtau, drel)
+
+
+def layernorm_fwd(x, rows, c, g, b, eps=1e-5):
+    y = np.empty(rows * c, np.float32)
+    xhat = np.empty(rows * c, np.float32)
+    invstd = np.empty(rows, np.float32)
+    lib().orc_layernorm_fwd(_f32(x).ravel(), rows, c, _f32(g), _f32(b), eps, y, xhat, invstd)
+    return y, xhat, invstd
+
+
+def layernorm_bwd(dy, xhat, invstd, rows, c, g, dg, db):
+    dx = np.empty(rows * c, np.float32)
+    lib().orc_layernorm_bwd(_f32(dy).ravel(), _f32(xhat).ravel(), _f32(invstd), rows, c, _f32(g), dx, dg, db)
+    return dx
+
+
+def _opt(b):
+    return None if b is None else C.c_void_p(b.ctypes.data)
+
+
+def linear_fwd(x, rows, fin, fout, w, b=None):
+    y = np.empty(rows * fout, np.float32)
+    bb = None if b is None else _f32(b)
+    lib().orc_linear_fwd(_f32(x).ravel(), rows, fin, fout, _f32(w).ravel(), _opt(bb), y)
+    return y
+
+
+def linear_bwd(x, dy, rows, fin, fout, w, dw, db=None):
+    dx = np.empty(rows * fin, np.float32)
+    lib().orc_linear_bwd(_f32(x).ravel(), _f32(dy).ravel(), rows, fin, fout, _f32(w).ravel(), dw, _opt(db), dx)
+    return dx
+
+
+def newton_schulz(g, rows, cols, steps):
+    out = _f32(g).ravel().copy()
+    lib().orc_newton_schulz(out, rows, cols, steps)
+    return out
 
 
 def set_threads(n: int):

@@ -1017,3 +1017,323 @@ uint64_t orc_resnet_flops(const orc_resnet *net, int h, int w) {
     f += 2ULL * c * net->fout;
     return f;
 }
+
+/* ======================================================================= */
+/* attn.rs                                                                  */
+/* ======================================================================= */
+
+int orc_rel_index(int th, int tw, int mh, int mw, uint32_t *idx) {
+    /* RelGeom::new, attn.rs:29-45 */
+    int sy, sx, scale, oy, ox;
+    if (mh == th) {
+        sy = 2 * th - 1; sx = 2 * tw - 1; scale = 1; oy = th - 1; ox = tw - 1;
+    } else {
+        sy = 2 * (th - 1) + mh; sx = 2 * (tw - 1) + mw; scale = 2; oy = mh - 1; ox = mw - 1;
+    }
+    if (idx) {
+        size_t k = 0;
+        for (int qy = 0; qy < th; qy++)
+            for (int qx = 0; qx < tw; qx++)
+                for (int my = 0; my < mh; my++)
+                    for (int mx = 0; mx < mw; mx++) {
+                        int dy = scale * qy - my + oy, dx = scale * qx - mx + ox;
+                        idx[k++] = (uint32_t)(dy * sx + dx);
+                    }
+    }
+    return sy * sx;
+}
+
+void orc_attn_fwd(int n, int h, int dh, int tq, int tk, int mask_diag,
+                  const uint32_t *relidx, int nrel, const float *q, int qstride,
+                  int qoff, const float *kv, int kvstride, int koff, int voff,
+                  const float *tau, const float *rel, float *p, float *o) {
+    const int c = h * dh;
+#pragma omp parallel
+    {
+        float *Q = (float *)malloc(sizeof(float) * (size_t)tq * dh);
+        float *K = (float *)malloc(sizeof(float) * (size_t)tk * dh);
+        float *V = (float *)malloc(sizeof(float) * (size_t)tk * dh);
+        float *S = (float *)malloc(sizeof(float) * (size_t)tq * tk);
+        float *O = (float *)malloc(sizeof(float) * (size_t)tq * dh);
+#pragma omp for schedule(dynamic)
+        for (int i = 0; i < n; i++) {
+            for (int hd = 0; hd < h; hd++) {
+                /* gather, attn.rs:176-178 */
+                for (int r = 0; r < tq; r++)
+                    memcpy(Q + (size_t)r * dh, q + ((size_t)i * tq + r) * qstride + qoff + hd * dh, sizeof(float) * dh);
+                for (int r = 0; r < tk; r++) {
+                    memcpy(K + (size_t)r * dh, kv + ((size_t)i * tk + r) * kvstride + koff + hd * dh, sizeof(float) * dh);
+                    memcpy(V + (size_t)r * dh, kv + ((size_t)i * tk + r) * kvstride + voff + hd * dh, sizeof(float) * dh);
+                }
+                gemm_small(tq, tk, dh, Q, 0, K, 1, S, 0); /* S = Q K^T */
+                const float t = tau[hd];
+                const float *rb = rel + (size_t)hd * nrel;
+                float *pr = p + (((size_t)i * h + hd) * tq) * tk;
+                for (int qi = 0; qi < tq; qi++) {
+                    const float *sr = S + (size_t)qi * tk;
+                    float *dr = pr + (size_t)qi * tk;
+                    const uint32_t *ridx = relidx + (size_t)qi * tk;
+                    float mx = -INFINITY;
+                    for (int kj = 0; kj < tk; kj++) {
+                        float val = t * sr[kj] + rb[ridx[kj]];
+                        dr[kj] = (mask_diag && kj == qi) ? -INFINITY : val;
+                        if (dr[kj] > mx) mx = dr[kj];
+                    }
+                    float sum = 0.0f;
+                    for (int kj = 0; kj < tk; kj++) {
+                        float e = dr[kj] == -INFINITY ? 0.0f : expf(dr[kj] - mx);
+                        dr[kj] = e;
+                        sum += e;
+                    }
+                    float inv = 1.0f / sum;
+                    for (int kj = 0; kj < tk; kj++) dr[kj] *= inv;
+                }
+                gemm_small(tq, dh, tk, pr, 0, V, 0, O, 0); /* O = P V */
+                for (int qi = 0; qi < tq; qi++)
+                    memcpy(o + ((size_t)i * tq + qi) * c + hd * dh, O + (size_t)qi * dh, sizeof(float) * dh);
+            }
+        }
+        free(Q); free(K); free(V); free(S); free(O);
+    }
+}
+
+void orc_attn_bwd(int n, int h, int dh, int tq, int tk, const uint32_t *relidx,
+                  int nrel, const float *q, int qstride, int qoff,
+                  const float *kv, int kvstride, int koff, int voff,
+                  const float *tau, const float *p, const float *dout,
+                  float *dq, float *dkv, float *dtau, float *drel) {
+    const int c = h * dh;
+    /* per-image partials of dtau / drel, summed in image order afterwards
+     * (attn.rs:247-342 folds per worker and reduces) */
+    float *at = (float *)calloc((size_t)n * h, sizeof(float));
+    float *ar = (float *)calloc((size_t)n * h * nrel, sizeof(float));
+#pragma omp parallel
+    {
+        float *Q = (float *)malloc(sizeof(float) * (size_t)tq * dh);
+        float *K = (float *)malloc(sizeof(float) * (size_t)tk * dh);
+        float *V = (float *)malloc(sizeof(float) * (size_t)tk * dh);
+        float *DO = (float *)malloc(sizeof(float) * (size_t)tq * dh);
+        float *S = (float *)malloc(sizeof(float) * (size_t)tq * tk);
+        float *SD = (float *)malloc(sizeof(float) * (size_t)tq * tk);
+        float *DQ = (float *)malloc(sizeof(float) * (size_t)tq * dh);
+        float *DK = (float *)malloc(sizeof(float) * (size_t)tk * dh);
+        float *DV = (float *)malloc(sizeof(float) * (size_t)tk * dh);
+#pragma omp for schedule(dynamic)
+        for (int i = 0; i < n; i++) {
+            for (int hd = 0; hd < h; hd++) {
+                for (int r = 0; r < tq; r++) {
+                    memcpy(Q + (size_t)r * dh, q + ((size_t)i * tq + r) * qstride + qoff + hd * dh, sizeof(float) * dh);
+                    memcpy(DO + (size_t)r * dh, dout + ((size_t)i * tq + r) * c + hd * dh, sizeof(float) * dh);
+                }
+                for (int r = 0; r < tk; r++) {
+                    memcpy(K + (size_t)r * dh, kv + ((size_t)i * tk + r) * kvstride + koff + hd * dh, sizeof(float) * dh);
+                    memcpy(V + (size_t)r * dh, kv + ((size_t)i * tk + r) * kvstride + voff + hd * dh, sizeof(float) * dh);
+                }
+                const float *pr = p + (((size_t)i * h + hd) * tq) * tk;
+                /* dV = P^T dO, attn.rs:270-274 */
+                gemm_small(tk, dh, tq, pr, 1, DO, 0, DV, 0);
+                for (int r = 0; r < tk; r++) {
+                    float *d = dkv + ((size_t)i * tk + r) * kvstride + voff + hd * dh;
+                    for (int z = 0; z < dh; z++) d[z] += DV[(size_t)r * dh + z];
+                }
+                /* dP = dO V^T, then dS = P (dP - rowdot), attn.rs:276-290 */
+                gemm_small(tq, tk, dh, DO, 0, V, 1, S, 0);
+                for (int qi = 0; qi < tq; qi++) {
+                    float *sr = S + (size_t)qi * tk;
+                    const float *prr = pr + (size_t)qi * tk;
+                    float dot = 0.0f;
+                    for (int kj = 0; kj < tk; kj++) dot += sr[kj] * prr[kj];
+                    for (int kj = 0; kj < tk; kj++) sr[kj] = prr[kj] * (sr[kj] - dot);
+                }
+                /* dtau from the recomputed raw scores, attn.rs:292-308 */
+                gemm_small(tq, tk, dh, Q, 0, K, 1, SD, 0);
+                float acc = 0.0f;
+                for (size_t z = 0; z < (size_t)tq * tk; z++) acc += S[z] * SD[z];
+                at[(size_t)i * h + hd] += acc;
+                /* drel, attn.rs:309-315 */
+                float *arh = ar + ((size_t)i * h + hd) * nrel;
+                for (int qi = 0; qi < tq; qi++)
+                    for (int kj = 0; kj < tk; kj++)
+                        arh[relidx[(size_t)qi * tk + kj]] += S[(size_t)qi * tk + kj];
+                const float t = tau[hd];
+                for (size_t z = 0; z < (size_t)tq * tk; z++) S[z] *= t;
+                /* dQ = dS K, dK = dS^T Q, attn.rs:318-327 */
+                gemm_small(tq, dh, tk, S, 0, K, 0, DQ, 0);
+                for (int r = 0; r < tq; r++) {
+                    float *d = dq + ((size_t)i * tq + r) * qstride + qoff + hd * dh;
+                    for (int z = 0; z < dh; z++) d[z] += DQ[(size_t)r * dh + z];
+                }
+                gemm_small(tk, dh, tq, S, 1, Q, 0, DK, 0);
+                for (int r = 0; r < tk; r++) {
+                    float *d = dkv + ((size_t)i * tk + r) * kvstride + koff + hd * dh;
+                    for (int z = 0; z < dh; z++) d[z] += DK[(size_t)r * dh + z];
+                }
+            }
+        }
+        free(Q); free(K); free(V); free(DO); free(S); free(SD); free(DQ); free(DK); free(DV);
+    }
+    for (int i = 0; i < n; i++) {
+        for (int hd = 0; hd < h; hd++) dtau[hd] += at[(size_t)i * h + hd];
+        for (size_t z = 0; z < (size_t)h * nrel; z++) drel[z] += ar[(size_t)i * h * nrel + z];
+    }
+    free(at);
+    free(ar);
+}
+
+/* ======================================================================= */
+/* norm.rs LayerNorm                                                        */
+/* ======================================================================= */
+
+void orc_layernorm_fwd(const float *x, int rows, int c, const float *g, const float *b,
+                       float eps, float *y, float *xhat, float *invstd) {
+#pragma omp parallel for
+    for (int r = 0; r < rows; r++) {
+        const float *xr = x + (size_t)r * c;
+        double s = 0.0, s2 = 0.0;
+        for (int j = 0; j < c; j++) {
+            s += (double)xr[j];
+            s2 += (double)xr[j] * (double)xr[j];
+        }
+        double m = (double)c, mu = s / m;
+        double va = s2 / m - mu * mu;
+        float var = (float)(va > 0.0 ? va : 0.0);
+        float is = 1.0f / sqrtf(var + eps);
+        if (invstd) invstd[r] = is;
+        for (int j = 0; j < c; j++) {
+            float hh = (xr[j] - (float)mu) * is;
+            if (xhat) xhat[(size_t)r * c + j] = hh;
+            y[(size_t)r * c + j] = g[j] * hh + b[j];
+        }
+    }
+}
+
+void orc_layernorm_bwd(const float *dy, const float *xhat, const float *invstd, int rows,
+                       int c, const float *g, float *dx, float *dg, float *db) {
+    for (int r = 0; r < rows; r++)
+        for (int j = 0; j < c; j++) {
+            dg[j] += dy[(size_t)r * c + j] * xhat[(size_t)r * c + j];
+            db[j] += dy[(size_t)r * c + j];
+        }
+    float inv = 1.0f / (float)c;
+#pragma omp parallel for
+    for (int r = 0; r < rows; r++) {
+        const float *dyr = dy + (size_t)r * c, *xh = xhat + (size_t)r * c;
+        float m1 = 0.0f, m2 = 0.0f;
+        for (int j = 0; j < c; j++) {
+            float d = dyr[j] * g[j];
+            m1 += d;
+            m2 += d * xh[j];
+        }
+        for (int j = 0; j < c; j++) {
+            float d = dyr[j] * g[j];
+            dx[(size_t)r * c + j] = invstd[r] * (d - m1 * inv - xh[j] * m2 * inv);
+        }
+    }
+}
+
+/* ======================================================================= */
+/* linear.rs                                                                */
+/* ======================================================================= */
+
+void orc_linear_fwd(const float *x, int rows, int fin, int fout, const float *w, const float *b,
+                    float *y) {
+    orc_matmul(rows, fout, fin, x, 0, w, 1, y, 0);
+    if (b)
+        for (int r = 0; r < rows; r++)
+            for (int o = 0; o < fout; o++) y[(size_t)r * fout + o] += b[o];
+}
+
+void orc_linear_bwd(const float *x, const float *dy, int rows, int fin, int fout, const float *w,
+                    float *dw, float *db, float *dx) {
+    orc_matmul_dw(fout, fin, rows, dy, x, dw);
+    if (db)
+        for (int r = 0; r < rows; r++)
+            for (int o = 0; o < fout; o++) db[o] += dy[(size_t)r * fout + o];
+    orc_matmul(rows, fin, fout, dy, 0, w, 0, dx, 0);
+}
+
+/* ======================================================================= */
+/* optim.rs                                                                 */
+/* ======================================================================= */
+
+void orc_newton_schulz(float *g, int rows, int cols, int steps) {
+    /* optim.rs:124-145: work on the wide orientation (m <= n) */
+    int m, n, tr;
+    if (rows <= cols) { m = rows; n = cols; tr = 0; } else { m = cols; n = rows; tr = 1; }
+    float *x = (float *)malloc(sizeof(float) * (size_t)m * n);
+    float *a = (float *)malloc(sizeof(float) * (size_t)m * m);
+    float *aa = (float *)malloc(sizeof(float) * (size_t)m * m);
+    float *t = (float *)malloc(sizeof(float) * (size_t)m * n);
+    if (!tr) memcpy(x, g, sizeof(float) * (size_t)m * n);
+    else
+        for (int i = 0; i < rows; i++)
+            for (int j = 0; j < cols; j++) x[(size_t)j * rows + i] = g[(size_t)i * cols + j];
+    float ss = 0.0f;
+    for (size_t i = 0; i < (size_t)m * n; i++) ss += x[i] * x[i];
+    float norm = sqrtf(ss) + 1e-7f;
+    float inv = 1.0f / norm;
+    for (size_t i = 0; i < (size_t)m * n; i++) x[i] *= inv;
+    const float A = 3.4445f, B = -4.7750f, Cc = 2.0315f; /* optim.rs:24-26 */
+    for (int s = 0; s < steps; s++) {
+        gemm_small(m, m, n, x, 0, x, 1, a, 0);   /* A = X X^T */
+        gemm_small(m, m, m, a, 0, a, 0, aa, 0);  /* AA = A A */
+        for (size_t i = 0; i < (size_t)m * m; i++) a[i] = B * a[i] + Cc * aa[i];
+        gemm_small(m, n, m, a, 0, x, 0, t, 0);   /* T = B X */
+        for (size_t i = 0; i < (size_t)m * n; i++) x[i] = A * x[i] + t[i];
+    }
+    if (!tr) memcpy(g, x, sizeof(float) * (size_t)m * n);
+    else
+        for (int i = 0; i < rows; i++)
+            for (int j = 0; j < cols; j++) g[(size_t)i * cols + j] = x[(size_t)j * rows + i];
+    free(x); free(a); free(aa); free(t);
+}
+
+void orc_muon_step(float *v, float *g, float *m, int rows, int cols, int steps, float lr,
+                   float mom, float wd, int decay) {
+    /* optim.rs:184-197 */
+    size_t n = (size_t)rows * cols;
+    float wdp = decay ? wd : 0.0f;
+    for (size_t i = 0; i < n; i++) {
+        m[i] = mom * m[i] + g[i];
+        g[i] += mom * m[i];
+    }
+    orc_newton_schulz(g, rows, cols, steps);
+    float scale = 0.2f * sqrtf((float)(rows > cols ? rows : cols));
+    for (size_t i = 0; i < n; i++) {
+        v[i] -= lr * (scale * g[i] + wdp * v[i]);
+        g[i] = 0.0f;
+    }
+}
+
+void orc_adamw_step(float *v, float *g, float *m, float *v2, size_t n, float lr, float wd,
+                    int decay, float b1, float b2, float eps, int t) {
+    /* step_adam, optim.rs:205-233 */
+    float w = decay ? wd : 0.0f;
+    float c1 = 1.0f - powf(b1, (float)(t + 1));
+    float c2 = 1.0f - powf(b2, (float)(t + 1));
+    for (size_t i = 0; i < n; i++) {
+        m[i] = b1 * m[i] + (1.0f - b1) * g[i];
+        v2[i] = b2 * v2[i] + (1.0f - b2) * g[i] * g[i];
+        v[i] -= lr * ((m[i] / c1) / (sqrtf(v2[i] / c2) + eps) + w * v[i]);
+        g[i] = 0.0f;
+    }
+}
+
+float orc_clip(float *g, size_t n, float max) {
+    /* clip_, optim.rs:237-250: f64 sum of squares */
+    double sq = 0.0;
+    for (size_t i = 0; i < n; i++) sq += (double)g[i] * (double)g[i];
+    float norm = (float)sqrt(sq);
+    if (norm > max && norm > 0.0f) {
+        float s = max / norm;
+        for (size_t i = 0; i < n; i++) g[i] *= s;
+    }
+    return norm;
+}
+
+void orc_ema_update(float *e, const float *v, size_t n, float decay, int t) {
+    /* Ema::update, optim.rs:281-286 (t already incremented) */
+    float cap = (1.0f + (float)t) / (10.0f + (float)t);
+    float d = decay < cap ? decay : cap;
+    for (size_t i = 0; i < n; i++) e[i] = d * e[i] + (1.0f - d) * v[i];
+}

@@ -125,6 +125,54 @@ float  orc_resnet_train_step(orc_resnet *net, const float *x,
 /* model.rs:179-198 */
 uint64_t orc_resnet_flops(const orc_resnet *net, int h, int w);
 
+/* ---- attn.rs ------------------------------------------------------------ */
+/* rel_index (attn.rs:53-72): writes th*tw*mh*mw indices when idx != NULL,
+ * returns nrel = span_y * span_x (attn.rs:23-46). */
+int  orc_rel_index(int th, int tw, int mh, int mw, uint32_t *idx);
+/* Core::forward (attn.rs:148-223) over n images: q rows strided by qstride
+ * (head hd at column qoff + hd*dh), kv rows by kvstride (K at koff, V at
+ * voff), tau[h], rel[h*nrel]; writes p [n,h,tq,tk] and o [n,tq,h*dh]. */
+void orc_attn_fwd(int n, int h, int dh, int tq, int tk, int mask_diag,
+                  const uint32_t *relidx, int nrel, const float *q, int qstride,
+                  int qoff, const float *kv, int kvstride, int koff, int voff,
+                  const float *tau, const float *rel, float *p, float *o);
+/* Core::backward (attn.rs:226-343): dq, dkv, dtau, drel accumulate. */
+void orc_attn_bwd(int n, int h, int dh, int tq, int tk, const uint32_t *relidx,
+                  int nrel, const float *q, int qstride, int qoff,
+                  const float *kv, int kvstride, int koff, int voff,
+                  const float *tau, const float *p, const float *dout,
+                  float *dq, float *dkv, float *dtau, float *drel);
+
+/* ---- norm.rs LayerNorm (f64 row statistics) ----------------------------- */
+void orc_layernorm_fwd(const float *x, int rows, int c, const float *g,
+                       const float *b, float eps, float *y, float *xhat,
+                       float *invstd);                         /* norm.rs:38-90 */
+void orc_layernorm_bwd(const float *dy, const float *xhat, const float *invstd,
+                       int rows, int c, const float *g, float *dx, float *dg,
+                       float *db);                             /* norm.rs:92-137 */
+
+/* ---- linear.rs ----------------------------------------------------------- */
+/* y[rows, fout] = x W^T + b (b may be NULL), linear.rs:44-63 */
+void orc_linear_fwd(const float *x, int rows, int fin, int fout, const float *w,
+                    const float *b, float *y);
+/* dW += dY^T X; db += colsum(dY) (b may be NULL); dx = dY W; linear.rs:66-96 */
+void orc_linear_bwd(const float *x, const float *dy, int rows, int fin, int fout,
+                    const float *w, float *dw, float *db, float *dx);
+
+/* ---- optim.rs ------------------------------------------------------------ */
+/* newton_schulz in place on g [rows x cols] (optim.rs:70-145) */
+void orc_newton_schulz(float *g, int rows, int cols, int steps);
+/* one Muon update of one matrix parameter (optim.rs:182-197) */
+void orc_muon_step(float *v, float *g, float *m, int rows, int cols, int steps,
+                   float lr, float mom, float wd, int decay);
+/* step_adam (optim.rs:205-233); t = steps taken before this one */
+void orc_adamw_step(float *v, float *g, float *m, float *v2, size_t n, float lr,
+                    float wd, int decay, float b1, float b2, float eps, int t);
+/* clip_ (optim.rs:237-250) over one flat gradient buffer; returns the norm */
+float orc_clip(float *g, size_t n, float max);
+/* Ema::update for t >= 2 (optim.rs:270-287): e = d e + (1-d) v */
+void orc_ema_update(float *e, const float *v, size_t n, float decay, int t);
+
 /* ---- threads ------------------------------------------------------------ */
 void orc_set_threads(int n);
 int  orc_get_threads(void);

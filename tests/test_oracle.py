@@ -231,3 +231,106 @@ def test_resnet_full_gradcheck():
     e = dircheck(p, g, EPS, rng, lossf)
     net.set_params(p)
     assert e < TOL, e
+
+
+# ------------------------------------------------------------------ attention, LN, linear, NS
+
+
+def test_rel_index_geometry():
+    """attn.rs:23-72: self 3x3 -> 5x5 offsets; cross 3x3 over 6x6 -> 10x10."""
+    idx, nrel = O.rel_index(3, 3, 3, 3)
+    assert nrel == 25 and idx.max() == 24 and idx.min() == 0
+    assert idx[0] == 12  # q (0,0) vs k (0,0): zero offset = origin (2,2)
+    idx, nrel = O.rel_index(3, 3, 6, 6)
+    assert nrel == 100 and idx.max() < 100
+
+
+def _attn_fixture(rng, n, h, dh, th, mh, self_attn):
+    c = h * dh
+    tq, tk = th * th, mh * mh
+    relidx, nrel = O.rel_index(th, th, mh, mh)
+    tau = np.full(h, np.float32(1.0 / np.sqrt(np.float32(dh))), np.float32)
+    rel = rng.rand_vec(h * nrel)
+    if self_attn:
+        ab = rng.rand_vec(n * tq * 3 * c)
+        geo = dict(q=ab, qstride=3 * c, qoff=0, kv=ab, kvstride=3 * c, koff=c, voff=2 * c)
+    else:
+        q = rng.rand_vec(n * tq * c)
+        mem = rng.rand_vec(n * tk * 2 * c)
+        geo = dict(q=q, qstride=c, qoff=0, kv=mem, kvstride=2 * c, koff=0, voff=c)
+    return c, tq, tk, relidx, nrel, tau, rel, geo
+
+
+@pytest.mark.parametrize("self_attn", [True, False])
+def test_attention_core_gradcheck(self_attn):
+    """check.rs:300-348 geometry (c=8, h=2, 3x3 grid, 6x6 memory) on Core."""
+    rng = O.Rng(77 + int(self_attn))
+    n, h, dh, th, mh = 3, 2, 4, 3, 3 if self_attn else 6
+    c, tq, tk, relidx, nrel, tau, rel, geo = _attn_fixture(rng, n, h, dh, th, mh, self_attn)
+    mask = self_attn
+
+    def fwd(geo_, tau_, rel_):
+        return O.attn_fwd(n, h, dh, tq, tk, mask, relidx, nrel, geo_["q"], geo_["qstride"], geo_["qoff"],
+                          geo_["kv"], geo_["kvstride"], geo_["koff"], geo_["voff"], tau_, rel_)
+
+    p, o = fwd(geo, tau, rel)
+    r = rng.rand_vec(o.size)
+    dq = np.zeros_like(geo["q"])
+    dkv = np.zeros_like(geo["kv"]) if not self_attn else dq  # self: fused buffer, one gradient
+    dtau, drel = np.zeros(h, np.float32), np.zeros(h * nrel, np.float32)
+    O.attn_bwd(n, h, dh, tq, tk, relidx, nrel, geo["q"], geo["qstride"], geo["qoff"], geo["kv"], geo["kvstride"],
+               geo["koff"], geo["voff"], tau, p, r, dq, dkv, dtau, drel)
+    loss = lambda g_, t_, r_: float(np.dot(fwd(g_, t_, r_)[1], r))
+    if self_attn:
+        e = dircheck(geo["q"], dq, EPS, rng, lambda v: loss({**geo, "q": v, "kv": v}, tau, rel))
+        assert e < TOL, e
+    else:
+        assert dircheck(geo["q"], dq, EPS, rng, lambda v: loss({**geo, "q": v}, tau, rel)) < TOL
+        assert dircheck(geo["kv"], dkv, EPS, rng, lambda v: loss({**geo, "kv": v}, tau, rel)) < TOL
+    assert dircheck(tau, dtau, EPS, rng, lambda v: loss(geo, v, rel)) < TOL
+    assert dircheck(rel, drel, EPS, rng, lambda v: loss(geo, tau, v)) < TOL
+
+
+def test_layernorm_gradcheck():
+    """check.rs:183-213 (Tok 3x9x8)."""
+    rng = O.Rng(31)
+    rows, c = 27, 8
+    x = rng.rand_vec(rows * c)
+    g = (1.0 + 0.2 * rng.rand_vec(c)).astype(np.float32)
+    b = rng.rand_vec(c)
+    r = rng.rand_vec(rows * c)
+    y, xhat, invstd = O.layernorm_fwd(x, rows, c, g, b)
+    dg, db = np.zeros(c, np.float32), np.zeros(c, np.float32)
+    dx = O.layernorm_bwd(r, xhat, invstd, rows, c, g, dg, db)
+    f = lambda xx, gg, bb: float(np.dot(O.layernorm_fwd(xx, rows, c, gg, bb)[0], r))
+    assert dircheck(x, dx, EPS, rng, lambda v: f(v, g, b)) < TOL
+    assert dircheck(g, dg, EPS, rng, lambda v: f(x, v, b)) < TOL
+    assert dircheck(b, db, EPS, rng, lambda v: f(x, g, v)) < TOL
+
+
+def test_linear_gradcheck():
+    rng = O.Rng(41)
+    rows, fin, fout = 27, 8, 12
+    x, w, b = rng.rand_vec(rows * fin), rng.rand_vec(fout * fin), rng.rand_vec(fout)
+    r = rng.rand_vec(rows * fout)
+    dw, db = np.zeros(fout * fin, np.float32), np.zeros(fout, np.float32)
+    dx = O.linear_bwd(x, r, rows, fin, fout, w, dw, db)
+    f = lambda xx, ww, bb: float(np.dot(O.linear_fwd(xx, rows, fin, fout, ww, bb), r))
+    assert dircheck(x, dx, EPS, rng, lambda v: f(v, w, b)) < TOL
+    assert dircheck(w, dw, EPS, rng, lambda v: f(x, v, b)) < TOL
+    assert dircheck(b, db, EPS, rng, lambda v: f(x, w, v)) < TOL
+
+
+def gram_error(g, m, n):
+    """check.rs:462-482."""
+    G = np.asarray(g, np.float64).reshape(m, n)
+    M = G @ G.T if m <= n else G.T @ G
+    return float(np.abs(M - np.eye(M.shape[0])).max())
+
+
+@pytest.mark.parametrize("m,n", [(12, 20), (20, 12), (16, 16)])
+def test_newton_schulz_band(m, n):
+    """check.rs:484-497: singular values in a band around 1 (tol 0.5)."""
+    g = O.Rng(m * 100 + n).rand_vec(m * n)
+    out = O.newton_schulz(g, m, n, 5)
+    assert gram_error(out, m, n) < 0.5
