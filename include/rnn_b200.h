@@ -151,6 +151,70 @@ int rnn_softmax_ce_dev(rnn_ctx *ctx, const float *logits, const uint32_t *labels
 int rnn_sgd_nesterov_dev(rnn_ctx *ctx, float *v, float *g, float *m, size_t len,
                          float lr, float mom, float wd, int decay);
 
+/* ---- attention (attn.rs) ------------------------------------------------ */
+/* rel_index (attn.rs:53-72) for a th x tw query grid over an mh x mw key grid
+ * (equal grids: self attention; otherwise the memory is at twice the
+ * resolution and offsets are in half-token units).  Writes th*tw*mh*mw
+ * indices when idx != NULL; *nrel = number of bias entries per head. */
+int rnn_rel_index(int th, int tw, int mh, int mw, uint32_t *idx, int *nrel);
+/* Core::forward (attn.rs:148-223) for all n images and h heads in one launch:
+ * S = tau_h Q K^T + rel_h[rel_index], diagonal masked when mask_diag (LSA),
+ * P = softmax(S) written to p [n,h,tq,tk] (the backward reads it), O = P V
+ * written to o [n,tq,h*dh].  Q rows are qstride floats apart with head hd at
+ * column qoff + hd*dh; K/V rows kvstride apart at koff/voff + hd*dh (the fused
+ * qkv [n*t,3c] buffer: qstride=kvstride=3c, qoff=0, koff=c, voff=2c; the
+ * cross-attention memory [n*tk,2c]: koff=0, voff=c).  dh in {4,8,16,32,64}. */
+int rnn_attn_fwd_dev(rnn_ctx *ctx, int n, int h, int dh, int th, int tw, int mh,
+                     int mw, int mask_diag, const float *q, int qstride,
+                     int qoff, const float *kv, int kvstride, int koff,
+                     int voff, const float *tau, const float *rel, float *p,
+                     float *o);
+/* Core::backward (attn.rs:226-343): dq, dkv, dtau, drel accumulate (+=); dq
+ * and dkv may be the same buffer (the fused qkv gradient).  Deterministic. */
+int rnn_attn_bwd_dev(rnn_ctx *ctx, int n, int h, int dh, int th, int tw, int mh,
+                     int mw, const float *q, int qstride, int qoff,
+                     const float *kv, int kvstride, int koff, int voff,
+                     const float *tau, const float *p, const float *dout,
+                     float *dq, float *dkv, float *dtau, float *drel);
+
+/* ---- LayerNorm (norm.rs:17-143) and Linear (linear.rs:44-96) ------------ */
+/* y = gamma * xhat + beta over rows of c, f64 row statistics; xhat [rows*c]
+ * and invstd [rows] are written when non-NULL (the backward needs them). */
+int rnn_layernorm_fwd_dev(rnn_ctx *ctx, const float *x, int rows, int c,
+                          const float *gamma, const float *beta, float eps,
+                          float *y, float *xhat, float *invstd);
+/* dx written; dgamma, dbeta accumulate (norm.rs:92-137). */
+int rnn_layernorm_bwd_dev(rnn_ctx *ctx, const float *dy, const float *xhat,
+                          const float *invstd, int rows, int c,
+                          const float *gamma, float *dx, float *dgamma,
+                          float *dbeta);
+/* Linear::forward: y[rows,fout] = x W^T (+ b; b may be NULL), W [fout,fin]. */
+int rnn_linear_fwd_dev(rnn_ctx *ctx, const float *x, int rows, int fin, int fout,
+                       const float *w, const float *b, float *y);
+/* Linear::backward: dW += dY^T X, db += colsum(dY) (b may be NULL), dx = dY W. */
+int rnn_linear_bwd_dev(rnn_ctx *ctx, const float *x, const float *dy, int rows,
+                       int fin, int fout, const float *w, float *dw, float *db,
+                       float *dx);
+
+/* ---- optimisers (optim.rs) ---------------------------------------------- */
+/* newton_schulz in place on g [rows x cols] (optim.rs:124-145). */
+int rnn_newton_schulz_dev(rnn_ctx *ctx, float *g, int rows, int cols, int steps);
+/* One Muon update of one matrix (optim.rs:184-197); g is zeroed. */
+int rnn_muon_step_dev(rnn_ctx *ctx, float *v, float *g, float *m, int rows,
+                      int cols, int steps, float lr, float mom, float wd,
+                      int decay);
+/* step_adam (optim.rs:205-233); t = updates already taken; g is zeroed. */
+int rnn_adamw_step_dev(rnn_ctx *ctx, float *v, float *g, float *m, float *v2,
+                       size_t n, float lr, float wd, int decay, float b1,
+                       float b2, float eps, int t);
+/* clip_ (optim.rs:237-250) over one flat gradient buffer; the pre-clip norm
+ * goes to norm_out[0] (device) when non-NULL. */
+int rnn_clip_dev(rnn_ctx *ctx, float *g, size_t n, float max, float *norm_out);
+/* Ema::update (optim.rs:270-287) for its t-th call (t >= 2; the first call
+ * copies the weights): e = d e + (1-d) v, d = min(decay, (1+t)/(10+t)). */
+int rnn_ema_update_dev(rnn_ctx *ctx, float *e, const float *v, size_t n,
+                       float decay, int t);
+
 /* ---- ResNet training step (model.rs, train.rs:684-699) ------------------ */
 /* ResNet::new(depth_n, width, nclass, seed) (model.rs:112-133), with the
  * reference's initialisation drawn from the same xoshiro256++ stream, so

@@ -65,6 +65,18 @@ SIGS = {
     "rnn_gap_bwd_dev": [CTX, FP, I, I, FP],
     "rnn_softmax_ce_dev": [CTX, FP, FP, I, I, F, FP, FP, FP],
     "rnn_sgd_nesterov_dev": [CTX, FP, FP, FP, Z, F, F, F, I],
+    "rnn_rel_index": [I, I, I, I, P, C.POINTER(I)],
+    "rnn_attn_fwd_dev": [CTX, I, I, I, I, I, I, I, I, FP, I, I, FP, I, I, I, FP, FP, FP, FP],
+    "rnn_attn_bwd_dev": [CTX, I, I, I, I, I, I, I, FP, I, I, FP, I, I, I, FP, FP, FP, FP, FP, FP, FP],
+    "rnn_layernorm_fwd_dev": [CTX, FP, I, I, FP, FP, F, FP, FP, FP],
+    "rnn_layernorm_bwd_dev": [CTX, FP, FP, FP, I, I, FP, FP, FP, FP],
+    "rnn_linear_fwd_dev": [CTX, FP, I, I, I, FP, FP, FP],
+    "rnn_linear_bwd_dev": [CTX, FP, FP, I, I, I, FP, FP, FP, FP],
+    "rnn_newton_schulz_dev": [CTX, FP, I, I, I],
+    "rnn_muon_step_dev": [CTX, FP, FP, FP, I, I, I, F, F, F, I],
+    "rnn_adamw_step_dev": [CTX, FP, FP, FP, FP, Z, F, F, I, F, F, F, I],
+    "rnn_clip_dev": [CTX, FP, Z, F, FP],
+    "rnn_ema_update_dev": [CTX, FP, FP, Z, F, I],
     "rnn_resnet_create": [CTX, I, I, I, U64, C.POINTER(NET)],
     "rnn_resnet_destroy": [NET],
     "rnn_resnet_num_params": [NET, C.POINTER(Z)],

@@ -106,6 +106,21 @@ int ensure_stage(rnn_ctx* ctx, size_t bytes) {
   return RNN_OK;
 }
 
+int ensure_aux(rnn_ctx* ctx, size_t bytes) {
+  if (bytes <= ctx->aux_bytes) return RNN_OK;
+  size_t want = std::max(bytes, ctx->aux_bytes * 2);
+  want = (want + (1 << 20) - 1) & ~(size_t)((1 << 20) - 1);
+  if (ctx->aux) {
+    RNN_CUDA(cudaStreamSynchronize(ctx->stream));
+    RNN_CUDA(cudaFree(ctx->aux));
+    ctx->aux = nullptr;
+    ctx->aux_bytes = 0;
+  }
+  RNN_CUDA(cudaMalloc(&ctx->aux, want));
+  ctx->aux_bytes = want;
+  return RNN_OK;
+}
+
 int ensure_pack(rnn_ctx* ctx, size_t bytes) {
   if (bytes <= ctx->pack_bytes) return RNN_OK;
   size_t want = std::max(bytes, ctx->pack_bytes * 2);
@@ -171,6 +186,7 @@ extern "C" int rnn_ctx_destroy(rnn_ctx* ctx) {
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->stage) cudaFree(ctx->stage);
   if (ctx->pack) cudaFree(ctx->pack);
+  if (ctx->aux) cudaFree(ctx->aux);
   if (ctx->dev_error) cudaFree(ctx->dev_error);
   if (ctx->own) cudaStreamDestroy(ctx->own);
   delete ctx;

@@ -89,6 +89,10 @@ struct rnn_ctx {
   // packed B-operand images (weights in the MMA's shared-memory layout)
   void* pack = nullptr;
   size_t pack_bytes = 0;
+  // optimiser scratch (Newton-Schulz iterates), separate from ws because the
+  // GEMMs it issues use ws for their split-K partials
+  void* aux = nullptr;
+  size_t aux_bytes = 0;
 };
 
 namespace rnn {
@@ -97,4 +101,5 @@ namespace rnn {
 int ensure_ws(rnn_ctx* ctx, size_t bytes);
 int ensure_stage(rnn_ctx* ctx, size_t bytes);
 int ensure_pack(rnn_ctx* ctx, size_t bytes);
+int ensure_aux(rnn_ctx* ctx, size_t bytes);
 }  // namespace rnn

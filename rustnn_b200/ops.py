@@ -24,6 +24,8 @@ __all__ = [
     "Context", "default_context", "matmul", "gemm_small", "matmul_dw", "conv2d_forward", "conv2d_dgrad",
     "conv2d_wgrad", "batchnorm_forward", "batchnorm_eval", "batchnorm_backward", "relu_back_", "add_",
     "add_relu_", "gap_forward", "gap_backward", "softmax_ce", "sgd_nesterov_", "out_dim", "RnnError",
+    "rel_index", "attn_forward", "attn_backward", "layernorm_forward", "layernorm_backward", "linear_forward",
+    "linear_backward", "newton_schulz_", "muon_step_", "adamw_step_", "clip_", "ema_update_",
 ]
 
 
@@ -218,3 +220,107 @@ def sgd_nesterov_(v, g, m, lr, mom, wd, decay, ctx=None):
     call("rnn_sgd_nesterov_dev", _ctx_of(v, ctx), _ptr(v, "v"), _ptr(g, "g"), _ptr(m, "m"), v.numel(), lr, mom, wd,
          int(bool(decay)))
     return v
+
+
+# ---------------------------------------------------------------- attn.rs
+
+
+def _opt_ptr(t, name):
+    return None if t is None else _ptr(t, name)
+
+
+def rel_index(th, tw, mh, mw):
+    """(relidx numpy u32 [th*tw*mh*mw], nrel) -- attn.rs:53-72."""
+    import numpy as np
+
+    idx = np.empty(th * tw * mh * mw, np.uint32)
+    nrel = C.c_int()
+    call("rnn_rel_index", th, tw, mh, mw, C.c_void_p(idx.ctypes.data), C.byref(nrel))
+    return idx, nrel.value
+
+
+def attn_forward(n, h, dh, th, tw, mh, mw, mask_diag, q, qstride, qoff, kv, kvstride, koff, voff, tau, rel,
+                 ctx=None):
+    """Core::forward (attn.rs:148): returns (p [n,h,tq,tk], o [n,tq,h*dh])."""
+    tq, tk = th * tw, mh * mw
+    p = torch.empty(n * h * tq * tk, device=q.device, dtype=torch.float32)
+    o = torch.empty(n * tq * h * dh, device=q.device, dtype=torch.float32)
+    call("rnn_attn_fwd_dev", _ctx_of(q, ctx), n, h, dh, th, tw, mh, mw, int(bool(mask_diag)), _ptr(q, "q"), qstride,
+         qoff, _ptr(kv, "kv"), kvstride, koff, voff, _ptr(tau, "tau"), _ptr(rel, "rel"), _ptr(p, "p"), _ptr(o, "o"))
+    return p, o
+
+
+def attn_backward(n, h, dh, th, tw, mh, mw, q, qstride, qoff, kv, kvstride, koff, voff, tau, p, dout, dq, dkv,
+                  dtau, drel, ctx=None):
+    """Core::backward (attn.rs:226): dq, dkv, dtau, drel accumulate."""
+    call("rnn_attn_bwd_dev", _ctx_of(q, ctx), n, h, dh, th, tw, mh, mw, _ptr(q, "q"), qstride, qoff, _ptr(kv, "kv"),
+         kvstride, koff, voff, _ptr(tau, "tau"), _ptr(p, "p"), _ptr(dout, "dout"), _ptr(dq, "dq"), _ptr(dkv, "dkv"),
+         _ptr(dtau, "dtau"), _ptr(drel, "drel"))
+
+
+# ---------------------------------------------------------------- norm.rs / linear.rs
+
+
+def layernorm_forward(x, rows, c, gamma, beta, eps=1e-5, ctx=None):
+    """LayerNorm::forward (norm.rs:38): returns (y, xhat, invstd)."""
+    y = torch.empty_like(x)
+    xhat = torch.empty_like(x)
+    invstd = torch.empty(rows, device=x.device, dtype=torch.float32)
+    call("rnn_layernorm_fwd_dev", _ctx_of(x, ctx), _ptr(x, "x"), rows, c, _ptr(gamma, "gamma"), _ptr(beta, "beta"),
+         eps, _ptr(y, "y"), _ptr(xhat, "xhat"), _ptr(invstd, "invstd"))
+    return y, xhat, invstd
+
+
+def layernorm_backward(dy, xhat, invstd, rows, c, gamma, dgamma, dbeta, ctx=None):
+    dx = torch.empty_like(dy)
+    call("rnn_layernorm_bwd_dev", _ctx_of(dy, ctx), _ptr(dy, "dy"), _ptr(xhat, "xhat"), _ptr(invstd, "invstd"), rows,
+         c, _ptr(gamma, "gamma"), _ptr(dx, "dx"), _ptr(dgamma, "dgamma"), _ptr(dbeta, "dbeta"))
+    return dx
+
+
+def linear_forward(x, rows, fin, fout, w, b=None, ctx=None):
+    """Linear::forward (linear.rs:44): y = x W^T + b."""
+    y = torch.empty(rows * fout, device=x.device, dtype=torch.float32)
+    call("rnn_linear_fwd_dev", _ctx_of(x, ctx), _ptr(x, "x"), rows, fin, fout, _ptr(w, "w"), _opt_ptr(b, "b"),
+         _ptr(y, "y"))
+    return y
+
+
+def linear_backward(x, dy, rows, fin, fout, w, dw, db=None, ctx=None):
+    """Linear::backward (linear.rs:66): dW, db accumulate; returns dx."""
+    dx = torch.empty(rows * fin, device=x.device, dtype=torch.float32)
+    call("rnn_linear_bwd_dev", _ctx_of(x, ctx), _ptr(x, "x"), _ptr(dy, "dy"), rows, fin, fout, _ptr(w, "w"),
+         _ptr(dw, "dw"), _opt_ptr(db, "db"), _ptr(dx, "dx"))
+    return dx
+
+
+# ---------------------------------------------------------------- optim.rs
+
+
+def newton_schulz_(g, rows, cols, steps, ctx=None):
+    call("rnn_newton_schulz_dev", _ctx_of(g, ctx), _ptr(g, "g"), rows, cols, steps)
+    return g
+
+
+def muon_step_(v, g, m, rows, cols, steps, lr, mom=0.95, wd=0.0, decay=True, ctx=None):
+    call("rnn_muon_step_dev", _ctx_of(v, ctx), _ptr(v, "v"), _ptr(g, "g"), _ptr(m, "m"), rows, cols, steps, lr, mom,
+         wd, int(bool(decay)))
+    return v
+
+
+def adamw_step_(v, g, m, v2, lr, wd, decay, t, b1=0.9, b2=0.999, eps=1e-8, ctx=None):
+    call("rnn_adamw_step_dev", _ctx_of(v, ctx), _ptr(v, "v"), _ptr(g, "g"), _ptr(m, "m"), _ptr(v2, "v2"), v.numel(),
+         lr, wd, int(bool(decay)), b1, b2, eps, t)
+    return v
+
+
+def clip_(g, max_norm, ctx=None):
+    """Returns the pre-clip norm as a 1-element device tensor."""
+    norm = torch.empty(1, device=g.device, dtype=torch.float32)
+    call("rnn_clip_dev", _ctx_of(g, ctx), _ptr(g, "g"), g.numel(), max_norm, _ptr(norm, "norm"))
+    return norm
+
+
+def ema_update_(e, v, decay, t, ctx=None):
+    call("rnn_ema_update_dev", _ctx_of(e, ctx), _ptr(e, "e"), _ptr(v, "v"), e.numel(), decay, t)
+    return e
