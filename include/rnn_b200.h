@@ -215,6 +215,66 @@ int rnn_clip_dev(rnn_ctx *ctx, float *g, size_t n, float max, float *norm_out);
 int rnn_ema_update_dev(rnn_ctx *ctx, float *e, const float *v, size_t n,
                        float decay, int t);
 
+/* ---- rustvit glue (norm.rs, vit.rs, tok.rs, loss.rs); [n,t,c] tokens ---- */
+/* LayerScale (norm.rs:151-212): y = l * x per channel (y may alias x);
+ * backward: dl += sum dy*x, dx = l * dy. */
+int rnn_layerscale_fwd_dev(rnn_ctx *ctx, const float *x, int rows, int c,
+                           const float *l, float *y);
+int rnn_layerscale_bwd_dev(rnn_ctx *ctx, const float *dy, const float *x,
+                           int rows, int c, const float *l, float *dl, float *dx);
+/* SwiGLU gate (norm.rs:250-286): u = silu(a) * b from ab [rows, 2h]. */
+int rnn_swiglu_act_fwd_dev(rnn_ctx *ctx, const float *ab, int rows, int h,
+                           float *u);
+int rnn_swiglu_act_bwd_dev(rnn_ctx *ctx, const float *du, const float *ab,
+                           int rows, int h, float *dab);
+/* DwConv3 (norm.rs:304-451): depthwise 3x3 over the th x tw token grid,
+ * channels-last, w [9, c], b [c]; dw, db accumulate; dx written. */
+int rnn_dwconv3_fwd_dev(rnn_ctx *ctx, const float *x, int n, int th, int tw,
+                        int c, const float *w, const float *b, float *y);
+int rnn_dwconv3_bwd_dev(rnn_ctx *ctx, const float *dy, const float *x, int n,
+                        int th, int tw, int c, const float *w, float *dw,
+                        float *db, float *dx);
+/* SeqPool (norm.rs:466-581): w = softmax_t(x.p) [n,t], z = sum_t w x [n,c];
+ * dp accumulates, dx written. */
+int rnn_seqpool_fwd_dev(rnn_ctx *ctx, const float *x, int n, int t, int c,
+                        const float *p, float *z, float *w);
+int rnn_seqpool_bwd_dev(rnn_ctx *ctx, const float *dz, const float *x,
+                        const float *w, int n, int t, int c, const float *p,
+                        float *dp, float *dx);
+/* DropPath (vit.rs:30-74): per-image keep mask drawn from Rng::new(seed)
+ * exactly like the reference (mask [n] device, 1/keep or 0); x scaled in
+ * place.  The backward scales dy by the same mask. */
+int rnn_droppath_fwd_dev(rnn_ctx *ctx, float *x, int n, size_t per_image,
+                         float p, uint64_t seed, float *mask);
+int rnn_droppath_bwd_dev(rnn_ctx *ctx, float *dy, int n, size_t per_image,
+                         const float *mask);
+/* token_merge (vit.rs:586-624): [n, th*th, c] -> [n, (th/2)^2, 4c] (2x2
+ * neighbours concatenated); backward=1 copies the gradient back. */
+int rnn_token_merge_dev(rnn_ctx *ctx, const float *src, int n, int th, int c,
+                        float *dst, int backward);
+/* Tok::from_tensor / to_tensor (tok.rs:54-87): [n,c,hw] <-> [n,hw,c]. */
+int rnn_tok_layout_dev(rnn_ctx *ctx, const float *in, int n, int c, int hw,
+                       float *out, int to_nchw);
+/* TaxoHead (vit.rs:283-310): zf[i,k] += zc[i,parent[k]]; backward writes
+ * dc = dzc + scatter(dzf). */
+int rnn_taxo_combine_fwd_dev(rnn_ctx *ctx, float *zf, const float *zc, int n,
+                             int nf, int nc, const uint32_t *parent);
+int rnn_taxo_combine_bwd_dev(rnn_ctx *ctx, const float *dzf, const float *dzc,
+                             int n, int nf, int nc, const uint32_t *parent,
+                             float *dc);
+/* ce_soft (loss.rs:39-81): dz = scale * d(mean CE)/dz written; loss_out[0],
+ * correct_out[0] (device) when non-NULL. */
+int rnn_ce_soft_dev(rnn_ctx *ctx, const float *logits, const float *target,
+                    const uint32_t *hard, int n, int nclass, float scale,
+                    float *dz, float *loss_out, int *correct_out);
+/* kl_distill (loss.rs:87-130): T^2 KL(teacher || student); dz accumulates. */
+int rnn_kl_distill_dev(rnn_ctx *ctx, const float *student, const float *teacher,
+                       int n, int nclass, float temp, float scale, float *dz,
+                       float *loss_out);
+/* hint_mse (loss.rs:133-151): dz accumulates. */
+int rnn_hint_mse_dev(rnn_ctx *ctx, const float *pred, const float *target,
+                     int n, int c, float scale, float *dz, float *loss_out);
+
 /* ---- ResNet training step (model.rs, train.rs:684-699) ------------------ */
 /* ResNet::new(depth_n, width, nclass, seed) (model.rs:112-133), with the
  * reference's initialisation drawn from the same xoshiro256++ stream, so

@@ -101,6 +101,24 @@ def lib():
         "orc_adamw_step": (V, [_f32p, _f32p, _f32p, _f32p, Z, F, F, I, F, F, F, I]),
         "orc_clip": (F, [_f32p, Z, F]),
         "orc_ema_update": (V, [_f32p, _f32p, Z, F, I]),
+        "orc_layerscale_fwd": (V, [_f32p, I, I, _f32p, _f32p]),
+        "orc_layerscale_bwd": (V, [_f32p, _f32p, I, I, _f32p, _f32p, _f32p]),
+        "orc_swiglu_act_fwd": (V, [_f32p, I, I, _f32p]),
+        "orc_swiglu_act_bwd": (V, [_f32p, _f32p, I, I, _f32p]),
+        "orc_dwconv3_fwd": (V, [_f32p, I, I, I, I, _f32p, _f32p, _f32p]),
+        "orc_dwconv3_bwd": (V, [_f32p, _f32p, I, I, I, I, _f32p, _f32p, _f32p, _f32p]),
+        "orc_seqpool_fwd": (V, [_f32p, I, I, I, _f32p, _f32p, _f32p]),
+        "orc_seqpool_bwd": (V, [_f32p, _f32p, _f32p, I, I, I, _f32p, _f32p, _f32p]),
+        "orc_droppath_mask": (V, [I, F, U64, _f32p]),
+        "orc_token_merge_fwd": (V, [_f32p, I, I, I, _f32p]),
+        "orc_token_merge_bwd": (V, [_f32p, I, I, I, _f32p]),
+        "orc_tok_from_nchw": (V, [_f32p, I, I, I, _f32p]),
+        "orc_tok_to_nchw": (V, [_f32p, I, I, I, _f32p]),
+        "orc_taxo_fwd": (V, [_f32p, _f32p, I, I, I, _u32p]),
+        "orc_taxo_bwd": (V, [_f32p, _f32p, I, I, I, _u32p, _f32p]),
+        "orc_ce_soft": (F, [_f32p, _f32p, _u32p, I, I, F, _f32p, C.POINTER(C.c_int)]),
+        "orc_kl_distill": (F, [_f32p, _f32p, I, I, F, F, _f32p]),
+        "orc_hint_mse": (F, [_f32p, _f32p, I, I, F, _f32p]),
         "orc_set_threads": (V, [I]),
         "orc_get_threads": (I, []),
     }

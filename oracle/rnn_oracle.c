@@ -1337,3 +1337,273 @@ void orc_ema_update(float *e, const float *v, size_t n, float decay, int t) {
     float d = decay < cap ? decay : cap;
     for (size_t i = 0; i < n; i++) e[i] = d * e[i] + (1.0f - d) * v[i];
 }
+
+/* ======================================================================= */
+/* rustvit glue                                                             */
+/* ======================================================================= */
+
+void orc_layerscale_fwd(const float *x, int rows, int c, const float *l, float *y) {
+    for (size_t i = 0; i < (size_t)rows * c; i++) y[i] = x[i] * l[i % c];
+}
+
+void orc_layerscale_bwd(const float *dy, const float *x, int rows, int c, const float *l, float *dl,
+                        float *dx) {
+    for (int r = 0; r < rows; r++)
+        for (int j = 0; j < c; j++) dl[j] += dy[(size_t)r * c + j] * x[(size_t)r * c + j];
+    for (size_t i = 0; i < (size_t)rows * c; i++) dx[i] = dy[i] * l[i % c];
+}
+
+static float sigmoidf_(float z) { return 1.0f / (1.0f + expf(-z)); }
+
+void orc_swiglu_act_fwd(const float *ab, int rows, int h, float *u) {
+    for (int r = 0; r < rows; r++)
+        for (int j = 0; j < h; j++) {
+            float a = ab[(size_t)r * 2 * h + j];
+            u[(size_t)r * h + j] = a * sigmoidf_(a) * ab[(size_t)r * 2 * h + h + j];
+        }
+}
+
+void orc_swiglu_act_bwd(const float *du, const float *ab, int rows, int h, float *dab) {
+    for (int r = 0; r < rows; r++)
+        for (int j = 0; j < h; j++) {
+            float a = ab[(size_t)r * 2 * h + j], b = ab[(size_t)r * 2 * h + h + j];
+            float s = sigmoidf_(a), d = du[(size_t)r * h + j];
+            dab[(size_t)r * 2 * h + j] = d * b * s * (1.0f + a * (1.0f - s));
+            dab[(size_t)r * 2 * h + h + j] = d * a * s;
+        }
+}
+
+void orc_dwconv3_fwd(const float *x, int n, int th, int tw, int c, const float *w, const float *b,
+                     float *y) {
+    size_t img = (size_t)th * tw * c;
+    for (int i = 0; i < n; i++) {
+        const float *xi = x + i * img;
+        float *yi = y + i * img;
+        for (int oy = 0; oy < th; oy++)
+            for (int ox = 0; ox < tw; ox++) {
+                float *dst = yi + ((size_t)oy * tw + ox) * c;
+                for (int j = 0; j < c; j++) dst[j] = b[j];
+                for (int ky = 0; ky < 3; ky++) {
+                    int sy = oy + ky - 1;
+                    if (sy < 0 || sy >= th) continue;
+                    for (int kx = 0; kx < 3; kx++) {
+                        int sx = ox + kx - 1;
+                        if (sx < 0 || sx >= tw) continue;
+                        const float *wr = w + (size_t)(ky * 3 + kx) * c;
+                        const float *src = xi + ((size_t)sy * tw + sx) * c;
+                        for (int j = 0; j < c; j++) dst[j] += wr[j] * src[j];
+                    }
+                }
+            }
+    }
+}
+
+void orc_dwconv3_bwd(const float *dy, const float *x, int n, int th, int tw, int c, const float *w,
+                     float *dw, float *db, float *dx) {
+    size_t img = (size_t)th * tw * c;
+    memset(dx, 0, sizeof(float) * img * n);
+    for (int i = 0; i < n; i++) {
+        const float *dyi = dy + i * img, *xi = x + i * img;
+        float *dxi = dx + i * img;
+        for (int oy = 0; oy < th; oy++)
+            for (int ox = 0; ox < tw; ox++) {
+                const float *d = dyi + ((size_t)oy * tw + ox) * c;
+                for (int j = 0; j < c; j++) db[j] += d[j];
+                for (int ky = 0; ky < 3; ky++) {
+                    int sy = oy + ky - 1;
+                    if (sy < 0 || sy >= th) continue;
+                    for (int kx = 0; kx < 3; kx++) {
+                        int sx = ox + kx - 1;
+                        if (sx < 0 || sx >= tw) continue;
+                        size_t s = ((size_t)sy * tw + sx) * c;
+                        float *acc = dw + (size_t)(ky * 3 + kx) * c;
+                        const float *wr = w + (size_t)(ky * 3 + kx) * c;
+                        for (int j = 0; j < c; j++) {
+                            acc[j] += d[j] * xi[s + j];
+                            dxi[s + j] += wr[j] * d[j];
+                        }
+                    }
+                }
+            }
+    }
+}
+
+void orc_seqpool_fwd(const float *x, int n, int t, int c, const float *p, float *z, float *w) {
+    for (int i = 0; i < n; i++) {
+        const float *xi = x + (size_t)i * t * c;
+        float *wi = w + (size_t)i * t, *zi = z + (size_t)i * c;
+        float mx = -INFINITY;
+        for (int j = 0; j < t; j++) {
+            float s = 0.0f;
+            for (int k = 0; k < c; k++) s += xi[(size_t)j * c + k] * p[k];
+            wi[j] = s;
+            if (s > mx) mx = s;
+        }
+        float sum = 0.0f;
+        for (int j = 0; j < t; j++) { wi[j] = expf(wi[j] - mx); sum += wi[j]; }
+        float inv = 1.0f / sum;
+        for (int k = 0; k < c; k++) zi[k] = 0.0f;
+        for (int j = 0; j < t; j++) {
+            wi[j] *= inv;
+            for (int k = 0; k < c; k++) zi[k] += wi[j] * xi[(size_t)j * c + k];
+        }
+    }
+}
+
+void orc_seqpool_bwd(const float *dz, const float *x, const float *w, int n, int t, int c,
+                     const float *p, float *dp, float *dx) {
+    float *dwv = (float *)malloc(sizeof(float) * t);
+    memset(dx, 0, sizeof(float) * (size_t)n * t * c);
+    for (int i = 0; i < n; i++) {
+        const float *xi = x + (size_t)i * t * c, *wi = w + (size_t)i * t, *dzi = dz + (size_t)i * c;
+        float *dxi = dx + (size_t)i * t * c;
+        float dot = 0.0f;
+        for (int j = 0; j < t; j++) {
+            float s = 0.0f;
+            for (int k = 0; k < c; k++) {
+                s += dzi[k] * xi[(size_t)j * c + k];
+                dxi[(size_t)j * c + k] += wi[j] * dzi[k];
+            }
+            dwv[j] = s;
+            dot += s * wi[j];
+        }
+        for (int j = 0; j < t; j++) {
+            float ds = wi[j] * (dwv[j] - dot);
+            for (int k = 0; k < c; k++) {
+                dp[k] += ds * xi[(size_t)j * c + k];
+                dxi[(size_t)j * c + k] += ds * p[k];
+            }
+        }
+    }
+    free(dwv);
+}
+
+void orc_droppath_mask(int n, float p, uint64_t seed, float *mask) {
+    float keep = 1.0f - p;
+    orc_rng r;
+    orc_rng_new(&r, seed);
+    for (int i = 0; i < n; i++) mask[i] = orc_rng_uniform(&r) < keep ? 1.0f / keep : 0.0f;
+}
+
+void orc_token_merge_fwd(const float *z, int n, int th, int c, float *y) {
+    int t2 = th / 2;
+    const int dys[4] = {0, 0, 1, 1}, dxs[4] = {0, 1, 0, 1};
+    for (int i = 0; i < n; i++)
+        for (int oy = 0; oy < t2; oy++)
+            for (int ox = 0; ox < t2; ox++)
+                for (int q = 0; q < 4; q++) {
+                    const float *src = z + (((size_t)i * th + 2 * oy + dys[q]) * th + 2 * ox + dxs[q]) * c;
+                    float *dst = y + (((size_t)i * t2 + oy) * t2 + ox) * 4 * c + (size_t)q * c;
+                    memcpy(dst, src, sizeof(float) * c);
+                }
+}
+
+void orc_token_merge_bwd(const float *dy, int n, int th, int c, float *dz) {
+    int t2 = th / 2;
+    const int dys[4] = {0, 0, 1, 1}, dxs[4] = {0, 1, 0, 1};
+    for (int i = 0; i < n; i++)
+        for (int oy = 0; oy < t2; oy++)
+            for (int ox = 0; ox < t2; ox++)
+                for (int q = 0; q < 4; q++) {
+                    float *dst = dz + (((size_t)i * th + 2 * oy + dys[q]) * th + 2 * ox + dxs[q]) * c;
+                    const float *src = dy + (((size_t)i * t2 + oy) * t2 + ox) * 4 * c + (size_t)q * c;
+                    memcpy(dst, src, sizeof(float) * c);
+                }
+}
+
+void orc_tok_from_nchw(const float *x, int n, int c, int hw, float *y) {
+    for (int i = 0; i < n; i++)
+        for (int ci = 0; ci < c; ci++)
+            for (int q = 0; q < hw; q++)
+                y[((size_t)i * hw + q) * c + ci] = x[((size_t)i * c + ci) * hw + q];
+}
+
+void orc_tok_to_nchw(const float *x, int n, int c, int hw, float *y) {
+    for (int i = 0; i < n; i++)
+        for (int ci = 0; ci < c; ci++)
+            for (int q = 0; q < hw; q++)
+                y[((size_t)i * c + ci) * hw + q] = x[((size_t)i * hw + q) * c + ci];
+}
+
+void orc_taxo_fwd(float *zf, const float *zc, int n, int nf, int nc, const uint32_t *parent) {
+    for (int i = 0; i < n; i++)
+        for (int k = 0; k < nf; k++) zf[(size_t)i * nf + k] += zc[(size_t)i * nc + parent[k]];
+}
+
+void orc_taxo_bwd(const float *dzf, const float *dzc, int n, int nf, int nc, const uint32_t *parent,
+                  float *dc) {
+    for (int i = 0; i < n; i++) {
+        memcpy(dc + (size_t)i * nc, dzc + (size_t)i * nc, sizeof(float) * nc);
+        for (int k = 0; k < nf; k++) dc[(size_t)i * nc + parent[k]] += dzf[(size_t)i * nf + k];
+    }
+}
+
+float orc_ce_soft(const float *logits, const float *target, const uint32_t *hard, int n, int nclass,
+                  float scale, float *dz, int *correct) {
+    float inv = 1.0f / (float)n, loss = 0.0f;
+    int corr = 0;
+    for (int i = 0; i < n; i++) {
+        const float *z = logits + (size_t)i * nclass, *t = target + (size_t)i * nclass;
+        float *d = dz + (size_t)i * nclass;
+        float mx = -INFINITY;
+        int arg = 0;
+        for (int j = 0; j < nclass; j++)
+            if (z[j] > mx) { mx = z[j]; arg = j; }
+        float sum = 0.0f;
+        for (int j = 0; j < nclass; j++) { d[j] = expf(z[j] - mx); sum += d[j]; }
+        float lse = mx + logf(sum), l = 0.0f;
+        for (int j = 0; j < nclass; j++) {
+            l += t[j] * (lse - z[j]);
+            d[j] = (d[j] / sum - t[j]) * inv * scale;
+        }
+        loss += l;
+        corr += arg == (int)hard[i];
+    }
+    if (correct) *correct = corr;
+    return loss * inv;
+}
+
+float orc_kl_distill(const float *s, const float *t, int n, int nclass, float temp, float scale,
+                     float *dz) {
+    float inv = 1.0f / (float)n, it = 1.0f / temp, total = 0.0f;
+    float *ps = (float *)malloc(sizeof(float) * nclass), *pt = (float *)malloc(sizeof(float) * nclass);
+    for (int i = 0; i < n; i++) {
+        const float *zs = s + (size_t)i * nclass, *zt = t + (size_t)i * nclass;
+        float *d = dz + (size_t)i * nclass;
+        for (int pass = 0; pass < 2; pass++) {
+            const float *z = pass ? zt : zs;
+            float *o = pass ? pt : ps;
+            float mx = -INFINITY;
+            for (int j = 0; j < nclass; j++) mx = z[j] > mx ? z[j] : mx;
+            float sm = 0.0f;
+            for (int j = 0; j < nclass; j++) { o[j] = expf((z[j] - mx) * it); sm += o[j]; }
+            float is = 1.0f / sm;
+            for (int j = 0; j < nclass; j++) o[j] *= is;
+        }
+        float l = 0.0f;
+        for (int j = 0; j < nclass; j++) {
+            if (pt[j] > 1e-9f) {
+                float a = pt[j] > 1e-9f ? pt[j] : 1e-9f, b = ps[j] > 1e-9f ? ps[j] : 1e-9f;
+                l += pt[j] * (logf(a) - logf(b));
+            }
+            d[j] += temp * (ps[j] - pt[j]) * inv * scale;
+        }
+        total += l * temp * temp;
+    }
+    free(ps); free(pt);
+    return total * inv;
+}
+
+float orc_hint_mse(const float *pred, const float *target, int n, int c, float scale, float *dz) {
+    float inv = 1.0f / (float)((size_t)n * c), l = 0.0f;
+    for (int i = 0; i < n; i++) {
+        float s = 0.0f;
+        for (int j = 0; j < c; j++) {
+            float e = pred[(size_t)i * c + j] - target[(size_t)i * c + j];
+            s += e * e;
+            dz[(size_t)i * c + j] += 2.0f * e * inv * scale;
+        }
+        l += s;
+    }
+    return l * inv * scale;
+}

@@ -173,6 +173,35 @@ float orc_clip(float *g, size_t n, float max);
 /* Ema::update for t >= 2 (optim.rs:270-287): e = d e + (1-d) v */
 void orc_ema_update(float *e, const float *v, size_t n, float decay, int t);
 
+/* ---- rustvit glue (norm.rs, vit.rs, tok.rs, loss.rs) -------------------- */
+void orc_layerscale_fwd(const float *x, int rows, int c, const float *l, float *y);      /* norm.rs:170-181 */
+void orc_layerscale_bwd(const float *dy, const float *x, int rows, int c, const float *l,
+                        float *dl, float *dx);                                           /* norm.rs:183-212 */
+void orc_swiglu_act_fwd(const float *ab, int rows, int h, float *u);                     /* norm.rs:250-266 */
+void orc_swiglu_act_bwd(const float *du, const float *ab, int rows, int h, float *dab);  /* norm.rs:272-286 */
+void orc_dwconv3_fwd(const float *x, int n, int th, int tw, int c, const float *w,
+                     const float *b, float *y);                                          /* norm.rs:328-368 */
+void orc_dwconv3_bwd(const float *dy, const float *x, int n, int th, int tw, int c,
+                     const float *w, float *dw, float *db, float *dx);                   /* norm.rs:370-451 */
+void orc_seqpool_fwd(const float *x, int n, int t, int c, const float *p, float *z,
+                     float *w);                                                          /* norm.rs:488-528 */
+void orc_seqpool_bwd(const float *dz, const float *x, const float *w, int n, int t, int c,
+                     const float *p, float *dp, float *dx);                              /* norm.rs:530-581 */
+void orc_droppath_mask(int n, float p, uint64_t seed, float *mask);                      /* vit.rs:40-60 */
+void orc_token_merge_fwd(const float *z, int n, int th, int c, float *y);                /* vit.rs:586-604 */
+void orc_token_merge_bwd(const float *dy, int n, int th, int c, float *dz);              /* vit.rs:606-624 */
+void orc_tok_from_nchw(const float *x, int n, int c, int hw, float *y);                  /* tok.rs:54-68 */
+void orc_tok_to_nchw(const float *x, int n, int c, int hw, float *y);                    /* tok.rs:71-87 */
+void orc_taxo_fwd(float *zf, const float *zc, int n, int nf, int nc, const uint32_t *parent); /* vit.rs:283-295 */
+void orc_taxo_bwd(const float *dzf, const float *dzc, int n, int nf, int nc,
+                  const uint32_t *parent, float *dc);                                    /* vit.rs:297-310 */
+float orc_ce_soft(const float *logits, const float *target, const uint32_t *hard, int n,
+                  int nclass, float scale, float *dz, int *correct);                     /* loss.rs:39-81 */
+float orc_kl_distill(const float *s, const float *t, int n, int nclass, float temp,
+                     float scale, float *dz);                                            /* loss.rs:87-130 */
+float orc_hint_mse(const float *pred, const float *target, int n, int c, float scale,
+                   float *dz);                                                           /* loss.rs:133-151 */
+
 /* ---- threads ------------------------------------------------------------ */
 void orc_set_threads(int n);
 int  orc_get_threads(void);

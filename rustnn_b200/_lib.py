@@ -77,6 +77,23 @@ SIGS = {
     "rnn_adamw_step_dev": [CTX, FP, FP, FP, FP, Z, F, F, I, F, F, F, I],
     "rnn_clip_dev": [CTX, FP, Z, F, FP],
     "rnn_ema_update_dev": [CTX, FP, FP, Z, F, I],
+    "rnn_layerscale_fwd_dev": [CTX, FP, I, I, FP, FP],
+    "rnn_layerscale_bwd_dev": [CTX, FP, FP, I, I, FP, FP, FP],
+    "rnn_swiglu_act_fwd_dev": [CTX, FP, I, I, FP],
+    "rnn_swiglu_act_bwd_dev": [CTX, FP, FP, I, I, FP],
+    "rnn_dwconv3_fwd_dev": [CTX, FP, I, I, I, I, FP, FP, FP],
+    "rnn_dwconv3_bwd_dev": [CTX, FP, FP, I, I, I, I, FP, FP, FP, FP],
+    "rnn_seqpool_fwd_dev": [CTX, FP, I, I, I, FP, FP, FP],
+    "rnn_seqpool_bwd_dev": [CTX, FP, FP, FP, I, I, I, FP, FP, FP],
+    "rnn_droppath_fwd_dev": [CTX, FP, I, Z, F, U64, FP],
+    "rnn_droppath_bwd_dev": [CTX, FP, I, Z, FP],
+    "rnn_token_merge_dev": [CTX, FP, I, I, I, FP, I],
+    "rnn_tok_layout_dev": [CTX, FP, I, I, I, FP, I],
+    "rnn_taxo_combine_fwd_dev": [CTX, FP, FP, I, I, I, FP],
+    "rnn_taxo_combine_bwd_dev": [CTX, FP, FP, I, I, I, FP, FP],
+    "rnn_ce_soft_dev": [CTX, FP, FP, FP, I, I, F, FP, FP, FP],
+    "rnn_kl_distill_dev": [CTX, FP, FP, I, I, F, F, FP, FP],
+    "rnn_hint_mse_dev": [CTX, FP, FP, I, I, F, FP, FP],
     "rnn_resnet_create": [CTX, I, I, I, U64, C.POINTER(NET)],
     "rnn_resnet_destroy": [NET],
     "rnn_resnet_num_params": [NET, C.POINTER(Z)],

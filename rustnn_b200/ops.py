@@ -26,6 +26,9 @@ __all__ = [
     "add_relu_", "gap_forward", "gap_backward", "softmax_ce", "sgd_nesterov_", "out_dim", "RnnError",
     "rel_index", "attn_forward", "attn_backward", "layernorm_forward", "layernorm_backward", "linear_forward",
     "linear_backward", "newton_schulz_", "muon_step_", "adamw_step_", "clip_", "ema_update_",
+    "layerscale_forward", "layerscale_backward", "swiglu_forward", "swiglu_backward", "dwconv3_forward",
+    "dwconv3_backward", "seqpool_forward", "seqpool_backward", "droppath_forward_", "droppath_backward_",
+    "token_merge", "tok_layout", "taxo_forward_", "taxo_backward", "ce_soft", "kl_distill", "hint_mse",
 ]
 
 
@@ -324,3 +327,120 @@ def clip_(g, max_norm, ctx=None):
 def ema_update_(e, v, decay, t, ctx=None):
     call("rnn_ema_update_dev", _ctx_of(e, ctx), _ptr(e, "e"), _ptr(v, "v"), e.numel(), decay, t)
     return e
+
+
+# ---------------------------------------------------------------- rustvit glue
+
+
+def _new(shape_numel, like):
+    return torch.empty(shape_numel, device=like.device, dtype=torch.float32)
+
+
+def layerscale_forward(x, rows, c, l, out=None, ctx=None):
+    y = out if out is not None else torch.empty_like(x)
+    call("rnn_layerscale_fwd_dev", _ctx_of(x, ctx), _ptr(x, "x"), rows, c, _ptr(l, "l"), _ptr(y, "y"))
+    return y
+
+
+def layerscale_backward(dy, x, rows, c, l, dl, ctx=None):
+    dx = torch.empty_like(dy)
+    call("rnn_layerscale_bwd_dev", _ctx_of(dy, ctx), _ptr(dy, "dy"), _ptr(x, "x"), rows, c, _ptr(l, "l"),
+         _ptr(dl, "dl"), _ptr(dx, "dx"))
+    return dx
+
+
+def swiglu_forward(ab, rows, h, ctx=None):
+    u = _new(rows * h, ab)
+    call("rnn_swiglu_act_fwd_dev", _ctx_of(ab, ctx), _ptr(ab, "ab"), rows, h, _ptr(u, "u"))
+    return u
+
+
+def swiglu_backward(du, ab, rows, h, ctx=None):
+    dab = torch.empty_like(ab)
+    call("rnn_swiglu_act_bwd_dev", _ctx_of(du, ctx), _ptr(du, "du"), _ptr(ab, "ab"), rows, h, _ptr(dab, "dab"))
+    return dab
+
+
+def dwconv3_forward(x, n, th, tw, c, w, b, ctx=None):
+    y = torch.empty_like(x)
+    call("rnn_dwconv3_fwd_dev", _ctx_of(x, ctx), _ptr(x, "x"), n, th, tw, c, _ptr(w, "w"), _ptr(b, "b"), _ptr(y, "y"))
+    return y
+
+
+def dwconv3_backward(dy, x, n, th, tw, c, w, dw, db, ctx=None):
+    dx = torch.empty_like(dy)
+    call("rnn_dwconv3_bwd_dev", _ctx_of(dy, ctx), _ptr(dy, "dy"), _ptr(x, "x"), n, th, tw, c, _ptr(w, "w"),
+         _ptr(dw, "dw"), _ptr(db, "db"), _ptr(dx, "dx"))
+    return dx
+
+
+def seqpool_forward(x, n, t, c, p, ctx=None):
+    z, w = _new(n * c, x), _new(n * t, x)
+    call("rnn_seqpool_fwd_dev", _ctx_of(x, ctx), _ptr(x, "x"), n, t, c, _ptr(p, "p"), _ptr(z, "z"), _ptr(w, "w"))
+    return z, w
+
+
+def seqpool_backward(dz, x, w, n, t, c, p, dp, ctx=None):
+    dx = torch.empty_like(x)
+    call("rnn_seqpool_bwd_dev", _ctx_of(dz, ctx), _ptr(dz, "dz"), _ptr(x, "x"), _ptr(w, "w"), n, t, c, _ptr(p, "p"),
+         _ptr(dp, "dp"), _ptr(dx, "dx"))
+    return dx
+
+
+def droppath_forward_(x, n, per_image, p, seed, ctx=None):
+    mask = _new(n, x)
+    call("rnn_droppath_fwd_dev", _ctx_of(x, ctx), _ptr(x, "x"), n, per_image, p, seed & (2**64 - 1), _ptr(mask, "mask"))
+    return mask
+
+
+def droppath_backward_(dy, n, per_image, mask, ctx=None):
+    call("rnn_droppath_bwd_dev", _ctx_of(dy, ctx), _ptr(dy, "dy"), n, per_image, _ptr(mask, "mask"))
+    return dy
+
+
+def token_merge(src, n, th, c, backward=False, ctx=None):
+    dst = torch.empty_like(src)
+    call("rnn_token_merge_dev", _ctx_of(src, ctx), _ptr(src, "src"), n, th, c, _ptr(dst, "dst"), int(bool(backward)))
+    return dst
+
+
+def tok_layout(x, n, c, hw, to_nchw=False, ctx=None):
+    y = torch.empty_like(x)
+    call("rnn_tok_layout_dev", _ctx_of(x, ctx), _ptr(x, "x"), n, c, hw, _ptr(y, "y"), int(bool(to_nchw)))
+    return y
+
+
+def taxo_forward_(zf, zc, n, nf, nc, parent, ctx=None):
+    call("rnn_taxo_combine_fwd_dev", _ctx_of(zf, ctx), _ptr(zf, "zf"), _ptr(zc, "zc"), n, nf, nc, _ptr(parent, "parent"))
+    return zf
+
+
+def taxo_backward(dzf, dzc, n, nf, nc, parent, ctx=None):
+    dc = torch.empty_like(dzc)
+    call("rnn_taxo_combine_bwd_dev", _ctx_of(dzf, ctx), _ptr(dzf, "dzf"), _ptr(dzc, "dzc"), n, nf, nc,
+         _ptr(parent, "parent"), _ptr(dc, "dc"))
+    return dc
+
+
+def ce_soft(logits, target, hard, nclass, scale=1.0, ctx=None):
+    n = hard.numel()
+    dz = torch.empty_like(logits)
+    loss = _new(1, logits)
+    corr = torch.empty(1, device=logits.device, dtype=torch.int32)
+    call("rnn_ce_soft_dev", _ctx_of(logits, ctx), _ptr(logits, "logits"), _ptr(target, "target"), _ptr(hard, "hard"), n,
+         nclass, scale, _ptr(dz, "dz"), _ptr(loss, "loss"), _ptr(corr, "correct"))
+    return loss, dz, corr
+
+
+def kl_distill(student, teacher, n, nclass, temp, scale, dz, ctx=None):
+    loss = _new(1, student)
+    call("rnn_kl_distill_dev", _ctx_of(student, ctx), _ptr(student, "student"), _ptr(teacher, "teacher"), n, nclass,
+         temp, scale, _ptr(dz, "dz"), _ptr(loss, "loss"))
+    return loss
+
+
+def hint_mse(pred, target, n, c, scale, dz, ctx=None):
+    loss = _new(1, pred)
+    call("rnn_hint_mse_dev", _ctx_of(pred, ctx), _ptr(pred, "pred"), _ptr(target, "target"), n, c, scale,
+         _ptr(dz, "dz"), _ptr(loss, "loss"))
+    return loss

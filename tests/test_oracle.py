@@ -334,3 +334,117 @@ def test_newton_schulz_band(m, n):
     g = O.Rng(m * 100 + n).rand_vec(m * n)
     out = O.newton_schulz(g, m, n, 5)
     assert gram_error(out, m, n) < 0.5
+
+
+# ------------------------------------------------------------------ rustvit glue (check.rs normcheck / losses)
+
+
+def _gc(x, g, f, rng):
+    return dircheck(x, g, EPS, rng, f)
+
+
+def test_glue_gradchecks():
+    L = O.lib()
+    rng = O.Rng(2024)
+    n, th, c = 3, 3, 8
+    rows = n * th * th
+    x = rng.rand_vec(rows * c)
+    r = rng.rand_vec(rows * c)
+    # LayerScale (norm.rs:151-212)
+    lv = rng.rand_vec(c)
+    fwd = lambda xx, ll: (lambda y: (L.orc_layerscale_fwd(np.ascontiguousarray(xx, np.float32), rows, c,
+                                                          np.ascontiguousarray(ll, np.float32), y), y)[1])(
+        np.empty(rows * c, np.float32))
+    dl, dx = np.zeros(c, np.float32), np.empty(rows * c, np.float32)
+    L.orc_layerscale_bwd(r, x, rows, c, lv, dl, dx)
+    assert _gc(x, dx, lambda v: float(np.dot(fwd(v, lv), r)), rng) < TOL
+    assert _gc(lv, dl, lambda v: float(np.dot(fwd(x, v), r)), rng) < TOL
+    # SwiGLU gate (norm.rs:250-286)
+    h = 6
+    ab = rng.rand_vec(rows * 2 * h)
+    ru = rng.rand_vec(rows * h)
+    act = lambda v: (lambda u: (L.orc_swiglu_act_fwd(np.ascontiguousarray(v, np.float32), rows, h, u), u)[1])(
+        np.empty(rows * h, np.float32))
+    dab = np.empty(rows * 2 * h, np.float32)
+    L.orc_swiglu_act_bwd(ru, ab, rows, h, dab)
+    assert _gc(ab, dab, lambda v: float(np.dot(act(v), ru)), rng) < TOL
+    # DwConv3 (norm.rs:304-451)
+    w, b = (0.1 * rng.rand_vec(9 * c)).astype(np.float32), rng.rand_vec(c)
+    dwf = lambda xx, ww, bb: (lambda y: (L.orc_dwconv3_fwd(np.ascontiguousarray(xx, np.float32), n, th, th, c,
+                                                            np.ascontiguousarray(ww, np.float32),
+                                                            np.ascontiguousarray(bb, np.float32), y), y)[1])(
+        np.empty(rows * c, np.float32))
+    dw, db, dx = np.zeros(9 * c, np.float32), np.zeros(c, np.float32), np.empty(rows * c, np.float32)
+    L.orc_dwconv3_bwd(r, x, n, th, th, c, w, dw, db, dx)
+    assert _gc(x, dx, lambda v: float(np.dot(dwf(v, w, b), r)), rng) < TOL
+    assert _gc(w, dw, lambda v: float(np.dot(dwf(x, v, b), r)), rng) < TOL
+    assert _gc(b, db, lambda v: float(np.dot(dwf(x, w, v), r)), rng) < TOL
+    # SeqPool (norm.rs:466-581)
+    t = th * th
+    pv = rng.rand_vec(c)
+    rz = rng.rand_vec(n * c)
+
+    def sp(xx, pp):
+        z, wt = np.empty(n * c, np.float32), np.empty(n * t, np.float32)
+        L.orc_seqpool_fwd(np.ascontiguousarray(xx, np.float32), n, t, c, np.ascontiguousarray(pp, np.float32), z, wt)
+        return z, wt
+
+    _, wt = sp(x, pv)
+    dp, dx = np.zeros(c, np.float32), np.empty(rows * c, np.float32)
+    L.orc_seqpool_bwd(rz, x, wt, n, t, c, pv, dp, dx)
+    assert _gc(x, dx, lambda v: float(np.dot(sp(v, pv)[0], rz)), rng) < TOL
+    assert _gc(pv, dp, lambda v: float(np.dot(sp(x, v)[0], rz)), rng) < TOL
+
+
+def test_loss_gradchecks():
+    """check.rs:678-722 (ce_soft, kl_distill) and hint_mse."""
+    L = O.lib()
+    rng = O.Rng(77)
+    n, nc = 4, 7
+    z = rng.rand_vec(n * nc)
+    labels = np.array([rng.below(nc) for _ in range(n)], np.uint32)
+    t = np.abs(rng.rand_vec(n * nc)) + 0.1
+    t = (t.reshape(n, nc) / t.reshape(n, nc).sum(1, keepdims=True)).astype(np.float32).ravel()
+    d = np.empty(n * nc, np.float32)
+    L.orc_ce_soft(z, t, labels, n, nc, 1.0, d, None)
+    tmp = np.empty(n * nc, np.float32)
+    assert dircheck(z, d, EPS, rng, lambda v: L.orc_ce_soft(np.ascontiguousarray(v, np.float32), t, labels, n, nc,
+                                                            1.0, tmp, None)) < TOL
+    teach = rng.rand_vec(n * nc)
+    d = np.zeros(n * nc, np.float32)
+    L.orc_kl_distill(z, teach, n, nc, 2.0, 1.0, d)
+
+    def kl(v):
+        tmp2 = np.zeros(n * nc, np.float32)
+        return L.orc_kl_distill(np.ascontiguousarray(v, np.float32), teach, n, nc, 2.0, 1.0, tmp2)
+
+    assert dircheck(z, d, EPS, rng, kl) < TOL
+    pred, tgt = rng.rand_vec(n * 5), rng.rand_vec(n * 5)
+    d = np.zeros(n * 5, np.float32)
+    L.orc_hint_mse(pred, tgt, n, 5, 0.7, d)
+
+    def hm(v):
+        tmp3 = np.zeros(n * 5, np.float32)
+        return L.orc_hint_mse(np.ascontiguousarray(v, np.float32), tgt, n, 5, 0.7, tmp3)
+
+    assert dircheck(pred, d, EPS, rng, hm) < TOL
+
+
+def test_layout_round_trips():
+    L = O.lib()
+    rng = O.Rng(3)
+    n, th, c = 2, 4, 3
+    z = rng.rand_vec(n * th * th * c)
+    y, back = np.empty_like(z), np.empty_like(z)
+    L.orc_token_merge_fwd(z, n, th, c, y)
+    L.orc_token_merge_bwd(y, n, th, c, back)
+    assert np.array_equal(back, z)
+    # merged token (0,0) holds source tokens (0,0), (0,1), (1,0), (1,1)
+    zz = z.reshape(n, th, th, c)
+    assert np.array_equal(y.reshape(n, 4, 4 * c)[0, 0], np.concatenate([zz[0, 0, 0], zz[0, 0, 1], zz[0, 1, 0], zz[0, 1, 1]]))
+    x = rng.rand_vec(n * c * 16)
+    tk, nchw = np.empty_like(x), np.empty_like(x)
+    L.orc_tok_from_nchw(x, n, c, 16, tk)
+    L.orc_tok_to_nchw(tk, n, c, 16, nchw)
+    assert np.array_equal(nchw, x)
+    assert np.array_equal(tk.reshape(n, 16, c), x.reshape(n, c, 16).transpose(0, 2, 1))
