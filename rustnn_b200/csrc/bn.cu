@@ -10,6 +10,8 @@
 // dx = gamma*invstd/m * (m*dy - sum(dy) - xhat*sum(dy*xhat)).  An optional
 // relu_out mask applies relu_back_ (nn.rs:433) to dy on the fly.
 #include <algorithm>
+#include <cstdint>
+#include <initializer_list>
 
 #include "bn.cuh"
 
@@ -40,35 +42,58 @@ static __device__ __forceinline__ void block_sum2(double a, double b, double* ou
 }
 
 constexpr int BN_NT = 256;
+constexpr int BN_U = 4;  // float4 loads in flight per thread and stream
 
-// grid (C, P): block (c, p) sums images [n*p/P, n*(p+1)/P) of channel c.
+// grid (C, P): block (c, p) sums the planes of images [n*p/P, n*(p+1)/P) of
+// channel c.  Scalar form, for hw % 4 != 0 or unaligned tensors.
 __global__ void __launch_bounds__(BN_NT) bn_fwd_partial_kernel(const float* __restrict__ y, int n, int C,
                                                              int hw, int P, double* __restrict__ part) {
   const int c = blockIdx.x, p = blockIdx.y;
   const int i0 = (int)((long)n * p / P), i1 = (int)((long)n * (p + 1) / P);
   double s = 0.0, s2 = 0.0;
-  const bool vec = (hw & 3) == 0;
   for (int img = i0; img < i1; img++) {
     const float* plane = y + ((size_t)img * C + c) * hw;
-    if (vec) {
-      const float4* p4 = reinterpret_cast<const float4*>(plane);
-      for (int q = threadIdx.x; q < hw / 4; q += BN_NT) {
-        float4 v = __ldg(p4 + q);
-        s += (double)v.x + (double)v.y + (double)v.z + (double)v.w;
-        s2 += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
-      }
-    } else {
-      for (int q = threadIdx.x; q < hw; q += BN_NT) {
-        double v = __ldg(plane + q);
-        s += v;
-        s2 += v * v;
-      }
+    for (int q = threadIdx.x; q < hw; q += BN_NT) {
+      double v = __ldg(plane + q);
+      s += v;
+      s2 += v * v;
     }
   }
   block_sum2<BN_NT>(s, s2, part + ((size_t)c * P + p) * 2);
 }
 
-// Backward partials: sum dy_eff and dy_eff * xhat.
+// Vector form: the block's planes are flattened into one float4 index space
+// (so small planes still occupy every thread) and each thread keeps BN_U
+// independent loads in flight.
+__global__ void __launch_bounds__(BN_NT) bn_fwd_partial4_kernel(const float4* __restrict__ y, int n, int C,
+                                                              int hw4, int P, double* __restrict__ part) {
+  const int c = blockIdx.x, p = blockIdx.y;
+  const int i0 = (int)((long)n * p / P), i1 = (int)((long)n * (p + 1) / P);
+  const unsigned tot = (unsigned)(i1 - i0) * (unsigned)hw4;
+  double s = 0.0, s2 = 0.0;
+  for (unsigned j = threadIdx.x; j < tot; j += BN_NT * BN_U) {
+    float4 v[BN_U];
+#pragma unroll
+    for (int u = 0; u < BN_U; u++) {
+      const unsigned jj = j + u * BN_NT;
+      if (jj < tot) {
+        const unsigned img = jj / (unsigned)hw4, q = jj - img * (unsigned)hw4;
+        v[u] = __ldg(y + ((size_t)(i0 + img) * C + c) * hw4 + q);
+      } else {
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < BN_U; u++) {
+      s += (double)v[u].x + (double)v[u].y + (double)v[u].z + (double)v[u].w;
+      s2 += (double)v[u].x * v[u].x + (double)v[u].y * v[u].y + (double)v[u].z * v[u].z +
+            (double)v[u].w * v[u].w;
+    }
+  }
+  block_sum2<BN_NT>(s, s2, part + ((size_t)c * P + p) * 2);
+}
+
+// Backward partials: sum dy_eff * xhat and dy_eff (scalar form).
 __global__ void __launch_bounds__(BN_NT) bn_bwd_partial_kernel(const float* __restrict__ dy,
                                                              const float* __restrict__ y,
                                                              const float* __restrict__ relu_out, int n,
@@ -88,6 +113,55 @@ __global__ void __launch_bounds__(BN_NT) bn_bwd_partial_kernel(const float* __re
       const float xh = (__ldg(y + base + q) - mu) * is;
       a += (double)d * (double)xh;
       b += (double)d;
+    }
+  }
+  block_sum2<BN_NT>(a, b, part + ((size_t)c * P + p) * 2);
+}
+
+static __device__ __forceinline__ void bwd_acc(float d, float yv, float r, bool has_r, float mu, float is,
+                                               double& a, double& b) {
+  if (has_r && r <= 0.0f) d = 0.0f;
+  const float xh = (yv - mu) * is;
+  a += (double)d * (double)xh;
+  b += (double)d;
+}
+
+template <bool RELU>
+__global__ void __launch_bounds__(BN_NT) bn_bwd_partial4_kernel(const float4* __restrict__ dy,
+                                                              const float4* __restrict__ y,
+                                                              const float4* __restrict__ relu_out, int n,
+                                                              int C, int hw4, int P,
+                                                              const float* __restrict__ mean,
+                                                              const float* __restrict__ invstd,
+                                                              double* __restrict__ part) {
+  const int c = blockIdx.x, p = blockIdx.y;
+  const int i0 = (int)((long)n * p / P), i1 = (int)((long)n * (p + 1) / P);
+  const unsigned tot = (unsigned)(i1 - i0) * (unsigned)hw4;
+  const float mu = mean[c], is = invstd[c];
+  double a = 0.0, b = 0.0;
+  for (unsigned j = threadIdx.x; j < tot; j += BN_NT * BN_U) {
+    float4 d[BN_U], v[BN_U], r[BN_U];
+#pragma unroll
+    for (int u = 0; u < BN_U; u++) {
+      const unsigned jj = j + u * BN_NT;
+      if (jj < tot) {
+        const unsigned img = jj / (unsigned)hw4, q = jj - img * (unsigned)hw4;
+        const size_t o = ((size_t)(i0 + img) * C + c) * hw4 + q;
+        d[u] = __ldg(dy + o);
+        v[u] = __ldg(y + o);
+        if (RELU) r[u] = __ldg(relu_out + o);
+      } else {
+        d[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        v[u] = make_float4(mu, mu, mu, mu);
+        if (RELU) r[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < BN_U; u++) {
+      bwd_acc(d[u].x, v[u].x, RELU ? r[u].x : 1.f, RELU, mu, is, a, b);
+      bwd_acc(d[u].y, v[u].y, RELU ? r[u].y : 1.f, RELU, mu, is, a, b);
+      bwd_acc(d[u].z, v[u].z, RELU ? r[u].z : 1.f, RELU, mu, is, a, b);
+      bwd_acc(d[u].w, v[u].w, RELU ? r[u].w : 1.f, RELU, mu, is, a, b);
     }
   }
   block_sum2<BN_NT>(a, b, part + ((size_t)c * P + p) * 2);
@@ -154,6 +228,90 @@ __global__ void bn_apply_kernel(const float* __restrict__ y, int C, int hw, size
   }
 }
 
+// Vector forms of apply and dx: float4 index j lies in plane j / hw4, whose
+// channel is plane % C; BN_U independent float4s per thread per iteration.
+__global__ void __launch_bounds__(256) bn_apply4_kernel(const float4* __restrict__ y, int C, unsigned hw4,
+                                                        unsigned total4, const float* __restrict__ gamma,
+                                                        const float* __restrict__ beta,
+                                                        const float* __restrict__ mean,
+                                                        const float* __restrict__ invstd, int relu,
+                                                        float4* __restrict__ out) {
+  const unsigned stride = gridDim.x * blockDim.x;
+  for (unsigned j = blockIdx.x * blockDim.x + threadIdx.x; j < total4; j += stride * BN_U) {
+    float4 v[BN_U];
+#pragma unroll
+    for (int u = 0; u < BN_U; u++) {
+      const unsigned jj = j + u * stride;
+      if (jj < total4) v[u] = __ldg(y + jj);
+    }
+#pragma unroll
+    for (int u = 0; u < BN_U; u++) {
+      const unsigned jj = j + u * stride;
+      if (jj >= total4) break;
+      const int c = (int)((jj / hw4) % (unsigned)C);
+      const float mu = __ldg(mean + c), is = __ldg(invstd + c), g = __ldg(gamma + c), bt = __ldg(beta + c);
+      float4 o;
+      o.x = g * ((v[u].x - mu) * is) + bt;
+      o.y = g * ((v[u].y - mu) * is) + bt;
+      o.z = g * ((v[u].z - mu) * is) + bt;
+      o.w = g * ((v[u].w - mu) * is) + bt;
+      if (relu) {
+        o.x = fmaxf(o.x, 0.0f);
+        o.y = fmaxf(o.y, 0.0f);
+        o.z = fmaxf(o.z, 0.0f);
+        o.w = fmaxf(o.w, 0.0f);
+      }
+      out[jj] = o;
+    }
+  }
+}
+
+template <bool RELU>
+__global__ void __launch_bounds__(256) bn_dx4_kernel(const float4* __restrict__ dy, const float4* __restrict__ y,
+                                                     const float4* __restrict__ relu_out, int C, unsigned hw4,
+                                                     unsigned total4, float m, const float* __restrict__ gamma,
+                                                     const float* __restrict__ mean,
+                                                     const float* __restrict__ invstd,
+                                                     const float* __restrict__ dg, const float* __restrict__ db,
+                                                     float4* __restrict__ dx) {
+  const unsigned stride = gridDim.x * blockDim.x;
+  for (unsigned j = blockIdx.x * blockDim.x + threadIdx.x; j < total4; j += stride * BN_U) {
+    float4 d[BN_U], v[BN_U], r[BN_U];
+#pragma unroll
+    for (int u = 0; u < BN_U; u++) {
+      const unsigned jj = j + u * stride;
+      if (jj < total4) {
+        d[u] = __ldg(dy + jj);
+        v[u] = __ldg(y + jj);
+        if (RELU) r[u] = __ldg(relu_out + jj);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < BN_U; u++) {
+      const unsigned jj = j + u * stride;
+      if (jj >= total4) break;
+      const int c = (int)((jj / hw4) % (unsigned)C);
+      const float mu = __ldg(mean + c), is = __ldg(invstd + c);
+      const float s = __ldg(gamma + c) * is / m, dbc = __ldg(db + c), dgc = __ldg(dg + c);
+      float dd[4] = {d[u].x, d[u].y, d[u].z, d[u].w};
+      const float vv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      if (RELU) {
+        const float rr[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+          if (rr[e] <= 0.0f) dd[e] = 0.0f;
+      }
+      float o[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const float xh = (vv[e] - mu) * is;
+        o[e] = s * (m * dd[e] - dbc - xh * dgc);
+      }
+      dx[jj] = make_float4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 __global__ void bn_eval_kernel(const float* __restrict__ y, int C, int hw, size_t total,
                                const float* __restrict__ gamma, const float* __restrict__ beta,
                                const float* __restrict__ rmean, const float* __restrict__ rvar, float eps,
@@ -185,10 +343,23 @@ __global__ void bn_dx_kernel(const float* __restrict__ dy, const float* __restri
 }
 
 static int bn_parts(int n, int C, int num_sms) {
-  int P = (4 * num_sms + C - 1) / C;
+  int P = (8 * num_sms + C - 1) / C;
   if (P > n) P = n;
   if (P < 1) P = 1;
   return P;
+}
+
+static bool vec4_ok(int hw, size_t total, std::initializer_list<const void*> ptrs) {
+  if (hw % 4 != 0 || total / 4 >= (size_t)INT32_MAX) return false;
+  for (const void* p : ptrs)
+    if (p && (reinterpret_cast<uintptr_t>(p) & 15)) return false;
+  return true;
+}
+
+static unsigned ew4_grid(size_t total4, int num_sms) {
+  size_t g = (total4 + 256 * BN_U - 1) / (256 * BN_U);
+  size_t cap = (size_t)num_sms * 8;
+  return (unsigned)std::max<size_t>(1, std::min(g, cap));
 }
 
 static unsigned ew_grid(size_t total, int num_sms) {
@@ -202,7 +373,11 @@ int bn_fwd_sums(rnn_ctx* ctx, const float* y, int n, int C, int hw, double* part
   RNN_RANGE(y, sizeof(float) * (size_t)n * C * hw);
   RNN_RANGE(part, sizeof(double) * (size_t)C * P * 2);
   RNN_RANGE(sums, sizeof(double) * (size_t)C * 2);
-  bn_fwd_partial_kernel<<<dim3(C, P), BN_NT, 0, ctx->stream>>>(y, n, C, hw, P, part);
+  if (vec4_ok(hw, (size_t)n * C * hw, {y}))
+    bn_fwd_partial4_kernel<<<dim3(C, P), BN_NT, 0, ctx->stream>>>(reinterpret_cast<const float4*>(y), n, C,
+                                                                 hw / 4, P, part);
+  else
+    bn_fwd_partial_kernel<<<dim3(C, P), BN_NT, 0, ctx->stream>>>(y, n, C, hw, P, part);
   RNN_CHECK_LAUNCH();
   bn_combine_kernel<<<(C + 127) / 128, 128, 0, ctx->stream>>>(part, C, P, sums);
   RNN_CHECK_LAUNCH();
@@ -225,8 +400,13 @@ int bn_fwd_finish(rnn_ctx* ctx, const float* y, int n, int C, int hw, double cou
                                                                 rmean, rvar);
   RNN_CHECK_LAUNCH();
   const size_t total = (size_t)n * C * hw;
-  bn_apply_kernel<<<ew_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(y, C, hw, total, gamma, beta,
-                                                                          mean, invstd, relu, out);
+  if (vec4_ok(hw, total, {y, out}))
+    bn_apply4_kernel<<<ew4_grid(total / 4, ctx->num_sms), 256, 0, ctx->stream>>>(
+        reinterpret_cast<const float4*>(y), C, (unsigned)(hw / 4), (unsigned)(total / 4), gamma, beta, mean,
+        invstd, relu, reinterpret_cast<float4*>(out));
+  else
+    bn_apply_kernel<<<ew_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(y, C, hw, total, gamma, beta,
+                                                                            mean, invstd, relu, out);
   RNN_CHECK_LAUNCH();
   return RNN_OK;
 }
@@ -241,8 +421,19 @@ int bn_bwd_sums(rnn_ctx* ctx, const float* dy, const float* y, const float* relu
   RNN_RANGE(invstd, sizeof(float) * C);
   RNN_RANGE(part, sizeof(double) * (size_t)C * P * 2);
   RNN_RANGE(sums, sizeof(double) * (size_t)C * 2);
-  bn_bwd_partial_kernel<<<dim3(C, P), BN_NT, 0, ctx->stream>>>(dy, y, relu_out, n, C, hw, P, mean,
-                                                               invstd, part);
+  if (vec4_ok(hw, (size_t)n * C * hw, {dy, y, relu_out})) {
+    const float4 *d4 = reinterpret_cast<const float4*>(dy), *y4 = reinterpret_cast<const float4*>(y),
+                 *r4 = reinterpret_cast<const float4*>(relu_out);
+    if (relu_out)
+      bn_bwd_partial4_kernel<true><<<dim3(C, P), BN_NT, 0, ctx->stream>>>(d4, y4, r4, n, C, hw / 4, P, mean,
+                                                                         invstd, part);
+    else
+      bn_bwd_partial4_kernel<false><<<dim3(C, P), BN_NT, 0, ctx->stream>>>(d4, y4, r4, n, C, hw / 4, P, mean,
+                                                                          invstd, part);
+  } else {
+    bn_bwd_partial_kernel<<<dim3(C, P), BN_NT, 0, ctx->stream>>>(dy, y, relu_out, n, C, hw, P, mean, invstd,
+                                                                 part);
+  }
   RNN_CHECK_LAUNCH();
   bn_combine_kernel<<<(C + 127) / 128, 128, 0, ctx->stream>>>(part, C, P, sums);
   RNN_CHECK_LAUNCH();
@@ -263,8 +454,22 @@ int bn_bwd_finish(rnn_ctx* ctx, const float* dy, const float* y, const float* re
                                                                     pscale);
   RNN_CHECK_LAUNCH();
   const size_t total = (size_t)n * C * hw;
-  bn_dx_kernel<<<ew_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(
-      dy, y, relu_out, C, hw, total, (float)count, gamma, mean, invstd, dgb, dgb + C, dx);
+  if (vec4_ok(hw, total, {dy, y, relu_out, dx})) {
+    const float4 *d4 = reinterpret_cast<const float4*>(dy), *y4 = reinterpret_cast<const float4*>(y),
+                 *r4 = reinterpret_cast<const float4*>(relu_out);
+    const unsigned g = ew4_grid(total / 4, ctx->num_sms);
+    if (relu_out)
+      bn_dx4_kernel<true><<<g, 256, 0, ctx->stream>>>(d4, y4, r4, C, (unsigned)(hw / 4), (unsigned)(total / 4),
+                                                      (float)count, gamma, mean, invstd, dgb, dgb + C,
+                                                      reinterpret_cast<float4*>(dx));
+    else
+      bn_dx4_kernel<false><<<g, 256, 0, ctx->stream>>>(d4, y4, r4, C, (unsigned)(hw / 4), (unsigned)(total / 4),
+                                                       (float)count, gamma, mean, invstd, dgb, dgb + C,
+                                                       reinterpret_cast<float4*>(dx));
+  } else {
+    bn_dx_kernel<<<ew_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(
+        dy, y, relu_out, C, hw, total, (float)count, gamma, mean, invstd, dgb, dgb + C, dx);
+  }
   RNN_CHECK_LAUNCH();
   return RNN_OK;
 }

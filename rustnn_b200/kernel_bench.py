@@ -2,6 +2,9 @@
 
     python -m rustnn_b200.kernel_bench conv --cin 64 --cout 64 --hw 32 --batch 256 [--k 3 --stride 1]
     python -m rustnn_b200.kernel_bench gemm            # the six gemm.rs bench shapes (bench.rs:17-24)
+    python -m rustnn_b200.kernel_bench attn            # Core fwd/bwd at the attention config (B=128, h=4, dh=32)
+    python -m rustnn_b200.kernel_bench ln              # LayerNorm fwd/bwd at the rustvit row counts
+    python -m rustnn_b200.kernel_bench muon            # Muon (Newton-Schulz) over the 39 rustvit weight matrices
 
 Prints one line per kernel: time per launch, algorithmic TFLOP/s (2*M*N*K),
 and the minimum HBM bytes / achieved GB/s.  Also the target of the ncu
@@ -80,9 +83,96 @@ def gemm(args):
     return out
 
 
+def attn(args):
+    """Core::forward/backward (attn.rs:148-343) at B=128, h=4, dh=32: self
+    attention over 8x8 tokens (diagonal masked) and cross attention from 8x8
+    queries into a 16x16 memory.  Bytes count every tensor the kernels must
+    read or write once, P included (the backward reads it)."""
+    n, h, dh = args.batch if args.batch != 256 else 128, 4, 32
+    c = h * dh
+    out = []
+    for tag, (th, mh, self_) in (("self 64x64", (8, 8, True)), ("cross 64x256", (8, 16, False))):
+        tq, tk = th * th, mh * mh
+        _, nrel = ops.rel_index(th, th, mh, mh)
+        g = torch.Generator(device="cuda").manual_seed(0)
+        if self_:
+            q = torch.randn(n * tq * 3 * c, device="cuda", generator=g) / 32 ** 0.5
+            kv, qs, qo, kvs, ko, vo = q, 3 * c, 0, 3 * c, c, 2 * c
+        else:
+            q = torch.randn(n * tq * c, device="cuda", generator=g) / 32 ** 0.5
+            kv = torch.randn(n * tk * 2 * c, device="cuda", generator=g) / 32 ** 0.5
+            qs, qo, kvs, ko, vo = c, 0, 2 * c, 0, c
+        tau = torch.full((h,), 1 / dh ** 0.5, device="cuda")
+        rel = torch.randn(h * nrel, device="cuda", generator=g)
+        p, o = ops.attn_forward(n, h, dh, th, th, mh, mh, self_, q, qs, qo, kv, kvs, ko, vo, tau, rel)
+        dout = torch.randn_like(o)
+        dq, dkv = torch.zeros_like(q), torch.zeros_like(kv)
+        dtau, drel = torch.zeros_like(tau), torch.zeros_like(rel)
+        fl_f = 2.0 * 2 * n * h * tq * tk * dh
+        fl_b = 2.0 * 5 * n * h * tq * tk * dh  # dV, dP, QK^T recompute (dtau), dQ, dK
+        pb = n * h * tq * tk * 4
+        qkvo = (n * tq * c * 2 + n * tk * c * 2) * 4
+        tf = _time(lambda: ops.attn_forward(n, h, dh, th, th, mh, mh, self_, q, qs, qo, kv, kvs, ko, vo, tau, rel),
+                   args.reps)
+        tb = _time(lambda: ops.attn_backward(n, h, dh, th, th, mh, mh, q, qs, qo, kv, kvs, ko, vo, tau, p, dout, dq,
+                                             dkv, dtau, drel), args.reps)
+        fb, bb = qkvo + pb, qkvo + pb + n * tq * c * 4 + (n * tq * c + n * tk * 2 * c) * 4 * 2
+        for kind, t, fl, by in (("fwd", tf, fl_f, fb), ("bwd", tb, fl_b, bb)):
+            out.append({"kernel": f"attn_{kind}", "shape": f"{tag} n{n} h{h} dh{dh}", "ms": round(t * 1e3, 4),
+                        "tflops": round(fl / t / 1e12, 2), "min_bytes": int(by), "gbs": round(by / t / 1e9, 1)})
+    return out
+
+
+def ln(args):
+    """LayerNorm (norm.rs:38-137) fwd/bwd at the rustvit row counts (B=128)."""
+    out = []
+    for rows, c in ((8192, 256), (2048, 384), (32768, 512), (2048, 1024)):
+        x = torch.randn(rows * c, device="cuda")
+        gm, bt = torch.randn(c, device="cuda"), torch.randn(c, device="cuda")
+        y, xh, inv = ops.layernorm_forward(x, rows, c, gm, bt)
+        dy = torch.randn_like(x)
+        dg, db = torch.zeros(c, device="cuda"), torch.zeros(c, device="cuda")
+        tf = _time(lambda: ops.layernorm_forward(x, rows, c, gm, bt), args.reps)
+        tb = _time(lambda: ops.layernorm_backward(dy, xh, inv, rows, c, gm, dg, db), args.reps)
+        fb, bb = rows * c * 4 * 3 + rows * 4, rows * c * 4 * 3 + rows * 4
+        out.append({"kernel": "layernorm_fwd", "shape": f"{rows}x{c}", "ms": round(tf * 1e3, 4), "min_bytes": fb,
+                    "gbs": round(fb / tf / 1e9, 1)})
+        out.append({"kernel": "layernorm_bwd", "shape": f"{rows}x{c}", "ms": round(tb * 1e3, 4), "min_bytes": bb,
+                    "gbs": round(bb / tb / 1e9, 1)})
+    return out
+
+
+RUSTVIT_2D = ([(768, 256), (256, 256), (704, 256), (256, 352)] * 5 + [(256, 256), (256, 256)] * 2
+              + [(1152, 384), (384, 384), (1024, 384), (384, 512)] * 2 + [(384, 1024), (20, 384), (100, 384),
+                                                                          (100, 96), (384, 96), (100, 256), (384, 256)])
+
+
+def muon(args):
+    """Muon over the 39 rustvit Linear weights (optim.rs:177-203): 3 quintic
+    Newton-Schulz iterations each.  Flops per matrix with s = min dim, l = max:
+    per iteration 2*s*s*l (X X^T) + 2*s*s*s (A A) + 2*s*s*l (B X)."""
+    mats = []
+    fl = 0.0
+    for r, c in RUSTVIT_2D:
+        v = torch.randn(r * c, device="cuda") * 0.02
+        g = torch.randn(r * c, device="cuda")
+        m = torch.zeros(r * c, device="cuda")
+        mats.append((v, g, m, r, c))
+        s, l = min(r, c), max(r, c)
+        fl += 3 * (4.0 * s * s * l + 2.0 * s * s * s)
+
+    def step():
+        for v, g, m, r, c in mats:
+            ops.muon_step_(v, g, m, r, c, 3, 0.02)
+
+    t = _time(step, args.reps)
+    return [{"kernel": "muon_step", "shape": f"{len(mats)} matrices (rustvit)", "ms": round(t * 1e3, 4),
+             "tflops": round(fl / t / 1e12, 2), "gflop": round(fl / 1e9, 2)}]
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["conv", "gemm"])
+    ap.add_argument("what", choices=["conv", "gemm", "attn", "ln", "muon"])
     ap.add_argument("--cin", type=int, default=64)
     ap.add_argument("--cout", type=int, default=64)
     ap.add_argument("--hw", type=int, default=32)
@@ -92,7 +182,7 @@ def main():
     ap.add_argument("--which", default="fwd,dgrad,wgrad")
     ap.add_argument("--reps", type=int, default=5)
     args = ap.parse_args()
-    rows = conv(args) if args.what == "conv" else gemm(args)
+    rows = {"conv": conv, "gemm": gemm, "attn": attn, "ln": ln, "muon": muon}[args.what](args)
     for r in rows:
         print(json.dumps(r))
 

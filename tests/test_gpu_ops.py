@@ -157,7 +157,8 @@ def test_conv_dgrad_accumulates(ops):
 # ------------------------------------------------------------------ BN / glue
 
 
-@pytest.mark.parametrize("n,c,hw,relu", [(3, 4, 25, False), (16, 64, 256, True), (8, 32, 1024, True)])
+@pytest.mark.parametrize("n,c,hw,relu", [(3, 4, 25, False), (16, 64, 256, True), (8, 32, 1024, True),
+                                         (64, 256, 64, True), (37, 8, 4, False), (5, 3, 12, True)])
 def test_batchnorm_parity(ops, n, c, hw, relu):
     rng = O.Rng(21)
     y = (rng.rand_vec(n * c * hw) * 2.0 + 1.0).astype(np.float32)
