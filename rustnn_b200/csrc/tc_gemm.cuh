@@ -94,15 +94,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that lets the hardware park the thread for up to `ns`
+// nanoseconds; it resumes as soon as the phase completes.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait.  Returns false when the CTA is aborting (another role timed
-// out) or when this wait itself ran past WAIT_TIMEOUT_NS.
+// out) or when this wait itself ran past WAIT_TIMEOUT_NS.  Waiting threads
+// are parked by the suspend hint instead of spinning, so they do not take
+// issue slots from the producer warps on the same sub-partition; the abort
+// flag and the clock are polled between parks.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* dev_error) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const unsigned long long t0 = globaltimer();
   while (true) {
-    if (mbar_try_wait(a, parity)) return true;
+    if (mbar_try_wait_hint(a, parity, 20000u)) return true;
     if (*abort_flag) return false;
     if (globaltimer() - t0 > WAIT_TIMEOUT_NS) {
       *abort_flag = 1;
@@ -110,6 +127,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
       return false;
     }
   }
+}
+
+// One lane of a converged warp (elect.sync); true in exactly one lane.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "elect.sync _|P, 0xffffffff;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
 }
 
 __device__ __forceinline__ void fence_barrier_init() {
@@ -420,47 +448,59 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     (void)lane;
   } else if (warp == MMA_WARP) {
     // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      uint32_t it = 0, tcount = 0;
-      bool ok = true;
-      bool issued = false;
-      for (int tile = blockIdx.x; tile < sched.num_tiles && ok; tile += gridDim.x, tcount++) {
-        const int split = tile / tiles_mn;
-        const int kb0 = split * sched.kb_per_split;
-        int kb1 = kb0 + sched.kb_per_split;
-        if (kb1 > sched.kblocks) kb1 = sched.kblocks;
-        const uint32_t buf = tcount & 1;
-        const uint32_t aphase = (tcount >> 1) & 1;
-        if (!mbar_wait(&acc_empty[buf], aphase ^ 1, abort_flag, dev_error)) { ok = false; break; }
+    // The whole warp walks the schedule, waits and builds the descriptors
+    // (warp-uniform values); one elected lane issues the MMAs and commits.
+    uint32_t it = 0, tcount = 0;
+    bool ok = true;
+    bool issued = false;
+    for (int tile = blockIdx.x; tile < sched.num_tiles && ok; tile += gridDim.x, tcount++) {
+      const int split = tile / tiles_mn;
+      const int kb0 = split * sched.kb_per_split;
+      int kb1 = kb0 + sched.kb_per_split;
+      if (kb1 > sched.kblocks) kb1 = sched.kblocks;
+      const uint32_t buf = tcount & 1;
+      const uint32_t aphase = (tcount >> 1) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_empty[buf], aphase ^ 1, abort_flag, dev_error))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + buf * BN;
+      for (int kb = kb0; kb < kb1; kb++, it++) {
+        const int stage = it % C::STAGES;
+        const uint32_t phase = (it / C::STAGES) & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort_flag, dev_error))) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * BN;
-        for (int kb = kb0; kb < kb1; kb++, it++) {
-          const int stage = it % C::STAGES;
-          const uint32_t phase = (it / C::STAGES) & 1;
-          if (!mbar_wait(&full[stage], phase, abort_flag, dev_error)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t a_hi = ring + stage * C::STAGE_BYTES;
-          const uint32_t a_lo = a_hi + C::A_BYTES;
-          const uint32_t b_hi = a_lo + C::A_BYTES;
-          const uint32_t b_lo = b_hi + C::B_BYTES;
+        const uint32_t a_hi = ring + stage * C::STAGE_BYTES;
+        const uint32_t a_lo = a_hi + C::A_BYTES;
+        const uint32_t b_hi = a_lo + C::A_BYTES;
+        const uint32_t b_lo = b_hi + C::B_BYTES;
+        if (elect_one()) {
 #pragma unroll
           for (int j = 0; j < BK / 8; j++) {
             const uint32_t koff = j * 32;  // 8 tf32 = 32 bytes along K
             const uint64_t dah = sdesc_sw128(a_hi + koff), dal = sdesc_sw128(a_lo + koff);
             const uint64_t dbh = sdesc_sw128(b_hi + koff), dbl = sdesc_sw128(b_lo + koff);
             const uint32_t first = (kb == kb0 && j == 0) ? 0u : 1u;
-            mma_tf32(d_tmem, dal, dbh, C::IDESC, first);
-            mma_tf32(d_tmem, dah, dbl, C::IDESC, 1u);
-            mma_tf32(d_tmem, dah, dbh, C::IDESC, 1u);
-            issued = true;
+            mma_tf32(d_tmem, dal, dbh, C::IDESC, first);  // lo * hi
+            mma_tf32(d_tmem, dah, dbl, C::IDESC, 1u);     // hi * lo
+            mma_tf32(d_tmem, dah, dbh, C::IDESC, 1u);     // hi * hi
           }
           mma_commit(&empty[stage]);
         }
-        if (!ok) break;
-        mma_commit(&acc_full[buf]);
+        __syncwarp();
+        issued = true;
       }
-      if (!ok && issued) {
-        // make sure no MMA still writes TMEM before it is released
+      if (!ok) break;
+      if (elect_one()) mma_commit(&acc_full[buf]);
+      __syncwarp();
+    }
+    if (!ok && issued) {
+      // make sure no MMA still writes TMEM before it is released
+      if (elect_one()) {
         mma_commit(drain);
         const uint32_t a = smem_u32(drain);
         const unsigned long long t0 = globaltimer();
@@ -479,7 +519,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int mt = mn % sched.m_tiles, nt = mn / sched.m_tiles;
       const uint32_t buf = tcount & 1;
       const uint32_t aphase = (tcount >> 1) & 1;
-      if (!mbar_wait(&acc_full[buf], aphase, abort_flag, dev_error)) break;
+      // warp-uniform outcome: tcgen05.ld below is .sync.aligned
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], aphase, abort_flag, dev_error))) break;
       tc_fence_after();
       const int row = mt * BM + q * 32 + lane;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;

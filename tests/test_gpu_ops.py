@@ -106,6 +106,10 @@ CONVS = [  # (n, cin, h, cout, k, stride, pad)
     (4, 64, 16, 128, 1, 2, 0),
     (2, 3, 32, 64, 3, 1, 1),  # stem
     (3, 128, 8, 256, 3, 1, 1),
+    (64, 64, 32, 64, 3, 1, 1),   # 512 row tiles: several tiles per persistent CTA
+    (24, 128, 16, 128, 3, 1, 1),
+    (40, 64, 16, 64, 1, 1, 0),
+    (9, 32, 16, 96, 3, 1, 1),
 ]
 
 
