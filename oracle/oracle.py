@@ -119,6 +119,8 @@ def lib():
         "orc_ce_soft": (F, [_f32p, _f32p, _u32p, I, I, F, _f32p, C.POINTER(C.c_int)]),
         "orc_kl_distill": (F, [_f32p, _f32p, I, I, F, F, _f32p]),
         "orc_hint_mse": (F, [_f32p, _f32p, I, I, F, _f32p]),
+        "orc_trunc_normal": (V, [C.POINTER(_Rng), _f32p, Z, F]),
+        "orc_kaiming": (V, [C.POINTER(_Rng), _f32p, Z, I]),
         "orc_set_threads": (V, [I]),
         "orc_get_threads": (I, []),
     }

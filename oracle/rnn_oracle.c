@@ -1607,3 +1607,26 @@ float orc_hint_mse(const float *pred, const float *target, int n, int c, float s
     }
     return l * inv * scale;
 }
+
+/* ---------------------------------------------------------------- rustvit initialisers */
+
+/* Param::trunc_normal, nn.rs:77-89: resample |z| > 2 up to 8 times, clamp. */
+void orc_trunc_normal(orc_rng *r, float *out, size_t n, float std) {
+    for (size_t i = 0; i < n; i++) {
+        float z = orc_rng_normal(r);
+        int tries = 0;
+        while (fabsf(z) > 2.0f && tries < 8) {
+            z = orc_rng_normal(r);
+            tries++;
+        }
+        if (z < -2.0f) z = -2.0f;
+        if (z > 2.0f) z = 2.0f;
+        out[i] = z * std;
+    }
+}
+
+/* Param::kaiming, nn.rs:95-100. */
+void orc_kaiming(orc_rng *r, float *out, size_t n, int fan_in) {
+    const float s = sqrtf(2.0f / (float)fan_in);
+    for (size_t i = 0; i < n; i++) out[i] = orc_rng_normal(r) * s;
+}

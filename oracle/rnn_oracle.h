@@ -202,6 +202,10 @@ float orc_kl_distill(const float *s, const float *t, int n, int nclass, float te
 float orc_hint_mse(const float *pred, const float *target, int n, int c, float scale,
                    float *dz);                                                           /* loss.rs:133-151 */
 
+/* rustvit parameter initialisers */
+void orc_trunc_normal(orc_rng *r, float *out, size_t n, float std); /* nn.rs:77-89 */
+void orc_kaiming(orc_rng *r, float *out, size_t n, int fan_in);      /* nn.rs:95-100 */
+
 /* ---- threads ------------------------------------------------------------ */
 void orc_set_threads(int n);
 int  orc_get_threads(void);
@@ -209,4 +213,5 @@ int  orc_get_threads(void);
 #ifdef __cplusplus
 }
 #endif
+
 #endif
