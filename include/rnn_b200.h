@@ -37,6 +37,7 @@ extern "C" {
 
 typedef struct rnn_ctx rnn_ctx;
 typedef struct rnn_resnet rnn_resnet;
+typedef struct rnn_rustvit rnn_rustvit;
 
 const char *rnn_last_error(void);
 /* Number of kernels this library has launched in this process. */
@@ -321,6 +322,59 @@ int rnn_dp_unique_id(unsigned char *uid_out);
  * like the single-process reference. */
 int rnn_resnet_dp_init(rnn_resnet *net, int rank, int world,
                        const unsigned char *uid, int sync_bn);
+
+/* ---- rustvit training step (vit.rs, train.rs:70-118 and 346-387) -------- */
+/* RustViT::new (vit.rs:441-509) on the device.  cfg9 = {width, cmid, dim,
+ * heads, depth3, dim4, heads4, depth4, img} (vit.rs:349-365); mem_at lists the
+ * reader blocks of stage 3; parent[nf] maps each fine class to its coarse
+ * group (TaxoHead, vit.rs:236-262).  Initial parameters are drawn from the
+ * reference's rng stream in its construction order (bit-identical).
+ * Parameters, gradients and moments are flat in for_each_param order
+ * (vit.rs:687-719); buffers (BatchNorm running statistics) in
+ * for_each_buffer order (vit.rs:721-728). */
+int rnn_rustvit_create(rnn_ctx *ctx, const int *cfg9, const int *mem_at,
+                       int n_mem, float droppath, const uint32_t *parent,
+                       int nf, int ncoarse, uint64_t seed, rnn_rustvit **out);
+int rnn_rustvit_destroy(rnn_rustvit *net);
+int rnn_rustvit_num_params(rnn_rustvit *net, size_t *out);
+int rnn_rustvit_num_buffers(rnn_rustvit *net, size_t *out);
+int rnn_rustvit_get_params(rnn_rustvit *net, float *out);   /* host or device dst */
+int rnn_rustvit_set_params(rnn_rustvit *net, const float *in);
+int rnn_rustvit_get_grads(rnn_rustvit *net, float *out);
+int rnn_rustvit_get_moments(rnn_rustvit *net, float *m, float *v2);
+int rnn_rustvit_get_ema(rnn_rustvit *net, float *out);
+int rnn_rustvit_get_buffers(rnn_rustvit *net, float *out);
+int rnn_rustvit_zero_grads(rnn_rustvit *net);
+/* RustViT::forward (vit.rs:511-582) with drop_seed = RustViT::drop_seed.
+ * Outputs (device, nullable) are copied out: logits/e1/e2 [n, nf], coarse
+ * [n, ncoarse], h1/h2/feat [n, dim4]; the exits exist only when train. */
+int rnn_rustvit_forward_dev(rnn_rustvit *net, const float *x, int n, int train,
+                            uint64_t drop_seed, float *logits, float *coarse,
+                            float *e1, float *e2, float *h1, float *h2,
+                            float *feat);
+/* RustViT::backward (vit.rs:627-685) with vit::Grads; gradients accumulate
+ * into the flat gradient buffer.  The exit gradients come as a set or not
+ * at all; dhfinal is nullable (an empty Grads::hfinal). */
+int rnn_rustvit_backward_dev(rnn_rustvit *net, const float *dlogits,
+                             const float *dcoarse, const float *de1,
+                             const float *de2, const float *dh1,
+                             const float *dh2, const float *dhfinal);
+/* Trainer::step (train.rs:346-387) at a given learning rate: forward,
+ * build_loss with the cli.rs defaults (tf/tc the soft targets of
+ * train.rs:120-155, hard/hardc the fine and coarse labels), backward, clip_
+ * at `clip` (0 = off), Optim::step_all (Muon + AdamW), Ema::update at
+ * `ema` (0 = off).  stats (host, nullable) = {total loss, ce, correct}. */
+int rnn_rustvit_train_step_dev(rnn_rustvit *net, const float *x,
+                               const float *tf, const float *tc,
+                               const uint32_t *hard, const uint32_t *hardc,
+                               int n, float lr, float wd, float clip, float ema,
+                               uint64_t drop_seed, float *stats);
+/* Host tier of the step: the batch comes from host memory. */
+int rnn_rustvit_train_step(rnn_rustvit *net, const float *x, const float *tf,
+                           const float *tc, const uint32_t *hard,
+                           const uint32_t *hardc, int n, float lr, float wd,
+                           float clip, float ema, uint64_t drop_seed,
+                           float *stats);
 
 #ifdef __cplusplus
 }

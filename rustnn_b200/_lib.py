@@ -30,9 +30,14 @@ class _NetS(C.Structure):
     """opaque rnn_resnet"""
 
 
+class _VitS(C.Structure):
+    """opaque rnn_rustvit"""
+
+
 # distinct handle types: ctypes rejects a context where a network is expected
 CTX = C.POINTER(_CtxS)
 NET = C.POINTER(_NetS)
+VIT = C.POINTER(_VitS)
 
 # name -> argtypes; every function returns int unless listed in _RESTYPE
 SIGS = {
@@ -111,6 +116,21 @@ SIGS = {
     "rnn_resnet_train_step": [NET, FP, FP, I, F, F, F, F, FP, FP],
     "rnn_dp_unique_id": [FP],
     "rnn_resnet_dp_init": [NET, I, I, FP, I],
+    "rnn_rustvit_create": [CTX, FP, FP, I, F, FP, I, I, U64, C.POINTER(VIT)],
+    "rnn_rustvit_destroy": [VIT],
+    "rnn_rustvit_num_params": [VIT, C.POINTER(Z)],
+    "rnn_rustvit_num_buffers": [VIT, C.POINTER(Z)],
+    "rnn_rustvit_get_params": [VIT, FP],
+    "rnn_rustvit_set_params": [VIT, FP],
+    "rnn_rustvit_get_grads": [VIT, FP],
+    "rnn_rustvit_get_moments": [VIT, FP, FP],
+    "rnn_rustvit_get_ema": [VIT, FP],
+    "rnn_rustvit_get_buffers": [VIT, FP],
+    "rnn_rustvit_zero_grads": [VIT],
+    "rnn_rustvit_forward_dev": [VIT, FP, I, I, U64, FP, FP, FP, FP, FP, FP, FP],
+    "rnn_rustvit_backward_dev": [VIT, FP, FP, FP, FP, FP, FP, FP],
+    "rnn_rustvit_train_step_dev": [VIT, FP, FP, FP, FP, FP, I, F, F, F, F, U64, FP],
+    "rnn_rustvit_train_step": [VIT, FP, FP, FP, FP, FP, I, F, F, F, F, U64, FP],
 }
 _RESTYPE = {"rnn_ctx_stream": P, "rnn_launch_count": C.c_ulonglong}
 

@@ -358,8 +358,9 @@ static int launch_bwd(rnn_ctx* ctx, AttnArgs a, float* dtau, float* drel) {
 static int check_args(int n, int h, int dh, int th, int tw, int mh, int mw, int qstride, int qoff, int kvstride,
                       int koff, int voff) {
   RNN_REQUIRE(n > 0 && h > 0 && th > 0 && tw > 0 && mh > 0 && mw > 0, "attention: bad shape");
-  RNN_REQUIRE(dh == 4 || dh == 8 || dh == 16 || dh == 32 || dh == 64,
-              "attention: head dim %d unsupported (4, 8, 16, 32 or 64)", dh);
+  RNN_REQUIRE(dh == 4 || dh == 6 || dh == 8 || dh == 12 || dh == 16 || dh == 24 || dh == 32 || dh == 48 ||
+                  dh == 64,
+              "attention: head dim %d unsupported (4, 6, 8, 12, 16, 24, 32, 48 or 64)", dh);
   RNN_REQUIRE(qoff >= 0 && qoff + h * dh <= qstride, "attention: q columns exceed its row stride");
   RNN_REQUIRE(koff >= 0 && voff >= 0 && koff + h * dh <= kvstride && voff + h * dh <= kvstride,
               "attention: k/v columns exceed the kv row stride");
@@ -369,9 +370,13 @@ static int check_args(int n, int h, int dh, int th, int tw, int mh, int mw, int 
 #define ATTN_DISPATCH(fn, dh, ...)                           \
   switch (dh) {                                              \
     case 4: return fn<4>(__VA_ARGS__);                       \
+    case 6: return fn<6>(__VA_ARGS__);                       \
     case 8: return fn<8>(__VA_ARGS__);                       \
+    case 12: return fn<12>(__VA_ARGS__);                     \
     case 16: return fn<16>(__VA_ARGS__);                     \
+    case 24: return fn<24>(__VA_ARGS__);                     \
     case 32: return fn<32>(__VA_ARGS__);                     \
+    case 48: return fn<48>(__VA_ARGS__);                     \
     default: return fn<64>(__VA_ARGS__);                     \
   }
 

@@ -538,19 +538,23 @@ extern "C" int rnn_seqpool_bwd_dev(rnn_ctx* ctx, const float* dz, const float* x
 }
 
 // DropPath (vit.rs:40-73): the per-image keep mask comes from Rng::new(seed)
-// exactly like the reference; the host draws n uniforms, the device scales.
+// exactly like the reference.  One device thread draws the n uniforms in
+// order (the stream is sequential and n is a batch size), so the mask needs
+// no host round trip and the call stays asynchronous.
+__global__ void droppath_mask_kernel(uint64_t seed, int n, float keep, float* __restrict__ mask) {
+  if (blockIdx.x != 0 || threadIdx.x != 0) return;
+  Rng rng(seed);
+  for (int i = 0; i < n; i++) mask[i] = rng.uniform() < keep ? 1.0f / keep : 0.0f;
+}
+
 extern "C" int rnn_droppath_fwd_dev(rnn_ctx* ctx, float* x, int n, size_t per_image, float p, uint64_t seed,
                                     float* mask) {
   RNN_REQUIRE(ctx && x && mask && n >= 0 && p >= 0.0f && p < 1.0f, "droppath_fwd: bad arguments");
   if (!n) return RNN_OK;
   RNN_RANGE(x, (size_t)n * per_image * 4);
   RNN_RANGE(mask, (size_t)n * 4);
-  std::vector<float> hm(n);
-  const float keep = 1.0f - p;
-  Rng rng(seed);
-  for (int i = 0; i < n; i++) hm[i] = rng.uniform() < keep ? 1.0f / keep : 0.0f;
-  RNN_CUDA(cudaMemcpyAsync(mask, hm.data(), (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream));
-  RNN_CUDA(cudaStreamSynchronize(ctx->stream));  // hm is a stack vector
+  droppath_mask_kernel<<<1, 32, 0, ctx->stream>>>(seed, n, 1.0f - p, mask);
+  RNN_CHECK_LAUNCH();
   const size_t total = (size_t)n * per_image;
   row_scale_kernel<<<gl_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(x, per_image, total, mask);
   RNN_CHECK_LAUNCH();

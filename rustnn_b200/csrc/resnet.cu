@@ -496,7 +496,9 @@ extern "C" int rnn_resnet_create(rnn_ctx* ctx, int depth_n, int width, int nclas
 
 extern "C" int rnn_resnet_destroy(rnn_resnet* net) {
   if (!net) return RNN_OK;
-  if (net->ctx) cudaStreamSynchronize(net->ctx->stream);
+  // the context may already be gone (interpreter teardown releases objects
+  // in any order): wait on the device, not on the context's stream
+  cudaDeviceSynchronize();
   free_acts(net);
   cudaFree(net->v);
   cudaFree(net->g);

@@ -1,17 +1,24 @@
-// Host-side restatement of rng.rs (SplitMix64-seeded xoshiro256++, 24-bit
-// uniform, f32 Box-Muller), used to draw the reference's parameter
-// initialisation bit for bit.
+// Restatement of rng.rs (SplitMix64-seeded xoshiro256++, 24-bit uniform, f32
+// Box-Muller), used on the host to draw the reference's parameter
+// initialisation bit for bit; the integer part (seeding, next_u64, uniform)
+// also runs on the device, where the DropPath masks are drawn.
 #pragma once
 
 #include <math.h>
 #include <stdint.h>
+
+#ifdef __CUDACC__
+#define RNN_HD __host__ __device__
+#else
+#define RNN_HD
+#endif
 
 namespace rnn {
 
 struct Rng {
   uint64_t s[4];
 
-  explicit Rng(uint64_t seed) {
+  RNN_HD explicit Rng(uint64_t seed) {
     // rng.rs:8-20
     uint64_t z = seed + 0x9E3779B97F4A7C15ULL;
     for (int i = 0; i < 4; i++) {
@@ -23,9 +30,9 @@ struct Rng {
     }
   }
 
-  static uint64_t rotl(uint64_t x, int k) { return (x << k) | (x >> (64 - k)); }
+  static RNN_HD uint64_t rotl(uint64_t x, int k) { return (x << k) | (x >> (64 - k)); }
 
-  uint64_t next_u64() {
+  RNN_HD uint64_t next_u64() {
     // rng.rs:23-36
     const uint64_t r = rotl(s[0] + s[3], 23) + s[0];
     const uint64_t t = s[1] << 17;
@@ -38,7 +45,7 @@ struct Rng {
     return r;
   }
 
-  float uniform() { return (float)(next_u64() >> 40) * (1.0f / (float)(1ULL << 24)); }  // rng.rs:50-52
+  RNN_HD float uniform() { return (float)(next_u64() >> 40) * (1.0f / (float)(1ULL << 24)); }  // rng.rs:50-52
 
   float normal() {
     // rng.rs:55-59

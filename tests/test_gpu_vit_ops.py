@@ -47,6 +47,10 @@ ATTN = [
     (3, 2, 4, 3, 3, True),       # check.rs:300 fixture
     (3, 2, 4, 3, 6, False),      # check.rs:327 fixture
     (4, 6, 64, 4, 4, True),      # rustvit stage 4 (dim 384 / 6 heads, 4x4)
+    (3, 2, 6, 2, 2, True),       # check.rs:397 tiny network, stage 4 (dim 12 / 2 heads)
+    (2, 3, 12, 4, 8, False),
+    (2, 2, 24, 4, 4, True),
+    (2, 2, 48, 4, 8, False),
 ]
 
 
