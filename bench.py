@@ -9,8 +9,12 @@ synthetic CIFAR-shaped data (uniform bytes normalised to mean 0 / std 1),
 random init, f32 arithmetic (3xTF32 on the tensor cores).  One step =
 forward + softmax_ce + backward + allreduce + SGD-Nesterov (train.rs:684-699).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config resnet56|resnet20]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config resnet56|resnet20|rustvit]
     python bench.py --impl reference ...   # the CPU reference arm
+
+--config rustvit (BASELINE config 4): the default rustvit (Cfg::default,
+6.37 M parameters) at batch 128 on one GPU; one step = Trainer::step
+(forward, multi-exit loss, backward, clip, Muon + AdamW, EMA; train.rs:346-387).
 
 Prints one JSON line (rank 0).
 """
@@ -125,6 +129,156 @@ def cpu_oracle_images_per_sec(depth_n, width, n_img, steps, threads=None):
         net.train_step(x, labels, smooth=0.1, lr=0.2, mom=0.9, wd=5e-4)
     dt = time.perf_counter() - t0
     return n_img * steps / dt, cores, dt
+
+
+VIT_BATCH = 128
+VIT_FLOP_PER_IMG = 318_579_712 * 6  # RustViT::macs() x 6, the bench.rs:108 convention
+
+
+def vit_batch(n, seed):
+    from rustnn_b200.vit import cifar_parent, targets
+
+    x, labels = synthetic_batch(n, seed)
+    tf, tc, coarse = targets(labels, cifar_parent(), 20)
+    return x, labels, tf, tc, coarse
+
+
+def cpu_oracle_vit_images_per_sec(n_img, steps):
+    """Times the oracle's rustvit Trainer::step (C kernels, OpenMP) on the host."""
+    from oracle import oracle as O
+    from oracle import rustvit as RV
+
+    cores = O.get_threads()
+    net = RV.RustViT(RV.Cfg(), RV.cifar_parent(), 20, 0)
+    tr = RV.Trainer(net)
+    x, labels = synthetic_batch(n_img, 1)
+    tr.step(x, labels, n_img, 6e-4, 0.06, 1)  # warm-up
+    t0 = time.perf_counter()
+    for i in range(steps):
+        tr.step(x, labels, n_img, 6e-4, 0.06, 2 + i)
+    dt = time.perf_counter() - t0
+    return n_img * steps / dt, cores, dt
+
+
+def run_reference_vit(args):
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    sample = int(os.environ.get("RNN_REF_SAMPLE", "8"))
+    ips, cores, dt = cpu_oracle_vit_images_per_sec(sample, max(1, args.steps))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(ips, 3), "unit": "images/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * dt / max(1, args.steps), 2),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "rustvit default (Cfg::default) train step (BASELINE config 4)",
+                   "global_batch": VIT_BATCH, "sample_batch": sample, "parallelism": "cpu-threads"},
+        "cpu_baseline": {"value": round(ips, 3), "unit": "images/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} steps of a {sample}-image batch of the rustvit step (oracle "
+                                   "restatement: C kernels composed as vit.rs; the Rust reference cannot be "
+                                   "built: no cargo/rustc in the image)"},
+        "e2e": {"value": round(ips, 3), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours_vit(args):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        print(json.dumps({"error": "--config rustvit runs on one GPU (no data-parallel rustvit step yet)"}))
+        return 2
+    torch.cuda.set_device(0)
+    from rustnn_b200 import _lib, vit
+
+    n = VIT_BATCH
+    net = vit.RustViT(vit.VitCfg(), vit.cifar_parent(), 20, 0)
+    x, labels, tf, tc, coarse = vit_batch(n, 100)
+    xd, tfd, tcd = (torch.from_numpy(a).cuda() for a in (x, tf, tc))
+    hd = torch.from_numpy(labels.astype(np.int32)).cuda()
+    cd = torch.from_numpy(coarse.astype(np.int32)).cuda()
+    for i in range(args.warmup):
+        net.train_step(xd, tfd, tcd, hd, cd, drop_seed=i, stats=False)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(0)
+    sampler.start()
+    time.sleep(0.3)
+    s = torch.cuda.current_stream()
+    l0 = _lib.lib().rnn_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(s)
+    for i in range(args.steps):
+        net.train_step(xd, tfd, tcd, hd, cd, drop_seed=1000 + i, stats=False)
+    e1.record(s)
+    torch.cuda.synchronize()
+    launches = _lib.lib().rnn_launch_count() - l0
+    clocks = sampler.stop()
+    t = e0.elapsed_time(e1) / 1e3
+    # end to end through the host tier: pinned batch in, (loss, ce, correct) out
+    pins = [torch.from_numpy(a).pin_memory().numpy() for a in (x, tf, tc, labels, coarse)]
+    net.train_step_host(*pins, drop_seed=7)
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(s)
+    total = ce = corr = None
+    for i in range(args.steps):
+        total, ce, corr = net.train_step_host(*pins, drop_seed=2000 + i)
+    e3.record(s)
+    torch.cuda.synchronize()
+    t_e2e = e2.elapsed_time(e3) / 1e3
+    # dominant GEMM: the stage-3 qkv projection, rows = batch x 64 tokens
+    from rustnn_b200 import ops
+
+    m, nn, k = n * 64, 768, 256
+    a = torch.randn(m * k, device="cuda")
+    w = torch.randn(nn * k, device="cuda")
+    c = torch.empty(m * nn, device="cuda")
+    for _ in range(3):
+        ops.matmul(m, nn, k, a, False, w, True, c)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    g0.record(s)
+    for _ in range(20):
+        ops.matmul(m, nn, k, a, False, w, True, c)
+    g1.record(s)
+    torch.cuda.synchronize()
+    tg = g0.elapsed_time(g1) / 20 / 1e3
+    peaks = {}
+    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pk):
+        peaks = json.load(open(pk))
+    bf16 = peaks.get("bf16_tflops") or 1590.0
+    achieved = 2.0 * m * nn * k / tg / 1e12
+    value = n * args.steps / t
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "images/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(1000 * t / args.steps, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "rustvit default (Cfg::default, 6.37 M params) train step (BASELINE config 4)",
+                   "global_batch": n, "image": "3x32x32", "nclass": 100, "ncoarse": 20,
+                   "step": "Trainer::step: forward, build_loss (3 heads, KL distill, hints), backward, clip 1.0, "
+                           "Muon (39 matrices) + AdamW, EMA 0.9998; lr 6e-4 wd 0.06",
+                   "parallelism": "dp1",
+                   "l2": "no flush: the step moves several GB of activations and parameters, beyond the L2",
+                   "algorithmic_tflops": round(VIT_FLOP_PER_IMG * value / 1e12, 2)},
+        "e2e": {"value": round(n * args.steps / t_e2e, 2), "unit": "images/s",
+                "h2d_bytes_per_step": int(sum(p.nbytes for p in pins)), "d2h_bytes_per_step": 12},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor", "kernel": f"tc3_gemm Linear qkv {m}x{nn}x{k} (stage 3)",
+                     "achieved": round(achieved, 2), "peak": round(bf16, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / bf16, 4), "traffic": None,
+                     "peak_note": "bf16 from MEASURED_PEAKS.json (1.59 PF fallback); achieved = 2MNK / event time"},
+        "clocks": clocks,
+        "loss": round(total, 5),
+    }
+    if not args.no_cpu_baseline:
+        ips, cores, dt = cpu_oracle_vit_images_per_sec(4, 2)
+        line["cpu_baseline"] = {"value": round(ips, 3), "unit": "images/s", "cores": cores, "kind": "port",
+                                "sample": "2 steps x 4 images of the rustvit step (oracle restatement)"}
+    print(json.dumps(line), flush=True)
+    net.close()
+    return 0
 
 
 def run_reference(args, cfg_name):
@@ -331,12 +485,14 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="resnet56", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="resnet56", choices=sorted(CONFIGS) + ["rustvit"])
     ap.add_argument("--local-bn", action="store_true", help="per-rank BN statistics instead of SyncBN")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.config == "rustvit":
+        return run_reference_vit(args) if args.impl == "reference" else run_ours_vit(args)
     if args.impl == "reference":
         return run_reference(args, args.config)
     return run_ours(args, args.config)

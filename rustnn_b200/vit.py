@@ -162,13 +162,15 @@ class RustViT:
         call("rnn_rustvit_backward_dev", self.h, _ptr(g["logits"]), _ptr(g["coarse"]), _ptr(g.get("e1")),
              _ptr(g.get("e2")), _ptr(g.get("h1")), _ptr(g.get("h2")), _ptr(g.get("hfinal")))
 
-    def train_step(self, x, tf, tc, hard, hardc, lr=6e-4, wd=0.06, clip=1.0, ema=0.9998, drop_seed=0):
-        """Trainer::step on device inputs; returns (total loss, ce, correct)."""
+    def train_step(self, x, tf, tc, hard, hardc, lr=6e-4, wd=0.06, clip=1.0, ema=0.9998, drop_seed=0,
+                   stats=True):
+        """Trainer::step on device inputs; returns (total loss, ce, correct),
+        or None without waiting for the device when stats is False."""
         self.ctx.bind()
-        stats = np.zeros(3, np.float32)
+        st = np.zeros(3, np.float32)
         call("rnn_rustvit_train_step_dev", self.h, _ptr(x), _ptr(tf), _ptr(tc), _ptr(hard), _ptr(hardc),
-             hard.numel(), lr, wd, clip, ema, drop_seed & (2**64 - 1), _ptr(stats))
-        return float(stats[0]), float(stats[1]), int(stats[2])
+             hard.numel(), lr, wd, clip, ema, drop_seed & (2**64 - 1), _ptr(st) if stats else None)
+        return (float(st[0]), float(st[1]), int(st[2])) if stats else None
 
     def train_step_host(self, x, tf, tc, hard, hardc, lr=6e-4, wd=0.06, clip=1.0, ema=0.9998, drop_seed=0):
         """The same step through the host tier of the C ABI (host batch arrays)."""
