@@ -374,6 +374,8 @@ def run_ours(args, cfg_name):
 
     _, n_local = dp.shard(gbatch, world, rank)
     net = model.ResNet(depth_n, width, NCLASS, 0)
+    if not args.no_graph:
+        net.use_graph(True)
     if world > 1:
         uid = dp.share_unique_id(model.dp_unique_id)
         net.dp_init(rank, world, uid, sync_bn=not args.local_bn)
@@ -413,7 +415,7 @@ def run_ours(args, cfg_name):
     lp = torch.from_numpy(lab_np).pin_memory()
     xh = xp.numpy()
     lh = lp.numpy()
-    for _ in range(max(1, args.warmup // 2)):
+    for _ in range(args.warmup):  # >= 3: eager, capture, replay when graphs are on
         net.train_step_host(xh, lh)
     barrier()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -452,7 +454,8 @@ def run_ours(args, cfg_name):
                        "global_batch": gbatch, "per_gpu_batch": n_local, "image": "3x32x32", "nclass": NCLASS,
                        "optimizer": "sgd-nesterov lr0.2 mom0.9 wd5e-4, smooth 0.1",
                        "parallelism": f"dp{world}" + ("" if world == 1 else (" localbn" if args.local_bn else " syncbn")),
-                       "l2": "no flush: one step moves tens of GB of activations, far beyond the 126 MB L2"},
+                       "l2": "no flush: one step moves tens of GB of activations, far beyond the 126 MB L2",
+                       "cuda_graph": not args.no_graph},
             "e2e": {"value": round(e2e, 2), "unit": "images/s", "h2d_bytes_per_step": int(x_np.nbytes + lab_np.nbytes),
                     "d2h_bytes_per_step": 8},
             "gpu_launches": int(launches),
@@ -488,6 +491,7 @@ def main():
     ap.add_argument("--config", default="resnet56", choices=sorted(CONFIGS) + ["rustvit"])
     ap.add_argument("--local-bn", action="store_true", help="per-rank BN statistics instead of SyncBN")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="launch the step's kernels one by one (no CUDA graph)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -301,6 +301,12 @@ int rnn_resnet_forward_dev(rnn_resnet *net, const float *x, int n, int h, int w,
 int rnn_resnet_backward_dev(rnn_resnet *net, const float *dlogits);
 /* ResNet::step (model.rs:206) */
 int rnn_resnet_step(rnn_resnet *net, float lr, float mom, float wd);
+/* No reference counterpart (a device-side execution option): when enabled,
+ * rnn_resnet_train_step[_dev] records the whole step (kernels and NCCL
+ * calls) into a CUDA graph on its second call with the same arguments and
+ * replays it afterwards; any change of pointers, sizes or hyperparameters
+ * runs the step eagerly and recaptures.  Results are identical. */
+int rnn_resnet_set_graph(rnn_resnet *net, int enable);
 /* forward + softmax_ce + backward (+ gradient allreduce when data-parallel)
  * + step, on device inputs.  loss/correct are device pointers (1 element). */
 int rnn_resnet_train_step_dev(rnn_resnet *net, const float *x,

@@ -112,6 +112,7 @@ SIGS = {
     "rnn_resnet_forward_dev": [NET, FP, I, I, I, I, FP],
     "rnn_resnet_backward_dev": [NET, FP],
     "rnn_resnet_step": [NET, F, F, F],
+    "rnn_resnet_set_graph": [NET, I],
     "rnn_resnet_train_step_dev": [NET, FP, FP, I, F, F, F, F, FP, FP],
     "rnn_resnet_train_step": [NET, FP, FP, I, F, F, F, F, FP, FP],
     "rnn_dp_unique_id": [FP],

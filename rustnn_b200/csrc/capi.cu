@@ -88,6 +88,7 @@ int ensure_ws(rnn_ctx* ctx, size_t bytes) {
   }
   RNN_CUDA(cudaMalloc(&ctx->ws, want));
   ctx->ws_bytes = want;
+  ctx->mem_epoch++;
   return RNN_OK;
 }
 
@@ -103,6 +104,7 @@ int ensure_stage(rnn_ctx* ctx, size_t bytes) {
   }
   RNN_CUDA(cudaMalloc(&ctx->stage, want));
   ctx->stage_bytes = want;
+  ctx->mem_epoch++;
   return RNN_OK;
 }
 
@@ -118,6 +120,7 @@ int ensure_aux(rnn_ctx* ctx, size_t bytes) {
   }
   RNN_CUDA(cudaMalloc(&ctx->aux, want));
   ctx->aux_bytes = want;
+  ctx->mem_epoch++;
   return RNN_OK;
 }
 
@@ -133,6 +136,7 @@ int ensure_pack(rnn_ctx* ctx, size_t bytes) {
   }
   RNN_CUDA(cudaMalloc(&ctx->pack, want));
   ctx->pack_bytes = want;
+  ctx->mem_epoch++;
   return RNN_OK;
 }
 

@@ -7,6 +7,7 @@
 #include <stdio.h>
 
 #include <string>
+#include <vector>
 
 #include "../../include/rnn_b200.h"
 
@@ -93,6 +94,9 @@ struct rnn_ctx {
   // GEMMs it issues use ws for their split-K partials
   void* aux = nullptr;
   size_t aux_bytes = 0;
+  // bumped whenever a workspace above is reallocated, so that a captured
+  // CUDA graph holding the old pointers is recaptured instead of replayed
+  unsigned long long mem_epoch = 0;
 };
 
 namespace rnn {
@@ -102,4 +106,84 @@ int ensure_ws(rnn_ctx* ctx, size_t bytes);
 int ensure_stage(rnn_ctx* ctx, size_t bytes);
 int ensure_pack(rnn_ctx* ctx, size_t bytes);
 int ensure_aux(rnn_ctx* ctx, size_t bytes);
+
+// ---- CUDA-graph replay of a whole training step
+//
+// run_step_graph(ctx, g, key, body) performs one step per call.  `body`
+// enqueues the step's work (kernels, memsets, device copies, NCCL calls) on
+// ctx->stream and must not synchronise.  The first call with a given key
+// runs body eagerly (which sizes every lazily grown workspace); the second
+// captures it on a private stream into a graph and launches the graph; later
+// calls with the same key replay the graph.  The key must hold every value
+// the body bakes into launches (pointers, sizes, scalars) and the epochs of
+// the allocations it uses; a changed key drops the graph.
+struct StepGraph {
+  cudaGraphExec_t exec = nullptr;
+  cudaStream_t cap = nullptr;
+  cudaEvent_t ev = nullptr;
+  std::vector<unsigned long long> key, last_key;
+  unsigned long long kernels = 0;  // launches per replay, for rnn_launch_count
+  void release() {
+    if (exec) cudaGraphExecDestroy(exec);
+    exec = nullptr;
+    key.clear();
+  }
+  void destroy() {
+    release();
+    if (cap) cudaStreamDestroy(cap);
+    if (ev) cudaEventDestroy(ev);
+    cap = nullptr;
+    ev = nullptr;
+  }
+};
+
+template <class F>
+int run_step_graph(rnn_ctx* ctx, StepGraph& g, std::vector<unsigned long long> key, F&& body) {
+  key.push_back(ctx->mem_epoch);
+  if (g.exec && key == g.key) {
+    RNN_CUDA(cudaGraphLaunch(g.exec, ctx->stream));
+    __atomic_add_fetch(&g_launches, g.kernels, __ATOMIC_RELAXED);
+    return RNN_OK;
+  }
+  g.release();
+  if (key != g.last_key) {  // eager step; capture on the next call if nothing moves
+    RNN_TRY(body());
+    key.back() = ctx->mem_epoch;
+    g.last_key = key;
+    return RNN_OK;
+  }
+  if (!g.cap) RNN_CUDA(cudaStreamCreateWithFlags(&g.cap, cudaStreamNonBlocking));
+  if (!g.ev) RNN_CUDA(cudaEventCreateWithFlags(&g.ev, cudaEventDisableTiming));
+  cudaStream_t user = ctx->stream;
+  RNN_CUDA(cudaEventRecord(g.ev, user));
+  RNN_CUDA(cudaStreamWaitEvent(g.cap, g.ev, 0));
+  const unsigned long long l0 = __atomic_load_n(&g_launches, __ATOMIC_RELAXED);
+  ctx->stream = g.cap;
+  cudaError_t e = cudaStreamBeginCapture(g.cap, cudaStreamCaptureModeRelaxed);
+  int rc = e == cudaSuccess ? body() : set_error(RNN_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+  cudaGraph_t graph = nullptr;
+  cudaError_t e2 = cudaSuccess;
+  if (e == cudaSuccess) e2 = cudaStreamEndCapture(g.cap, &graph);
+  ctx->stream = user;
+  cudaGetLastError();
+  if (rc == RNN_OK && e2 == cudaSuccess && graph && ctx->mem_epoch == key.back()) {
+    cudaGraphExec_t exec = nullptr;
+    if (cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess) {
+      g.exec = exec;
+      g.key = key;
+      g.kernels = __atomic_load_n(&g_launches, __ATOMIC_RELAXED) - l0;
+    }
+  }
+  if (graph) cudaGraphDestroy(graph);
+  __atomic_sub_fetch(&g_launches, __atomic_load_n(&g_launches, __ATOMIC_RELAXED) - l0, __ATOMIC_RELAXED);
+  if (g.exec) {
+    RNN_CUDA(cudaGraphLaunch(g.exec, ctx->stream));
+    __atomic_add_fetch(&g_launches, g.kernels, __ATOMIC_RELAXED);
+    return RNN_OK;
+  }
+  // capture was not possible (nothing of it ran): do the step eagerly
+  cudaGetLastError();
+  g.last_key.clear();
+  return body();
+}
 }  // namespace rnn

@@ -84,6 +84,10 @@ struct rnn_resnet {
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1;
   bool sync_bn = false;
+  // CUDA-graph replay of the training step (rnn_resnet_set_graph)
+  bool use_graph = false;
+  rnn::StepGraph graph;
+  unsigned long long act_epoch = 0;  // bumped when the activations are reallocated
 };
 
 namespace rnn {
@@ -121,6 +125,7 @@ static int ensure_acts(rnn_resnet* net, int n, int h, int w) {
   if (n <= net->cap_n && h == net->cap_h && w == net->cap_w) return RNN_OK;
   RNN_CUDA(cudaStreamSynchronize(net->ctx->stream));
   free_acts(net);
+  net->act_epoch++;
   const int W = net->width;
   size_t stem = (size_t)n * W * h * w;
   RNN_TRY(alloc_f(net, &net->stem_y, stem));
@@ -335,6 +340,25 @@ static int train_step(rnn_resnet* net, const float* x, const uint32_t* labels, i
   return resnet_step(net, lr, mom, wd);
 }
 
+static unsigned long long fbits(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  return u;
+}
+
+// train_step, replayed from a CUDA graph when enabled (one launch per step
+// instead of ~900; the NCCL calls of the data-parallel step are captured too)
+static int train_step_any(rnn_resnet* net, const float* x, const uint32_t* labels, int n, float smooth, float lr,
+                          float mom, float wd, float* loss, int* correct) {
+  if (!net->use_graph) return train_step(net, x, labels, n, smooth, lr, mom, wd, loss, correct);
+  RNN_TRY(ensure_acts(net, n, 32, 32));
+  std::vector<unsigned long long> key = {(uintptr_t)x, (uintptr_t)labels, (unsigned long long)n, fbits(smooth),
+                                         fbits(lr), fbits(mom), fbits(wd), (uintptr_t)loss, (uintptr_t)correct,
+                                         net->act_epoch};
+  return run_step_graph(net->ctx, net->graph, key,
+                        [&]() { return train_step(net, x, labels, n, smooth, lr, mom, wd, loss, correct); });
+}
+
 }  // namespace rnn
 
 // ==================================================================== C ABI
@@ -499,6 +523,7 @@ extern "C" int rnn_resnet_destroy(rnn_resnet* net) {
   // the context may already be gone (interpreter teardown releases objects
   // in any order): wait on the device, not on the context's stream
   cudaDeviceSynchronize();
+  net->graph.destroy();  // before the NCCL communicator its graph may hold
   free_acts(net);
   cudaFree(net->v);
   cudaFree(net->g);
@@ -573,6 +598,13 @@ extern "C" int rnn_resnet_backward_dev(rnn_resnet* net, const float* dlogits) {
   return resnet_backward(net, dlogits);
 }
 
+extern "C" int rnn_resnet_set_graph(rnn_resnet* net, int enable) {
+  RNN_REQUIRE(net, "set_graph: null argument");
+  net->use_graph = enable != 0;
+  if (!net->use_graph) net->graph.release();
+  return RNN_OK;
+}
+
 extern "C" int rnn_resnet_step(rnn_resnet* net, float lr, float mom, float wd) {
   RNN_REQUIRE(net, "null argument");
   return resnet_step(net, lr, mom, wd);
@@ -582,8 +614,8 @@ extern "C" int rnn_resnet_train_step_dev(rnn_resnet* net, const float* x, const 
                                          float smooth, float lr, float mom, float wd, float* loss, int* correct) {
   RNN_REQUIRE(net && x && labels, "train_step: null argument");
   RNN_REQUIRE(n > 0, "train_step: empty batch");
-  return train_step(net, x, labels, n, smooth, lr, mom, wd, loss ? loss : net->loss_dev,
-                    correct ? correct : net->correct_dev);
+  return train_step_any(net, x, labels, n, smooth, lr, mom, wd, loss ? loss : net->loss_dev,
+                        correct ? correct : net->correct_dev);
 }
 
 extern "C" int rnn_resnet_train_step(rnn_resnet* net, const float* x, const uint32_t* labels, int n, float smooth,
@@ -594,7 +626,8 @@ extern "C" int rnn_resnet_train_step(rnn_resnet* net, const float* x, const uint
   RNN_TRY(ensure_acts(net, n, 32, 32));
   RNN_CUDA(cudaMemcpyAsync(net->x_stage, x, (size_t)n * 3 * 32 * 32 * 4, cudaMemcpyHostToDevice, ctx->stream));
   RNN_CUDA(cudaMemcpyAsync(net->lab_stage, labels, (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream));
-  RNN_TRY(train_step(net, net->x_stage, net->lab_stage, n, smooth, lr, mom, wd, net->loss_dev, net->correct_dev));
+  RNN_TRY(train_step_any(net, net->x_stage, net->lab_stage, n, smooth, lr, mom, wd, net->loss_dev,
+                         net->correct_dev));
   float l = 0.0f;
   int c = 0;
   RNN_CUDA(cudaMemcpyAsync(&l, net->loss_dev, 4, cudaMemcpyDeviceToHost, ctx->stream));

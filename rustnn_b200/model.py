@@ -95,6 +95,10 @@ class ResNet:
         self.ctx.bind()
         call("rnn_resnet_backward_dev", self.h, C.c_void_p(dlogits.data_ptr()))
 
+    def use_graph(self, enable: bool = True):
+        """Replay the training step from a CUDA graph (see rnn_resnet_set_graph)."""
+        call("rnn_resnet_set_graph", self.h, int(bool(enable)))
+
     def step(self, lr: float, mom: float, wd: float):
         self.ctx.bind()
         call("rnn_resnet_step", self.h, lr, mom, wd)
