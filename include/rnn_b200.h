@@ -276,6 +276,57 @@ int rnn_kl_distill_dev(rnn_ctx *ctx, const float *student, const float *teacher,
 int rnn_hint_mse_dev(rnn_ctx *ctx, const float *pred, const float *target,
                      int n, int c, float scale, float *dz, float *loss_out);
 
+/* ---- host-pointer tier of the attention / norm / optimiser entries -------
+ * Same arguments as the _dev entries above, on host memory: the call stages
+ * the operands, runs the device entry, copies results back and
+ * synchronises.  Accumulating outputs are read and written back. */
+int rnn_attn_fwd(rnn_ctx *ctx, int n, int h, int dh, int th, int tw, int mh,
+                 int mw, int mask_diag, const float *q, int qstride, int qoff,
+                 const float *kv, int kvstride, int koff, int voff,
+                 const float *tau, const float *rel, float *p, float *o);   /* attn.rs:148 */
+int rnn_attn_bwd(rnn_ctx *ctx, int n, int h, int dh, int th, int tw, int mh,
+                 int mw, const float *q, int qstride, int qoff,
+                 const float *kv, int kvstride, int koff, int voff,
+                 const float *tau, const float *p, const float *dout,
+                 float *dq, float *dkv, float *dtau, float *drel);          /* attn.rs:226 */
+int rnn_layernorm_fwd(rnn_ctx *ctx, const float *x, int rows, int c,
+                      const float *gamma, const float *beta, float eps,
+                      float *y, float *xhat, float *invstd);                 /* norm.rs:59 */
+int rnn_layernorm_bwd(rnn_ctx *ctx, const float *dy, const float *xhat,
+                      const float *invstd, int rows, int c, const float *gamma,
+                      float *dx, float *dgamma, float *dbeta);               /* norm.rs:101 */
+int rnn_linear_fwd(rnn_ctx *ctx, const float *x, int rows, int fin, int fout,
+                   const float *w, const float *b, float *y);                /* linear.rs:44 */
+int rnn_linear_bwd(rnn_ctx *ctx, const float *x, const float *dy, int rows,
+                   int fin, int fout, const float *w, float *dw, float *db,
+                   float *dx);                                               /* linear.rs:66 */
+int rnn_batchnorm_fwd(rnn_ctx *ctx, const float *y, int n, int c, int hw,
+                      const float *gamma, const float *beta, float *rmean,
+                      float *rvar, float mom, float eps, int relu,
+                      float *mean, float *invstd, float *out);               /* nn.rs:290-354 */
+int rnn_batchnorm_bwd(rnn_ctx *ctx, const float *dy, const float *y, int n,
+                      int c, int hw, const float *gamma, const float *mean,
+                      const float *invstd, const float *relu_out, float *dx,
+                      float *dgamma, float *dbeta);                          /* nn.rs:384-427 */
+/* newton_schulz (optim.rs:124-145) over `count` matrices in one call, each
+ * in place; the device form takes an array of device pointers (the 39
+ * matrices of Optim::step_all, optim.rs:182-190, in one call). */
+int rnn_newton_schulz_batched_dev(rnn_ctx *ctx, int count, float *const *g,
+                                  const int *rows, const int *cols, int steps);
+int rnn_newton_schulz_batched(rnn_ctx *ctx, int count, float *const *g,
+                              const int *rows, const int *cols, int steps);
+int rnn_muon_step(rnn_ctx *ctx, float *v, float *g, float *m, int rows,
+                  int cols, int steps, float lr, float mom, float wd,
+                  int decay);                                                /* optim.rs:183-199 */
+int rnn_adamw_step(rnn_ctx *ctx, float *v, float *g, float *m, float *v2,
+                   size_t n, float lr, float wd, int decay, float b1, float b2,
+                   float eps, int t);                                        /* optim.rs:205-233 */
+int rnn_sgd_nesterov(rnn_ctx *ctx, float *v, float *g, float *m, size_t len,
+                     float lr, float mom, float wd, int decay);              /* nn.rs:102-110 */
+int rnn_clip(rnn_ctx *ctx, float *g, size_t n, float max, float *norm_out);  /* optim.rs:237-250 */
+int rnn_ema_update(rnn_ctx *ctx, float *e, const float *v, size_t n,
+                   float decay, int t);                                      /* optim.rs:270-287 */
+
 /* ---- ResNet training step (model.rs, train.rs:684-699) ------------------ */
 /* ResNet::new(depth_n, width, nclass, seed) (model.rs:112-133), with the
  * reference's initialisation drawn from the same xoshiro256++ stream, so

@@ -99,6 +99,21 @@ SIGS = {
     "rnn_ce_soft_dev": [CTX, FP, FP, FP, I, I, F, FP, FP, FP],
     "rnn_kl_distill_dev": [CTX, FP, FP, I, I, F, F, FP, FP],
     "rnn_hint_mse_dev": [CTX, FP, FP, I, I, F, FP, FP],
+    "rnn_attn_fwd": [CTX, I, I, I, I, I, I, I, I, FP, I, I, FP, I, I, I, FP, FP, FP, FP],
+    "rnn_attn_bwd": [CTX, I, I, I, I, I, I, I, FP, I, I, FP, I, I, I, FP, FP, FP, FP, FP, FP, FP],
+    "rnn_layernorm_fwd": [CTX, FP, I, I, FP, FP, F, FP, FP, FP],
+    "rnn_layernorm_bwd": [CTX, FP, FP, FP, I, I, FP, FP, FP, FP],
+    "rnn_linear_fwd": [CTX, FP, I, I, I, FP, FP, FP],
+    "rnn_linear_bwd": [CTX, FP, FP, I, I, I, FP, FP, FP, FP],
+    "rnn_batchnorm_fwd": [CTX, FP, I, I, I, FP, FP, FP, FP, F, F, I, FP, FP, FP],
+    "rnn_batchnorm_bwd": [CTX, FP, FP, I, I, I, FP, FP, FP, FP, FP, FP, FP],
+    "rnn_newton_schulz_batched_dev": [CTX, I, P, P, P, I],
+    "rnn_newton_schulz_batched": [CTX, I, P, P, P, I],
+    "rnn_muon_step": [CTX, FP, FP, FP, I, I, I, F, F, F, I],
+    "rnn_adamw_step": [CTX, FP, FP, FP, FP, Z, F, F, I, F, F, F, I],
+    "rnn_sgd_nesterov": [CTX, FP, FP, FP, Z, F, F, F, I],
+    "rnn_clip": [CTX, FP, Z, F, FP],
+    "rnn_ema_update": [CTX, FP, FP, Z, F, I],
     "rnn_resnet_create": [CTX, I, I, I, U64, C.POINTER(NET)],
     "rnn_resnet_destroy": [NET],
     "rnn_resnet_num_params": [NET, C.POINTER(Z)],

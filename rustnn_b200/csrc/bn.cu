@@ -342,7 +342,7 @@ __global__ void bn_dx_kernel(const float* __restrict__ dy, const float* __restri
   }
 }
 
-static int bn_parts(int n, int C, int num_sms) {
+int bn_parts(int n, int C, int num_sms) {
   int P = (8 * num_sms + C - 1) / C;
   if (P > n) P = n;
   if (P < 1) P = 1;
@@ -370,6 +370,10 @@ static unsigned ew_grid(size_t total, int num_sms) {
 
 int bn_fwd_sums(rnn_ctx* ctx, const float* y, int n, int C, int hw, double* part, double* sums) {
   const int P = bn_parts(n, C, ctx->num_sms);
+  // the partials and the per-channel sums must not overlap (the combine
+  // kernel reads one while it writes the other)
+  RNN_REQUIRE(part + (size_t)C * P * 2 <= sums || sums + (size_t)C * 2 <= part,
+              "batchnorm: partial-sum buffer (%d x %d) overlaps the sums", C, P);
   RNN_RANGE(y, sizeof(float) * (size_t)n * C * hw);
   RNN_RANGE(part, sizeof(double) * (size_t)C * P * 2);
   RNN_RANGE(sums, sizeof(double) * (size_t)C * 2);
@@ -414,6 +418,10 @@ int bn_fwd_finish(rnn_ctx* ctx, const float* y, int n, int C, int hw, double cou
 int bn_bwd_sums(rnn_ctx* ctx, const float* dy, const float* y, const float* relu_out, int n, int C, int hw,
                 const float* mean, const float* invstd, double* part, double* sums) {
   const int P = bn_parts(n, C, ctx->num_sms);
+  // the partials and the per-channel sums must not overlap (the combine
+  // kernel reads one while it writes the other)
+  RNN_REQUIRE(part + (size_t)C * P * 2 <= sums || sums + (size_t)C * 2 <= part,
+              "batchnorm: partial-sum buffer (%d x %d) overlaps the sums", C, P);
   RNN_RANGE(dy, sizeof(float) * (size_t)n * C * hw);
   RNN_RANGE(y, sizeof(float) * (size_t)n * C * hw);
   if (relu_out) RNN_RANGE(relu_out, sizeof(float) * (size_t)n * C * hw);

@@ -8,6 +8,9 @@
 namespace rnn {
 
 size_t bn_scratch_bytes(int n, int C, int num_sms);
+// Number of per-channel partial sums the BN kernels write ([C][P][2] f64);
+// every caller that lays out its own partial buffer must use this count.
+int bn_parts(int n, int C, int num_sms);
 
 // sums[c] = (sum y, sum y^2)
 int bn_fwd_sums(rnn_ctx* ctx, const float* y, int n, int C, int hw, double* part, double* sums);

@@ -177,7 +177,7 @@ struct BnScratch {
 static BnScratch bn_scratch(rnn_resnet* net, int n, int C) {
   BnScratch s;
   char* base = static_cast<char*>(net->scratch);
-  const int P = std::max(1, std::min(n, (4 * net->ctx->num_sms + C - 1) / C));
+  const int P = bn_parts(n, C, net->ctx->num_sms);
   size_t a = ((size_t)C * P * 2 * sizeof(double) + 255) & ~(size_t)255;
   size_t b = ((size_t)C * 2 * sizeof(double) + 255) & ~(size_t)255;
   s.part = reinterpret_cast<double*>(base);
