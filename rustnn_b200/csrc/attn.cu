@@ -1,21 +1,23 @@
 // Fused batched attention: attn.rs Core::forward (:148-223) and
 // Core::backward (:226-343) for every (image, head) in one launch.
 //
-// One CTA per (head, image, query chunk).  K and V of the (image, head) and
-// the chunk's Q / dO rows live in shared memory (rows padded to dh+1 floats
-// so column walks are bank-conflict free), next to the chunk's score block.
-// The contractions are register-tiled f32 FFMA: a warp owns 8 rows, a lane
-// owns columns lane + 32*j, so A reads are warp broadcasts and B reads hit 32
-// distinct banks.  Softmax is one warp per row.
+// Forward: one CTA per (head, image, chunk of query rows) holds K and V of
+// the pair in shared memory (rows padded to dh+1 floats so a lane walking its
+// own key row hits its own bank); each warp streams query rows: lane l scores
+// keys l+32k against the row held in registers, the softmax is two warp
+// reductions, P goes to HBM (the backward reads it, attn.rs:186-211) and to a
+// per-warp row buffer, and lane d forms O[i][d].
 //
-// Outputs follow the reference exactly: P is written to HBM (the backward
-// reads it, attn.rs:186-211), O goes to [n, tq, h*dh], and the backward
-// accumulates (+=) into strided dq / dkv (attn.rs:274, 323, 327) and into
-// dtau / drel.  dtau and drel are reduced without atomics: each CTA writes a
-// partial (drel built row by row: within one query row every key maps to a
-// distinct relative-position index), and a second kernel sums the partials
-// in a fixed order.  The query-chunked backward runs one launch per chunk so
-// the += into dK / dV never races.
+// Backward in two phases.  Row phase (per query chunk): dP = dO V^T and the
+// raw scores Q K^T are recomputed per key, dS = P (dP - sum dP P), dtau and
+// drel partials (drel in a warp-private buffer: within one query row every
+// key maps to a distinct relative index), tau*dS to a workspace, and dQ +=
+// tau dS K.  Column phase (per key chunk): dV += P^T dO and dK += (tau dS)^T
+// Q from shared-memory copies of the chunk's columns.  The per-CTA partials
+// are summed in a fixed order by a warp-per-output kernel, so the whole
+// backward is deterministic and uses no atomics.  dq / dkv / dtau / drel
+// accumulate (+=) like attn.rs:274, 323, 327.
+#include <algorithm>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -78,54 +80,22 @@ struct AttnArgs {
   int kvstride, koff, voff;
   const float* tau;
   const float* rel;
-  float* p;        // forward writes P
+  float* p;          // forward writes P
   const float* pin;  // backward reads P
   float* o;
   const float* dout;
   float* dq;
   float* dkv;
+  float* ds;    // backward: tau * dS [n][h][tq][tk]
   float* part;  // backward partials [n][nchunk][h][1 + nrel]
-  int tqc, nchunk, chunk;
+  int qc, nchunk;
 };
 
-constexpr int ATT_THREADS = 256;
-constexpr int ATT_WARPS = ATT_THREADS / 32;
-
-// out(i, j) = sum_k fa(i, k) * fb(k, j) for i < M, j < N.  Warp w owns rows
-// w*TM.. (stepping by 8*TM), lane l owns columns l + 32*jj (jj < TN).
-template <int TM, int TN, class FA, class FB, class FO>
-__device__ __forceinline__ void tile_mm(int M, int N, int K, FA fa, FB fb, FO fo) {
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  for (int i0 = w * TM; i0 < M; i0 += ATT_WARPS * TM)
-    for (int jb = 0; jb < N; jb += 32 * TN) {
-      float acc[TM][TN];
-#pragma unroll
-      for (int ii = 0; ii < TM; ii++)
-#pragma unroll
-        for (int jj = 0; jj < TN; jj++) acc[ii][jj] = 0.0f;
-      for (int k = 0; k < K; k++) {
-        float av[TM], bv[TN];
-#pragma unroll
-        for (int ii = 0; ii < TM; ii++) av[ii] = (i0 + ii < M) ? fa(i0 + ii, k) : 0.0f;
-#pragma unroll
-        for (int jj = 0; jj < TN; jj++) {
-          const int j = jb + l + 32 * jj;
-          bv[jj] = (j < N) ? fb(k, j) : 0.0f;
-        }
-#pragma unroll
-        for (int ii = 0; ii < TM; ii++)
-#pragma unroll
-          for (int jj = 0; jj < TN; jj++) acc[ii][jj] = fmaf(av[ii], bv[jj], acc[ii][jj]);
-      }
-#pragma unroll
-      for (int ii = 0; ii < TM; ii++)
-#pragma unroll
-        for (int jj = 0; jj < TN; jj++) {
-          const int i = i0 + ii, j = jb + l + 32 * jj;
-          if (i < M && j < N) fo(i, j, acc[ii][jj]);
-        }
-    }
-}
+constexpr int AT_THREADS = 256;
+constexpr int AT_WARPS = AT_THREADS / 32;
+constexpr int AT_MAXK = 8;   // keys per lane: tk <= 256
+constexpr int AT_QC = 64;    // query rows per CTA (row kernels)
+constexpr int AT_KC = 32;    // keys per CTA (column kernel)
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -138,219 +108,336 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// K and V of one (image, head) into shared memory, rows padded to DH+1
+// floats (a lane walking its own key row hits a distinct bank).
 template <int DH>
-__global__ void __launch_bounds__(ATT_THREADS) attn_fwd_kernel(const AttnArgs a) {
-  extern __shared__ float sm[];
+__device__ __forceinline__ void load_kv(const AttnArgs& a, int img, int hd, float* Ks, float* Vs) {
   constexpr int LD = DH + 1;
-  constexpr int TND = DH >= 32 ? DH / 32 : 1;
-  const int hd = blockIdx.x, img = blockIdx.y;
-  const int q0 = blockIdx.z * a.tqc;
-  const int tqc = min(a.tqc, a.tq - q0);
-  const int tk = a.tk, c = a.h * DH;
-  float* Qs = sm;
-  float* Ks = Qs + a.tqc * LD;
-  float* Vs = Ks + tk * LD;
-  float* Ss = Vs + tk * LD;
-  for (int e = threadIdx.x; e < tqc * DH; e += ATT_THREADS) {
+  for (int e = threadIdx.x; e < a.tk * DH; e += AT_THREADS) {
     const int r = e / DH, d = e - r * DH;
-    Qs[r * LD + d] = a.q[((size_t)img * a.tq + q0 + r) * a.qstride + a.qoff + hd * DH + d];
-  }
-  for (int e = threadIdx.x; e < tk * DH; e += ATT_THREADS) {
-    const int r = e / DH, d = e - r * DH;
-    const float* row = a.kv + ((size_t)img * tk + r) * a.kvstride + hd * DH + d;
+    const float* row = a.kv + ((size_t)img * a.tk + r) * a.kvstride + hd * DH + d;
     Ks[r * LD + d] = row[a.koff];
     Vs[r * LD + d] = row[a.voff];
   }
+}
+
+// Forward (attn.rs:167-221), one CTA per (head, image, chunk of AT_QC query
+// rows), one warp per query row at a time: lane l scores keys l + 32k
+// against the row (held in registers), the row softmax is two warp
+// reductions, P goes to HBM and to a per-warp row buffer, and lane d forms
+// O[i][d] = sum_j P[i][j] V[j][d].
+template <int DH>
+__global__ void __launch_bounds__(AT_THREADS) attn_fwd_kernel(const AttnArgs a) {
+  extern __shared__ float sm[];
+  constexpr int LD = DH + 1;
+  const int hd = blockIdx.x, img = blockIdx.y, q0 = blockIdx.z * a.qc;
+  const int rows = min(a.qc, a.tq - q0), tk = a.tk, c = a.h * DH;
+  float* Ks = sm;
+  float* Vs = Ks + tk * LD;
+  float* Pw = Vs + tk * LD;  // [AT_WARPS][tk]
+  load_kv<DH>(a, img, hd, Ks, Vs);
   __syncthreads();
-  // S = tau * Q K^T + rel[relidx], diagonal masked (attn.rs:181-195)
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   const float t = a.tau[hd];
   const float* rb = a.rel + (size_t)hd * a.nrel;
-  tile_mm<8, 2>(
-      tqc, tk, DH, [&](int i, int k) { return Qs[i * LD + k]; }, [&](int k, int j) { return Ks[j * LD + k]; },
-      [&](int i, int j, float v) {
-        const int qi = q0 + i;
-        float val = t * v + rb[a.relidx[(size_t)qi * tk + j]];
-        if (a.mask && j == qi) val = -INFINITY;
-        Ss[i * tk + j] = val;
-      });
-  __syncthreads();
-  // row softmax (attn.rs:191-211); P to HBM for the backward
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  for (int i = w; i < tqc; i += ATT_WARPS) {
-    float* row = Ss + i * tk;
+  float* prow = Pw + w * tk;
+  for (int i = w; i < rows; i += AT_WARPS) {
+    const int qi = q0 + i;
+    float qr[DH];
+    const float* qg = a.q + ((size_t)img * a.tq + qi) * a.qstride + a.qoff + hd * DH;
+#pragma unroll
+    for (int d = 0; d < DH; d++) qr[d] = __ldg(qg + d);
+    const uint32_t* ridx = a.relidx + (size_t)qi * tk;
+    float sv[AT_MAXK];
     float mx = -INFINITY;
-    for (int j = l; j < tk; j += 32) mx = fmaxf(mx, row[j]);
+#pragma unroll
+    for (int k = 0; k < AT_MAXK; k++) {
+      const int j = l + 32 * k;
+      float val = -INFINITY;
+      if (j < tk) {
+        const float* kr = Ks + j * LD;
+        float acc = 0.0f;
+#pragma unroll
+        for (int d = 0; d < DH; d++) acc = fmaf(qr[d], kr[d], acc);
+        val = t * acc + rb[ridx[j]];  // attn.rs:181-190
+        if (a.mask && j == qi) val = -INFINITY;  // attn.rs:194
+      }
+      sv[k] = val;
+      mx = fmaxf(mx, val);
+    }
     mx = warp_max(mx);
     float sum = 0.0f;
-    for (int j = l; j < tk; j += 32) {
-      const float e = row[j] == -INFINITY ? 0.0f : expf(row[j] - mx);
-      row[j] = e;
+#pragma unroll
+    for (int k = 0; k < AT_MAXK; k++) {
+      const float e = sv[k] == -INFINITY ? 0.0f : expf(sv[k] - mx);
+      sv[k] = e;
       sum += e;
     }
     sum = warp_sum(sum);
     const float inv = 1.0f / sum;
-    float* prow = a.p + (((size_t)img * a.h + hd) * a.tq + q0 + i) * tk;
-    for (int j = l; j < tk; j += 32) {
-      const float pv = row[j] * inv;
-      row[j] = pv;
-      prow[j] = pv;
+    float* pg = a.p + (((size_t)img * a.h + hd) * a.tq + qi) * tk;
+#pragma unroll
+    for (int k = 0; k < AT_MAXK; k++) {
+      const int j = l + 32 * k;
+      if (j < tk) {
+        const float pv = sv[k] * inv;
+        pg[j] = pv;
+        prow[j] = pv;
+      }
     }
+    __syncwarp();
+    float* og = a.o + ((size_t)img * a.tq + qi) * c + hd * DH;
+    for (int d = l; d < DH; d += 32) {
+      float acc = 0.0f;
+      for (int j = 0; j < tk; j++) acc = fmaf(prow[j], Vs[j * LD + d], acc);
+      og[d] = acc;
+    }
+    __syncwarp();
   }
-  __syncthreads();
-  // O = P V (attn.rs:213-220)
-  tile_mm<8, TND>(
-      tqc, DH, tk, [&](int i, int k) { return Ss[i * tk + k]; }, [&](int k, int j) { return Vs[k * LD + j]; },
-      [&](int i, int j, float v) { a.o[((size_t)img * a.tq + q0 + i) * c + hd * DH + j] = v; });
 }
 
+// Backward, row phase (attn.rs:276-321), one CTA per (head, image, chunk of
+// query rows), a warp per row: dP = dO V^T and the raw scores Q K^T are
+// recomputed per key, dS = P (dP - sum_k dP P); dtau accumulates dS * QK^T,
+// drel accumulates dS at the row's relative indices (distinct within a row,
+// so a warp-private buffer takes them without atomics), tau * dS goes to HBM
+// for the column phase, and lane d adds tau * sum_j dS[i][j] K[j][d] to dQ.
+// Partials (dtau, drel) per CTA are summed in a fixed order afterwards.
 template <int DH>
-__global__ void __launch_bounds__(ATT_THREADS) attn_bwd_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(AT_THREADS) attn_bwd_rows_kernel(const AttnArgs a) {
   extern __shared__ float sm[];
   constexpr int LD = DH + 1;
-  constexpr int TND = DH >= 32 ? DH / 32 : 1;
-  const int hd = blockIdx.x, img = blockIdx.y;
-  const int q0 = a.chunk * a.tqc;
-  const int tqc = min(a.tqc, a.tq - q0);
-  const int tk = a.tk, c = a.h * DH, nrel = a.nrel;
+  const int hd = blockIdx.x, img = blockIdx.y, chunk = blockIdx.z, q0 = chunk * a.qc;
+  const int rows = min(a.qc, a.tq - q0), tk = a.tk, c = a.h * DH, nrel = a.nrel;
   float* Ks = sm;
   float* Vs = Ks + tk * LD;
-  float* Qs = Vs + tk * LD;
-  float* Ds = Qs + a.tqc * LD;  // dO chunk
-  float* Ps = Ds + a.tqc * LD;  // P chunk
-  float* Gs = Ps + a.tqc * tk;  // dP -> dS
-  float* Rs = Gs + a.tqc * tk;  // drel partial [nrel]
-  __shared__ float red[ATT_WARPS];
-  for (int e = threadIdx.x; e < tk * DH; e += ATT_THREADS) {
-    const int r = e / DH, d = e - r * DH;
-    const float* row = a.kv + ((size_t)img * tk + r) * a.kvstride + hd * DH + d;
-    Ks[r * LD + d] = row[a.koff];
-    Vs[r * LD + d] = row[a.voff];
-  }
-  for (int e = threadIdx.x; e < tqc * DH; e += ATT_THREADS) {
-    const int r = e / DH, d = e - r * DH;
-    Qs[r * LD + d] = a.q[((size_t)img * a.tq + q0 + r) * a.qstride + a.qoff + hd * DH + d];
-    Ds[r * LD + d] = a.dout[((size_t)img * a.tq + q0 + r) * c + hd * DH + d];
-  }
-  const float* pbase = a.pin + (((size_t)img * a.h + hd) * a.tq + q0) * tk;
-  for (int e = threadIdx.x; e < tqc * tk; e += ATT_THREADS) Ps[e] = pbase[e];
-  for (int e = threadIdx.x; e < nrel; e += ATT_THREADS) Rs[e] = 0.0f;
+  float* Dw = Vs + tk * LD;              // [AT_WARPS][tk] tau * dS row
+  float* Rw = Dw + AT_WARPS * tk;        // [AT_WARPS][nrel] drel per warp
+  __shared__ float red[AT_WARPS];
+  load_kv<DH>(a, img, hd, Ks, Vs);
+  for (int e = threadIdx.x; e < AT_WARPS * nrel; e += AT_THREADS) Rw[e] = 0.0f;
   __syncthreads();
-  // dV += P^T dO (attn.rs:270-274)
-  tile_mm<8, TND>(
-      tk, DH, tqc, [&](int kj, int i) { return Ps[i * tk + kj]; }, [&](int i, int d) { return Ds[i * LD + d]; },
-      [&](int kj, int d, float v) { a.dkv[((size_t)img * tk + kj) * a.kvstride + a.voff + hd * DH + d] += v; });
-  // dP = dO V^T (attn.rs:276-279)
-  tile_mm<8, 2>(
-      tqc, tk, DH, [&](int i, int d) { return Ds[i * LD + d]; }, [&](int d, int kj) { return Vs[kj * LD + d]; },
-      [&](int i, int kj, float v) { Gs[i * tk + kj] = v; });
-  __syncthreads();
-  // dS = P (dP - sum_k dP P) (attn.rs:280-290)
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  for (int i = w; i < tqc; i += ATT_WARPS) {
-    float* g = Gs + i * tk;
-    const float* pr = Ps + i * tk;
-    float dot = 0.0f;
-    for (int j = l; j < tk; j += 32) dot += g[j] * pr[j];
-    dot = warp_sum(dot);
-    for (int j = l; j < tk; j += 32) g[j] = pr[j] * (g[j] - dot);
-  }
-  __syncthreads();
-  // dtau partial: sum dS * (Q K^T), raw scores recomputed (attn.rs:292-308)
+  const float t = a.tau[hd];
+  float* dsrow = Dw + w * tk;
+  float* rw = Rw + w * nrel;
   float tacc = 0.0f;
-  tile_mm<8, 2>(
-      tqc, tk, DH, [&](int i, int k) { return Qs[i * LD + k]; }, [&](int k, int j) { return Ks[j * LD + k]; },
-      [&](int i, int j, float v) { tacc += Gs[i * tk + j] * v; });
+  for (int i = w; i < rows; i += AT_WARPS) {
+    const int qi = q0 + i;
+    float qr[DH], dr[DH];
+    const float* qg = a.q + ((size_t)img * a.tq + qi) * a.qstride + a.qoff + hd * DH;
+    const float* dg = a.dout + ((size_t)img * a.tq + qi) * c + hd * DH;
+#pragma unroll
+    for (int d = 0; d < DH; d++) {
+      qr[d] = __ldg(qg + d);
+      dr[d] = __ldg(dg + d);
+    }
+    const float* pg = a.pin + (((size_t)img * a.h + hd) * a.tq + qi) * tk;
+    float pv[AT_MAXK], dp[AT_MAXK], raw[AT_MAXK];
+    float dot = 0.0f;
+#pragma unroll
+    for (int k = 0; k < AT_MAXK; k++) {
+      const int j = l + 32 * k;
+      pv[k] = dp[k] = raw[k] = 0.0f;
+      if (j < tk) {
+        const float* kr = Ks + j * LD;
+        const float* vr = Vs + j * LD;
+        float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+        for (int d = 0; d < DH; d++) {
+          s1 = fmaf(dr[d], vr[d], s1);
+          s2 = fmaf(qr[d], kr[d], s2);
+        }
+        dp[k] = s1;
+        raw[k] = s2;
+        pv[k] = __ldg(pg + j);
+        dot = fmaf(s1, pv[k], dot);
+      }
+    }
+    dot = warp_sum(dot);
+    const uint32_t* ridx = a.relidx + (size_t)qi * tk;
+    float* dsg = a.ds + (((size_t)img * a.h + hd) * a.tq + qi) * tk;
+#pragma unroll
+    for (int k = 0; k < AT_MAXK; k++) {
+      const int j = l + 32 * k;
+      if (j < tk) {
+        const float ds = pv[k] * (dp[k] - dot);
+        tacc = fmaf(ds, raw[k], tacc);
+        rw[ridx[j]] += ds;
+        const float dst = ds * t;
+        dsrow[j] = dst;
+        dsg[j] = dst;
+      }
+    }
+    __syncwarp();
+    float* dqg = a.dq + ((size_t)img * a.tq + qi) * a.qstride + a.qoff + hd * DH;
+    for (int d = l; d < DH; d += 32) {
+      float acc = 0.0f;
+      for (int j = 0; j < tk; j++) acc = fmaf(dsrow[j], Ks[j * LD + d], acc);
+      dqg[d] += acc;
+    }
+    __syncwarp();
+  }
   tacc = warp_sum(tacc);
   if (l == 0) red[w] = tacc;
-  // drel partial, one query row at a time (distinct indices within a row)
-  for (int i = 0; i < tqc; i++) {
-    const uint32_t* ridx = a.relidx + (size_t)(q0 + i) * tk;
-    for (int j = threadIdx.x; j < tk; j += ATT_THREADS) Rs[ridx[j]] += Gs[i * tk + j];
-    __syncthreads();
-  }
-  float* part = a.part + (((size_t)img * a.nchunk + a.chunk) * a.h + hd) * (1 + nrel);
+  __syncthreads();
+  float* part = a.part + (((size_t)img * a.nchunk + chunk) * a.h + hd) * (1 + nrel);
   if (threadIdx.x == 0) {
     float s = 0.0f;
-    for (int k = 0; k < ATT_WARPS; k++) s += red[k];
+    for (int k = 0; k < AT_WARPS; k++) s += red[k];
     part[0] = s;
   }
-  for (int e = threadIdx.x; e < nrel; e += ATT_THREADS) part[1 + e] = Rs[e];
-  // dS *= tau (attn.rs:316)
-  const float t = a.tau[hd];
-  for (int e = threadIdx.x; e < tqc * tk; e += ATT_THREADS) Gs[e] *= t;
+  for (int r = threadIdx.x; r < nrel; r += AT_THREADS) {
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < AT_WARPS; k++) s += Rw[k * nrel + r];
+    part[1 + r] = s;
+  }
+}
+
+// Backward, column phase (attn.rs:270-274, 322-327): one CTA per (head,
+// image, chunk of AT_KC keys); warp w owns keys w, w+4, ... of the chunk and
+// lane d the head-dim columns d, d+32: dV[j][d] += sum_i P[i][j] dO[i][d],
+// dK[j][d] += sum_i (tau dS)[i][j] Q[i][d], with the chunk's P / dS columns
+// and all Q / dO rows staged in shared memory.
+template <int DH>
+__global__ void __launch_bounds__(AT_THREADS) attn_bwd_cols_kernel(const AttnArgs a) {
+  extern __shared__ float sm[];
+  constexpr int KPW = AT_KC / AT_WARPS;       // keys per warp
+  constexpr int DPL = (DH + 31) / 32;         // columns per lane
+  const int hd = blockIdx.x, img = blockIdx.y, k0 = blockIdx.z * AT_KC;
+  const int nk = min(AT_KC, a.tk - k0), tq = a.tq, tk = a.tk, c = a.h * DH;
+  float* Qs = sm;                  // [tq][DH]
+  float* Os = Qs + tq * DH;        // [tq][DH]  dO
+  float* Ps = Os + tq * DH;        // [tq][AT_KC]
+  float* Ss = Ps + tq * AT_KC;     // [tq][AT_KC]  tau * dS
+  for (int e = threadIdx.x; e < tq * DH; e += AT_THREADS) {
+    const int r = e / DH, d = e - r * DH;
+    Qs[e] = a.q[((size_t)img * tq + r) * a.qstride + a.qoff + hd * DH + d];
+    Os[e] = a.dout[((size_t)img * tq + r) * c + hd * DH + d];
+  }
+  const size_t pb = (((size_t)img * a.h + hd) * tq) * tk + k0;
+  for (int e = threadIdx.x; e < tq * AT_KC; e += AT_THREADS) {
+    const int r = e / AT_KC, j = e - r * AT_KC;
+    const bool ok = j < nk;
+    Ps[e] = ok ? a.pin[pb + (size_t)r * tk + j] : 0.0f;
+    Ss[e] = ok ? a.ds[pb + (size_t)r * tk + j] : 0.0f;
+  }
   __syncthreads();
-  // dQ += dS K, dK += dS^T Q (attn.rs:318-327)
-  tile_mm<8, TND>(
-      tqc, DH, tk, [&](int i, int kj) { return Gs[i * tk + kj]; }, [&](int kj, int d) { return Ks[kj * LD + d]; },
-      [&](int i, int d, float v) { a.dq[((size_t)img * a.tq + q0 + i) * a.qstride + a.qoff + hd * DH + d] += v; });
-  tile_mm<8, TND>(
-      tk, DH, tqc, [&](int kj, int i) { return Gs[i * tk + kj]; }, [&](int i, int d) { return Qs[i * LD + d]; },
-      [&](int kj, int d, float v) { a.dkv[((size_t)img * tk + kj) * a.kvstride + a.koff + hd * DH + d] += v; });
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  float dv[KPW][DPL], dk[KPW][DPL];
+#pragma unroll
+  for (int u = 0; u < KPW; u++)
+#pragma unroll
+    for (int v = 0; v < DPL; v++) dv[u][v] = dk[u][v] = 0.0f;
+  for (int i = 0; i < tq; i++) {
+    float qv[DPL], ov[DPL];
+#pragma unroll
+    for (int v = 0; v < DPL; v++) {
+      const int d = l + 32 * v;
+      qv[v] = d < DH ? Qs[i * DH + d] : 0.0f;
+      ov[v] = d < DH ? Os[i * DH + d] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < KPW; u++) {
+      const float p = Ps[i * AT_KC + w + AT_WARPS * u];
+      const float g = Ss[i * AT_KC + w + AT_WARPS * u];
+#pragma unroll
+      for (int v = 0; v < DPL; v++) {
+        dv[u][v] = fmaf(p, ov[v], dv[u][v]);
+        dk[u][v] = fmaf(g, qv[v], dk[u][v]);
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < KPW; u++) {
+    const int j = w + AT_WARPS * u;
+    if (j >= nk) continue;
+    float* row = a.dkv + ((size_t)img * tk + k0 + j) * a.kvstride + hd * DH;
+#pragma unroll
+    for (int v = 0; v < DPL; v++) {
+      const int d = l + 32 * v;
+      if (d < DH) {
+        row[a.voff + d] += dv[u][v];
+        row[a.koff + d] += dk[u][v];
+      }
+    }
+  }
 }
 
 // dtau[hd] += sum over (image, chunk) of part[..][0]; drel[hd*nrel+r] +=
-// sum of part[..][1+r]; images then chunks, in order.
-__global__ void attn_reduce_kernel(const float* __restrict__ part, int n, int nchunk, int h, int nrel,
+// sum of part[..][1+r].  One warp per output: lane l adds items l, l+32, ...
+// in order, then a fixed shuffle tree; deterministic.
+__global__ void attn_reduce_kernel(const float* __restrict__ part, int items, int h, int nrel,
                                    float* __restrict__ dtau, float* __restrict__ drel) {
   const int total = h * (1 + nrel);
-  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, l = threadIdx.x & 31;
+  const int nwarps = (gridDim.x * blockDim.x) >> 5;
+  for (int e = warp; e < total; e += nwarps) {
     const int hd = e / (1 + nrel), r = e - hd * (1 + nrel);
     float s = 0.0f;
-    for (int i = 0; i < n; i++)
-      for (int ch = 0; ch < nchunk; ch++) s += part[(((size_t)i * nchunk + ch) * h + hd) * (1 + nrel) + r];
-    if (r == 0) dtau[hd] += s;
-    else drel[(size_t)hd * nrel + r - 1] += s;
+    for (int it = l; it < items; it += 32) s += part[((size_t)it * h + hd) * (1 + nrel) + r];
+    s = warp_sum(s);
+    if (l == 0) {
+      if (r == 0) dtau[hd] += s;
+      else drel[(size_t)hd * nrel + r - 1] += s;
+    }
   }
 }
 
 // ---------------------------------------------------------------- host
 
-static size_t fwd_smem(int dh, int tqc, int tk) {
-  return sizeof(float) * ((size_t)tqc * (dh + 1) + 2 * (size_t)tk * (dh + 1) + (size_t)tqc * tk);
+constexpr size_t ATT_SMEM_CAP = 200 * 1024;
+
+static size_t fwd_smem(int dh, int tk) {
+  return sizeof(float) * (2 * (size_t)tk * (dh + 1) + (size_t)AT_WARPS * tk);
 }
-static size_t bwd_smem(int dh, int tqc, int tk, int nrel) {
-  return sizeof(float) *
-         (2 * (size_t)tk * (dh + 1) + 2 * (size_t)tqc * (dh + 1) + 2 * (size_t)tqc * tk + (size_t)nrel);
+static size_t rows_smem(int dh, int tk, int nrel) {
+  return sizeof(float) * (2 * (size_t)tk * (dh + 1) + (size_t)AT_WARPS * tk + (size_t)AT_WARPS * nrel);
 }
-constexpr size_t ATT_SMEM_CAP = 220 * 1024;
+static size_t cols_smem(int dh, int tq) {
+  return sizeof(float) * (2 * (size_t)tq * dh + 2 * (size_t)tq * AT_KC);
+}
 
 template <int DH>
 static int launch_fwd(rnn_ctx* ctx, AttnArgs a) {
-  int tqc = 64;
-  while (tqc > 1 && fwd_smem(DH, tqc, a.tk) > ATT_SMEM_CAP) tqc /= 2;
-  if (tqc > a.tq) tqc = a.tq;
-  const size_t smem = fwd_smem(DH, tqc, a.tk);
+  RNN_REQUIRE(a.tk <= 32 * AT_MAXK, "attention: %d keys unsupported (at most %d)", a.tk, 32 * AT_MAXK);
+  const size_t smem = fwd_smem(DH, a.tk);
   RNN_REQUIRE(smem <= ATT_SMEM_CAP, "attention: %d keys of head dim %d do not fit in shared memory", a.tk, DH);
-  a.tqc = tqc;
+  a.qc = AT_QC;
   RNN_CUDA(cudaFuncSetAttribute(attn_fwd_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  dim3 grid(a.h, a.n, (a.tq + tqc - 1) / tqc);
-  attn_fwd_kernel<DH><<<grid, ATT_THREADS, smem, ctx->stream>>>(a);
+  dim3 grid(a.h, a.n, (a.tq + a.qc - 1) / a.qc);
+  attn_fwd_kernel<DH><<<grid, AT_THREADS, smem, ctx->stream>>>(a);
   RNN_CHECK_LAUNCH();
   return RNN_OK;
 }
 
 template <int DH>
 static int launch_bwd(rnn_ctx* ctx, AttnArgs a, float* dtau, float* drel) {
-  int tqc = 64;
-  while (tqc > 1 && bwd_smem(DH, tqc, a.tk, a.nrel) > ATT_SMEM_CAP) tqc /= 2;
-  if (tqc > a.tq) tqc = a.tq;
-  const size_t smem = bwd_smem(DH, tqc, a.tk, a.nrel);
-  RNN_REQUIRE(smem <= ATT_SMEM_CAP, "attention backward: %d keys of head dim %d do not fit in shared memory",
-              a.tk, DH);
-  a.tqc = tqc;
-  a.nchunk = (a.tq + tqc - 1) / tqc;
+  RNN_REQUIRE(a.tk <= 32 * AT_MAXK, "attention backward: %d keys unsupported (at most %d)", a.tk, 32 * AT_MAXK);
+  const size_t rsm = rows_smem(DH, a.tk, a.nrel), csm = cols_smem(DH, a.tq);
+  RNN_REQUIRE(rsm <= ATT_SMEM_CAP && csm <= ATT_SMEM_CAP,
+              "attention backward: %d queries x %d keys of head dim %d do not fit in shared memory", a.tq, a.tk,
+              DH);
+  a.qc = AT_QC;
+  a.nchunk = (a.tq + a.qc - 1) / a.qc;
+  const size_t ds_floats = (size_t)a.n * a.h * a.tq * a.tk;
   const size_t part_floats = (size_t)a.n * a.nchunk * a.h * (1 + a.nrel);
-  RNN_TRY(ensure_ws(ctx, part_floats * sizeof(float)));
-  a.part = static_cast<float*>(ctx->ws);
+  const size_t ds_bytes = (ds_floats * sizeof(float) + 255) & ~(size_t)255;
+  RNN_TRY(ensure_ws(ctx, ds_bytes + part_floats * sizeof(float)));
+  a.ds = static_cast<float*>(ctx->ws);
+  a.part = reinterpret_cast<float*>(static_cast<char*>(ctx->ws) + ds_bytes);
+  RNN_RANGE(a.ds, ds_floats * sizeof(float));
   RNN_RANGE(a.part, part_floats * sizeof(float));
-  RNN_CUDA(cudaFuncSetAttribute(attn_bwd_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  for (int ch = 0; ch < a.nchunk; ch++) {  // chunks in stream order: dK/dV += never race
-    a.chunk = ch;
-    attn_bwd_kernel<DH><<<dim3(a.h, a.n, 1), ATT_THREADS, smem, ctx->stream>>>(a);
-    RNN_CHECK_LAUNCH();
-  }
+  RNN_CUDA(cudaFuncSetAttribute(attn_bwd_rows_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm));
+  RNN_CUDA(cudaFuncSetAttribute(attn_bwd_cols_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csm));
+  attn_bwd_rows_kernel<DH><<<dim3(a.h, a.n, a.nchunk), AT_THREADS, rsm, ctx->stream>>>(a);
+  RNN_CHECK_LAUNCH();
+  attn_bwd_cols_kernel<DH><<<dim3(a.h, a.n, (a.tk + AT_KC - 1) / AT_KC), AT_THREADS, csm, ctx->stream>>>(a);
+  RNN_CHECK_LAUNCH();
   const int total = a.h * (1 + a.nrel);
-  attn_reduce_kernel<<<(total + 255) / 256, 256, 0, ctx->stream>>>(a.part, a.n, a.nchunk, a.h, a.nrel, dtau, drel);
+  const int blocks = std::min((total + 7) / 8, ctx->num_sms * 16);
+  attn_reduce_kernel<<<blocks, 256, 0, ctx->stream>>>(a.part, a.n * a.nchunk, a.h, a.nrel, dtau, drel);
   RNN_CHECK_LAUNCH();
   return RNN_OK;
 }
