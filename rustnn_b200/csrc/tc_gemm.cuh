@@ -263,11 +263,21 @@ struct Cfg {
   static constexpr int B_BYTES = BN * BK * 4;
   static constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);  // hi + lo
   static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 4 ? 4 : (200 * 1024) / STAGE_BYTES;
-  static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
-                                   : (2 * BN <= 256) ? 256 : 512;
+  // Narrow tiles (BN <= 64) issue each 8-deep K step as two MMAs of width
+  // 2*BN over the stacked [B_hi; B_lo] image (the lo tile follows the hi
+  // tile in shared memory, so one descriptor covers both): columns [0, BN)
+  // collect A*B_hi = (hi+lo)*B_hi, columns [BN, 2BN) collect A*B_lo, and the
+  // epilogue adds the halves.  Two wide MMAs cost less than three narrow
+  // ones (a 128x64x8 tf32 MMA takes ~86 cycles, a 128x128x8 ~107, measured),
+  // and the fourth product lo*lo comes along for free.
+  static constexpr bool STACK = BN <= 64;
+  static constexpr int ACC_COLS = STACK ? 2 * BN : BN;  // columns per accumulator buffer
+  static constexpr int TMEM_COLS = (2 * ACC_COLS <= 32) ? 32 : (2 * ACC_COLS <= 64) ? 64
+                                   : (2 * ACC_COLS <= 128) ? 128 : (2 * ACC_COLS <= 256) ? 256 : 512;
   // 1024 bytes of alignment slack + barriers
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
   static constexpr uint32_t IDESC = idesc_tf32(BM, BN);
+  static constexpr uint32_t IDESC2 = idesc_tf32(BM, 2 * BN);  // stacked-B MMA (STACK)
   static constexpr int BCH = BN / 16;  // B chunks (4 K values) per producer thread
 };
 
@@ -465,7 +475,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       tc_fence_after();
-      const uint32_t d_tmem = tmem_base + buf * BN;
+      const uint32_t d_tmem = tmem_base + buf * C::ACC_COLS;
       for (int kb = kb0; kb < kb1; kb++, it++) {
         const int stage = it % C::STAGES;
         const uint32_t phase = (it / C::STAGES) & 1;
@@ -485,9 +495,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const uint64_t dah = sdesc_sw128(a_hi + koff), dal = sdesc_sw128(a_lo + koff);
             const uint64_t dbh = sdesc_sw128(b_hi + koff), dbl = sdesc_sw128(b_lo + koff);
             const uint32_t first = (kb == kb0 && j == 0) ? 0u : 1u;
-            mma_tf32(d_tmem, dal, dbh, C::IDESC, first);  // lo * hi
-            mma_tf32(d_tmem, dah, dbl, C::IDESC, 1u);     // hi * lo
-            mma_tf32(d_tmem, dah, dbh, C::IDESC, 1u);     // hi * hi
+            if constexpr (C::STACK) {
+              mma_tf32(d_tmem, dal, dbh, C::IDESC2, first);  // lo * [hi; lo]
+              mma_tf32(d_tmem, dah, dbh, C::IDESC2, 1u);     // hi * [hi; lo]
+              (void)dbl;
+            } else {
+              mma_tf32(d_tmem, dal, dbh, C::IDESC, first);  // lo * hi
+              mma_tf32(d_tmem, dah, dbl, C::IDESC, 1u);     // hi * lo
+              mma_tf32(d_tmem, dah, dbh, C::IDESC, 1u);     // hi * hi
+            }
           }
           mma_commit(&empty[stage]);
         }
@@ -523,11 +539,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], aphase, abort_flag, dev_error))) break;
       tc_fence_after();
       const int row = mt * BM + q * 32 + lane;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * C::ACC_COLS;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; c++) {
         float v[32];
         tmem_ld32(taddr + c * 32, v);
+        if constexpr (C::STACK) {
+          float w[32];
+          tmem_ld32(taddr + BN + c * 32, w);
+#pragma unroll
+          for (int e = 0; e < 32; e++) v[e] += w[e];
+        }
         prob.store(row, nt * BN + c * 32, split, v);
       }
       tc_fence_before();
