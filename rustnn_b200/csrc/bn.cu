@@ -41,8 +41,35 @@ static __device__ __forceinline__ void block_sum2(double a, double b, double* ou
   }
 }
 
+// The last CTA of a partial-sum launch to finish sums the [C][P][2]
+// partials in a fixed order (so the result is deterministic) and writes
+// sums[C][2]; it then returns the counter to zero for the next launch.
+static __device__ __forceinline__ void last_block_combine(const double* part, int C, int P,
+                                                          unsigned* counter, double* sums) {
+  __shared__ bool last;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(counter, 1u);
+    last = prev == gridDim.x * gridDim.y - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    double a = 0.0, b = 0.0;
+    for (int p = 0; p < P; p++) {
+      a += __ldcg(part + ((size_t)c * P + p) * 2);
+      b += __ldcg(part + ((size_t)c * P + p) * 2 + 1);
+    }
+    sums[c * 2] = a;
+    sums[c * 2 + 1] = b;
+  }
+  if (threadIdx.x == 0) *counter = 0u;
+}
+
 constexpr int BN_NT = 256;
 constexpr int BN_U = 4;  // float4 loads in flight per thread and stream
+constexpr int BN_FUSE_MAX_C = 4096;  // fused finalize keeps 2*C floats (<= 32 KB) per CTA in shared memory
 
 // grid (C, P): block (c, p) sums the planes of images [n*p/P, n*(p+1)/P) of
 // channel c.  Scalar form, for hw % 4 != 0 or unaligned tensors.
@@ -66,7 +93,8 @@ __global__ void __launch_bounds__(BN_NT) bn_fwd_partial_kernel(const float* __re
 // (so small planes still occupy every thread) and each thread keeps BN_U
 // independent loads in flight.
 __global__ void __launch_bounds__(BN_NT) bn_fwd_partial4_kernel(const float4* __restrict__ y, int n, int C,
-                                                              int hw4, int P, double* __restrict__ part) {
+                                                              int hw4, int P, double* __restrict__ part,
+                                                              unsigned* counter, double* __restrict__ sums) {
   const int c = blockIdx.x, p = blockIdx.y;
   const int i0 = (int)((long)n * p / P), i1 = (int)((long)n * (p + 1) / P);
   const unsigned tot = (unsigned)(i1 - i0) * (unsigned)hw4;
@@ -91,6 +119,7 @@ __global__ void __launch_bounds__(BN_NT) bn_fwd_partial4_kernel(const float4* __
     }
   }
   block_sum2<BN_NT>(s, s2, part + ((size_t)c * P + p) * 2);
+  last_block_combine(part, C, P, counter, sums);
 }
 
 // Backward partials: sum dy_eff * xhat and dy_eff (scalar form).
@@ -133,7 +162,8 @@ __global__ void __launch_bounds__(BN_NT) bn_bwd_partial4_kernel(const float4* __
                                                               int C, int hw4, int P,
                                                               const float* __restrict__ mean,
                                                               const float* __restrict__ invstd,
-                                                              double* __restrict__ part) {
+                                                              double* __restrict__ part, unsigned* counter,
+                                                              double* __restrict__ sums) {
   const int c = blockIdx.x, p = blockIdx.y;
   const int i0 = (int)((long)n * p / P), i1 = (int)((long)n * (p + 1) / P);
   const unsigned tot = (unsigned)(i1 - i0) * (unsigned)hw4;
@@ -165,6 +195,7 @@ __global__ void __launch_bounds__(BN_NT) bn_bwd_partial4_kernel(const float4* __
     }
   }
   block_sum2<BN_NT>(a, b, part + ((size_t)c * P + p) * 2);
+  last_block_combine(part, C, P, counter, sums);
 }
 
 // part [C][P][2] -> sums [C][2] in fixed order
@@ -312,6 +343,135 @@ __global__ void __launch_bounds__(256) bn_dx4_kernel(const float4* __restrict__ 
   }
 }
 
+// Fused finalize + apply (nn.rs:317-353): every CTA derives mean and invstd
+// of all channels from the f64 sums into shared memory (identical
+// arithmetic to bn_finalize_kernel); CTA 0 also stores them for the backward
+// and updates the running statistics.
+__global__ void __launch_bounds__(256) bn_apply4_fin_kernel(const float4* __restrict__ y, int C, unsigned hw4,
+                                                            unsigned total4, const float* __restrict__ gamma,
+                                                            const float* __restrict__ beta,
+                                                            const double* __restrict__ sums, double m, float mom,
+                                                            float eps, float* __restrict__ rmean,
+                                                            float* __restrict__ rvar, int relu,
+                                                            float* __restrict__ mean_out,
+                                                            float* __restrict__ invstd_out,
+                                                            float4* __restrict__ out) {
+  extern __shared__ float sh[];
+  float* smu = sh;
+  float* sis = sh + C;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    const double mu = sums[c * 2] / m;
+    const double va = sums[c * 2 + 1] / m - mu * mu;
+    const float muf = (float)mu;
+    const float var = (float)(va > 0.0 ? va : 0.0);
+    const float is = 1.0f / sqrtf(var + eps);
+    smu[c] = muf;
+    sis[c] = is;
+    if (blockIdx.x == 0) {
+      mean_out[c] = muf;
+      invstd_out[c] = is;
+      const float mf = (float)m;
+      if (rmean) rmean[c] = (1.0f - mom) * rmean[c] + mom * muf;
+      if (rvar) {
+        const float den = (mf - 1.0f) > 1.0f ? (mf - 1.0f) : 1.0f;
+        rvar[c] = (1.0f - mom) * rvar[c] + mom * (var * mf / den);
+      }
+    }
+  }
+  __syncthreads();
+  const unsigned stride = gridDim.x * blockDim.x;
+  for (unsigned j = blockIdx.x * blockDim.x + threadIdx.x; j < total4; j += stride * BN_U) {
+    float4 v[BN_U];
+#pragma unroll
+    for (int u = 0; u < BN_U; u++) {
+      const unsigned jj = j + u * stride;
+      if (jj < total4) v[u] = __ldg(y + jj);
+    }
+#pragma unroll
+    for (int u = 0; u < BN_U; u++) {
+      const unsigned jj = j + u * stride;
+      if (jj >= total4) break;
+      const int c = (int)((jj / hw4) % (unsigned)C);
+      const float mu = smu[c], is = sis[c], g = __ldg(gamma + c), bt = __ldg(beta + c);
+      float4 o;
+      o.x = g * ((v[u].x - mu) * is) + bt;
+      o.y = g * ((v[u].y - mu) * is) + bt;
+      o.z = g * ((v[u].z - mu) * is) + bt;
+      o.w = g * ((v[u].w - mu) * is) + bt;
+      if (relu) {
+        o.x = fmaxf(o.x, 0.0f);
+        o.y = fmaxf(o.y, 0.0f);
+        o.z = fmaxf(o.z, 0.0f);
+        o.w = fmaxf(o.w, 0.0f);
+      }
+      out[jj] = o;
+    }
+  }
+}
+
+// Fused backward finalize + dx (nn.rs:400-427): dgamma/dbeta sums from the
+// f64 sums in every CTA; CTA 0 adds them (scaled) into the gradients.
+template <bool RELU>
+__global__ void __launch_bounds__(256) bn_dx4_fin_kernel(const float4* __restrict__ dy,
+                                                         const float4* __restrict__ y,
+                                                         const float4* __restrict__ relu_out, int C, unsigned hw4,
+                                                         unsigned total4, float m, const float* __restrict__ gamma,
+                                                         const float* __restrict__ mean,
+                                                         const float* __restrict__ invstd,
+                                                         const double* __restrict__ sums,
+                                                         float* __restrict__ dgamma, float* __restrict__ dbeta,
+                                                         float pscale, float4* __restrict__ dx) {
+  extern __shared__ float sh[];
+  float* sdg = sh;
+  float* sdb = sh + C;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    const float dg = (float)sums[c * 2], db = (float)sums[c * 2 + 1];
+    sdg[c] = dg;
+    sdb[c] = db;
+    if (blockIdx.x == 0) {
+      if (dgamma) dgamma[c] += dg * pscale;
+      if (dbeta) dbeta[c] += db * pscale;
+    }
+  }
+  __syncthreads();
+  const unsigned stride = gridDim.x * blockDim.x;
+  for (unsigned j = blockIdx.x * blockDim.x + threadIdx.x; j < total4; j += stride * BN_U) {
+    float4 d[BN_U], v[BN_U], r[BN_U];
+#pragma unroll
+    for (int u = 0; u < BN_U; u++) {
+      const unsigned jj = j + u * stride;
+      if (jj < total4) {
+        d[u] = __ldg(dy + jj);
+        v[u] = __ldg(y + jj);
+        if (RELU) r[u] = __ldg(relu_out + jj);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < BN_U; u++) {
+      const unsigned jj = j + u * stride;
+      if (jj >= total4) break;
+      const int c = (int)((jj / hw4) % (unsigned)C);
+      const float mu = __ldg(mean + c), is = __ldg(invstd + c);
+      const float s = __ldg(gamma + c) * is / m, dbc = sdb[c], dgc = sdg[c];
+      float dd[4] = {d[u].x, d[u].y, d[u].z, d[u].w};
+      const float vv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      if (RELU) {
+        const float rr[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+          if (rr[e] <= 0.0f) dd[e] = 0.0f;
+      }
+      float o[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const float xh = (vv[e] - mu) * is;
+        o[e] = s * (m * dd[e] - dbc - xh * dgc);
+      }
+      dx[jj] = make_float4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 __global__ void bn_eval_kernel(const float* __restrict__ y, int C, int hw, size_t total,
                                const float* __restrict__ gamma, const float* __restrict__ beta,
                                const float* __restrict__ rmean, const float* __restrict__ rvar, float eps,
@@ -377,11 +537,13 @@ int bn_fwd_sums(rnn_ctx* ctx, const float* y, int n, int C, int hw, double* part
   RNN_RANGE(y, sizeof(float) * (size_t)n * C * hw);
   RNN_RANGE(part, sizeof(double) * (size_t)C * P * 2);
   RNN_RANGE(sums, sizeof(double) * (size_t)C * 2);
-  if (vec4_ok(hw, (size_t)n * C * hw, {y}))
+  if (vec4_ok(hw, (size_t)n * C * hw, {y})) {  // partials + last-CTA combine in one launch
     bn_fwd_partial4_kernel<<<dim3(C, P), BN_NT, 0, ctx->stream>>>(reinterpret_cast<const float4*>(y), n, C,
-                                                                 hw / 4, P, part);
-  else
-    bn_fwd_partial_kernel<<<dim3(C, P), BN_NT, 0, ctx->stream>>>(y, n, C, hw, P, part);
+                                                                 hw / 4, P, part, ctx->counters, sums);
+    RNN_CHECK_LAUNCH();
+    return RNN_OK;
+  }
+  bn_fwd_partial_kernel<<<dim3(C, P), BN_NT, 0, ctx->stream>>>(y, n, C, hw, P, part);
   RNN_CHECK_LAUNCH();
   bn_combine_kernel<<<(C + 127) / 128, 128, 0, ctx->stream>>>(part, C, P, sums);
   RNN_CHECK_LAUNCH();
@@ -400,10 +562,17 @@ int bn_fwd_finish(rnn_ctx* ctx, const float* y, int n, int C, int hw, double cou
   RNN_RANGE(beta, sizeof(float) * C);
   RNN_RANGE(y, sizeof(float) * (size_t)n * C * hw);
   RNN_RANGE(out, sizeof(float) * (size_t)n * C * hw);
+  const size_t total = (size_t)n * C * hw;
+  if (vec4_ok(hw, total, {y, out}) && C <= BN_FUSE_MAX_C) {  // finalize fused into the apply
+    bn_apply4_fin_kernel<<<ew4_grid(total / 4, ctx->num_sms), 256, 2 * C * sizeof(float), ctx->stream>>>(
+        reinterpret_cast<const float4*>(y), C, (unsigned)(hw / 4), (unsigned)(total / 4), gamma, beta, sums, count,
+        mom, eps, rmean, rvar, relu, mean, invstd, reinterpret_cast<float4*>(out));
+    RNN_CHECK_LAUNCH();
+    return RNN_OK;
+  }
   bn_finalize_kernel<<<(C + 127) / 128, 128, 0, ctx->stream>>>(sums, C, count, mom, eps, mean, invstd,
                                                                 rmean, rvar);
   RNN_CHECK_LAUNCH();
-  const size_t total = (size_t)n * C * hw;
   if (vec4_ok(hw, total, {y, out}))
     bn_apply4_kernel<<<ew4_grid(total / 4, ctx->num_sms), 256, 0, ctx->stream>>>(
         reinterpret_cast<const float4*>(y), C, (unsigned)(hw / 4), (unsigned)(total / 4), gamma, beta, mean,
@@ -434,10 +603,12 @@ int bn_bwd_sums(rnn_ctx* ctx, const float* dy, const float* y, const float* relu
                  *r4 = reinterpret_cast<const float4*>(relu_out);
     if (relu_out)
       bn_bwd_partial4_kernel<true><<<dim3(C, P), BN_NT, 0, ctx->stream>>>(d4, y4, r4, n, C, hw / 4, P, mean,
-                                                                         invstd, part);
+                                                                         invstd, part, ctx->counters, sums);
     else
       bn_bwd_partial4_kernel<false><<<dim3(C, P), BN_NT, 0, ctx->stream>>>(d4, y4, r4, n, C, hw / 4, P, mean,
-                                                                          invstd, part);
+                                                                          invstd, part, ctx->counters, sums);
+    RNN_CHECK_LAUNCH();
+    return RNN_OK;  // partials + last-CTA combine in one launch
   } else {
     bn_bwd_partial_kernel<<<dim3(C, P), BN_NT, 0, ctx->stream>>>(dy, y, relu_out, n, C, hw, P, mean, invstd,
                                                                  part);
@@ -458,10 +629,27 @@ int bn_bwd_finish(rnn_ctx* ctx, const float* dy, const float* y, const float* re
   if (dbeta) RNN_RANGE(dbeta, sizeof(float) * C);
   RNN_RANGE(gamma, sizeof(float) * C);
   RNN_RANGE(dx, sizeof(float) * (size_t)n * C * hw);
+  const size_t total = (size_t)n * C * hw;
+  if (vec4_ok(hw, total, {dy, y, relu_out, dx}) && C <= BN_FUSE_MAX_C) {  // finalize fused into dx
+    const float4 *d4 = reinterpret_cast<const float4*>(dy), *y4 = reinterpret_cast<const float4*>(y),
+                 *r4 = reinterpret_cast<const float4*>(relu_out);
+    const unsigned g = ew4_grid(total / 4, ctx->num_sms);
+    const size_t shm = 2 * C * sizeof(float);
+    if (relu_out)
+      bn_dx4_fin_kernel<true><<<g, 256, shm, ctx->stream>>>(d4, y4, r4, C, (unsigned)(hw / 4), (unsigned)(total / 4),
+                                                            (float)count, gamma, mean, invstd, sums, dgamma, dbeta,
+                                                            pscale, reinterpret_cast<float4*>(dx));
+    else
+      bn_dx4_fin_kernel<false><<<g, 256, shm, ctx->stream>>>(d4, y4, r4, C, (unsigned)(hw / 4),
+                                                             (unsigned)(total / 4), (float)count, gamma, mean,
+                                                             invstd, sums, dgamma, dbeta, pscale,
+                                                             reinterpret_cast<float4*>(dx));
+    RNN_CHECK_LAUNCH();
+    return RNN_OK;
+  }
   bn_bwd_finalize_kernel<<<(C + 127) / 128, 128, 0, ctx->stream>>>(sums, C, dgb, dgb + C, dgamma, dbeta,
                                                                     pscale);
   RNN_CHECK_LAUNCH();
-  const size_t total = (size_t)n * C * hw;
   if (vec4_ok(hw, total, {dy, y, relu_out, dx})) {
     const float4 *d4 = reinterpret_cast<const float4*>(dy), *y4 = reinterpret_cast<const float4*>(y),
                  *r4 = reinterpret_cast<const float4*>(relu_out);

@@ -174,6 +174,8 @@ extern "C" int rnn_ctx_create(rnn_ctx** out, int device) {
   ctx->stream = ctx->own;
   e = cudaMalloc(&ctx->dev_error, sizeof(int));
   if (e == cudaSuccess) e = cudaMemset(ctx->dev_error, 0, sizeof(int));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->counters, 16 * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemset(ctx->counters, 0, 16 * sizeof(unsigned));
   if (e != cudaSuccess) {
     cudaStreamDestroy(ctx->own);
     delete ctx;
@@ -192,6 +194,7 @@ extern "C" int rnn_ctx_destroy(rnn_ctx* ctx) {
   if (ctx->pack) cudaFree(ctx->pack);
   if (ctx->aux) cudaFree(ctx->aux);
   if (ctx->dev_error) cudaFree(ctx->dev_error);
+  if (ctx->counters) cudaFree(ctx->counters);
   if (ctx->own) cudaStreamDestroy(ctx->own);
   delete ctx;
   return RNN_OK;

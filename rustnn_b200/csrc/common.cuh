@@ -94,6 +94,9 @@ struct rnn_ctx {
   // GEMMs it issues use ws for their split-K partials
   void* aux = nullptr;
   size_t aux_bytes = 0;
+  // device counters for kernels whose last CTA finishes a reduction
+  // (zeroed at creation; each such kernel leaves its slot at zero again)
+  unsigned* counters = nullptr;
   // bumped whenever a workspace above is reallocated, so that a captured
   // CUDA graph holding the old pointers is recaptured instead of replayed
   unsigned long long mem_epoch = 0;

@@ -14,18 +14,18 @@
 // f32 TMEM accumulator (the lo*lo term, ~2^-22 relative, is dropped).  This
 // is the split-TF32 scheme of Ootomo & Yokota (2022).
 //
-// CTA layout (416 threads, one CTA per SM, persistent over output tiles):
-//   warps 0-7  producers in two groups of four that take alternate K blocks,
-//              so two blocks' global loads are in flight at once:
+// CTA layout (one CTA per SM, persistent over output tiles):
+//   warps 0..4G-1  producers in G groups of four (G = 3 when the ring has
+//              at least three stages, else 2) that take K blocks round-robin,
+//              so G blocks' global loads are in flight at once:
 //              global -> registers -> hi/lo split -> shared memory in the
 //              canonical K-major SWIZZLE_128B layout, STAGES-deep ring.  When
 //              the B operand is a weight tensor it is pre-packed once per call
 //              into that exact shared-memory image (hi and lo) and one thread
 //              streams it with cp.async.bulk instead (no register traffic)
-//   warp  8    TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 9-12 epilogue: tcgen05.ld from a double-buffered TMEM accumulator
-//              (2 x BN columns), so the epilogue of tile i overlaps the
-//              main loop of tile i+1
+//   warp 4G    TMEM allocator + MMA issuer (one elected lane issues)
+//   next four  epilogue: tcgen05.ld from a double-buffered TMEM accumulator,
+//              so the epilogue of tile i overlaps the main loop of tile i+1
 // Tiles are BM=128 rows (TMEM lanes) x BN columns, BK=32 f32 (128 bytes) of K
 // per pipeline stage.  Every wait is bounded: on timeout the CTA raises an
 // abort flag, all roles drain, TMEM is freed and an error word is set.
@@ -39,11 +39,7 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 32;  // f32 elements of K per stage = one 128-byte swizzle row
-constexpr int NUM_PRODUCER_WARPS = 8;  // two groups of four
-constexpr int GROUP_THREADS = 128;
-constexpr int MMA_WARP = 8;
-constexpr int FIRST_EPI_WARP = 9;
-constexpr int NUM_THREADS = 13 * 32;
+constexpr int GROUP_THREADS = 128;  // one producer group = four warps, one A row per thread
 constexpr unsigned long long WAIT_TIMEOUT_NS = 2000000000ull;  // 2 s
 
 // ------------------------------------------------------------------ PTX
@@ -278,6 +274,17 @@ struct Cfg {
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
   static constexpr uint32_t IDESC = idesc_tf32(BM, BN);
   static constexpr uint32_t IDESC2 = idesc_tf32(BM, 2 * BN);  // stacked-B MMA (STACK)
+  // Producer groups take K blocks round-robin (block it -> group it % GROUPS),
+  // so GROUPS blocks' global loads are in flight.  A group's next block is
+  // GROUPS ahead of its last one; its wait on the stage's empty barrier can
+  // only tell the awaited phase from the one before it, so a group must never
+  // run more than one ring lap ahead: GROUPS <= STAGES.
+  static constexpr int GROUPS = STAGES >= 3 ? 3 : 2;
+  static_assert(GROUPS <= STAGES, "producer groups may not outrun the stage ring");
+  static constexpr int PRODUCER_WARPS = 4 * GROUPS;
+  static constexpr int MMA_WARP = PRODUCER_WARPS;     // TMEM allocator + MMA issuer
+  static constexpr int FIRST_EPI_WARP = MMA_WARP + 1;  // four epilogue warps follow
+  static constexpr int THREADS = (PRODUCER_WARPS + 5) * 32;
   static constexpr int BCH = BN / 16;  // B chunks (4 K values) per producer thread
 };
 
@@ -355,7 +362,7 @@ struct ChunkProb : P {
 // ------------------------------------------------------------------ kernel
 
 template <int BN, class Prob>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
     tc3_gemm_kernel(const Prob prob, const Sched sched, int* dev_error) {
   using C = Cfg<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -389,7 +396,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == MMA_WARP) {
+  if (warp == C::MMA_WARP) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
@@ -400,9 +407,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const int tiles_mn = sched.m_tiles * sched.n_tiles;
 
-  if (warp < NUM_PRODUCER_WARPS) {
+  if (warp < C::PRODUCER_WARPS) {
     // ---------------------------------------------------------- producers
-    const int group = warp >> 2;                 // 0 or 1
+    const int group = warp >> 2;                 // 0 .. GROUPS-1
     const int gt = threadIdx.x & (GROUP_THREADS - 1);
     uint32_t it = 0;
     bool ok = true;
@@ -416,7 +423,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       typename Prob::TS ts;
       prob.tile_begin(ts, mt * BM, nt * BN, gt);
       for (int kb = kb0; kb < kb1; kb++, it++) {
-        if ((int)(it & 1) != group) continue;
+        if ((int)(it % C::GROUPS) != group) continue;
         const int stage = it % C::STAGES;
         const uint32_t phase = (it / C::STAGES) & 1;
         float va[32];
@@ -456,7 +463,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
     (void)lane;
-  } else if (warp == MMA_WARP) {
+  } else if (warp == C::MMA_WARP) {
     // ---------------------------------------------------------- MMA issuer
     // The whole warp walks the schedule, waits and builds the descriptors
     // (warp-uniform values); one elected lane issues the MMAs and commits.
@@ -560,7 +567,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == MMA_WARP) tmem_dealloc(tmem_base, C::TMEM_COLS);
+  if (warp == C::MMA_WARP) tmem_dealloc(tmem_base, C::TMEM_COLS);
 }
 
 // ------------------------------------------------------------------ packing

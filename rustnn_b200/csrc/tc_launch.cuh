@@ -102,7 +102,7 @@ int launch_native(rnn_ctx* ctx, const Prob& prob, const Sched& sched) {
   }
   if (sched.num_tiles <= 0) return RNN_OK;
   int grid = std::min(sched.num_tiles, ctx->num_sms);
-  tc3_gemm_kernel<BN, Prob><<<grid, NUM_THREADS, C::SMEM_BYTES, ctx->stream>>>(prob, sched, ctx->dev_error);
+  tc3_gemm_kernel<BN, Prob><<<grid, C::THREADS, C::SMEM_BYTES, ctx->stream>>>(prob, sched, ctx->dev_error);
   RNN_CHECK_LAUNCH();
   return RNN_OK;
 }
