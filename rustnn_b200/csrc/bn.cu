@@ -41,11 +41,65 @@ static __device__ __forceinline__ void block_sum2(double a, double b, double* ou
   }
 }
 
+static __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+static __device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+static __device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Cross-rank step of the last CTA (all its threads; `sums` holds this
+// rank's totals): publish them in slot seq&1 of the own mailbox, raise the
+// flag to seq, wait for every peer's flag (bounded: 5 s, then an error bit
+// and garbage instead of a hang), and sum every rank's slot in rank order.
+// Two slots suffice: a rank can only publish seq+2 after passing the wait
+// for seq+1, which needs this rank's flag, raised after it read seq.
+static __device__ void peer_exchange(const PeerSums& ps, double* sums, int C) {
+  __shared__ unsigned long long seq;
+  if (threadIdx.x == 0) seq = ++(*ps.seq);
+  __syncthreads();
+  const size_t slot_off = PEER_MAIL_HEADER + (size_t)(seq & 1) * ps.cmax * 2 * sizeof(double);
+  double* mine = reinterpret_cast<double*>(ps.mail[ps.rank] + slot_off);
+  for (int c = threadIdx.x; c < 2 * C; c += blockDim.x) mine[c] = sums[c];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    st_release_sys(reinterpret_cast<unsigned long long*>(ps.mail[ps.rank]), seq);
+  }
+  if ((int)threadIdx.x < ps.world && (int)threadIdx.x != ps.rank) {
+    const unsigned long long* flag = reinterpret_cast<const unsigned long long*>(ps.mail[threadIdx.x]);
+    const unsigned long long t0 = gtimer();
+    while (ld_acquire_sys(flag) < seq) {
+      if (gtimer() - t0 > 5000000000ull) {
+        if (ps.dev_error) atomicOr(ps.dev_error, DEV_ERR_PEER);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < 2 * C; c += blockDim.x) {
+    double t = 0.0;
+    for (int r = 0; r < ps.world; r++) {
+      const double* d = reinterpret_cast<const double*>(ps.mail[r] + slot_off);
+      t += r == ps.rank ? mine[c] : __ldcv(d + c);
+    }
+    sums[c] = t;
+  }
+}
+
 // The last CTA of a partial-sum launch to finish sums the [C][P][2]
 // partials in a fixed order (so the result is deterministic) and writes
-// sums[C][2]; it then returns the counter to zero for the next launch.
+// sums[C][2]; with peers it then runs the cross-rank exchange; it finally
+// returns the counter to zero for the next launch.
 static __device__ __forceinline__ void last_block_combine(const double* part, int C, int P,
-                                                          unsigned* counter, double* sums) {
+                                                          unsigned* counter, double* sums, PeerSums ps) {
   __shared__ bool last;
   if (threadIdx.x == 0) {
     __threadfence();
@@ -63,6 +117,10 @@ static __device__ __forceinline__ void last_block_combine(const double* part, in
     }
     sums[c * 2] = a;
     sums[c * 2 + 1] = b;
+  }
+  if (ps.world > 1) {
+    __syncthreads();
+    peer_exchange(ps, sums, C);
   }
   if (threadIdx.x == 0) *counter = 0u;
 }
@@ -94,7 +152,8 @@ __global__ void __launch_bounds__(BN_NT) bn_fwd_partial_kernel(const float* __re
 // independent loads in flight.
 __global__ void __launch_bounds__(BN_NT) bn_fwd_partial4_kernel(const float4* __restrict__ y, int n, int C,
                                                               int hw4, int P, double* __restrict__ part,
-                                                              unsigned* counter, double* __restrict__ sums) {
+                                                              unsigned* counter, double* __restrict__ sums,
+                                                              PeerSums ps) {
   const int c = blockIdx.x, p = blockIdx.y;
   const int i0 = (int)((long)n * p / P), i1 = (int)((long)n * (p + 1) / P);
   const unsigned tot = (unsigned)(i1 - i0) * (unsigned)hw4;
@@ -119,7 +178,7 @@ __global__ void __launch_bounds__(BN_NT) bn_fwd_partial4_kernel(const float4* __
     }
   }
   block_sum2<BN_NT>(s, s2, part + ((size_t)c * P + p) * 2);
-  last_block_combine(part, C, P, counter, sums);
+  last_block_combine(part, C, P, counter, sums, ps);
 }
 
 // Backward partials: sum dy_eff * xhat and dy_eff (scalar form).
@@ -163,7 +222,7 @@ __global__ void __launch_bounds__(BN_NT) bn_bwd_partial4_kernel(const float4* __
                                                               const float* __restrict__ mean,
                                                               const float* __restrict__ invstd,
                                                               double* __restrict__ part, unsigned* counter,
-                                                              double* __restrict__ sums) {
+                                                              double* __restrict__ sums, PeerSums ps) {
   const int c = blockIdx.x, p = blockIdx.y;
   const int i0 = (int)((long)n * p / P), i1 = (int)((long)n * (p + 1) / P);
   const unsigned tot = (unsigned)(i1 - i0) * (unsigned)hw4;
@@ -195,7 +254,7 @@ __global__ void __launch_bounds__(BN_NT) bn_bwd_partial4_kernel(const float4* __
     }
   }
   block_sum2<BN_NT>(a, b, part + ((size_t)c * P + p) * 2);
-  last_block_combine(part, C, P, counter, sums);
+  last_block_combine(part, C, P, counter, sums, ps);
 }
 
 // part [C][P][2] -> sums [C][2] in fixed order
@@ -528,8 +587,10 @@ static unsigned ew_grid(size_t total, int num_sms) {
   return (unsigned)std::max<size_t>(1, std::min(g, cap));
 }
 
-int bn_fwd_sums(rnn_ctx* ctx, const float* y, int n, int C, int hw, double* part, double* sums) {
+int bn_fwd_sums(rnn_ctx* ctx, const float* y, int n, int C, int hw, double* part, double* sums,
+                const PeerSums* ps, bool* reduced) {
   const int P = bn_parts(n, C, ctx->num_sms);
+  if (reduced) *reduced = false;
   // the partials and the per-channel sums must not overlap (the combine
   // kernel reads one while it writes the other)
   RNN_REQUIRE(part + (size_t)C * P * 2 <= sums || sums + (size_t)C * 2 <= part,
@@ -538,9 +599,11 @@ int bn_fwd_sums(rnn_ctx* ctx, const float* y, int n, int C, int hw, double* part
   RNN_RANGE(part, sizeof(double) * (size_t)C * P * 2);
   RNN_RANGE(sums, sizeof(double) * (size_t)C * 2);
   if (vec4_ok(hw, (size_t)n * C * hw, {y})) {  // partials + last-CTA combine in one launch
+    const PeerSums pv = (ps && ps->world > 1 && C <= ps->cmax) ? *ps : PeerSums{};
     bn_fwd_partial4_kernel<<<dim3(C, P), BN_NT, 0, ctx->stream>>>(reinterpret_cast<const float4*>(y), n, C,
-                                                                 hw / 4, P, part, ctx->counters, sums);
+                                                                 hw / 4, P, part, ctx->counters, sums, pv);
     RNN_CHECK_LAUNCH();
+    if (reduced) *reduced = pv.world > 1;
     return RNN_OK;
   }
   bn_fwd_partial_kernel<<<dim3(C, P), BN_NT, 0, ctx->stream>>>(y, n, C, hw, P, part);
@@ -585,8 +648,10 @@ int bn_fwd_finish(rnn_ctx* ctx, const float* y, int n, int C, int hw, double cou
 }
 
 int bn_bwd_sums(rnn_ctx* ctx, const float* dy, const float* y, const float* relu_out, int n, int C, int hw,
-                const float* mean, const float* invstd, double* part, double* sums) {
+                const float* mean, const float* invstd, double* part, double* sums, const PeerSums* ps,
+                bool* reduced) {
   const int P = bn_parts(n, C, ctx->num_sms);
+  if (reduced) *reduced = false;
   // the partials and the per-channel sums must not overlap (the combine
   // kernel reads one while it writes the other)
   RNN_REQUIRE(part + (size_t)C * P * 2 <= sums || sums + (size_t)C * 2 <= part,
@@ -601,14 +666,16 @@ int bn_bwd_sums(rnn_ctx* ctx, const float* dy, const float* y, const float* relu
   if (vec4_ok(hw, (size_t)n * C * hw, {dy, y, relu_out})) {
     const float4 *d4 = reinterpret_cast<const float4*>(dy), *y4 = reinterpret_cast<const float4*>(y),
                  *r4 = reinterpret_cast<const float4*>(relu_out);
+    const PeerSums pv = (ps && ps->world > 1 && C <= ps->cmax) ? *ps : PeerSums{};
     if (relu_out)
       bn_bwd_partial4_kernel<true><<<dim3(C, P), BN_NT, 0, ctx->stream>>>(d4, y4, r4, n, C, hw / 4, P, mean,
-                                                                         invstd, part, ctx->counters, sums);
+                                                                         invstd, part, ctx->counters, sums, pv);
     else
       bn_bwd_partial4_kernel<false><<<dim3(C, P), BN_NT, 0, ctx->stream>>>(d4, y4, r4, n, C, hw / 4, P, mean,
-                                                                          invstd, part, ctx->counters, sums);
+                                                                          invstd, part, ctx->counters, sums, pv);
     RNN_CHECK_LAUNCH();
-    return RNN_OK;  // partials + last-CTA combine in one launch
+    if (reduced) *reduced = pv.world > 1;
+    return RNN_OK;  // partials + last-CTA combine (+ cross-rank sum) in one launch
   } else {
     bn_bwd_partial_kernel<<<dim3(C, P), BN_NT, 0, ctx->stream>>>(dy, y, relu_out, n, C, hw, P, mean, invstd,
                                                                  part);

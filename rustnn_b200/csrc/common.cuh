@@ -70,6 +70,7 @@ int check_range(const void* p, size_t bytes, const char* what, const char* file,
 enum DeviceError : int {
   DEV_ERR_TIMEOUT = 1,  // a pipeline wait gave up
   DEV_ERR_LABEL = 2,    // softmax_ce saw a label >= nclass
+  DEV_ERR_PEER = 4,     // a peer GPU did not publish its SyncBN sums in time
 };
 
 }  // namespace rnn

@@ -84,6 +84,12 @@ struct rnn_resnet {
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1;
   bool sync_bn = false;
+  // SyncBN over peer memory (bn.cuh PeerSums); world 1 = NCCL path
+  rnn::PeerSums peer;
+  char* mail = nullptr;                 // this rank's mailbox
+  std::vector<char*> peer_mail;         // mapped peer mailboxes (IPC)
+  char** mail_dev = nullptr;            // device array of every rank's mailbox
+  unsigned long long* peer_seq = nullptr;
   // CUDA-graph replay of the training step (rnn_resnet_set_graph)
   bool use_graph = false;
   rnn::StepGraph graph;
@@ -207,8 +213,9 @@ static int bn_forward(rnn_resnet* net, BNL& bn, const float* y, int n, int hw, b
   float* rv = rm + bn.c;
   if (!train) return rnn_batchnorm_eval_dev(ctx, y, n, bn.c, hw, gamma, beta, rm, rv, 1e-5f, relu, out);
   BnScratch s = bn_scratch(net, n, bn.c);
-  RNN_TRY(bn_fwd_sums(ctx, y, n, bn.c, hw, s.part, s.sums));
-  RNN_TRY(allreduce_sums(net, s.sums, bn.c));
+  bool reduced = false;
+  RNN_TRY(bn_fwd_sums(ctx, y, n, bn.c, hw, s.part, s.sums, net->sync_bn ? &net->peer : nullptr, &reduced));
+  if (!reduced) RNN_TRY(allreduce_sums(net, s.sums, bn.c));
   const double count = (double)n * hw * (net->sync_bn ? net->world : 1);
   return bn_fwd_finish(ctx, y, n, bn.c, hw, count, s.sums, gamma, beta, rm, rv, 0.1f, 1e-5f, relu ? 1 : 0,
                        bn.mean, bn.invstd, out);
@@ -218,8 +225,10 @@ static int bn_backward(rnn_resnet* net, BNL& bn, const float* dy, const float* y
                        int hw, float* dx) {
   rnn_ctx* ctx = net->ctx;
   BnScratch s = bn_scratch(net, n, bn.c);
-  RNN_TRY(bn_bwd_sums(ctx, dy, y, relu_out, n, bn.c, hw, bn.mean, bn.invstd, s.part, s.sums));
-  RNN_TRY(allreduce_sums(net, s.sums, bn.c));
+  bool reduced = false;
+  RNN_TRY(bn_bwd_sums(ctx, dy, y, relu_out, n, bn.c, hw, bn.mean, bn.invstd, s.part, s.sums,
+                      net->sync_bn ? &net->peer : nullptr, &reduced));
+  if (!reduced) RNN_TRY(allreduce_sums(net, s.sums, bn.c));
   const bool sb = net->sync_bn && net->comm;
   const double count = (double)n * hw * (sb ? net->world : 1);
   const float pscale = sb ? 1.0f / (float)net->world : 1.0f;
@@ -318,6 +327,82 @@ static int resnet_backward(rnn_resnet* net, const float* dlogits) {
 static int resnet_step(rnn_resnet* net, float lr, float mom, float wd) {
   const float gscale = net->comm ? 1.0f / (float)net->world : 1.0f;
   return sgd_nesterov(net->ctx, net->v, net->g, net->m, net->decay, 0, net->nparams, lr, mom, wd, gscale);
+}
+
+// Unmaps the peers' mailboxes and frees this rank's (after the device is idle).
+static void peer_release(rnn_resnet* net) {
+  for (char* p : net->peer_mail)
+    if (p) cudaIpcCloseMemHandle(p);
+  net->peer_mail.clear();
+  if (net->mail) cudaFree(net->mail);
+  if (net->mail_dev) cudaFree(net->mail_dev);
+  if (net->peer_seq) cudaFree(net->peer_seq);
+  net->mail = nullptr;
+  net->mail_dev = nullptr;
+  net->peer_seq = nullptr;
+  net->peer = PeerSums{};
+}
+
+// Maps every rank's SyncBN mailbox into this process (CUDA IPC handles
+// exchanged with one NCCL all-gather).  Returns RNN_OK without enabling the
+// peer path when the GPUs cannot reach each other; SyncBN then uses NCCL.
+static int peer_setup(rnn_resnet* net) {
+  const int world = net->world, rank = net->rank;
+  const int cmax = 4 * net->width;  // widest BatchNorm of the network
+  RNN_CUDA(cudaMalloc(&net->mail, peer_mail_bytes(cmax)));
+  RNN_CUDA(cudaMemset(net->mail, 0, peer_mail_bytes(cmax)));
+  RNN_CUDA(cudaMalloc(&net->peer_seq, sizeof(unsigned long long)));
+  RNN_CUDA(cudaMemset(net->peer_seq, 0, sizeof(unsigned long long)));
+  cudaIpcMemHandle_t h;
+  RNN_CUDA(cudaIpcGetMemHandle(&h, net->mail));
+  const size_t hb = sizeof(cudaIpcMemHandle_t);
+  char* dh = nullptr;
+  RNN_CUDA(cudaMalloc(&dh, hb * world));
+  RNN_CUDA(cudaMemcpy(dh + hb * rank, &h, hb, cudaMemcpyHostToDevice));
+  ncclResult_t r = ncclAllGather(dh + hb * rank, dh, hb, ncclChar, net->comm, net->ctx->stream);
+  std::vector<cudaIpcMemHandle_t> all(world);
+  cudaError_t e = cudaStreamSynchronize(net->ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpy(all.data(), dh, hb * world, cudaMemcpyDeviceToHost);
+  cudaFree(dh);
+  if (r != ncclSuccess) return set_error(RNN_ERR_NCCL, "mailbox handle exchange: %s", ncclGetErrorString(r));
+  RNN_CUDA(e);
+  std::vector<char*> ptrs(world, nullptr);
+  ptrs[rank] = net->mail;
+  bool ok = true;
+  for (int q = 0; q < world && ok; q++) {
+    if (q == rank) continue;
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, all[q], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      ok = false;
+      break;
+    }
+    ptrs[q] = static_cast<char*>(p);
+    net->peer_mail.push_back(ptrs[q]);
+  }
+  // every rank must agree on the path: any failure anywhere -> NCCL for all
+  int flag = ok ? 1 : 0, *dflag = nullptr;
+  RNN_CUDA(cudaMalloc(&dflag, sizeof(int)));
+  RNN_CUDA(cudaMemcpy(dflag, &flag, sizeof(int), cudaMemcpyHostToDevice));
+  r = ncclAllReduce(dflag, dflag, 1, ncclInt, ncclMin, net->comm, net->ctx->stream);
+  e = cudaStreamSynchronize(net->ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpy(&flag, dflag, sizeof(int), cudaMemcpyDeviceToHost);
+  cudaFree(dflag);
+  if (r != ncclSuccess) return set_error(RNN_ERR_NCCL, "mailbox agreement: %s", ncclGetErrorString(r));
+  RNN_CUDA(e);
+  if (!flag) {
+    peer_release(net);
+    return RNN_OK;
+  }
+  RNN_CUDA(cudaMalloc(&net->mail_dev, world * sizeof(char*)));
+  RNN_CUDA(cudaMemcpy(net->mail_dev, ptrs.data(), world * sizeof(char*), cudaMemcpyHostToDevice));
+  net->peer.rank = rank;
+  net->peer.world = world;
+  net->peer.cmax = cmax;
+  net->peer.mail = net->mail_dev;
+  net->peer.seq = net->peer_seq;
+  net->peer.dev_error = net->ctx->dev_error;
+  return RNN_OK;
 }
 
 static int allreduce_grads(rnn_resnet* net) {
@@ -524,6 +609,7 @@ extern "C" int rnn_resnet_destroy(rnn_resnet* net) {
   // in any order): wait on the device, not on the context's stream
   cudaDeviceSynchronize();
   net->graph.destroy();  // before the NCCL communicator its graph may hold
+  peer_release(net);
   free_acts(net);
   cudaFree(net->v);
   cudaFree(net->g);
@@ -650,9 +736,18 @@ extern "C" int rnn_dp_unique_id(unsigned char* uid_out) {
   return RNN_OK;
 }
 
+// RNN_SYNCBN_NCCL=1 keeps SyncBN on NCCL all-reduces (for comparison).
+static bool peer_sync_disabled() {
+  const char* v = getenv("RNN_SYNCBN_NCCL");
+  return v && v[0] == '1';
+}
+
 extern "C" int rnn_resnet_dp_init(rnn_resnet* net, int rank, int world, const unsigned char* uid, int sync_bn) {
   RNN_REQUIRE(net && uid, "null argument");
   RNN_REQUIRE(world >= 1 && rank >= 0 && rank < world, "dp_init: bad rank/world");
+  cudaDeviceSynchronize();
+  net->graph.release();
+  peer_release(net);
   if (net->comm) {
     ncclCommDestroy(net->comm);
     net->comm = nullptr;
@@ -665,5 +760,6 @@ extern "C" int rnn_resnet_dp_init(rnn_resnet* net, int rank, int world, const un
   net->rank = rank;
   net->world = world;
   net->sync_bn = sync_bn != 0;
+  if (world > 1 && net->sync_bn && !peer_sync_disabled()) RNN_TRY(peer_setup(net));
   return RNN_OK;
 }
