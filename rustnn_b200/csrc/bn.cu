@@ -308,12 +308,13 @@ __global__ void bn_bwd_finalize_kernel(const double* __restrict__ sums, int C, f
 __global__ void bn_apply_kernel(const float* __restrict__ y, int C, int hw, size_t total,
                                 const float* __restrict__ gamma, const float* __restrict__ beta,
                                 const float* __restrict__ mean, const float* __restrict__ invstd, int relu,
-                                float* __restrict__ out) {
+                                const float* res, float* out) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
        i += (size_t)gridDim.x * blockDim.x) {
     const int c = (int)((i / hw) % C);
     const float xh = (y[i] - mean[c]) * invstd[c];
     float v = gamma[c] * xh + beta[c];
+    if (res) v += res[i];
     out[i] = relu ? fmaxf(v, 0.0f) : v;
   }
 }
@@ -325,7 +326,7 @@ __global__ void __launch_bounds__(256) bn_apply4_kernel(const float4* __restrict
                                                         const float* __restrict__ beta,
                                                         const float* __restrict__ mean,
                                                         const float* __restrict__ invstd, int relu,
-                                                        float4* __restrict__ out) {
+                                                        const float4* res, float4* out) {
   const unsigned stride = gridDim.x * blockDim.x;
   for (unsigned j = blockIdx.x * blockDim.x + threadIdx.x; j < total4; j += stride * BN_U) {
     float4 v[BN_U];
@@ -345,6 +346,10 @@ __global__ void __launch_bounds__(256) bn_apply4_kernel(const float4* __restrict
       o.y = g * ((v[u].y - mu) * is) + bt;
       o.z = g * ((v[u].z - mu) * is) + bt;
       o.w = g * ((v[u].w - mu) * is) + bt;
+      if (res) {
+        const float4 r = res[jj];
+        o.x += r.x; o.y += r.y; o.z += r.z; o.w += r.w;
+      }
       if (relu) {
         o.x = fmaxf(o.x, 0.0f);
         o.y = fmaxf(o.y, 0.0f);
@@ -414,7 +419,7 @@ __global__ void __launch_bounds__(256) bn_apply4_fin_kernel(const float4* __rest
                                                             float* __restrict__ rvar, int relu,
                                                             float* __restrict__ mean_out,
                                                             float* __restrict__ invstd_out,
-                                                            float4* __restrict__ out) {
+                                                            const float4* res, float4* out) {
   extern __shared__ float sh[];
   float* smu = sh;
   float* sis = sh + C;
@@ -457,6 +462,10 @@ __global__ void __launch_bounds__(256) bn_apply4_fin_kernel(const float4* __rest
       o.y = g * ((v[u].y - mu) * is) + bt;
       o.z = g * ((v[u].z - mu) * is) + bt;
       o.w = g * ((v[u].w - mu) * is) + bt;
+      if (res) {
+        const float4 r = res[jj];
+        o.x += r.x; o.y += r.y; o.z += r.z; o.w += r.w;
+      }
       if (relu) {
         o.x = fmaxf(o.x, 0.0f);
         o.y = fmaxf(o.y, 0.0f);
@@ -615,7 +624,7 @@ int bn_fwd_sums(rnn_ctx* ctx, const float* y, int n, int C, int hw, double* part
 
 int bn_fwd_finish(rnn_ctx* ctx, const float* y, int n, int C, int hw, double count, const double* sums,
                   const float* gamma, const float* beta, float* rmean, float* rvar, float mom, float eps,
-                  int relu, float* mean, float* invstd, float* out) {
+                  int relu, float* mean, float* invstd, float* out, const float* res) {
   RNN_RANGE(sums, sizeof(double) * (size_t)C * 2);
   RNN_RANGE(mean, sizeof(float) * C);
   RNN_RANGE(invstd, sizeof(float) * C);
@@ -625,24 +634,26 @@ int bn_fwd_finish(rnn_ctx* ctx, const float* y, int n, int C, int hw, double cou
   RNN_RANGE(beta, sizeof(float) * C);
   RNN_RANGE(y, sizeof(float) * (size_t)n * C * hw);
   RNN_RANGE(out, sizeof(float) * (size_t)n * C * hw);
+  if (res) RNN_RANGE(res, sizeof(float) * (size_t)n * C * hw);
   const size_t total = (size_t)n * C * hw;
-  if (vec4_ok(hw, total, {y, out}) && C <= BN_FUSE_MAX_C) {  // finalize fused into the apply
+  const float4* res4 = reinterpret_cast<const float4*>(res);
+  if (vec4_ok(hw, total, {y, out, res}) && C <= BN_FUSE_MAX_C) {  // finalize fused into the apply
     bn_apply4_fin_kernel<<<ew4_grid(total / 4, ctx->num_sms), 256, 2 * C * sizeof(float), ctx->stream>>>(
         reinterpret_cast<const float4*>(y), C, (unsigned)(hw / 4), (unsigned)(total / 4), gamma, beta, sums, count,
-        mom, eps, rmean, rvar, relu, mean, invstd, reinterpret_cast<float4*>(out));
+        mom, eps, rmean, rvar, relu, mean, invstd, res4, reinterpret_cast<float4*>(out));
     RNN_CHECK_LAUNCH();
     return RNN_OK;
   }
   bn_finalize_kernel<<<(C + 127) / 128, 128, 0, ctx->stream>>>(sums, C, count, mom, eps, mean, invstd,
                                                                 rmean, rvar);
   RNN_CHECK_LAUNCH();
-  if (vec4_ok(hw, total, {y, out}))
+  if (vec4_ok(hw, total, {y, out, res}))
     bn_apply4_kernel<<<ew4_grid(total / 4, ctx->num_sms), 256, 0, ctx->stream>>>(
         reinterpret_cast<const float4*>(y), C, (unsigned)(hw / 4), (unsigned)(total / 4), gamma, beta, mean,
-        invstd, relu, reinterpret_cast<float4*>(out));
+        invstd, relu, res4, reinterpret_cast<float4*>(out));
   else
     bn_apply_kernel<<<ew_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(y, C, hw, total, gamma, beta,
-                                                                            mean, invstd, relu, out);
+                                                                            mean, invstd, relu, res, out);
   RNN_CHECK_LAUNCH();
   return RNN_OK;
 }

@@ -32,9 +32,10 @@ inline size_t peer_mail_bytes(int cmax) { return PEER_MAIL_HEADER + 2 * (size_t)
 // *reduced is set when the kernel did that reduction (else the caller must)
 int bn_fwd_sums(rnn_ctx* ctx, const float* y, int n, int C, int hw, double* part, double* sums,
                 const PeerSums* ps = nullptr, bool* reduced = nullptr);
+// out = [relu](bn(y) [+ res]); res may alias out (the residual join of a block)
 int bn_fwd_finish(rnn_ctx* ctx, const float* y, int n, int C, int hw, double count, const double* sums,
                   const float* gamma, const float* beta, float* rmean, float* rvar, float mom, float eps,
-                  int relu, float* mean, float* invstd, float* out);
+                  int relu, float* mean, float* invstd, float* out, const float* res = nullptr);
 // sums[c] = (sum dy*xhat, sum dy)
 int bn_bwd_sums(rnn_ctx* ctx, const float* dy, const float* y, const float* relu_out, int n, int C, int hw,
                 const float* mean, const float* invstd, double* part, double* sums, const PeerSums* ps = nullptr,

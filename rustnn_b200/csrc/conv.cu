@@ -11,6 +11,7 @@
 // layout [cout][cin][kh][kw] of nn.rs:116.  dgrad handles stride 2 by
 // testing divisibility of (i + pad - kh) by the stride (the transposed
 // convolution of scatter_span, conv.rs:124-165).
+#include "ew.cuh"
 #include "tc_launch.cuh"
 
 namespace rnn {
@@ -340,6 +341,8 @@ struct FastConvDgrad {
   const float* dy;
   float* dx;
   const float* bpack;
+  const float* res;   // optional join: dx = dgrad + (mask <= 0 ? 0 : res)
+  const float* mask;
   ConvGeom g;
   int M, N;
   int CB;  // cout blocks of 32 per tap
@@ -389,7 +392,76 @@ struct FastConvDgrad {
     if (row >= M) return;
     const int hw = g.h * g.w;
     const int img = row / hw, rem = row - img * hw;
-    float* xp = dx + ((size_t)img * g.cin) * hw + rem;
+    const size_t o0 = ((size_t)img * g.cin) * hw + rem;
+    float* xp = dx + o0;
+    if (res) {
+#pragma unroll
+      for (int j = 0; j < 32; j++) {
+        const int ci = col0 + j;
+        if (ci < N) {
+          const size_t o = o0 + (size_t)ci * hw;
+          const float m = __ldg(mask + o), r = __ldg(res + o);
+          dx[o] = v[j] + (m <= 0.0f ? 0.0f : r);
+        }
+      }
+      return;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; j++) {
+      const int ci = col0 + j;
+      if (ci < N) {
+        float* q = xp + (size_t)ci * hw;
+        *q = acc ? *q + v[j] : v[j];
+      }
+    }
+  }
+};
+
+// dgrad of a 1x1 convolution with stride s > 1 and no padding (the
+// projection shortcut): only the input pixels (s*oy, s*ox) receive gradient,
+// so the GEMM runs over the n*oh*ow output pixels (rows), reads dY like the
+// 1x1 forward reads x, and scatters each row into dX; the other pixels are
+// zeroed by the caller (or keep their value when accumulating).
+template <int BN>
+struct FastDgrad1x1Strided {
+  static constexpr bool B_BULK = true;
+  const float* dy;
+  float* dx;
+  const float* bpack;
+  ConvGeom g;
+  int M, N;
+  int kblocks;  // cout / 32
+  int acc;
+  int splits;
+
+  struct TS {
+    const float* p;
+    bool ok;
+  };
+  __device__ __forceinline__ void tile_begin(TS& ts, int m0, int, int gt) const {
+    const int row = m0 + gt;
+    ts.ok = row < M;
+    const int ohw = g.oh * g.ow;
+    const int r = ts.ok ? row : 0;
+    const int img = r / ohw, rem = r - img * ohw;
+    ts.p = dy + (size_t)img * g.cout * ohw + rem;
+  }
+  static __device__ __forceinline__ void a_slot(int gt, int j, int& r, int& c) { r = gt; c = j; }
+  __device__ __forceinline__ void load_a(const TS& ts, int kb, int, float (&v)[32]) const {
+    const size_t ohw = (size_t)g.oh * g.ow;
+    const float* p = ts.p + (size_t)(kb * 32) * ohw;
+#pragma unroll
+    for (int j = 0; j < 32; j++) v[j] = ts.ok ? __ldg(p + (size_t)j * ohw) : 0.0f;
+  }
+  __device__ __forceinline__ const void* b_src(int nt, int kb) const {
+    return bpack + ((size_t)nt * kblocks + kb) * (2 * BN * BK);
+  }
+  __device__ __forceinline__ void store(int row, int col0, int, const float (&v)[32]) const {
+    if (row >= M) return;
+    const int ohw = g.oh * g.ow, hw = g.h * g.w;
+    const int img = row / ohw, rem = row - img * ohw;
+    const int oy = rem / g.ow, ox = rem - oy * g.ow;
+    float* xp = dx + ((size_t)img * g.cin) * hw + (size_t)(oy * g.stride) * g.w + ox * g.stride;
 #pragma unroll
     for (int j = 0; j < 32; j++) {
       const int ci = col0 + j;
@@ -415,7 +487,13 @@ struct PackDgradSrc {
 // consecutive pixels lies in one output row (ow % 4 == 0).  A producer
 // thread owns 4 consecutive pixels of 8 rows; it decodes the pixel block once
 // per K block and the 8 rows once per tile.  dY is read with 16-byte loads.
-template <int KS>
+//
+// VEC (stride 1, "same" padding, W % 4 == 0): the thread's 4 pixels of one
+// row are x[ci][iy][ox .. ox+3] shifted by kw - pad in {-1, 0, 1}; it reads
+// the aligned window with one 16-byte load and takes the pixel that the
+// shift brings in from the neighbouring lane (the next or previous 4 pixels
+// of the same K block), or from padding at an image-row edge.
+template <int KS, bool VEC = false>
 struct FastConvWgrad {
   static constexpr bool B_BULK = false;
   static constexpr int KK = KS * KS;
@@ -428,13 +506,15 @@ struct FastConvWgrad {
   int splits;
 
   struct TS {
-    int rowoff[8];  // ci*H*W + (kh-pad)*W + (kw-pad)
-    int dkh[8], dkw[8];
-    uint32_t rok;   // bit j: row j in range
+    int wof[8];     // ci*H*W + (kh-pad)*W: the row's window before the kw shift
+    uint64_t meta;  // byte j: bit 0 row j in range, bits 1-3 kh, bits 4-6 kw
     int n0;
   };
+  static __device__ __forceinline__ bool rok(const TS& ts, int j) { return (ts.meta >> (8 * j)) & 1u; }
+  __device__ __forceinline__ int dkh(const TS& ts, int j) const { return (int)((ts.meta >> (8 * j + 1)) & 7u) - g.pad; }
+  __device__ __forceinline__ int dkw(const TS& ts, int j) const { return (int)((ts.meta >> (8 * j + 4)) & 7u) - g.pad; }
   __device__ __forceinline__ void tile_begin(TS& ts, int m0, int n0, int gt) const {
-    ts.rok = 0;
+    ts.meta = 0;
     ts.n0 = n0;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
@@ -442,10 +522,8 @@ struct FastConvWgrad {
       const int r = row < M ? row : 0;
       const int ci = r / KK, kk = r - ci * KK;
       const int kh = kk / KS, kw = kk - kh * KS;
-      ts.dkh[j] = kh - g.pad;
-      ts.dkw[j] = kw - g.pad;
-      ts.rowoff[j] = ci * g.h * g.w + ts.dkh[j] * g.w + ts.dkw[j];
-      if (row < M) ts.rok |= 1u << j;
+      ts.wof[j] = ci * g.h * g.w + (kh - g.pad) * g.w;
+      ts.meta |= (uint64_t)((row < M ? 1u : 0u) | ((unsigned)kh << 1) | ((unsigned)kw << 4)) << (8 * j);
     }
   }
   static __device__ __forceinline__ void a_slot(int gt, int j, int& r, int& c) {
@@ -457,7 +535,40 @@ struct FastConvWgrad {
     r = idx >> 3;
     c = idx & 7;
   }
+  __device__ __forceinline__ void load_a_vec(const TS& ts, int kb, int gt, float (&v)[32]) const {
+    const int sub = gt & 7;  // pixel group within the K block (lanes 8q .. 8q+7 share the rows)
+    const int p0 = kb * BK + 4 * sub;
+    const bool pin = p0 < K;
+    const int ohw = g.oh * g.ow;
+    const int pp = pin ? p0 : 0;
+    const int img = pp / ohw, rem = pp - img * ohw;
+    const int oy = rem / g.ow, ox = rem - oy * g.ow;
+    const float* base = x + (size_t)img * g.cin * g.h * g.w + oy * g.w + ox;
+    const bool lpad = ox == 0, rpad = ox + 4 == g.w;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int iy = oy + dkh(ts, j);
+      const bool rv = pin && rok(ts, j) && iy >= 0 && iy < g.h;
+      const float* q = base + (rv ? ts.wof[j] : 0);  // x[ci][iy][ox]
+      float4 c = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (rv) c = __ldg(reinterpret_cast<const float4*>(q));
+      const float from_left = __shfl_up_sync(0xffffffffu, c.w, 1);
+      const float from_right = __shfl_down_sync(0xffffffffu, c.x, 1);
+      const int dkw = this->dkw(ts, j);
+      float l = 0.0f, r = 0.0f;
+      if (dkw < 0 && rv && !lpad) l = sub == 0 ? __ldg(q - 1) : from_left;
+      if (dkw > 0 && rv && !rpad) r = sub == 7 ? __ldg(q + 4) : from_right;
+      v[4 * j + 0] = dkw < 0 ? l : dkw > 0 ? c.y : c.x;
+      v[4 * j + 1] = dkw < 0 ? c.x : dkw > 0 ? c.z : c.y;
+      v[4 * j + 2] = dkw < 0 ? c.y : dkw > 0 ? c.w : c.z;
+      v[4 * j + 3] = dkw < 0 ? c.z : dkw > 0 ? r : c.w;
+    }
+  }
   __device__ __forceinline__ void load_a(const TS& ts, int kb, int gt, float (&v)[32]) const {
+    if constexpr (VEC) {
+      load_a_vec(ts, kb, gt, v);
+      return;
+    }
     const int p0 = kb * BK + 4 * (gt & 7);
     const int ohw = g.oh * g.ow;
     if (p0 >= K) {
@@ -471,12 +582,13 @@ struct FastConvWgrad {
     const float* base = x + (size_t)img * g.cin * g.h * g.w + ys * g.w + xs;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-      const int iy = ys + ts.dkh[j];
-      const bool rv = ((ts.rok >> j) & 1u) && iy >= 0 && iy < g.h;
-      const float* p = base + (rv ? ts.rowoff[j] : 0);
+      const int iy = ys + dkh(ts, j);
+      const int dx = dkw(ts, j);
+      const bool rv = rok(ts, j) && iy >= 0 && iy < g.h;
+      const float* p = base + (rv ? ts.wof[j] + dx : 0);
 #pragma unroll
       for (int i = 0; i < 4; i++) {
-        const int ix = xs + i * g.stride + ts.dkw[j];
+        const int ix = xs + i * g.stride + dx;
         const bool ok = rv && ix >= 0 && ix < g.w;
         v[4 * j + i] = ok ? __ldg(p + i * g.stride) : 0.0f;
       }
@@ -597,10 +709,12 @@ static int fast_fwd(rnn_ctx* ctx, const float* x, const float* wt, float* y, con
 }
 
 template <int KS, int BN>
-static int fast_dgrad(rnn_ctx* ctx, const float* dy, const float* wt, float* dx, const ConvGeom& g, bool acc) {
+static int fast_dgrad(rnn_ctx* ctx, const float* dy, const float* wt, float* dx, const ConvGeom& g, bool acc,
+                      const float* res = nullptr, const float* mask = nullptr) {
   constexpr int KK = KS * KS;
   FastConvDgrad<KS, BN> p;
   p.dy = dy; p.dx = dx; p.g = g; p.acc = acc ? 1 : 0; p.splits = 1;
+  p.res = res; p.mask = mask;
   p.M = g.n * g.h * g.w; p.N = g.cin;
   p.CB = g.cout / 32;
   p.kblocks = KK * p.CB;
@@ -610,6 +724,24 @@ static int fast_dgrad(rnn_ctx* ctx, const float* dy, const float* wt, float* dx,
   p.bpack = static_cast<const float*>(ctx->pack);
   RNN_RANGE(ctx->pack, bytes);
   PackDgradSrc src{wt, g.cout, g.cin, KK};
+  RNN_TRY(launch_pack<BN>(ctx, src, s.n_tiles, p.kblocks, static_cast<float*>(ctx->pack)));
+  return launch<BN>(ctx, p, s);
+}
+
+template <int BN>
+static int fast_dgrad_1x1_strided(rnn_ctx* ctx, const float* dy, const float* wt, float* dx, const ConvGeom& g,
+                                  bool acc) {
+  if (!acc) RNN_CUDA(cudaMemsetAsync(dx, 0, sizeof(float) * (size_t)g.n * g.cin * g.h * g.w, ctx->stream));
+  FastDgrad1x1Strided<BN> p;
+  p.dy = dy; p.dx = dx; p.g = g; p.acc = acc ? 1 : 0; p.splits = 1;
+  p.M = g.n * g.oh * g.ow; p.N = g.cin;
+  p.kblocks = g.cout / 32;
+  Sched s = make_sched(p.M, p.N, p.kblocks * BK, BN, 1);
+  const size_t bytes = (size_t)s.n_tiles * p.kblocks * 2 * BN * BK * sizeof(float);
+  RNN_TRY(ensure_pack(ctx, bytes));
+  p.bpack = static_cast<const float*>(ctx->pack);
+  RNN_RANGE(ctx->pack, bytes);
+  PackDgradSrc src{wt, g.cout, g.cin, 1};
   RNN_TRY(launch_pack<BN>(ctx, src, s.n_tiles, p.kblocks, static_cast<float*>(ctx->pack)));
   return launch<BN>(ctx, p, s);
 }
@@ -661,6 +793,15 @@ int conv_dgrad(rnn_ctx* ctx, const float* dy, int n, int cin, int h, int w, cons
     p.dy = dy; p.w = wt; p.dx = dx; p.g = g; p.M = M; p.N = N; p.K = K; p.acc = acc ? 1 : 0;
     p.splits = 1;
   };
+  if (cout % 32 == 0 && k == 1 && stride > 1 && pad == 0) {
+    // the GEMM covers the n*oh*ow pixels that receive gradient
+    switch (pick_bn(N, (n * g.oh * g.ow + BM - 1) / BM, ctx->num_sms)) {
+      case 32: return fast_dgrad_1x1_strided<32>(ctx, dy, wt, dx, g, acc);
+      case 64: return fast_dgrad_1x1_strided<64>(ctx, dy, wt, dx, g, acc);
+      case 128: return fast_dgrad_1x1_strided<128>(ctx, dy, wt, dx, g, acc);
+      default: return fast_dgrad_1x1_strided<256>(ctx, dy, wt, dx, g, acc);
+    }
+  }
   if (cout % 32 == 0) {
     switch (bn) {
       case 32: return k == 3 ? fast_dgrad<3, 32>(ctx, dy, wt, dx, g, acc) : fast_dgrad<1, 32>(ctx, dy, wt, dx, g, acc);
@@ -677,6 +818,30 @@ int conv_dgrad(rnn_ctx* ctx, const float* dy, int n, int cin, int h, int w, cons
   }
   ConvDgradProb<1> p; fill(p);
   return run_bn<ConvLauncher>(ctx, bn, p, 1);
+}
+
+int conv_dgrad_join(rnn_ctx* ctx, const float* dy, int n, int cin, int h, int w, const float* wt, int cout,
+                    int k, int stride, int pad, float* dx, const float* res, const float* mask) {
+  ConvGeom g;
+  RNN_TRY(check_geom(n, cin, h, w, cout, k, stride, pad, &g));
+  if (n == 0) return RNN_OK;
+  const ConvSpans sp = spans(g, k);
+  if (cout % 32 == 0 && k == 3) {
+    RNN_RANGE(dy, sp.y);
+    RNN_RANGE(wt, sp.w);
+    RNN_RANGE(dx, sp.x);
+    RNN_RANGE(res, sp.x);
+    RNN_RANGE(mask, sp.x);
+    const int M = n * h * w;
+    switch (pick_bn(cin, (M + BM - 1) / BM, ctx->num_sms)) {
+      case 32: return fast_dgrad<3, 32>(ctx, dy, wt, dx, g, false, res, mask);
+      case 64: return fast_dgrad<3, 64>(ctx, dy, wt, dx, g, false, res, mask);
+      case 128: return fast_dgrad<3, 128>(ctx, dy, wt, dx, g, false, res, mask);
+      default: return fast_dgrad<3, 256>(ctx, dy, wt, dx, g, false, res, mask);
+    }
+  }
+  RNN_TRY(conv_dgrad(ctx, dy, n, cin, h, w, wt, cout, k, stride, pad, dx, false));
+  return add_masked(ctx, dx, res, mask, sp.x / sizeof(float));
 }
 
 int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, int h, int w,
@@ -699,10 +864,16 @@ int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, in
     p.splits = 1;
     p.dy_vec = ((g.oh * g.ow) % 4 == 0) && ((reinterpret_cast<uintptr_t>(dy) & 15) == 0);
   };
-  if (g.ow % 4 == 0) {
+  if (g.ow % 4 == 0 && (reinterpret_cast<uintptr_t>(dy) & 15) == 0) {  // dY read as float4
     auto ffill = [&](auto& p) {
       p.x = x; p.dy = dy; p.dw = dw; p.ws = nullptr; p.g = g; p.M = M; p.N = N; p.K = K; p.splits = 1;
     };
+    // 16-byte window loads: stride 1, "same" padding, rows of whole float4s
+    const bool vec = stride == 1 && 2 * pad == k - 1 && w % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    if (k == 3 && vec) {
+      FastConvWgrad<3, true> p; ffill(p);
+      return run_bn<WgradLauncher>(ctx, bn, p, splits);
+    }
     if (k == 3) {
       FastConvWgrad<3> p; ffill(p);
       return run_bn<WgradLauncher>(ctx, bn, p, splits);

@@ -52,6 +52,26 @@ __global__ void add_kernel(float* __restrict__ a, const float* __restrict__ b, s
   }
 }
 
+// a += (y <= 0 ? 0 : b): the identity shortcut's gradient with the join's
+// relu_back_ folded in (nn.rs:433-450, relu_back_ then add_)
+__global__ void add_masked_kernel(float* __restrict__ a, const float* __restrict__ b,
+                                  const float* __restrict__ y, size_t n) {
+  const size_t n4 = n / 4;
+  float4* a4 = reinterpret_cast<float4*>(a);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+  const float4* y4 = reinterpret_cast<const float4*>(y);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+    float4 x = a4[i], d = __ldg(b4 + i), m = __ldg(y4 + i);
+    x.x += m.x <= 0.0f ? 0.0f : d.x;
+    x.y += m.y <= 0.0f ? 0.0f : d.y;
+    x.z += m.z <= 0.0f ? 0.0f : d.z;
+    x.w += m.w <= 0.0f ? 0.0f : d.w;
+    a4[i] = x;
+  }
+  for (size_t i = n4 * 4 + blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    a[i] += y[i] <= 0.0f ? 0.0f : b[i];
+}
+
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 int relu_back(rnn_ctx* ctx, float* d, const float* y, size_t n) {
@@ -70,6 +90,17 @@ int add(rnn_ctx* ctx, float* a, const float* b, size_t n, bool relu) {
   RNN_RANGE(a, n * sizeof(float));
   RNN_RANGE(b, n * sizeof(float));
   add_kernel<<<grid_for(n / 4 + 1, ctx->num_sms), 256, 0, ctx->stream>>>(a, b, n, relu ? 1 : 0);
+  RNN_CHECK_LAUNCH();
+  return RNN_OK;
+}
+
+int add_masked(rnn_ctx* ctx, float* a, const float* b, const float* y, size_t n) {
+  if (n == 0) return RNN_OK;
+  RNN_REQUIRE(al16(a) && al16(b) && al16(y), "add_masked: pointers must be 16-byte aligned");
+  RNN_RANGE(a, n * sizeof(float));
+  RNN_RANGE(b, n * sizeof(float));
+  RNN_RANGE(y, n * sizeof(float));
+  add_masked_kernel<<<grid_for(n / 4 + 1, ctx->num_sms), 256, 0, ctx->stream>>>(a, b, y, n);
   RNN_CHECK_LAUNCH();
   return RNN_OK;
 }

@@ -7,6 +7,8 @@ namespace rnn {
 
 int relu_back(rnn_ctx* ctx, float* d, const float* y, size_t n);
 int add(rnn_ctx* ctx, float* a, const float* b, size_t n, bool relu);
+// a += (y <= 0 ? 0 : b)
+int add_masked(rnn_ctx* ctx, float* a, const float* b, const float* y, size_t n);
 int gap_fwd(rnn_ctx* ctx, const float* x, int nc, int hw, float* y);
 int gap_bwd(rnn_ctx* ctx, const float* dy, int nc, int hw, float* dx);
 int fc_fwd(rnn_ctx* ctx, const float* x, int n, int fin, int fout, const float* w, const float* b, float* y);
@@ -26,6 +28,10 @@ int conv_dgrad(rnn_ctx* ctx, const float* dy, int n, int cin, int h, int w, cons
                int stride, int pad, float* dx, bool acc);
 int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, int h, int w, int cout, int k,
                int stride, int pad, float* dw, int force_splits);
+// dx = dgrad(dy) + (mask <= 0 ? 0 : res), elementwise over dx: the identity
+// shortcut's gradient joined in the dgrad epilogue where the fast path runs
+int conv_dgrad_join(rnn_ctx* ctx, const float* dy, int n, int cin, int h, int w, const float* wt, int cout,
+                    int k, int stride, int pad, float* dx, const float* res, const float* mask);
 }  // namespace tc
 
 }  // namespace rnn

@@ -204,21 +204,33 @@ static int allreduce_sums(rnn_resnet* net, double* sums, int C) {
   return RNN_OK;
 }
 
+// out = [relu](bn(y) [+ res]): with res the block's residual join
+// (model.rs:52-54, add_relu_) is fused into the normalisation pass.
 static int bn_forward(rnn_resnet* net, BNL& bn, const float* y, int n, int hw, bool train, bool relu,
-                      float* out) {
+                      float* out, const float* res = nullptr) {
   rnn_ctx* ctx = net->ctx;
   float* gamma = net->v + bn.g_off;
   float* beta = net->v + bn.b_off;
   float* rm = net->bnbuf + bn.rm_off;
   float* rv = rm + bn.c;
-  if (!train) return rnn_batchnorm_eval_dev(ctx, y, n, bn.c, hw, gamma, beta, rm, rv, 1e-5f, relu, out);
+  if (!train) {
+    if (!res) return rnn_batchnorm_eval_dev(ctx, y, n, bn.c, hw, gamma, beta, rm, rv, 1e-5f, relu, out);
+    const size_t len = (size_t)n * bn.c * hw;
+    if (res == out) {  // out already holds the other branch: out = relu(out + bn(y))
+      float* tmp = net->gbuf[0];
+      RNN_TRY(rnn_batchnorm_eval_dev(ctx, y, n, bn.c, hw, gamma, beta, rm, rv, 1e-5f, 0, tmp));
+      return add(ctx, out, tmp, len, relu);
+    }
+    RNN_TRY(rnn_batchnorm_eval_dev(ctx, y, n, bn.c, hw, gamma, beta, rm, rv, 1e-5f, 0, out));
+    return add(ctx, out, res, len, relu);
+  }
   BnScratch s = bn_scratch(net, n, bn.c);
   bool reduced = false;
   RNN_TRY(bn_fwd_sums(ctx, y, n, bn.c, hw, s.part, s.sums, net->sync_bn ? &net->peer : nullptr, &reduced));
   if (!reduced) RNN_TRY(allreduce_sums(net, s.sums, bn.c));
   const double count = (double)n * hw * (net->sync_bn ? net->world : 1);
   return bn_fwd_finish(ctx, y, n, bn.c, hw, count, s.sums, gamma, beta, rm, rv, 0.1f, 1e-5f, relu ? 1 : 0,
-                       bn.mean, bn.invstd, out);
+                       bn.mean, bn.invstd, out, res);
 }
 
 static int bn_backward(rnn_resnet* net, BNL& bn, const float* dy, const float* y, const float* relu_out, int n,
@@ -240,10 +252,14 @@ static int conv_forward(rnn_resnet* net, const ConvL& c, const float* x, int n, 
   return tc::conv_fwd(net->ctx, x, n, c.cin, h, w, net->v + c.w_off, c.cout, c.k, c.stride, c.pad, y, false);
 }
 
+// nn.rs:230-250: backward_w then dX.  With res, dX also receives the
+// identity shortcut's gradient masked by the join's ReLU (model.rs:59-70).
 static int conv_backward(rnn_resnet* net, const ConvL& c, const float* x, const float* dy, int n, int h, int w,
-                         float* dx, bool dx_acc) {
-  // nn.rs:230-250: backward_w then dX
+                         float* dx, bool dx_acc, const float* res = nullptr, const float* mask = nullptr) {
   RNN_TRY(tc::conv_wgrad(net->ctx, x, dy, n, c.cin, h, w, c.cout, c.k, c.stride, c.pad, net->g + c.w_off, 0));
+  if (dx && res)
+    return tc::conv_dgrad_join(net->ctx, dy, n, c.cin, h, w, net->v + c.w_off, c.cout, c.k, c.stride, c.pad, dx,
+                               res, mask);
   if (dx)
     RNN_TRY(tc::conv_dgrad(net->ctx, dy, n, c.cin, h, w, net->v + c.w_off, c.cout, c.k, c.stride, c.pad, dx,
                            dx_acc));
@@ -261,20 +277,18 @@ static int resnet_forward(rnn_resnet* net, const float* x, int n, int h, int w, 
     // model.rs:39-55
     const int oh = (ch + 2 - 3) / b.stride + 1, ow = (cw + 2 - 3) / b.stride + 1;
     const int ohw = oh * ow;
-    const size_t no = (size_t)n * b.cout * ohw;
     b.x_in = cur;
     b.n = n; b.h = ch; b.w = cw; b.oh = oh; b.ow = ow;
     RNN_TRY(conv_forward(net, b.c1, cur, n, ch, cw, b.y1));
     RNN_TRY(bn_forward(net, b.b1, b.y1, n, ohw, train, true, b.h1));
     RNN_TRY(conv_forward(net, b.c2, b.h1, n, oh, ow, b.y2));
-    RNN_TRY(bn_forward(net, b.b2, b.y2, n, ohw, train, false, b.out));
     if (b.down) {
+      // out = relu(bn2(y2) + bnd(yd)): bn2 first, then bnd joins it in place
+      RNN_TRY(bn_forward(net, b.b2, b.y2, n, ohw, train, false, b.out));
       RNN_TRY(conv_forward(net, b.cd, cur, n, ch, cw, b.yd));
-      float* s = net->gbuf[0];
-      RNN_TRY(bn_forward(net, b.bd, b.yd, n, ohw, train, false, s));
-      RNN_TRY(add(net->ctx, b.out, s, no, true));
+      RNN_TRY(bn_forward(net, b.bd, b.yd, n, ohw, train, true, b.out, b.out));
     } else {
-      RNN_TRY(add(net->ctx, b.out, cur, no, true));
+      RNN_TRY(bn_forward(net, b.b2, b.y2, n, ohw, train, true, b.out, cur));
     }
     cur = b.out;
     ch = oh;
@@ -300,19 +314,19 @@ static int resnet_backward(rnn_resnet* net, const float* dlogits) {
   for (int bi = (int)net->blocks.size() - 1; bi >= 0; bi--) {
     Block& b = net->blocks[bi];
     const int ohw = b.oh * b.ow;
-    const size_t no = (size_t)n * b.cout * ohw, ni = (size_t)n * b.cin * b.h * b.w;
     float *d = G[id], *t = G[it], *dmain = G[idm], *dx = G[idx];
     // model.rs:57-72
-    RNN_TRY(relu_back(ctx, d, b.out, no));
-    RNN_TRY(bn_backward(net, b.b2, d, b.y2, nullptr, n, ohw, t));
+    // relu_back_ of the join (model.rs:59) is applied on the fly: every
+    // consumer of d masks it with out > 0
+    RNN_TRY(bn_backward(net, b.b2, d, b.y2, b.out, n, ohw, t));
     RNN_TRY(conv_backward(net, b.c2, b.h1, t, n, b.oh, b.ow, dmain, false));
     RNN_TRY(bn_backward(net, b.b1, dmain, b.y1, b.h1, n, ohw, t));
-    RNN_TRY(conv_backward(net, b.c1, b.x_in, t, n, b.h, b.w, dx, false));
     if (b.down) {
-      RNN_TRY(bn_backward(net, b.bd, d, b.yd, nullptr, n, ohw, t));
+      RNN_TRY(conv_backward(net, b.c1, b.x_in, t, n, b.h, b.w, dx, false));
+      RNN_TRY(bn_backward(net, b.bd, d, b.yd, b.out, n, ohw, t));
       RNN_TRY(conv_backward(net, b.cd, b.x_in, t, n, b.h, b.w, dx, true));
     } else {
-      RNN_TRY(add(ctx, dx, d, ni, false));
+      RNN_TRY(conv_backward(net, b.c1, b.x_in, t, n, b.h, b.w, dx, false, d, b.out));
     }
     std::swap(id, idx);
   }

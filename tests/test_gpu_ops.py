@@ -110,7 +110,26 @@ CONVS = [  # (n, cin, h, cout, k, stride, pad)
     (24, 128, 16, 128, 3, 1, 1),
     (40, 64, 16, 64, 1, 1, 0),
     (9, 32, 16, 96, 3, 1, 1),
+    (2, 32, 64, 32, 3, 1, 1),    # rows wider than a 32-pixel K block: window edges inside a row
+    (3, 32, 12, 64, 3, 1, 1),    # 12-wide rows: K blocks straddle image rows, ragged last K block
+    (3, 64, 15, 64, 1, 2, 0),    # strided 1x1 dgrad over an odd input: last row/column hit
+    (2, 32, 16, 64, 1, 3, 0),    # stride 3: two of every three rows/columns get no gradient
 ]
+
+
+@pytest.mark.parametrize("n,cin,h,cout,k,stride,pad", [(4, 64, 16, 128, 1, 2, 0), (2, 32, 9, 64, 3, 2, 1),
+                                                       (4, 64, 8, 64, 3, 1, 1)])
+def test_conv_dgrad_accumulate(ops, n, cin, h, cout, k, stride, pad):
+    """dgrad with acc adds into dX (the projection shortcut's gradient joins the main path's)."""
+    rng = O.Rng(7 + cin + k)
+    w = (rng.rand_vec(cout * cin * k * k) * np.float32(np.sqrt(2.0 / (cin * k * k)))).astype(np.float32)
+    oh = (h + 2 * pad - k) // stride + 1
+    dy = rng.rand_vec(n * cout * oh * oh)
+    base = rng.rand_vec(n * cin * h * h)
+    dx_ref = base + O.conv2d_dgrad(dy, n, cin, h, h, w, cout, k, stride, pad)
+    dx = dev(base)
+    ops.conv2d_dgrad(dev(dy), dev(w), n, cin, h, h, cout, k, stride, pad, dx=dx, acc=True)
+    assert rel(host(dx), dx_ref) < TOL
 
 
 @pytest.mark.parametrize("n,cin,h,cout,k,stride,pad", CONVS)
