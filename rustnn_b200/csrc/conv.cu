@@ -11,7 +11,6 @@
 // layout [cout][cin][kh][kw] of nn.rs:116.  dgrad handles stride 2 by
 // testing divisibility of (i + pad - kh) by the stride (the transposed
 // convolution of scatter_span, conv.rs:124-165).
-#include "ew.cuh"
 #include "tc_launch.cuh"
 
 namespace rnn {
@@ -20,6 +19,25 @@ namespace tc {
 struct ConvGeom {
   int n, cin, h, w, cout, stride, pad, oh, ow;
 };
+
+// Epilogue store of 32 consecutive output channels of one pixel into a
+// channel-planar tensor: out[o0 + j*plane], j < nvalid, becomes v or, with
+// acc, out + v.  When accumulating, the loads of each group of 8 channels
+// are issued before its stores, so the warp waits on memory 4 times per call
+// rather than once per channel (the compiler may not hoist a load above a
+// store to the same array).
+__device__ __forceinline__ void store_planes32(float* out, size_t o0, size_t plane, int nvalid,
+                                               const float (&v)[32], int acc) {
+#pragma unroll
+  for (int g = 0; g < 32; g += 8) {
+    float add[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) add[e] = (acc && g + e < nvalid) ? out[o0 + (size_t)(g + e) * plane] : 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+      if (g + e < nvalid) out[o0 + (size_t)(g + e) * plane] = acc ? add[e] + v[g + e] : v[g + e];
+  }
+}
 
 // ---------------------------------------------------------------- forward
 
@@ -312,15 +330,7 @@ struct FastConvFwd {
     if (row >= M) return;
     const int ohw = g.oh * g.ow;
     const int img = row / ohw, rem = row - img * ohw;
-    float* yp = y + ((size_t)img * g.cout) * ohw + rem;
-#pragma unroll
-    for (int j = 0; j < 32; j++) {
-      const int co = col0 + j;
-      if (co < N) {
-        float* q = yp + (size_t)co * ohw;
-        *q = acc ? *q + v[j] : v[j];
-      }
-    }
+    store_planes32(y, ((size_t)img * g.cout + col0) * ohw + rem, ohw, N - col0, v, acc);
   }
 };
 
@@ -341,8 +351,6 @@ struct FastConvDgrad {
   const float* dy;
   float* dx;
   const float* bpack;
-  const float* res;   // optional join: dx = dgrad + (mask <= 0 ? 0 : res)
-  const float* mask;
   ConvGeom g;
   int M, N;
   int CB;  // cout blocks of 32 per tap
@@ -392,28 +400,7 @@ struct FastConvDgrad {
     if (row >= M) return;
     const int hw = g.h * g.w;
     const int img = row / hw, rem = row - img * hw;
-    const size_t o0 = ((size_t)img * g.cin) * hw + rem;
-    float* xp = dx + o0;
-    if (res) {
-#pragma unroll
-      for (int j = 0; j < 32; j++) {
-        const int ci = col0 + j;
-        if (ci < N) {
-          const size_t o = o0 + (size_t)ci * hw;
-          const float m = __ldg(mask + o), r = __ldg(res + o);
-          dx[o] = v[j] + (m <= 0.0f ? 0.0f : r);
-        }
-      }
-      return;
-    }
-#pragma unroll
-    for (int j = 0; j < 32; j++) {
-      const int ci = col0 + j;
-      if (ci < N) {
-        float* q = xp + (size_t)ci * hw;
-        *q = acc ? *q + v[j] : v[j];
-      }
-    }
+    store_planes32(dx, ((size_t)img * g.cin + col0) * hw + rem, hw, N - col0, v, acc);
   }
 };
 
@@ -461,15 +448,96 @@ struct FastDgrad1x1Strided {
     const int ohw = g.oh * g.ow, hw = g.h * g.w;
     const int img = row / ohw, rem = row - img * ohw;
     const int oy = rem / g.ow, ox = rem - oy * g.ow;
-    float* xp = dx + ((size_t)img * g.cin) * hw + (size_t)(oy * g.stride) * g.w + ox * g.stride;
-#pragma unroll
-    for (int j = 0; j < 32; j++) {
-      const int ci = col0 + j;
-      if (ci < N) {
-        float* q = xp + (size_t)ci * hw;
-        *q = acc ? *q + v[j] : v[j];
-      }
+    store_planes32(dx, ((size_t)img * g.cin + col0) * hw + (size_t)(oy * g.stride) * g.w + ox * g.stride, hw,
+                   N - col0, v, acc);
+  }
+};
+
+// 3x3, stride 1, pad 1 convolution over 32-pixel-wide images whose height
+// is a multiple of 4 (the 32x32 stage of the CIFAR networks), as forward
+// (src = x, out = y) or as dgrad (src = dY, out = dX, taps flipped in the
+// packed weights).  A row tile is 4 whole image rows; K is ordered
+// (32-channel block cb, tap, channel), and for each cb the producers stage
+// the tile's halo -- 32 channels x 6 rows x 40 columns (columns -4 .. 35,
+// so every 16-byte chunk is either inside the row or all padding) -- in
+// shared memory with cp.async, then build all nine tap-shifted A tiles from
+// it: one global read of the input per channel block instead of nine.
+template <int BN>
+struct HaloConv3x3 {
+  static constexpr bool B_BULK = true;
+  static constexpr int TAPS = 9;
+  static constexpr int W = 32;
+  static constexpr int TR = BM / W;      // image rows per tile
+  static constexpr int HR = TR + 2;      // halo rows
+  static constexpr int HX = W + 8;       // halo columns (-4 .. W+3)
+  static constexpr int HCH = HX / 4;     // 16-byte chunks per halo row
+  static constexpr int HALO_FLOATS = 32 * HR * HX;
+  static constexpr int HALO_BYTES = 2 * HALO_FLOATS * 4;
+  const float* src;  // [n][CS][H][32]
+  float* out;        // [n][N][H][32]
+  const float* bpack;
+  int CS, H;
+  int M, N;
+  int kblocks;
+  int acc;
+  int splits;
+
+  struct TS {
+    int unused;
+  };
+  __device__ __forceinline__ void tile_begin(TS&, int, int, int) const {}
+  static __device__ __forceinline__ void a_slot(int gt, int j, int& r, int& c) { r = gt; c = j; }
+  __device__ __forceinline__ void halo_issue(uint32_t halo, int buf, int mt, int cb, int ptid, int npt) const {
+    const int hw = H * W;
+    const int m0 = mt * BM;
+    const int img = m0 / hw, oy0 = (m0 - img * hw) / W;
+    const float* base = src + ((size_t)img * CS + cb * 32) * hw;
+    const uint32_t dst0 = halo + (uint32_t)(buf * HALO_FLOATS * 4);
+    for (int q = ptid; q < 32 * HR * HCH; q += npt) {
+      const int c = q / (HR * HCH), rem = q - c * (HR * HCH);
+      const int r = rem / HCH, xc = rem - r * HCH;
+      const int iy = oy0 - 1 + r, ix = xc * 4 - 4;
+      const bool in = iy >= 0 && iy < H && ix >= 0 && ix < W;
+      const float* g = in ? base + ((size_t)c * H + iy) * W + ix : src;
+      cp_async16(dst0 + (uint32_t)(((c * HR + r) * HX + xc * 4) * 4), g, in ? 16u : 0u);
     }
+  }
+  __device__ __forceinline__ void load_a_halo(uint32_t halo, int buf, const TS&, int tap, int gt,
+                                              float (&v)[32]) const {
+    const int kh = tap / 3, kw = tap - kh * 3;
+    const int oyl = gt / W, ox = gt - oyl * W;
+    const uint32_t a = halo + (uint32_t)((buf * HALO_FLOATS + (oyl + kh) * HX + ox + kw + 3) * 4);
+#pragma unroll
+    for (int j = 0; j < 32; j++) v[j] = ld_shared_f32(a + (uint32_t)(j * HR * HX * 4));
+  }
+  __device__ __forceinline__ const void* b_src(int nt, int kb) const {
+    return bpack + ((size_t)nt * kblocks + kb) * (2 * BN * BK);
+  }
+  __device__ __forceinline__ void store(int row, int col0, int, const float (&v)[32]) const {
+    if (row >= M) return;
+    const int hw = H * W;
+    const int img = row / hw, rem = row - img * hw;
+    store_planes32(out, ((size_t)img * N + col0) * hw + rem, hw, N - col0, v, acc);
+  }
+};
+
+// K = (32-channel block, tap, channel) for the halo kernels.
+// forward: B(co, k) = W[co][cb*32 + c][tap]
+struct PackHaloFwdSrc {
+  const float* w;
+  int cout, cin;
+  __device__ __forceinline__ float operator()(int co, int k) const {
+    const int cb = k / 288, r = k - cb * 288, tap = r >> 5, ci = cb * 32 + (r & 31);
+    return (co < cout && ci < cin) ? __ldg(w + ((size_t)co * cin + ci) * 9 + tap) : 0.0f;
+  }
+};
+// dgrad: B(ci, k) = W[cb*32 + c][ci][8 - tap] (the flipped kernel)
+struct PackHaloDgradSrc {
+  const float* w;
+  int cout, cin;
+  __device__ __forceinline__ float operator()(int ci, int k) const {
+    const int cb = k / 288, r = k - cb * 288, tap = r >> 5, co = cb * 32 + (r & 31);
+    return (ci < cin && co < cout) ? __ldg(w + ((size_t)co * cin + ci) * 9 + (8 - tap)) : 0.0f;
   }
 };
 
@@ -487,13 +555,7 @@ struct PackDgradSrc {
 // consecutive pixels lies in one output row (ow % 4 == 0).  A producer
 // thread owns 4 consecutive pixels of 8 rows; it decodes the pixel block once
 // per K block and the 8 rows once per tile.  dY is read with 16-byte loads.
-//
-// VEC (stride 1, "same" padding, W % 4 == 0): the thread's 4 pixels of one
-// row are x[ci][iy][ox .. ox+3] shifted by kw - pad in {-1, 0, 1}; it reads
-// the aligned window with one 16-byte load and takes the pixel that the
-// shift brings in from the neighbouring lane (the next or previous 4 pixels
-// of the same K block), or from padding at an image-row edge.
-template <int KS, bool VEC = false>
+template <int KS>
 struct FastConvWgrad {
   static constexpr bool B_BULK = false;
   static constexpr int KK = KS * KS;
@@ -506,15 +568,13 @@ struct FastConvWgrad {
   int splits;
 
   struct TS {
-    int wof[8];     // ci*H*W + (kh-pad)*W: the row's window before the kw shift
-    uint64_t meta;  // byte j: bit 0 row j in range, bits 1-3 kh, bits 4-6 kw
+    int rowoff[8];  // ci*H*W + (kh-pad)*W + (kw-pad)
+    int dkh[8], dkw[8];
+    uint32_t rok;   // bit j: row j in range
     int n0;
   };
-  static __device__ __forceinline__ bool rok(const TS& ts, int j) { return (ts.meta >> (8 * j)) & 1u; }
-  __device__ __forceinline__ int dkh(const TS& ts, int j) const { return (int)((ts.meta >> (8 * j + 1)) & 7u) - g.pad; }
-  __device__ __forceinline__ int dkw(const TS& ts, int j) const { return (int)((ts.meta >> (8 * j + 4)) & 7u) - g.pad; }
   __device__ __forceinline__ void tile_begin(TS& ts, int m0, int n0, int gt) const {
-    ts.meta = 0;
+    ts.rok = 0;
     ts.n0 = n0;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
@@ -522,8 +582,10 @@ struct FastConvWgrad {
       const int r = row < M ? row : 0;
       const int ci = r / KK, kk = r - ci * KK;
       const int kh = kk / KS, kw = kk - kh * KS;
-      ts.wof[j] = ci * g.h * g.w + (kh - g.pad) * g.w;
-      ts.meta |= (uint64_t)((row < M ? 1u : 0u) | ((unsigned)kh << 1) | ((unsigned)kw << 4)) << (8 * j);
+      ts.dkh[j] = kh - g.pad;
+      ts.dkw[j] = kw - g.pad;
+      ts.rowoff[j] = ci * g.h * g.w + ts.dkh[j] * g.w + ts.dkw[j];
+      if (row < M) ts.rok |= 1u << j;
     }
   }
   static __device__ __forceinline__ void a_slot(int gt, int j, int& r, int& c) {
@@ -535,40 +597,7 @@ struct FastConvWgrad {
     r = idx >> 3;
     c = idx & 7;
   }
-  __device__ __forceinline__ void load_a_vec(const TS& ts, int kb, int gt, float (&v)[32]) const {
-    const int sub = gt & 7;  // pixel group within the K block (lanes 8q .. 8q+7 share the rows)
-    const int p0 = kb * BK + 4 * sub;
-    const bool pin = p0 < K;
-    const int ohw = g.oh * g.ow;
-    const int pp = pin ? p0 : 0;
-    const int img = pp / ohw, rem = pp - img * ohw;
-    const int oy = rem / g.ow, ox = rem - oy * g.ow;
-    const float* base = x + (size_t)img * g.cin * g.h * g.w + oy * g.w + ox;
-    const bool lpad = ox == 0, rpad = ox + 4 == g.w;
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-      const int iy = oy + dkh(ts, j);
-      const bool rv = pin && rok(ts, j) && iy >= 0 && iy < g.h;
-      const float* q = base + (rv ? ts.wof[j] : 0);  // x[ci][iy][ox]
-      float4 c = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      if (rv) c = __ldg(reinterpret_cast<const float4*>(q));
-      const float from_left = __shfl_up_sync(0xffffffffu, c.w, 1);
-      const float from_right = __shfl_down_sync(0xffffffffu, c.x, 1);
-      const int dkw = this->dkw(ts, j);
-      float l = 0.0f, r = 0.0f;
-      if (dkw < 0 && rv && !lpad) l = sub == 0 ? __ldg(q - 1) : from_left;
-      if (dkw > 0 && rv && !rpad) r = sub == 7 ? __ldg(q + 4) : from_right;
-      v[4 * j + 0] = dkw < 0 ? l : dkw > 0 ? c.y : c.x;
-      v[4 * j + 1] = dkw < 0 ? c.x : dkw > 0 ? c.z : c.y;
-      v[4 * j + 2] = dkw < 0 ? c.y : dkw > 0 ? c.w : c.z;
-      v[4 * j + 3] = dkw < 0 ? c.z : dkw > 0 ? r : c.w;
-    }
-  }
   __device__ __forceinline__ void load_a(const TS& ts, int kb, int gt, float (&v)[32]) const {
-    if constexpr (VEC) {
-      load_a_vec(ts, kb, gt, v);
-      return;
-    }
     const int p0 = kb * BK + 4 * (gt & 7);
     const int ohw = g.oh * g.ow;
     if (p0 >= K) {
@@ -582,13 +611,12 @@ struct FastConvWgrad {
     const float* base = x + (size_t)img * g.cin * g.h * g.w + ys * g.w + xs;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-      const int iy = ys + dkh(ts, j);
-      const int dx = dkw(ts, j);
-      const bool rv = rok(ts, j) && iy >= 0 && iy < g.h;
-      const float* p = base + (rv ? ts.wof[j] + dx : 0);
+      const int iy = ys + ts.dkh[j];
+      const bool rv = ((ts.rok >> j) & 1u) && iy >= 0 && iy < g.h;
+      const float* p = base + (rv ? ts.rowoff[j] : 0);
 #pragma unroll
       for (int i = 0; i < 4; i++) {
-        const int ix = xs + i * g.stride + dx;
+        const int ix = xs + i * g.stride + ts.dkw[j];
         const bool ok = rv && ix >= 0 && ix < g.w;
         v[4 * j + i] = ok ? __ldg(p + i * g.stride) : 0.0f;
       }
@@ -709,12 +737,10 @@ static int fast_fwd(rnn_ctx* ctx, const float* x, const float* wt, float* y, con
 }
 
 template <int KS, int BN>
-static int fast_dgrad(rnn_ctx* ctx, const float* dy, const float* wt, float* dx, const ConvGeom& g, bool acc,
-                      const float* res = nullptr, const float* mask = nullptr) {
+static int fast_dgrad(rnn_ctx* ctx, const float* dy, const float* wt, float* dx, const ConvGeom& g, bool acc) {
   constexpr int KK = KS * KS;
   FastConvDgrad<KS, BN> p;
   p.dy = dy; p.dx = dx; p.g = g; p.acc = acc ? 1 : 0; p.splits = 1;
-  p.res = res; p.mask = mask;
   p.M = g.n * g.h * g.w; p.N = g.cin;
   p.CB = g.cout / 32;
   p.kblocks = KK * p.CB;
@@ -726,6 +752,56 @@ static int fast_dgrad(rnn_ctx* ctx, const float* dy, const float* wt, float* dx,
   PackDgradSrc src{wt, g.cout, g.cin, KK};
   RNN_TRY(launch_pack<BN>(ctx, src, s.n_tiles, p.kblocks, static_cast<float*>(ctx->pack)));
   return launch<BN>(ctx, p, s);
+}
+
+// True when the halo kernels cover a 3x3/s1/p1 convolution whose gathered
+// operand has cs channels over h x w pixels.
+static bool halo_ok(int cs, int h, int w, int k, int stride, int pad, const void* src) {
+  return k == 3 && stride == 1 && pad == 1 && w == 32 && h % 4 == 0 && cs % 32 == 0 &&
+         (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+}
+
+// fwd (dgrad = false): src = x [n][cin], out = y [n][cout];
+// dgrad: src = dY [n][cout], out = dX [n][cin].
+template <int BN>
+static int halo_conv(rnn_ctx* ctx, const float* src, const float* wt, float* out, const ConvGeom& g, bool dgrad,
+                     bool acc) {
+  HaloConv3x3<BN> p;
+  p.src = src; p.out = out;
+  p.CS = dgrad ? g.cout : g.cin;
+  p.H = g.h;
+  p.M = g.n * g.h * g.w;
+  p.N = dgrad ? g.cin : g.cout;
+  p.kblocks = 9 * (p.CS / 32);
+  p.acc = acc ? 1 : 0;
+  p.splits = 1;
+  Sched s = make_sched(p.M, p.N, p.kblocks * BK, BN, 1);
+  const size_t bytes = (size_t)s.n_tiles * p.kblocks * 2 * BN * BK * sizeof(float);
+  RNN_TRY(ensure_pack(ctx, bytes));
+  p.bpack = static_cast<const float*>(ctx->pack);
+  RNN_RANGE(ctx->pack, bytes);
+  if (dgrad) {
+    PackHaloDgradSrc ps{wt, g.cout, g.cin};
+    RNN_TRY(launch_pack<BN>(ctx, ps, s.n_tiles, p.kblocks, static_cast<float*>(ctx->pack)));
+  } else {
+    PackHaloFwdSrc ps{wt, g.cout, g.cin};
+    RNN_TRY(launch_pack<BN>(ctx, ps, s.n_tiles, p.kblocks, static_cast<float*>(ctx->pack)));
+  }
+  return launch<BN>(ctx, p, s);
+}
+
+static int halo_dispatch(rnn_ctx* ctx, const float* src, const float* wt, float* out, const ConvGeom& g,
+                         bool dgrad, bool acc) {
+  const int N = dgrad ? g.cin : g.cout;
+  const int M = g.n * g.h * g.w;
+  // 256-wide tiles leave no room for a ring next to the halo buffers
+  int bn = pick_bn(N, (M + BM - 1) / BM, ctx->num_sms);
+  if (bn > 128) bn = 128;
+  switch (bn) {
+    case 32: return halo_conv<32>(ctx, src, wt, out, g, dgrad, acc);
+    case 64: return halo_conv<64>(ctx, src, wt, out, g, dgrad, acc);
+    default: return halo_conv<128>(ctx, src, wt, out, g, dgrad, acc);
+  }
 }
 
 template <int BN>
@@ -762,6 +838,7 @@ int conv_fwd(rnn_ctx* ctx, const float* x, int n, int cin, int h, int w, const f
     p.splits = 1;
     p.w_vec = (K % 4 == 0) && ((reinterpret_cast<uintptr_t>(wt) & 15) == 0);
   };
+  if (halo_ok(cin, h, w, k, stride, pad, x)) return halo_dispatch(ctx, x, wt, y, g, false, acc);
   if (cin % 32 == 0) {
     switch (bn) {
       case 32: return k == 3 ? fast_fwd<3, 32>(ctx, x, wt, y, g, acc) : fast_fwd<1, 32>(ctx, x, wt, y, g, acc);
@@ -802,6 +879,7 @@ int conv_dgrad(rnn_ctx* ctx, const float* dy, int n, int cin, int h, int w, cons
       default: return fast_dgrad_1x1_strided<256>(ctx, dy, wt, dx, g, acc);
     }
   }
+  if (halo_ok(cout, h, w, k, stride, pad, dy)) return halo_dispatch(ctx, dy, wt, dx, g, true, acc);
   if (cout % 32 == 0) {
     switch (bn) {
       case 32: return k == 3 ? fast_dgrad<3, 32>(ctx, dy, wt, dx, g, acc) : fast_dgrad<1, 32>(ctx, dy, wt, dx, g, acc);
@@ -818,30 +896,6 @@ int conv_dgrad(rnn_ctx* ctx, const float* dy, int n, int cin, int h, int w, cons
   }
   ConvDgradProb<1> p; fill(p);
   return run_bn<ConvLauncher>(ctx, bn, p, 1);
-}
-
-int conv_dgrad_join(rnn_ctx* ctx, const float* dy, int n, int cin, int h, int w, const float* wt, int cout,
-                    int k, int stride, int pad, float* dx, const float* res, const float* mask) {
-  ConvGeom g;
-  RNN_TRY(check_geom(n, cin, h, w, cout, k, stride, pad, &g));
-  if (n == 0) return RNN_OK;
-  const ConvSpans sp = spans(g, k);
-  if (cout % 32 == 0 && k == 3) {
-    RNN_RANGE(dy, sp.y);
-    RNN_RANGE(wt, sp.w);
-    RNN_RANGE(dx, sp.x);
-    RNN_RANGE(res, sp.x);
-    RNN_RANGE(mask, sp.x);
-    const int M = n * h * w;
-    switch (pick_bn(cin, (M + BM - 1) / BM, ctx->num_sms)) {
-      case 32: return fast_dgrad<3, 32>(ctx, dy, wt, dx, g, false, res, mask);
-      case 64: return fast_dgrad<3, 64>(ctx, dy, wt, dx, g, false, res, mask);
-      case 128: return fast_dgrad<3, 128>(ctx, dy, wt, dx, g, false, res, mask);
-      default: return fast_dgrad<3, 256>(ctx, dy, wt, dx, g, false, res, mask);
-    }
-  }
-  RNN_TRY(conv_dgrad(ctx, dy, n, cin, h, w, wt, cout, k, stride, pad, dx, false));
-  return add_masked(ctx, dx, res, mask, sp.x / sizeof(float));
 }
 
 int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, int h, int w,
@@ -868,12 +922,6 @@ int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, in
     auto ffill = [&](auto& p) {
       p.x = x; p.dy = dy; p.dw = dw; p.ws = nullptr; p.g = g; p.M = M; p.N = N; p.K = K; p.splits = 1;
     };
-    // 16-byte window loads: stride 1, "same" padding, rows of whole float4s
-    const bool vec = stride == 1 && 2 * pad == k - 1 && w % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
-    if (k == 3 && vec) {
-      FastConvWgrad<3, true> p; ffill(p);
-      return run_bn<WgradLauncher>(ctx, bn, p, splits);
-    }
     if (k == 3) {
       FastConvWgrad<3> p; ffill(p);
       return run_bn<WgradLauncher>(ctx, bn, p, splits);

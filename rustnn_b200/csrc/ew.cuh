@@ -28,10 +28,6 @@ int conv_dgrad(rnn_ctx* ctx, const float* dy, int n, int cin, int h, int w, cons
                int stride, int pad, float* dx, bool acc);
 int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, int h, int w, int cout, int k,
                int stride, int pad, float* dw, int force_splits);
-// dx = dgrad(dy) + (mask <= 0 ? 0 : res), elementwise over dx: the identity
-// shortcut's gradient joined in the dgrad epilogue where the fast path runs
-int conv_dgrad_join(rnn_ctx* ctx, const float* dy, int n, int cin, int h, int w, const float* wt, int cout,
-                    int k, int stride, int pad, float* dx, const float* res, const float* mask);
 }  // namespace tc
 
 }  // namespace rnn

@@ -252,14 +252,10 @@ static int conv_forward(rnn_resnet* net, const ConvL& c, const float* x, int n, 
   return tc::conv_fwd(net->ctx, x, n, c.cin, h, w, net->v + c.w_off, c.cout, c.k, c.stride, c.pad, y, false);
 }
 
-// nn.rs:230-250: backward_w then dX.  With res, dX also receives the
-// identity shortcut's gradient masked by the join's ReLU (model.rs:59-70).
+// nn.rs:230-250: backward_w then dX
 static int conv_backward(rnn_resnet* net, const ConvL& c, const float* x, const float* dy, int n, int h, int w,
-                         float* dx, bool dx_acc, const float* res = nullptr, const float* mask = nullptr) {
+                         float* dx, bool dx_acc) {
   RNN_TRY(tc::conv_wgrad(net->ctx, x, dy, n, c.cin, h, w, c.cout, c.k, c.stride, c.pad, net->g + c.w_off, 0));
-  if (dx && res)
-    return tc::conv_dgrad_join(net->ctx, dy, n, c.cin, h, w, net->v + c.w_off, c.cout, c.k, c.stride, c.pad, dx,
-                               res, mask);
   if (dx)
     RNN_TRY(tc::conv_dgrad(net->ctx, dy, n, c.cin, h, w, net->v + c.w_off, c.cout, c.k, c.stride, c.pad, dx,
                            dx_acc));
@@ -321,12 +317,15 @@ static int resnet_backward(rnn_resnet* net, const float* dlogits) {
     RNN_TRY(bn_backward(net, b.b2, d, b.y2, b.out, n, ohw, t));
     RNN_TRY(conv_backward(net, b.c2, b.h1, t, n, b.oh, b.ow, dmain, false));
     RNN_TRY(bn_backward(net, b.b1, dmain, b.y1, b.h1, n, ohw, t));
+    RNN_TRY(conv_backward(net, b.c1, b.x_in, t, n, b.h, b.w, dx, false));
     if (b.down) {
-      RNN_TRY(conv_backward(net, b.c1, b.x_in, t, n, b.h, b.w, dx, false));
       RNN_TRY(bn_backward(net, b.bd, d, b.yd, b.out, n, ohw, t));
       RNN_TRY(conv_backward(net, b.cd, b.x_in, t, n, b.h, b.w, dx, true));
     } else {
-      RNN_TRY(conv_backward(net, b.c1, b.x_in, t, n, b.h, b.w, dx, false, d, b.out));
+      // identity shortcut: a separate streaming pass; joined in the dgrad
+      // epilogue the loads of d and out stall the epilogue warps (measured
+      // 2-3x the dgrad's own time)
+      RNN_TRY(add_masked(ctx, dx, d, b.out, (size_t)n * b.cin * b.h * b.w));
     }
     std::swap(id, idx);
   }

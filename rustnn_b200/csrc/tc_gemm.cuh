@@ -34,6 +34,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+#include <utility>
+
 namespace rnn {
 namespace tc {
 
@@ -76,6 +79,22 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst_smem, const void* src, uin
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst_smem),
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
+}
+
+// 16-byte asynchronous copy global -> shared through L2 (cp.async.cg, not
+// the bulk/TMA engine); src_bytes = 0 zero-fills the 16 bytes and reads
+// nothing.  Completion: cp_async_wait_all() in the issuing thread.
+__device__ __forceinline__ void cp_async16(uint32_t dst_smem, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst_smem), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+__device__ __forceinline__ float ld_shared_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
@@ -251,14 +270,21 @@ __device__ __forceinline__ void store_split(uint32_t hi_base, uint32_t lo_base, 
 
 // ------------------------------------------------------------------ config
 
-template <int BN_>
+// EXTRA: bytes of problem-owned shared memory after the ring (the halo
+// buffers of HALO problems); the ring gets what is left of the budget.
+template <int BN_, int EXTRA_ = 0>
 struct Cfg {
   static constexpr int BN = BN_;
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+  static constexpr int EXTRA = EXTRA_;
+  static_assert(EXTRA % 1024 == 0, "EXTRA keeps the barriers 8-byte and the ring 1024-byte aligned");
   static constexpr int A_BYTES = BM * BK * 4;  // 16 KB
   static constexpr int B_BYTES = BN * BK * 4;
   static constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);  // hi + lo
-  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 4 ? 4 : (200 * 1024) / STAGE_BYTES;
+  // 227 KB per CTA minus the alignment slack and barriers below
+  static constexpr int RING_BUDGET = 227 * 1024 - 1024 - 256 - EXTRA;
+  static constexpr int STAGES = RING_BUDGET / STAGE_BYTES > 4 ? 4 : RING_BUDGET / STAGE_BYTES;
+  static_assert(STAGES >= 2, "the ring needs two stages");
   // Narrow tiles (BN <= 64) issue each 8-deep K step as two MMAs of width
   // 2*BN over the stacked [B_hi; B_lo] image (the lo tile follows the hi
   // tile in shared memory, so one descriptor covers both): columns [0, BN)
@@ -271,7 +297,7 @@ struct Cfg {
   static constexpr int TMEM_COLS = (2 * ACC_COLS <= 32) ? 32 : (2 * ACC_COLS <= 64) ? 64
                                    : (2 * ACC_COLS <= 128) ? 128 : (2 * ACC_COLS <= 256) ? 256 : 512;
   // 1024 bytes of alignment slack + barriers
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EXTRA + 1024 + 256;
   static constexpr uint32_t IDESC = idesc_tf32(BM, BN);
   static constexpr uint32_t IDESC2 = idesc_tf32(BM, 2 * BN);  // stacked-B MMA (STACK)
   // Producer groups take K blocks round-robin (block it -> group it % GROUPS),
@@ -359,24 +385,42 @@ struct ChunkProb : P {
   __device__ __forceinline__ const void* b_src(int, int) const { return nullptr; }
 };
 
+// Problems that stage a halo of the gathered operand in shared memory
+// declare HALO_BYTES (both buffers) and TAPS, and supply
+//   void halo_issue(uint32_t halo, int buf, int m_tile, int cb, int ptid, int npt) const;
+//        cp.async the halo of K-block group cb (TAPS consecutive K blocks)
+//        of row tile m_tile into buffer buf; producer thread ptid of npt
+//   void load_a_halo(uint32_t halo, int buf, const TS&, int tap, int gt, float (&v)[32]) const;
+template <class P, class = void>
+struct prob_extra {
+  static constexpr int value = 0;
+};
+template <class P>
+struct prob_extra<P, std::void_t<decltype(P::HALO_BYTES)>> {
+  static constexpr int value = P::HALO_BYTES;
+};
+
 // ------------------------------------------------------------------ kernel
 
 template <int BN, class Prob>
-__global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
+__global__ void __launch_bounds__(Cfg<BN, prob_extra<Prob>::value>::THREADS, 1)
     tc3_gemm_kernel(const Prob prob, const Sched sched, int* dev_error) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, prob_extra<Prob>::value>;
+  constexpr bool HALO = C::EXTRA > 0;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte aligned operand ring
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t ring = (raw_addr + 1023u) & ~1023u;
   uint8_t* ring_ptr = smem_raw + (ring - raw_addr);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ring_ptr + C::STAGES * C::STAGE_BYTES);
+  const uint32_t halo = ring + C::STAGES * C::STAGE_BYTES;  // HALO problems' buffers
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring_ptr + C::STAGES * C::STAGE_BYTES + C::EXTRA);
   uint64_t* full = bars;                      // [STAGES] producers -> MMA
   uint64_t* empty = bars + C::STAGES;         // [STAGES] MMA commit -> producers
   uint64_t* acc_full = bars + 2 * C::STAGES;  // [2] MMA commit -> epilogue
   uint64_t* acc_empty = acc_full + 2;         // [2] epilogue -> MMA
   uint64_t* drain = acc_empty + 2;            // [1] abort path
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* halo_bar = drain + 1;             // [1] all producers: a halo buffer is filled / released
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(halo_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -393,6 +437,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
       mbar_init(&acc_empty[b], 4 * 32);
     }
     mbar_init(drain, 1);
+    mbar_init(halo_bar, C::PRODUCER_WARPS * 32);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -408,6 +453,71 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
   const int tiles_mn = sched.m_tiles * sched.n_tiles;
 
   if (warp < C::PRODUCER_WARPS) {
+   if constexpr (HALO) {
+    // ---------------------------------------------------- halo producers
+    // K runs in groups of TAPS blocks (one 32-channel block, every tap).
+    // All producer threads cp.async the halo of the next group into the
+    // spare buffer while the current one is read, and meet on halo_bar at
+    // every group boundary: it publishes the landed halo and releases the
+    // buffer the next prefetch overwrites.  Groups keep taking K blocks
+    // round-robin as below.  splits == 1 (the launcher guarantees it).
+    const int group = warp >> 2;
+    const int gt = threadIdx.x & (GROUP_THREADS - 1);
+    const int ptid = threadIdx.x;
+    constexpr int NPT = C::PRODUCER_WARPS * 32;
+    constexpr int TAPS = Prob::TAPS;
+    auto mt_of = [&](int tile) { return (tile % tiles_mn) % sched.m_tiles; };
+    uint32_t it = 0, hc = 0;
+    bool ok = true;
+    if (blockIdx.x < sched.num_tiles) {
+      prob.halo_issue(halo, 0, mt_of(blockIdx.x), 0, ptid, NPT);
+    }
+    cp_async_commit();
+    for (int tile = blockIdx.x; tile < sched.num_tiles && ok; tile += gridDim.x) {
+      const int mn = tile % tiles_mn;
+      const int mt = mn % sched.m_tiles, nt = mn / sched.m_tiles;
+      typename Prob::TS ts;
+      prob.tile_begin(ts, mt * BM, nt * BN, gt);
+      for (int kb = 0; kb < sched.kblocks; kb++, it++) {
+        const int cb = kb / TAPS, tap = kb - cb * TAPS;
+        if (tap == 0) {
+          cp_async_wait_all();
+          mbar_arrive(halo_bar);
+          if (!mbar_wait(halo_bar, hc & 1, abort_flag, dev_error)) { ok = false; break; }
+          int ntile = tile, ncb = cb + 1;
+          if (ncb * TAPS >= sched.kblocks) { ntile = tile + gridDim.x; ncb = 0; }
+          if (ntile < sched.num_tiles) {
+            prob.halo_issue(halo, (hc + 1) & 1, mt_of(ntile), ncb, ptid, NPT);
+          }
+          cp_async_commit();
+          hc++;
+        }
+        if ((int)(it % C::GROUPS) != group) continue;
+        const int stage = it % C::STAGES;
+        const uint32_t phase = (it / C::STAGES) & 1;
+        float va[32];
+        prob.load_a_halo(halo, (hc - 1) & 1, ts, tap, gt, va);
+        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, dev_error)) { ok = false; break; }
+        const uint32_t a_hi = ring + stage * C::STAGE_BYTES;
+        const uint32_t a_lo = a_hi + C::A_BYTES;
+        const uint32_t b_hi = a_lo + C::A_BYTES;
+        if (gt == 0) {
+          mbar_arrive_expect_tx(&full[stage], 2 * C::B_BYTES);
+          bulk_g2s(b_hi, prob.b_src(nt, kb), 2 * C::B_BYTES, &full[stage]);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          int r, c;
+          Prob::a_slot(gt, j, r, c);
+          const float t[4] = {va[4 * j], va[4 * j + 1], va[4 * j + 2], va[4 * j + 3]};
+          store_split(a_hi, a_lo, sw128_offset(r, c), t);
+        }
+        fence_async_smem();
+        mbar_arrive(&full[stage]);
+      }
+    }
+    cp_async_wait_all();
+   } else {
     // ---------------------------------------------------------- producers
     const int group = warp >> 2;                 // 0 .. GROUPS-1
     const int gt = threadIdx.x & (GROUP_THREADS - 1);
@@ -463,6 +573,7 @@ __global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
       }
     }
     (void)lane;
+   }
   } else if (warp == C::MMA_WARP) {
     // ---------------------------------------------------------- MMA issuer
     // The whole warp walks the schedule, waits and builds the descriptors
