@@ -453,28 +453,40 @@ struct FastDgrad1x1Strided {
   }
 };
 
-// 3x3, stride 1, pad 1 convolution over 32-pixel-wide images whose height
-// is a multiple of 4 (the 32x32 stage of the CIFAR networks), as forward
-// (src = x, out = y) or as dgrad (src = dY, out = dX, taps flipped in the
-// packed weights).  A row tile is 4 whole image rows; K is ordered
-// (32-channel block cb, tap, channel), and for each cb the producers stage
-// the tile's halo -- 32 channels x 6 rows x 40 columns (columns -4 .. 35,
-// so every 16-byte chunk is either inside the row or all padding) -- in
-// shared memory with cp.async, then build all nine tap-shifted A tiles from
-// it: one global read of the input per channel block instead of nine.
-template <int BN>
+// 3x3, stride 1, pad 1 convolution over W = 32 (or 16) pixel-wide images
+// whose height is a multiple of 128/W (the 32x32 and 16x16 stages of the
+// CIFAR networks), as forward (src = x, out = y) or as dgrad (src = dY,
+// out = dX, taps flipped in the packed weights).  A row tile is 128/W whole
+// image rows; K is ordered (32-channel block cb, tap, channel), and for each
+// cb the producers stage the tile's halo -- 32 channels x (128/W + 2) rows x
+// (W + 8) columns (columns -4 .. W+3, so every 16-byte chunk is either
+// inside the row or all padding) -- in shared memory with cp.async, then
+// build all nine tap-shifted A tiles from it: one global read of the input
+// per channel block instead of nine.  At W = 16 a warp reads two image rows
+// per load, so halo rows are stored in pairs interleaved by 16-byte chunk
+// (row pair, column chunk, row parity, column % 4): the half-warp reading
+// an even row and the one reading the odd row use disjoint banks.
+template <int BN, int W_ = 32>
 struct HaloConv3x3 {
   static constexpr bool B_BULK = true;
   static constexpr int TAPS = 9;
-  static constexpr int W = 32;
+  static constexpr int W = W_;
+  static_assert(W == 32 || W == 16, "halo widths");
   static constexpr int TR = BM / W;      // image rows per tile
   static constexpr int HR = TR + 2;      // halo rows
   static constexpr int HX = W + 8;       // halo columns (-4 .. W+3)
   static constexpr int HCH = HX / 4;     // 16-byte chunks per halo row
-  static constexpr int HALO_FLOATS = 32 * HR * HX;
+  static constexpr bool PAIRS = W < 32;
+  static constexpr int CSTR = PAIRS ? ((HR + 1) / 2) * 2 * HX : HR * HX;  // floats per channel
+  static constexpr int HALO_FLOATS = 32 * CSTR;
   static constexpr int HALO_BYTES = 2 * HALO_FLOATS * 4;
-  const float* src;  // [n][CS][H][32]
-  float* out;        // [n][N][H][32]
+  // float offset of halo row r, halo column x (0 .. HX-1) within a channel
+  static __device__ __forceinline__ int pos(int r, int x) {
+    if constexpr (PAIRS) return (r >> 1) * (2 * HX) + (x >> 2) * 8 + (r & 1) * 4 + (x & 3);
+    return r * HX + x;
+  }
+  const float* src;  // [n][CS][H][W]
+  float* out;        // [n][N][H][W]
   const float* bpack;
   int CS, H;
   int M, N;
@@ -499,16 +511,16 @@ struct HaloConv3x3 {
       const int iy = oy0 - 1 + r, ix = xc * 4 - 4;
       const bool in = iy >= 0 && iy < H && ix >= 0 && ix < W;
       const float* g = in ? base + ((size_t)c * H + iy) * W + ix : src;
-      cp_async16(dst0 + (uint32_t)(((c * HR + r) * HX + xc * 4) * 4), g, in ? 16u : 0u);
+      cp_async16(dst0 + (uint32_t)((c * CSTR + pos(r, xc * 4)) * 4), g, in ? 16u : 0u);
     }
   }
   __device__ __forceinline__ void load_a_halo(uint32_t halo, int buf, const TS&, int tap, int gt,
                                               float (&v)[32]) const {
     const int kh = tap / 3, kw = tap - kh * 3;
     const int oyl = gt / W, ox = gt - oyl * W;
-    const uint32_t a = halo + (uint32_t)((buf * HALO_FLOATS + (oyl + kh) * HX + ox + kw + 3) * 4);
+    const uint32_t a = halo + (uint32_t)((buf * HALO_FLOATS + pos(oyl + kh, ox + kw + 3)) * 4);
 #pragma unroll
-    for (int j = 0; j < 32; j++) v[j] = ld_shared_f32(a + (uint32_t)(j * HR * HX * 4));
+    for (int j = 0; j < 32; j++) v[j] = ld_shared_f32(a + (uint32_t)(j * CSTR * 4));
   }
   __device__ __forceinline__ const void* b_src(int nt, int kb) const {
     return bpack + ((size_t)nt * kblocks + kb) * (2 * BN * BK);
@@ -802,16 +814,21 @@ static int fast_dgrad(rnn_ctx* ctx, const float* dy, const float* wt, float* dx,
 // True when the halo kernels cover a 3x3/s1/p1 convolution whose gathered
 // operand has cs channels over h x w pixels.
 static bool halo_ok(int cs, int h, int w, int k, int stride, int pad, const void* src) {
-  return k == 3 && stride == 1 && pad == 1 && w == 32 && h % 4 == 0 && cs % 32 == 0 &&
+  return k == 3 && stride == 1 && pad == 1 && (w == 32 || w == 16) && h % (BM / w) == 0 && cs % 32 == 0 &&
          (reinterpret_cast<uintptr_t>(src) & 15) == 0;
 }
+// Widest tile for 16-pixel-wide images.  The halo leaves room for 2 ring
+// stages at BN = 128 and 3 at BN = 64; measured at 128 channels, batch 1024:
+// BN = 128 fwd/dgrad 0.405/0.393 ms (0.407/0.405 without the halo), BN = 64
+// (two column tiles each rebuilding A) 0.60/0.59 ms.
+constexpr int HALO16_MAX_BN = 128;
 
 // fwd (dgrad = false): src = x [n][cin], out = y [n][cout];
 // dgrad: src = dY [n][cout], out = dX [n][cin].
-template <int BN>
+template <int BN, int W>
 static int halo_conv(rnn_ctx* ctx, const float* src, const float* wt, float* out, const ConvGeom& g, bool dgrad,
                      bool acc) {
-  HaloConv3x3<BN> p;
+  HaloConv3x3<BN, W> p;
   p.src = src; p.out = out;
   p.CS = dgrad ? g.cout : g.cin;
   p.H = g.h;
@@ -842,10 +859,18 @@ static int halo_dispatch(rnn_ctx* ctx, const float* src, const float* wt, float*
   // 256-wide tiles leave no room for a ring next to the halo buffers
   int bn = pick_bn(N, (M + BM - 1) / BM, ctx->num_sms);
   if (bn > 128) bn = 128;
+  if (g.w == 16) {
+    if (bn > HALO16_MAX_BN) bn = HALO16_MAX_BN;
+    switch (bn) {
+      case 32: return halo_conv<32, 16>(ctx, src, wt, out, g, dgrad, acc);
+      case 64: return halo_conv<64, 16>(ctx, src, wt, out, g, dgrad, acc);
+      default: return halo_conv<128, 16>(ctx, src, wt, out, g, dgrad, acc);
+    }
+  }
   switch (bn) {
-    case 32: return halo_conv<32>(ctx, src, wt, out, g, dgrad, acc);
-    case 64: return halo_conv<64>(ctx, src, wt, out, g, dgrad, acc);
-    default: return halo_conv<128>(ctx, src, wt, out, g, dgrad, acc);
+    case 32: return halo_conv<32, 32>(ctx, src, wt, out, g, dgrad, acc);
+    case 64: return halo_conv<64, 32>(ctx, src, wt, out, g, dgrad, acc);
+    default: return halo_conv<128, 32>(ctx, src, wt, out, g, dgrad, acc);
   }
 }
 
