@@ -563,6 +563,76 @@ struct PackDgradSrc {
   }
 };
 
+// dgrad of a 3x3, stride-2, pad-1 convolution split by input-pixel parity
+// (py, px): pixel (2a+py, 2b+px) only receives taps with kh = 1 (py = 0) or
+// kh in {0, 2} (py = 1), the same for kw, at dY position (a + (py+1-kh)/2,
+// b + (px+1-kw)/2).  One launch per class runs M = n*A*B pixels of the
+// class against K = taps(class)*cout (1, 2, 2 and 4 taps): 9 taps in all
+// instead of the 36 a stride-blind gather multiplies by zero.
+template <int BN>
+struct FastDgradS2 {
+  static constexpr bool B_BULK = true;
+  const float* dy;
+  float* dx;
+  const float* bpack;
+  ConvGeom g;
+  int M, N;
+  int CB;        // cout blocks of 32 per tap
+  int kblocks;   // ntaps * CB
+  int acc;
+  int splits;
+  int py, px, A, B;  // class parity and its rows / columns per image
+  int dyo[4], dxo[4];  // per class tap: dY row / column offset (a + dyo, b + dxo)
+
+  struct TS {
+    const float* dyb;
+    int a, b;
+    bool ok;
+  };
+  __device__ __forceinline__ void tile_begin(TS& ts, int m0, int, int gt) const {
+    const int row = m0 + gt;
+    ts.ok = row < M;
+    const int ab = A * B;
+    const int r = ts.ok ? row : 0;
+    const int img = r / ab, rem = r - img * ab;
+    ts.a = rem / B;
+    ts.b = rem - ts.a * B;
+    ts.dyb = dy + (size_t)img * g.cout * g.oh * g.ow;
+  }
+  static __device__ __forceinline__ void a_slot(int gt, int j, int& r, int& c) { r = gt; c = j; }
+  __device__ __forceinline__ void load_a(const TS& ts, int kb, int, float (&v)[32]) const {
+    const int t = kb / CB, cb = kb - t * CB;
+    const int oy = ts.a + dyo[t], ox = ts.b + dxo[t];
+    const bool valid = ts.ok && oy >= 0 && oy < g.oh && ox >= 0 && ox < g.ow;
+    const int ohw = g.oh * g.ow;
+    const float* p = ts.dyb + (size_t)(cb * 32) * ohw + (valid ? oy * g.ow + ox : 0);
+#pragma unroll
+    for (int j = 0; j < 32; j++) v[j] = valid ? __ldg(p + (size_t)j * ohw) : 0.0f;
+  }
+  __device__ __forceinline__ const void* b_src(int nt, int kb) const {
+    return bpack + ((size_t)nt * kblocks + kb) * (2 * BN * BK);
+  }
+  __device__ __forceinline__ void store(int row, int col0, int, const float (&v)[32]) const {
+    if (row >= M) return;
+    const int ab = A * B, hw = g.h * g.w;
+    const int img = row / ab, rem = row - img * ab;
+    const int a = rem / B, b = rem - a * B;
+    store_planes32(dx, ((size_t)img * g.cin + col0) * hw + (size_t)(2 * a + py) * g.w + 2 * b + px, hw, N - col0,
+                   v, acc);
+  }
+};
+
+// B(ci, k = t*cout + co) = W[co][ci][tap[t]] for the class's taps
+struct PackDgradS2Src {
+  const float* w;
+  int cout, cin, ntaps;
+  int tap[4];
+  __device__ __forceinline__ float operator()(int ci, int k) const {
+    const int t = k / cout, co = k - t * cout;
+    return (ci < cin && t < ntaps) ? __ldg(w + ((size_t)co * cin + ci) * 9 + tap[t]) : 0.0f;
+  }
+};
+
 // wgrad: M = (ci, kh, kw) rows, N = cout, K = pixels, when every group of 4
 // consecutive pixels lies in one output row (ow % 4 == 0).  A producer
 // thread owns 4 consecutive pixels of 8 rows; it decodes the pixel block once
@@ -874,6 +944,49 @@ static int halo_dispatch(rnn_ctx* ctx, const float* src, const float* wt, float*
   }
 }
 
+// The four parity classes of a 3x3/s2/p1 dgrad, one launch each; together
+// they write every pixel of dX exactly once.
+template <int BN>
+static int dgrad_s2(rnn_ctx* ctx, const float* dy, const float* wt, float* dx, const ConvGeom& g, bool acc) {
+  // the pack buffer is sized once for the widest class (4 taps): growing it
+  // between the launches would free memory a queued launch still reads
+  const size_t max_bytes = (size_t)((g.cin + BN - 1) / BN) * (4 * (g.cout / 32)) * 2 * BN * BK * sizeof(float);
+  RNN_TRY(ensure_pack(ctx, max_bytes));
+  for (int cls = 0; cls < 4; cls++) {
+    FastDgradS2<BN> p;
+    p.dy = dy; p.dx = dx; p.g = g; p.acc = acc ? 1 : 0; p.splits = 1;
+    p.py = cls >> 1;
+    p.px = cls & 1;
+    p.A = (g.h + 1 - p.py) / 2;
+    p.B = (g.w + 1 - p.px) / 2;
+    if (p.A <= 0 || p.B <= 0) continue;
+    // taps of the class: kh = 1 for even rows, {0, 2} for odd rows (same for kw)
+    int khs[2], kws[2], nkh = 0, nkw = 0;
+    if (p.py == 0) khs[nkh++] = 1; else { khs[nkh++] = 0; khs[nkh++] = 2; }
+    if (p.px == 0) kws[nkw++] = 1; else { kws[nkw++] = 0; kws[nkw++] = 2; }
+    PackDgradS2Src src{wt, g.cout, g.cin, 0, {0, 0, 0, 0}};
+    for (int i = 0; i < nkh; i++)
+      for (int j = 0; j < nkw; j++) {
+        const int t = src.ntaps++;
+        src.tap[t] = khs[i] * 3 + kws[j];
+        p.dyo[t] = (p.py + 1 - khs[i]) / 2;  // iy = 2a + py = 2*oy - 1 + kh
+        p.dxo[t] = (p.px + 1 - kws[j]) / 2;
+      }
+    for (int t = src.ntaps; t < 4; t++) { p.dyo[t] = 0; p.dxo[t] = 0; }
+    p.M = g.n * p.A * p.B;
+    p.N = g.cin;
+    p.CB = g.cout / 32;
+    p.kblocks = src.ntaps * p.CB;
+    Sched s = make_sched(p.M, p.N, p.kblocks * BK, BN, 1);
+    const size_t bytes = (size_t)s.n_tiles * p.kblocks * 2 * BN * BK * sizeof(float);
+    p.bpack = static_cast<const float*>(ctx->pack);
+    RNN_RANGE(ctx->pack, bytes);
+    RNN_TRY(launch_pack<BN>(ctx, src, s.n_tiles, p.kblocks, static_cast<float*>(ctx->pack)));
+    RNN_TRY(launch<BN>(ctx, p, s));
+  }
+  return RNN_OK;
+}
+
 template <int BN>
 static int fast_dgrad_1x1_strided(rnn_ctx* ctx, const float* dy, const float* wt, float* dx, const ConvGeom& g,
                                   bool acc) {
@@ -950,6 +1063,15 @@ int conv_dgrad(rnn_ctx* ctx, const float* dy, int n, int cin, int h, int w, cons
     }
   }
   if (halo_ok(cout, h, w, k, stride, pad, dy)) return halo_dispatch(ctx, dy, wt, dx, g, true, acc);
+  if (cout % 32 == 0 && k == 3 && stride == 2 && pad == 1) {
+    // per parity class M = n*h*w/4: choose the tile width for that
+    switch (pick_bn(N, (n * ((h + 1) / 2) * ((w + 1) / 2) + BM - 1) / BM, ctx->num_sms)) {
+      case 32: return dgrad_s2<32>(ctx, dy, wt, dx, g, acc);
+      case 64: return dgrad_s2<64>(ctx, dy, wt, dx, g, acc);
+      case 128: return dgrad_s2<128>(ctx, dy, wt, dx, g, acc);
+      default: return dgrad_s2<256>(ctx, dy, wt, dx, g, acc);
+    }
+  }
   if (cout % 32 == 0) {
     switch (bn) {
       case 32: return k == 3 ? fast_dgrad<3, 32>(ctx, dy, wt, dx, g, acc) : fast_dgrad<1, 32>(ctx, dy, wt, dx, g, acc);
