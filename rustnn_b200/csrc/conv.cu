@@ -466,6 +466,8 @@ struct FastDgrad1x1Strided {
 // per load, so halo rows are stored in pairs interleaved by 16-byte chunk
 // (row pair, column chunk, row parity, column % 4): the half-warp reading
 // an even row and the one reading the odd row use disjoint banks.
+constexpr bool HALO_A_TMEM = true;
+
 template <int BN, int W_ = 32>
 struct HaloConv3x3 {
   static constexpr bool B_BULK = true;
@@ -480,6 +482,9 @@ struct HaloConv3x3 {
   static constexpr int CSTR = PAIRS ? ((HR + 1) / 2) * 2 * HX : HR * HX;  // floats per channel
   static constexpr int HALO_FLOATS = 32 * CSTR;
   static constexpr int HALO_BYTES = 2 * HALO_FLOATS * 4;
+  // the producers write the split A tile into tensor memory (tcgen05.st):
+  // shared memory then carries only the halo and the B images
+  static constexpr bool A_TMEM = HALO_A_TMEM;
   // float offset of halo row r, halo column x (0 .. HX-1) within a channel
   static __device__ __forceinline__ int pos(int r, int x) {
     if constexpr (PAIRS) return (r >> 1) * (2 * HX) + (x >> 2) * 8 + (r & 1) * 4 + (x & 3);

@@ -204,6 +204,33 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 
 // 32 TMEM lanes x 32 consecutive f32 columns; thread i of the warp receives
 // lane (base_lane + i).
+// D(tmem) (+)= A(tmem) * B(smem)^T, kind::tf32, one CTA.
+__device__ __forceinline__ void mma_tf32_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 lanes x 32 consecutive columns from registers; thread i of the warp
+// writes lane (base lane + i).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
   asm volatile(
@@ -272,19 +299,12 @@ __device__ __forceinline__ void store_split(uint32_t hi_base, uint32_t lo_base, 
 
 // EXTRA: bytes of problem-owned shared memory after the ring (the halo
 // buffers of HALO problems); the ring gets what is left of the budget.
-template <int BN_, int EXTRA_ = 0>
+template <int BN_, int EXTRA_ = 0, bool ATM_ = false>
 struct Cfg {
   static constexpr int BN = BN_;
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
   static constexpr int EXTRA = EXTRA_;
   static_assert(EXTRA % 1024 == 0, "EXTRA keeps the barriers 8-byte and the ring 1024-byte aligned");
-  static constexpr int A_BYTES = BM * BK * 4;  // 16 KB
-  static constexpr int B_BYTES = BN * BK * 4;
-  static constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);  // hi + lo
-  // 227 KB per CTA minus the alignment slack and barriers below
-  static constexpr int RING_BUDGET = 227 * 1024 - 1024 - 256 - EXTRA;
-  static constexpr int STAGES = RING_BUDGET / STAGE_BYTES > 4 ? 4 : RING_BUDGET / STAGE_BYTES;
-  static_assert(STAGES >= 2, "the ring needs two stages");
   // Narrow tiles (BN <= 64) issue each 8-deep K step as two MMAs of width
   // 2*BN over the stacked [B_hi; B_lo] image (the lo tile follows the hi
   // tile in shared memory, so one descriptor covers both): columns [0, BN)
@@ -294,7 +314,24 @@ struct Cfg {
   // and the fourth product lo*lo comes along for free.
   static constexpr bool STACK = BN <= 64;
   static constexpr int ACC_COLS = STACK ? 2 * BN : BN;  // columns per accumulator buffer
-  static constexpr int TMEM_COLS = (2 * ACC_COLS <= 32) ? 32 : (2 * ACC_COLS <= 64) ? 64
+  // ATM: the A operand (hi and lo) lives in tensor memory: the producers
+  // write it with tcgen05.st and the MMA reads it from there, so shared
+  // memory carries only B.  TMEM: [0, 2*ACC_COLS) accumulators, then one
+  // 64-column slot (32 hi + 32 lo, lane = A row) per ring stage.
+  static constexpr bool ATM = ATM_;
+  static constexpr int A_COL0 = 2 * ACC_COLS;
+  static constexpr int A_BYTES = BM * BK * 4;  // 16 KB
+  static constexpr int B_BYTES = BN * BK * 4;
+  static constexpr int A_SMEM = ATM ? 0 : 2 * A_BYTES;     // A hi + lo in the stage, unless in TMEM
+  static constexpr int STAGE_BYTES = A_SMEM + 2 * B_BYTES;  // [A hi | A lo |] B hi | B lo
+  // 227 KB per CTA minus the alignment slack and barriers below
+  static constexpr int RING_BUDGET = 227 * 1024 - 1024 - 256 - EXTRA;
+  static constexpr int STAGES_SMEM = RING_BUDGET / STAGE_BYTES;
+  static constexpr int STAGES_TMEM = ATM ? (512 - A_COL0) / 64 : 4;
+  static constexpr int STAGES_MIN = STAGES_SMEM < STAGES_TMEM ? STAGES_SMEM : STAGES_TMEM;
+  static constexpr int STAGES = STAGES_MIN > 4 ? 4 : STAGES_MIN;
+  static_assert(STAGES >= 2, "the ring needs two stages");
+  static constexpr int TMEM_COLS = ATM ? 512 : (2 * ACC_COLS <= 32) ? 32 : (2 * ACC_COLS <= 64) ? 64
                                    : (2 * ACC_COLS <= 128) ? 128 : (2 * ACC_COLS <= 256) ? 256 : 512;
   // 1024 bytes of alignment slack + barriers
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EXTRA + 1024 + 256;
@@ -399,14 +436,27 @@ template <class P>
 struct prob_extra<P, std::void_t<decltype(P::HALO_BYTES)>> {
   static constexpr int value = P::HALO_BYTES;
 };
+// HALO problems may set A_TMEM: their producers write A into tensor memory.
+template <class P, class = void>
+struct prob_atm {
+  static constexpr bool value = false;
+};
+template <class P>
+struct prob_atm<P, std::void_t<decltype(P::A_TMEM)>> {
+  static constexpr bool value = P::A_TMEM;
+};
 
 // ------------------------------------------------------------------ kernel
 
+template <class Prob, int BN>
+using CfgOf = Cfg<BN, prob_extra<Prob>::value, prob_atm<Prob>::value>;
+
 template <int BN, class Prob>
-__global__ void __launch_bounds__(Cfg<BN, prob_extra<Prob>::value>::THREADS, 1)
+__global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
     tc3_gemm_kernel(const Prob prob, const Sched sched, int* dev_error) {
-  using C = Cfg<BN, prob_extra<Prob>::value>;
+  using C = CfgOf<Prob, BN>;
   constexpr bool HALO = C::EXTRA > 0;
+  static_assert(HALO || !C::ATM, "A in tensor memory is built by the halo producers");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte aligned operand ring
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -497,22 +547,44 @@ __global__ void __launch_bounds__(Cfg<BN, prob_extra<Prob>::value>::THREADS, 1)
         const uint32_t phase = (it / C::STAGES) & 1;
         float va[32];
         prob.load_a_halo(halo, (hc - 1) & 1, ts, tap, gt, va);
-        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, dev_error)) { ok = false; break; }
+        // warp-uniform outcome: tcgen05.st below is .sync.aligned
+        if (!__all_sync(0xffffffffu, mbar_wait(&empty[stage], phase ^ 1, abort_flag, dev_error))) {
+          ok = false;
+          break;
+        }
         const uint32_t a_hi = ring + stage * C::STAGE_BYTES;
         const uint32_t a_lo = a_hi + C::A_BYTES;
-        const uint32_t b_hi = a_lo + C::A_BYTES;
+        const uint32_t b_hi = a_hi + C::A_SMEM;
         if (gt == 0) {
           mbar_arrive_expect_tx(&full[stage], 2 * C::B_BYTES);
           bulk_g2s(b_hi, prob.b_src(nt, kb), 2 * C::B_BYTES, &full[stage]);
         }
+        if constexpr (C::ATM) {
+          // thread gt owns A row gt = TMEM lane gt (warp w of a group
+          // reaches lanes 32*(w%4) ..; groups are 4 warps)
+          uint32_t hi[32], lo[32];
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-          int r, c;
-          Prob::a_slot(gt, j, r, c);
-          const float t[4] = {va[4 * j], va[4 * j + 1], va[4 * j + 2], va[4 * j + 3]};
-          store_split(a_hi, a_lo, sw128_offset(r, c), t);
+          for (int j = 0; j < 32; j++) {
+            const float h = tf32_round(va[j]);
+            hi[j] = __float_as_uint(h);
+            lo[j] = __float_as_uint(va[j] - h);
+          }
+          const uint32_t acol = tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + C::A_COL0 + stage * 64;
+          tmem_st32(acol, hi);
+          tmem_st32(acol + 32, lo);
+          tmem_wait_st();
+          tc_fence_before();
+          (void)a_lo;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; j++) {
+            int r, c;
+            Prob::a_slot(gt, j, r, c);
+            const float t[4] = {va[4 * j], va[4 * j + 1], va[4 * j + 2], va[4 * j + 3]};
+            store_split(a_hi, a_lo, sw128_offset(r, c), t);
+          }
+          fence_async_smem();
         }
-        fence_async_smem();
         mbar_arrive(&full[stage]);
       }
     }
@@ -604,7 +676,7 @@ __global__ void __launch_bounds__(Cfg<BN, prob_extra<Prob>::value>::THREADS, 1)
         tc_fence_after();
         const uint32_t a_hi = ring + stage * C::STAGE_BYTES;
         const uint32_t a_lo = a_hi + C::A_BYTES;
-        const uint32_t b_hi = a_lo + C::A_BYTES;
+        const uint32_t b_hi = a_hi + C::A_SMEM;
         const uint32_t b_lo = b_hi + C::B_BYTES;
         if (elect_one()) {
 #pragma unroll
@@ -613,7 +685,20 @@ __global__ void __launch_bounds__(Cfg<BN, prob_extra<Prob>::value>::THREADS, 1)
             const uint64_t dah = sdesc_sw128(a_hi + koff), dal = sdesc_sw128(a_lo + koff);
             const uint64_t dbh = sdesc_sw128(b_hi + koff), dbl = sdesc_sw128(b_lo + koff);
             const uint32_t first = (kb == kb0 && j == 0) ? 0u : 1u;
-            if constexpr (C::STACK) {
+            if constexpr (C::ATM) {
+              // A hi at columns [stage*64, +32), lo at [+32, +64); 8 columns per K step
+              const uint32_t tah = tmem_base + C::A_COL0 + stage * 64 + j * 8, tal = tah + 32;
+              if constexpr (C::STACK) {
+                mma_tf32_ta(d_tmem, tal, dbh, C::IDESC2, first);  // lo * [hi; lo]
+                mma_tf32_ta(d_tmem, tah, dbh, C::IDESC2, 1u);     // hi * [hi; lo]
+              } else {
+                mma_tf32_ta(d_tmem, tal, dbh, C::IDESC, first);  // lo * hi
+                mma_tf32_ta(d_tmem, tah, dbl, C::IDESC, 1u);     // hi * lo
+                mma_tf32_ta(d_tmem, tah, dbh, C::IDESC, 1u);     // hi * hi
+              }
+              (void)dah;
+              (void)dal;
+            } else if constexpr (C::STACK) {
               mma_tf32(d_tmem, dal, dbh, C::IDESC2, first);  // lo * [hi; lo]
               mma_tf32(d_tmem, dah, dbh, C::IDESC2, 1u);     // hi * [hi; lo]
               (void)dbl;

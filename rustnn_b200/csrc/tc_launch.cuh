@@ -93,7 +93,7 @@ struct has_ts<P, std::void_t<typename P::TS>> : std::true_type {};
 
 template <int BN, class Prob>
 int launch_native(rnn_ctx* ctx, const Prob& prob, const Sched& sched) {
-  using C = Cfg<BN, prob_extra<Prob>::value>;
+  using C = CfgOf<Prob, BN>;
   static bool attr_set = false;  // per instantiation; set once per process
   if (!attr_set) {
     RNN_CUDA(cudaFuncSetAttribute(tc3_gemm_kernel<BN, Prob>, cudaFuncAttributeMaxDynamicSharedMemorySize,
