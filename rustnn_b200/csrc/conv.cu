@@ -756,6 +756,65 @@ struct FastConvWgradPacked : FastConvWgrad<KS> {
   }
 };
 
+// wgrad of a 3x3/s1/p1 convolution over W in {8, 16, 32} pixel-wide images
+// (W*H a multiple of 32, so a K block is 32/W whole rows of one image) with
+// A in tensor memory: a producer thread owns one (ci, kh, kw) row and builds
+// its 32 pixels of the K block from eight aligned 16-byte loads of the
+// input rows, shifting by kw - 1 across neighbouring chunks (zero at the
+// row ends); the three kw rows of a (ci, kh) sit in adjacent lanes and read
+// the same addresses.  dY is pre-packed and bulk-copied as B.
+template <int BN, int W>
+struct FastConvWgradT : FastConvWgradPacked<3, BN> {
+  static constexpr bool A_TMEM = true;
+  static_assert(W == 8 || W == 16 || W == 32, "row widths");
+  static constexpr int R = 32 / W;  // image rows per K block
+  struct TS {
+    const float* xc;  // channel ci's plane of image 0
+    int kh, kw;
+    bool ok;
+  };
+  __device__ __forceinline__ void tile_begin(TS& ts, int m0, int, int gt) const {
+    const int row = m0 + gt;
+    ts.ok = row < this->M;
+    const int r = ts.ok ? row : 0;
+    const int ci = r / 9, kk = r - ci * 9;
+    ts.kh = kk / 3;
+    ts.kw = kk - ts.kh * 3;
+    ts.xc = this->x + (size_t)ci * this->g.h * W;
+  }
+  static __device__ __forceinline__ void a_slot(int gt, int j, int& r, int& c) { r = gt; c = j; }
+  __device__ __forceinline__ void load_a(const TS& ts, int kb, int, float (&v)[32]) const {
+    const int h = this->g.h, hw = h * W;
+    const int p0 = kb * BK;
+    const bool pin = ts.ok && p0 < this->K;
+    const int pp = pin ? p0 : 0;
+    const int img = pp / hw, oy0 = (pp - img * hw) / W;
+    const float* base = ts.xc + (size_t)img * this->g.cin * hw;
+    float4 c[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      const int r = (4 * q) / W, px0 = (4 * q) % W;
+      const int iy = oy0 + r + ts.kh - 1;
+      c[q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (pin && iy >= 0 && iy < h) c[q] = __ldg(reinterpret_cast<const float4*>(base + iy * W + px0));
+    }
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      const int px0 = (4 * q) % W;
+      const float left = px0 > 0 ? c[q - (px0 > 0 ? 1 : 0)].w : 0.0f;       // pixel px0 - 1 of the row
+      const float right = px0 + 4 < W ? c[q + (px0 + 4 < W ? 1 : 0)].x : 0.0f;  // pixel px0 + 4
+      const float4 m = c[q];
+      if (ts.kw == 1) {
+        v[4 * q] = m.x; v[4 * q + 1] = m.y; v[4 * q + 2] = m.z; v[4 * q + 3] = m.w;
+      } else if (ts.kw == 0) {
+        v[4 * q] = left; v[4 * q + 1] = m.x; v[4 * q + 2] = m.y; v[4 * q + 3] = m.z;
+      } else {
+        v[4 * q] = m.y; v[4 * q + 1] = m.z; v[4 * q + 2] = m.w; v[4 * q + 3] = right;
+      }
+    }
+  }
+};
+
 // B(co, k = pixel) = dY[img][co][pixel]
 struct PackWgradDySrc {
   const float* dy;
@@ -820,6 +879,32 @@ static int wgrad_packed(rnn_ctx* ctx, const float* x, const float* dy, float* dw
   PackWgradDySrc src{dy, g.cout, g.oh * g.ow, K};
   RNN_TRY(launch_pack<BN>(ctx, src, n_tiles, p.kblocks, static_cast<float*>(ctx->pack)));
   return WgradLauncher<BN>::run(ctx, p, splits);
+}
+
+template <int BN, int W>
+static int wgrad_t(rnn_ctx* ctx, const float* x, const float* dy, float* dw, const ConvGeom& g, int M, int N,
+                   int K, int splits) {
+  FastConvWgradT<BN, W> p;
+  p.x = x; p.dy = dy; p.dw = dw; p.ws = nullptr; p.g = g; p.M = M; p.N = N; p.K = K; p.splits = 1;
+  p.kblocks = (K + BK - 1) / BK;
+  const int n_tiles = (N + BN - 1) / BN;
+  const size_t bytes = (size_t)n_tiles * p.kblocks * 2 * BN * BK * sizeof(float);
+  RNN_TRY(ensure_pack(ctx, bytes));
+  p.bpack = static_cast<const float*>(ctx->pack);
+  RNN_RANGE(ctx->pack, bytes);
+  PackWgradDySrc src{dy, g.cout, g.oh * g.ow, K};
+  RNN_TRY(launch_pack<BN>(ctx, src, n_tiles, p.kblocks, static_cast<float*>(ctx->pack)));
+  return WgradLauncher<BN>::run(ctx, p, splits);
+}
+
+template <int W>
+static int wgrad_t_bn(rnn_ctx* ctx, int bn, const float* x, const float* dy, float* dw, const ConvGeom& g, int M,
+                      int N, int K, int splits) {
+  switch (bn) {
+    case 32: return wgrad_t<32, W>(ctx, x, dy, dw, g, M, N, K, splits);
+    case 64: return wgrad_t<64, W>(ctx, x, dy, dw, g, M, N, K, splits);
+    default: return wgrad_t<128, W>(ctx, x, dy, dw, g, M, N, K, splits);
+  }
 }
 
 // Tile widths from which wgrad pre-packs dY.  Measured at batch 1024: 64ch
@@ -1119,6 +1204,14 @@ int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, in
     auto ffill = [&](auto& p) {
       p.x = x; p.dy = dy; p.dw = dw; p.ws = nullptr; p.g = g; p.M = M; p.N = N; p.K = K; p.splits = 1;
     };
+    // A in tensor memory: 3x3/s1/p1 over 8/16/32-wide rows, whole-row K blocks;
+    // 256-wide tiles leave no tensor memory for A next to their accumulators
+    if (k == 3 && stride == 1 && pad == 1 && (h * w) % 32 == 0 && bn <= 128 &&
+        (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+      if (w == 32) return wgrad_t_bn<32>(ctx, bn, x, dy, dw, g, M, N, K, splits);
+      if (w == 16) return wgrad_t_bn<16>(ctx, bn, x, dy, dw, g, M, N, K, splits);
+      if (w == 8) return wgrad_t_bn<8>(ctx, bn, x, dy, dw, g, M, N, K, splits);
+    }
     if (k == 3 && bn >= WGRAD_PACK_MIN_BN) {
       switch (bn) {
         case 32: return wgrad_packed<3, 32>(ctx, x, dy, dw, g, M, N, K, splits);

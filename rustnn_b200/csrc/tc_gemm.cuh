@@ -456,7 +456,7 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
     tc3_gemm_kernel(const Prob prob, const Sched sched, int* dev_error) {
   using C = CfgOf<Prob, BN>;
   constexpr bool HALO = C::EXTRA > 0;
-  static_assert(HALO || !C::ATM, "A in tensor memory is built by the halo producers");
+  static_assert(!C::ATM || Prob::B_BULK, "A in tensor memory needs a bulk-copied B");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte aligned operand ring
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -613,10 +613,14 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
         constexpr int NB = Prob::B_BULK ? 4 : C::BCH * 4;
         float vb[NB];
         if constexpr (!Prob::B_BULK) prob.template load_b<NB>(ts, kb, gt, vb);
-        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, dev_error)) { ok = false; break; }
+        // warp-uniform outcome: the ATM path's tcgen05.st is .sync.aligned
+        if (!__all_sync(0xffffffffu, mbar_wait(&empty[stage], phase ^ 1, abort_flag, dev_error))) {
+          ok = false;
+          break;
+        }
         const uint32_t a_hi = ring + stage * C::STAGE_BYTES;
         const uint32_t a_lo = a_hi + C::A_BYTES;
-        const uint32_t b_hi = a_lo + C::A_BYTES;
+        const uint32_t b_hi = a_hi + C::A_SMEM;
         const uint32_t b_lo = b_hi + C::B_BYTES;
         if constexpr (Prob::B_BULK) {
           if (gt == 0) {
@@ -624,12 +628,30 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
             bulk_g2s(b_hi, prob.b_src(nt, kb), 2 * C::B_BYTES, &full[stage]);
           }
         }
+        if constexpr (C::ATM) {
+          // load_a returned the thread's own A row (a_slot(gt, j) == (gt, j)):
+          // row gt = TMEM lane gt
+          uint32_t hi[32], lo[32];
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-          int r, c;
-          Prob::a_slot(gt, j, r, c);
-          const float t[4] = {va[4 * j], va[4 * j + 1], va[4 * j + 2], va[4 * j + 3]};
-          store_split(a_hi, a_lo, sw128_offset(r, c), t);
+          for (int j = 0; j < 32; j++) {
+            const float h = tf32_round(va[j]);
+            hi[j] = __float_as_uint(h);
+            lo[j] = __float_as_uint(va[j] - h);
+          }
+          const uint32_t acol = tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + C::A_COL0 + stage * 64;
+          tmem_st32(acol, hi);
+          tmem_st32(acol + 32, lo);
+          tmem_wait_st();
+          tc_fence_before();
+          (void)a_lo;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; j++) {
+            int r, c;
+            Prob::a_slot(gt, j, r, c);
+            const float t[4] = {va[4 * j], va[4 * j + 1], va[4 * j + 2], va[4 * j + 3]};
+            store_split(a_hi, a_lo, sw128_offset(r, c), t);
+          }
         }
         if constexpr (!Prob::B_BULK) {
 #pragma unroll
@@ -640,7 +662,7 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
             store_split(b_hi, b_lo, sw128_offset(r, c), t);
           }
         }
-        fence_async_smem();
+        if constexpr (!C::ATM) fence_async_smem();
         mbar_arrive(&full[stage]);
       }
     }

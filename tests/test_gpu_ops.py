@@ -114,6 +114,7 @@ CONVS = [  # (n, cin, h, cout, k, stride, pad)
     (3, 32, 12, 64, 3, 1, 1),    # 12-wide rows: K blocks straddle image rows, ragged last K block
     (2, 96, 16, 160, 3, 1, 1),   # 16-wide halo: three channel blocks, 160 outputs over two column tiles
     (3, 32, 15, 64, 3, 2, 1),    # stride-2 dgrad by parity class over an odd input (classes of 8 and 7 rows)
+    (4, 32, 8, 64, 3, 1, 1),     # 8-wide rows: wgrad K blocks of four image rows
     (1, 32, 24, 32, 3, 1, 1),    # 24-pixel rows: not a halo width, per-pixel gather path
     (3, 64, 15, 64, 1, 2, 0),    # strided 1x1 dgrad over an odd input: last row/column hit
     (2, 32, 16, 64, 1, 3, 0),    # stride 3: two of every three rows/columns get no gradient
