@@ -41,59 +41,6 @@ static __device__ __forceinline__ void block_sum2(double a, double b, double* ou
   }
 }
 
-static __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-static __device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-static __device__ __forceinline__ unsigned long long gtimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Cross-rank step of the last CTA (all its threads; `sums` holds this
-// rank's totals): publish them in slot seq&1 of the own mailbox, raise the
-// flag to seq, wait for every peer's flag (bounded: 5 s, then an error bit
-// and garbage instead of a hang), and sum every rank's slot in rank order.
-// Two slots suffice: a rank can only publish seq+2 after passing the wait
-// for seq+1, which needs this rank's flag, raised after it read seq.
-static __device__ void peer_exchange(const PeerSums& ps, double* sums, int C) {
-  __shared__ unsigned long long seq;
-  if (threadIdx.x == 0) seq = ++(*ps.seq);
-  __syncthreads();
-  const size_t slot_off = PEER_MAIL_HEADER + (size_t)(seq & 1) * ps.cmax * 2 * sizeof(double);
-  double* mine = reinterpret_cast<double*>(ps.mail[ps.rank] + slot_off);
-  for (int c = threadIdx.x; c < 2 * C; c += blockDim.x) mine[c] = sums[c];
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    st_release_sys(reinterpret_cast<unsigned long long*>(ps.mail[ps.rank]), seq);
-  }
-  if ((int)threadIdx.x < ps.world && (int)threadIdx.x != ps.rank) {
-    const unsigned long long* flag = reinterpret_cast<const unsigned long long*>(ps.mail[threadIdx.x]);
-    const unsigned long long t0 = gtimer();
-    while (ld_acquire_sys(flag) < seq) {
-      if (gtimer() - t0 > 5000000000ull) {
-        if (ps.dev_error) atomicOr(ps.dev_error, DEV_ERR_PEER);
-        break;
-      }
-    }
-  }
-  __syncthreads();
-  for (int c = threadIdx.x; c < 2 * C; c += blockDim.x) {
-    double t = 0.0;
-    for (int r = 0; r < ps.world; r++) {
-      const double* d = reinterpret_cast<const double*>(ps.mail[r] + slot_off);
-      t += r == ps.rank ? mine[c] : __ldcv(d + c);
-    }
-    sums[c] = t;
-  }
-}
-
 // The last CTA of a partial-sum launch to finish sums the [C][P][2]
 // partials in a fixed order (so the result is deterministic) and writes
 // sums[C][2]; with peers it then runs the cross-rank exchange; it finally
@@ -610,7 +557,7 @@ int bn_fwd_sums(rnn_ctx* ctx, const float* y, int n, int C, int hw, double* part
   if (vec4_ok(hw, (size_t)n * C * hw, {y})) {  // partials + last-CTA combine in one launch
     const PeerSums pv = (ps && ps->world > 1 && C <= ps->cmax) ? *ps : PeerSums{};
     bn_fwd_partial4_kernel<<<dim3(C, P), BN_NT, 0, ctx->stream>>>(reinterpret_cast<const float4*>(y), n, C,
-                                                                 hw / 4, P, part, ctx->counters, sums, pv);
+                                                                 hw / 4, P, part, ctx->counters + COUNTER_BN, sums, pv);
     RNN_CHECK_LAUNCH();
     if (reduced) *reduced = pv.world > 1;
     return RNN_OK;
@@ -680,10 +627,10 @@ int bn_bwd_sums(rnn_ctx* ctx, const float* dy, const float* y, const float* relu
     const PeerSums pv = (ps && ps->world > 1 && C <= ps->cmax) ? *ps : PeerSums{};
     if (relu_out)
       bn_bwd_partial4_kernel<true><<<dim3(C, P), BN_NT, 0, ctx->stream>>>(d4, y4, r4, n, C, hw / 4, P, mean,
-                                                                         invstd, part, ctx->counters, sums, pv);
+                                                                         invstd, part, ctx->counters + COUNTER_BN, sums, pv);
     else
       bn_bwd_partial4_kernel<false><<<dim3(C, P), BN_NT, 0, ctx->stream>>>(d4, y4, r4, n, C, hw / 4, P, mean,
-                                                                          invstd, part, ctx->counters, sums, pv);
+                                                                          invstd, part, ctx->counters + COUNTER_BN, sums, pv);
     RNN_CHECK_LAUNCH();
     if (reduced) *reduced = pv.world > 1;
     return RNN_OK;  // partials + last-CTA combine (+ cross-rank sum) in one launch

@@ -124,6 +124,21 @@ int ensure_aux(rnn_ctx* ctx, size_t bytes) {
   return RNN_OK;
 }
 
+int ensure_statp(rnn_ctx* ctx, size_t bytes) {
+  if (bytes <= ctx->statp_bytes) return RNN_OK;
+  size_t want = std::max(bytes, (size_t)1 << 20);
+  if (ctx->statp) {
+    RNN_CUDA(cudaStreamSynchronize(ctx->stream));
+    RNN_CUDA(cudaFree(ctx->statp));
+    ctx->statp = nullptr;
+    ctx->statp_bytes = 0;
+  }
+  RNN_CUDA(cudaMalloc(&ctx->statp, want));
+  ctx->statp_bytes = want;
+  ctx->mem_epoch++;
+  return RNN_OK;
+}
+
 int ensure_pack(rnn_ctx* ctx, size_t bytes) {
   if (bytes <= ctx->pack_bytes) return RNN_OK;
   size_t want = std::max(bytes, ctx->pack_bytes * 2);
@@ -195,6 +210,7 @@ extern "C" int rnn_ctx_destroy(rnn_ctx* ctx) {
   if (ctx->aux) cudaFree(ctx->aux);
   if (ctx->dev_error) cudaFree(ctx->dev_error);
   if (ctx->counters) cudaFree(ctx->counters);
+  if (ctx->statp) cudaFree(ctx->statp);
   if (ctx->own) cudaStreamDestroy(ctx->own);
   delete ctx;
   return RNN_OK;

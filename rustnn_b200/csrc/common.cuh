@@ -95,6 +95,9 @@ struct rnn_ctx {
   // GEMMs it issues use ws for their split-K partials
   void* aux = nullptr;
   size_t aux_bytes = 0;
+  // per-CTA partial sums of the convolution epilogues' BN statistics
+  void* statp = nullptr;
+  size_t statp_bytes = 0;
   // device counters for kernels whose last CTA finishes a reduction
   // (zeroed at creation; each such kernel leaves its slot at zero again)
   unsigned* counters = nullptr;
@@ -110,6 +113,10 @@ int ensure_ws(rnn_ctx* ctx, size_t bytes);
 int ensure_stage(rnn_ctx* ctx, size_t bytes);
 int ensure_pack(rnn_ctx* ctx, size_t bytes);
 int ensure_aux(rnn_ctx* ctx, size_t bytes);
+int ensure_statp(rnn_ctx* ctx, size_t bytes);
+// ctx->counters slots: 0 BatchNorm partial-sum kernels, 1 convolution
+// epilogue statistics
+constexpr int COUNTER_BN = 0, COUNTER_CONV_STATS = 1;
 
 // ---- CUDA-graph replay of a whole training step
 //

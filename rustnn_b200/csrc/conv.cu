@@ -11,6 +11,8 @@
 // layout [cout][cin][kh][kw] of nn.rs:116.  dgrad handles stride 2 by
 // testing divisibility of (i + pad - kh) by the stride (the transposed
 // convolution of scatter_span, conv.rs:124-165).
+#include "bn.cuh"
+#include "ew.cuh"
 #include "tc_launch.cuh"
 
 namespace rnn {
@@ -37,6 +39,55 @@ __device__ __forceinline__ void store_planes32(float* out, size_t o0, size_t pla
     for (int e = 0; e < 8; e++)
       if (g + e < nvalid) out[o0 + (size_t)(g + e) * plane] = acc ? add[e] + v[g + e] : v[g + e];
   }
+}
+
+// BatchNorm statistics of a forward convolution's output, summed in its
+// epilogue (the engine's STATS hook) so the BN layer that follows does not
+// re-read y: per-channel (sum y, sum y^2) in f64.
+struct ConvStatsDev {
+  double* part = nullptr;    // [gridDim.x][N][2] per-CTA partials; nullptr = off
+  unsigned* counter = nullptr;
+  double* sums = nullptr;    // [N][2] totals (over ranks when ps.world > 1)
+  PeerSums ps;
+};
+
+// After the CTA's last tile (all threads): fold the four epilogue warps'
+// sums of each column in order into this CTA's partial; the last CTA to
+// finish adds the partials in CTA order (deterministic), runs the
+// cross-rank exchange when there are peers, and rearms the counter.
+__device__ inline void conv_stats_flush(const double* sm, const ConvStatsDev& st, int N) {
+  for (int col = threadIdx.x; col < N; col += blockDim.x) {
+    const int c = col >> 5, l = col & 31;
+    double s = 0.0, q = 0.0;
+#pragma unroll
+    for (int w = 0; w < 4; w++) {
+      s += sm[(2 * c) * 128 + w * 32 + l];
+      q += sm[(2 * c + 1) * 128 + w * 32 + l];
+    }
+    st.part[((size_t)blockIdx.x * N + col) * 2] = s;
+    st.part[((size_t)blockIdx.x * N + col) * 2 + 1] = q;
+    __threadfence();
+  }
+  __shared__ bool last;
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(st.counter, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  for (int col = threadIdx.x; col < N; col += blockDim.x) {
+    double s = 0.0, q = 0.0;
+    for (unsigned p = 0; p < gridDim.x; p++) {
+      s += __ldcg(st.part + ((size_t)p * N + col) * 2);
+      q += __ldcg(st.part + ((size_t)p * N + col) * 2 + 1);
+    }
+    st.sums[col * 2] = s;
+    st.sums[col * 2 + 1] = q;
+  }
+  if (st.ps.world > 1) {
+    __syncthreads();
+    peer_exchange(st.ps, st.sums, N);
+  }
+  if (threadIdx.x == 0) *st.counter = 0u;
 }
 
 // ---------------------------------------------------------------- forward
@@ -285,10 +336,12 @@ struct ConvWgradProb {
 template <int KS, int BN>
 struct FastConvFwd {
   static constexpr bool B_BULK = true;
+  static constexpr bool STATS = true;
   static constexpr int KK = KS * KS;
   const float* x;
   float* y;
   const float* bpack;
+  ConvStatsDev st;
   ConvGeom g;
   int M, N;
   int CB;  // channel blocks of 32 per tap
@@ -332,6 +385,8 @@ struct FastConvFwd {
     const int img = row / ohw, rem = row - img * ohw;
     store_planes32(y, ((size_t)img * g.cout + col0) * ohw + rem, ohw, N - col0, v, acc);
   }
+  __device__ __forceinline__ bool stats_on() const { return st.part != nullptr; }
+  __device__ __forceinline__ void stats_flush(const double* sm) const { conv_stats_flush(sm, st, N); }
 };
 
 // B(co, k = tap*cin + ci) = W[co][ci][tap]
@@ -485,6 +540,7 @@ struct HaloConv3x3 {
   // the producers write the split A tile into tensor memory (tcgen05.st):
   // shared memory then carries only the halo and the B images
   static constexpr bool A_TMEM = HALO_A_TMEM;
+  static constexpr bool STATS = true;
   // float offset of halo row r, halo column x (0 .. HX-1) within a channel
   static __device__ __forceinline__ int pos(int r, int x) {
     if constexpr (PAIRS) return (r >> 1) * (2 * HX) + (x >> 2) * 8 + (r & 1) * 4 + (x & 3);
@@ -493,6 +549,7 @@ struct HaloConv3x3 {
   const float* src;  // [n][CS][H][W]
   float* out;        // [n][N][H][W]
   const float* bpack;
+  ConvStatsDev st;
   int CS, H;
   int M, N;
   int kblocks;
@@ -536,6 +593,8 @@ struct HaloConv3x3 {
     const int img = row / hw, rem = row - img * hw;
     store_planes32(out, ((size_t)img * N + col0) * hw + rem, hw, N - col0, v, acc);
   }
+  __device__ __forceinline__ bool stats_on() const { return st.part != nullptr; }
+  __device__ __forceinline__ void stats_flush(const double* sm) const { conv_stats_flush(sm, st, N); }
 };
 
 // K = (32-channel block, tap, channel) for the halo kernels.
@@ -935,8 +994,28 @@ static int check_geom(int n, int cin, int h, int w, int cout, int k, int stride,
   return RNN_OK;
 }
 
+// Arms the epilogue statistics of a forward problem when they were asked
+// for and one column tile covers every channel.
+template <class P>
+static int setup_stats(rnn_ctx* ctx, P& p, const Sched& s, ConvStats* stats) {
+  if (!stats || !stats->sums || s.n_tiles != 1) return RNN_OK;
+  const int grid = std::min(s.num_tiles, ctx->num_sms);
+  const size_t bytes = (size_t)grid * p.N * 2 * sizeof(double);
+  RNN_TRY(ensure_statp(ctx, bytes));
+  RNN_RANGE(stats->sums, (size_t)p.N * 2 * sizeof(double));
+  p.st.part = static_cast<double*>(ctx->statp);
+  p.st.counter = ctx->counters + COUNTER_CONV_STATS;
+  p.st.sums = stats->sums;
+  const PeerSums* ps = stats->ps;
+  p.st.ps = (ps && ps->world > 1 && p.N <= ps->cmax) ? *ps : PeerSums{};
+  stats->fused = true;
+  stats->reduced = p.st.ps.world > 1;
+  return RNN_OK;
+}
+
 template <int KS, int BN>
-static int fast_fwd(rnn_ctx* ctx, const float* x, const float* wt, float* y, const ConvGeom& g, bool acc) {
+static int fast_fwd(rnn_ctx* ctx, const float* x, const float* wt, float* y, const ConvGeom& g, bool acc,
+                    ConvStats* stats) {
   constexpr int KK = KS * KS;
   FastConvFwd<KS, BN> p;
   p.x = x; p.y = y; p.g = g; p.acc = acc ? 1 : 0; p.splits = 1;
@@ -950,6 +1029,7 @@ static int fast_fwd(rnn_ctx* ctx, const float* x, const float* wt, float* y, con
   RNN_RANGE(ctx->pack, bytes);
   PackFwdSrc src{wt, g.cout, g.cin, KK};
   RNN_TRY(launch_pack<BN>(ctx, src, s.n_tiles, p.kblocks, static_cast<float*>(ctx->pack)));
+  RNN_TRY(setup_stats(ctx, p, s, stats));
   return launch<BN>(ctx, p, s);
 }
 
@@ -987,7 +1067,7 @@ constexpr int HALO16_MAX_BN = 128;
 // dgrad: src = dY [n][cout], out = dX [n][cin].
 template <int BN, int W>
 static int halo_conv(rnn_ctx* ctx, const float* src, const float* wt, float* out, const ConvGeom& g, bool dgrad,
-                     bool acc) {
+                     bool acc, ConvStats* stats) {
   HaloConv3x3<BN, W> p;
   p.src = src; p.out = out;
   p.CS = dgrad ? g.cout : g.cin;
@@ -1008,12 +1088,13 @@ static int halo_conv(rnn_ctx* ctx, const float* src, const float* wt, float* out
   } else {
     PackHaloFwdSrc ps{wt, g.cout, g.cin};
     RNN_TRY(launch_pack<BN>(ctx, ps, s.n_tiles, p.kblocks, static_cast<float*>(ctx->pack)));
+    RNN_TRY(setup_stats(ctx, p, s, stats));
   }
   return launch<BN>(ctx, p, s);
 }
 
 static int halo_dispatch(rnn_ctx* ctx, const float* src, const float* wt, float* out, const ConvGeom& g,
-                         bool dgrad, bool acc) {
+                         bool dgrad, bool acc, ConvStats* stats = nullptr) {
   const int N = dgrad ? g.cin : g.cout;
   const int M = g.n * g.h * g.w;
   // 256-wide tiles leave no room for a ring next to the halo buffers
@@ -1022,15 +1103,15 @@ static int halo_dispatch(rnn_ctx* ctx, const float* src, const float* wt, float*
   if (g.w == 16) {
     if (bn > HALO16_MAX_BN) bn = HALO16_MAX_BN;
     switch (bn) {
-      case 32: return halo_conv<32, 16>(ctx, src, wt, out, g, dgrad, acc);
-      case 64: return halo_conv<64, 16>(ctx, src, wt, out, g, dgrad, acc);
-      default: return halo_conv<128, 16>(ctx, src, wt, out, g, dgrad, acc);
+      case 32: return halo_conv<32, 16>(ctx, src, wt, out, g, dgrad, acc, stats);
+      case 64: return halo_conv<64, 16>(ctx, src, wt, out, g, dgrad, acc, stats);
+      default: return halo_conv<128, 16>(ctx, src, wt, out, g, dgrad, acc, stats);
     }
   }
   switch (bn) {
-    case 32: return halo_conv<32, 32>(ctx, src, wt, out, g, dgrad, acc);
-    case 64: return halo_conv<64, 32>(ctx, src, wt, out, g, dgrad, acc);
-    default: return halo_conv<128, 32>(ctx, src, wt, out, g, dgrad, acc);
+    case 32: return halo_conv<32, 32>(ctx, src, wt, out, g, dgrad, acc, stats);
+    case 64: return halo_conv<64, 32>(ctx, src, wt, out, g, dgrad, acc, stats);
+    default: return halo_conv<128, 32>(ctx, src, wt, out, g, dgrad, acc, stats);
   }
 }
 
@@ -1096,7 +1177,8 @@ static int fast_dgrad_1x1_strided(rnn_ctx* ctx, const float* dy, const float* wt
 }
 
 int conv_fwd(rnn_ctx* ctx, const float* x, int n, int cin, int h, int w, const float* wt, int cout,
-             int k, int stride, int pad, float* y, bool acc) {
+             int k, int stride, int pad, float* y, bool acc, ConvStats* stats) {
+  if (stats) stats->fused = stats->reduced = false;
   ConvGeom g;
   RNN_TRY(check_geom(n, cin, h, w, cout, k, stride, pad, &g));
   if (n == 0) return RNN_OK;
@@ -1111,13 +1193,19 @@ int conv_fwd(rnn_ctx* ctx, const float* x, int n, int cin, int h, int w, const f
     p.splits = 1;
     p.w_vec = (K % 4 == 0) && ((reinterpret_cast<uintptr_t>(wt) & 15) == 0);
   };
-  if (halo_ok(cin, h, w, k, stride, pad, x)) return halo_dispatch(ctx, x, wt, y, g, false, acc);
+  if (halo_ok(cin, h, w, k, stride, pad, x)) return halo_dispatch(ctx, x, wt, y, g, false, acc, stats);
   if (cin % 32 == 0) {
     switch (bn) {
-      case 32: return k == 3 ? fast_fwd<3, 32>(ctx, x, wt, y, g, acc) : fast_fwd<1, 32>(ctx, x, wt, y, g, acc);
-      case 64: return k == 3 ? fast_fwd<3, 64>(ctx, x, wt, y, g, acc) : fast_fwd<1, 64>(ctx, x, wt, y, g, acc);
-      case 128: return k == 3 ? fast_fwd<3, 128>(ctx, x, wt, y, g, acc) : fast_fwd<1, 128>(ctx, x, wt, y, g, acc);
-      default: return k == 3 ? fast_fwd<3, 256>(ctx, x, wt, y, g, acc) : fast_fwd<1, 256>(ctx, x, wt, y, g, acc);
+      case 32:
+        return k == 3 ? fast_fwd<3, 32>(ctx, x, wt, y, g, acc, stats) : fast_fwd<1, 32>(ctx, x, wt, y, g, acc, stats);
+      case 64:
+        return k == 3 ? fast_fwd<3, 64>(ctx, x, wt, y, g, acc, stats) : fast_fwd<1, 64>(ctx, x, wt, y, g, acc, stats);
+      case 128:
+        return k == 3 ? fast_fwd<3, 128>(ctx, x, wt, y, g, acc, stats)
+                      : fast_fwd<1, 128>(ctx, x, wt, y, g, acc, stats);
+      default:
+        return k == 3 ? fast_fwd<3, 256>(ctx, x, wt, y, g, acc, stats)
+                      : fast_fwd<1, 256>(ctx, x, wt, y, g, acc, stats);
     }
   }
   if (k == 3) {

@@ -19,11 +19,22 @@ int softmax_ce(rnn_ctx* ctx, const float* logits, const uint32_t* labels, int n,
 int sgd_nesterov(rnn_ctx* ctx, float* v, float* g, float* m, const uint8_t* decay_mask, int decay_all, size_t n,
                  float lr, float mom, float wd, float gscale);
 
+struct PeerSums;
 namespace tc {
+// BatchNorm statistics requested from a forward convolution's epilogue:
+// with `sums` set, conv_fwd may fill it with per-channel (sum y, sum y^2)
+// of its output (over every rank when `ps` has peers) and sets `fused`;
+// `reduced` says the sums already cover all ranks.
+struct ConvStats {
+  double* sums = nullptr;
+  const PeerSums* ps = nullptr;
+  bool fused = false;
+  bool reduced = false;
+};
 int gemm_dev(rnn_ctx* ctx, int m, int n, int k, const float* a, bool at, const float* b, bool bt, float* c,
              bool acc, bool force_split);
 int conv_fwd(rnn_ctx* ctx, const float* x, int n, int cin, int h, int w, const float* wt, int cout, int k,
-             int stride, int pad, float* y, bool acc);
+             int stride, int pad, float* y, bool acc, ConvStats* stats = nullptr);
 int conv_dgrad(rnn_ctx* ctx, const float* dy, int n, int cin, int h, int w, const float* wt, int cout, int k,
                int stride, int pad, float* dx, bool acc);
 int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, int h, int w, int cout, int k,

@@ -31,6 +31,9 @@ struct BNL {
   size_t rm_off;        // running mean offset in the buffer array; rv follows
   float* mean = nullptr;
   float* invstd = nullptr;
+  // the statistics of the next forward pass were summed by the producing
+  // convolution's epilogue (over all ranks when pre_reduced)
+  bool pre = false, pre_reduced = false;
 };
 
 struct Block {
@@ -226,7 +229,12 @@ static int bn_forward(rnn_resnet* net, BNL& bn, const float* y, int n, int hw, b
   }
   BnScratch s = bn_scratch(net, n, bn.c);
   bool reduced = false;
-  RNN_TRY(bn_fwd_sums(ctx, y, n, bn.c, hw, s.part, s.sums, net->sync_bn ? &net->peer : nullptr, &reduced));
+  if (bn.pre) {
+    reduced = bn.pre_reduced;
+    bn.pre = false;
+  } else {
+    RNN_TRY(bn_fwd_sums(ctx, y, n, bn.c, hw, s.part, s.sums, net->sync_bn ? &net->peer : nullptr, &reduced));
+  }
   if (!reduced) RNN_TRY(allreduce_sums(net, s.sums, bn.c));
   const double count = (double)n * hw * (net->sync_bn ? net->world : 1);
   return bn_fwd_finish(ctx, y, n, bn.c, hw, count, s.sums, gamma, beta, rm, rv, 0.1f, 1e-5f, relu ? 1 : 0,
@@ -248,8 +256,18 @@ static int bn_backward(rnn_resnet* net, BNL& bn, const float* dy, const float* y
                        s.dgb, dx, net->g + bn.g_off, net->g + bn.b_off, pscale);
 }
 
-static int conv_forward(rnn_resnet* net, const ConvL& c, const float* x, int n, int h, int w, float* y) {
-  return tc::conv_fwd(net->ctx, x, n, c.cin, h, w, net->v + c.w_off, c.cout, c.k, c.stride, c.pad, y, false);
+// With `bn` (training), the convolution's epilogue also sums the BN
+// statistics of y where its kernel can (bn->pre says it did).
+static int conv_forward(rnn_resnet* net, const ConvL& c, const float* x, int n, int h, int w, float* y,
+                        BNL* bn = nullptr) {
+  if (!bn) return tc::conv_fwd(net->ctx, x, n, c.cin, h, w, net->v + c.w_off, c.cout, c.k, c.stride, c.pad, y, false);
+  tc::ConvStats st;
+  st.sums = bn_scratch(net, n, bn->c).sums;
+  st.ps = net->sync_bn ? &net->peer : nullptr;
+  RNN_TRY(tc::conv_fwd(net->ctx, x, n, c.cin, h, w, net->v + c.w_off, c.cout, c.k, c.stride, c.pad, y, false, &st));
+  bn->pre = st.fused;
+  bn->pre_reduced = st.reduced;
+  return RNN_OK;
 }
 
 // nn.rs:230-250: backward_w then dX
@@ -265,7 +283,7 @@ static int conv_backward(rnn_resnet* net, const ConvL& c, const float* x, const 
 static int resnet_forward(rnn_resnet* net, const float* x, int n, int h, int w, bool train, float* logits) {
   RNN_TRY(ensure_acts(net, n, h, w));
   // stem conv + BN + ReLU (model.rs:136)
-  RNN_TRY(conv_forward(net, net->stem, x, n, h, w, net->stem_y));
+  RNN_TRY(conv_forward(net, net->stem, x, n, h, w, net->stem_y, train ? &net->stem_bn : nullptr));
   RNN_TRY(bn_forward(net, net->stem_bn, net->stem_y, n, h * w, train, true, net->stem_out));
   const float* cur = net->stem_out;
   int ch = h, cw = w;
@@ -275,13 +293,13 @@ static int resnet_forward(rnn_resnet* net, const float* x, int n, int h, int w, 
     const int ohw = oh * ow;
     b.x_in = cur;
     b.n = n; b.h = ch; b.w = cw; b.oh = oh; b.ow = ow;
-    RNN_TRY(conv_forward(net, b.c1, cur, n, ch, cw, b.y1));
+    RNN_TRY(conv_forward(net, b.c1, cur, n, ch, cw, b.y1, train ? &b.b1 : nullptr));
     RNN_TRY(bn_forward(net, b.b1, b.y1, n, ohw, train, true, b.h1));
-    RNN_TRY(conv_forward(net, b.c2, b.h1, n, oh, ow, b.y2));
+    RNN_TRY(conv_forward(net, b.c2, b.h1, n, oh, ow, b.y2, train ? &b.b2 : nullptr));
     if (b.down) {
       // out = relu(bn2(y2) + bnd(yd)): bn2 first, then bnd joins it in place
       RNN_TRY(bn_forward(net, b.b2, b.y2, n, ohw, train, false, b.out));
-      RNN_TRY(conv_forward(net, b.cd, cur, n, ch, cw, b.yd));
+      RNN_TRY(conv_forward(net, b.cd, cur, n, ch, cw, b.yd, train ? &b.bd : nullptr));
       RNN_TRY(bn_forward(net, b.bd, b.yd, n, ohw, train, true, b.out, b.out));
     } else {
       RNN_TRY(bn_forward(net, b.b2, b.y2, n, ohw, train, true, b.out, cur));

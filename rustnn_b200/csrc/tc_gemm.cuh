@@ -429,12 +429,31 @@ struct ChunkProb : P {
 //        of row tile m_tile into buffer buf; producer thread ptid of npt
 //   void load_a_halo(uint32_t halo, int buf, const TS&, int tap, int gt, float (&v)[32]) const;
 template <class P, class = void>
-struct prob_extra {
+struct prob_halo {
   static constexpr int value = 0;
 };
 template <class P>
-struct prob_extra<P, std::void_t<decltype(P::HALO_BYTES)>> {
+struct prob_halo<P, std::void_t<decltype(P::HALO_BYTES)>> {
   static constexpr int value = P::HALO_BYTES;
+};
+// Problems with STATS = true can have the epilogue sum every output column
+// over the rows (f64, per CTA, in shared memory after the halo) and supply
+//   bool stats_on() const;                       runtime switch
+//   void stats_flush(const double* sm) const;    all threads, after the tiles
+// sm = [BN/32 chunks][2 (sum, sum of squares)][128 epilogue threads]
+template <class P, class = void>
+struct prob_stats {
+  static constexpr bool value = false;
+};
+template <class P>
+struct prob_stats<P, std::void_t<decltype(P::STATS)>> {
+  static constexpr bool value = P::STATS;
+};
+template <int BN>
+constexpr int stats_bytes() { return (BN / 32) * 2 * 128 * 8; }
+template <class P, int BN>
+struct prob_extra_bn {
+  static constexpr int value = prob_halo<P>::value + (prob_stats<P>::value ? stats_bytes<BN>() : 0);
 };
 // HALO problems may set A_TMEM: their producers write A into tensor memory.
 template <class P, class = void>
@@ -449,13 +468,58 @@ struct prob_atm<P, std::void_t<decltype(P::A_TMEM)>> {
 // ------------------------------------------------------------------ kernel
 
 template <class Prob, int BN>
-using CfgOf = Cfg<BN, prob_extra<Prob>::value, prob_atm<Prob>::value>;
+using CfgOf = Cfg<BN, prob_extra_bn<Prob, BN>::value, prob_atm<Prob>::value>;
+
+// Column sums over the warp's 32 rows: v holds this lane's row; lane l
+// returns (sum, sum of squares) of column l.  Recursive halving: at each of
+// the five levels a lane keeps the half of its columns that its lane bit
+// selects and adds the partner's copy; the first two levels in f32 (sums of
+// at most four rows), the last three in f64.
+__device__ __forceinline__ void warp_colsum2(const float (&v)[32], double& s_out, double& q_out) {
+  const int lane = threadIdx.x & 31;
+  float a[16], b[16];
+  {
+    const bool up = lane & 16;
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const float lo = v[i], hi = v[i + 16];
+      a[i] = (up ? hi : lo) + __shfl_xor_sync(0xffffffffu, up ? lo : hi, 16);
+      const float lo2 = lo * lo, hi2 = hi * hi;
+      b[i] = (up ? hi2 : lo2) + __shfl_xor_sync(0xffffffffu, up ? lo2 : hi2, 16);
+    }
+  }
+  double da[8], db[8];
+  {
+    const bool up = lane & 8;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const float ka = up ? a[i + 8] : a[i], sa = up ? a[i] : a[i + 8];
+      const float kb = up ? b[i + 8] : b[i], sb = up ? b[i] : b[i + 8];
+      da[i] = (double)ka + (double)__shfl_xor_sync(0xffffffffu, sa, 8);
+      db[i] = (double)kb + (double)__shfl_xor_sync(0xffffffffu, sb, 8);
+    }
+  }
+#pragma unroll
+  for (int k = 4; k >= 1; k >>= 1) {
+    const bool up = lane & k;
+#pragma unroll
+    for (int i = 0; i < k; i++) {
+      const double ka = up ? da[i + k] : da[i], sa = up ? da[i] : da[i + k];
+      const double kb = up ? db[i + k] : db[i], sb = up ? db[i] : db[i + k];
+      da[i] = ka + __shfl_xor_sync(0xffffffffu, sa, k);
+      db[i] = kb + __shfl_xor_sync(0xffffffffu, sb, k);
+    }
+  }
+  s_out = da[0];
+  q_out = db[0];
+}
 
 template <int BN, class Prob>
 __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
     tc3_gemm_kernel(const Prob prob, const Sched sched, int* dev_error) {
   using C = CfgOf<Prob, BN>;
-  constexpr bool HALO = C::EXTRA > 0;
+  constexpr bool HALO = prob_halo<Prob>::value > 0;
+  constexpr bool STATS = prob_stats<Prob>::value;
   static_assert(!C::ATM || Prob::B_BULK, "A in tensor memory needs a bulk-copied B");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte aligned operand ring
@@ -463,6 +527,8 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
   const uint32_t ring = (raw_addr + 1023u) & ~1023u;
   uint8_t* ring_ptr = smem_raw + (ring - raw_addr);
   const uint32_t halo = ring + C::STAGES * C::STAGE_BYTES;  // HALO problems' buffers
+  // STATS problems' per-thread column sums follow the halo
+  double* stats_sm = reinterpret_cast<double*>(ring_ptr + C::STAGES * C::STAGE_BYTES + prob_halo<Prob>::value);
   uint64_t* bars = reinterpret_cast<uint64_t*>(ring_ptr + C::STAGES * C::STAGE_BYTES + C::EXTRA);
   uint64_t* full = bars;                      // [STAGES] producers -> MMA
   uint64_t* empty = bars + C::STAGES;         // [STAGES] MMA commit -> producers
@@ -753,6 +819,13 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
   } else {
     // ---------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int et = (warp - C::FIRST_EPI_WARP) * 32 + lane;
+    bool stats = false;
+    if constexpr (STATS) {
+      stats = prob.stats_on();
+      if (stats)
+        for (int c = 0; c < 2 * (BN / 32); c++) stats_sm[c * 128 + et] = 0.0;
+    }
     uint32_t tcount = 0;
     for (int tile = blockIdx.x; tile < sched.num_tiles; tile += gridDim.x, tcount++) {
       const int split = tile / tiles_mn;
@@ -776,6 +849,14 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
           for (int e = 0; e < 32; e++) v[e] += w[e];
         }
         prob.store(row, nt * BN + c * 32, split, v);
+        if constexpr (STATS) {
+          if (stats) {
+            double cs, cq;
+            warp_colsum2(v, cs, cq);
+            stats_sm[(2 * c) * 128 + et] += cs;
+            stats_sm[(2 * c + 1) * 128 + et] += cq;
+          }
+        }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
@@ -786,6 +867,9 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == C::MMA_WARP) tmem_dealloc(tmem_base, C::TMEM_COLS);
+  if constexpr (STATS) {
+    if (prob.stats_on()) prob.stats_flush(stats_sm);
+  }
 }
 
 // ------------------------------------------------------------------ packing
