@@ -14,6 +14,7 @@
 #include <initializer_list>
 
 #include "bn.cuh"
+#include "tc_gemm.cuh"
 
 namespace rnn {
 
@@ -435,7 +436,8 @@ __global__ void __launch_bounds__(256) bn_dx4_fin_kernel(const float4* __restric
                                                          const float* __restrict__ invstd,
                                                          const double* __restrict__ sums,
                                                          float* __restrict__ dgamma, float* __restrict__ dbeta,
-                                                         float pscale, float4* __restrict__ dx) {
+                                                         float pscale, float4* __restrict__ dx,
+                                                         char* __restrict__ pack, int pack_bn) {
   extern __shared__ float sh[];
   float* sdg = sh;
   float* sdb = sh + C;
@@ -483,6 +485,25 @@ __global__ void __launch_bounds__(256) bn_dx4_fin_kernel(const float4* __restric
         o[e] = s * (m * dd[e] - dbc - xh * dgc);
       }
       dx[jj] = make_float4(o[0], o[1], o[2], o[3]);
+      if (pack) {
+        // the 4 pixels are one 16-byte chunk of row c of the wgrad's B
+        // image for K block p / 32 (hi tile, then lo tile; SWIZZLE_128B)
+        const unsigned chw4 = (unsigned)C * hw4;
+        const unsigned img = jj / chw4, pix = (jj % hw4) * 4;
+        const size_t p = (size_t)img * hw4 * 4 + pix;
+        const size_t kb = p >> 5;
+        const int ch = (int)((p & 31) >> 2);
+        char* tile = pack + kb * (size_t)(2 * pack_bn * 128);
+        const size_t off = (size_t)(c >> 3) * 1024 + (c & 7) * 128 + ((ch ^ (c & 7)) << 4);
+        float hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          hi[e] = tc::tf32_round(o[e]);
+          lo[e] = o[e] - hi[e];
+        }
+        *reinterpret_cast<float4*>(tile + off) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<float4*>(tile + (size_t)pack_bn * 128 + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+      }
     }
   }
 }
@@ -647,7 +668,8 @@ int bn_bwd_sums(rnn_ctx* ctx, const float* dy, const float* y, const float* relu
 int bn_bwd_finish(rnn_ctx* ctx, const float* dy, const float* y, const float* relu_out, int n, int C, int hw,
                   double count, const double* sums, const float* gamma, const float* mean,
                   const float* invstd, float* dgb /* [2C] scratch */, float* dx, float* dgamma,
-                  float* dbeta, float pscale) {
+                  float* dbeta, float pscale, float* pack, int pack_bn, bool* packed) {
+  if (packed) *packed = false;
   RNN_RANGE(sums, sizeof(double) * (size_t)C * 2);
   RNN_RANGE(dgb, sizeof(float) * (size_t)C * 2);
   if (dgamma) RNN_RANGE(dgamma, sizeof(float) * C);
@@ -660,16 +682,21 @@ int bn_bwd_finish(rnn_ctx* ctx, const float* dy, const float* y, const float* re
                  *r4 = reinterpret_cast<const float4*>(relu_out);
     const unsigned g = ew4_grid(total / 4, ctx->num_sms);
     const size_t shm = 2 * C * sizeof(float);
+    // the wgrad's B image of dx: one column tile of exactly C rows, whole
+    // 32-pixel K blocks
+    char* pk = (pack && pack_bn == C && total % (32 * (size_t)C) == 0) ? reinterpret_cast<char*>(pack) : nullptr;
+    if (pk) RNN_RANGE(pk, total * 2 * sizeof(float));
     if (relu_out)
       bn_dx4_fin_kernel<true><<<g, 256, shm, ctx->stream>>>(d4, y4, r4, C, (unsigned)(hw / 4), (unsigned)(total / 4),
                                                             (float)count, gamma, mean, invstd, sums, dgamma, dbeta,
-                                                            pscale, reinterpret_cast<float4*>(dx));
+                                                            pscale, reinterpret_cast<float4*>(dx), pk, pack_bn);
     else
       bn_dx4_fin_kernel<false><<<g, 256, shm, ctx->stream>>>(d4, y4, r4, C, (unsigned)(hw / 4),
                                                              (unsigned)(total / 4), (float)count, gamma, mean,
                                                              invstd, sums, dgamma, dbeta, pscale,
-                                                             reinterpret_cast<float4*>(dx));
+                                                             reinterpret_cast<float4*>(dx), pk, pack_bn);
     RNN_CHECK_LAUNCH();
+    if (packed) *packed = pk != nullptr;
     return RNN_OK;
   }
   bn_bwd_finalize_kernel<<<(C + 127) / 128, 128, 0, ctx->stream>>>(sums, C, dgb, dgb + C, dgamma, dbeta,

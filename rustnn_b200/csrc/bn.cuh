@@ -98,6 +98,9 @@ int bn_bwd_sums(rnn_ctx* ctx, const float* dy, const float* y, const float* relu
                 bool* reduced = nullptr);
 int bn_bwd_finish(rnn_ctx* ctx, const float* dy, const float* y, const float* relu_out, int n, int C, int hw,
                   double count, const double* sums, const float* gamma, const float* mean,
-                  const float* invstd, float* dgb, float* dx, float* dgamma, float* dbeta, float pscale);
+                  const float* invstd, float* dgb, float* dx, float* dgamma, float* dbeta, float pscale,
+                  float* pack = nullptr, int pack_bn = 0, bool* packed = nullptr);
+// With `pack` (pack_bn == C), dx is also written as the hi/lo B image a
+// 3x3 wgrad consumes (see tc::wgrad_dy_pack_bn); *packed says it was.
 
 }  // namespace rnn

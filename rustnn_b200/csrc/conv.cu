@@ -924,45 +924,52 @@ struct WgradLauncher {
   }
 };
 
-template <int KS, int BN>
-static int wgrad_packed(rnn_ctx* ctx, const float* x, const float* dy, float* dw, const ConvGeom& g, int M, int N,
-                        int K, int splits) {
-  FastConvWgradPacked<KS, BN> p;
-  p.x = x; p.dy = dy; p.dw = dw; p.ws = nullptr; p.g = g; p.M = M; p.N = N; p.K = K; p.splits = 1;
+// The packed dY image (B of the wgrad kernels): made here, or handed in by
+// the caller (`dy_packed`, written by the BatchNorm backward that produced
+// dY) when it has this tile width and one column tile.
+template <int BN, class P>
+static int wgrad_dy_image(rnn_ctx* ctx, P& p, const ConvGeom& g, int N, int K, const float* dy,
+                          const float* dy_packed) {
   p.kblocks = (K + BK - 1) / BK;
   const int n_tiles = (N + BN - 1) / BN;
   const size_t bytes = (size_t)n_tiles * p.kblocks * 2 * BN * BK * sizeof(float);
+  if (dy_packed) {
+    RNN_RANGE(dy_packed, bytes);
+    p.bpack = dy_packed;
+    return RNN_OK;
+  }
   RNN_TRY(ensure_pack(ctx, bytes));
   p.bpack = static_cast<const float*>(ctx->pack);
   RNN_RANGE(ctx->pack, bytes);
   PackWgradDySrc src{dy, g.cout, g.oh * g.ow, K};
-  RNN_TRY(launch_pack<BN>(ctx, src, n_tiles, p.kblocks, static_cast<float*>(ctx->pack)));
+  return launch_pack<BN>(ctx, src, n_tiles, p.kblocks, static_cast<float*>(ctx->pack));
+}
+
+template <int KS, int BN>
+static int wgrad_packed(rnn_ctx* ctx, const float* x, const float* dy, float* dw, const ConvGeom& g, int M, int N,
+                        int K, int splits, const float* dy_packed) {
+  FastConvWgradPacked<KS, BN> p;
+  p.x = x; p.dy = dy; p.dw = dw; p.ws = nullptr; p.g = g; p.M = M; p.N = N; p.K = K; p.splits = 1;
+  RNN_TRY(wgrad_dy_image<BN>(ctx, p, g, N, K, dy, dy_packed));
   return WgradLauncher<BN>::run(ctx, p, splits);
 }
 
 template <int BN, int W>
 static int wgrad_t(rnn_ctx* ctx, const float* x, const float* dy, float* dw, const ConvGeom& g, int M, int N,
-                   int K, int splits) {
+                   int K, int splits, const float* dy_packed) {
   FastConvWgradT<BN, W> p;
   p.x = x; p.dy = dy; p.dw = dw; p.ws = nullptr; p.g = g; p.M = M; p.N = N; p.K = K; p.splits = 1;
-  p.kblocks = (K + BK - 1) / BK;
-  const int n_tiles = (N + BN - 1) / BN;
-  const size_t bytes = (size_t)n_tiles * p.kblocks * 2 * BN * BK * sizeof(float);
-  RNN_TRY(ensure_pack(ctx, bytes));
-  p.bpack = static_cast<const float*>(ctx->pack);
-  RNN_RANGE(ctx->pack, bytes);
-  PackWgradDySrc src{dy, g.cout, g.oh * g.ow, K};
-  RNN_TRY(launch_pack<BN>(ctx, src, n_tiles, p.kblocks, static_cast<float*>(ctx->pack)));
+  RNN_TRY(wgrad_dy_image<BN>(ctx, p, g, N, K, dy, dy_packed));
   return WgradLauncher<BN>::run(ctx, p, splits);
 }
 
 template <int W>
 static int wgrad_t_bn(rnn_ctx* ctx, int bn, const float* x, const float* dy, float* dw, const ConvGeom& g, int M,
-                      int N, int K, int splits) {
+                      int N, int K, int splits, const float* dy_packed) {
   switch (bn) {
-    case 32: return wgrad_t<32, W>(ctx, x, dy, dw, g, M, N, K, splits);
-    case 64: return wgrad_t<64, W>(ctx, x, dy, dw, g, M, N, K, splits);
-    default: return wgrad_t<128, W>(ctx, x, dy, dw, g, M, N, K, splits);
+    case 32: return wgrad_t<32, W>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
+    case 64: return wgrad_t<64, W>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
+    default: return wgrad_t<128, W>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
   }
 }
 
@@ -1268,8 +1275,14 @@ int conv_dgrad(rnn_ctx* ctx, const float* dy, int n, int cin, int h, int w, cons
   return run_bn<ConvLauncher>(ctx, bn, p, 1);
 }
 
+int wgrad_dy_pack_bn(int n, int cout, int k, int oh, int ow, const void* dy) {
+  const int bn = cout <= 32 ? 32 : cout <= 64 ? 64 : cout <= 128 ? 128 : 256;
+  const bool packed = k == 3 && ow % 4 == 0 && (reinterpret_cast<uintptr_t>(dy) & 15) == 0 && bn >= WGRAD_PACK_MIN_BN;
+  return (packed && bn == cout && ((long)n * oh * ow) % BK == 0) ? bn : 0;
+}
+
 int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, int h, int w,
-               int cout, int k, int stride, int pad, float* dw, int force_splits) {
+               int cout, int k, int stride, int pad, float* dw, int force_splits, const float* dy_packed) {
   ConvGeom g;
   RNN_TRY(check_geom(n, cin, h, w, cout, k, stride, pad, &g));
   if (n == 0) return RNN_OK;
@@ -1296,16 +1309,16 @@ int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, in
     // 256-wide tiles leave no tensor memory for A next to their accumulators
     if (k == 3 && stride == 1 && pad == 1 && (h * w) % 32 == 0 && bn <= 128 &&
         (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
-      if (w == 32) return wgrad_t_bn<32>(ctx, bn, x, dy, dw, g, M, N, K, splits);
-      if (w == 16) return wgrad_t_bn<16>(ctx, bn, x, dy, dw, g, M, N, K, splits);
-      if (w == 8) return wgrad_t_bn<8>(ctx, bn, x, dy, dw, g, M, N, K, splits);
+      if (w == 32) return wgrad_t_bn<32>(ctx, bn, x, dy, dw, g, M, N, K, splits, dy_packed);
+      if (w == 16) return wgrad_t_bn<16>(ctx, bn, x, dy, dw, g, M, N, K, splits, dy_packed);
+      if (w == 8) return wgrad_t_bn<8>(ctx, bn, x, dy, dw, g, M, N, K, splits, dy_packed);
     }
     if (k == 3 && bn >= WGRAD_PACK_MIN_BN) {
       switch (bn) {
-        case 32: return wgrad_packed<3, 32>(ctx, x, dy, dw, g, M, N, K, splits);
-        case 64: return wgrad_packed<3, 64>(ctx, x, dy, dw, g, M, N, K, splits);
-        case 128: return wgrad_packed<3, 128>(ctx, x, dy, dw, g, M, N, K, splits);
-        default: return wgrad_packed<3, 256>(ctx, x, dy, dw, g, M, N, K, splits);
+        case 32: return wgrad_packed<3, 32>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
+        case 64: return wgrad_packed<3, 64>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
+        case 128: return wgrad_packed<3, 128>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
+        default: return wgrad_packed<3, 256>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
       }
     }
     if (k == 3) {

@@ -38,7 +38,11 @@ int conv_fwd(rnn_ctx* ctx, const float* x, int n, int cin, int h, int w, const f
 int conv_dgrad(rnn_ctx* ctx, const float* dy, int n, int cin, int h, int w, const float* wt, int cout, int k,
                int stride, int pad, float* dx, bool acc);
 int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, int h, int w, int cout, int k,
-               int stride, int pad, float* dw, int force_splits);
+               int stride, int pad, float* dw, int force_splits, const float* dy_packed = nullptr);
+// Tile width of the packed dY image conv_wgrad would build for these shapes
+// when a producer of dY may write it instead (one column tile, cout == the
+// tile width, 32-pixel K blocks); 0 when it would not use one.
+int wgrad_dy_pack_bn(int n, int cout, int k, int oh, int ow, const void* dy);
 }  // namespace tc
 
 }  // namespace rnn

@@ -241,9 +241,23 @@ static int bn_forward(rnn_resnet* net, BNL& bn, const float* y, int n, int hw, b
                        bn.mean, bn.invstd, out, res);
 }
 
+// With `consumer` (the 3x3 convolution whose wgrad reads dx next, whose
+// output rows are `ow` wide), dx is also written as that wgrad's packed B
+// image in ctx->pack when the shapes allow; *dx_packed returns it or null.
 static int bn_backward(rnn_resnet* net, BNL& bn, const float* dy, const float* y, const float* relu_out, int n,
-                       int hw, float* dx) {
+                       int hw, float* dx, const ConvL* consumer = nullptr, int ow = 0,
+                       const float** dx_packed = nullptr) {
   rnn_ctx* ctx = net->ctx;
+  float* pack = nullptr;
+  int pbn = 0;
+  if (consumer && dx_packed) {
+    *dx_packed = nullptr;
+    pbn = tc::wgrad_dy_pack_bn(n, consumer->cout, consumer->k, hw / ow, ow, dx);
+    if (pbn) {
+      RNN_TRY(ensure_pack(ctx, (size_t)n * bn.c * hw * 2 * sizeof(float)));
+      pack = static_cast<float*>(ctx->pack);
+    }
+  }
   BnScratch s = bn_scratch(net, n, bn.c);
   bool reduced = false;
   RNN_TRY(bn_bwd_sums(ctx, dy, y, relu_out, n, bn.c, hw, bn.mean, bn.invstd, s.part, s.sums,
@@ -252,8 +266,11 @@ static int bn_backward(rnn_resnet* net, BNL& bn, const float* dy, const float* y
   const bool sb = net->sync_bn && net->comm;
   const double count = (double)n * hw * (sb ? net->world : 1);
   const float pscale = sb ? 1.0f / (float)net->world : 1.0f;
-  return bn_bwd_finish(ctx, dy, y, relu_out, n, bn.c, hw, count, s.sums, net->v + bn.g_off, bn.mean, bn.invstd,
-                       s.dgb, dx, net->g + bn.g_off, net->g + bn.b_off, pscale);
+  bool packed = false;
+  RNN_TRY(bn_bwd_finish(ctx, dy, y, relu_out, n, bn.c, hw, count, s.sums, net->v + bn.g_off, bn.mean, bn.invstd,
+                        s.dgb, dx, net->g + bn.g_off, net->g + bn.b_off, pscale, pack, pbn, &packed));
+  if (dx_packed) *dx_packed = packed ? pack : nullptr;
+  return RNN_OK;
 }
 
 // With `bn` (training), the convolution's epilogue also sums the BN
@@ -272,8 +289,9 @@ static int conv_forward(rnn_resnet* net, const ConvL& c, const float* x, int n, 
 
 // nn.rs:230-250: backward_w then dX
 static int conv_backward(rnn_resnet* net, const ConvL& c, const float* x, const float* dy, int n, int h, int w,
-                         float* dx, bool dx_acc) {
-  RNN_TRY(tc::conv_wgrad(net->ctx, x, dy, n, c.cin, h, w, c.cout, c.k, c.stride, c.pad, net->g + c.w_off, 0));
+                         float* dx, bool dx_acc, const float* dy_packed = nullptr) {
+  RNN_TRY(tc::conv_wgrad(net->ctx, x, dy, n, c.cin, h, w, c.cout, c.k, c.stride, c.pad, net->g + c.w_off, 0,
+                         dy_packed));
   if (dx)
     RNN_TRY(tc::conv_dgrad(net->ctx, dy, n, c.cin, h, w, net->v + c.w_off, c.cout, c.k, c.stride, c.pad, dx,
                            dx_acc));
@@ -332,10 +350,12 @@ static int resnet_backward(rnn_resnet* net, const float* dlogits) {
     // model.rs:57-72
     // relu_back_ of the join (model.rs:59) is applied on the fly: every
     // consumer of d masks it with out > 0
-    RNN_TRY(bn_backward(net, b.b2, d, b.y2, b.out, n, ohw, t));
-    RNN_TRY(conv_backward(net, b.c2, b.h1, t, n, b.oh, b.ow, dmain, false));
-    RNN_TRY(bn_backward(net, b.b1, dmain, b.y1, b.h1, n, ohw, t));
-    RNN_TRY(conv_backward(net, b.c1, b.x_in, t, n, b.h, b.w, dx, false));
+    // the BN backward passes also write dY as the next wgrad's B image
+    const float* tp = nullptr;
+    RNN_TRY(bn_backward(net, b.b2, d, b.y2, b.out, n, ohw, t, &b.c2, b.ow, &tp));
+    RNN_TRY(conv_backward(net, b.c2, b.h1, t, n, b.oh, b.ow, dmain, false, tp));
+    RNN_TRY(bn_backward(net, b.b1, dmain, b.y1, b.h1, n, ohw, t, &b.c1, b.ow, &tp));
+    RNN_TRY(conv_backward(net, b.c1, b.x_in, t, n, b.h, b.w, dx, false, tp));
     if (b.down) {
       RNN_TRY(bn_backward(net, b.bd, d, b.yd, b.out, n, ohw, t));
       RNN_TRY(conv_backward(net, b.cd, b.x_in, t, n, b.h, b.w, dx, true));
@@ -350,8 +370,9 @@ static int resnet_backward(rnn_resnet* net, const float* dlogits) {
   // stem: relu_back, BN backward, dW only (model.rs:154-156)
   const int hw = net->h * net->w;
   float *d = G[id], *t = G[it];
-  RNN_TRY(bn_backward(net, net->stem_bn, d, net->stem_y, net->stem_out, n, hw, t));
-  RNN_TRY(conv_backward(net, net->stem, net->x_in, t, n, net->h, net->w, nullptr, false));
+  const float* tp = nullptr;
+  RNN_TRY(bn_backward(net, net->stem_bn, d, net->stem_y, net->stem_out, n, hw, t, &net->stem, net->w, &tp));
+  RNN_TRY(conv_backward(net, net->stem, net->x_in, t, n, net->h, net->w, nullptr, false, tp));
   return RNN_OK;
 }
 
