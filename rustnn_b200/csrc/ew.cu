@@ -161,21 +161,17 @@ __global__ void fc_fwd_kernel(const float* __restrict__ x, int n, int fin, int f
   if (l == 0) y[gw] = b[o] + s;
 }
 
-// dW[o,j] += sum_i dy[i,o] x[i,j]; db[o] += sum_i dy[i,o]  (nn.rs:524-539)
-__global__ void fc_bwd_w_kernel(const float* __restrict__ x, const float* __restrict__ dy, int n, int fin,
-                                int fout, float* __restrict__ dw, float* __restrict__ db) {
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx < fout * fin) {
-    const int o = idx / fin, j = idx - o * fin;
-    float s = 0.0f;
-    for (int i = 0; i < n; i++) s += dy[(size_t)i * fout + o] * x[(size_t)i * fin + j];
-    dw[idx] += s;
-  }
-  if (idx < fout) {
-    float s = 0.0f;
-    for (int i = 0; i < n; i++) s += dy[(size_t)i * fout + idx];
-    db[idx] += s;
-  }
+// Classifier backward (nn.rs:524-539): dW[o,j] += sum_i dy[i,o] x[i,j] runs
+// on the GEMM engine (fc_bwd); db[o] += sum_i dy[i,o] here, one warp per
+// output, lanes striding the batch, fixed-order shuffle reduction.
+__global__ void fc_bwd_b_kernel(const float* __restrict__ dy, int n, int fout, float* __restrict__ db) {
+  const int o = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, l = threadIdx.x & 31;
+  if (o >= fout) return;
+  float s = 0.0f;
+  for (int i = l; i < n; i += 32) s += dy[(size_t)i * fout + o];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (l == 0) db[o] += s;
 }
 
 // dx[i,j] = sum_o dy[i,o] w[o,j]  (nn.rs:541-557)
@@ -203,14 +199,15 @@ int fc_fwd(rnn_ctx* ctx, const float* x, int n, int fin, int fout, const float* 
 
 int fc_bwd(rnn_ctx* ctx, const float* x, const float* dy, int n, int fin, int fout, const float* w, float* dw,
            float* db, float* dx) {
-  const int nw = std::max(fout * fin, fout);
   RNN_RANGE(x, sizeof(float) * (size_t)n * fin);
   RNN_RANGE(dy, sizeof(float) * (size_t)n * fout);
   RNN_RANGE(w, sizeof(float) * (size_t)fout * fin);
   RNN_RANGE(dw, sizeof(float) * (size_t)fout * fin);
   RNN_RANGE(db, sizeof(float) * (size_t)fout);
   if (dx) RNN_RANGE(dx, sizeof(float) * (size_t)n * fin);
-  fc_bwd_w_kernel<<<(nw + 255) / 256, 256, 0, ctx->stream>>>(x, dy, n, fin, fout, dw, db);
+  // dW[fout][fin] += dy^T x on the tensor-core engine (nn.rs:524-539)
+  RNN_TRY(tc::gemm_dev(ctx, fout, fin, n, dy, true, x, false, dw, true, false));
+  fc_bwd_b_kernel<<<(fout * 32 + 255) / 256, 256, 0, ctx->stream>>>(dy, n, fout, db);
   RNN_CHECK_LAUNCH();
   if (dx) {
     fc_bwd_x_kernel<<<(n * fin + 255) / 256, 256, 0, ctx->stream>>>(dy, n, fin, fout, w, dx);

@@ -163,13 +163,28 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, float* __rest
     const int tr = (rows + 31) / 32, tcn = (cols + 31) / 32;
     for (int t = blockIdx.x; t < tr * tcn; t += gridDim.x) {
       const int r0 = (t % tr) * 32, c0 = (t / tr) * 32;
-      for (int e = threadIdx.x; e < 1024; e += blockDim.x) {
-        const int rr = e / 32, cc = e % 32;
-        const int r = r0 + rr, c = c0 + cc;
-        float s = 0.0f;
-        if (r < rows && c < cols)
-          for (int p = 0; p < splits; p++) s += ws[p * plane + (size_t)r * cols + c];
-        tile[rr][cc] = s;
+      // each of the 256 threads sums 4 elements of the tile together, so
+      // 4 (x 4 unrolled) independent partial loads are in flight at once;
+      // every element still adds its splits in order 0, 1, ...
+      float s[4];
+      size_t off[4];
+      bool in[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const int e = threadIdx.x + q * 256;
+        const int r = r0 + e / 32, c = c0 + e % 32;
+        in[q] = r < rows && c < cols;
+        off[q] = in[q] ? (size_t)r * cols + c : 0;
+        s[q] = 0.0f;
+      }
+#pragma unroll 4
+      for (int p = 0; p < splits; p++)
+#pragma unroll
+        for (int q = 0; q < 4; q++) s[q] += in[q] ? ws[p * plane + off[q]] : 0.0f;
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const int e = threadIdx.x + q * 256;
+        tile[e / 32][e % 32] = s[q];
       }
       __syncthreads();
       for (int e = threadIdx.x; e < 1024; e += blockDim.x) {
@@ -194,6 +209,7 @@ int launch_splitk_reduce(rnn_ctx* ctx, const float* ws, float* out, int rows, in
   if (transpose) grid = (unsigned)std::min<size_t>(((rows + 31) / 32) * (size_t)((cols + 31) / 32), 4096);
   else grid = (unsigned)std::min<size_t>((total + 255) / 256, (size_t)ctx->num_sms * 8);
   if (grid == 0) return RNN_OK;
+  // the transposed form assumes 256 threads (4 tile elements each)
   splitk_reduce_kernel<<<grid, 256, 0, ctx->stream>>>(ws, out, rows, cols, splits, acc ? 1 : 0,
                                                       transpose ? 1 : 0);
   RNN_CHECK_LAUNCH();
