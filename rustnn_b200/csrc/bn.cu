@@ -154,6 +154,25 @@ __global__ void __launch_bounds__(BN_NT) bn_bwd_partial_kernel(const float* __re
   block_sum2<BN_NT>(a, b, part + ((size_t)c * P + p) * 2);
 }
 
+// ReLU masks kept as bits (RELU mode 2): bit e of word e/32 is set where the
+// forward's ReLU output was > 0.  float4 index o covers bits 4*(o%8)..+3 of
+// word o/8.
+static __device__ __forceinline__ float4 mask4(const uint32_t* __restrict__ m, size_t o) {
+  const uint32_t w = __ldg(m + (o >> 3)) >> (4 * (unsigned)(o & 7));
+  return make_float4((w & 1u) ? 1.f : 0.f, (w & 2u) ? 1.f : 0.f, (w & 4u) ? 1.f : 0.f, (w & 8u) ? 1.f : 0.f);
+}
+
+// Writes the mask bits of float4 jj's four values (> 0) from a full warp
+// whose lanes hold consecutive jj: eight lanes share one word.
+static __device__ __forceinline__ void store_mask4(uint32_t* __restrict__ m, unsigned jj, const float (&o)[4]) {
+  uint32_t v = (o[0] > 0.f ? 1u : 0u) | (o[1] > 0.f ? 2u : 0u) | (o[2] > 0.f ? 4u : 0u) | (o[3] > 0.f ? 8u : 0u);
+  v <<= 4 * (jj & 7);
+  v |= __shfl_xor_sync(0xffffffffu, v, 1);
+  v |= __shfl_xor_sync(0xffffffffu, v, 2);
+  v |= __shfl_xor_sync(0xffffffffu, v, 4);
+  if ((jj & 7) == 0) m[jj >> 3] = v;
+}
+
 static __device__ __forceinline__ void bwd_acc(float d, float yv, float r, bool has_r, float mu, float is,
                                                double& a, double& b) {
   if (has_r && r <= 0.0f) d = 0.0f;
@@ -162,10 +181,12 @@ static __device__ __forceinline__ void bwd_acc(float d, float yv, float r, bool 
   b += (double)d;
 }
 
-template <bool RELU>
+// RELU: 0 no mask, 1 relu_out (float), 2 relu_mask (bits)
+template <int RELU>
 __global__ void __launch_bounds__(BN_NT) bn_bwd_partial4_kernel(const float4* __restrict__ dy,
                                                               const float4* __restrict__ y,
-                                                              const float4* __restrict__ relu_out, int n,
+                                                              const float4* __restrict__ relu_out,
+                                                              const uint32_t* __restrict__ relu_mask, int n,
                                                               int C, int hw4, int P,
                                                               const float* __restrict__ mean,
                                                               const float* __restrict__ invstd,
@@ -186,7 +207,8 @@ __global__ void __launch_bounds__(BN_NT) bn_bwd_partial4_kernel(const float4* __
         const size_t o = ((size_t)(i0 + img) * C + c) * hw4 + q;
         d[u] = __ldg(dy + o);
         v[u] = __ldg(y + o);
-        if (RELU) r[u] = __ldg(relu_out + o);
+        if (RELU == 1) r[u] = __ldg(relu_out + o);
+        if (RELU == 2) r[u] = mask4(relu_mask, o);
       } else {
         d[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         v[u] = make_float4(mu, mu, mu, mu);
@@ -274,7 +296,7 @@ __global__ void __launch_bounds__(256) bn_apply4_kernel(const float4* __restrict
                                                         const float* __restrict__ beta,
                                                         const float* __restrict__ mean,
                                                         const float* __restrict__ invstd, int relu,
-                                                        const float4* res, float4* out) {
+                                                        const float4* res, float4* out, uint32_t* mask_out) {
   const unsigned stride = gridDim.x * blockDim.x;
   for (unsigned j = blockIdx.x * blockDim.x + threadIdx.x; j < total4; j += stride * BN_U) {
     float4 v[BN_U];
@@ -305,13 +327,18 @@ __global__ void __launch_bounds__(256) bn_apply4_kernel(const float4* __restrict
         o.w = fmaxf(o.w, 0.0f);
       }
       out[jj] = o;
+      if (mask_out) {
+        const float m[4] = {o.x, o.y, o.z, o.w};
+        store_mask4(mask_out, jj, m);
+      }
     }
   }
 }
 
-template <bool RELU>
+template <int RELU>
 __global__ void __launch_bounds__(256) bn_dx4_kernel(const float4* __restrict__ dy, const float4* __restrict__ y,
-                                                     const float4* __restrict__ relu_out, int C, unsigned hw4,
+                                                     const float4* __restrict__ relu_out,
+                                                     const uint32_t* __restrict__ relu_mask, int C, unsigned hw4,
                                                      unsigned total4, float m, const float* __restrict__ gamma,
                                                      const float* __restrict__ mean,
                                                      const float* __restrict__ invstd,
@@ -326,7 +353,8 @@ __global__ void __launch_bounds__(256) bn_dx4_kernel(const float4* __restrict__ 
       if (jj < total4) {
         d[u] = __ldg(dy + jj);
         v[u] = __ldg(y + jj);
-        if (RELU) r[u] = __ldg(relu_out + jj);
+        if (RELU == 1) r[u] = __ldg(relu_out + jj);
+        if (RELU == 2) r[u] = mask4(relu_mask, jj);
       }
     }
 #pragma unroll
@@ -367,7 +395,7 @@ __global__ void __launch_bounds__(256) bn_apply4_fin_kernel(const float4* __rest
                                                             float* __restrict__ rvar, int relu,
                                                             float* __restrict__ mean_out,
                                                             float* __restrict__ invstd_out,
-                                                            const float4* res, float4* out) {
+                                                            const float4* res, float4* out, uint32_t* mask_out) {
   extern __shared__ float sh[];
   float* smu = sh;
   float* sis = sh + C;
@@ -421,16 +449,21 @@ __global__ void __launch_bounds__(256) bn_apply4_fin_kernel(const float4* __rest
         o.w = fmaxf(o.w, 0.0f);
       }
       out[jj] = o;
+      if (mask_out) {
+        const float m[4] = {o.x, o.y, o.z, o.w};
+        store_mask4(mask_out, jj, m);
+      }
     }
   }
 }
 
 // Fused backward finalize + dx (nn.rs:400-427): dgamma/dbeta sums from the
 // f64 sums in every CTA; CTA 0 adds them (scaled) into the gradients.
-template <bool RELU>
+template <int RELU>
 __global__ void __launch_bounds__(256) bn_dx4_fin_kernel(const float4* __restrict__ dy,
                                                          const float4* __restrict__ y,
-                                                         const float4* __restrict__ relu_out, int C, unsigned hw4,
+                                                         const float4* __restrict__ relu_out,
+                                                         const uint32_t* __restrict__ relu_mask, int C, unsigned hw4,
                                                          unsigned total4, float m, const float* __restrict__ gamma,
                                                          const float* __restrict__ mean,
                                                          const float* __restrict__ invstd,
@@ -460,7 +493,8 @@ __global__ void __launch_bounds__(256) bn_dx4_fin_kernel(const float4* __restric
       if (jj < total4) {
         d[u] = __ldg(dy + jj);
         v[u] = __ldg(y + jj);
-        if (RELU) r[u] = __ldg(relu_out + jj);
+        if (RELU == 1) r[u] = __ldg(relu_out + jj);
+        if (RELU == 2) r[u] = mask4(relu_mask, jj);
       }
     }
 #pragma unroll
@@ -592,7 +626,9 @@ int bn_fwd_sums(rnn_ctx* ctx, const float* y, int n, int C, int hw, double* part
 
 int bn_fwd_finish(rnn_ctx* ctx, const float* y, int n, int C, int hw, double count, const double* sums,
                   const float* gamma, const float* beta, float* rmean, float* rvar, float mom, float eps,
-                  int relu, float* mean, float* invstd, float* out, const float* res) {
+                  int relu, float* mean, float* invstd, float* out, const float* res, uint32_t* mask,
+                  bool* masked) {
+  if (masked) *masked = false;
   RNN_RANGE(sums, sizeof(double) * (size_t)C * 2);
   RNN_RANGE(mean, sizeof(float) * C);
   RNN_RANGE(invstd, sizeof(float) * C);
@@ -605,10 +641,14 @@ int bn_fwd_finish(rnn_ctx* ctx, const float* y, int n, int C, int hw, double cou
   if (res) RNN_RANGE(res, sizeof(float) * (size_t)n * C * hw);
   const size_t total = (size_t)n * C * hw;
   const float4* res4 = reinterpret_cast<const float4*>(res);
+  // ReLU mask bits: every warp of the vector kernels covers 32 whole float4s
+  uint32_t* mk = (mask && relu && total % 128 == 0 && vec4_ok(hw, total, {y, out, res})) ? mask : nullptr;
+  if (mk) RNN_RANGE(mk, total / 8);
+  if (masked) *masked = mk != nullptr;
   if (vec4_ok(hw, total, {y, out, res}) && C <= BN_FUSE_MAX_C) {  // finalize fused into the apply
     bn_apply4_fin_kernel<<<ew4_grid(total / 4, ctx->num_sms), 256, 2 * C * sizeof(float), ctx->stream>>>(
         reinterpret_cast<const float4*>(y), C, (unsigned)(hw / 4), (unsigned)(total / 4), gamma, beta, sums, count,
-        mom, eps, rmean, rvar, relu, mean, invstd, res4, reinterpret_cast<float4*>(out));
+        mom, eps, rmean, rvar, relu, mean, invstd, res4, reinterpret_cast<float4*>(out), mk);
     RNN_CHECK_LAUNCH();
     return RNN_OK;
   }
@@ -618,7 +658,7 @@ int bn_fwd_finish(rnn_ctx* ctx, const float* y, int n, int C, int hw, double cou
   if (vec4_ok(hw, total, {y, out, res}))
     bn_apply4_kernel<<<ew4_grid(total / 4, ctx->num_sms), 256, 0, ctx->stream>>>(
         reinterpret_cast<const float4*>(y), C, (unsigned)(hw / 4), (unsigned)(total / 4), gamma, beta, mean,
-        invstd, relu, res4, reinterpret_cast<float4*>(out));
+        invstd, relu, res4, reinterpret_cast<float4*>(out), mk);
   else
     bn_apply_kernel<<<ew_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(y, C, hw, total, gamma, beta,
                                                                             mean, invstd, relu, res, out);
@@ -628,7 +668,7 @@ int bn_fwd_finish(rnn_ctx* ctx, const float* y, int n, int C, int hw, double cou
 
 int bn_bwd_sums(rnn_ctx* ctx, const float* dy, const float* y, const float* relu_out, int n, int C, int hw,
                 const float* mean, const float* invstd, double* part, double* sums, const PeerSums* ps,
-                bool* reduced) {
+                bool* reduced, const uint32_t* relu_mask) {
   const int P = bn_parts(n, C, ctx->num_sms);
   if (reduced) *reduced = false;
   // the partials and the per-channel sums must not overlap (the combine
@@ -646,12 +686,18 @@ int bn_bwd_sums(rnn_ctx* ctx, const float* dy, const float* y, const float* relu
     const float4 *d4 = reinterpret_cast<const float4*>(dy), *y4 = reinterpret_cast<const float4*>(y),
                  *r4 = reinterpret_cast<const float4*>(relu_out);
     const PeerSums pv = (ps && ps->world > 1 && C <= ps->cmax) ? *ps : PeerSums{};
-    if (relu_out)
-      bn_bwd_partial4_kernel<true><<<dim3(C, P), BN_NT, 0, ctx->stream>>>(d4, y4, r4, n, C, hw / 4, P, mean,
-                                                                         invstd, part, ctx->counters + COUNTER_BN, sums, pv);
-    else
-      bn_bwd_partial4_kernel<false><<<dim3(C, P), BN_NT, 0, ctx->stream>>>(d4, y4, r4, n, C, hw / 4, P, mean,
-                                                                          invstd, part, ctx->counters + COUNTER_BN, sums, pv);
+    unsigned* cnt = ctx->counters + COUNTER_BN;
+    if (relu_mask) {
+      RNN_RANGE(relu_mask, (size_t)n * C * hw / 8);
+      bn_bwd_partial4_kernel<2><<<dim3(C, P), BN_NT, 0, ctx->stream>>>(d4, y4, r4, relu_mask, n, C, hw / 4, P,
+                                                                      mean, invstd, part, cnt, sums, pv);
+    } else if (relu_out) {
+      bn_bwd_partial4_kernel<1><<<dim3(C, P), BN_NT, 0, ctx->stream>>>(d4, y4, r4, nullptr, n, C, hw / 4, P,
+                                                                      mean, invstd, part, cnt, sums, pv);
+    } else {
+      bn_bwd_partial4_kernel<0><<<dim3(C, P), BN_NT, 0, ctx->stream>>>(d4, y4, r4, nullptr, n, C, hw / 4, P,
+                                                                      mean, invstd, part, cnt, sums, pv);
+    }
     RNN_CHECK_LAUNCH();
     if (reduced) *reduced = pv.world > 1;
     return RNN_OK;  // partials + last-CTA combine (+ cross-rank sum) in one launch
@@ -668,7 +714,8 @@ int bn_bwd_sums(rnn_ctx* ctx, const float* dy, const float* y, const float* relu
 int bn_bwd_finish(rnn_ctx* ctx, const float* dy, const float* y, const float* relu_out, int n, int C, int hw,
                   double count, const double* sums, const float* gamma, const float* mean,
                   const float* invstd, float* dgb /* [2C] scratch */, float* dx, float* dgamma,
-                  float* dbeta, float pscale, float* pack, int pack_bn, bool* packed) {
+                  float* dbeta, float pscale, float* pack, int pack_bn, bool* packed,
+                  const uint32_t* relu_mask) {
   if (packed) *packed = false;
   RNN_RANGE(sums, sizeof(double) * (size_t)C * 2);
   RNN_RANGE(dgb, sizeof(float) * (size_t)C * 2);
@@ -686,15 +733,22 @@ int bn_bwd_finish(rnn_ctx* ctx, const float* dy, const float* y, const float* re
     // 32-pixel K blocks
     char* pk = (pack && pack_bn == C && total % (32 * (size_t)C) == 0) ? reinterpret_cast<char*>(pack) : nullptr;
     if (pk) RNN_RANGE(pk, total * 2 * sizeof(float));
-    if (relu_out)
-      bn_dx4_fin_kernel<true><<<g, 256, shm, ctx->stream>>>(d4, y4, r4, C, (unsigned)(hw / 4), (unsigned)(total / 4),
-                                                            (float)count, gamma, mean, invstd, sums, dgamma, dbeta,
-                                                            pscale, reinterpret_cast<float4*>(dx), pk, pack_bn);
-    else
-      bn_dx4_fin_kernel<false><<<g, 256, shm, ctx->stream>>>(d4, y4, r4, C, (unsigned)(hw / 4),
-                                                             (unsigned)(total / 4), (float)count, gamma, mean,
-                                                             invstd, sums, dgamma, dbeta, pscale,
-                                                             reinterpret_cast<float4*>(dx), pk, pack_bn);
+    float4* dx4 = reinterpret_cast<float4*>(dx);
+    const unsigned hw4 = (unsigned)(hw / 4), t4 = (unsigned)(total / 4);
+    if (relu_mask) {
+      RNN_RANGE(relu_mask, total / 8);
+      bn_dx4_fin_kernel<2><<<g, 256, shm, ctx->stream>>>(d4, y4, r4, relu_mask, C, hw4, t4, (float)count, gamma,
+                                                         mean, invstd, sums, dgamma, dbeta, pscale, dx4, pk,
+                                                         pack_bn);
+    } else if (relu_out) {
+      bn_dx4_fin_kernel<1><<<g, 256, shm, ctx->stream>>>(d4, y4, r4, nullptr, C, hw4, t4, (float)count, gamma,
+                                                         mean, invstd, sums, dgamma, dbeta, pscale, dx4, pk,
+                                                         pack_bn);
+    } else {
+      bn_dx4_fin_kernel<0><<<g, 256, shm, ctx->stream>>>(d4, y4, r4, nullptr, C, hw4, t4, (float)count, gamma,
+                                                         mean, invstd, sums, dgamma, dbeta, pscale, dx4, pk,
+                                                         pack_bn);
+    }
     RNN_CHECK_LAUNCH();
     if (packed) *packed = pk != nullptr;
     return RNN_OK;
@@ -706,14 +760,18 @@ int bn_bwd_finish(rnn_ctx* ctx, const float* dy, const float* y, const float* re
     const float4 *d4 = reinterpret_cast<const float4*>(dy), *y4 = reinterpret_cast<const float4*>(y),
                  *r4 = reinterpret_cast<const float4*>(relu_out);
     const unsigned g = ew4_grid(total / 4, ctx->num_sms);
-    if (relu_out)
-      bn_dx4_kernel<true><<<g, 256, 0, ctx->stream>>>(d4, y4, r4, C, (unsigned)(hw / 4), (unsigned)(total / 4),
-                                                      (float)count, gamma, mean, invstd, dgb, dgb + C,
-                                                      reinterpret_cast<float4*>(dx));
+    if (relu_mask)
+      bn_dx4_kernel<2><<<g, 256, 0, ctx->stream>>>(d4, y4, r4, relu_mask, C, (unsigned)(hw / 4),
+                                                   (unsigned)(total / 4), (float)count, gamma, mean, invstd, dgb,
+                                                   dgb + C, reinterpret_cast<float4*>(dx));
+    else if (relu_out)
+      bn_dx4_kernel<1><<<g, 256, 0, ctx->stream>>>(d4, y4, r4, nullptr, C, (unsigned)(hw / 4),
+                                                   (unsigned)(total / 4), (float)count, gamma, mean, invstd, dgb,
+                                                   dgb + C, reinterpret_cast<float4*>(dx));
     else
-      bn_dx4_kernel<false><<<g, 256, 0, ctx->stream>>>(d4, y4, r4, C, (unsigned)(hw / 4), (unsigned)(total / 4),
-                                                       (float)count, gamma, mean, invstd, dgb, dgb + C,
-                                                       reinterpret_cast<float4*>(dx));
+      bn_dx4_kernel<0><<<g, 256, 0, ctx->stream>>>(d4, y4, r4, nullptr, C, (unsigned)(hw / 4),
+                                                   (unsigned)(total / 4), (float)count, gamma, mean, invstd, dgb,
+                                                   dgb + C, reinterpret_cast<float4*>(dx));
   } else {
     bn_dx_kernel<<<ew_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(
         dy, y, relu_out, C, hw, total, (float)count, gamma, mean, invstd, dgb, dgb + C, dx);

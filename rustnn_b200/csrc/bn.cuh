@@ -91,15 +91,21 @@ int bn_fwd_sums(rnn_ctx* ctx, const float* y, int n, int C, int hw, double* part
 // out = [relu](bn(y) [+ res]); res may alias out (the residual join of a block)
 int bn_fwd_finish(rnn_ctx* ctx, const float* y, int n, int C, int hw, double count, const double* sums,
                   const float* gamma, const float* beta, float* rmean, float* rvar, float mom, float eps,
-                  int relu, float* mean, float* invstd, float* out, const float* res = nullptr);
+                  int relu, float* mean, float* invstd, float* out, const float* res = nullptr,
+                  uint32_t* mask = nullptr, bool* masked = nullptr);
+// With `mask` (relu), the ReLU outcome is also stored as bits (bit e of word
+// e/32 set where out[e] > 0) when the shape allows; *masked says it was.
+// The backward calls below accept those bits (relu_mask) instead of
+// re-reading the float relu_out (which they still use as the fallback).
 // sums[c] = (sum dy*xhat, sum dy)
 int bn_bwd_sums(rnn_ctx* ctx, const float* dy, const float* y, const float* relu_out, int n, int C, int hw,
                 const float* mean, const float* invstd, double* part, double* sums, const PeerSums* ps = nullptr,
-                bool* reduced = nullptr);
+                bool* reduced = nullptr, const uint32_t* relu_mask = nullptr);
 int bn_bwd_finish(rnn_ctx* ctx, const float* dy, const float* y, const float* relu_out, int n, int C, int hw,
                   double count, const double* sums, const float* gamma, const float* mean,
                   const float* invstd, float* dgb, float* dx, float* dgamma, float* dbeta, float pscale,
-                  float* pack = nullptr, int pack_bn = 0, bool* packed = nullptr);
+                  float* pack = nullptr, int pack_bn = 0, bool* packed = nullptr,
+                  const uint32_t* relu_mask = nullptr);
 // With `pack` (pack_bn == C), dx is also written as the hi/lo B image a
 // 3x3 wgrad consumes (see tc::wgrad_dy_pack_bn); *packed says it was.
 

@@ -72,6 +72,24 @@ __global__ void add_masked_kernel(float* __restrict__ a, const float* __restrict
     a[i] += y[i] <= 0.0f ? 0.0f : b[i];
 }
 
+// a += (mask bit <= 0 ? 0 : b) with the ReLU outcome as bits (bit e of word
+// e/32); float4 i covers bits 4*(i%8)..+3 of word i/8
+__global__ void add_masked_bits_kernel(float* __restrict__ a, const float* __restrict__ b,
+                                       const uint32_t* __restrict__ m, size_t n4) {
+  float4* a4 = reinterpret_cast<float4*>(a);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+    const uint32_t w = __ldg(m + (i >> 3)) >> (4 * (unsigned)(i & 7));
+    float4 x = a4[i];
+    const float4 d = __ldg(b4 + i);
+    x.x += (w & 1u) ? d.x : 0.0f;
+    x.y += (w & 2u) ? d.y : 0.0f;
+    x.z += (w & 4u) ? d.z : 0.0f;
+    x.w += (w & 8u) ? d.w : 0.0f;
+    a4[i] = x;
+  }
+}
+
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 int relu_back(rnn_ctx* ctx, float* d, const float* y, size_t n) {
@@ -94,8 +112,16 @@ int add(rnn_ctx* ctx, float* a, const float* b, size_t n, bool relu) {
   return RNN_OK;
 }
 
-int add_masked(rnn_ctx* ctx, float* a, const float* b, const float* y, size_t n) {
+int add_masked(rnn_ctx* ctx, float* a, const float* b, const float* y, size_t n, const uint32_t* mask) {
   if (n == 0) return RNN_OK;
+  if (mask && n % 4 == 0 && al16(a) && al16(b)) {
+    RNN_RANGE(a, n * sizeof(float));
+    RNN_RANGE(b, n * sizeof(float));
+    RNN_RANGE(mask, (n + 7) / 8);
+    add_masked_bits_kernel<<<grid_for(n / 4 + 1, ctx->num_sms), 256, 0, ctx->stream>>>(a, b, mask, n / 4);
+    RNN_CHECK_LAUNCH();
+    return RNN_OK;
+  }
   RNN_REQUIRE(al16(a) && al16(b) && al16(y), "add_masked: pointers must be 16-byte aligned");
   RNN_RANGE(a, n * sizeof(float));
   RNN_RANGE(b, n * sizeof(float));

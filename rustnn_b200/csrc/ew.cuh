@@ -8,7 +8,8 @@ namespace rnn {
 int relu_back(rnn_ctx* ctx, float* d, const float* y, size_t n);
 int add(rnn_ctx* ctx, float* a, const float* b, size_t n, bool relu);
 // a += (y <= 0 ? 0 : b)
-int add_masked(rnn_ctx* ctx, float* a, const float* b, const float* y, size_t n);
+// (with `mask`, the ReLU outcome as bits instead of y: bit e of word e/32)
+int add_masked(rnn_ctx* ctx, float* a, const float* b, const float* y, size_t n, const uint32_t* mask = nullptr);
 int gap_fwd(rnn_ctx* ctx, const float* x, int nc, int hw, float* y);
 int gap_bwd(rnn_ctx* ctx, const float* dy, int nc, int hw, float* dx);
 int fc_fwd(rnn_ctx* ctx, const float* x, int n, int fin, int fout, const float* w, const float* b, float* y);

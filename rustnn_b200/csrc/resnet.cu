@@ -42,6 +42,9 @@ struct Block {
   bool down = false;
   int cin, cout, stride;
   float *y1 = nullptr, *h1 = nullptr, *y2 = nullptr, *yd = nullptr, *out = nullptr;
+  // ReLU outcomes of h1 and of the join as bits (valid when *_ok)
+  uint32_t *m1 = nullptr, *mout = nullptr;
+  bool m1_ok = false, mout_ok = false;
   const float* x_in = nullptr;
   int n = 0, h = 0, w = 0, oh = 0, ow = 0;
 };
@@ -69,6 +72,8 @@ struct rnn_resnet {
   float* bnstat = nullptr;  // mean/invstd arrays of every BN
   // activations
   int cap_n = 0, cap_h = 0, cap_w = 0;
+  uint32_t* stem_m = nullptr;  // ReLU outcome of stem_out as bits (valid when stem_m_ok)
+  bool stem_m_ok = false;
   float *stem_y = nullptr, *stem_out = nullptr, *pooled = nullptr, *logits = nullptr, *dlogits = nullptr,
         *dpool = nullptr;
   float* gbuf[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -112,7 +117,13 @@ static size_t bn_scratch_need(rnn_resnet* net, int n) {
 static void free_acts(rnn_resnet* net) {
   for (void* p : net->act_allocs) cudaFree(p);
   net->act_allocs.clear();
-  for (auto& b : net->blocks) b.y1 = b.h1 = b.y2 = b.yd = b.out = nullptr;
+  for (auto& b : net->blocks) {
+    b.y1 = b.h1 = b.y2 = b.yd = b.out = nullptr;
+    b.m1 = b.mout = nullptr;
+    b.m1_ok = b.mout_ok = false;
+  }
+  net->stem_m = nullptr;
+  net->stem_m_ok = false;
   net->stem_y = net->stem_out = net->pooled = net->logits = net->dlogits = net->dpool = nullptr;
   for (auto& p : net->gbuf) p = nullptr;
   net->scratch = nullptr;
@@ -130,6 +141,14 @@ static int alloc_f(rnn_resnet* net, float** p, size_t n) {
 }
 
 // (Re)allocates every activation for batch n at h x w input.
+// one bit per element, whole 32-bit words
+static int alloc_mask(rnn_resnet* net, uint32_t** p, size_t elems) {
+  float* f = nullptr;
+  RNN_TRY(alloc_f(net, &f, (elems + 31) / 32));
+  *p = reinterpret_cast<uint32_t*>(f);
+  return RNN_OK;
+}
+
 static int ensure_acts(rnn_resnet* net, int n, int h, int w) {
   if (n <= net->cap_n && h == net->cap_h && w == net->cap_w) return RNN_OK;
   RNN_CUDA(cudaStreamSynchronize(net->ctx->stream));
@@ -139,6 +158,7 @@ static int ensure_acts(rnn_resnet* net, int n, int h, int w) {
   size_t stem = (size_t)n * W * h * w;
   RNN_TRY(alloc_f(net, &net->stem_y, stem));
   RNN_TRY(alloc_f(net, &net->stem_out, stem));
+  RNN_TRY(alloc_mask(net, &net->stem_m, stem));
   size_t gmax = stem;
   int ch = h, cw = w;
   for (auto& b : net->blocks) {
@@ -148,6 +168,8 @@ static int ensure_acts(rnn_resnet* net, int n, int h, int w) {
     RNN_TRY(alloc_f(net, &b.h1, no));
     RNN_TRY(alloc_f(net, &b.y2, no));
     RNN_TRY(alloc_f(net, &b.out, no));
+    RNN_TRY(alloc_mask(net, &b.m1, no));
+    RNN_TRY(alloc_mask(net, &b.mout, no));
     if (b.down) RNN_TRY(alloc_f(net, &b.yd, no));
     gmax = std::max(gmax, no);
     gmax = std::max(gmax, (size_t)n * b.cin * ch * cw);
@@ -210,7 +232,8 @@ static int allreduce_sums(rnn_resnet* net, double* sums, int C) {
 // out = [relu](bn(y) [+ res]): with res the block's residual join
 // (model.rs:52-54, add_relu_) is fused into the normalisation pass.
 static int bn_forward(rnn_resnet* net, BNL& bn, const float* y, int n, int hw, bool train, bool relu,
-                      float* out, const float* res = nullptr) {
+                      float* out, const float* res = nullptr, uint32_t* mask = nullptr, bool* masked = nullptr) {
+  if (masked) *masked = false;
   rnn_ctx* ctx = net->ctx;
   float* gamma = net->v + bn.g_off;
   float* beta = net->v + bn.b_off;
@@ -238,7 +261,7 @@ static int bn_forward(rnn_resnet* net, BNL& bn, const float* y, int n, int hw, b
   if (!reduced) RNN_TRY(allreduce_sums(net, s.sums, bn.c));
   const double count = (double)n * hw * (net->sync_bn ? net->world : 1);
   return bn_fwd_finish(ctx, y, n, bn.c, hw, count, s.sums, gamma, beta, rm, rv, 0.1f, 1e-5f, relu ? 1 : 0,
-                       bn.mean, bn.invstd, out, res);
+                       bn.mean, bn.invstd, out, res, mask, masked);
 }
 
 // With `consumer` (the 3x3 convolution whose wgrad reads dx next, whose
@@ -246,7 +269,7 @@ static int bn_forward(rnn_resnet* net, BNL& bn, const float* y, int n, int hw, b
 // image in ctx->pack when the shapes allow; *dx_packed returns it or null.
 static int bn_backward(rnn_resnet* net, BNL& bn, const float* dy, const float* y, const float* relu_out, int n,
                        int hw, float* dx, const ConvL* consumer = nullptr, int ow = 0,
-                       const float** dx_packed = nullptr) {
+                       const float** dx_packed = nullptr, const uint32_t* relu_mask = nullptr) {
   rnn_ctx* ctx = net->ctx;
   float* pack = nullptr;
   int pbn = 0;
@@ -261,14 +284,14 @@ static int bn_backward(rnn_resnet* net, BNL& bn, const float* dy, const float* y
   BnScratch s = bn_scratch(net, n, bn.c);
   bool reduced = false;
   RNN_TRY(bn_bwd_sums(ctx, dy, y, relu_out, n, bn.c, hw, bn.mean, bn.invstd, s.part, s.sums,
-                      net->sync_bn ? &net->peer : nullptr, &reduced));
+                      net->sync_bn ? &net->peer : nullptr, &reduced, relu_mask));
   if (!reduced) RNN_TRY(allreduce_sums(net, s.sums, bn.c));
   const bool sb = net->sync_bn && net->comm;
   const double count = (double)n * hw * (sb ? net->world : 1);
   const float pscale = sb ? 1.0f / (float)net->world : 1.0f;
   bool packed = false;
   RNN_TRY(bn_bwd_finish(ctx, dy, y, relu_out, n, bn.c, hw, count, s.sums, net->v + bn.g_off, bn.mean, bn.invstd,
-                        s.dgb, dx, net->g + bn.g_off, net->g + bn.b_off, pscale, pack, pbn, &packed));
+                        s.dgb, dx, net->g + bn.g_off, net->g + bn.b_off, pscale, pack, pbn, &packed, relu_mask));
   if (dx_packed) *dx_packed = packed ? pack : nullptr;
   return RNN_OK;
 }
@@ -302,7 +325,8 @@ static int resnet_forward(rnn_resnet* net, const float* x, int n, int h, int w, 
   RNN_TRY(ensure_acts(net, n, h, w));
   // stem conv + BN + ReLU (model.rs:136)
   RNN_TRY(conv_forward(net, net->stem, x, n, h, w, net->stem_y, train ? &net->stem_bn : nullptr));
-  RNN_TRY(bn_forward(net, net->stem_bn, net->stem_y, n, h * w, train, true, net->stem_out));
+  RNN_TRY(bn_forward(net, net->stem_bn, net->stem_y, n, h * w, train, true, net->stem_out, nullptr, net->stem_m,
+                     &net->stem_m_ok));
   const float* cur = net->stem_out;
   int ch = h, cw = w;
   for (auto& b : net->blocks) {
@@ -312,15 +336,15 @@ static int resnet_forward(rnn_resnet* net, const float* x, int n, int h, int w, 
     b.x_in = cur;
     b.n = n; b.h = ch; b.w = cw; b.oh = oh; b.ow = ow;
     RNN_TRY(conv_forward(net, b.c1, cur, n, ch, cw, b.y1, train ? &b.b1 : nullptr));
-    RNN_TRY(bn_forward(net, b.b1, b.y1, n, ohw, train, true, b.h1));
+    RNN_TRY(bn_forward(net, b.b1, b.y1, n, ohw, train, true, b.h1, nullptr, b.m1, &b.m1_ok));
     RNN_TRY(conv_forward(net, b.c2, b.h1, n, oh, ow, b.y2, train ? &b.b2 : nullptr));
     if (b.down) {
       // out = relu(bn2(y2) + bnd(yd)): bn2 first, then bnd joins it in place
       RNN_TRY(bn_forward(net, b.b2, b.y2, n, ohw, train, false, b.out));
       RNN_TRY(conv_forward(net, b.cd, cur, n, ch, cw, b.yd, train ? &b.bd : nullptr));
-      RNN_TRY(bn_forward(net, b.bd, b.yd, n, ohw, train, true, b.out, b.out));
+      RNN_TRY(bn_forward(net, b.bd, b.yd, n, ohw, train, true, b.out, b.out, b.mout, &b.mout_ok));
     } else {
-      RNN_TRY(bn_forward(net, b.b2, b.y2, n, ohw, train, true, b.out, cur));
+      RNN_TRY(bn_forward(net, b.b2, b.y2, n, ohw, train, true, b.out, cur, b.mout, &b.mout_ok));
     }
     cur = b.out;
     ch = oh;
@@ -352,18 +376,20 @@ static int resnet_backward(rnn_resnet* net, const float* dlogits) {
     // consumer of d masks it with out > 0
     // the BN backward passes also write dY as the next wgrad's B image
     const float* tp = nullptr;
-    RNN_TRY(bn_backward(net, b.b2, d, b.y2, b.out, n, ohw, t, &b.c2, b.ow, &tp));
+    // the ReLU masks come as bits from the forward when it could store them
+    const uint32_t* mo = b.mout_ok ? b.mout : nullptr;
+    RNN_TRY(bn_backward(net, b.b2, d, b.y2, b.out, n, ohw, t, &b.c2, b.ow, &tp, mo));
     RNN_TRY(conv_backward(net, b.c2, b.h1, t, n, b.oh, b.ow, dmain, false, tp));
-    RNN_TRY(bn_backward(net, b.b1, dmain, b.y1, b.h1, n, ohw, t, &b.c1, b.ow, &tp));
+    RNN_TRY(bn_backward(net, b.b1, dmain, b.y1, b.h1, n, ohw, t, &b.c1, b.ow, &tp, b.m1_ok ? b.m1 : nullptr));
     RNN_TRY(conv_backward(net, b.c1, b.x_in, t, n, b.h, b.w, dx, false, tp));
     if (b.down) {
-      RNN_TRY(bn_backward(net, b.bd, d, b.yd, b.out, n, ohw, t));
+      RNN_TRY(bn_backward(net, b.bd, d, b.yd, b.out, n, ohw, t, nullptr, 0, nullptr, mo));
       RNN_TRY(conv_backward(net, b.cd, b.x_in, t, n, b.h, b.w, dx, true));
     } else {
       // identity shortcut: a separate streaming pass; joined in the dgrad
       // epilogue the loads of d and out stall the epilogue warps (measured
       // 2-3x the dgrad's own time)
-      RNN_TRY(add_masked(ctx, dx, d, b.out, (size_t)n * b.cin * b.h * b.w));
+      RNN_TRY(add_masked(ctx, dx, d, b.out, (size_t)n * b.cin * b.h * b.w, mo));
     }
     std::swap(id, idx);
   }
@@ -371,7 +397,8 @@ static int resnet_backward(rnn_resnet* net, const float* dlogits) {
   const int hw = net->h * net->w;
   float *d = G[id], *t = G[it];
   const float* tp = nullptr;
-  RNN_TRY(bn_backward(net, net->stem_bn, d, net->stem_y, net->stem_out, n, hw, t, &net->stem, net->w, &tp));
+  RNN_TRY(bn_backward(net, net->stem_bn, d, net->stem_y, net->stem_out, n, hw, t, &net->stem, net->w, &tp,
+                      net->stem_m_ok ? net->stem_m : nullptr));
   RNN_TRY(conv_backward(net, net->stem, net->x_in, t, n, net->h, net->w, nullptr, false, tp));
   return RNN_OK;
 }
