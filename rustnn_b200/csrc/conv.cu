@@ -822,9 +822,10 @@ struct FastConvWgradPacked : FastConvWgrad<KS> {
 // input rows, shifting by kw - 1 across neighbouring chunks (zero at the
 // row ends); the three kw rows of a (ci, kh) sit in adjacent lanes and read
 // the same addresses.  dY is pre-packed and bulk-copied as B.
-template <int BN, int W>
+template <int BN, int W, bool ATM = true>
 struct FastConvWgradT : FastConvWgradPacked<3, BN> {
-  static constexpr bool A_TMEM = true;
+  // A in tensor memory (ATM) unless the tile's accumulators fill it (BN 256)
+  static constexpr bool A_TMEM = ATM;
   static_assert(W == 8 || W == 16 || W == 32, "row widths");
   static constexpr int R = 32 / W;  // image rows per K block
   struct TS {
@@ -957,7 +958,7 @@ static int wgrad_packed(rnn_ctx* ctx, const float* x, const float* dy, float* dw
 template <int BN, int W>
 static int wgrad_t(rnn_ctx* ctx, const float* x, const float* dy, float* dw, const ConvGeom& g, int M, int N,
                    int K, int splits, const float* dy_packed) {
-  FastConvWgradT<BN, W> p;
+  FastConvWgradT<BN, W, (BN <= 128)> p;
   p.x = x; p.dy = dy; p.dw = dw; p.ws = nullptr; p.g = g; p.M = M; p.N = N; p.K = K; p.splits = 1;
   RNN_TRY(wgrad_dy_image<BN>(ctx, p, g, N, K, dy, dy_packed));
   return WgradLauncher<BN>::run(ctx, p, splits);
@@ -969,9 +970,13 @@ static int wgrad_t_bn(rnn_ctx* ctx, int bn, const float* x, const float* dy, flo
   switch (bn) {
     case 32: return wgrad_t<32, W>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
     case 64: return wgrad_t<64, W>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
-    default: return wgrad_t<128, W>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
+    case 128: return wgrad_t<128, W>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
+    default: return wgrad_t<256, W>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
   }
 }
+
+// Widest tile the thread-per-row wgrad gather serves.
+constexpr int WGRAD_T_MAX_BN = 256;
 
 // Tile widths from which wgrad pre-packs dY.  Measured at batch 1024: 64ch
 // 1.00 -> 0.91 ms, 128ch 0.63 -> 0.50, 256ch 0.55 -> 0.35 (pack included).
@@ -1305,9 +1310,10 @@ int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, in
     auto ffill = [&](auto& p) {
       p.x = x; p.dy = dy; p.dw = dw; p.ws = nullptr; p.g = g; p.M = M; p.N = N; p.K = K; p.splits = 1;
     };
-    // A in tensor memory: 3x3/s1/p1 over 8/16/32-wide rows, whole-row K blocks;
-    // 256-wide tiles leave no tensor memory for A next to their accumulators
-    if (k == 3 && stride == 1 && pad == 1 && (h * w) % 32 == 0 && bn <= 128 &&
+    // thread-per-row gather: 3x3/s1/p1 over 8/16/32-wide rows, whole-row K
+    // blocks; A in tensor memory up to 128-wide tiles (256-wide tiles'
+    // accumulators fill it, they keep A in shared memory)
+    if (k == 3 && stride == 1 && pad == 1 && (h * w) % 32 == 0 && bn <= WGRAD_T_MAX_BN &&
         (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
       if (w == 32) return wgrad_t_bn<32>(ctx, bn, x, dy, dw, g, M, N, K, splits, dy_packed);
       if (w == 16) return wgrad_t_bn<16>(ctx, bn, x, dy, dw, g, M, N, K, splits, dy_packed);
