@@ -978,9 +978,9 @@ static int wgrad_t_bn(rnn_ctx* ctx, int bn, const float* x, const float* dy, flo
 // Widest tile the thread-per-row wgrad gather serves.
 constexpr int WGRAD_T_MAX_BN = 256;
 
-// Tile widths from which wgrad pre-packs dY.  Measured at batch 1024: 64ch
-// 1.00 -> 0.91 ms, 128ch 0.63 -> 0.50, 256ch 0.55 -> 0.35 (pack included).
-constexpr int WGRAD_PACK_MIN_BN = 32;
+// Every 3x3 wgrad pre-packs dY (the B operand every row tile re-reads);
+// measured at batch 1024 against gathering it per tile: 64ch 1.00 -> 0.91
+// ms, 128ch 0.63 -> 0.50, 256ch 0.55 -> 0.35 (pack included).
 
 template <template <int> class L, class P>
 static int run_bn(rnn_ctx* ctx, int bn, const P& p, int splits) {
@@ -1282,7 +1282,7 @@ int conv_dgrad(rnn_ctx* ctx, const float* dy, int n, int cin, int h, int w, cons
 
 int wgrad_dy_pack_bn(int n, int cout, int k, int oh, int ow, const void* dy) {
   const int bn = cout <= 32 ? 32 : cout <= 64 ? 64 : cout <= 128 ? 128 : 256;
-  const bool packed = k == 3 && ow % 4 == 0 && (reinterpret_cast<uintptr_t>(dy) & 15) == 0 && bn >= WGRAD_PACK_MIN_BN;
+  const bool packed = k == 3 && ow % 4 == 0 && (reinterpret_cast<uintptr_t>(dy) & 15) == 0;
   return (packed && bn == cout && ((long)n * oh * ow) % BK == 0) ? bn : 0;
 }
 
@@ -1319,17 +1319,13 @@ int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, in
       if (w == 16) return wgrad_t_bn<16>(ctx, bn, x, dy, dw, g, M, N, K, splits, dy_packed);
       if (w == 8) return wgrad_t_bn<8>(ctx, bn, x, dy, dw, g, M, N, K, splits, dy_packed);
     }
-    if (k == 3 && bn >= WGRAD_PACK_MIN_BN) {
+    if (k == 3) {  // other 3x3 shapes (stride 2, other widths): 4 pixels x 8 rows per thread, dY packed
       switch (bn) {
         case 32: return wgrad_packed<3, 32>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
         case 64: return wgrad_packed<3, 64>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
         case 128: return wgrad_packed<3, 128>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
         default: return wgrad_packed<3, 256>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
       }
-    }
-    if (k == 3) {
-      FastConvWgrad<3> p; ffill(p);
-      return run_bn<WgradLauncher>(ctx, bn, p, splits);
     }
     FastConvWgrad<1> p; ffill(p);
     return run_bn<WgradLauncher>(ctx, bn, p, splits);
