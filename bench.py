@@ -11,6 +11,7 @@ forward + softmax_ce + backward + allreduce + SGD-Nesterov (train.rs:684-699).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config resnet56|resnet20|rustvit]
     python bench.py --impl reference ...   # the CPU reference arm
+    python bench.py --workload eval        # eval::resnet over a 10,000-image split
 
 --config rustvit (BASELINE config 4): the default rustvit (Cfg::default,
 6.37 M parameters) at batch 128 on one GPU; one step = Trainer::step
@@ -129,6 +130,32 @@ def cpu_oracle_images_per_sec(depth_n, width, n_img, steps, threads=None):
         net.train_step(x, labels, smooth=0.1, lr=0.2, mom=0.9, wd=5e-4)
     dt = time.perf_counter() - t0
     return n_img * steps / dt, cores, dt
+
+
+EVAL_IMAGES = 10_000  # the size of the CIFAR-100 test split the reference evaluates on
+EVAL_METRIC = "eval images/sec (forward train=false + softmax_ce over the test split)"
+
+
+def synthetic_dataset(n: int, seed: int):
+    """A CIFAR-shaped u8 dataset (data.rs:16-24): uniform bytes, labels 0..99."""
+    rs = np.random.default_rng(seed)
+    return (rs.integers(0, 256, size=n * 3 * 32 * 32, dtype=np.uint8),
+            rs.integers(0, NCLASS, size=n, dtype=np.uint8))
+
+
+def cpu_oracle_eval_images_per_sec(depth_n, width, n_img, batch, reps):
+    """eval::resnet of the C restatement on a bounded sample of the split."""
+    from oracle import oracle as O
+
+    cores = O.get_threads()
+    net = O.ResNet(depth_n, width, NCLASS, 0)
+    images, labels = synthetic_dataset(n_img, 2)
+    net.eval(images, labels, batch)  # warm-up
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        net.eval(images, labels, batch)
+    dt = time.perf_counter() - t0
+    return n_img * reps / dt, cores, dt
 
 
 VIT_BATCH = 128  # BASELINE config 4
@@ -276,6 +303,106 @@ def run_ours_vit(args):
         ips, cores, dt = cpu_oracle_vit_images_per_sec(4, 2)
         line["cpu_baseline"] = {"value": round(ips, 3), "unit": "images/s", "cores": cores, "kind": "port",
                                 "sample": "2 steps x 4 images of the rustvit step (oracle restatement)"}
+    print(json.dumps(line), flush=True)
+    net.close()
+    return 0
+
+
+def run_reference_eval(args, cfg_name):
+    depth_n, width, gbatch, cfg_idx = CONFIGS[cfg_name]
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    sample = int(os.environ.get("RNN_REF_SAMPLE", "16"))
+    ips, cores, dt = cpu_oracle_eval_images_per_sec(depth_n, width, sample, sample, max(1, args.steps))
+    line = {
+        "impl": "reference", "metric": EVAL_METRIC, "value": round(ips, 3), "unit": "images/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000 * dt / max(1, args.steps), 2), "higher_is_better": True, "scaling": "replicas",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"eval::resnet {cfg_name}-w{width}, {EVAL_IMAGES} images, batch {gbatch}",
+                   "sample_images": sample, "parallelism": "cpu-threads"},
+        "cpu_baseline": {"value": round(ips, 3), "unit": "images/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} passes of eval over {sample} images (C restatement, OpenMP)"},
+        "e2e": {"value": round(ips, 3), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours_eval(args, cfg_name):
+    """One step = eval::resnet over a {EVAL_IMAGES}-image split at the config's
+    batch.  value: dataset resident on the device (rnn_resnet_eval_dev);
+    e2e: host dataset copied in inside the timed region (rnn_resnet_eval)."""
+    import torch
+
+    depth_n, width, gbatch, cfg_idx = CONFIGS[cfg_name]
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1 and int(os.environ.get("RANK", "0")) != 0:
+        return 0  # evaluation is one process in the reference: replicas only
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    from rustnn_b200 import _lib, model
+
+    net = model.ResNet(depth_n, width, NCLASS, 0)
+    x_np, lab_np = synthetic_batch(gbatch, 100)
+    net.train_step(torch.from_numpy(x_np).cuda(), torch.from_numpy(lab_np.astype(np.int32)).cuda())
+    images, labels = synthetic_dataset(EVAL_IMAGES, 7)
+    images_d, labels_d = torch.from_numpy(images).cuda(), torch.from_numpy(labels).cuda()
+    s = torch.cuda.current_stream()
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(args.steps):
+            out = fn()
+        e1.record(s)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3, out
+
+    sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    sampler.start()
+    time.sleep(0.3)
+    l0 = _lib.lib().rnn_launch_count()
+    t, (loss, acc) = timed(lambda: net.eval(images_d, labels_d, gbatch))
+    launches = (_lib.lib().rnn_launch_count() - l0) // max(1, args.steps + args.warmup) * args.steps
+    clocks = sampler.stop()
+    pinned_i = torch.from_numpy(images).pin_memory().numpy()
+    pinned_l = torch.from_numpy(labels).pin_memory().numpy()
+    t_e2e, (loss_h, acc_h) = timed(lambda: net.eval(pinned_i, pinned_l, gbatch))
+    assert (loss_h, acc_h) == (loss, acc)
+    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    flops, ktimes = conv_kernel_roofline(None, torch, gbatch, peaks)
+    bf16 = peaks.get("bf16_tflops")
+    peak_src = "measured bf16 (MEASURED_PEAKS.json)"
+    if bf16 is None:
+        bf16, peak_src = 1590.0, "fallback bf16 1.59 PF/s"
+    achieved = flops / ktimes["conv_fwd"] / 1e12
+    trafb = read_traffic("conv_fwd")
+    line = {
+        "metric": EVAL_METRIC, "value": round(EVAL_IMAGES * args.steps / t, 2), "unit": "images/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * t / args.steps, 3),
+        "higher_is_better": True, "scaling": "replicas", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"eval::resnet {cfg_name}-w{width}, {EVAL_IMAGES} u8 images, batch {gbatch} "
+                               f"(BASELINE config {cfg_idx} model)",
+                   "image": "3x32x32 u8 CHW", "nclass": NCLASS,
+                   "l2": "no flush: one pass moves tens of GB of activations, far beyond the 126 MB L2"},
+        "e2e": {"value": round(EVAL_IMAGES * args.steps / t_e2e, 2), "unit": "images/s",
+                "h2d_bytes_per_step": int(images.nbytes + labels.nbytes), "d2h_bytes_per_step": 12},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor",
+                     "kernel": f"tc3_gemm HaloConv3x3<64,32> (conv_fwd) stage-1 3x3 64->64, batch {gbatch}",
+                     "achieved": round(achieved, 2), "peak": round(bf16, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / bf16, 4), "peak_note": peak_src,
+                     "traffic": None if trafb is None else round(trafb * gbatch)},
+        "clocks": clocks,
+        "loss": round(loss, 5), "acc": round(acc, 5),
+    }
+    if not args.no_cpu_baseline:
+        ips, cores, _ = cpu_oracle_eval_images_per_sec(depth_n, width, 16, 16, 2)
+        line["cpu_baseline"] = {"value": round(ips, 3), "unit": "images/s", "cores": cores, "kind": "port",
+                                "sample": "2 passes of eval over 16 images (C restatement)"}
     print(json.dumps(line), flush=True)
     net.close()
     return 0
@@ -498,11 +625,15 @@ def main():
     ap.add_argument("--local-bn", action="store_true", help="per-rank BN statistics instead of SyncBN")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch the step's kernels one by one (no CUDA graph)")
+    ap.add_argument("--workload", default="train", choices=["train", "eval"],
+                    help="eval: eval::resnet over a 10,000-image split instead of the training step")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.config == "rustvit":
         return run_reference_vit(args) if args.impl == "reference" else run_ours_vit(args)
+    if args.workload == "eval":
+        return run_reference_eval(args, args.config) if args.impl == "reference" else run_ours_eval(args, args.config)
     if args.impl == "reference":
         return run_reference(args, args.config)
     return run_ours(args, args.config)

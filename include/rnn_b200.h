@@ -433,6 +433,38 @@ int rnn_rustvit_train_step(rnn_rustvit *net, const float *x, const float *tf,
                            float clip, float ema, uint64_t drop_seed,
                            float *stats);
 
+/* ---- evaluation (data.rs:494-512, eval.rs:15-66) ------------------------ */
+/* A dataset is data::Dataset's images and fine labels (data.rs:16-24): len
+ * images of 3 x 32 x 32 bytes in CHW order, then len label bytes. */
+/* data::make_batch_eval (data.rs:494-512): images/labels/out/labels_out on
+ * the device; writes bs images from `start`, normalised per channel
+ * ((v / 255 - mean) / std, data.rs:95-98), mirrored left-right when flip, and
+ * their labels widened to u32. */
+int rnn_make_batch_eval_dev(rnn_ctx *ctx, const uint8_t *images,
+                            const uint8_t *labels, size_t start, int bs,
+                            int flip, float *out, uint32_t *labels_out);
+/* eval::resnet (eval.rs:41-43): batches of `batch` images, forward with
+ * train false (BatchNorm on running statistics), softmax_ce without
+ * smoothing; loss = sum(batch loss * bs) / len, acc = correct / len (host
+ * floats, NaN both when len == 0).  _dev takes the dataset on the device;
+ * the plain form copies a host dataset in first. */
+int rnn_resnet_eval_dev(rnn_resnet *net, const uint8_t *images,
+                        const uint8_t *labels, int len, int batch, float *loss,
+                        float *acc);
+int rnn_resnet_eval(rnn_resnet *net, const uint8_t *images,
+                    const uint8_t *labels, int len, int batch, float *loss,
+                    float *acc);
+/* eval::vit (eval.rs:47-66): exits off, forward with train false; with tta
+ * the logits of each batch and of its mirror are averaged (0.5 * (a + b)).
+ * use_ema evaluates the EMA weights, swapped in for the pass and out again
+ * (Trainer::eval_ema, train.rs:390-402).  The model's img must be 32. */
+int rnn_rustvit_eval_dev(rnn_rustvit *net, const uint8_t *images,
+                         const uint8_t *labels, int len, int batch, int tta,
+                         int use_ema, float *loss, float *acc);
+int rnn_rustvit_eval(rnn_rustvit *net, const uint8_t *images,
+                     const uint8_t *labels, int len, int batch, int tta,
+                     int use_ema, float *loss, float *acc);
+
 #ifdef __cplusplus
 }
 #endif

@@ -18,6 +18,7 @@ LIB_PATH = os.path.join(HERE, "librnn_oracle.so")
 
 _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _u32p = np.ctypeslib.ndpointer(dtype=np.uint32, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
 _i64p = np.ctypeslib.ndpointer(dtype=np.int64, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
 
@@ -88,6 +89,8 @@ def lib():
         "orc_resnet_step": (V, [P, F, F, F]),
         "orc_resnet_train_step": (F, [P, _f32p, _u32p, I, F, F, F, F, C.POINTER(C.c_int)]),
         "orc_resnet_flops": (U64, [P, I, I]),
+        "orc_make_batch_eval": (V, [_u8p, _u8p, Z, I, I, _f32p, _u32p]),
+        "orc_resnet_eval": (V, [P, _u8p, _u8p, I, I, _f32p]),
         "orc_rel_index": (I, [I, I, I, I, C.c_void_p]),
         "orc_attn_fwd": (V, [I, I, I, I, I, I, _u32p, I, _f32p, I, I, _f32p, I, I, I, _f32p, _f32p, _f32p, _f32p]),
         "orc_attn_bwd": (V, [I, I, I, I, I, _u32p, I, _f32p, I, I, _f32p, I, I, I, _f32p, _f32p, _f32p,
@@ -224,6 +227,23 @@ def bn_fwd_train(y, n, c, hw, gamma, beta, rmean, rvar, relu, mom=0.1, eps=1e-5)
     return out, xhat, invstd
 
 
+def bn_fwd_eval(y, n, c, hw, gamma, beta, rmean, rvar, relu, eps=1e-5):
+    """BatchNorm2d with running statistics (nn.rs:358-369); returns a new array."""
+    out = _f32(y).ravel().copy()
+    lib().orc_bn_fwd_eval(out, n, c, hw, _f32(gamma), _f32(beta), _f32(rmean), _f32(rvar), eps, int(relu))
+    return out
+
+
+def make_batch_eval(images, labels, start, bs, flip):
+    """data::make_batch_eval (data.rs:494-512): (x [bs*3072] f32, labels u32)."""
+    images = np.ascontiguousarray(images, dtype=np.uint8).ravel()
+    labels = np.ascontiguousarray(labels, dtype=np.uint8).ravel()
+    x = np.empty(bs * 3 * 32 * 32, np.float32)
+    lab = np.empty(bs, np.uint32)
+    lib().orc_make_batch_eval(images, labels, start, bs, int(flip), x, lab)
+    return x, lab
+
+
 def bn_bwd(dy, xhat, n, c, hw, gamma, invstd, dgamma, dbeta):
     dx = np.empty(n * c * hw, np.float32)
     lib().orc_bn_bwd(_f32(dy).ravel(), _f32(xhat).ravel(), n, c, hw, _f32(gamma), _f32(invstd), dx, dgamma, dbeta)
@@ -314,6 +334,15 @@ class ResNet:
 
     def flops(self, h=32, w=32):
         return lib().orc_resnet_flops(self.h, h, w)
+
+    def eval(self, images, labels, batch):
+        """eval::resnet (eval.rs:41-43) over a u8 CHW dataset: (loss, accuracy)."""
+        assert batch > 0
+        images = np.ascontiguousarray(images, dtype=np.uint8).ravel()
+        labels = np.ascontiguousarray(labels, dtype=np.uint8).ravel()
+        out = np.empty(2, np.float32)
+        lib().orc_resnet_eval(self.h, images, labels, len(labels), batch, out)
+        return float(out[0]), float(out[1])
 
 
 # ---------------------------------------------------------------- attn.rs

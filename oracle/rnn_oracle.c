@@ -1000,6 +1000,63 @@ float orc_resnet_train_step(orc_resnet *net, const float *x, const uint32_t *lab
     return loss;
 }
 
+/* data.rs:13-14: CIFAR-100 channel mean and standard deviation */
+static const float EVAL_MEAN[3] = {0.5071f, 0.4865f, 0.4409f};
+static const float EVAL_STD[3] = {0.2673f, 0.2564f, 0.2762f};
+
+void orc_make_batch_eval(const uint8_t *images, const uint8_t *labels,
+                         size_t start, int bs, int flip, float *out,
+                         uint32_t *labels_out) {
+    /* data.rs:494-512; with no shift every source pixel is inside the image,
+     * so crop_flip_normalize (data.rs:331-360) is norm() of the (mirrored)
+     * column: (v / 255 - mean) / std in f32, data.rs:95-98 */
+    const int img = 32, pix = 3 * 32 * 32;
+    for (int b = 0; b < bs; b++) labels_out[b] = labels[start + (size_t)b];
+    for (int b = 0; b < bs; b++) {
+        const uint8_t *src = images + (start + (size_t)b) * pix;
+        float *dst = out + (size_t)b * pix;
+        for (int c = 0; c < 3; c++)
+            for (int y = 0; y < img; y++)
+                for (int x = 0; x < img; x++) {
+                    int sx = flip ? img - 1 - x : x;
+                    float v = (float)src[c * img * img + y * img + sx];
+                    dst[c * img * img + y * img + x] = (v / 255.0f - EVAL_MEAN[c]) / EVAL_STD[c];
+                }
+    }
+}
+
+void orc_resnet_eval(orc_resnet *net, const uint8_t *images,
+                     const uint8_t *labels, int len, int batch, float *out2) {
+    /* eval.rs:15-43 */
+    const int pix = 3 * 32 * 32;
+    float *x = (float *)malloc(sizeof(float) * (size_t)batch * pix);
+    uint32_t *lab = (uint32_t *)malloc(sizeof(uint32_t) * (size_t)batch);
+    float *lg = (float *)malloc(sizeof(float) * (size_t)batch * net->fout);
+    float *dl = (float *)malloc(sizeof(float) * (size_t)batch * net->fout);
+    float sum = 0.0f;
+    size_t correct = 0, seen = 0;
+    for (int s = 0; s < len;) {
+        int bs = batch < len - s ? batch : len - s;
+        orc_make_batch_eval(images, labels, (size_t)s, bs, 0, x, lab);
+        resnet_forward_hw(net, x, bs, 32, 32, 0, lg);
+        int c = 0;
+        float l = orc_softmax_ce(lg, lab, bs, net->fout, 0.0f, dl, &c);
+        /* sum += l * bs as f32: a rounded product, then the add (the Rust
+         * expression is not fused) */
+        volatile float prod = l * (float)bs;
+        sum += prod;
+        correct += (size_t)c;
+        seen += (size_t)bs;
+        s += bs;
+    }
+    out2[0] = sum / (float)seen;
+    out2[1] = (float)correct / (float)seen;
+    free(x);
+    free(lab);
+    free(lg);
+    free(dl);
+}
+
 uint64_t orc_resnet_flops(const orc_resnet *net, int h, int w) {
     /* model.rs:179-198 */
     uint64_t f = 0;

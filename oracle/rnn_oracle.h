@@ -125,6 +125,19 @@ float  orc_resnet_train_step(orc_resnet *net, const float *x,
 /* model.rs:179-198 */
 uint64_t orc_resnet_flops(const orc_resnet *net, int h, int w);
 
+/* ---- data.rs / eval.rs: evaluation batches and the eval loop ------------ */
+/* make_batch_eval (data.rs:494-512): bs images from `start` of a CHW u8
+ * dataset of 3 x 32 x 32 images, normalised per channel (data.rs:95-98),
+ * mirrored left-right when flip (crop_flip_normalize with no shift,
+ * data.rs:331-360); labels widened to u32. */
+void   orc_make_batch_eval(const uint8_t *images, const uint8_t *labels,
+                           size_t start, int bs, int flip, float *out,
+                           uint32_t *labels_out);
+/* eval::resnet (eval.rs:15-43): batches of `batch`, forward with train
+ * false, softmax_ce without smoothing; out2 = {mean loss, accuracy}. */
+void   orc_resnet_eval(orc_resnet *net, const uint8_t *images,
+                       const uint8_t *labels, int len, int batch, float *out2);
+
 /* ---- attn.rs ------------------------------------------------------------ */
 /* rel_index (attn.rs:53-72): writes th*tw*mh*mw indices when idx != NULL,
  * returns nrel = span_y * span_x (attn.rs:23-46). */

@@ -117,7 +117,9 @@ class BatchNorm2d:
         self.rv = np.ones(c, F32)
         self.c = c
 
-    def forward(self, y, n, hw, relu):
+    def forward(self, y, n, hw, relu, train=True):
+        if not train:  # running statistics (nn.rs:358-369)
+            return O.bn_fwd_eval(y, n, self.c, hw, self.g.v, self.b.v, self.rm, self.rv, relu)
         out, self.xhat, self.invstd = O.bn_fwd_train(y, n, self.c, hw, self.g.v, self.b.v, self.rm, self.rv, relu)
         self.n, self.hw = n, hw
         return out
@@ -152,14 +154,14 @@ class BasicBlock:
         self.down = (Conv2d(cin, cout, 1, stride, 0, rng), BatchNorm2d(cout)) if (stride != 1 or cin != cout) else None
         self.cout = cout
 
-    def forward(self, x, n, h, w):
+    def forward(self, x, n, h, w, train=True):
         y1 = self.c1.forward(x, n, h, w)
         oh = self.c1.out_hw(h)
-        hh = self.b1.forward(y1, n, oh * oh, True)
-        y = self.b2.forward(self.c2.forward(hh, n, oh, oh), n, oh * oh, False)
+        hh = self.b1.forward(y1, n, oh * oh, True, train)
+        y = self.b2.forward(self.c2.forward(hh, n, oh, oh), n, oh * oh, False, train)
         if self.down is not None:
             c, b = self.down
-            s = b.forward(c.forward(x, n, h, w), n, oh * oh, False)
+            s = b.forward(c.forward(x, n, h, w), n, oh * oh, False, train)
         else:
             s = x
         _L().orc_add_relu(y, O._f32(s), y.size)
@@ -675,15 +677,15 @@ class RustViT:
     def forward(self, x, n, train=True):
         cfg, d = self.cfg, self.cfg.dim
         img, th, mh = cfg.img, self.th, self.mh
-        h = self.stem_bn.forward(self.stem.forward(x, n, img, img), n, img * img, True)
+        h = self.stem_bn.forward(self.stem.forward(x, n, img, img), n, img * img, True, train)
         self.stem_out = h
-        h = self.c1.forward(h, n, img, img)
-        h = self.c2.forward(h, n, img, img)
+        h = self.c1.forward(h, n, img, img, train)
+        h = self.c2.forward(h, n, img, img, train)
         self.c2_out = h
         cm = cfg.cmid
         memt = tok_from_nchw(self.memconv.forward(h, n, mh, mh), n, 2 * d, mh * mh)
         mem = self.memln.forward(memt, n * mh * mh)
-        t = self.tok_bn.forward(self.tokconv.forward(h, n, mh, mh), n, th * th, False)
+        t = self.tok_bn.forward(self.tokconv.forward(h, n, mh, mh), n, th * th, False, train)
         z = tok_from_nchw(t, n, d, th * th)
         seed = self.drop_seed
         for b in self.blocks3:
@@ -896,3 +898,33 @@ class Trainer:
         if self.ema is not None:
             self.ema.update(net.V)
         return total, ce, correct
+
+
+def eval_vit(net: RustViT, images, labels, batch, tta):
+    """eval::vit (eval.rs:47-66) over a u8 CHW dataset: the exits are off, each
+    batch runs forward with train false, and with tta its logits are averaged
+    with those of the mirrored batch, 0.5 * (a + b); softmax_ce without
+    smoothing, loss summed as l * bs in f32 (eval.rs:15-39).  Returns
+    (loss, accuracy)."""
+    assert batch > 0
+    exits = net.use_exits
+    net.use_exits = False
+    total = len(labels)
+    acc_sum, correct, seen, s = F32(0.0), 0, 0, 0
+    while s < total:
+        bs = min(batch, total - s)
+        x, lab = O.make_batch_eval(images, labels, s, bs, False)
+        lg = net.forward(x, bs, False)["logits"]
+        if tta:
+            xm, lab = O.make_batch_eval(images, labels, s, bs, True)
+            mirrored = net.forward(xm, bs, False)["logits"]
+            lg = (F32(0.5) * (lg + mirrored)).astype(F32)
+        loss, _, c = O.softmax_ce(lg, lab, net.nf, 0.0)
+        acc_sum = F32(acc_sum + F32(F32(loss) * F32(bs)))
+        correct += c
+        seen += bs
+        s += bs
+    net.use_exits = exits
+    if seen == 0:
+        return float("nan"), float("nan")
+    return float(acc_sum / F32(seen)), float(F32(correct) / F32(seen))

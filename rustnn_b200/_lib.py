@@ -147,6 +147,11 @@ SIGS = {
     "rnn_rustvit_backward_dev": [VIT, FP, FP, FP, FP, FP, FP, FP],
     "rnn_rustvit_train_step_dev": [VIT, FP, FP, FP, FP, FP, I, F, F, F, F, U64, FP],
     "rnn_rustvit_train_step": [VIT, FP, FP, FP, FP, FP, I, F, F, F, F, U64, FP],
+    "rnn_make_batch_eval_dev": [CTX, FP, FP, Z, I, I, FP, FP],
+    "rnn_resnet_eval_dev": [NET, FP, FP, I, I, FP, FP],
+    "rnn_resnet_eval": [NET, FP, FP, I, I, FP, FP],
+    "rnn_rustvit_eval_dev": [VIT, FP, FP, I, I, I, I, FP, FP],
+    "rnn_rustvit_eval": [VIT, FP, FP, I, I, I, I, FP, FP],
 }
 _RESTYPE = {"rnn_ctx_stream": P, "rnn_launch_count": C.c_ulonglong}
 

@@ -15,6 +15,7 @@
 #include <vector>
 
 #include "bn.cuh"
+#include "eval.cuh"
 #include "ew.cuh"
 #include "rng.h"
 
@@ -101,6 +102,8 @@ struct rnn_resnet {
   // CUDA-graph replay of the training step (rnn_resnet_set_graph)
   bool use_graph = false;
   rnn::StepGraph graph;
+  // evaluation buffers (rnn_resnet_eval)
+  rnn::EvalWs eval;
   unsigned long long act_epoch = 0;  // bumped when the activations are reallocated
 };
 
@@ -690,6 +693,7 @@ extern "C" int rnn_resnet_destroy(rnn_resnet* net) {
   net->graph.destroy();  // before the NCCL communicator its graph may hold
   peer_release(net);
   free_acts(net);
+  rnn::eval_ws_free(net->eval);
   cudaFree(net->v);
   cudaFree(net->g);
   cudaFree(net->m);
@@ -801,6 +805,40 @@ extern "C" int rnn_resnet_train_step(rnn_resnet* net, const float* x, const uint
   if (loss) *loss = l;
   if (correct) *correct = c;
   return RNN_OK;
+}
+
+// ---------------------------------------------------------------- eval
+
+// eval::resnet (eval.rs:41-43): forward with train false over the dataset
+static int resnet_eval(rnn_resnet* net, const uint8_t* images, const uint8_t* labels, int len, int batch,
+                       float* loss, float* acc) {
+  float out2[2];
+  RNN_TRY(rnn::eval_loop(net->ctx, net->eval, images, labels, len, batch, net->fout, false,
+                         [net](const float* x, int bs, const float** lg) {
+                           RNN_TRY(ensure_acts(net, bs, 32, 32));
+                           RNN_TRY(resnet_forward(net, x, bs, 32, 32, false, net->logits));
+                           *lg = net->logits;
+                           return (int)RNN_OK;
+                         },
+                         out2));
+  if (loss) *loss = out2[0];
+  if (acc) *acc = out2[1];
+  return RNN_OK;
+}
+
+extern "C" int rnn_resnet_eval_dev(rnn_resnet* net, const uint8_t* images, const uint8_t* labels, int len,
+                                   int batch, float* loss, float* acc) {
+  RNN_REQUIRE(net && (len == 0 || (images && labels)), "resnet_eval: null argument");
+  return resnet_eval(net, images, labels, len, batch, loss, acc);
+}
+
+extern "C" int rnn_resnet_eval(rnn_resnet* net, const uint8_t* images, const uint8_t* labels, int len, int batch,
+                               float* loss, float* acc) {
+  RNN_REQUIRE(net && (len == 0 || (images && labels)), "resnet_eval: null argument");
+  RNN_REQUIRE(len >= 0 && batch > 0, "resnet_eval: bad sizes");
+  const uint8_t *di = nullptr, *dl = nullptr;
+  if (len > 0) RNN_TRY(rnn::eval_ws_stage(net->eval, net->ctx, images, labels, len, &di, &dl));
+  return resnet_eval(net, di, dl, len, batch, loss, acc);
 }
 
 // ---------------------------------------------------------------- DP

@@ -22,6 +22,7 @@
 
 #include "../../include/rnn_b200.h"
 #include "common.cuh"
+#include "eval.cuh"
 #include "rng.h"
 
 namespace rnn {
@@ -295,6 +296,7 @@ struct rnn_rustvit {
   SeqPoolL pool, pool2;
   LinL head_coarse, head_resid, e1_fc, e1_hint, e2_fc, e2_hint;
   bool use_exits = true;
+  rnn::EvalWs eval;  // evaluation buffers (rnn_rustvit_eval)
   // optimiser state
   int opt_t = 0, ema_t = 0;
   bool ema_ready = false;
@@ -1128,6 +1130,7 @@ extern "C" int rnn_rustvit_destroy(rnn_rustvit* net) {
   // in any order): wait on the device, not on the context's stream
   cudaDeviceSynchronize();
   free_acts(net);
+  rnn::eval_ws_free(net->eval);
   for (void* p : {(void*)net->V, (void*)net->G, (void*)net->M, (void*)net->V2, (void*)net->E, (void*)net->B,
                   (void*)net->parent, (void*)net->st_x, (void*)net->st_tf, (void*)net->st_tc, (void*)net->st_hard})
     if (p) cudaFree(p);
@@ -1252,4 +1255,62 @@ extern "C" int rnn_rustvit_train_step(rnn_rustvit* net, const float* x, const fl
   RNN_CUDA(cudaMemcpyAsync(net->st_hard + n, hardc, n * sizeof(uint32_t), cudaMemcpyHostToDevice, s));
   return train_step(net, net->st_x, net->st_tf, net->st_tc, net->st_hard, net->st_hard + n, n, lr, wd, clip, ema,
                     drop_seed, stats);
+}
+
+// ---------------------------------------------------------------- eval
+
+namespace {
+
+// Trainer::eval_ema (train.rs:390-402) swaps the EMA weights in around the
+// evaluation; the flat parameter and EMA buffers have one layout and every
+// layer reads its weights through net->V, so the swap is an exchange of the
+// two pointers, undone when the guard leaves scope.
+struct EmaSwap {
+  rnn_rustvit* net;
+  bool on;
+  EmaSwap(rnn_rustvit* n, bool use) : net(n), on(use) {
+    if (on) std::swap(net->V, net->E);
+  }
+  ~EmaSwap() {
+    if (on) std::swap(net->V, net->E);
+  }
+};
+
+// eval::vit (eval.rs:47-66): exits off (they run only in training, vit.rs:539
+// and :565), forward with train false, test-time augmentation when tta
+int vit_eval(rnn_rustvit* net, const uint8_t* images, const uint8_t* labels, int len, int batch, bool tta,
+             bool use_ema, float* loss, float* acc) {
+  RNN_REQUIRE(net->cfg.img == 32, "rustvit_eval: the dataset images are 32x32, the model takes %d", net->cfg.img);
+  RNN_REQUIRE(!use_ema || net->ema_ready, "rustvit_eval: no EMA update has run");
+  float out2[2];
+  {
+    EmaSwap swap(net, use_ema);
+    RNN_TRY(rnn::eval_loop(net->ctx, net->eval, images, labels, len, batch, net->nf, tta,
+                           [net](const float* x, int bs, const float** lg) {
+                             RNN_TRY(forward(net, x, bs, false, 0));
+                             *lg = net->zl;
+                             return (int)RNN_OK;
+                           },
+                           out2));
+  }
+  if (loss) *loss = out2[0];
+  if (acc) *acc = out2[1];
+  return RNN_OK;
+}
+
+}  // namespace
+
+extern "C" int rnn_rustvit_eval_dev(rnn_rustvit* net, const uint8_t* images, const uint8_t* labels, int len,
+                                    int batch, int tta, int use_ema, float* loss, float* acc) {
+  RNN_REQUIRE(net && (len == 0 || (images && labels)), "rustvit_eval: null argument");
+  return vit_eval(net, images, labels, len, batch, tta != 0, use_ema != 0, loss, acc);
+}
+
+extern "C" int rnn_rustvit_eval(rnn_rustvit* net, const uint8_t* images, const uint8_t* labels, int len,
+                                int batch, int tta, int use_ema, float* loss, float* acc) {
+  RNN_REQUIRE(net && (len == 0 || (images && labels)), "rustvit_eval: null argument");
+  RNN_REQUIRE(len >= 0 && batch > 0, "rustvit_eval: bad sizes");
+  const uint8_t *di = nullptr, *dl = nullptr;
+  if (len > 0) RNN_TRY(rnn::eval_ws_stage(net->eval, net->ctx, images, labels, len, &di, &dl));
+  return vit_eval(net, di, dl, len, batch, tta != 0, use_ema != 0, loss, acc);
 }

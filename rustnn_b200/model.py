@@ -24,6 +24,16 @@ def dp_unique_id() -> bytes:
     return bytes(buf)
 
 
+def _addr(t):
+    if isinstance(t, np.ndarray):
+        return C.c_void_p(t.ctypes.data)
+    return C.c_void_p(t.data_ptr())
+
+
+def _numel(t):
+    return int(t.size) if isinstance(t, np.ndarray) else int(t.numel())
+
+
 class ResNet:
     def __init__(self, depth_n: int, width: int, nclass: int, seed: int, device: int | None = None):
         self.ctx = default_context(device)
@@ -119,6 +129,17 @@ class ResNet:
              C.c_void_p(labels.ctypes.data if isinstance(labels, np.ndarray) else labels.data_ptr()), len(labels),
              smooth, lr, mom, wd, C.c_void_p(C.addressof(loss)), C.c_void_p(C.addressof(corr)))
         return loss.value, corr.value
+
+    def eval(self, images, labels, batch: int):
+        """eval::resnet (eval.rs:41-43) over a u8 CHW dataset [len, 3, 32, 32]
+        with u8 labels: (mean loss, accuracy).  Device tensors are read in
+        place; host arrays go through the host tier (one copy in)."""
+        self.ctx.bind()
+        loss, acc = C.c_float(), C.c_float()
+        name = "rnn_resnet_eval_dev" if isinstance(labels, torch.Tensor) and labels.is_cuda else "rnn_resnet_eval"
+        call(name, self.h, _addr(images), _addr(labels), _numel(labels), batch,
+             C.c_void_p(C.addressof(loss)), C.c_void_p(C.addressof(acc)))
+        return loss.value, acc.value
 
     def dp_init(self, rank: int, world: int, uid: bytes, sync_bn: bool = True):
         buf = (C.c_ubyte * UID_BYTES).from_buffer_copy(uid)

@@ -172,6 +172,19 @@ class RustViT:
              hard.numel(), lr, wd, clip, ema, drop_seed & (2**64 - 1), _ptr(st) if stats else None)
         return (float(st[0]), float(st[1]), int(st[2])) if stats else None
 
+    def eval(self, images, labels, batch: int, tta: bool = False, use_ema: bool = False):
+        """eval::vit (eval.rs:47-66) over a u8 CHW dataset [len, 3, 32, 32]
+        with u8 labels: (mean loss, accuracy); use_ema evaluates the EMA
+        weights (Trainer::eval_ema, train.rs:390-402).  Device tensors are
+        read in place; host arrays go through the host tier."""
+        self.ctx.bind()
+        out = np.zeros(2, np.float32)
+        dev = isinstance(labels, torch.Tensor) and labels.is_cuda
+        n = int(labels.size) if isinstance(labels, np.ndarray) else int(labels.numel())
+        call("rnn_rustvit_eval_dev" if dev else "rnn_rustvit_eval", self.h, _ptr(images), _ptr(labels), n, batch,
+             int(bool(tta)), int(bool(use_ema)), _ptr(out[0:1]), _ptr(out[1:2]))
+        return float(out[0]), float(out[1])
+
     def train_step_host(self, x, tf, tc, hard, hardc, lr=6e-4, wd=0.06, clip=1.0, ema=0.9998, drop_seed=0):
         """The same step through the host tier of the C ABI (host batch arrays)."""
         self.ctx.bind()
