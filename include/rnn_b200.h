@@ -443,6 +443,29 @@ int rnn_rustvit_train_step(rnn_rustvit *net, const float *x, const float *tf,
 int rnn_make_batch_eval_dev(rnn_ctx *ctx, const uint8_t *images,
                             const uint8_t *labels, size_t start, int bs,
                             int flip, float *out, uint32_t *labels_out);
+/* data::make_batch_train (data.rs:384-412): images/labels (and coarse
+ * labels, nullable) of a dataset, idx [bs] (u32) its images to use, all on
+ * the device.  Augmentation = data::Aug (data.rs:281-293): RandAugment of
+ * ra_n ops (at most 8) at magnitude ra_mag (off at 0), crop offset within
+ * pad, flip, normalise, random erasing with probability `erase` of an
+ * erase_side square of normal noise.  Image b draws from
+ * Rng::new(seed ^ b * 0x9E3779B97F4A7C15) in the reference's order.
+ * out [bs, 3, 32, 32], labels_out / coarse_out (nullable) [bs] u32. */
+int rnn_make_batch_train_dev(rnn_ctx *ctx, const uint8_t *images,
+                             const uint8_t *labels, const uint8_t *coarse,
+                             const uint32_t *idx, int bs, int pad,
+                             float ra_mag, int ra_n, float erase,
+                             int erase_side, uint64_t seed, float *out,
+                             uint32_t *labels_out, uint32_t *coarse_out);
+/* data::mix_batch (data.rs:467-491) in place on the device batch x
+ * [bs, 3, 32, 32] (16-byte aligned): mixup or cutmix with a permutation of
+ * the batch, drawn from the caller's generator, rng_state = the four
+ * xoshiro256++ words of rng.rs's Rng (host, advanced in place).  perm and
+ * lam (host, [bs], nullable) receive the permutation and the per-image
+ * lambdas (1 = not mixed). */
+int rnn_mix_batch_dev(rnn_ctx *ctx, float *x, int bs, float alpha_mix,
+                      float alpha_cut, float sw, uint64_t *rng_state,
+                      uint32_t *perm, float *lam);
 /* eval::resnet (eval.rs:41-43): batches of `batch` images, forward with
  * train false (BatchNorm on running statistics), softmax_ce without
  * smoothing; loss = sum(batch loss * bs) / len, acc = correct / len (host

@@ -19,6 +19,7 @@ LIB_PATH = os.path.join(HERE, "librnn_oracle.so")
 _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _u32p = np.ctypeslib.ndpointer(dtype=np.uint32, flags="C_CONTIGUOUS")
 _u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+_u64p = np.ctypeslib.ndpointer(dtype=np.uint64, flags="C_CONTIGUOUS")
 _i64p = np.ctypeslib.ndpointer(dtype=np.int64, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
 
@@ -26,7 +27,8 @@ _i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
 def build(force: bool = False) -> str:
     """Compile the oracle with the recipe in ``oracle/Makefile``."""
     if force or not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < max(
-        os.path.getmtime(os.path.join(HERE, f)) for f in ("rnn_oracle.c", "rnn_oracle.h")
+        os.path.getmtime(os.path.join(HERE, f)) for f in ("rnn_oracle.c", "rnn_oracle_data.c", "rnn_oracle.h",
+                                                          "Makefile")
     ):
         subprocess.check_call(["make", "-s", "-C", HERE])
     return LIB_PATH
@@ -91,6 +93,9 @@ def lib():
         "orc_resnet_flops": (U64, [P, I, I]),
         "orc_make_batch_eval": (V, [_u8p, _u8p, Z, I, I, _f32p, _u32p]),
         "orc_resnet_eval": (V, [P, _u8p, _u8p, I, I, _f32p]),
+        "orc_make_batch_train": (V, [_u8p, _u8p, C.c_void_p, _u32p, I, I, F, I, F, I, U64, _f32p, _u32p,
+                                     C.c_void_p]),
+        "orc_mix_batch": (I, [_f32p, I, F, F, F, _u64p, _u32p, _f32p, _i32p]),
         "orc_rel_index": (I, [I, I, I, I, C.c_void_p]),
         "orc_attn_fwd": (V, [I, I, I, I, I, I, _u32p, I, _f32p, I, I, _f32p, I, I, I, _f32p, _f32p, _f32p, _f32p]),
         "orc_attn_bwd": (V, [I, I, I, I, I, _u32p, I, _f32p, I, I, _f32p, I, I, I, _f32p, _f32p, _f32p,
@@ -166,6 +171,14 @@ class Rng:
         lib().orc_rand_vec(out, n, C.byref(self._s))
         return out
 
+    def state(self) -> np.ndarray:
+        """The xoshiro256++ state words (rng.rs:3-5)."""
+        return np.array(list(self._s.s), np.uint64)
+
+    def set_state(self, st) -> None:
+        for i in range(4):
+            self._s.s[i] = int(st[i])
+
 
 # ---------------------------------------------------------------- gemm.rs
 
@@ -232,6 +245,33 @@ def bn_fwd_eval(y, n, c, hw, gamma, beta, rmean, rvar, relu, eps=1e-5):
     out = _f32(y).ravel().copy()
     lib().orc_bn_fwd_eval(out, n, c, hw, _f32(gamma), _f32(beta), _f32(rmean), _f32(rvar), eps, int(relu))
     return out
+
+
+def make_batch_train(images, labels, coarse, idx, pad=4, ra_mag=0.0, ra_n=2, erase=0.0, erase_side=8, seed=0):
+    """data::make_batch_train (data.rs:384-412): (x [bs*3072] f32, labels u32,
+    coarse u32 or None)."""
+    images = np.ascontiguousarray(images, dtype=np.uint8).ravel()
+    labels = np.ascontiguousarray(labels, dtype=np.uint8).ravel()
+    idx = np.ascontiguousarray(idx, dtype=np.uint32).ravel()
+    bs = len(idx)
+    x = np.empty(bs * 3 * 32 * 32, np.float32)
+    lab = np.empty(bs, np.uint32)
+    cz = None if coarse is None else np.ascontiguousarray(coarse, dtype=np.uint8).ravel()
+    cout = None if coarse is None else np.empty(bs, np.uint32)
+    lib().orc_make_batch_train(images, labels, None if cz is None else cz.ctypes.data, idx, bs, pad, ra_mag, ra_n,
+                               erase, erase_side, seed & (2**64 - 1), x, lab,
+                               None if cout is None else cout.ctypes.data)
+    return x, lab, cout
+
+
+def mix_batch(x, bs, alpha_mix, alpha_cut, sw, state):
+    """data::mix_batch (data.rs:467-491) in place on x; state (uint64[4]) is the
+    caller's generator, advanced.  Returns (kind, perm, lam, rect)."""
+    perm = np.empty(bs, np.uint32)
+    lam = np.empty(bs, np.float32)
+    rect = np.zeros(4, np.int32)
+    kind = lib().orc_mix_batch(x, bs, alpha_mix, alpha_cut, sw, state, perm, lam, rect)
+    return kind, perm, lam, rect
 
 
 def make_batch_eval(images, labels, start, bs, flip):

@@ -1000,31 +1000,6 @@ float orc_resnet_train_step(orc_resnet *net, const float *x, const uint32_t *lab
     return loss;
 }
 
-/* data.rs:13-14: CIFAR-100 channel mean and standard deviation */
-static const float EVAL_MEAN[3] = {0.5071f, 0.4865f, 0.4409f};
-static const float EVAL_STD[3] = {0.2673f, 0.2564f, 0.2762f};
-
-void orc_make_batch_eval(const uint8_t *images, const uint8_t *labels,
-                         size_t start, int bs, int flip, float *out,
-                         uint32_t *labels_out) {
-    /* data.rs:494-512; with no shift every source pixel is inside the image,
-     * so crop_flip_normalize (data.rs:331-360) is norm() of the (mirrored)
-     * column: (v / 255 - mean) / std in f32, data.rs:95-98 */
-    const int img = 32, pix = 3 * 32 * 32;
-    for (int b = 0; b < bs; b++) labels_out[b] = labels[start + (size_t)b];
-    for (int b = 0; b < bs; b++) {
-        const uint8_t *src = images + (start + (size_t)b) * pix;
-        float *dst = out + (size_t)b * pix;
-        for (int c = 0; c < 3; c++)
-            for (int y = 0; y < img; y++)
-                for (int x = 0; x < img; x++) {
-                    int sx = flip ? img - 1 - x : x;
-                    float v = (float)src[c * img * img + y * img + sx];
-                    dst[c * img * img + y * img + x] = (v / 255.0f - EVAL_MEAN[c]) / EVAL_STD[c];
-                }
-    }
-}
-
 void orc_resnet_eval(orc_resnet *net, const uint8_t *images,
                      const uint8_t *labels, int len, int batch, float *out2) {
     /* eval.rs:15-43 */

@@ -126,6 +126,24 @@ float  orc_resnet_train_step(orc_resnet *net, const float *x,
 uint64_t orc_resnet_flops(const orc_resnet *net, int h, int w);
 
 /* ---- data.rs / eval.rs: evaluation batches and the eval loop ------------ */
+/* make_batch_train (data.rs:384-412) with the augmentation of data.rs:
+ * RandAugment on the bytes (ra_n ops of magnitude ra_mag, off at 0,
+ * data.rs:100-306), crop offset within `pad` (data.rs:309-318), flip,
+ * normalise (data.rs:331-360) and random erasing with probability `erase`
+ * of an erase_side square of normal noise (data.rs:364-377).  Image b draws
+ * from Rng::new(seed ^ b * 0x9E3779B97F4A7C15).  coarse / coarse_out may be
+ * NULL.  (rnn_oracle_data.c) */
+void   orc_make_batch_train(const uint8_t *images, const uint8_t *labels,
+                            const uint8_t *coarse, const uint32_t *idx, int bs,
+                            int pad, float ra_mag, int ra_n, float erase,
+                            int erase_side, uint64_t seed, float *out,
+                            uint32_t *labels_out, uint32_t *coarse_out);
+/* mix_batch (data.rs:467-491): state = the caller's xoshiro256++ state,
+ * advanced in place; perm/lam [bs] out; rect (nullable) = {y0, y1, x0, x1}
+ * of a cutmix.  Returns 0 (no mixing), 1 (mixup) or 2 (cutmix). */
+int    orc_mix_batch(float *x, int bs, float alpha_mix, float alpha_cut,
+                     float sw, uint64_t *state, uint32_t *perm, float *lam,
+                     int *rect);
 /* make_batch_eval (data.rs:494-512): bs images from `start` of a CHW u8
  * dataset of 3 x 32 x 32 images, normalised per channel (data.rs:95-98),
  * mirrored left-right when flip (crop_flip_normalize with no shift,
