@@ -34,6 +34,7 @@ extern "C" {
 #define RNN_ERR_NCCL -3    /* NCCL error */
 #define RNN_ERR_DEVICE -4  /* a kernel raised its device error word (timeout) */
 #define RNN_ERR_UNSUPPORTED -5
+#define RNN_ERR_IO -6       /* a checkpoint file could not be read or written */
 
 typedef struct rnn_ctx rnn_ctx;
 typedef struct rnn_resnet rnn_resnet;
@@ -487,6 +488,40 @@ int rnn_rustvit_eval_dev(rnn_rustvit *net, const uint8_t *images,
 int rnn_rustvit_eval(rnn_rustvit *net, const uint8_t *images,
                      const uint8_t *labels, int len, int batch, int tta,
                      int use_ema, float *loss, float *acc);
+
+/* ---- checkpoints (ckpt.rs:8-247) ---------------------------------------- */
+/* The reference's file format: "RUSTNN\0", tensor count (u32), scalar count
+ * (u64), configuration hash (u64), little endian, then the f32 payload
+ * (every parameter in for_each_param order, then every buffer in
+ * for_each_buffer order).  Saves go to path.tmp, renamed over path; loads
+ * check count, size and hash (or accept a bare legacy payload of the right
+ * size) before any value is replaced. */
+/* ckpt::config_hash (ckpt.rs:83-96): FNV-1a of kind, then of each value's 8
+ * little-endian bytes. */
+uint64_t rnn_ckpt_config_hash(const char *kind, size_t kind_len,
+                              const uint64_t *values, size_t n);
+/* write_checkpoint / read_checkpoint (ckpt.rs:99-189) of a host payload. */
+int rnn_ckpt_write(const char *path, uint32_t tensors, uint64_t config_hash,
+                   const float *payload, size_t scalars);
+int rnn_ckpt_read(const char *path, uint32_t tensors, uint64_t config_hash,
+                  float *payload, size_t scalars);
+/* Checkpointed::save / load (ckpt.rs:51-77) of the device models, with
+ * ResNet's hash of ("resnet", [depth_n, width, nclass]) (model.rs:220-229)
+ * and rustvit's of ("rustvit", cfg, nclass, ncoarse, use_exits, mem_at,
+ * parent) (vit.rs:780-801). */
+int rnn_resnet_save(rnn_resnet *net, const char *path);
+int rnn_resnet_load(rnn_resnet *net, const char *path);
+int rnn_rustvit_save(rnn_rustvit *net, const char *path);
+int rnn_rustvit_load(rnn_rustvit *net, const char *path);
+/* No reference counterpart: the optimiser state the reference's checkpoint
+ * omits, in the same format under the hash of "<kind>-optim" — ResNet: the
+ * SGD momentum; rustvit: the first and second moments, the EMA weights and
+ * the step counters (Adam t, EMA t, EMA ready: three u32 words at the end of
+ * the payload). */
+int rnn_resnet_save_optim(rnn_resnet *net, const char *path);
+int rnn_resnet_load_optim(rnn_resnet *net, const char *path);
+int rnn_rustvit_save_optim(rnn_rustvit *net, const char *path);
+int rnn_rustvit_load_optim(rnn_rustvit *net, const char *path);
 
 #ifdef __cplusplus
 }

@@ -96,6 +96,7 @@ def lib():
         "orc_make_batch_train": (V, [_u8p, _u8p, C.c_void_p, _u32p, I, I, F, I, F, I, U64, _f32p, _u32p,
                                      C.c_void_p]),
         "orc_mix_batch": (I, [_f32p, I, F, F, F, _u64p, _u32p, _f32p, _i32p]),
+        "orc_data_set_cr_math": (V, [I]),
         "orc_rel_index": (I, [I, I, I, I, C.c_void_p]),
         "orc_attn_fwd": (V, [I, I, I, I, I, I, _u32p, I, _f32p, I, I, _f32p, I, I, I, _f32p, _f32p, _f32p, _f32p]),
         "orc_attn_bwd": (V, [I, I, I, I, I, _u32p, I, _f32p, I, I, _f32p, I, I, I, _f32p, _f32p, _f32p,
@@ -262,6 +263,17 @@ def make_batch_train(images, labels, coarse, idx, pad=4, ra_mag=0.0, ra_n=2, era
                                erase, erase_side, seed & (2**64 - 1), x, lab,
                                None if cout is None else cout.ctypes.data)
     return x, lab, cout
+
+
+class cr_math:
+    """Within this context the data pipeline's logf / cosf / sinf are
+    correctly rounded (the device's convention) instead of the C library's."""
+
+    def __enter__(self):
+        lib().orc_data_set_cr_math(1)
+
+    def __exit__(self, *a):
+        lib().orc_data_set_cr_math(0)
 
 
 def mix_batch(x, bs, alpha_mix, alpha_cut, sw, state):

@@ -138,6 +138,10 @@ void   orc_make_batch_train(const uint8_t *images, const uint8_t *labels,
                             int pad, float ra_mag, int ra_n, float erase,
                             int erase_side, uint64_t seed, float *out,
                             uint32_t *labels_out, uint32_t *coarse_out);
+/* 1: the data pipeline's logf / cosf / sinf return correctly rounded
+ * values instead of the C library's (see rnn_oracle_data.c); 0 (default):
+ * the C library's, as the reference. */
+void   orc_data_set_cr_math(int on);
 /* mix_batch (data.rs:467-491): state = the caller's xoshiro256++ state,
  * advanced in place; perm/lam [bs] out; rect (nullable) = {y0, y1, x0, x1}
  * of a cutmix.  Returns 0 (no mixing), 1 (mixup) or 2 (cutmix). */

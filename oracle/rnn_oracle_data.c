@@ -18,6 +18,26 @@
 #define PLANE (IMG * IMG)
 #define PIX (CH * PLANE)
 
+/* The reference calls f32 logf / cosf / sinf (glibc here, as for the Rust
+ * build on this host).  glibc's single-precision results are not correctly
+ * rounded for a few percent of arguments; with cr_math set they are replaced
+ * by the correctly rounded value ((float) of the double function), which is
+ * the convention of the device implementation.  Off by default. */
+static int g_cr_math = 0;
+void orc_data_set_cr_math(int on) { g_cr_math = on; }
+static float o_logf(float x) { return g_cr_math ? (float)log((double)x) : logf(x); }
+static float o_cosf(float x) { return g_cr_math ? (float)cos((double)x) : cosf(x); }
+static float o_sinf(float x) { return g_cr_math ? (float)sin((double)x) : sinf(x); }
+
+/* Rng::normal (rng.rs:55-59) with the functions above */
+static float data_normal(orc_rng *r) {
+    float u1 = orc_rng_uniform(r);
+    if (u1 < 1e-7f) u1 = 1e-7f;
+    float u2 = orc_rng_uniform(r);
+    const float tau = 6.28318530717958647692f;
+    return sqrtf(-2.0f * o_logf(u1)) * o_cosf(tau * u2);
+}
+
 /* data.rs:13-14 */
 static const float MEAN[3] = {0.5071f, 0.4865f, 0.4409f};
 static const float STDV[3] = {0.2673f, 0.2564f, 0.2762f};
@@ -153,7 +173,7 @@ static void apply_op(uint8_t *im, int op, float v, orc_rng *rng) {
         case 3: affine(im, 1.0f, 0.0f, 0.0f, 0.0f, 1.0f, sign * 10.0f * v); break;
         case 4: {
             float t = sign * 30.0f * v * 3.14159265358979323846f / 180.0f;
-            affine(im, cosf(t), -sinf(t), 0.0f, sinf(t), cosf(t), 0.0f);
+            affine(im, o_cosf(t), -o_sinf(t), 0.0f, o_sinf(t), o_cosf(t), 0.0f);
             break;
         }
         case 5: posterize(im, v); break;
@@ -187,7 +207,7 @@ static void randaugment(uint8_t *work, float ra_mag, int ra_n, orc_rng *rng) {
     if (ra_mag <= 0.0f) return;
     for (int i = 0; i < ra_n; i++) {
         int op = (int)orc_rng_below(rng, 13);
-        float v = ra_mag * (1.0f + 0.5f * orc_rng_normal(rng));
+        float v = ra_mag * (1.0f + 0.5f * data_normal(rng));
         if (v < 0.0f) v = 0.0f;
         if (v > 1.0f) v = 1.0f;
         apply_op(work, op, v, rng);
@@ -219,7 +239,7 @@ static void random_erase(float *dst, float erase, int erase_side, orc_rng *rng) 
     int x0 = cx - h > 0 ? cx - h : 0, x1 = cx + h < IMG ? cx + h : IMG;
     for (int c = 0; c < CH; c++)
         for (int y = y0; y < y1; y++)
-            for (int x = x0; x < x1; x++) dst[c * PLANE + y * IMG + x] = orc_rng_normal(rng);
+            for (int x = x0; x < x1; x++) dst[c * PLANE + y * IMG + x] = data_normal(rng);
 }
 
 void orc_make_batch_train(const uint8_t *images, const uint8_t *labels, const uint8_t *coarse,

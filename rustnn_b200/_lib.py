@@ -13,7 +13,8 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG, "librnn_b200.so")
 
 RNN_OK = 0
-ERRORS = {-1: "RNN_ERR_ARG", -2: "RNN_ERR_CUDA", -3: "RNN_ERR_NCCL", -4: "RNN_ERR_DEVICE", -5: "RNN_ERR_UNSUPPORTED"}
+ERRORS = {-1: "RNN_ERR_ARG", -2: "RNN_ERR_CUDA", -3: "RNN_ERR_NCCL", -4: "RNN_ERR_DEVICE", -5: "RNN_ERR_UNSUPPORTED",
+          -6: "RNN_ERR_IO"}
 
 _lock = threading.Lock()
 _lib = None
@@ -150,12 +151,23 @@ SIGS = {
     "rnn_make_batch_eval_dev": [CTX, FP, FP, Z, I, I, FP, FP],
     "rnn_make_batch_train_dev": [CTX, FP, FP, FP, FP, I, I, F, I, F, I, U64, FP, FP, FP],
     "rnn_mix_batch_dev": [CTX, FP, I, F, F, F, FP, FP, FP],
+    "rnn_ckpt_config_hash": [C.c_char_p, Z, FP, Z],
+    "rnn_ckpt_write": [C.c_char_p, C.c_uint32, U64, FP, Z],
+    "rnn_ckpt_read": [C.c_char_p, C.c_uint32, U64, FP, Z],
+    "rnn_resnet_save": [NET, C.c_char_p],
+    "rnn_resnet_load": [NET, C.c_char_p],
+    "rnn_resnet_save_optim": [NET, C.c_char_p],
+    "rnn_resnet_load_optim": [NET, C.c_char_p],
+    "rnn_rustvit_save": [VIT, C.c_char_p],
+    "rnn_rustvit_load": [VIT, C.c_char_p],
+    "rnn_rustvit_save_optim": [VIT, C.c_char_p],
+    "rnn_rustvit_load_optim": [VIT, C.c_char_p],
     "rnn_resnet_eval_dev": [NET, FP, FP, I, I, FP, FP],
     "rnn_resnet_eval": [NET, FP, FP, I, I, FP, FP],
     "rnn_rustvit_eval_dev": [VIT, FP, FP, I, I, I, I, FP, FP],
     "rnn_rustvit_eval": [VIT, FP, FP, I, I, I, I, FP, FP],
 }
-_RESTYPE = {"rnn_ctx_stream": P, "rnn_launch_count": C.c_ulonglong}
+_RESTYPE = {"rnn_ctx_stream": P, "rnn_launch_count": C.c_ulonglong, "rnn_ckpt_config_hash": C.c_uint64}
 
 
 class RnnError(RuntimeError):

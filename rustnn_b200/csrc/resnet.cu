@@ -15,6 +15,7 @@
 #include <vector>
 
 #include "bn.cuh"
+#include "ckpt.cuh"
 #include "eval.cuh"
 #include "ew.cuh"
 #include "rng.h"
@@ -70,6 +71,8 @@ struct rnn_resnet {
   // BN running statistics (for_each_buffer order: [rm, rv] per BN)
   size_t nbuf = 0;
   float* bnbuf = nullptr;
+  // tensor counts of for_each_param / for_each_buffer (checkpoint header)
+  int n_param_tensors = 0, n_buf_tensors = 0;
   float* bnstat = nullptr;  // mean/invstd arrays of every BN
   // activations
   int cap_n = 0, cap_h = 0, cap_w = 0;
@@ -558,6 +561,7 @@ extern "C" int rnn_resnet_create(rnn_ctx* ctx, int depth_n, int width, int nclas
   };
   auto mk_bn = [&](BNL& b, int c) {
     b.c = c;
+    net->n_buf_tensors += 2;  // running mean, running variance
     b.g_off = take(c, false);
     b.b_off = take(c, false);
     b.rm_off = boff;
@@ -591,6 +595,7 @@ extern "C" int rnn_resnet_create(rnn_ctx* ctx, int depth_n, int width, int nclas
   net->fcb_off = take(nclass, false);
   net->nparams = off;
   net->nbuf = boff;
+  net->n_param_tensors = (int)sizes.size();
 
   // ---- initial values, drawn in ResNet::new order (model.rs:112-133):
   // every block (c1, c2, shortcut conv) first, then the stem, then the
@@ -839,6 +844,61 @@ extern "C" int rnn_resnet_eval(rnn_resnet* net, const uint8_t* images, const uin
   const uint8_t *di = nullptr, *dl = nullptr;
   if (len > 0) RNN_TRY(rnn::eval_ws_stage(net->eval, net->ctx, images, labels, len, &di, &dl));
   return resnet_eval(net, di, dl, len, batch, loss, acc);
+}
+
+// ---------------------------------------------------------------- checkpoints
+
+// ResNet::config_hash (model.rs:220-229): blocks / 3 = depth_n, the stem's
+// cout = width, the classifier's fout = nclass
+static uint64_t resnet_hash(const rnn_resnet* net, const char* kind) {
+  const uint64_t v[3] = {(uint64_t)net->depth_n, (uint64_t)net->width, (uint64_t)net->nclass};
+  return rnn::ckpt_hash(kind, strlen(kind), v, 3);
+}
+
+static int to_host(rnn_resnet* net, std::vector<float>& h, const float* d, size_t n) {
+  h.resize(n);
+  if (n) RNN_CUDA(cudaMemcpyAsync(h.data(), d, n * sizeof(float), cudaMemcpyDeviceToHost, net->ctx->stream));
+  return RNN_OK;
+}
+
+extern "C" int rnn_resnet_save(rnn_resnet* net, const char* path) {
+  RNN_REQUIRE(net && path, "resnet_save: null argument");
+  std::vector<float> v, b;
+  RNN_TRY(to_host(net, v, net->v, net->nparams));
+  RNN_TRY(to_host(net, b, net->bnbuf, net->nbuf));
+  RNN_TRY(rnn_ctx_synchronize(net->ctx));
+  return rnn::ckpt_write(path, (uint32_t)(net->n_param_tensors + net->n_buf_tensors), resnet_hash(net, "resnet"),
+                         {{v.data(), v.size()}, {b.data(), b.size()}});
+}
+
+extern "C" int rnn_resnet_load(rnn_resnet* net, const char* path) {
+  RNN_REQUIRE(net && path, "resnet_load: null argument");
+  std::vector<float> p;
+  RNN_TRY(rnn::ckpt_read(path, (uint32_t)(net->n_param_tensors + net->n_buf_tensors), resnet_hash(net, "resnet"),
+                         net->nparams + net->nbuf, p));
+  RNN_CUDA(cudaMemcpyAsync(net->v, p.data(), net->nparams * sizeof(float), cudaMemcpyHostToDevice,
+                           net->ctx->stream));
+  RNN_CUDA(cudaMemcpyAsync(net->bnbuf, p.data() + net->nparams, net->nbuf * sizeof(float), cudaMemcpyHostToDevice,
+                           net->ctx->stream));
+  return rnn_ctx_synchronize(net->ctx);
+}
+
+extern "C" int rnn_resnet_save_optim(rnn_resnet* net, const char* path) {
+  RNN_REQUIRE(net && path, "resnet_save_optim: null argument");
+  std::vector<float> m;
+  RNN_TRY(to_host(net, m, net->m, net->nparams));
+  RNN_TRY(rnn_ctx_synchronize(net->ctx));
+  return rnn::ckpt_write(path, (uint32_t)net->n_param_tensors, resnet_hash(net, "resnet-optim"),
+                         {{m.data(), m.size()}});
+}
+
+extern "C" int rnn_resnet_load_optim(rnn_resnet* net, const char* path) {
+  RNN_REQUIRE(net && path, "resnet_load_optim: null argument");
+  std::vector<float> m;
+  RNN_TRY(rnn::ckpt_read(path, (uint32_t)net->n_param_tensors, resnet_hash(net, "resnet-optim"), net->nparams, m));
+  RNN_CUDA(cudaMemcpyAsync(net->m, m.data(), net->nparams * sizeof(float), cudaMemcpyHostToDevice,
+                           net->ctx->stream));
+  return rnn_ctx_synchronize(net->ctx);
 }
 
 // ---------------------------------------------------------------- DP

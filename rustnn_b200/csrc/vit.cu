@@ -21,6 +21,7 @@
 #include <vector>
 
 #include "../../include/rnn_b200.h"
+#include "ckpt.cuh"
 #include "common.cuh"
 #include "eval.cuh"
 #include "rng.h"
@@ -277,6 +278,8 @@ struct rnn_rustvit {
   Cfg cfg;
   int nf = 0, nc = 0, th = 0, mh = 0;
   uint32_t* parent = nullptr;  // device [nf]
+  std::vector<uint32_t> parent_host;  // for the checkpoint hash
+  int n_buf_tensors = 0;
   // parameters
   Registry R;
   std::vector<size_t> off;  // per registry id
@@ -965,6 +968,7 @@ static int build(rnn_rustvit* net, uint64_t seed) {
     hb.insert(hb.end(), b->c, 1.0f);
   }
   net->nb = hb.size();
+  net->n_buf_tensors = 2 * (int)bns.size();
   RNN_CUDA(cudaMalloc(&net->B, hb.size() * sizeof(float)));
   RNN_CUDA(cudaMemcpy(net->B, hb.data(), hb.size() * sizeof(float), cudaMemcpyHostToDevice));
   return RNN_OK;
@@ -1110,6 +1114,7 @@ extern "C" int rnn_rustvit_create(rnn_ctx* ctx, const int* cfg9, const int* mem_
   net->cfg = c;
   net->nf = nf;
   net->nc = ncoarse;
+  net->parent_host.assign(parent, parent + nf);
   int rc = cudaMalloc(&net->parent, nf * sizeof(uint32_t)) == cudaSuccess
                ? RNN_OK
                : set_error(RNN_ERR_CUDA, "rustvit_create: cudaMalloc failed");
@@ -1313,4 +1318,88 @@ extern "C" int rnn_rustvit_eval(rnn_rustvit* net, const uint8_t* images, const u
   const uint8_t *di = nullptr, *dl = nullptr;
   if (len > 0) RNN_TRY(rnn::eval_ws_stage(net->eval, net->ctx, images, labels, len, &di, &dl));
   return vit_eval(net, di, dl, len, batch, tta != 0, use_ema != 0, loss, acc);
+}
+
+// ---------------------------------------------------------------- checkpoints
+
+namespace {
+
+// RustViT::config_hash (vit.rs:780-801)
+uint64_t vit_hash(const rnn_rustvit* net, const char* kind) {
+  const Cfg& c = net->cfg;
+  uint32_t dp_bits;
+  memcpy(&dp_bits, &c.droppath, 4);
+  std::vector<uint64_t> f = {(uint64_t)c.width, (uint64_t)c.cmid,   (uint64_t)c.dim,    (uint64_t)c.heads,
+                             (uint64_t)c.depth3, (uint64_t)c.dim4,  (uint64_t)c.heads4, (uint64_t)c.depth4,
+                             (uint64_t)dp_bits,  (uint64_t)c.img,   (uint64_t)net->nf,  (uint64_t)net->nc,
+                             (uint64_t)net->use_exits, (uint64_t)c.mem_at.size()};
+  for (int m : c.mem_at) f.push_back((uint64_t)m);
+  f.push_back(net->parent_host.size());
+  for (uint32_t p : net->parent_host) f.push_back(p);
+  return rnn::ckpt_hash(kind, strlen(kind), f.data(), f.size());
+}
+
+int vit_to_host(rnn_rustvit* net, std::vector<float>& h, const float* d, size_t n) {
+  h.assign(n, 0.0f);
+  if (n && d) RNN_CUDA(cudaMemcpyAsync(h.data(), d, n * sizeof(float), cudaMemcpyDeviceToHost, net->ctx->stream));
+  return RNN_OK;
+}
+
+}  // namespace
+
+extern "C" int rnn_rustvit_save(rnn_rustvit* net, const char* path) {
+  RNN_REQUIRE(net && path, "rustvit_save: null argument");
+  std::vector<float> v, b;
+  RNN_TRY(vit_to_host(net, v, net->V, net->np));
+  RNN_TRY(vit_to_host(net, b, net->B, net->nb));
+  RNN_TRY(rnn_ctx_synchronize(net->ctx));
+  return rnn::ckpt_write(path, (uint32_t)(net->order.size() + net->n_buf_tensors), vit_hash(net, "rustvit"),
+                         {{v.data(), v.size()}, {b.data(), b.size()}});
+}
+
+extern "C" int rnn_rustvit_load(rnn_rustvit* net, const char* path) {
+  RNN_REQUIRE(net && path, "rustvit_load: null argument");
+  std::vector<float> p;
+  RNN_TRY(rnn::ckpt_read(path, (uint32_t)(net->order.size() + net->n_buf_tensors), vit_hash(net, "rustvit"),
+                         net->np + net->nb, p));
+  RNN_CUDA(cudaMemcpyAsync(net->V, p.data(), net->np * sizeof(float), cudaMemcpyHostToDevice, net->ctx->stream));
+  RNN_CUDA(cudaMemcpyAsync(net->B, p.data() + net->np, net->nb * sizeof(float), cudaMemcpyHostToDevice,
+                           net->ctx->stream));
+  return rnn_ctx_synchronize(net->ctx);
+}
+
+// payload: M, V2, E (zeros until the first EMA update), then the u32 words
+// opt_t, ema_t, ema_ready
+extern "C" int rnn_rustvit_save_optim(rnn_rustvit* net, const char* path) {
+  RNN_REQUIRE(net && path, "rustvit_save_optim: null argument");
+  std::vector<float> m, v2, e;
+  RNN_TRY(vit_to_host(net, m, net->M, net->np));
+  RNN_TRY(vit_to_host(net, v2, net->V2, net->np));
+  RNN_TRY(vit_to_host(net, e, net->ema_ready ? net->E : nullptr, net->np));
+  RNN_TRY(rnn_ctx_synchronize(net->ctx));
+  const uint32_t words[3] = {(uint32_t)net->opt_t, (uint32_t)net->ema_t, (uint32_t)net->ema_ready};
+  float tail[3];
+  memcpy(tail, words, sizeof(words));
+  return rnn::ckpt_write(path, (uint32_t)(3 * net->order.size() + 1), vit_hash(net, "rustvit-optim"),
+                         {{m.data(), m.size()}, {v2.data(), v2.size()}, {e.data(), e.size()}, {tail, 3}});
+}
+
+extern "C" int rnn_rustvit_load_optim(rnn_rustvit* net, const char* path) {
+  RNN_REQUIRE(net && path, "rustvit_load_optim: null argument");
+  std::vector<float> p;
+  const size_t np = net->np;
+  RNN_TRY(rnn::ckpt_read(path, (uint32_t)(3 * net->order.size() + 1), vit_hash(net, "rustvit-optim"), 3 * np + 3, p));
+  uint32_t words[3];
+  memcpy(words, p.data() + 3 * np, sizeof(words));
+  if (words[2] && !net->E) RNN_CUDA(cudaMalloc(&net->E, np * sizeof(float)));
+  RNN_CUDA(cudaMemcpyAsync(net->M, p.data(), np * sizeof(float), cudaMemcpyHostToDevice, net->ctx->stream));
+  RNN_CUDA(cudaMemcpyAsync(net->V2, p.data() + np, np * sizeof(float), cudaMemcpyHostToDevice, net->ctx->stream));
+  if (words[2])
+    RNN_CUDA(cudaMemcpyAsync(net->E, p.data() + 2 * np, np * sizeof(float), cudaMemcpyHostToDevice,
+                             net->ctx->stream));
+  RNN_TRY(rnn_ctx_synchronize(net->ctx));
+  net->opt_t = (int)words[0];
+  net->ema_t = (int)words[1];
+  net->ema_ready = words[2] != 0;
+  return RNN_OK;
 }

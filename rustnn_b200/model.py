@@ -141,6 +141,25 @@ class ResNet:
              C.c_void_p(C.addressof(loss)), C.c_void_p(C.addressof(acc)))
         return loss.value, acc.value
 
+    def save(self, path: str):
+        """Checkpointed::save (ckpt.rs:62-68) in the reference's format."""
+        self.ctx.bind()
+        call("rnn_resnet_save", self.h, str(path).encode())
+
+    def load(self, path: str):
+        """Checkpointed::load (ckpt.rs:70-76)."""
+        self.ctx.bind()
+        call("rnn_resnet_load", self.h, str(path).encode())
+
+    def save_optim(self, path: str):
+        """The SGD momentum, which the reference's checkpoint omits."""
+        self.ctx.bind()
+        call("rnn_resnet_save_optim", self.h, str(path).encode())
+
+    def load_optim(self, path: str):
+        self.ctx.bind()
+        call("rnn_resnet_load_optim", self.h, str(path).encode())
+
     def dp_init(self, rank: int, world: int, uid: bytes, sync_bn: bool = True):
         buf = (C.c_ubyte * UID_BYTES).from_buffer_copy(uid)
         call("rnn_resnet_dp_init", self.h, rank, world, C.cast(buf, C.c_void_p), int(sync_bn))

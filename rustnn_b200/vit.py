@@ -185,6 +185,25 @@ class RustViT:
              int(bool(tta)), int(bool(use_ema)), _ptr(out[0:1]), _ptr(out[1:2]))
         return float(out[0]), float(out[1])
 
+    def save(self, path: str):
+        """Checkpointed::save (ckpt.rs:62-68) in the reference's format."""
+        self.ctx.bind()
+        call("rnn_rustvit_save", self.h, str(path).encode())
+
+    def load(self, path: str):
+        self.ctx.bind()
+        call("rnn_rustvit_load", self.h, str(path).encode())
+
+    def save_optim(self, path: str):
+        """Both moments, the EMA weights and the step counters, which the
+        reference's checkpoint omits."""
+        self.ctx.bind()
+        call("rnn_rustvit_save_optim", self.h, str(path).encode())
+
+    def load_optim(self, path: str):
+        self.ctx.bind()
+        call("rnn_rustvit_load_optim", self.h, str(path).encode())
+
     def train_step_host(self, x, tf, tc, hard, hardc, lr=6e-4, wd=0.06, clip=1.0, ema=0.9998, drop_seed=0):
         """The same step through the host tier of the C ABI (host batch arrays)."""
         self.ctx.bind()

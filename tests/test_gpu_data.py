@@ -1,14 +1,12 @@
 """The device batch builders (csrc/data.cu) against the CPU oracle
 (oracle/rnn_oracle_data.c): make_batch_train (data.rs:384-412) and mix_batch
-(data.rs:467-491).
+(data.rs:467-491), bit for bit.
 
-Bytes, crop offsets, flips, labels and every value that does not pass through
-a transcendental function are compared bit for bit.  The reference's logf /
-cosf / sinf (the erase noise, RandAugment magnitudes, rotations) are
-evaluated on the device in double and rounded to f32; the CPU's single
-precision functions agree with that rounding except within a fraction of an
-ulp of a tie, so the noise values are checked to 2 ulp and a RandAugment
-batch to at most a few differing pixels."""
+The device evaluates the reference's f32 logf / cosf / sinf (erase noise,
+RandAugment magnitudes, rotations) correctly rounded; the oracle runs in the
+same convention here (oracle.cr_math).  How far the C library's
+single-precision functions, which the reference calls, move a batch is
+measured on the CPU in tests/test_oracle_data.py."""
 import numpy as np
 import pytest
 
@@ -33,8 +31,9 @@ def both(seed, n, bs, aug):
     images, labels, coarse = dataset(seed, n)
     idx = np.random.default_rng(seed + 1).permutation(n)[:bs].astype(np.uint32)
     s = seed * 1_000_003 + 7
-    want, wl, wc = O.make_batch_train(images, labels, coarse, idx, aug.pad, aug.ra_mag, aug.ra_n, aug.erase,
-                                      aug.erase_side, s)
+    with O.cr_math():
+        want, wl, wc = O.make_batch_train(images, labels, coarse, idx, aug.pad, aug.ra_mag, aug.ra_n, aug.erase,
+                                          aug.erase_side, s)
     dv = lambda a: torch.from_numpy(a).cuda()
     got, gl, gc = data.make_batch_train(dv(images), dv(labels), dv(coarse), dv(idx.view(np.int32)), aug, s)
     torch.cuda.synchronize()
@@ -43,51 +42,26 @@ def both(seed, n, bs, aug):
     return got.cpu().numpy(), want
 
 
-def erase_mask(seed, bs, aug):
-    """Pixels the reference fills with noise, from the generator's draws."""
-    m = np.zeros((bs, 3, 32, 32), bool)
-    s = seed * 1_000_003 + 7
-    for b in range(bs):
-        rng = O.Rng(s ^ ((b * 0x9E3779B97F4A7C15) & (2**64 - 1)))
-        assert aug.ra_mag <= 0
-        if aug.pad > 0:
-            rng.below(2 * aug.pad + 1)
-            rng.below(2 * aug.pad + 1)
-        rng.next_u64()
-        if aug.erase > 0 and not rng.uniform() >= aug.erase:
-            cy, cx, h = rng.below(32), rng.below(32), aug.erase_side // 2
-            m[b, :, max(cy - h, 0):min(cy + h, 32), max(cx - h, 0):min(cx + h, 32)] = True
-    return m.ravel()
-
-
-@pytest.mark.parametrize("pad,erase,side", [(4, 1.0, 8), (4, 0.0, 8), (32, 0.5, 16), (0, 1.0, 40)])
+@pytest.mark.parametrize("pad,erase,side", [(4, 1.0, 8), (4, 0.0, 8), (32, 0.5, 16), (0, 1.0, 40), (4, 1.0, 1)])
 def test_batch_train_no_randaugment(pad, erase, side):
-    """The ResNet loop's augmentation (train.rs:654-660) and its corners:
-    every pixel outside the erased square bit for bit, the noise to 2 ulp."""
+    """The ResNet loop's augmentation (train.rs:654-660) and its corners."""
     from rustnn_b200.data import Aug
 
     aug = Aug(pad=pad, ra_mag=0.0, ra_n=0, erase=erase, erase_side=side)
     got, want = both(pad + side, 64, 48, aug)
-    m = erase_mask(pad + side, 48, aug)
-    assert np.array_equal(got[~m], want[~m])
-    if m.any():
-        ulp = np.spacing(np.abs(want[m]).astype(F32))
-        assert np.all(np.abs(got[m] - want[m]) <= 2 * ulp)
+    assert np.array_equal(got, want)
 
 
-@pytest.mark.parametrize("ra_mag,ra_n,seed", [(0.5, 2, 3), (1.0, 3, 4), (0.8, 8, 5)])
-def test_batch_train_randaugment(ra_mag, ra_n, seed):
-    """RandAugment (data.rs:100-306) before crop/flip/normalise, no erasing:
-    at most a few pixels of the batch may differ (a magnitude or a rotation
-    one f32 ulp apart can move a byte by one), and the batch stays within
-    1e-4 relative Frobenius of the oracle's."""
+@pytest.mark.parametrize("ra_mag,ra_n,erase,seed", [(0.5, 2, 0.0, 3), (1.0, 3, 0.5, 4), (0.8, 8, 0.0, 5),
+                                                    (0.6, 2, 0.25, 6)])
+def test_batch_train_randaugment(ra_mag, ra_n, erase, seed):
+    """RandAugment (data.rs:100-306) before crop/flip/normalise/erase; 96
+    images x up to 8 ops draw every op many times."""
     from rustnn_b200.data import Aug
 
-    aug = Aug(pad=4, ra_mag=ra_mag, ra_n=ra_n, erase=0.0, erase_side=8)
+    aug = Aug(pad=4, ra_mag=ra_mag, ra_n=ra_n, erase=erase, erase_side=8)
     got, want = both(seed, 96, 96, aug)
-    diff = np.count_nonzero(got != want)
-    assert diff <= 64, diff
-    assert np.linalg.norm(got - want) <= 1e-4 * np.linalg.norm(want)
+    assert np.array_equal(got, want)
 
 
 @pytest.mark.parametrize("m,c,seed", [(0.8, 0.0, 1), (0.0, 1.0, 2), (0.8, 1.0, 3), (0.0, 0.0, 4), (0.2, 0.3, 5)])

@@ -244,3 +244,24 @@ def test_mix_on_gives_valid_lambdas(m, c):
             want[:, :, y0:y1, x0:x1] = s3[perm][:, :, y0:y1, x0:x1]
             assert np.array_equal(x.reshape(bs, 3, IMG, IMG), want)
             assert lam[0] == F32(1) - F32((y1 - y0) * (x1 - x0)) / F32(PLANE)
+
+
+@pytest.mark.parametrize("ra_mag,ra_n,erase,seed", [(0.5, 2, 0.0, 3), (0.0, 0, 1.0, 11), (0.6, 2, 0.25, 12),
+                                                    (0.8, 8, 0.0, 5)])
+def test_cr_math_gap(ra_mag, ra_n, erase, seed):
+    """The device evaluates logf / cosf / sinf correctly rounded; the C
+    library's single-precision results (the reference's) differ in the last
+    bit for a few percent of arguments.  Over a batch that moves the erase
+    noise by an ulp and, through a RandAugment magnitude or angle, a handful
+    of bytes: everything else is identical."""
+    images, labels, _ = dataset(seed, 96)
+    idx = np.arange(96, dtype=np.uint32)
+    a, _, _ = O.make_batch_train(images, labels, None, idx, 4, ra_mag, ra_n, erase, 8, seed)
+    with O.cr_math():
+        b, _, _ = O.make_batch_train(images, labels, None, idx, 4, ra_mag, ra_n, erase, 8, seed)
+    d = a != b
+    assert np.count_nonzero(d) <= 1e-3 * a.size
+    if ra_mag <= 0:
+        # a last-bit change of ln or cos moves sqrt(-2 ln u1) * cos(.) by a few ulp
+        assert np.all(np.abs(a[d] - b[d]) <= 4 * np.spacing(np.abs(a[d])))
+    assert np.linalg.norm(a - b) <= 2e-4 * np.linalg.norm(a)
