@@ -5,6 +5,9 @@
     python -m rustnn_b200.kernel_bench attn            # Core fwd/bwd at the attention config (B=128, h=4, dh=32)
     python -m rustnn_b200.kernel_bench ln              # LayerNorm fwd/bwd at the rustvit row counts
     python -m rustnn_b200.kernel_bench muon            # Muon (Newton-Schulz) over the 39 rustvit weight matrices
+    python -m rustnn_b200.kernel_bench vitstep         # one rustvit Trainer::step (batch 128) after 3 warm-ups,
+                                                       # alone between cudaProfilerStart/Stop (ncu
+                                                       # --profile-from-start off lists exactly its launches)
 
 Prints one line per kernel: time per launch, algorithmic TFLOP/s (2*M*N*K),
 and the minimum HBM bytes / achieved GB/s.  Also the target of the ncu
@@ -170,9 +173,44 @@ def muon(args):
              "tflops": round(fl / t / 1e12, 2), "gflop": round(fl / 1e9, 2)}]
 
 
+def vitstep(args):
+    """Trainer::step of the default rustvit (train.rs:346-387) at batch
+    args.batch, synthetic data; the timed step runs alone inside the
+    profiler range."""
+    import numpy as np
+
+    from . import vit
+
+    n = args.batch
+    net = vit.RustViT(vit.VitCfg(), vit.cifar_parent(), 20, 0)
+    rng = np.random.default_rng(100)
+    x = torch.from_numpy(rng.standard_normal(n * 3 * 32 * 32).astype(np.float32)).cuda()
+    hard = rng.integers(0, 100, size=n).astype(np.uint32)
+    tf, tc, coarse = vit.targets(hard, vit.cifar_parent(), 20)
+    tfd, tcd = torch.from_numpy(tf).cuda(), torch.from_numpy(tc).cuda()
+    hd = torch.from_numpy(hard.astype(np.int32)).cuda()
+    cd = torch.from_numpy(coarse.astype(np.int32)).cuda()
+    for i in range(3):
+        net.train_step(x, tfd, tcd, hd, cd, drop_seed=i, stats=False)
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = ops.lib().rnn_launch_count()
+    torch.cuda.cudart().cudaProfilerStart()
+    e0.record(s)
+    net.train_step(x, tfd, tcd, hd, cd, drop_seed=9, stats=False)
+    e1.record(s)
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    launches = ops.lib().rnn_launch_count() - l0
+    net.close()
+    return [{"kernel": "rustvit_step", "shape": f"batch {n}", "ms": round(e0.elapsed_time(e1), 3),
+             "launches": int(launches)}]
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["conv", "gemm", "attn", "ln", "muon"])
+    ap.add_argument("what", choices=["conv", "gemm", "attn", "ln", "muon", "vitstep"])
     ap.add_argument("--cin", type=int, default=64)
     ap.add_argument("--cout", type=int, default=64)
     ap.add_argument("--hw", type=int, default=32)
@@ -182,7 +220,7 @@ def main():
     ap.add_argument("--which", default="fwd,dgrad,wgrad")
     ap.add_argument("--reps", type=int, default=5)
     args = ap.parse_args()
-    rows = {"conv": conv, "gemm": gemm, "attn": attn, "ln": ln, "muon": muon}[args.what](args)
+    rows = {"conv": conv, "gemm": gemm, "attn": attn, "ln": ln, "muon": muon, "vitstep": vitstep}[args.what](args)
     for r in rows:
         print(json.dumps(r))
 
