@@ -10,6 +10,7 @@
 #include <algorithm>
 #include <vector>
 
+#include "colsum.cuh"
 #include "ew.cuh"
 #include "rng.h"
 
@@ -27,33 +28,33 @@ __global__ void chan_scale_kernel(const float* __restrict__ x, size_t total, int
     y[i] = x[i] * l[i % c];
 }
 
-// part[b][j] = sum over rows [b*R, (b+1)*R) of a[r][j] * m[r][j] (m optional)
-constexpr int GL_ROWS = 64;
-__global__ void gl_colsum_partial(const float* __restrict__ a, const float* __restrict__ m, int rows, int c,
-                                  float* __restrict__ part) {
-  const int b = blockIdx.y, r0 = b * GL_ROWS, r1 = min(rows, r0 + GL_ROWS);
-  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < c; j += gridDim.x * blockDim.x) {
-    float s = 0.0f;
-    for (int r = r0; r < r1; r++) s += m ? a[(size_t)r * c + j] * m[(size_t)r * c + j] : a[(size_t)r * c + j];
-    part[(size_t)b * c + j] = s;
+// float4 form (c % 4 == 0, all operands 16-byte aligned)
+__global__ void chan_scale4_kernel(const float4* __restrict__ x, size_t total4, int c4, const float4* __restrict__ l,
+                                   float4* __restrict__ y) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total4; i += (size_t)gridDim.x * blockDim.x) {
+    const float4 v = x[i], q = __ldg(l + i % c4);
+    y[i] = make_float4(v.x * q.x, v.y * q.y, v.z * q.z, v.w * q.w);
   }
 }
-__global__ void gl_colsum_final(const float* __restrict__ part, int nb, int c, float* __restrict__ out) {
-  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < c; j += gridDim.x * blockDim.x) {
-    float s = 0.0f;
-    for (int b = 0; b < nb; b++) s += part[(size_t)b * c + j];
-    out[j] += s;
-  }
-}
-static int gl_colsum(rnn_ctx* ctx, const float* a, const float* m, int rows, int c, float* out) {
-  const int nb = (rows + GL_ROWS - 1) / GL_ROWS;
-  RNN_TRY(ensure_aux(ctx, (size_t)nb * c * 4));
-  float* part = static_cast<float*>(ctx->aux);
-  gl_colsum_partial<<<dim3((c + 255) / 256, nb), 256, 0, ctx->stream>>>(a, m, rows, c, part);
-  RNN_CHECK_LAUNCH();
-  gl_colsum_final<<<(c + 255) / 256, 256, 0, ctx->stream>>>(part, nb, c, out);
+static bool gl_al16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+// y = x * l per channel
+static int chan_scale(rnn_ctx* ctx, const float* x, size_t total, int c, const float* l, float* y) {
+  if (c % 4 == 0 && gl_al16(x) && gl_al16(l) && gl_al16(y))
+    chan_scale4_kernel<<<gl_grid(total / 4, ctx->num_sms), 256, 0, ctx->stream>>>(
+        reinterpret_cast<const float4*>(x), total / 4, c / 4, reinterpret_cast<const float4*>(l),
+        reinterpret_cast<float4*>(y));
+  else
+    chan_scale_kernel<<<gl_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(x, total, c, l, y);
   RNN_CHECK_LAUNCH();
   return RNN_OK;
+}
+
+// part[b][j] = sum over rows [b*R, (b+1)*R) of a[r][j] * m[r][j] (m optional)
+static int gl_colsum(rnn_ctx* ctx, const float* a, const float* m, int rows, int c, float* out) {
+  const int nb = (rows + CS_ROWS - 1) / CS_ROWS;
+  RNN_TRY(ensure_aux(ctx, (size_t)nb * c * 4));
+  float* part = static_cast<float*>(ctx->aux);
+  return colsum_two_pass(ctx, a, m, rows, c, part, out);
 }
 
 // ---------------------------------------------------------------- SwiGLU gate
@@ -240,6 +241,27 @@ __global__ void seqpool_bwd_kernel(const float* __restrict__ dz, const float* __
 __global__ void row_scale_kernel(float* __restrict__ x, size_t per, size_t total, const float* __restrict__ mask) {
   for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x)
     x[e] *= mask[e / per];
+}
+// float4 form (per % 4 == 0, x 16-byte aligned): a float4 never spans two images
+__global__ void row_scale4_kernel(float4* __restrict__ x, size_t per4, size_t total4, const float* __restrict__ mask) {
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total4; e += (size_t)gridDim.x * blockDim.x) {
+    const float m = __ldg(mask + e / per4);
+    float4 v = x[e];
+    v.x *= m;
+    v.y *= m;
+    v.z *= m;
+    v.w *= m;
+    x[e] = v;
+  }
+}
+static int row_scale(rnn_ctx* ctx, float* x, size_t per, size_t total, const float* mask) {
+  if (per % 4 == 0 && ((uintptr_t)x & 15) == 0)
+    row_scale4_kernel<<<gl_grid(total / 4, ctx->num_sms), 256, 0, ctx->stream>>>(reinterpret_cast<float4*>(x),
+                                                                                per / 4, total / 4, mask);
+  else
+    row_scale_kernel<<<gl_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(x, per, total, mask);
+  RNN_CHECK_LAUNCH();
+  return RNN_OK;
 }
 
 // y[i, (oy,ox), q*c + j] = z[i, (2oy+dy_q, 2ox+dx_q), j]; dir=1 is the inverse copy
@@ -444,9 +466,7 @@ extern "C" int rnn_layerscale_fwd_dev(rnn_ctx* ctx, const float* x, int rows, in
   const size_t total = (size_t)rows * c;
   if (!total) return RNN_OK;
   RNN_RANGE(x, total * 4); RNN_RANGE(y, total * 4); RNN_RANGE(l, (size_t)c * 4);
-  chan_scale_kernel<<<gl_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(x, total, c, l, y);
-  RNN_CHECK_LAUNCH();
-  return RNN_OK;
+  return chan_scale(ctx, x, total, c, l, y);
 }
 
 extern "C" int rnn_layerscale_bwd_dev(rnn_ctx* ctx, const float* dy, const float* x, int rows, int c, const float* l,
@@ -456,9 +476,7 @@ extern "C" int rnn_layerscale_bwd_dev(rnn_ctx* ctx, const float* dy, const float
   if (!total) return RNN_OK;
   RNN_RANGE(dy, total * 4); RNN_RANGE(x, total * 4); RNN_RANGE(dx, total * 4); RNN_RANGE(dl, (size_t)c * 4);
   RNN_TRY(gl_colsum(ctx, dy, x, rows, c, dl));
-  chan_scale_kernel<<<gl_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(dy, total, c, l, dx);
-  RNN_CHECK_LAUNCH();
-  return RNN_OK;
+  return chan_scale(ctx, dy, total, c, l, dx);
 }
 
 extern "C" int rnn_swiglu_act_fwd_dev(rnn_ctx* ctx, const float* ab, int rows, int h, float* u) {
@@ -528,13 +546,11 @@ extern "C" int rnn_seqpool_bwd_dev(rnn_ctx* ctx, const float* dz, const float* x
   if (!n) return RNN_OK;
   RNN_RANGE(dz, (size_t)n * c * 4); RNN_RANGE(x, (size_t)n * t * c * 4); RNN_RANGE(w, (size_t)n * t * 4);
   RNN_RANGE(dx, (size_t)n * t * c * 4); RNN_RANGE(dp, (size_t)c * 4); RNN_RANGE(p, (size_t)c * 4);
-  RNN_TRY(ensure_aux(ctx, (size_t)n * c * 4 + (size_t)GL_ROWS * c * 4 * 4));
+  RNN_TRY(ensure_aux(ctx, (size_t)n * c * 4 + (size_t)CS_ROWS * c * 4 * 4));
   float* part = static_cast<float*>(ctx->aux);
   seqpool_bwd_kernel<<<n, 256, (size_t)2 * t * 4, ctx->stream>>>(dz, x, w, t, c, p, dx, part);
   RNN_CHECK_LAUNCH();
-  gl_colsum_final<<<(c + 255) / 256, 256, 0, ctx->stream>>>(part, n, c, dp);
-  RNN_CHECK_LAUNCH();
-  return RNN_OK;
+  return colsum_final(ctx, part, n, c, dp);
 }
 
 // DropPath (vit.rs:40-73): the per-image keep mask comes from Rng::new(seed)
@@ -556,9 +572,7 @@ extern "C" int rnn_droppath_fwd_dev(rnn_ctx* ctx, float* x, int n, size_t per_im
   droppath_mask_kernel<<<1, 32, 0, ctx->stream>>>(seed, n, 1.0f - p, mask);
   RNN_CHECK_LAUNCH();
   const size_t total = (size_t)n * per_image;
-  row_scale_kernel<<<gl_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(x, per_image, total, mask);
-  RNN_CHECK_LAUNCH();
-  return RNN_OK;
+  return row_scale(ctx, x, per_image, total, mask);
 }
 
 extern "C" int rnn_droppath_bwd_dev(rnn_ctx* ctx, float* dy, int n, size_t per_image, const float* mask) {
@@ -567,9 +581,7 @@ extern "C" int rnn_droppath_bwd_dev(rnn_ctx* ctx, float* dy, int n, size_t per_i
   RNN_RANGE(dy, (size_t)n * per_image * 4);
   RNN_RANGE(mask, (size_t)n * 4);
   const size_t total = (size_t)n * per_image;
-  row_scale_kernel<<<gl_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(dy, per_image, total, mask);
-  RNN_CHECK_LAUNCH();
-  return RNN_OK;
+  return row_scale(ctx, dy, per_image, total, mask);
 }
 
 extern "C" int rnn_token_merge_dev(rnn_ctx* ctx, const float* src, int n, int th, int c, float* dst, int backward) {

@@ -8,6 +8,7 @@
 // Linear's three products are GEMMs on the tcgen05 engine.
 #include <algorithm>
 
+#include "colsum.cuh"
 #include "ew.cuh"
 
 namespace rnn {
@@ -73,37 +74,23 @@ __global__ void ln_dx_kernel(const float* __restrict__ dy, const float* __restri
   }
 }
 
-// part[blk][j] = sum over the block's rows of a[r][j] (* bm[r][j] when given)
-constexpr int COL_ROWS = 64;  // rows per partial block
-__global__ void colsum_partial_kernel(const float* __restrict__ a, const float* __restrict__ bm, int rows, int c,
-                                      float* __restrict__ part) {
-  const int blk = blockIdx.y;
-  const int r0 = blk * COL_ROWS, r1 = min(rows, r0 + COL_ROWS);
-  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < c; j += gridDim.x * blockDim.x) {
-    float s = 0.0f;
-    for (int r = r0; r < r1; r++) s += bm ? a[(size_t)r * c + j] * bm[(size_t)r * c + j] : a[(size_t)r * c + j];
-    part[(size_t)blk * c + j] = s;
-  }
-}
-__global__ void colsum_final_kernel(const float* __restrict__ part, int nblk, int c, float* __restrict__ out) {
-  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < c; j += gridDim.x * blockDim.x) {
-    float s = 0.0f;
-    for (int b = 0; b < nblk; b++) s += part[(size_t)b * c + j];
-    out[j] += s;
-  }
-}
-
-// out[c] += sum_r a[r][c] (* bm[r][c]); part is scratch of nblk * c floats
+// out[c] += sum_r a[r][c] (* bm[r][c]); part is scratch of ceil(rows / CS_ROWS) * c floats
 static int colsum(rnn_ctx* ctx, const float* a, const float* bm, int rows, int c, float* part, float* out) {
-  const int nblk = (rows + COL_ROWS - 1) / COL_ROWS;
-  dim3 grid((c + 255) / 256, nblk);
-  colsum_partial_kernel<<<grid, 256, 0, ctx->stream>>>(a, bm, rows, c, part);
-  RNN_CHECK_LAUNCH();
-  colsum_final_kernel<<<(c + 255) / 256, 256, 0, ctx->stream>>>(part, nblk, c, out);
-  RNN_CHECK_LAUNCH();
-  return RNN_OK;
+  return colsum_two_pass(ctx, a, bm, rows, c, part, out);
 }
 
+// float4 form (c % 4 == 0, y and b 16-byte aligned)
+__global__ void bias_add4_kernel(float4* __restrict__ y, const float4* __restrict__ b, size_t total4, int c4) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total4; i += (size_t)gridDim.x * blockDim.x) {
+    float4 v = y[i];
+    const float4 q = __ldg(b + i % c4);
+    v.x += q.x;
+    v.y += q.y;
+    v.z += q.z;
+    v.w += q.w;
+    y[i] = v;
+  }
+}
 __global__ void bias_add_kernel(float* __restrict__ y, const float* __restrict__ b, size_t rows, int c) {
   const size_t total = rows * (size_t)c;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x)
@@ -143,7 +130,7 @@ extern "C" int rnn_layernorm_bwd_dev(rnn_ctx* ctx, const float* dy, const float*
   RNN_RANGE(invstd, (size_t)rows * 4);
   RNN_RANGE(dg, (size_t)c * 4);
   RNN_RANGE(db, (size_t)c * 4);
-  const int nblk = (rows + COL_ROWS - 1) / COL_ROWS;
+  const int nblk = (rows + CS_ROWS - 1) / CS_ROWS;
   RNN_TRY(ensure_ws(ctx, (size_t)nblk * c * 4));
   float* part = static_cast<float*>(ctx->ws);
   // dgamma, dbeta (norm.rs:96-117)
@@ -162,8 +149,13 @@ extern "C" int rnn_linear_fwd_dev(rnn_ctx* ctx, const float* x, int rows, int fi
   if (b && rows > 0) {
     RNN_RANGE(b, (size_t)fout * 4);
     const size_t total = (size_t)rows * fout;
-    bias_add_kernel<<<(unsigned)std::min<size_t>((total + 255) / 256, (size_t)ctx->num_sms * 16), 256, 0,
-                      ctx->stream>>>(y, b, rows, fout);
+    if (fout % 4 == 0 && ((uintptr_t)y & 15) == 0 && ((uintptr_t)b & 15) == 0)
+      bias_add4_kernel<<<(unsigned)std::min<size_t>((total / 4 + 255) / 256, (size_t)ctx->num_sms * 16), 256, 0,
+                         ctx->stream>>>(reinterpret_cast<float4*>(y), reinterpret_cast<const float4*>(b),
+                                        total / 4, fout / 4);
+    else
+      bias_add_kernel<<<(unsigned)std::min<size_t>((total + 255) / 256, (size_t)ctx->num_sms * 16), 256, 0,
+                        ctx->stream>>>(y, b, rows, fout);
     RNN_CHECK_LAUNCH();
   }
   return RNN_OK;
@@ -177,7 +169,7 @@ extern "C" int rnn_linear_bwd_dev(rnn_ctx* ctx, const float* x, const float* dy,
   RNN_TRY(tc::gemm_dev(ctx, fout, fin, rows, dy, true, x, false, dw, true, true));
   if (db) {
     RNN_RANGE(db, (size_t)fout * 4);
-    const int nblk = (rows + COL_ROWS - 1) / COL_ROWS;
+    const int nblk = (rows + CS_ROWS - 1) / CS_ROWS;
     RNN_TRY(ensure_aux(ctx, (size_t)nblk * fout * 4));
     RNN_TRY(colsum(ctx, dy, nullptr, rows, fout, static_cast<float*>(ctx->aux), db));
   }
