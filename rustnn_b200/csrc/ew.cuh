@@ -34,6 +34,10 @@ struct ConvStats {
 };
 int gemm_dev(rnn_ctx* ctx, int m, int n, int k, const float* a, bool at, const float* b, bool bt, float* c,
              bool acc, bool force_split);
+// batch same-shape GEMMs in one launch: C_i (+)= op(A_i) op(B_i), item i at
+// a + i*sa, b + i*sb, c + i*sc (strides in floats)
+int gemm_batched_dev(rnn_ctx* ctx, int batch, int m, int n, int k, const float* a, size_t sa, bool at,
+                     const float* b, size_t sb, bool bt, float* c, size_t sc, bool acc);
 int conv_fwd(rnn_ctx* ctx, const float* x, int n, int cin, int h, int w, const float* wt, int cout, int k,
              int stride, int pad, float* y, bool acc, ConvStats* stats = nullptr);
 int conv_dgrad(rnn_ctx* ctx, const float* dy, int n, int cin, int h, int w, const float* wt, int cout, int k,
@@ -45,5 +49,12 @@ int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, in
 // tile width, 32-pixel K blocks); 0 when it would not use one.
 int wgrad_dy_pack_bn(int n, int cout, int k, int oh, int ow, const void* dy);
 }  // namespace tc
+// Newton-Schulz (optim.rs:124-145) in place on `count` matrices, the
+// matrices of one working shape batched into shared launches (optim.cu)
+int newton_schulz_grouped(rnn_ctx* ctx, int count, float* const* g, const int* rows, const int* cols, int steps);
+// Muon's momentum (optim.rs:186-190) and update (optim.rs:192-196) of one
+// matrix; rnn_muon_step_dev is momentum, newton_schulz, update
+int muon_momentum(rnn_ctx* ctx, float* g, float* m, size_t n, float mom);
+int muon_update(rnn_ctx* ctx, float* v, float* g, int rows, int cols, float lr, float wd, int decay);
 
 }  // namespace rnn

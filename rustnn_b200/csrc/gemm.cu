@@ -116,6 +116,135 @@ static int gemm_typed(rnn_ctx* ctx, int m, int n, int k, const float* a, const f
   }
 }
 
+// A batch of same-shape GEMMs in one launch: C_i (+)= op(A_i) op(B_i) for
+// i < batch, the operands of item i at a + i*sa, b + i*sb, c + i*sc.  The
+// M dimension of the schedule stacks the items, each padded to whole
+// 128-row tiles (mp rows), so a tile never spans two items; the tile's item
+// selects the A and B operands and the C block.  No split over K: the items
+// fill the SMs.
+template <bool AT, bool BT, int BN>
+struct BatchedDenseProb {
+  static constexpr bool A_KMAJOR = !AT;
+  static constexpr bool B_KMAJOR = BT;
+  static constexpr bool B_BULK = false;
+  const float* a;
+  const float* b;
+  float* c;
+  size_t sa, sb, sc;
+  int M, N, K, mp;
+  int acc;
+  bool a_vec, b_vec, c_vec;
+
+  struct TS {
+    int item, m0, n0;
+  };
+  __device__ __forceinline__ void tile_begin(TS& ts, int m0, int n0, int) const {
+    ts.item = m0 / mp;
+    ts.m0 = m0 - ts.item * mp;
+    ts.n0 = n0;
+  }
+  static __device__ __forceinline__ void a_slot(int gt, int j, int& r, int& c) {
+    if (A_KMAJOR) { r = (gt >> 3) + 16 * j; c = gt & 7; }
+    else { r = gt; c = j; }
+  }
+  static __device__ __forceinline__ void b_slot(int gt, int j, int& r, int& c) {
+    const int idx = gt + 128 * j;
+    if (B_KMAJOR) { r = idx >> 3; c = idx & 7; }
+    else { r = idx % BN; c = idx / BN; }
+  }
+  __device__ __forceinline__ void load_a(const TS& ts, int kb, int gt, float (&v)[32]) const {
+    const float* ai = a + (size_t)ts.item * sa;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      int r, cc;
+      a_slot(gt, j, r, cc);
+      const int row = ts.m0 + r, k4 = kb * BK + 4 * cc;
+      if (!AT && row < M && a_vec && k4 + 3 < K) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(ai + (size_t)row * K + k4));
+        v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+          v[4 * j + i] = (row < M && k4 + i < K)
+                             ? __ldg(AT ? ai + (size_t)(k4 + i) * M + row : ai + (size_t)row * K + k4 + i)
+                             : 0.0f;
+      }
+    }
+  }
+  template <int NB>
+  __device__ __forceinline__ void load_b(const TS& ts, int kb, int gt, float (&v)[NB]) const {
+    const float* bi = b + (size_t)ts.item * sb;
+#pragma unroll
+    for (int j = 0; j < NB / 4; j++) {
+      int r, cc;
+      b_slot(gt, j, r, cc);
+      const int row = ts.n0 + r, k4 = kb * BK + 4 * cc;
+      if (BT && row < N && b_vec && k4 + 3 < K) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(bi + (size_t)row * K + k4));
+        v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+          v[4 * j + i] = (row < N && k4 + i < K)
+                             ? __ldg(BT ? bi + (size_t)row * K + k4 + i : bi + (size_t)(k4 + i) * N + row)
+                             : 0.0f;
+      }
+    }
+  }
+  __device__ __forceinline__ const void* b_src(int, int) const { return nullptr; }
+  __device__ __forceinline__ void store(int row, int col0, int, const float (&v)[32]) const {
+    const int item = row / mp, r = row - item * mp;
+    if (r >= M || col0 >= N) return;
+    store_row32(c + (size_t)item * sc + (size_t)r * N + col0, N - col0, v, acc != 0, c_vec);
+  }
+};
+
+template <int BN, bool AT, bool BT>
+static int gemm_batched_bn(rnn_ctx* ctx, int batch, int m, int n, int k, const float* a, size_t sa, const float* b,
+                           size_t sb, float* c, size_t sc, bool acc) {
+  BatchedDenseProb<AT, BT, BN> p;
+  p.a = a; p.b = b; p.c = c;
+  p.sa = sa; p.sb = sb; p.sc = sc;
+  p.M = m; p.N = n; p.K = k;
+  const int m_tiles = (m + BM - 1) / BM;
+  p.mp = m_tiles * BM;
+  p.acc = acc ? 1 : 0;
+  p.a_vec = (k % 4 == 0) && al16(a) && sa % 4 == 0;
+  p.b_vec = (k % 4 == 0) && al16(b) && sb % 4 == 0;
+  p.c_vec = (n % 4 == 0) && al16(c) && sc % 4 == 0;
+  const Sched s = make_sched(batch * p.mp, n, k, BN, 1);
+  return launch_native<BN>(ctx, p, s);
+}
+
+template <bool AT, bool BT>
+static int gemm_batched_typed(rnn_ctx* ctx, int batch, int m, int n, int k, const float* a, size_t sa,
+                              const float* b, size_t sb, float* c, size_t sc, bool acc) {
+  const int bn = pick_bn(n, batch * ((m + BM - 1) / BM), ctx->num_sms);
+  switch (bn) {
+    case 32: return gemm_batched_bn<32, AT, BT>(ctx, batch, m, n, k, a, sa, b, sb, c, sc, acc);
+    case 64: return gemm_batched_bn<64, AT, BT>(ctx, batch, m, n, k, a, sa, b, sb, c, sc, acc);
+    case 128: return gemm_batched_bn<128, AT, BT>(ctx, batch, m, n, k, a, sa, b, sb, c, sc, acc);
+    default: return gemm_batched_bn<256, AT, BT>(ctx, batch, m, n, k, a, sa, b, sb, c, sc, acc);
+  }
+}
+
+int gemm_batched_dev(rnn_ctx* ctx, int batch, int m, int n, int k, const float* a, size_t sa, bool at,
+                     const float* b, size_t sb, bool bt, float* c, size_t sc, bool acc) {
+  RNN_REQUIRE(batch >= 0 && m >= 0 && n >= 0 && k > 0, "gemm_batched: bad size batch=%d m=%d n=%d k=%d", batch, m,
+              n, k);
+  if (batch == 0 || m == 0 || n == 0) return RNN_OK;
+  RNN_REQUIRE(a && b && c, "gemm_batched: null operand");
+  RNN_REQUIRE(sa >= (size_t)m * k && sb >= (size_t)n * k && sc >= (size_t)m * n,
+              "gemm_batched: item strides overlap");
+  RNN_RANGE(a, sizeof(float) * ((size_t)(batch - 1) * sa + (size_t)m * k));
+  RNN_RANGE(b, sizeof(float) * ((size_t)(batch - 1) * sb + (size_t)n * k));
+  RNN_RANGE(c, sizeof(float) * ((size_t)(batch - 1) * sc + (size_t)m * n));
+  if (!at && !bt) return gemm_batched_typed<false, false>(ctx, batch, m, n, k, a, sa, b, sb, c, sc, acc);
+  if (!at && bt) return gemm_batched_typed<false, true>(ctx, batch, m, n, k, a, sa, b, sb, c, sc, acc);
+  if (at && !bt) return gemm_batched_typed<true, false>(ctx, batch, m, n, k, a, sa, b, sb, c, sc, acc);
+  return gemm_batched_typed<true, true>(ctx, batch, m, n, k, a, sa, b, sb, c, sc, acc);
+}
+
 __global__ void zero_kernel(float* c, size_t len) {
   size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   size_t stride = (size_t)gridDim.x * blockDim.x;

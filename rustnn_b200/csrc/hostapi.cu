@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "ew.cuh"
 
 using namespace rnn;
 
@@ -265,8 +266,12 @@ extern "C" int rnn_batchnorm_bwd(rnn_ctx* ctx, const float* dy, const float* y, 
 extern "C" int rnn_newton_schulz_batched_dev(rnn_ctx* ctx, int count, float* const* g, const int* rows,
                                              const int* cols, int steps) {
   RNN_REQUIRE(ctx && count >= 0 && (count == 0 || (g && rows && cols)), "newton_schulz_batched: bad arguments");
-  for (int i = 0; i < count; i++) RNN_TRY(rnn_newton_schulz_dev(ctx, g[i], rows[i], cols[i], steps));
-  return RNN_OK;
+  for (int i = 0; i < count; i++) {
+    RNN_REQUIRE(g[i] && rows[i] > 0 && cols[i] > 0, "newton_schulz_batched: matrix %d is empty", i);
+    RNN_RANGE(g[i], (size_t)rows[i] * cols[i] * 4);
+  }
+  RNN_REQUIRE(steps >= 0, "newton_schulz_batched: negative steps");
+  return rnn::newton_schulz_grouped(ctx, count, g, rows, cols, steps);
 }
 
 extern "C" int rnn_newton_schulz_batched(rnn_ctx* ctx, int count, float* const* g, const int* rows,

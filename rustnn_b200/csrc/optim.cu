@@ -11,6 +11,8 @@
 // optim.rs:238-241).
 #include <algorithm>
 #include <cmath>
+#include <utility>
+#include <vector>
 
 #include "ew.cuh"
 
@@ -123,6 +125,103 @@ int newton_schulz(rnn_ctx* ctx, float* g, int rows, int cols, int steps, float* 
   return RNN_OK;
 }
 
+// ---- Newton-Schulz over many matrices at once
+//
+// Matrices with one working shape (m = min(rows, cols), n = max) form a
+// group whose items sit back to back in scratch: one launch normalises all
+// of them, each of the three products per iteration is one batched GEMM
+// over the group, and the b A + c AA and a X + T combinations run over the
+// whole group's buffer.  Per item the arithmetic is that of newton_schulz:
+// the same f32 sum-of-squares slices (RED_BLOCKS per item, combined in the
+// same order) and the same products.
+
+// part[item][b] = f32 sum of squares over block b's slice of item's x
+__global__ void sumsq_items_kernel(const float* __restrict__ x, size_t n, double* __restrict__ part) {
+  __shared__ double sh[256];
+  const float* xi = x + (size_t)blockIdx.y * n;
+  float sf = 0.0f;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    sf += xi[i] * xi[i];
+  sh[threadIdx.x] = (double)sf;
+  __syncthreads();
+  for (int k = 128; k > 0; k >>= 1) {
+    if (threadIdx.x < k) sh[threadIdx.x] += sh[threadIdx.x + k];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) part[(size_t)blockIdx.y * gridDim.x + blockIdx.x] = sh[0];
+}
+
+// x_item *= 1 / (sqrt(sum of its partials) + 1e-7)
+__global__ void ns_scale_items_kernel(float* __restrict__ x, size_t n, const double* __restrict__ part, int nb) {
+  __shared__ float inv;
+  if (threadIdx.x == 0) {
+    double s = 0.0;
+    for (int b = 0; b < nb; b++) s += part[(size_t)blockIdx.y * nb + b];
+    inv = 1.0f / (sqrtf((float)s) + 1e-7f);
+  }
+  __syncthreads();
+  float* xi = x + (size_t)blockIdx.y * n;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    xi[i] *= inv;
+}
+
+int newton_schulz_grouped(rnn_ctx* ctx, int count, float* const* g, const int* rows, const int* cols, int steps) {
+  // groups by working shape, in first-appearance order
+  std::vector<std::pair<int, int>> shapes;
+  std::vector<std::vector<int>> members;
+  for (int i = 0; i < count; i++) {
+    const int m = std::min(rows[i], cols[i]), n = std::max(rows[i], cols[i]);
+    size_t gi = 0;
+    while (gi < shapes.size() && shapes[gi] != std::make_pair(m, n)) gi++;
+    if (gi == shapes.size()) {
+      shapes.push_back({m, n});
+      members.emplace_back();
+    }
+    members[gi].push_back(i);
+  }
+  size_t need = 0;
+  for (size_t gi = 0; gi < shapes.size(); gi++) {
+    const size_t m = shapes[gi].first, n = shapes[gi].second, c = members[gi].size();
+    need = std::max(need, c * (2 * m * n + 2 * m * m) * 4 + c * RED_BLOCKS * 8 + 256);
+  }
+  RNN_TRY(ensure_aux(ctx, need));
+  for (size_t gi = 0; gi < shapes.size(); gi++) {
+    const int m = shapes[gi].first, n = shapes[gi].second, cnt = (int)members[gi].size();
+    const size_t mn = (size_t)m * n, mm = (size_t)m * m;
+    float* x = static_cast<float*>(ctx->aux);
+    float* t = x + cnt * mn;
+    float* a = t + cnt * mn;
+    float* aa = a + cnt * mm;
+    double* part = reinterpret_cast<double*>(
+        (reinterpret_cast<uintptr_t>(aa + cnt * mm) + 255) & ~static_cast<uintptr_t>(255));
+    for (int j = 0; j < cnt; j++) {
+      const int i = members[gi][j];
+      if (rows[i] > cols[i]) RNN_TRY(transpose(ctx, g[i], rows[i], cols[i], x + j * mn));
+      else RNN_CUDA(cudaMemcpyAsync(x + j * mn, g[i], mn * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+    }
+    sumsq_items_kernel<<<dim3(RED_BLOCKS, cnt), 256, 0, ctx->stream>>>(x, mn, part);
+    RNN_CHECK_LAUNCH();
+    const unsigned gx = std::max(1u, egrid(mn, ctx->num_sms) / (unsigned)cnt);
+    ns_scale_items_kernel<<<dim3(gx, cnt), 256, 0, ctx->stream>>>(x, mn, part, RED_BLOCKS);
+    RNN_CHECK_LAUNCH();
+    for (int st = 0; st < steps; st++) {
+      RNN_TRY(tc::gemm_batched_dev(ctx, cnt, m, m, n, x, mn, false, x, mn, true, a, mm, false));   // A = X X^T
+      RNN_TRY(tc::gemm_batched_dev(ctx, cnt, m, m, m, a, mm, false, a, mm, false, aa, mm, false)); // AA = A A
+      ns_poly_kernel<<<egrid(cnt * mm, ctx->num_sms), 256, 0, ctx->stream>>>(a, aa, cnt * mm);
+      RNN_CHECK_LAUNCH();
+      RNN_TRY(tc::gemm_batched_dev(ctx, cnt, m, n, m, a, mm, false, x, mn, false, t, mn, false));  // T = B X
+      ns_axpy_kernel<<<egrid(cnt * mn, ctx->num_sms), 256, 0, ctx->stream>>>(x, t, cnt * mn);
+      RNN_CHECK_LAUNCH();
+    }
+    for (int j = 0; j < cnt; j++) {
+      const int i = members[gi][j];
+      if (rows[i] > cols[i]) RNN_TRY(transpose(ctx, x + j * mn, m, n, g[i]));
+      else RNN_CUDA(cudaMemcpyAsync(g[i], x + j * mn, mn * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+    }
+  }
+  return RNN_OK;
+}
+
 // Muon momentum (optim.rs:186-190): m = mom m + g; g += mom m
 __global__ void muon_mom_kernel(float* __restrict__ g, float* __restrict__ m, size_t n, float mom) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
@@ -189,20 +288,34 @@ extern "C" int rnn_newton_schulz_dev(rnn_ctx* ctx, float* g, int rows, int cols,
   return newton_schulz(ctx, g, rows, cols, steps, static_cast<float*>(ctx->aux));
 }
 
-extern "C" int rnn_muon_step_dev(rnn_ctx* ctx, float* v, float* g, float* m, int rows, int cols, int steps, float lr,
-                                 float mom, float wd, int decay) {
-  RNN_REQUIRE(ctx && v && g && m && rows > 0 && cols > 0, "muon_step: bad arguments");
-  const size_t n = (size_t)rows * cols;
-  RNN_RANGE(v, n * 4);
+namespace rnn {
+
+int muon_momentum(rnn_ctx* ctx, float* g, float* m, size_t n, float mom) {
   RNN_RANGE(g, n * 4);
   RNN_RANGE(m, n * 4);
   muon_mom_kernel<<<egrid(n, ctx->num_sms), 256, 0, ctx->stream>>>(g, m, n, mom);
   RNN_CHECK_LAUNCH();
-  RNN_TRY(rnn_newton_schulz_dev(ctx, g, rows, cols, steps));
+  return RNN_OK;
+}
+
+int muon_update(rnn_ctx* ctx, float* v, float* g, int rows, int cols, float lr, float wd, int decay) {
+  const size_t n = (size_t)rows * cols;
+  RNN_RANGE(v, n * 4);
+  RNN_RANGE(g, n * 4);
   const float scale = 0.2f * sqrtf((float)std::max(rows, cols));
   muon_update_kernel<<<egrid(n, ctx->num_sms), 256, 0, ctx->stream>>>(v, g, n, lr, scale, decay ? wd : 0.0f);
   RNN_CHECK_LAUNCH();
   return RNN_OK;
+}
+
+}  // namespace rnn
+
+extern "C" int rnn_muon_step_dev(rnn_ctx* ctx, float* v, float* g, float* m, int rows, int cols, int steps, float lr,
+                                 float mom, float wd, int decay) {
+  RNN_REQUIRE(ctx && v && g && m && rows > 0 && cols > 0, "muon_step: bad arguments");
+  RNN_TRY(rnn::muon_momentum(ctx, g, m, (size_t)rows * cols, mom));
+  RNN_TRY(rnn_newton_schulz_dev(ctx, g, rows, cols, steps));
+  return rnn::muon_update(ctx, v, g, rows, cols, lr, wd, decay);
 }
 
 extern "C" int rnn_adamw_step_dev(rnn_ctx* ctx, float* v, float* g, float* m, float* v2, size_t n, float lr, float wd,

@@ -24,6 +24,7 @@
 #include "ckpt.cuh"
 #include "common.cuh"
 #include "eval.cuh"
+#include "ew.cuh"
 #include "rng.h"
 
 namespace rnn {
@@ -1006,12 +1007,27 @@ static bool is_muon(const HostParam& p) { return p.rows > 0 && std::min(p.rows, 
 // the rest (consecutive parameters with the same decay flag in one call).
 static int step_all(rnn_rustvit* net, float lr, float wd) {
   rnn_ctx* ctx = net->ctx;
+  // Muon (optim.rs:183-196) per matrix: momentum, Newton-Schulz, update.
+  // The matrices are independent, so the momentum of all of them runs
+  // first, then one grouped Newton-Schulz over every gradient, then the
+  // updates.
+  std::vector<float*> mg;
+  std::vector<int> mr, mc;
   for (int id : net->order) {
     const HostParam& p = net->R.ps[id];
     if (!is_muon(p)) continue;
     const size_t o = net->off[id];
-    RNN_TRY(rnn_muon_step_dev(ctx, net->V + o, net->G + o, net->M + o, p.rows, p.cols, 3, lr, 0.95f, wd,
-                              p.decay ? 1 : 0));
+    RNN_TRY(rnn::muon_momentum(ctx, net->G + o, net->M + o, (size_t)p.rows * p.cols, 0.95f));
+    mg.push_back(net->G + o);
+    mr.push_back(p.rows);
+    mc.push_back(p.cols);
+  }
+  RNN_TRY(rnn::newton_schulz_grouped(ctx, (int)mg.size(), mg.data(), mr.data(), mc.data(), 3));
+  for (int id : net->order) {
+    const HostParam& p = net->R.ps[id];
+    if (!is_muon(p)) continue;
+    const size_t o = net->off[id];
+    RNN_TRY(rnn::muon_update(ctx, net->V + o, net->G + o, p.rows, p.cols, lr, wd, p.decay ? 1 : 0));
   }
   size_t run0 = 0, runlen = 0;
   int rundecay = -1;

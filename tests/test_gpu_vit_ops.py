@@ -248,3 +248,32 @@ def test_muon_adamw_clip_ema_parity(ops):
     ed = dev(e)
     ops.ema_update_(ed, dev(w), 0.9998, 5)
     assert rel(host(ed), er) < 1e-6
+
+
+def test_newton_schulz_grouped_rustvit_matrices(ops):
+    """Newton-Schulz over all 39 Muon matrices of the default rustvit at once
+    (rnn_newton_schulz_batched_dev: same-shape matrices batched into shared
+    GEMM launches, tall ones transposed in and out) against one matrix at a
+    time, and the small shapes against the oracle (optim.rs:124-145)."""
+    import ctypes as C
+
+    from rustnn_b200 import _lib
+    from rustnn_b200.kernel_bench import RUSTVIT_2D
+
+    rng = np.random.default_rng(8)
+    mats = [rng.standard_normal(r * c).astype(np.float32) for r, c in RUSTVIT_2D]
+    one = [dev(m) for m in mats]
+    for t, (r, c) in zip(one, RUSTVIT_2D):
+        ops.newton_schulz_(t, r, c, 3)
+    grp = [dev(m) for m in mats]
+    ptrs = (C.c_void_p * len(grp))(*[t.data_ptr() for t in grp])
+    rows = (C.c_int * len(grp))(*[r for r, _ in RUSTVIT_2D])
+    cols = (C.c_int * len(grp))(*[c for _, c in RUSTVIT_2D])
+    ctx = ops.default_context()
+    _lib.call("rnn_newton_schulz_batched_dev", ctx.bind(), len(grp), C.cast(ptrs, C.c_void_p),
+              C.cast(rows, C.c_void_p), C.cast(cols, C.c_void_p), 3)
+    torch.cuda.synchronize()
+    for a, b, (r, c), m in zip(grp, one, RUSTVIT_2D, mats):
+        assert rel(host(a), host(b)) < TOL, (r, c)
+        if r * c <= 40000:
+            assert rel(host(a), O.newton_schulz(m, r, c, 3)) < TOL, (r, c)
