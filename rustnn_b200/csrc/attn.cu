@@ -108,6 +108,22 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// sum_j w[j] * col[j * ld] with four independent accumulators (j mod 4),
+// combined as (a0 + a1) + (a2 + a3): a tk-long dependent FMA chain becomes
+// four chains a quarter as long
+__device__ __forceinline__ float row_dot4(const float* __restrict__ w, const float* __restrict__ col, int ld, int tk) {
+  float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+  int j = 0;
+  for (; j + 3 < tk; j += 4) {
+    a0 = fmaf(w[j], col[j * ld], a0);
+    a1 = fmaf(w[j + 1], col[(j + 1) * ld], a1);
+    a2 = fmaf(w[j + 2], col[(j + 2) * ld], a2);
+    a3 = fmaf(w[j + 3], col[(j + 3) * ld], a3);
+  }
+  for (; j < tk; j++) a0 = fmaf(w[j], col[j * ld], a0);
+  return (a0 + a1) + (a2 + a3);
+}
+
 // K and V of one (image, head) into shared memory, rows padded to DH+1
 // floats (a lane walking its own key row hits a distinct bank).
 template <int DH>
@@ -187,11 +203,7 @@ __global__ void __launch_bounds__(AT_THREADS) attn_fwd_kernel(const AttnArgs a) 
     }
     __syncwarp();
     float* og = a.o + ((size_t)img * a.tq + qi) * c + hd * DH;
-    for (int d = l; d < DH; d += 32) {
-      float acc = 0.0f;
-      for (int j = 0; j < tk; j++) acc = fmaf(prow[j], Vs[j * LD + d], acc);
-      og[d] = acc;
-    }
+    for (int d = l; d < DH; d += 32) og[d] = row_dot4(prow, Vs + d, LD, tk);
     __syncwarp();
   }
 }
@@ -271,11 +283,7 @@ __global__ void __launch_bounds__(AT_THREADS) attn_bwd_rows_kernel(const AttnArg
     }
     __syncwarp();
     float* dqg = a.dq + ((size_t)img * a.tq + qi) * a.qstride + a.qoff + hd * DH;
-    for (int d = l; d < DH; d += 32) {
-      float acc = 0.0f;
-      for (int j = 0; j < tk; j++) acc = fmaf(dsrow[j], Ks[j * LD + d], acc);
-      dqg[d] += acc;
-    }
+    for (int d = l; d < DH; d += 32) dqg[d] += row_dot4(dsrow, Ks + d, LD, tk);
     __syncwarp();
   }
   tacc = warp_sum(tacc);
