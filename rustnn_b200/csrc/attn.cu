@@ -124,11 +124,23 @@ __device__ __forceinline__ float row_dot4(const float* __restrict__ w, const flo
   return (a0 + a1) + (a2 + a3);
 }
 
-// K and V of one (image, head) into shared memory, rows padded to DH+1
-// floats (a lane walking its own key row hits a distinct bank).
-template <int DH>
+// Row length of K and V in the forward kernel's shared memory.  A lane walks
+// its own key row, so the rows are padded: with DH a multiple of 4 the rows are read as float4
+// and hold an odd number of 16-byte units (DH, or DH + 4), which keeps the
+// eight lanes of each quarter-warp LDS.128 phase on distinct banks; other
+// head dims are read as floats from rows of DH + 1.
+__host__ __device__ constexpr int attn_ld(int dh) {
+  return dh % 4 != 0 ? dh + 1 : ((dh / 4) % 2 == 1 ? dh : dh + 4);
+}
+// The backward's row kernel reads its rows as float4 only from head dim 64
+// up (measured: faster at 64, slower at 32, where the wider rows cost
+// occupancy); below that it keeps scalar walks over rows of DH + 1.
+__host__ __device__ constexpr bool attn_bwd_vec(int dh) { return dh >= 64 && dh % 4 == 0; }
+__host__ __device__ constexpr int attn_bwd_ld(int dh) { return attn_bwd_vec(dh) ? attn_ld(dh) : dh + 1; }
+
+// K and V of one (image, head) into shared memory, rows of LD floats.
+template <int DH, int LD>
 __device__ __forceinline__ void load_kv(const AttnArgs& a, int img, int hd, float* Ks, float* Vs) {
-  constexpr int LD = DH + 1;
   for (int e = threadIdx.x; e < a.tk * DH; e += AT_THREADS) {
     const int r = e / DH, d = e - r * DH;
     const float* row = a.kv + ((size_t)img * a.tk + r) * a.kvstride + hd * DH + d;
@@ -144,14 +156,14 @@ __device__ __forceinline__ void load_kv(const AttnArgs& a, int img, int hd, floa
 // O[i][d] = sum_j P[i][j] V[j][d].
 template <int DH>
 __global__ void __launch_bounds__(AT_THREADS) attn_fwd_kernel(const AttnArgs a) {
-  extern __shared__ float sm[];
-  constexpr int LD = DH + 1;
+  extern __shared__ __align__(16) float sm[];
+  constexpr int LD = attn_ld(DH);
   const int hd = blockIdx.x, img = blockIdx.y, q0 = blockIdx.z * a.qc;
   const int rows = min(a.qc, a.tq - q0), tk = a.tk, c = a.h * DH;
   float* Ks = sm;
   float* Vs = Ks + tk * LD;
   float* Pw = Vs + tk * LD;  // [AT_WARPS][tk]
-  load_kv<DH>(a, img, hd, Ks, Vs);
+  load_kv<DH, LD>(a, img, hd, Ks, Vs);
   __syncthreads();
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   const float t = a.tau[hd];
@@ -173,8 +185,19 @@ __global__ void __launch_bounds__(AT_THREADS) attn_fwd_kernel(const AttnArgs a) 
       if (j < tk) {
         const float* kr = Ks + j * LD;
         float acc = 0.0f;
+        if constexpr (DH % 4 == 0) {
 #pragma unroll
-        for (int d = 0; d < DH; d++) acc = fmaf(qr[d], kr[d], acc);
+          for (int d = 0; d < DH; d += 4) {
+            const float4 k4 = *reinterpret_cast<const float4*>(kr + d);
+            acc = fmaf(qr[d], k4.x, acc);
+            acc = fmaf(qr[d + 1], k4.y, acc);
+            acc = fmaf(qr[d + 2], k4.z, acc);
+            acc = fmaf(qr[d + 3], k4.w, acc);
+          }
+        } else {
+#pragma unroll
+          for (int d = 0; d < DH; d++) acc = fmaf(qr[d], kr[d], acc);
+        }
         val = t * acc + rb[ridx[j]];  // attn.rs:181-190
         if (a.mask && j == qi) val = -INFINITY;  // attn.rs:194
       }
@@ -217,8 +240,8 @@ __global__ void __launch_bounds__(AT_THREADS) attn_fwd_kernel(const AttnArgs a) 
 // Partials (dtau, drel) per CTA are summed in a fixed order afterwards.
 template <int DH>
 __global__ void __launch_bounds__(AT_THREADS) attn_bwd_rows_kernel(const AttnArgs a) {
-  extern __shared__ float sm[];
-  constexpr int LD = DH + 1;
+  extern __shared__ __align__(16) float sm[];
+  constexpr int LD = attn_bwd_ld(DH);
   const int hd = blockIdx.x, img = blockIdx.y, chunk = blockIdx.z, q0 = chunk * a.qc;
   const int rows = min(a.qc, a.tq - q0), tk = a.tk, c = a.h * DH, nrel = a.nrel;
   float* Ks = sm;
@@ -226,7 +249,7 @@ __global__ void __launch_bounds__(AT_THREADS) attn_bwd_rows_kernel(const AttnArg
   float* Dw = Vs + tk * LD;              // [AT_WARPS][tk] tau * dS row
   float* Rw = Dw + AT_WARPS * tk;        // [AT_WARPS][nrel] drel per warp
   __shared__ float red[AT_WARPS];
-  load_kv<DH>(a, img, hd, Ks, Vs);
+  load_kv<DH, LD>(a, img, hd, Ks, Vs);
   for (int e = threadIdx.x; e < AT_WARPS * nrel; e += AT_THREADS) Rw[e] = 0.0f;
   __syncthreads();
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -255,10 +278,26 @@ __global__ void __launch_bounds__(AT_THREADS) attn_bwd_rows_kernel(const AttnArg
         const float* kr = Ks + j * LD;
         const float* vr = Vs + j * LD;
         float s1 = 0.0f, s2 = 0.0f;
+        if constexpr (attn_bwd_vec(DH)) {
 #pragma unroll
-        for (int d = 0; d < DH; d++) {
-          s1 = fmaf(dr[d], vr[d], s1);
-          s2 = fmaf(qr[d], kr[d], s2);
+          for (int d = 0; d < DH; d += 4) {
+            const float4 v4 = *reinterpret_cast<const float4*>(vr + d);
+            const float4 k4 = *reinterpret_cast<const float4*>(kr + d);
+            s1 = fmaf(dr[d], v4.x, s1);
+            s2 = fmaf(qr[d], k4.x, s2);
+            s1 = fmaf(dr[d + 1], v4.y, s1);
+            s2 = fmaf(qr[d + 1], k4.y, s2);
+            s1 = fmaf(dr[d + 2], v4.z, s1);
+            s2 = fmaf(qr[d + 2], k4.z, s2);
+            s1 = fmaf(dr[d + 3], v4.w, s1);
+            s2 = fmaf(qr[d + 3], k4.w, s2);
+          }
+        } else {
+#pragma unroll
+          for (int d = 0; d < DH; d++) {
+            s1 = fmaf(dr[d], vr[d], s1);
+            s2 = fmaf(qr[d], kr[d], s2);
+          }
         }
         dp[k] = s1;
         raw[k] = s2;
@@ -310,7 +349,7 @@ __global__ void __launch_bounds__(AT_THREADS) attn_bwd_rows_kernel(const AttnArg
 // and all Q / dO rows staged in shared memory.
 template <int DH>
 __global__ void __launch_bounds__(AT_THREADS) attn_bwd_cols_kernel(const AttnArgs a) {
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) float sm[];
   constexpr int KPW = AT_KC / AT_WARPS;       // keys per warp
   constexpr int DPL = (DH + 31) / 32;         // columns per lane
   const int hd = blockIdx.x, img = blockIdx.y, k0 = blockIdx.z * AT_KC;
@@ -398,10 +437,10 @@ __global__ void attn_reduce_kernel(const float* __restrict__ part, int items, in
 constexpr size_t ATT_SMEM_CAP = 200 * 1024;
 
 static size_t fwd_smem(int dh, int tk) {
-  return sizeof(float) * (2 * (size_t)tk * (dh + 1) + (size_t)AT_WARPS * tk);
+  return sizeof(float) * (2 * (size_t)tk * attn_ld(dh) + (size_t)AT_WARPS * tk);
 }
 static size_t rows_smem(int dh, int tk, int nrel) {
-  return sizeof(float) * (2 * (size_t)tk * (dh + 1) + (size_t)AT_WARPS * tk + (size_t)AT_WARPS * nrel);
+  return sizeof(float) * (2 * (size_t)tk * attn_bwd_ld(dh) + (size_t)AT_WARPS * tk + (size_t)AT_WARPS * nrel);
 }
 static size_t cols_smem(int dh, int tq) {
   return sizeof(float) * (2 * (size_t)tq * dh + 2 * (size_t)tq * AT_KC);
