@@ -68,8 +68,10 @@ __global__ void __launch_bounds__(256) cs_final4_kernel(const float4* __restrict
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int j = blockIdx.x * 32 + lane;
   float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  if (j < c4)
+  if (j < c4) {
+#pragma unroll 8
     for (int b = w; b < nb; b += 8) cs_add4(s, __ldg(part + (size_t)b * c4 + j));
+  }
   red[w][lane] = s;
   __syncthreads();
   if (w == 0 && j < c4) {

@@ -131,9 +131,9 @@ int newton_schulz(rnn_ctx* ctx, float* g, int rows, int cols, int steps, float* 
 // group whose items sit back to back in scratch: one launch normalises all
 // of them, each of the three products per iteration is one batched GEMM
 // over the group, and the b A + c AA and a X + T combinations run over the
-// whole group's buffer.  Per item the arithmetic is that of newton_schulz:
-// the same f32 sum-of-squares slices (RED_BLOCKS per item, combined in the
-// same order) and the same products.
+// whole group's buffer.  Per item the arithmetic is that of newton_schulz
+// (the same f32 sum-of-squares slices, RED_BLOCKS per item, whose f64 sums
+// are combined by a warp instead of one thread) and the same products.
 
 // part[item][b] = f32 sum of squares over block b's slice of item's x
 __global__ void sumsq_items_kernel(const float* __restrict__ x, size_t n, double* __restrict__ part) {
@@ -154,10 +154,12 @@ __global__ void sumsq_items_kernel(const float* __restrict__ x, size_t n, double
 // x_item *= 1 / (sqrt(sum of its partials) + 1e-7)
 __global__ void ns_scale_items_kernel(float* __restrict__ x, size_t n, const double* __restrict__ part, int nb) {
   __shared__ float inv;
-  if (threadIdx.x == 0) {
+  if (threadIdx.x < 32) {  // lane l sums partials l, l+32, ..., then a fixed shuffle tree
     double s = 0.0;
-    for (int b = 0; b < nb; b++) s += part[(size_t)blockIdx.y * nb + b];
-    inv = 1.0f / (sqrtf((float)s) + 1e-7f);
+    for (int b = threadIdx.x; b < nb; b += 32) s += part[(size_t)blockIdx.y * nb + b];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (threadIdx.x == 0) inv = 1.0f / (sqrtf((float)s) + 1e-7f);
   }
   __syncthreads();
   float* xi = x + (size_t)blockIdx.y * n;
