@@ -12,6 +12,7 @@ forward + softmax_ce + backward + allreduce + SGD-Nesterov (train.rs:684-699).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config resnet56|resnet20|rustvit]
     python bench.py --impl reference ...   # the CPU reference arm
     python bench.py --workload eval        # eval::resnet over a 10,000-image split
+    python bench.py --workload train-data  # the step fed by the device batch builder
 
 --config rustvit (BASELINE config 4): the default rustvit (Cfg::default,
 6.37 M parameters) at batch 128 on one GPU; one step = Trainer::step
@@ -408,6 +409,70 @@ def run_ours_eval(args, cfg_name):
     return 0
 
 
+def run_ours_train_data(args, cfg_name):
+    """The training step fed from a device-resident u8 dataset: per step the
+    host sends the batch's indices (train.rs:675-680) and the device builds
+    the batch (data::make_batch_train with the ResNet loop's augmentation:
+    pad 4, erase 1.0, cutout 8; train.rs:654-660, cli.rs:77-78), then runs
+    the step.  One GPU."""
+    import torch
+
+    from rustnn_b200 import _lib, data, model
+
+    depth_n, width, gbatch, cfg_idx = CONFIGS[cfg_name]
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1 and int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    ntrain = 50_000  # the size of the CIFAR-100 training split
+    images, labels = synthetic_dataset(ntrain, 11)
+    images_d, labels_d = torch.from_numpy(images).cuda(), torch.from_numpy(labels).cuda()
+    net = model.ResNet(depth_n, width, NCLASS, 0)
+    if not args.no_graph:
+        net.use_graph(True)
+    aug = data.Aug(pad=4, ra_mag=0.0, ra_n=0, erase=1.0, erase_side=8)
+    x = torch.empty(gbatch * 3 * 32 * 32, device="cuda")
+    # the epoch's shuffled order goes to the device once (train.rs:672-673)
+    order_d = torch.from_numpy(np.random.default_rng(5).permutation(ntrain).astype(np.int32)).cuda()
+    lab = torch.empty(gbatch, dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream()
+
+    def step(i):
+        b = i % (ntrain // gbatch)
+        data.make_batch_train(images_d, labels_d, None, order_d[b * gbatch:(b + 1) * gbatch], aug, 1000 + i,
+                              out=x, labels_out=lab)
+        net.train_step(x, lab)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    l0 = _lib.lib().rnn_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for i in range(args.steps):
+        step(args.warmup + i)
+    e1.record(s)
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / 1e3
+    launches = _lib.lib().rnn_launch_count() - l0
+    value = gbatch * args.steps / t
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "images/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(1000 * t / args.steps, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"resnet{6 * depth_n + 2}-w{width} train step with the batch built on the device "
+                               f"from a resident {ntrain}-image u8 split (BASELINE config {cfg_idx} model)",
+                   "global_batch": gbatch, "augmentation": "pad 4, flip, normalise, erase 1.0 side 8",
+                   "cuda_graph": not args.no_graph},
+        "e2e": {"value": round(value, 2), "unit": "images/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0,
+                "note": "dataset (153.6 MB) and the epoch order (200 KB) uploaded once, outside the timed steps"},
+        "gpu_launches": int(launches),
+    }
+    print(json.dumps(line), flush=True)
+    net.close()
+    return 0
+
+
 def run_reference(args, cfg_name):
     depth_n, width, gbatch, cfg_idx = CONFIGS[cfg_name]
     rank = int(os.environ.get("RANK", "0"))
@@ -625,13 +690,16 @@ def main():
     ap.add_argument("--local-bn", action="store_true", help="per-rank BN statistics instead of SyncBN")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch the step's kernels one by one (no CUDA graph)")
-    ap.add_argument("--workload", default="train", choices=["train", "eval"],
-                    help="eval: eval::resnet over a 10,000-image split instead of the training step")
+    ap.add_argument("--workload", default="train", choices=["train", "eval", "train-data"],
+                    help="eval: eval::resnet over a 10,000-image split instead of the training step; "
+                         "train-data: the step fed by the device batch builder from a resident u8 split")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.config == "rustvit":
         return run_reference_vit(args) if args.impl == "reference" else run_ours_vit(args)
+    if args.workload == "train-data" and args.impl == "ours":
+        return run_ours_train_data(args, args.config)
     if args.workload == "eval":
         return run_reference_eval(args, args.config) if args.impl == "reference" else run_ours_eval(args, args.config)
     if args.impl == "reference":

@@ -32,7 +32,7 @@ def _p(t):
 
 
 def make_batch_train(images: torch.Tensor, labels: torch.Tensor, coarse: torch.Tensor | None, idx: torch.Tensor,
-                     aug: Aug, seed: int, out: torch.Tensor | None = None):
+                     aug: Aug, seed: int, out: torch.Tensor | None = None, labels_out: torch.Tensor | None = None):
     """Returns (x [bs*3072] f32, labels u32 as int32, coarse or None), all on
     the device; idx holds the dataset indices (int32 / uint32)."""
     ctx = default_context()
@@ -40,7 +40,7 @@ def make_batch_train(images: torch.Tensor, labels: torch.Tensor, coarse: torch.T
     bs = idx.numel()
     dev = images.device
     out = torch.empty(bs * PIX, dtype=torch.float32, device=dev) if out is None else out
-    lab = torch.empty(bs, dtype=torch.int32, device=dev)
+    lab = torch.empty(bs, dtype=torch.int32, device=dev) if labels_out is None else labels_out
     co = None if coarse is None else torch.empty(bs, dtype=torch.int32, device=dev)
     call("rnn_make_batch_train_dev", ctx.h, _p(images), _p(labels), _p(coarse), _p(idx), bs, aug.pad, aug.ra_mag,
          aug.ra_n, aug.erase, aug.erase_side, seed & (2**64 - 1), _p(out), _p(lab), _p(co))
