@@ -437,16 +437,20 @@ int rnn_rustvit_train_step(rnn_rustvit *net, const float *x, const float *tf,
 /* ---- evaluation (data.rs:494-512, eval.rs:15-66) ------------------------ */
 /* A dataset is data::Dataset's images and fine labels (data.rs:16-24): len
  * images of 3 x 32 x 32 bytes in CHW order, then len label bytes. */
-/* data::make_batch_eval (data.rs:494-512): images/labels/out/labels_out on
- * the device; writes bs images from `start`, normalised per channel
+/* data::make_batch_eval (data.rs:494-512): images/labels (len images) and
+ * out/labels_out on the device; [start, start + bs) must lie inside the
+ * dataset (RNN_ERR_ARG otherwise); writes bs images from `start`, normalised per channel
  * ((v / 255 - mean) / std, data.rs:95-98), mirrored left-right when flip, and
  * their labels widened to u32. */
 int rnn_make_batch_eval_dev(rnn_ctx *ctx, const uint8_t *images,
-                            const uint8_t *labels, size_t start, int bs,
-                            int flip, float *out, uint32_t *labels_out);
+                            const uint8_t *labels, size_t len, size_t start,
+                            int bs, int flip, float *out,
+                            uint32_t *labels_out);
 /* data::make_batch_train (data.rs:384-412): images/labels (and coarse
- * labels, nullable) of a dataset, idx [bs] (u32) its images to use, all on
- * the device.  Augmentation = data::Aug (data.rs:281-293): RandAugment of
+ * labels, nullable) of a dataset of len images, idx [bs] (u32) its images to
+ * use, all on the device.  An index >= len raises the device error
+ * (RNN_ERR_DEVICE at the next rnn_ctx_synchronize) and leaves that image's
+ * slot zero, where the reference panics.  Augmentation = data::Aug (data.rs:281-293): RandAugment of
  * ra_n ops (at most 8) at magnitude ra_mag (off at 0), crop offset within
  * pad, flip, normalise, random erasing with probability `erase` of an
  * erase_side square of normal noise.  Image b draws from
@@ -454,7 +458,7 @@ int rnn_make_batch_eval_dev(rnn_ctx *ctx, const uint8_t *images,
  * out [bs, 3, 32, 32], labels_out / coarse_out (nullable) [bs] u32. */
 int rnn_make_batch_train_dev(rnn_ctx *ctx, const uint8_t *images,
                              const uint8_t *labels, const uint8_t *coarse,
-                             const uint32_t *idx, int bs, int pad,
+                             size_t len, const uint32_t *idx, int bs, int pad,
                              float ra_mag, int ra_n, float erase,
                              int erase_side, uint64_t seed, float *out,
                              uint32_t *labels_out, uint32_t *coarse_out);

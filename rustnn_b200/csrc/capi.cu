@@ -240,9 +240,11 @@ extern "C" int rnn_ctx_synchronize(rnn_ctx* ctx) {
   RNN_CUDA(cudaMemcpy(&err, ctx->dev_error, sizeof(int), cudaMemcpyDeviceToHost));
   if (err) {
     RNN_CUDA(cudaMemset(ctx->dev_error, 0, sizeof(int)));
-    return set_error(RNN_ERR_DEVICE, "device error 0x%x (%s%s)", err,
+    return set_error(RNN_ERR_DEVICE, "device error 0x%x (%s%s%s%s)", err,
                      (err & 1) ? "a kernel gave up waiting on a pipeline barrier " : "",
-                     (err & 2) ? "a label is >= nclass" : "");
+                     (err & 2) ? "a label is >= nclass " : "",
+                     (err & 4) ? "a peer GPU did not publish its statistics in time " : "",
+                     (err & 8) ? "a batch index is outside the dataset" : "");
   }
   return RNN_OK;
 }

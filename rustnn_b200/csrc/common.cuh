@@ -71,6 +71,7 @@ enum DeviceError : int {
   DEV_ERR_TIMEOUT = 1,  // a pipeline wait gave up
   DEV_ERR_LABEL = 2,    // softmax_ce saw a label >= nclass
   DEV_ERR_PEER = 4,     // a peer GPU did not publish its SyncBN sums in time
+  DEV_ERR_INDEX = 8,    // a batch index is outside its dataset
 };
 
 }  // namespace rnn

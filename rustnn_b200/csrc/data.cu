@@ -83,8 +83,8 @@ struct Draws {
 
 __global__ void __launch_bounds__(THREADS) make_batch_train_kernel(
     const uint8_t* __restrict__ images, const uint8_t* __restrict__ labels, const uint8_t* __restrict__ coarse,
-    const uint32_t* __restrict__ idx, Aug aug, uint64_t seed, float* __restrict__ out,
-    uint32_t* __restrict__ labels_out, uint32_t* __restrict__ coarse_out) {
+    size_t len, const uint32_t* __restrict__ idx, Aug aug, uint64_t seed, float* __restrict__ out,
+    uint32_t* __restrict__ labels_out, uint32_t* __restrict__ coarse_out, int* __restrict__ dev_error) {
   __shared__ uint8_t work[PIX], src[PIX], tmp[PIX];
   __shared__ uint32_t red[3][256];
   __shared__ uint32_t eq_lo[3];
@@ -93,6 +93,15 @@ __global__ void __launch_bounds__(THREADS) make_batch_train_kernel(
   const int tid = threadIdx.x;
   const int b = blockIdx.x;
   const size_t img = idx[b];
+  if (img >= len) {  // the reference panics on the slice index; flag it and leave zeros
+    if (tid == 0) {
+      atomicOr(dev_error, DEV_ERR_INDEX);
+      labels_out[b] = 0;
+      if (coarse_out) coarse_out[b] = 0;
+    }
+    for (int i = tid; i < PIX; i += THREADS) out[(size_t)b * PIX + i] = 0.0f;
+    return;
+  }
 
   if (tid == 0) {
     labels_out[b] = labels[img];
@@ -328,12 +337,15 @@ float beta_like(float a, Rng& rng) {
 }  // namespace
 
 int make_batch_train(rnn_ctx* ctx, const uint8_t* images, const uint8_t* labels, const uint8_t* coarse,
-                     const uint32_t* idx, int bs, int pad, float ra_mag, int ra_n, float erase, int erase_side,
+                     size_t len, const uint32_t* idx, int bs, int pad, float ra_mag, int ra_n, float erase, int erase_side,
                      uint64_t seed, float* out, uint32_t* labels_out, uint32_t* coarse_out) {
   RNN_REQUIRE(bs >= 0 && pad >= 0 && ra_n >= 0 && erase_side >= 0, "make_batch_train: negative argument");
   RNN_REQUIRE(ra_mag <= 0.0f || ra_n <= MAX_RA, "make_batch_train: at most %d RandAugment ops (ra_n %d)", MAX_RA,
               ra_n);
   if (bs == 0) return RNN_OK;
+  RNN_RANGE(images, (size_t)PIX * len);
+  RNN_RANGE(labels, len);
+  if (coarse) RNN_RANGE(coarse, len);
   RNN_RANGE(idx, sizeof(uint32_t) * (size_t)bs);
   RNN_RANGE(out, sizeof(float) * (size_t)bs * PIX);
   RNN_RANGE(labels_out, sizeof(uint32_t) * (size_t)bs);
@@ -341,8 +353,8 @@ int make_batch_train(rnn_ctx* ctx, const uint8_t* images, const uint8_t* labels,
   const int span = erase > 0.0f ? std::min(2 * (erase_side / 2), IMG) : 0;
   const size_t smem = sizeof(float) * 2 * 3 * (size_t)span * span;
   Aug aug{pad, ra_mag, ra_n, erase, erase_side};
-  make_batch_train_kernel<<<bs, THREADS, smem, ctx->stream>>>(images, labels, coarse, idx, aug, seed, out,
-                                                              labels_out, coarse_out);
+  make_batch_train_kernel<<<bs, THREADS, smem, ctx->stream>>>(images, labels, coarse, len, idx, aug, seed, out,
+                                                              labels_out, coarse_out, ctx->dev_error);
   RNN_CHECK_LAUNCH();
   return RNN_OK;
 }
@@ -404,11 +416,11 @@ int mix_batch(rnn_ctx* ctx, float* x, int bs, float alpha_mix, float alpha_cut, 
 }  // namespace rnn
 
 extern "C" int rnn_make_batch_train_dev(rnn_ctx* ctx, const uint8_t* images, const uint8_t* labels,
-                                        const uint8_t* coarse, const uint32_t* idx, int bs, int pad, float ra_mag,
-                                        int ra_n, float erase, int erase_side, uint64_t seed, float* out,
+                                        const uint8_t* coarse, size_t len, const uint32_t* idx, int bs, int pad,
+                                        float ra_mag, int ra_n, float erase, int erase_side, uint64_t seed, float* out,
                                         uint32_t* labels_out, uint32_t* coarse_out) {
   RNN_REQUIRE(ctx && images && labels && idx && out && labels_out, "make_batch_train: null argument");
-  return rnn::make_batch_train(ctx, images, labels, coarse, idx, bs, pad, ra_mag, ra_n, erase, erase_side, seed, out,
+  return rnn::make_batch_train(ctx, images, labels, coarse, len, idx, bs, pad, ra_mag, ra_n, erase, erase_side, seed, out,
                                labels_out, coarse_out);
 }
 

@@ -181,9 +181,11 @@ int eval_loop(rnn_ctx* ctx, EvalWs& ws, const uint8_t* images, const uint8_t* la
 
 }  // namespace rnn
 
-extern "C" int rnn_make_batch_eval_dev(rnn_ctx* ctx, const uint8_t* images, const uint8_t* labels, size_t start,
-                                       int bs, int flip, float* out, uint32_t* labels_out) {
+extern "C" int rnn_make_batch_eval_dev(rnn_ctx* ctx, const uint8_t* images, const uint8_t* labels, size_t len,
+                                       size_t start, int bs, int flip, float* out, uint32_t* labels_out) {
   RNN_REQUIRE(ctx && images && labels && out && labels_out, "make_batch_eval: null argument");
   RNN_REQUIRE(bs >= 0, "make_batch_eval: negative batch");
+  RNN_REQUIRE(start <= len && (size_t)bs <= len - start,
+              "make_batch_eval: images [%zu, %zu) are outside a dataset of %zu", start, start + (size_t)bs, len);
   return rnn::make_batch_eval(ctx, images, labels, start, bs, flip != 0, out, labels_out);
 }

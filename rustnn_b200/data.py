@@ -42,7 +42,8 @@ def make_batch_train(images: torch.Tensor, labels: torch.Tensor, coarse: torch.T
     out = torch.empty(bs * PIX, dtype=torch.float32, device=dev) if out is None else out
     lab = torch.empty(bs, dtype=torch.int32, device=dev) if labels_out is None else labels_out
     co = None if coarse is None else torch.empty(bs, dtype=torch.int32, device=dev)
-    call("rnn_make_batch_train_dev", ctx.h, _p(images), _p(labels), _p(coarse), _p(idx), bs, aug.pad, aug.ra_mag,
+    call("rnn_make_batch_train_dev", ctx.h, _p(images), _p(labels), _p(coarse), labels.numel(), _p(idx), bs,
+         aug.pad, aug.ra_mag,
          aug.ra_n, aug.erase, aug.erase_side, seed & (2**64 - 1), _p(out), _p(lab), _p(co))
     return out, lab, co
 
@@ -53,7 +54,8 @@ def make_batch_eval(images: torch.Tensor, labels: torch.Tensor, start: int, bs: 
     ctx.bind()
     out = torch.empty(bs * PIX, dtype=torch.float32, device=images.device) if out is None else out
     lab = torch.empty(bs, dtype=torch.int32, device=images.device)
-    call("rnn_make_batch_eval_dev", ctx.h, _p(images), _p(labels), start, bs, int(flip), _p(out), _p(lab))
+    call("rnn_make_batch_eval_dev", ctx.h, _p(images), _p(labels), labels.numel(), start, bs, int(flip), _p(out),
+         _p(lab))
     return out, lab
 
 

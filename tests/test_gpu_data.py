@@ -83,3 +83,24 @@ def test_mix_batch(m, c, seed):
         assert np.array_equal(st_d, st_o)
         assert np.array_equal(perm_d, perm_o) and np.array_equal(lam_d, lam_o)
         assert np.array_equal(xd.cpu().numpy(), want)
+
+
+def test_batch_train_index_outside_dataset():
+    """An index past the dataset's end is flagged by the kernel (the
+    reference panics on the slice): the next synchronisation reports the
+    device error, the slot is left zero, and the context stays usable."""
+    from rustnn_b200 import data
+    from rustnn_b200._lib import RnnError
+    from rustnn_b200.ops import default_context
+
+    images, labels, coarse = dataset(3, 8)
+    dv = lambda a: torch.from_numpy(a).cuda()
+    idx = np.array([1, 8, 3], np.uint32)  # 8 == len
+    got, gl, _ = data.make_batch_train(dv(images), dv(labels), None, dv(idx.view(np.int32)), data.Aug(), 5)
+    with pytest.raises(RnnError):
+        default_context().synchronize()
+    assert not np.any(got[PIX:2 * PIX].cpu().numpy())
+    ok = np.array([1, 7, 3], np.uint32)
+    got, gl, _ = data.make_batch_train(dv(images), dv(labels), None, dv(ok.view(np.int32)), data.Aug(), 5)
+    default_context().synchronize()
+    assert np.array_equal(gl.cpu().numpy().view(np.uint32), labels[ok].astype(np.uint32))

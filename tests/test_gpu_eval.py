@@ -38,7 +38,8 @@ def make_batch_dev(images_d, labels_d, start, bs, flip, out_offset=0):
     out = torch.zeros(bs * PIX + out_offset, device="cuda")
     lab = torch.zeros(bs, dtype=torch.int32, device="cuda")
     _lib.call("rnn_make_batch_eval_dev", ctx.h, C.c_void_p(images_d.data_ptr()), C.c_void_p(labels_d.data_ptr()),
-              start, bs, int(flip), C.c_void_p(out.data_ptr() + 4 * out_offset), C.c_void_p(lab.data_ptr()))
+              labels_d.numel(), start, bs, int(flip), C.c_void_p(out.data_ptr() + 4 * out_offset),
+              C.c_void_p(lab.data_ptr()))
     torch.cuda.synchronize()
     return out[out_offset:].cpu().numpy(), lab.cpu().numpy().view(np.uint32)
 
@@ -154,3 +155,12 @@ def test_vit_eval_ema_swaps_back():
     want = d.eval(images, labels, 2, tta=True)
     assert got == want
     d.close()
+
+
+def test_make_batch_eval_outside_dataset():
+    """A window past the end of the dataset is refused on the host."""
+    from rustnn_b200._lib import RnnError
+
+    images, labels = dataset(1, 4, 100)
+    with pytest.raises(RnnError):
+        make_batch_dev(torch.from_numpy(images).cuda(), torch.from_numpy(labels).cuda(), 2, 3, False)
