@@ -800,13 +800,22 @@ def uniform_target(y, k, eps):
     return out
 
 
-def targets(labels, parent, nc, lc: LossCfg):
-    """train.rs:120-155 with mixup off (lambda = 1): (tf [n, nf], tc [n, nc], coarse labels)."""
+def targets(labels, parent, nc, lc: LossCfg, perm=None, lam=None):
+    """train.rs:120-155: (tf [n, nf], tc [n, nc], coarse labels).  With perm /
+    lam (data::mix_batch's) row i is lam[i] * target(i) + (1 - lam[i]) *
+    target(perm[i]) in f32, unfused; without them lambda = 1."""
     nf = len(parent)
-    tf = np.concatenate([taxo_target(int(y), parent, nf, lc.smooth, lc.sib) for y in labels]).astype(F32)
     coarse = parent[labels].astype(np.uint32)
-    tc = np.concatenate([uniform_target(int(c), nc, lc.smooth) for c in coarse]).astype(F32)
-    return tf, tc, coarse
+    fa = [taxo_target(int(y), parent, nf, lc.smooth, lc.sib).astype(F32) for y in labels]
+    ca = [uniform_target(int(c), nc, lc.smooth).astype(F32) for c in coarse]
+    if perm is None:
+        return np.concatenate(fa), np.concatenate(ca), coarse
+    tf, tc = [], []
+    for i in range(len(labels)):
+        lv = F32(lam[i])
+        tf.append(lv * fa[i] + (F32(1.0) - lv) * fa[perm[i]])
+        tc.append(lv * ca[i] + (F32(1.0) - lv) * ca[perm[i]])
+    return np.concatenate(tf).astype(F32), np.concatenate(tc).astype(F32), coarse
 
 
 def ce_soft(logits, target, hard, nclass, scale):

@@ -41,10 +41,12 @@ def cifar_parent() -> np.ndarray:
     return np.array([i // 5 for i in range(100)], np.uint32)
 
 
-def targets(labels, parent, ncoarse, smooth=0.1, sib=0.7):
-    """Soft targets of train.rs:120-155 with mixup off: taxo_target for the
-    fine labels (loss.rs:11-28), uniform_target for the coarse ones
-    (loss.rs:30-34).  Returns (tf [n, nf], tc [n, nc], coarse labels)."""
+def targets(labels, parent, ncoarse, smooth=0.1, sib=0.7, perm=None, lam=None):
+    """Soft targets of train.rs:120-155: taxo_target for the fine labels
+    (loss.rs:11-28), uniform_target for the coarse ones (loss.rs:30-34).
+    With perm / lam from mix_batch (data.rs:467-491) row i becomes
+    lam[i] * target(i) + (1 - lam[i]) * target(perm[i]).  Returns
+    (tf [n * nf], tc [n * nc], coarse labels)."""
     parent = np.asarray(parent, np.uint32)
     labels = np.asarray(labels, np.uint32)
     nf = len(parent)
@@ -60,6 +62,11 @@ def targets(labels, parent, ncoarse, smooth=0.1, sib=0.7):
     coarse = parent[labels].astype(np.uint32)
     tc = np.full((len(labels), ncoarse), f32(smooth) / f32(ncoarse), f32)
     tc[np.arange(len(labels)), coarse] += f32(1.0) - f32(smooth)
+    if perm is not None:  # train.rs:148-153, each product rounded before the add
+        perm = np.asarray(perm, np.int64)
+        lv = np.asarray(lam, f32)[:, None]
+        tf = (lv * tf + (f32(1.0) - lv) * tf[perm]).astype(f32)
+        tc = (lv * tc + (f32(1.0) - lv) * tc[perm]).astype(f32)
     return tf.ravel(), tc.ravel(), coarse
 
 

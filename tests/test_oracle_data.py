@@ -265,3 +265,29 @@ def test_cr_math_gap(ra_mag, ra_n, erase, seed):
         # a last-bit change of ln or cos moves sqrt(-2 ln u1) * cos(.) by a few ulp
         assert np.all(np.abs(a[d] - b[d]) <= 4 * np.spacing(np.abs(a[d])))
     assert np.linalg.norm(a - b) <= 2e-4 * np.linalg.norm(a)
+
+
+@pytest.mark.parametrize("m,c,seed", [(0.8, 0.0, 1), (0.0, 1.0, 2), (0.0, 0.0, 3)])
+def test_mixed_targets(m, c, seed):
+    """train.rs:120-155 after mix_batch: the host mirror (rustnn_b200.vit
+    .targets) and the oracle's restatement give the same rows bit for bit;
+    every row sums to 1 (to f32 rounding); lambda = 1 rows are the unmixed
+    targets."""
+    from oracle import rustvit as RV
+    from rustnn_b200 import vit
+
+    bs = 16
+    rng = np.random.default_rng(seed)
+    labels = rng.integers(0, 100, size=bs).astype(np.uint32)
+    x = np.zeros(bs * PIX, F32)
+    _, perm, lam, _ = O.mix_batch(x, bs, m, c, 0.5, O.Rng(seed).state())
+    parent = RV.cifar_parent()
+    lc = RV.LossCfg()
+    tf_o, tc_o, _ = RV.targets(labels, parent, 20, lc, perm, lam)
+    tf_h, tc_h, _ = vit.targets(labels, parent, 20, lc.smooth, lc.sib, perm=perm, lam=lam)
+    assert np.array_equal(tf_o, tf_h) and np.array_equal(tc_o, tc_h)
+    assert np.allclose(tf_h.reshape(bs, 100).sum(1), 1.0, atol=1e-5)
+    assert np.allclose(tc_h.reshape(bs, 20).sum(1), 1.0, atol=1e-5)
+    plain, _, _ = vit.targets(labels, parent, 20, lc.smooth, lc.sib)
+    one = lam == 1.0
+    assert np.array_equal(tf_h.reshape(bs, 100)[one], plain.reshape(bs, 100)[one])
