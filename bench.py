@@ -116,13 +116,33 @@ class ClockSampler:
 # ---------------------------------------------------------------- CPU legs
 
 
-def cpu_oracle_images_per_sec(depth_n, width, n_img, steps, threads=None):
+def host_cores() -> int:
+    """Every host core this process may run on.  Set explicitly on the CPU
+    legs, because torchrun exports OMP_NUM_THREADS=1 to each rank."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
+def ref_sample(cores: int) -> int:
+    """Images per CPU step: at least two per thread, so every thread has
+    whole images to work on, and never fewer than 64."""
+    return int(os.environ.get("RNN_REF_SAMPLE", str(max(64, 2 * cores))))
+
+
+def oracle_all_cores():
+    from oracle import oracle as O
+
+    O.set_threads(host_cores())
+    return O.get_threads()
+
+
+def cpu_oracle_images_per_sec(depth_n, width, n_img, steps):
     """Times the C restatement of the reference (oracle) on the host cores."""
     from oracle import oracle as O
 
-    if threads:
-        O.set_threads(threads)
-    cores = O.get_threads()
+    cores = oracle_all_cores()
     net = O.ResNet(depth_n, width, NCLASS, 0)
     x, labels = synthetic_batch(n_img, 1)
     net.train_step(x, labels)  # warm-up (allocations)
@@ -148,7 +168,7 @@ def cpu_oracle_eval_images_per_sec(depth_n, width, n_img, batch, reps):
     """eval::resnet of the C restatement on a bounded sample of the split."""
     from oracle import oracle as O
 
-    cores = O.get_threads()
+    cores = oracle_all_cores()
     net = O.ResNet(depth_n, width, NCLASS, 0)
     images, labels = synthetic_dataset(n_img, 2)
     net.eval(images, labels, batch)  # warm-up
@@ -176,7 +196,7 @@ def cpu_oracle_vit_images_per_sec(n_img, steps):
     from oracle import oracle as O
     from oracle import rustvit as RV
 
-    cores = O.get_threads()
+    cores = oracle_all_cores()
     net = RV.RustViT(RV.Cfg(), RV.cifar_parent(), 20, 0)
     tr = RV.Trainer(net)
     x, labels = synthetic_batch(n_img, 1)
@@ -191,7 +211,7 @@ def cpu_oracle_vit_images_per_sec(n_img, steps):
 def run_reference_vit(args):
     if int(os.environ.get("RANK", "0")) != 0:
         return 0
-    sample = int(os.environ.get("RNN_REF_SAMPLE", "8"))
+    sample = ref_sample(host_cores())
     ips, cores, dt = cpu_oracle_vit_images_per_sec(sample, max(1, args.steps))
     line = {
         "impl": "reference", "metric": METRIC, "value": round(ips, 3), "unit": "images/s", "n_gpus": args.gpus,
@@ -301,9 +321,10 @@ def run_ours_vit(args):
         "loss": round(total, 5),
     }
     if not args.no_cpu_baseline:
-        ips, cores, dt = cpu_oracle_vit_images_per_sec(4, 2)
+        sample = ref_sample(host_cores())
+        ips, cores, dt = cpu_oracle_vit_images_per_sec(sample, 2)
         line["cpu_baseline"] = {"value": round(ips, 3), "unit": "images/s", "cores": cores, "kind": "port",
-                                "sample": "2 steps x 4 images of the rustvit step (oracle restatement)"}
+                                "sample": f"2 steps x {sample} images of the rustvit step (oracle restatement)"}
     print(json.dumps(line), flush=True)
     net.close()
     return 0
@@ -313,7 +334,7 @@ def run_reference_eval(args, cfg_name):
     depth_n, width, gbatch, cfg_idx = CONFIGS[cfg_name]
     if int(os.environ.get("RANK", "0")) != 0:
         return 0
-    sample = int(os.environ.get("RNN_REF_SAMPLE", "16"))
+    sample = ref_sample(host_cores())
     ips, cores, dt = cpu_oracle_eval_images_per_sec(depth_n, width, sample, sample, max(1, args.steps))
     line = {
         "impl": "reference", "metric": EVAL_METRIC, "value": round(ips, 3), "unit": "images/s",
@@ -401,9 +422,10 @@ def run_ours_eval(args, cfg_name):
         "loss": round(loss, 5), "acc": round(acc, 5),
     }
     if not args.no_cpu_baseline:
-        ips, cores, _ = cpu_oracle_eval_images_per_sec(depth_n, width, 16, 16, 2)
+        sample = ref_sample(host_cores())
+        ips, cores, _ = cpu_oracle_eval_images_per_sec(depth_n, width, sample, sample, 2)
         line["cpu_baseline"] = {"value": round(ips, 3), "unit": "images/s", "cores": cores, "kind": "port",
-                                "sample": "2 passes of eval over 16 images (C restatement)"}
+                                "sample": f"2 passes of eval over {sample} images (C restatement)"}
     print(json.dumps(line), flush=True)
     net.close()
     return 0
@@ -479,7 +501,7 @@ def run_reference(args, cfg_name):
     if rank != 0:
         return 0
     # bounded per-step sample of the same workload, all host threads
-    sample = int(os.environ.get("RNN_REF_SAMPLE", "8" if cfg_name == "resnet56" else "32"))
+    sample = ref_sample(host_cores())
     ips, cores, dt = cpu_oracle_images_per_sec(depth_n, width, sample, max(1, args.steps))
     line = {
         "impl": "reference", "metric": METRIC, "value": round(ips, 3), "unit": "images/s", "n_gpus": args.gpus,
@@ -669,7 +691,7 @@ def run_ours(args, cfg_name):
             "loss": round(loss, 5),
         }
         if world == 1 and not args.no_cpu_baseline:
-            sample = 8 if cfg_name == "resnet56" else 32
+            sample = ref_sample(host_cores())
             ips, cores, dt = cpu_oracle_images_per_sec(depth_n, width, sample, 2)
             line["cpu_baseline"] = {"value": round(ips, 3), "unit": "images/s", "cores": cores, "kind": "port",
                                     "sample": f"2 steps x {sample} images of the same step (C restatement)"}

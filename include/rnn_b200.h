@@ -81,10 +81,19 @@ int rnn_gemm_dw(rnn_ctx *ctx, int m, int n, int k, const float *a,
  * stream).  Split-K partials live in a fixed 16-MiB device array inside the
  * library, held by every GPU that loads it until exit; m*n may not exceed
  * 2,097,152 (RNN_ERR_ARG otherwise).  The first call on a device looks up the
- * array's device address, so make that first call before any stream capture.
- * All calls share the array: calls that overlap on a GPU race. */
+ * array's device address, and the first call of each tile width on a device
+ * sets that kernel's shared-memory opt-in, so make those first calls before
+ * any stream capture.  All calls share the array: calls that overlap on a GPU
+ * race.  A kernel that gives up waiting on its pipeline (a 2 s bound) does not
+ * fail the call, which has already returned: it sets a device word that
+ * rnn_gemm_dw_noalloc_status reports. */
 int rnn_gemm_dw_noalloc_dev(int m, int n, int k, const float *a,
                             const float *b, float *c, void *cuda_stream);
+/* No counterpart in the reference.  Companion of rnn_gemm_dw_noalloc_dev:
+ * waits for `cuda_stream`, then returns RNN_ERR_DEVICE (and clears the word)
+ * if a kernel of that entry on the current device gave up waiting since the
+ * last query, else RNN_OK.  Allocates nothing. */
+int rnn_gemm_dw_noalloc_status(void *cuda_stream);
 
 /* ---- Conv2d (nn.rs:115-251, conv.rs) ------------------------------------ */
 /* x [n,cin,h,w], w [cout, cin*k*k] in (ci,kh,kw) order, y [n,cout,oh,ow]

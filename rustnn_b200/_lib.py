@@ -55,6 +55,7 @@ SIGS = {
     "rnn_gemm_dw_dev": [CTX, I, I, I, FP, FP, FP],
     "rnn_gemm_dw": [CTX, I, I, I, FP, FP, FP],
     "rnn_gemm_dw_noalloc_dev": [I, I, I, FP, FP, FP, P],
+    "rnn_gemm_dw_noalloc_status": [P],
     "rnn_conv2d_fwd_dev": [CTX, FP, I, I, I, I, FP, I, I, I, I, FP, I],
     "rnn_conv2d_fwd": [CTX, FP, I, I, I, I, FP, I, I, I, I, FP],
     "rnn_conv2d_dgrad_dev": [CTX, FP, I, I, I, I, FP, I, I, I, I, FP, I],

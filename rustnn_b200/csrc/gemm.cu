@@ -474,3 +474,27 @@ extern "C" int rnn_gemm_dw_noalloc_dev(int m, int n, int k, const float* a, cons
     default: return noalloc_run<256>(&ctx, p, splits);
   }
 }
+
+// The allocation-free entry has no context whose synchronise could report a
+// kernel that gave up waiting on its pipeline, so its kernels OR that into
+// g_noalloc_error and this query reports it: it waits for `stream`, reads the
+// word of the current device, clears it, and returns RNN_ERR_DEVICE when it
+// was set (the C written by the calls since the last query is then not to be
+// trusted).  Nothing is allocated; the read goes to a host stack variable.
+extern "C" int rnn_gemm_dw_noalloc_status(void* stream) {
+  using namespace rnn::tc;
+  int device = 0;
+  RNN_CUDA(cudaGetDevice(&device));
+  NoAllocDevice* d = nullptr;
+  RNN_TRY(noalloc_setup(device, &d));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int err = 0;
+  RNN_CUDA(cudaMemcpyAsync(&err, d->error, sizeof(int), cudaMemcpyDeviceToHost, s));
+  RNN_CUDA(cudaStreamSynchronize(s));
+  if (err == 0) return RNN_OK;
+  RNN_CUDA(cudaMemsetAsync(d->error, 0, sizeof(int), s));
+  RNN_CUDA(cudaStreamSynchronize(s));
+  return rnn::set_error(RNN_ERR_DEVICE,
+                        "gemm_dw_noalloc: device error 0x%x (a kernel gave up waiting on a pipeline barrier); "
+                        "C of the calls since the last status query is not valid", err);
+}

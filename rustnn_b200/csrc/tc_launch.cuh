@@ -4,6 +4,7 @@
 #pragma once
 
 #include <algorithm>
+#include <atomic>
 #include <type_traits>
 
 #include "common.cuh"
@@ -91,15 +92,24 @@ struct has_ts : std::false_type {};
 template <class P>
 struct has_ts<P, std::void_t<typename P::TS>> : std::true_type {};
 
+// cudaFuncSetAttribute acts on the current device only, so the dynamic
+// shared-memory opt-in of a kernel is recorded per device: one bit per device
+// ordinal below 64 in an atomic mask (two threads that race both set the same
+// attribute, which is harmless); devices beyond 63 set it on every launch.
+template <class Kernel>
+int ensure_smem_optin(Kernel kernel, std::atomic<unsigned long long>& done, int device, int bytes) {
+  const unsigned long long bit = device >= 0 && device < 64 ? 1ull << device : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return RNN_OK;
+  RNN_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  if (bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return RNN_OK;
+}
+
 template <int BN, class Prob>
 int launch_native(rnn_ctx* ctx, const Prob& prob, const Sched& sched) {
   using C = CfgOf<Prob, BN>;
-  static bool attr_set = false;  // per instantiation; set once per process
-  if (!attr_set) {
-    RNN_CUDA(cudaFuncSetAttribute(tc3_gemm_kernel<BN, Prob>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  C::SMEM_BYTES));
-    attr_set = true;
-  }
+  static std::atomic<unsigned long long> optin_done{0};  // per instantiation, one bit per device
+  RNN_TRY(ensure_smem_optin(tc3_gemm_kernel<BN, Prob>, optin_done, ctx->device, C::SMEM_BYTES));
   if (sched.num_tiles <= 0) return RNN_OK;
   int grid = std::min(sched.num_tiles, ctx->num_sms);
   tc3_gemm_kernel<BN, Prob><<<grid, C::THREADS, C::SMEM_BYTES, ctx->stream>>>(prob, sched, ctx->dev_error);

@@ -1,11 +1,11 @@
-"""Data-parallel ResNet step on 2 GPUs (one process per GPU, NCCL).
+"""Data-parallel ResNet step on 2 and 4 GPUs (one process per GPU, NCCL).
 
-With SyncBN, two ranks that each take half of a batch must reproduce the
+With SyncBN, ranks that each take a slice of a batch must reproduce the
 single-process step on the whole batch (the reference's semantics: one
 process, whole-batch BatchNorm statistics, loss averaged over the batch).
 The ranks run as spawned child processes with a short NCCL setup; the
 parent compares their parameters with the CPU oracle on the full batch.
-Skipped when fewer than two GPUs are visible.
+Each case is skipped when fewer GPUs than its ranks are visible.
 """
 import multiprocessing as mp
 import os
@@ -18,30 +18,42 @@ from oracle import oracle as O
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
-N_FULL, DEPTH, WIDTH, NCLASS, SEED, STEPS = 16, 1, 16, 100, 0, 2
+CASES = {
+    # name: (world, depth_n, width, global batch, steps, CUDA graph)
+    "dp2-resnet8-w16": (2, 1, 16, 16, 2, False),
+    # BASELINE config 5's network through bench.py's code path: graph replay
+    # (eager, capture, replay), SyncBN over peer memory with the statistics
+    # exchanged from the conv epilogue
+    "dp2-resnet56-w64": (2, 9, 64, 16, 3, True),
+    "dp4-resnet56-w64": (4, 9, 64, 32, 3, True),
+}
+NCLASS, SEED = 100, 0
 
 
-def batch(step):
+def batch(n_full, step):
     rs = np.random.default_rng(1000 + step)
-    u = rs.integers(0, 256, size=(N_FULL, 3, 32, 32)).astype(np.float32)
+    u = rs.integers(0, 256, size=(n_full, 3, 32, 32)).astype(np.float32)
     x = ((u - 127.5) / 73.9).astype(np.float32)
-    labels = rs.integers(0, NCLASS, size=N_FULL).astype(np.uint32)
+    labels = rs.integers(0, NCLASS, size=n_full).astype(np.uint32)
     return x, labels
 
 
-def _rank_main(rank, world, uid, sync_bn, q):
+def _rank_main(rank, world, uid, sync_bn, case, q):
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     try:
         import torch as T
 
         from rustnn_b200 import model
 
+        _, depth, width, n_full, steps, graph = CASES[case]
         T.cuda.set_device(rank)
-        net = model.ResNet(DEPTH, WIDTH, NCLASS, SEED)
+        net = model.ResNet(depth, width, NCLASS, SEED)
+        if graph:
+            net.use_graph(True)
         net.dp_init(rank, world, uid, sync_bn=sync_bn)
-        per = N_FULL // world
-        for step in range(STEPS):
-            x, labels = batch(step)
+        per = n_full // world
+        for step in range(steps):
+            x, labels = batch(n_full, step)
             xs = T.from_numpy(np.ascontiguousarray(x[rank * per:(rank + 1) * per]).ravel()).cuda()
             ls = T.from_numpy(labels[rank * per:(rank + 1) * per].astype(np.int32)).cuda()
             net.train_step(xs, ls)
@@ -53,19 +65,19 @@ def _rank_main(rank, world, uid, sync_bn, q):
         q.put((rank, repr(e), None))
 
 
-def _run(world, sync_bn):
+def _run(world, sync_bn, case):
     from rustnn_b200 import model
 
     uid = model.dp_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, uid, sync_bn, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, uid, sync_bn, case, q)) for r in range(world)]
     for p in procs:
         p.start()
     out = {}
     try:
         for _ in range(world):
-            rank, params, bufs = q.get(timeout=300)
+            rank, params, bufs = q.get(timeout=600)
             out[rank] = (params, bufs)
     finally:
         for p in procs:
@@ -81,16 +93,24 @@ def rel(a, b):
     return float(np.linalg.norm(a - b) / np.linalg.norm(b))
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_dp2_syncbn_matches_single_process_full_batch():
-    out = _run(2, True)
-    for r in (0, 1):
+def _gpus():
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_dp_syncbn_matches_single_process_full_batch(case):
+    world, depth, width, n_full, steps, _ = CASES[case]
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    out = _run(world, True, case)
+    for r in range(world):
         assert not isinstance(out[r][0], str), out[r][0]
-    o = O.ResNet(DEPTH, WIDTH, NCLASS, SEED)
-    for step in range(STEPS):
-        x, labels = batch(step)
+    o = O.ResNet(depth, width, NCLASS, SEED)
+    for step in range(steps):
+        x, labels = batch(n_full, step)
         o.train_step(x.ravel(), labels)
-    p0, p1 = out[0][0], out[1][0]
-    assert np.array_equal(p0, p1), "ranks diverged"
+    p0 = out[0][0]
+    for r in range(1, world):
+        assert np.array_equal(p0, out[r][0]), f"rank {r} diverged"
     assert rel(p0, o.params()) < 1e-4
     assert rel(out[0][1], o.buffers()) < 1e-4

@@ -86,15 +86,16 @@ def test_forward_backward_parity():
     d.close()
 
 
-def test_train_steps_parity():
+@pytest.mark.parametrize("n", [4, 128])
+def test_train_steps_parity(n):
     """Two Trainer::step calls (forward, build_loss, backward, clip, Muon +
-    AdamW, EMA) from the same initialisation on the same batches."""
+    AdamW, EMA) from the same initialisation on the same batches; n = 128 is
+    BASELINE config 4's batch, the one bench.py --config rustvit times."""
     from rustnn_b200 import vit
 
     d, o = pair({}, RV.cifar_parent(), 20, 4321)
     tr = RV.Trainer(o)
     rng = O.Rng(17)
-    n = 4
     for step, seed in enumerate((11, 12)):
         x, labels = _batch(rng, n, 32, 100)
         tf, tc, coarse = vit.targets(labels, d.parent, 20)
