@@ -23,6 +23,7 @@
 #include <tuple>
 #include <vector>
 
+#include "attn_tc.cuh"
 #include "common.cuh"
 
 namespace rnn {
@@ -501,6 +502,41 @@ static int check_args(int n, int h, int dh, int th, int tw, int mh, int mw, int 
   return RNN_OK;
 }
 
+// RNN_ATTN_SIMT=1 keeps every call on the SIMT kernels above (A/B runs);
+// by default calls the tensor-core path covers go there (attn_tc.cu).
+static bool attn_simt_forced() {
+  const char* v = getenv("RNN_ATTN_SIMT");
+  return v && v[0] && v[0] != '0';
+}
+
+static AttnTC tc_args(const AttnArgs& a, int dh) {
+  AttnTC t{};
+  t.n = a.n; t.h = a.h; t.dh = dh; t.tq = a.tq; t.tk = a.tk; t.nrel = a.nrel; t.mask = a.mask; t.hp = a.h / 2;
+  t.relidx = a.relidx;
+  t.q = a.q; t.qstride = a.qstride; t.qoff = a.qoff;
+  t.kv = a.kv; t.kvstride = a.kvstride; t.koff = a.koff; t.voff = a.voff;
+  t.tau = a.tau; t.rel = a.rel; t.p = a.p; t.o = a.o;
+  t.pin = a.pin; t.dout = a.dout; t.dq = a.dq; t.dkv = a.dkv;
+  return t;
+}
+
+static int tc_bwd(rnn_ctx* ctx, AttnTC t, float* dtau, float* drel) {
+  const size_t ds_floats = (size_t)t.n * t.h * t.tq * t.tk;
+  const size_t part_floats = (size_t)t.n * 2 * t.h * (1 + t.nrel);
+  const size_t ds_bytes = (ds_floats * sizeof(float) + 255) & ~(size_t)255;
+  RNN_TRY(ensure_ws(ctx, ds_bytes + part_floats * sizeof(float)));
+  t.ds = static_cast<float*>(ctx->ws);
+  t.part = reinterpret_cast<float*>(static_cast<char*>(ctx->ws) + ds_bytes);
+  RNN_RANGE(t.ds, ds_floats * sizeof(float));
+  RNN_RANGE(t.part, part_floats * sizeof(float));
+  RNN_TRY(tc::attn_tc_bwd(ctx, t));
+  const int total = t.h * (1 + t.nrel);
+  const int blocks = std::min((total + 7) / 8, ctx->num_sms * 16);
+  attn_reduce_kernel<<<blocks, 256, 0, ctx->stream>>>(t.part, t.n * 2, t.h, t.nrel, dtau, drel);
+  RNN_CHECK_LAUNCH();
+  return RNN_OK;
+}
+
 #define ATTN_DISPATCH(fn, dh, ...)                           \
   switch (dh) {                                              \
     case 4: return fn<4>(__VA_ARGS__);                       \
@@ -544,6 +580,8 @@ extern "C" int rnn_attn_fwd_dev(rnn_ctx* ctx, int n, int h, int dh, int th, int 
   RNN_RANGE(rel, sizeof(float) * (size_t)h * a.nrel);
   RNN_RANGE(p, sizeof(float) * (size_t)n * h * a.tq * a.tk);
   RNN_RANGE(o, sizeof(float) * (size_t)n * a.tq * h * dh);
+  const AttnTC t = tc_args(a, dh);
+  if (!attn_simt_forced() && tc::attn_tc_ok(t, false)) return tc::attn_tc_fwd(ctx, t);
   ATTN_DISPATCH(launch_fwd, dh, ctx, a)
 }
 
@@ -567,5 +605,7 @@ extern "C" int rnn_attn_bwd_dev(rnn_ctx* ctx, int n, int h, int dh, int th, int 
   RNN_RANGE(dout, sizeof(float) * (size_t)n * a.tq * h * dh);
   RNN_RANGE(dtau, sizeof(float) * h);
   RNN_RANGE(drel, sizeof(float) * (size_t)h * a.nrel);
+  const AttnTC t = tc_args(a, dh);
+  if (!attn_simt_forced() && tc::attn_tc_ok(t, true)) return tc_bwd(ctx, t, dtau, drel);
   ATTN_DISPATCH(launch_bwd, dh, ctx, a, dtau, drel)
 }

@@ -248,6 +248,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// Columns [32c, 32c + 32) of this lane's accumulator row; narrow (STACK)
+// tiles hold A*B_hi and A*B_lo in two halves BN columns apart, added here
+// exactly as the engine's own epilogue adds them.
+template <int BN, bool STACK>
+__device__ __forceinline__ void acc_ld32(uint32_t taddr, int c, float (&v)[32]) {
+  tmem_ld32(taddr + c * 32, v);
+  if constexpr (STACK) {
+    float w[32];
+    tmem_ld32(taddr + BN + c * 32, w);
+#pragma unroll
+    for (int e = 0; e < 32; e++) v[e] += w[e];
+  }
+}
+
 // Shared-memory matrix descriptor: K-major operand, SWIZZLE_128B, 8-row
 // groups 1024 bytes apart (SBO), sm_100 descriptor version 1.
 __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
@@ -451,9 +465,29 @@ struct prob_stats<P, std::void_t<decltype(P::STATS)>> {
 };
 template <int BN>
 constexpr int stats_bytes() { return (BN / 32) * 2 * 128 * 8; }
+// Problems that need a whole accumulator row at once (a row softmax, a row
+// dot product) declare ROW_EPI_WARP_BYTES (shared memory per epilogue warp,
+// possibly 0) and supply
+//   template <int BN, bool STACK>
+//   void epi_row(int m_tile, int n_tile, int q, int lane, uint32_t taddr, uint8_t* wsm) const;
+// called by all 32 lanes of epilogue warp q (0..3) in place of store(): the
+// warp owns accumulator rows q*32 + lane of the tile at TMEM address taddr
+// (lane quarter and buffer applied) and reads them with acc_ld32 (warp-wide,
+// .sync.aligned); wsm is the warp's own shared memory.
+template <class P, class = void>
+struct prob_rowepi {
+  static constexpr bool value = false;
+  static constexpr int bytes = 0;
+};
+template <class P>
+struct prob_rowepi<P, std::void_t<decltype(P::ROW_EPI_WARP_BYTES)>> {
+  static constexpr bool value = true;
+  static constexpr int bytes = (4 * P::ROW_EPI_WARP_BYTES + 1023) / 1024 * 1024;
+};
 template <class P, int BN>
 struct prob_extra_bn {
-  static constexpr int value = prob_halo<P>::value + (prob_stats<P>::value ? stats_bytes<BN>() : 0);
+  static constexpr int value =
+      prob_halo<P>::value + (prob_stats<P>::value ? stats_bytes<BN>() : 0) + prob_rowepi<P>::bytes;
 };
 // HALO problems may set A_TMEM: their producers write A into tensor memory.
 template <class P, class = void>
@@ -520,6 +554,7 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
   using C = CfgOf<Prob, BN>;
   constexpr bool HALO = prob_halo<Prob>::value > 0;
   constexpr bool STATS = prob_stats<Prob>::value;
+  constexpr bool ROWEPI = prob_rowepi<Prob>::value;
   static_assert(!C::ATM || Prob::B_BULK, "A in tensor memory needs a bulk-copied B");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte aligned operand ring
@@ -838,23 +873,31 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
       tc_fence_after();
       const int row = mt * BM + q * 32 + lane;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * C::ACC_COLS;
+      if constexpr (ROWEPI) {
+        uint8_t* wsm = ring_ptr + C::STAGES * C::STAGE_BYTES + prob_halo<Prob>::value +
+                       (STATS ? stats_bytes<BN>() : 0) + (warp - C::FIRST_EPI_WARP) * Prob::ROW_EPI_WARP_BYTES;
+        prob.template epi_row<BN, C::STACK>(mt, nt, q, lane, taddr, wsm);
+        (void)row;
+      }
+      if constexpr (!ROWEPI) {
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; c++) {
-        float v[32];
-        tmem_ld32(taddr + c * 32, v);
-        if constexpr (C::STACK) {
-          float w[32];
-          tmem_ld32(taddr + BN + c * 32, w);
+        for (int c = 0; c < BN / 32; c++) {
+          float v[32];
+          tmem_ld32(taddr + c * 32, v);
+          if constexpr (C::STACK) {
+            float w[32];
+            tmem_ld32(taddr + BN + c * 32, w);
 #pragma unroll
-          for (int e = 0; e < 32; e++) v[e] += w[e];
-        }
-        prob.store(row, nt * BN + c * 32, split, v);
-        if constexpr (STATS) {
-          if (stats) {
-            double cs, cq;
-            warp_colsum2(v, cs, cq);
-            stats_sm[(2 * c) * 128 + et] += cs;
-            stats_sm[(2 * c + 1) * 128 + et] += cq;
+            for (int e = 0; e < 32; e++) v[e] += w[e];
+          }
+          prob.store(row, nt * BN + c * 32, split, v);
+          if constexpr (STATS) {
+            if (stats) {
+              double cs, cq;
+              warp_colsum2(v, cs, cq);
+              stats_sm[(2 * c) * 128 + et] += cs;
+              stats_sm[(2 * c + 1) * 128 + et] += cq;
+            }
           }
         }
       }

@@ -2,7 +2,7 @@
 
     python -m rustnn_b200.kernel_bench conv --cin 64 --cout 64 --hw 32 --batch 256 [--k 3 --stride 1]
     python -m rustnn_b200.kernel_bench gemm            # the six gemm.rs bench shapes (bench.rs:17-24)
-    python -m rustnn_b200.kernel_bench attn            # Core fwd/bwd at the attention config (B=128, h=4, dh=32)
+    python -m rustnn_b200.kernel_bench attn [--dh 64]  # Core fwd/bwd at the attention config (B=128, h=4, dh=32)
     python -m rustnn_b200.kernel_bench ln              # LayerNorm fwd/bwd at the rustvit row counts
     python -m rustnn_b200.kernel_bench muon            # Muon (Newton-Schulz) over the 39 rustvit weight matrices
     python -m rustnn_b200.kernel_bench vitstep         # one rustvit Trainer::step (batch 128) after 3 warm-ups,
@@ -91,7 +91,7 @@ def attn(args):
     attention over 8x8 tokens (diagonal masked) and cross attention from 8x8
     queries into a 16x16 memory.  Bytes count every tensor the kernels must
     read or write once, P included (the backward reads it)."""
-    n, h, dh = args.batch if args.batch != 256 else 128, 4, 32
+    n, h, dh = args.batch if args.batch != 256 else 128, 4, args.dh
     c = h * dh
     out = []
     for tag, (th, mh, self_) in (("self 64x64", (8, 8, True)), ("cross 64x256", (8, 16, False))):
@@ -219,6 +219,7 @@ def main():
     ap.add_argument("--stride", type=int, default=1)
     ap.add_argument("--which", default="fwd,dgrad,wgrad")
     ap.add_argument("--reps", type=int, default=5)
+    ap.add_argument("--dh", type=int, default=32, help="attention head dim (32: BASELINE config 3; 64: rustvit)")
     args = ap.parse_args()
     rows = {"conv": conv, "gemm": gemm, "attn": attn, "ln": ln, "muon": muon, "vitstep": vitstep}[args.what](args)
     for r in rows:

@@ -119,6 +119,43 @@ def test_attention_backward_is_deterministic(ops):
         assert np.array_equal(a, b)
 
 
+@pytest.mark.parametrize("n,h,dh,th,mh,self_attn", [(128, 4, 32, 8, 8, True), (128, 4, 32, 8, 16, False),
+                                                    (16, 4, 64, 8, 8, True), (16, 4, 64, 8, 16, False)])
+def test_attention_tensor_core_path_matches_simt(ops, monkeypatch, n, h, dh, th, mh, self_attn):
+    """At 64 query tokens with head dim 32/64 the calls run on the tcgen05
+    engine (2 forward launches, 4 backward: scores+softmax, P V; dS, dQ, dK/dV,
+    the partial reduction) and agree with the SIMT kernels (RNN_ATTN_SIMT=1)."""
+    from rustnn_b200 import _lib
+
+    L = _lib.lib()
+    rng = O.Rng(700 + dh + mh)
+    c, tq, tk, g = _geometry(rng, n, h, dh, th, mh, self_attn)
+    _, nrel = ops.rel_index(th, th, mh, mh)
+    tau = dev(np.full(h, np.float32(1.0 / np.sqrt(np.float32(dh))), np.float32))
+    relv = dev(rng.rand_vec(h * nrel))
+    qd = dev(g["q"])
+    kvd = qd if self_attn else dev(g["kv"])
+    dout = dev(rng.rand_vec(n * tq * c))
+    res = {}
+    for simt in (False, True):
+        monkeypatch.setenv("RNN_ATTN_SIMT", "1" if simt else "0")
+        l0 = L.rnn_launch_count()
+        p, o = ops.attn_forward(n, h, dh, th, th, mh, mh, self_attn, qd, g["qstride"], g["qoff"], kvd,
+                                g["kvstride"], g["koff"], g["voff"], tau, relv)
+        l1 = L.rnn_launch_count()
+        dq = torch.zeros_like(qd)
+        dkv = dq if self_attn else torch.zeros_like(kvd)
+        dt, dr = torch.zeros(h, device="cuda"), torch.zeros(h * nrel, device="cuda")
+        ops.attn_backward(n, h, dh, th, th, mh, mh, qd, g["qstride"], g["qoff"], kvd, g["kvstride"], g["koff"],
+                          g["voff"], tau, p, dout, dq, dkv, dt, dr)
+        l2 = L.rnn_launch_count()
+        if not simt:
+            assert (l1 - l0, l2 - l1) == (2, 4), (l1 - l0, l2 - l1)
+        res[simt] = [host(t) for t in (p, o, dq, dkv, dt, dr)]
+    for name, a, b in zip(("p", "o", "dq", "dkv", "dtau", "drel"), res[False], res[True]):
+        assert rel(a, b) < TOL, (name, rel(a, b))
+
+
 def _dircheck(base, grad, eps, rng, lossf):
     base = np.asarray(base, np.float32)
     v = rng.rand_vec(base.size)
