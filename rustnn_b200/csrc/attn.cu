@@ -70,6 +70,31 @@ static int rel_table(rnn_ctx* ctx, int th, int tw, int mh, int mw, const uint32_
   return RNN_OK;
 }
 
+// Inverse of the index table, one per (device, geometry): inv[i][r] = the key
+// j with relidx[i][j] == r, or -1 (within a query row the indices are
+// distinct, so there is at most one).
+static std::map<std::tuple<int, int, int, int, int>, int*> g_inv_tables;
+
+static int rel_inv_table(rnn_ctx* ctx, int th, int tw, int mh, int mw, const int** out) {
+  std::vector<uint32_t> idx;
+  const int nrel = rel_index_host(th, tw, mh, mw, &idx);
+  const int tq = th * tw, tk = mh * mw;
+  std::lock_guard<std::mutex> lock(g_rel_mu);
+  auto key = std::make_tuple(ctx->device, th, tw, mh, mw);
+  auto it = g_inv_tables.find(key);
+  if (it == g_inv_tables.end()) {
+    std::vector<int> inv((size_t)tq * nrel, -1);
+    for (int i = 0; i < tq; i++)
+      for (int j = 0; j < tk; j++) inv[(size_t)i * nrel + idx[(size_t)i * tk + j]] = j;
+    int* d = nullptr;
+    RNN_CUDA(cudaMalloc(&d, inv.size() * sizeof(int)));
+    RNN_CUDA(cudaMemcpy(d, inv.data(), inv.size() * sizeof(int), cudaMemcpyHostToDevice));
+    it = g_inv_tables.emplace(key, d).first;
+  }
+  *out = it->second;
+  return RNN_OK;
+}
+
 // ---------------------------------------------------------------- kernels
 
 struct AttnArgs {
@@ -520,21 +545,37 @@ static AttnTC tc_args(const AttnArgs& a, int dh) {
   return t;
 }
 
-static int tc_bwd(rnn_ctx* ctx, AttnTC t, float* dtau, float* drel) {
+static size_t al256(size_t bytes) { return (bytes + 255) & ~(size_t)255; }
+
+static int tc_fwd(rnn_ctx* ctx, AttnTC t) {
+  const size_t bias_floats = (size_t)t.h * t.tq * t.tk;
+  RNN_TRY(ensure_ws(ctx, bias_floats * sizeof(float)));
+  float* bias = static_cast<float*>(ctx->ws);
+  RNN_RANGE(bias, bias_floats * sizeof(float));
+  RNN_TRY(tc::attn_bias_build(ctx, t, bias));
+  t.bias = bias;
+  return tc::attn_tc_fwd(ctx, t);
+}
+
+static int tc_bwd(rnn_ctx* ctx, AttnTC t, int th, int tw, int mh, int mw, float* dtau, float* drel) {
+  const int* inv = nullptr;
+  RNN_TRY(rel_inv_table(ctx, th, tw, mh, mw, &inv));
   const size_t ds_floats = (size_t)t.n * t.h * t.tq * t.tk;
-  const size_t part_floats = (size_t)t.n * 2 * t.h * (1 + t.nrel);
-  const size_t ds_bytes = (ds_floats * sizeof(float) + 255) & ~(size_t)255;
-  RNN_TRY(ensure_ws(ctx, ds_bytes + part_floats * sizeof(float)));
-  t.ds = static_cast<float*>(ctx->ws);
-  t.part = reinterpret_cast<float*>(static_cast<char*>(ctx->ws) + ds_bytes);
+  const size_t part_floats = (size_t)t.n * 2 * t.h;
+  const size_t sum_floats = (size_t)t.h * t.tq * t.tk;
+  const size_t ds_bytes = al256(ds_floats * sizeof(float)), part_bytes = al256(part_floats * sizeof(float));
+  RNN_TRY(ensure_ws(ctx, ds_bytes + part_bytes + sum_floats * sizeof(float)));
+  char* ws = static_cast<char*>(ctx->ws);
+  t.ds = reinterpret_cast<float*>(ws);
+  t.part = reinterpret_cast<float*>(ws + ds_bytes);
+  float* dssum = reinterpret_cast<float*>(ws + ds_bytes + part_bytes);
   RNN_RANGE(t.ds, ds_floats * sizeof(float));
   RNN_RANGE(t.part, part_floats * sizeof(float));
+  RNN_RANGE(dssum, sum_floats * sizeof(float));
   RNN_TRY(tc::attn_tc_bwd(ctx, t));
-  const int total = t.h * (1 + t.nrel);
-  const int blocks = std::min((total + 7) / 8, ctx->num_sms * 16);
-  attn_reduce_kernel<<<blocks, 256, 0, ctx->stream>>>(t.part, t.n * 2, t.h, t.nrel, dtau, drel);
+  attn_reduce_kernel<<<1, 256, 0, ctx->stream>>>(t.part, t.n * 2, t.h, 0, dtau, drel);
   RNN_CHECK_LAUNCH();
-  return RNN_OK;
+  return tc::attn_drel(ctx, t, inv, dssum, drel);
 }
 
 #define ATTN_DISPATCH(fn, dh, ...)                           \
@@ -581,7 +622,7 @@ extern "C" int rnn_attn_fwd_dev(rnn_ctx* ctx, int n, int h, int dh, int th, int 
   RNN_RANGE(p, sizeof(float) * (size_t)n * h * a.tq * a.tk);
   RNN_RANGE(o, sizeof(float) * (size_t)n * a.tq * h * dh);
   const AttnTC t = tc_args(a, dh);
-  if (!attn_simt_forced() && tc::attn_tc_ok(t, false)) return tc::attn_tc_fwd(ctx, t);
+  if (!attn_simt_forced() && tc::attn_tc_ok(t, false)) return tc_fwd(ctx, t);
   ATTN_DISPATCH(launch_fwd, dh, ctx, a)
 }
 
@@ -606,6 +647,6 @@ extern "C" int rnn_attn_bwd_dev(rnn_ctx* ctx, int n, int h, int dh, int th, int 
   RNN_RANGE(dtau, sizeof(float) * h);
   RNN_RANGE(drel, sizeof(float) * (size_t)h * a.nrel);
   const AttnTC t = tc_args(a, dh);
-  if (!attn_simt_forced() && tc::attn_tc_ok(t, true)) return tc_bwd(ctx, t, dtau, drel);
+  if (!attn_simt_forced() && tc::attn_tc_ok(t, true)) return tc_bwd(ctx, t, th, tw, mh, mw, dtau, drel);
   ATTN_DISPATCH(launch_bwd, dh, ctx, a, dtau, drel)
 }

@@ -12,24 +12,24 @@
 // row.  Products whose output columns are per head (O = P V, dQ = dS K) run
 // over N = 2dh columns and keep each row's own head block.
 //
-//   forward   AttnScoreProb   S = Q K^T; epilogue: tau*S + rel[relidx],
-//                             diagonal mask, row softmax -> P (HBM, as
-//                             attn.rs:186-211 stores it)
+//   forward   AttnScoreProb   S = Q K^T; epilogue: tau*S + bias (the
+//                             per-head table rel[relidx] with the diagonal
+//                             mask folded in, built once per call), row
+//                             softmax -> P (HBM, as attn.rs:186-211 stores it)
 //             AttnPVProb      O = P V
 //   backward  AttnDSProb      dP = dO V^T; epilogue: dS = P (dP - rowsum(dP P))
-//                             -> workspace, drel partials (attn.rs:276-315)
+//                             -> workspace (attn.rs:276-291)
 //             AttnDQProb      G = dS K; epilogue: dq += tau G and the dtau
 //                             partial sum_i Q_i . G_i, which equals the
 //                             reference's sum dS * (Q K^T) (attn.rs:292-308)
 //                             without recomputing the scores
 //             AttnDKVProb     dV = P^T dO and dK = tau dS^T Q per head (two
 //                             items of one launch), += into dkv
-// dtau / drel partials are per (image, half of a head's rows) and reduced in
-// a fixed order afterwards (attn.cu), so the backward is deterministic and
-// uses no atomics.  The rows of the drel partial: within one accumulator row
-// (one query) every key has a distinct relative index, and for one key every
-// query has a distinct index, so the 32 lanes of a warp (32 queries) walking
-// the keys in step add into a warp-private buffer without conflicts.
+//             attn_drel       drel (attn.rs:309-315): the image sum of dS,
+//                             then per relative index a fixed-order gather
+// dtau partials are per (image, half of a head's rows) and reduced in a fixed
+// order afterwards (attn.cu), so the backward is deterministic and uses no
+// atomics.
 #include <cmath>
 
 #include "attn_tc.cuh"
@@ -173,61 +173,61 @@ struct AttnScoreProb {
   }
   __device__ __forceinline__ const void* b_src(int, int) const { return nullptr; }
 
-  __device__ __forceinline__ float logit(float s, float t, const float* rb, uint32_t idx, int i, int j) const {
-    float z = t * s + __ldg(rb + idx);
-    if (a.mask && j == i) z = -INFINITY;
-    return z;
+  // z = tau * S + bias for the 32 columns of chunk c (bias is -inf on a
+  // masked diagonal, so z is too)
+  template <int BN, bool STACK>
+  __device__ __forceinline__ void logits32(uint32_t taddr, int c, float t, const float* brow, float (&z)[32]) const {
+    float4 b4[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) b4[e] = ldg4(brow + c * 32 + 4 * e);
+    float v[32];
+    acc_ld32<BN, STACK>(taddr, c, v);
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      z[4 * e] = t * v[4 * e] + b4[e].x;
+      z[4 * e + 1] = t * v[4 * e + 1] + b4[e].y;
+      z[4 * e + 2] = t * v[4 * e + 2] + b4[e].z;
+      z[4 * e + 3] = t * v[4 * e + 3] + b4[e].w;
+    }
   }
 
+  // Two passes over the row in TMEM: the running maximum and the sum of
+  // exp(z - max) (rescaled when a chunk raises the maximum), then P.
   template <int BN, bool STACK>
   __device__ __forceinline__ void epi_row(int mt, int, int q, int lane, uint32_t taddr, uint8_t*) const {
     PairTS ts;
     pair_of(a, mt, ts);
     const int row = q * 32 + lane, hl = row >> 6, i = row & 63, hd = 2 * ts.pr + hl;
     const float t = __ldg(a.tau + hd);
-    const float* rb = a.rel + (size_t)hd * a.nrel;
-    const uint32_t* ridx = a.relidx + (size_t)i * a.tk;
+    const float* brow = a.bias + ((size_t)hd * a.tq + i) * a.tk;
     const int nch = a.tk / 32;
-    float mx = -INFINITY;
+    float mx = -INFINITY, sum = 0.0f;
 #pragma unroll 1
     for (int c = 0; c < nch; c++) {
-      float v[32];
-      acc_ld32<BN, STACK>(taddr, c, v);
+      float z[32];
+      logits32<BN, STACK>(taddr, c, t, brow, z);
+      float cm = z[0];
 #pragma unroll
-      for (int e = 0; e < 32; e++) {
-        const int j = c * 32 + e;
-        mx = fmaxf(mx, logit(v[e], t, rb, __ldg(ridx + j), i, j));
+      for (int e = 1; e < 32; e++) cm = fmaxf(cm, z[e]);
+      if (cm == -INFINITY) continue;  // every key of the chunk masked
+      if (cm > mx) {
+        sum = mx == -INFINITY ? 0.0f : sum * expf(mx - cm);
+        mx = cm;
       }
-    }
-    float sum = 0.0f;
-#pragma unroll 1
-    for (int c = 0; c < nch; c++) {
-      float v[32];
-      acc_ld32<BN, STACK>(taddr, c, v);
 #pragma unroll
-      for (int e = 0; e < 32; e++) {
-        const int j = c * 32 + e;
-        const float z = logit(v[e], t, rb, __ldg(ridx + j), i, j);
-        sum += z == -INFINITY ? 0.0f : expf(z - mx);
-      }
+      for (int e = 0; e < 32; e++) sum += expf(z[e] - mx);
     }
     const float inv = 1.0f / sum;
     float* pg = a.p + ((size_t)(ts.img * a.h + hd) * a.tq + i) * a.tk;
 #pragma unroll 1
     for (int c = 0; c < nch; c++) {
-      float v[32];
-      acc_ld32<BN, STACK>(taddr, c, v);
+      float z[32];
+      logits32<BN, STACK>(taddr, c, t, brow, z);
 #pragma unroll
-      for (int e = 0; e < 32; e += 4) {
-        float w[4];
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-          const int j = c * 32 + e + u;
-          const float z = logit(v[e + u], t, rb, __ldg(ridx + j), i, j);
-          w[u] = (z == -INFINITY ? 0.0f : expf(z - mx)) * inv;
-        }
-        *reinterpret_cast<float4*>(pg + c * 32 + e) = make_float4(w[0], w[1], w[2], w[3]);
-      }
+      for (int e = 0; e < 32; e += 4)
+        *reinterpret_cast<float4*>(pg + c * 32 + e) =
+            make_float4(expf(z[e] - mx) * inv, expf(z[e + 1] - mx) * inv, expf(z[e + 2] - mx) * inv,
+                        expf(z[e + 3] - mx) * inv);
     }
   }
 };
@@ -265,12 +265,12 @@ struct AttnPVProb {
 // ---------------------------------------------------------------- backward
 
 // dP = dO V^T for the pair; the epilogue forms dS = P (dP - sum_j dP_j P_j)
-// (attn.rs:280-291), writes it to the workspace and adds it into the warp's
-// drel buffer at the row's relative indices (attn.rs:309-315).
+// (attn.rs:280-291) and writes it to the workspace; drel is formed from the
+// workspace afterwards (attn_drel).
 template <int DH>
 struct AttnDSProb {
   static constexpr bool B_BULK = false;
-  static constexpr int ROW_EPI_WARP_BYTES = ATTN_TC_MAX_NREL * 4;
+  static constexpr int ROW_EPI_WARP_BYTES = 0;
   AttnTC a;
   int M, N;
   using TS = PairTS;
@@ -287,59 +287,43 @@ struct AttnDSProb {
   __device__ __forceinline__ const void* b_src(int, int) const { return nullptr; }
 
   template <int BN, bool STACK>
-  __device__ __forceinline__ void epi_row(int mt, int, int q, int lane, uint32_t taddr, uint8_t* wsm) const {
+  __device__ __forceinline__ void epi_row(int mt, int, int q, int lane, uint32_t taddr, uint8_t*) const {
     PairTS ts;
     pair_of(a, mt, ts);
     const int row = q * 32 + lane, hl = row >> 6, i = row & 63, hd = 2 * ts.pr + hl;
-    float* rw = reinterpret_cast<float*>(wsm);
-    for (int r = lane; r < a.nrel; r += 32) rw[r] = 0.0f;
-    __syncwarp();
     const size_t prow = ((size_t)(ts.img * a.h + hd) * a.tq + i) * a.tk;
     const float* pg = a.pin + prow;
     float* dsg = a.ds + prow;
-    const uint32_t* ridx = a.relidx + (size_t)i * a.tk;
     const int nch = a.tk / 32;
     float dot = 0.0f;
 #pragma unroll 1
     for (int c = 0; c < nch; c++) {
+      float4 p4[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) p4[e] = ldg4(pg + c * 32 + 4 * e);
       float v[32];
       acc_ld32<BN, STACK>(taddr, c, v);
 #pragma unroll
-      for (int e = 0; e < 32; e += 4) {
-        const float4 p4 = ldg4(pg + c * 32 + e);
-        dot = fmaf(v[e], p4.x, dot);
-        dot = fmaf(v[e + 1], p4.y, dot);
-        dot = fmaf(v[e + 2], p4.z, dot);
-        dot = fmaf(v[e + 3], p4.w, dot);
+      for (int e = 0; e < 8; e++) {
+        dot = fmaf(v[4 * e], p4[e].x, dot);
+        dot = fmaf(v[4 * e + 1], p4[e].y, dot);
+        dot = fmaf(v[4 * e + 2], p4[e].z, dot);
+        dot = fmaf(v[4 * e + 3], p4[e].w, dot);
       }
     }
 #pragma unroll 1
     for (int c = 0; c < nch; c++) {
+      float4 p4[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) p4[e] = ldg4(pg + c * 32 + 4 * e);
       float v[32];
       acc_ld32<BN, STACK>(taddr, c, v);
 #pragma unroll
-      for (int e = 0; e < 32; e += 4) {
-        const float4 p4 = ldg4(pg + c * 32 + e);
-        const uint4 x4 = __ldg(reinterpret_cast<const uint4*>(ridx + c * 32 + e));
-        const float d0 = p4.x * (v[e] - dot), d1 = p4.y * (v[e + 1] - dot);
-        const float d2 = p4.z * (v[e + 2] - dot), d3 = p4.w * (v[e + 3] - dot);
-        *reinterpret_cast<float4*>(dsg + c * 32 + e) = make_float4(d0, d1, d2, d3);
-        // lanes hold distinct queries: for one key their indices are
-        // distinct, so each step's 32 updates touch 32 different words
-        rw[x4.x] += d0;
-        __syncwarp();
-        rw[x4.y] += d1;
-        __syncwarp();
-        rw[x4.z] += d2;
-        __syncwarp();
-        rw[x4.w] += d3;
-        __syncwarp();
-      }
+      for (int e = 0; e < 8; e++)
+        *reinterpret_cast<float4*>(dsg + c * 32 + 4 * e) =
+            make_float4(p4[e].x * (v[4 * e] - dot), p4[e].y * (v[4 * e + 1] - dot), p4[e].z * (v[4 * e + 2] - dot),
+                        p4[e].w * (v[4 * e + 3] - dot));
     }
-    const int half = q & 1;
-    float* part = a.part + ((size_t)(ts.img * 2 + half) * a.h + hd) * (1 + a.nrel) + 1;
-    for (int r = lane; r < a.nrel; r += 32) part[r] = rw[r];
-    __syncwarp();
   }
 };
 
@@ -398,7 +382,7 @@ struct AttnDQProb {
       }
     }
     tacc = warp_sum_f(tacc);
-    if (lane == 0) a.part[((size_t)(ts.img * 2 + (q & 1)) * a.h + hd) * (1 + a.nrel)] = tacc;
+    if (lane == 0) a.part[(size_t)(ts.img * 2 + (q & 1)) * a.h + hd] = tacc;
   }
 };
 
@@ -471,13 +455,76 @@ struct AttnDKVProb {
   }
 };
 
+// ---------------------------------------------------------------- small kernels
+
+__global__ void attn_bias_kernel(const float* __restrict__ rel, const uint32_t* __restrict__ relidx, int h, int tq,
+                                 int tk, int nrel, int mask, float* __restrict__ bias) {
+  const int total = h * tq * tk;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
+    const int hd = e / (tq * tk), ij = e - hd * tq * tk, i = ij / tk, j = ij - i * tk;
+    bias[e] = (mask && i == j) ? -INFINITY : rel[(size_t)hd * nrel + relidx[ij]];
+  }
+}
+
+// dssum[e] = sum_n ds[n][e] over the n images, n ascending.
+__global__ void attn_image_sum_kernel(const float* __restrict__ ds, int n, int per, float* __restrict__ dssum) {
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < per; e += gridDim.x * blockDim.x) {
+    float s = 0.0f;
+    int k = 0;
+    for (; k + 4 <= n; k += 4) {
+      const float a0 = __ldg(ds + (size_t)k * per + e), a1 = __ldg(ds + (size_t)(k + 1) * per + e);
+      const float a2 = __ldg(ds + (size_t)(k + 2) * per + e), a3 = __ldg(ds + (size_t)(k + 3) * per + e);
+      s += a0;
+      s += a1;
+      s += a2;
+      s += a3;
+    }
+    for (; k < n; k++) s += __ldg(ds + (size_t)k * per + e);
+    dssum[e] = s;
+  }
+}
+
+// drel[h][r] += sum_i dssum[h][i][inv[i][r]], queries ascending.
+__global__ void attn_drel_gather_kernel(const float* __restrict__ dssum, const int* __restrict__ inv, int h, int tq,
+                                        int tk, int nrel, float* __restrict__ drel) {
+  const int total = h * nrel;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
+    const int hd = e / nrel, r = e - hd * nrel;
+    float s = 0.0f;
+    for (int i = 0; i < tq; i++) {
+      const int j = __ldg(inv + (size_t)i * nrel + r);
+      if (j >= 0) s += __ldg(dssum + ((size_t)hd * tq + i) * tk + j);
+    }
+    drel[e] += s;
+  }
+}
+
 // ---------------------------------------------------------------- host
 
 static inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+int attn_bias_build(rnn_ctx* ctx, const AttnTC& a, float* bias) {
+  const int total = a.h * a.tq * a.tk;
+  const int grid = std::min((total + 255) / 256, ctx->num_sms * 8);
+  attn_bias_kernel<<<grid, 256, 0, ctx->stream>>>(a.rel, a.relidx, a.h, a.tq, a.tk, a.nrel, a.mask, bias);
+  RNN_CHECK_LAUNCH();
+  return RNN_OK;
+}
+
+int attn_drel(rnn_ctx* ctx, const AttnTC& a, const int* inv, float* dssum, float* drel) {
+  const int per = a.h * a.tq * a.tk;
+  attn_image_sum_kernel<<<std::min((per + 255) / 256, ctx->num_sms * 8), 256, 0, ctx->stream>>>(a.ds, a.n, per,
+                                                                                                dssum);
+  RNN_CHECK_LAUNCH();
+  const int total = a.h * a.nrel;
+  attn_drel_gather_kernel<<<(total + 127) / 128, 128, 0, ctx->stream>>>(dssum, inv, a.h, a.tq, a.tk, a.nrel, drel);
+  RNN_CHECK_LAUNCH();
+  return RNN_OK;
+}
+
 bool attn_tc_ok(const AttnTC& a, bool backward) {
   if (a.tq != 64 || a.h % 2 != 0 || !(a.dh == 32 || a.dh == 64)) return false;
-  if (a.tk % 32 != 0 || a.tk < 32 || a.tk > 256 || a.nrel > ATTN_TC_MAX_NREL) return false;
+  if (a.tk % 32 != 0 || a.tk < 32 || a.tk > 256) return false;
   if (a.qstride % 4 || a.qoff % 4 || a.kvstride % 4 || a.koff % 4 || a.voff % 4) return false;
   if (!al16(a.q) || !al16(a.kv)) return false;
   if (!backward) return al16(a.p) && al16(a.o);

@@ -27,8 +27,9 @@ struct AttnTC {
   const float* dout; // backward: dO [n*tq][h*dh]
   float* dq;         // += , strided like q
   float* dkv;        // += , strided like kv
+  const float* bias; // forward: rel[h][relidx[i][j]], -inf on a masked diagonal, [h][tq][tk]
   float* ds;         // backward workspace: dS [n][h][tq][tk] (before the tau scale)
-  float* part;       // backward partials [n*2][h][1 + nrel]: dtau, then drel
+  float* part;       // backward: dtau partials [n*2][h]
 };
 
 namespace tc {
@@ -36,10 +37,16 @@ namespace tc {
 // grid), an even head count, head dim 32 or 64, a key count that is a
 // multiple of 32 up to 256, and 16-byte aligned rows.
 bool attn_tc_ok(const AttnTC& a, bool backward);
+// a.bias must hold the table (attn_bias_build).
 int attn_tc_fwd(rnn_ctx* ctx, const AttnTC& a);
-// Writes ds and part; the caller reduces part into dtau / drel.
+// Writes ds and the dtau partials; the caller reduces them (attn_reduce) and
+// forms drel from ds (attn_drel).
 int attn_tc_bwd(rnn_ctx* ctx, const AttnTC& a);
-// Largest relative-position table the backward's per-warp buffers hold.
-constexpr int ATTN_TC_MAX_NREL = 1024;
+// bias[h][i][j] = rel[h][relidx[i][j]], -inf at j == i under the mask.
+int attn_bias_build(rnn_ctx* ctx, const AttnTC& a, float* bias);
+// drel[h][r] += sum over images n and queries i of ds[n][h][i][inv[i][r]]
+// (inv[i][r] = the key of query i at relative index r, or -1), in a fixed
+// order: first the image sum of ds into dssum [h][tq][tk], then the gather.
+int attn_drel(rnn_ctx* ctx, const AttnTC& a, const int* inv, float* dssum, float* drel);
 }  // namespace tc
 }  // namespace rnn
