@@ -39,6 +39,7 @@ extern "C" {
 typedef struct rnn_ctx rnn_ctx;
 typedef struct rnn_resnet rnn_resnet;
 typedef struct rnn_rustvit rnn_rustvit;
+typedef struct rnn_comm rnn_comm;
 
 const char *rnn_last_error(void);
 /* Number of kernels this library has launched in this process. */
@@ -389,6 +390,37 @@ int rnn_dp_unique_id(unsigned char *uid_out);
  * like the single-process reference. */
 int rnn_resnet_dp_init(rnn_resnet *net, int rank, int world,
                        const unsigned char *uid, int sync_bn);
+/* The network's communicator as a handle for rnn_comm_wait / rnn_comm_check
+ * (failure detection of its collectives); it belongs to the network. */
+int rnn_resnet_comm(rnn_resnet *net, rnn_comm **out);
+
+/* ---- Tier-2 runtime (no reference counterpart: the reference is one process
+ * with host memory only; pool.rs is its allocator and it has no collective).
+ * Device memory on the context's device; copies enqueued on its stream. */
+int rnn_alloc(rnn_ctx *ctx, size_t bytes, void **out);
+/* waits for the context's stream first (queued work may still read p) */
+int rnn_free(rnn_ctx *ctx, void *p);
+int rnn_memcpy_h2d(rnn_ctx *ctx, void *dst, const void *src, size_t bytes);
+int rnn_memcpy_d2h(rnn_ctx *ctx, void *dst, const void *src, size_t bytes);
+/* An NCCL communicator for the batch-sharded step (one rank per GPU; uid from
+ * rnn_dp_unique_id, the same bytes on every rank). */
+int rnn_comm_init(rnn_comm **out, int device, int rank, int world,
+                  const unsigned char *uid);
+int rnn_comm_destroy(rnn_comm *comm);
+/* Sum (average != 0: mean) of a flat f32 gradient buffer over all ranks, in
+ * place, on the context's stream (train.rs:684-699 with the batch sharded). */
+int rnn_allreduce_grads(rnn_ctx *ctx, rnn_comm *comm, float *grads, size_t n,
+                        int average);
+/* RNN_ERR_NCCL when the communicator has an asynchronous error. */
+int rnn_comm_check(rnn_comm *comm);
+/* Makes every pending collective of the communicator return; it is unusable
+ * afterwards. */
+int rnn_comm_abort(rnn_comm *comm);
+/* Host watchdog: waits for the context's stream, polling the communicator's
+ * asynchronous error every millisecond.  On an error, or when the stream has
+ * not finished within timeout_ms (a peer never joined a collective), aborts
+ * the communicator and returns RNN_ERR_NCCL. */
+int rnn_comm_wait(rnn_ctx *ctx, rnn_comm *comm, int timeout_ms);
 
 /* ---- rustvit training step (vit.rs, train.rs:70-118 and 346-387) -------- */
 /* RustViT::new (vit.rs:441-509) on the device.  cfg9 = {width, cmid, dim,

@@ -56,6 +56,17 @@ SIGS = {
     "rnn_gemm_dw": [CTX, I, I, I, FP, FP, FP],
     "rnn_gemm_dw_noalloc_dev": [I, I, I, FP, FP, FP, P],
     "rnn_gemm_dw_noalloc_status": [P],
+    "rnn_alloc": [CTX, Z, P],
+    "rnn_free": [CTX, P],
+    "rnn_memcpy_h2d": [CTX, P, P, Z],
+    "rnn_memcpy_d2h": [CTX, P, P, Z],
+    "rnn_comm_init": [P, I, I, I, P],
+    "rnn_comm_destroy": [P],
+    "rnn_allreduce_grads": [CTX, P, P, Z, I],
+    "rnn_comm_check": [P],
+    "rnn_comm_abort": [P],
+    "rnn_comm_wait": [CTX, P, I],
+    "rnn_resnet_comm": [NET, P],
     "rnn_conv2d_fwd_dev": [CTX, FP, I, I, I, I, FP, I, I, I, I, FP, I],
     "rnn_conv2d_fwd": [CTX, FP, I, I, I, I, FP, I, I, I, I, FP],
     "rnn_conv2d_dgrad_dev": [CTX, FP, I, I, I, I, FP, I, I, I, I, FP, I],

@@ -16,6 +16,7 @@
 
 #include "bn.cuh"
 #include "ckpt.cuh"
+#include "comm.cuh"
 #include "eval.cuh"
 #include "ew.cuh"
 #include "rng.h"
@@ -94,6 +95,7 @@ struct rnn_resnet {
   const float* x_in = nullptr;
   // data parallel
   ncclComm_t comm = nullptr;
+  rnn_comm handle;  // the communicator as a C ABI handle (rnn_resnet_comm), borrowed
   int rank = 0, world = 1;
   bool sync_bn = false;
   // SyncBN over peer memory (bn.cuh PeerSums); world 1 = NCCL path
@@ -707,7 +709,7 @@ extern "C" int rnn_resnet_destroy(rnn_resnet* net) {
   cudaFree(net->bnstat);
   cudaFree(net->loss_dev);
   cudaFree(net->correct_dev);
-  if (net->comm) ncclCommDestroy(net->comm);
+  if (net->comm && !net->handle.aborted) ncclCommDestroy(net->comm);  // an abort already released it
   delete net;
   return RNN_OK;
 }
@@ -926,7 +928,7 @@ extern "C" int rnn_resnet_dp_init(rnn_resnet* net, int rank, int world, const un
   net->graph.release();
   peer_release(net);
   if (net->comm) {
-    ncclCommDestroy(net->comm);
+    if (!net->handle.aborted) ncclCommDestroy(net->comm);
     net->comm = nullptr;
   }
   ncclUniqueId id;
@@ -934,9 +936,23 @@ extern "C" int rnn_resnet_dp_init(rnn_resnet* net, int rank, int world, const un
   RNN_CUDA(cudaSetDevice(net->ctx->device));
   ncclResult_t r = ncclCommInitRank(&net->comm, world, id, rank);
   if (r != ncclSuccess) return set_error(RNN_ERR_NCCL, "ncclCommInitRank: %s", ncclGetErrorString(r));
+  net->handle = rnn_comm{};
+  net->handle.comm = net->comm;
+  net->handle.device = net->ctx->device;
+  net->handle.rank = rank;
+  net->handle.world = world;
+  net->handle.owned = false;
   net->rank = rank;
   net->world = world;
   net->sync_bn = sync_bn != 0;
   if (world > 1 && net->sync_bn && !peer_sync_disabled()) RNN_TRY(peer_setup(net));
+  return RNN_OK;
+}
+
+extern "C" int rnn_resnet_comm(rnn_resnet* net, rnn_comm** out) {
+  RNN_REQUIRE(net && out, "resnet_comm: null argument");
+  *out = nullptr;
+  RNN_REQUIRE(net->comm, "resnet_comm: the network is not data-parallel (rnn_resnet_dp_init)");
+  *out = &net->handle;
   return RNN_OK;
 }

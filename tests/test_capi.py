@@ -64,3 +64,28 @@ def test_errors_are_reported_without_gpu(lib):
     assert code == -1
     assert b"context" in lib.rnn_last_error()
     del C
+
+
+def _header_arity():
+    out = {}
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+        for m in re.finditer(r"\b(rnn_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", text, flags=re.S):
+            args = " ".join(m.group(2).split())
+            out[m.group(1)] = 0 if args in ("", "void") else args.count(",") + 1
+    return out
+
+
+def test_rust_sys_crate_binds_every_entry_point():
+    """rust/rnn-b200-sys (the -sys crate a Rust host links; no cargo in this
+    image, so it is checked against the header as text): one extern "C"
+    item per declared function, with the same number of parameters."""
+    src = open(os.path.join(ROOT, "rust", "rnn-b200-sys", "src", "lib.rs")).read()
+    rust = {}
+    for m in re.finditer(r"pub fn (rnn_[a-z0-9_]+)\(([^)]*)\)", src):
+        args = m.group(2).strip()
+        rust[m.group(1)] = 0 if not args else args.count(":")
+    hdr = _header_arity()
+    assert set(hdr) == set(rust), (sorted(set(hdr) - set(rust)), sorted(set(rust) - set(hdr)))
+    bad = {k: (hdr[k], rust[k]) for k in hdr if hdr[k] != rust[k]}
+    assert not bad, bad

@@ -114,3 +114,89 @@ def test_dp_syncbn_matches_single_process_full_batch(case):
         assert np.array_equal(p0, out[r][0]), f"rank {r} diverged"
     assert rel(p0, o.params()) < 1e-4
     assert rel(out[0][1], o.buffers()) < 1e-4
+
+
+# ------------------------------------------------------------------ communicator
+
+
+def _comm_rank(rank, world, uid, mode, q, ev):
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    try:
+        import torch as T
+
+        from rustnn_b200 import dp, ops
+        from rustnn_b200._lib import RnnError
+
+        T.cuda.set_device(rank)
+        ctx = ops.default_context(rank)
+        comm = dp.Comm(rank, world, uid, device=rank)
+        g = T.full((1 << 20,), float(rank + 1), device=f"cuda:{rank}")
+        comm.allreduce(ctx, g)
+        comm.wait(ctx, 30_000)
+        total = float(g[0].item())
+        comm.allreduce(ctx, g, average=True)
+        comm.wait(ctx, 30_000)
+        mean = float(g[0].item())
+        if mode == "ok":
+            q.put((rank, total, mean, None))
+            comm.close()
+            return
+        # a rank that stays alive but never joins the next collective: the
+        # other rank's watchdog must end its wait with an error, not hang
+        if rank == 0:
+            comm.allreduce(ctx, g)
+            try:
+                comm.wait(ctx, 2_000)
+                q.put((rank, total, mean, "no error"))
+            except RnnError as e:
+                q.put((rank, total, mean, str(e)))
+            ev.set()
+        else:
+            ev.wait(120)
+            comm.abort()
+            q.put((rank, total, mean, "abstained"))
+        comm.close()
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, None, None, repr(e)))
+
+
+def _run_comm(world, mode):
+    from rustnn_b200 import model
+
+    uid = model.dp_unique_id()
+    ctx = mp.get_context("spawn")
+    q, ev = ctx.Queue(), ctx.Event()
+    procs = [ctx.Process(target=_comm_rank, args=(r, world, uid, mode, q, ev)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    try:
+        for _ in range(world):
+            rank, total, mean, note = q.get(timeout=300)
+            out[rank] = (total, mean, note)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    return out
+
+
+def test_comm_allreduce_grads_two_ranks():
+    if _gpus() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = _run_comm(2, "ok")
+    for r in (0, 1):
+        assert out[r][2] is None, out[r]
+        assert out[r][0] == 3.0 and out[r][1] == 3.0  # 1 + 2 summed, then the mean of (3, 3)
+
+
+def test_comm_watchdog_detects_a_rank_that_never_joins():
+    """Rank 1 stays alive between collectives and skips the next one; rank
+    0's rnn_comm_wait gives up after 2 s, aborts the communicator and
+    reports RNN_ERR_NCCL instead of waiting forever (NVLS off)."""
+    if _gpus() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = _run_comm(2, "fail")
+    assert out[1][2] == "abstained", out[1]
+    assert "aborted" in out[0][2], out[0]
