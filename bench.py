@@ -574,6 +574,8 @@ def run_ours(args, cfg_name):
     import torch.distributed as dist
 
     depth_n, width, gbatch, cfg_idx = CONFIGS[cfg_name]
+    if args.global_batch:
+        gbatch = args.global_batch
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -710,6 +712,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="resnet56", choices=sorted(CONFIGS) + ["rustvit"])
     ap.add_argument("--local-bn", action="store_true", help="per-rank BN statistics instead of SyncBN")
+    ap.add_argument("--global-batch", type=int, default=0,
+                    help="override the config's global batch (e.g. 128: one rank's share of config 5 at 8 GPUs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch the step's kernels one by one (no CUDA graph)")
     ap.add_argument("--workload", default="train", choices=["train", "eval", "train-data"],

@@ -96,6 +96,11 @@ struct rnn_resnet {
   // data parallel
   ncclComm_t comm = nullptr;
   rnn_comm handle;  // the communicator as a C ABI handle (rnn_resnet_comm), borrowed
+  // gradient buckets: all-reduced on comm_stream while the backward goes on
+  cudaStream_t comm_stream = nullptr;
+  cudaEvent_t bucket_ev = nullptr, comm_done = nullptr;
+  size_t bucket_floats = 0;  // 0: one all-reduce after the backward
+  bool in_step = false;      // buckets only inside train_step, which joins them
   int rank = 0, world = 1;
   bool sync_bn = false;
   // SyncBN over peer memory (bn.cuh PeerSums); world 1 = NCCL path
@@ -366,12 +371,32 @@ static int resnet_forward(rnn_resnet* net, const float* x, int n, int h, int w, 
   return RNN_OK;
 }
 
+// Sum of grads [lo, hi) over the ranks on comm_stream, after everything the
+// compute stream has queued so far (the backward that finished them).
+static int grad_bucket(rnn_resnet* net, size_t lo, size_t hi) {
+  RNN_CUDA(cudaEventRecord(net->bucket_ev, net->ctx->stream));
+  RNN_CUDA(cudaStreamWaitEvent(net->comm_stream, net->bucket_ev, 0));
+  ncclResult_t r = ncclAllReduce(net->g + lo, net->g + lo, hi - lo, ncclFloat, ncclSum, net->comm, net->comm_stream);
+  if (r != ncclSuccess) return set_error(RNN_ERR_NCCL, "gradient bucket all-reduce: %s", ncclGetErrorString(r));
+  return RNN_OK;
+}
+
 static int resnet_backward(rnn_resnet* net, const float* dlogits) {
   rnn_ctx* ctx = net->ctx;
   const int n = net->n;
   // model.rs:148-157
   RNN_TRY(fc_bwd(ctx, net->pooled, dlogits, n, net->fin, net->fout, net->v + net->fcw_off, net->g + net->fcw_off,
                  net->g + net->fcb_off, net->dpool));
+  // The parameters are laid out stem, blocks, classifier and the backward
+  // finishes them from the end: [lo, pending_hi) is final and not yet summed.
+  size_t pending_hi = net->nparams;
+  auto flush = [&](size_t lo, bool last) -> int {
+    if (!net->in_step || !net->bucket_floats || pending_hi == lo) return RNN_OK;
+    if (!last && pending_hi - lo < net->bucket_floats) return RNN_OK;
+    RNN_TRY(grad_bucket(net, lo, pending_hi));
+    pending_hi = lo;
+    return RNN_OK;
+  };
   int id = 0, it = 1, idm = 2, idx = 3;
   float** G = net->gbuf;
   RNN_TRY(gap_bwd(ctx, net->dpool, n * net->fin, net->fh * net->fw, G[id]));
@@ -400,6 +425,7 @@ static int resnet_backward(rnn_resnet* net, const float* dlogits) {
       RNN_TRY(add_masked(ctx, dx, d, b.out, (size_t)n * b.cin * b.h * b.w, mo));
     }
     std::swap(id, idx);
+    RNN_TRY(flush(b.c1.w_off, false));  // the block's parameters start at its first conv
   }
   // stem: relu_back, BN backward, dW only (model.rs:154-156)
   const int hw = net->h * net->w;
@@ -408,7 +434,7 @@ static int resnet_backward(rnn_resnet* net, const float* dlogits) {
   RNN_TRY(bn_backward(net, net->stem_bn, d, net->stem_y, net->stem_out, n, hw, t, &net->stem, net->w, &tp,
                       net->stem_m_ok ? net->stem_m : nullptr));
   RNN_TRY(conv_backward(net, net->stem, net->x_in, t, n, net->h, net->w, nullptr, false, tp));
-  return RNN_OK;
+  return flush(0, true);
 }
 
 static int resnet_step(rnn_resnet* net, float lr, float mom, float wd) {
@@ -494,6 +520,11 @@ static int peer_setup(rnn_resnet* net) {
 
 static int allreduce_grads(rnn_resnet* net) {
   if (!net->comm || net->world <= 1) return RNN_OK;
+  if (net->bucket_floats) {  // the buckets ran during train_step's backward: join them
+    RNN_CUDA(cudaEventRecord(net->comm_done, net->comm_stream));
+    RNN_CUDA(cudaStreamWaitEvent(net->ctx->stream, net->comm_done, 0));
+    return RNN_OK;
+  }
   ncclResult_t r = ncclAllReduce(net->g, net->g, net->nparams, ncclFloat, ncclSum, net->comm, net->ctx->stream);
   if (r != ncclSuccess) return set_error(RNN_ERR_NCCL, "gradient allreduce: %s", ncclGetErrorString(r));
   return RNN_OK;
@@ -507,7 +538,10 @@ static int train_step(rnn_resnet* net, const float* x, const uint32_t* labels, i
   BnScratch s = bn_scratch(net, n, 1);
   RNN_TRY(softmax_ce(net->ctx, net->logits, labels, n, net->fout, smooth, net->dlogits, s.row_loss, s.hit, loss,
                      correct));
-  RNN_TRY(resnet_backward(net, net->dlogits));
+  net->in_step = net->comm && net->world > 1;
+  const int rc = resnet_backward(net, net->dlogits);
+  net->in_step = false;
+  RNN_TRY(rc);
   RNN_TRY(allreduce_grads(net));
   return resnet_step(net, lr, mom, wd);
 }
@@ -710,6 +744,9 @@ extern "C" int rnn_resnet_destroy(rnn_resnet* net) {
   cudaFree(net->loss_dev);
   cudaFree(net->correct_dev);
   if (net->comm && !net->handle.aborted) ncclCommDestroy(net->comm);  // an abort already released it
+  if (net->comm_stream) cudaStreamDestroy(net->comm_stream);
+  if (net->bucket_ev) cudaEventDestroy(net->bucket_ev);
+  if (net->comm_done) cudaEventDestroy(net->comm_done);
   delete net;
   return RNN_OK;
 }
@@ -945,6 +982,19 @@ extern "C" int rnn_resnet_dp_init(rnn_resnet* net, int rank, int world, const un
   net->rank = rank;
   net->world = world;
   net->sync_bn = sync_bn != 0;
+  // gradient buckets of ~8 MB (RNN_GRAD_BUCKET_MB, 0 = one all-reduce after
+  // the backward), summed on their own stream while the backward goes on
+  net->bucket_floats = 0;
+  if (world > 1) {
+    const char* e = getenv("RNN_GRAD_BUCKET_MB");
+    const double mb = e && e[0] ? atof(e) : 8.0;
+    if (mb > 0) {
+      net->bucket_floats = (size_t)(mb * (1 << 20) / sizeof(float));
+      if (!net->comm_stream) RNN_CUDA(cudaStreamCreateWithFlags(&net->comm_stream, cudaStreamNonBlocking));
+      if (!net->bucket_ev) RNN_CUDA(cudaEventCreateWithFlags(&net->bucket_ev, cudaEventDisableTiming));
+      if (!net->comm_done) RNN_CUDA(cudaEventCreateWithFlags(&net->comm_done, cudaEventDisableTiming));
+    }
+  }
   if (world > 1 && net->sync_bn && !peer_sync_disabled()) RNN_TRY(peer_setup(net));
   return RNN_OK;
 }
