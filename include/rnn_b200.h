@@ -422,6 +422,34 @@ int rnn_comm_abort(rnn_comm *comm);
  * the communicator and returns RNN_ERR_NCCL. */
 int rnn_comm_wait(rnn_ctx *ctx, rnn_comm *comm, int timeout_ms);
 
+/* ---- rustvit fusions the reference identified and did not build
+ * (README.md:549-552) ------------------------------------------------------ */
+/* s = x (+ r1) (+ r2) (vit.rs:160-176: the block's residual adds, each rounded
+ * like the reference's add_), written to sum_out when non-null, then
+ * LayerNorm::forward of s (norm.rs:38-100) into y / xhat / invstd.  With
+ * a_image, y is also written as the packed A operand of the GEMM that reads
+ * it: per 128-row tile and 32-column block, a [hi | lo] pair of 16 KB TF32
+ * tiles in the engine's shared-memory layout (rnn_linear_fwd_packed_dev,
+ * rnn_swiglu_fwd_dev bulk-copy it); it holds ceil(rows/128)*128*c*2 floats.
+ * c a multiple of 128 up to 512; 16-byte aligned tensors. */
+int rnn_layernorm_res_fwd_dev(rnn_ctx *ctx, const float *x, const float *r1,
+                              const float *r2, int rows, int c, const float *g,
+                              const float *b, float eps, float *sum_out,
+                              float *y, float *xhat, float *invstd,
+                              float *a_image);
+/* Linear::forward (linear.rs:44-63) from a packed A image of x: y = x W^T + b,
+ * the bias added in the GEMM's epilogue.  fin a multiple of 32. */
+int rnn_linear_fwd_packed_dev(rnn_ctx *ctx, const float *a_image, int rows,
+                              int fin, int fout, const float *w, const float *b,
+                              float *y);
+/* SwiGlu::forward's first half (norm.rs:250-260) as one GEMM: ab = x Wg^T + bg
+ * ([rows, 2h], value columns then gate columns, kept for the backward) and
+ * u = silu(a) * g ([rows, h]) from its epilogue.  x row-major, or a_image
+ * (then x may be null).  c a multiple of 32, h a multiple of 16. */
+int rnn_swiglu_fwd_dev(rnn_ctx *ctx, const float *x, const float *a_image,
+                       int rows, int c, int h, const float *wg, const float *bg,
+                       float *ab, float *u);
+
 /* ---- rustvit training step (vit.rs, train.rs:70-118 and 346-387) -------- */
 /* RustViT::new (vit.rs:441-509) on the device.  cfg9 = {width, cmid, dim,
  * heads, depth3, dim4, heads4, depth4, img} (vit.rs:349-365); mem_at lists the

@@ -148,6 +148,9 @@ extern "C" {
     pub fn rnn_comm_check(comm: *mut RnnComm) -> c_int;
     pub fn rnn_comm_abort(comm: *mut RnnComm) -> c_int;
     pub fn rnn_comm_wait(ctx: *mut RnnCtx, comm: *mut RnnComm, timeout_ms: c_int) -> c_int;
+    pub fn rnn_layernorm_res_fwd_dev(ctx: *mut RnnCtx, x: *const f32, r1: *const f32, r2: *const f32, rows: c_int, c: c_int, g: *const f32, b: *const f32, eps: f32, sum_out: *mut f32, y: *mut f32, xhat: *mut f32, invstd: *mut f32, a_image: *mut f32) -> c_int;
+    pub fn rnn_linear_fwd_packed_dev(ctx: *mut RnnCtx, a_image: *const f32, rows: c_int, fin: c_int, fout: c_int, w: *const f32, b: *const f32, y: *mut f32) -> c_int;
+    pub fn rnn_swiglu_fwd_dev(ctx: *mut RnnCtx, x: *const f32, a_image: *const f32, rows: c_int, c: c_int, h: c_int, wg: *const f32, bg: *const f32, ab: *mut f32, u: *mut f32) -> c_int;
     pub fn rnn_rustvit_create(ctx: *mut RnnCtx, cfg9: *const c_int, mem_at: *const c_int, n_mem: c_int, droppath: f32, parent: *const u32, nf: c_int, ncoarse: c_int, seed: u64, out: *mut *mut RnnRustvit) -> c_int;
     pub fn rnn_rustvit_destroy(net: *mut RnnRustvit) -> c_int;
     pub fn rnn_rustvit_num_params(net: *mut RnnRustvit, out: *mut usize) -> c_int;

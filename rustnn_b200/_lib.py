@@ -56,6 +56,9 @@ SIGS = {
     "rnn_gemm_dw": [CTX, I, I, I, FP, FP, FP],
     "rnn_gemm_dw_noalloc_dev": [I, I, I, FP, FP, FP, P],
     "rnn_gemm_dw_noalloc_status": [P],
+    "rnn_layernorm_res_fwd_dev": [CTX, FP, FP, FP, I, I, FP, FP, F, FP, FP, FP, FP, FP],
+    "rnn_linear_fwd_packed_dev": [CTX, FP, I, I, I, FP, FP, FP],
+    "rnn_swiglu_fwd_dev": [CTX, FP, FP, I, I, I, FP, FP, FP, FP],
     "rnn_alloc": [CTX, Z, P],
     "rnn_free": [CTX, P],
     "rnn_memcpy_h2d": [CTX, P, P, Z],

@@ -489,6 +489,18 @@ struct prob_extra_bn {
   static constexpr int value =
       prob_halo<P>::value + (prob_stats<P>::value ? stats_bytes<BN>() : 0) + prob_rowepi<P>::bytes;
 };
+// Problems with A_BULK = true supply the A operand pre-packed, like a bulk
+// B: const void* a_src(int m_tile, int kb) const returns the [hi | lo] image
+// of that 128-row tile and K block (K-major SWIZZLE_128B rows), and load_a
+// is not called.
+template <class P, class = void>
+struct prob_abulk {
+  static constexpr bool value = false;
+};
+template <class P>
+struct prob_abulk<P, std::void_t<decltype(P::A_BULK)>> {
+  static constexpr bool value = P::A_BULK;
+};
 // HALO problems may set A_TMEM: their producers write A into tensor memory.
 template <class P, class = void>
 struct prob_atm {
@@ -556,6 +568,8 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
   constexpr bool STATS = prob_stats<Prob>::value;
   constexpr bool ROWEPI = prob_rowepi<Prob>::value;
   static_assert(!C::ATM || Prob::B_BULK, "A in tensor memory needs a bulk-copied B");
+  constexpr bool A_BULK = prob_abulk<Prob>::value;
+  static_assert(!(A_BULK && (C::ATM || HALO)), "a bulk-copied A lives in shared memory");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte aligned operand ring
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -580,7 +594,7 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; s++) {
       // one group's 128 threads, plus the bulk-copy thread's expect_tx arrival
-      mbar_init(&full[s], GROUP_THREADS + (Prob::B_BULK ? 1 : 0));
+      mbar_init(&full[s], GROUP_THREADS + ((Prob::B_BULK || A_BULK) ? 1 : 0));
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; b++) {
@@ -710,7 +724,7 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
         const int stage = it % C::STAGES;
         const uint32_t phase = (it / C::STAGES) & 1;
         float va[32];
-        prob.load_a(ts, kb, gt, va);
+        if constexpr (!A_BULK) prob.load_a(ts, kb, gt, va);
         constexpr int NB = Prob::B_BULK ? 4 : C::BCH * 4;
         float vb[NB];
         if constexpr (!Prob::B_BULK) prob.template load_b<NB>(ts, kb, gt, vb);
@@ -723,13 +737,16 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
         const uint32_t a_lo = a_hi + C::A_BYTES;
         const uint32_t b_hi = a_hi + C::A_SMEM;
         const uint32_t b_lo = b_hi + C::B_BYTES;
-        if constexpr (Prob::B_BULK) {
+        if constexpr (Prob::B_BULK || A_BULK) {
           if (gt == 0) {
-            mbar_arrive_expect_tx(&full[stage], 2 * C::B_BYTES);
-            bulk_g2s(b_hi, prob.b_src(nt, kb), 2 * C::B_BYTES, &full[stage]);
+            mbar_arrive_expect_tx(&full[stage], (Prob::B_BULK ? 2 * C::B_BYTES : 0) + (A_BULK ? 2 * C::A_BYTES : 0));
+            if constexpr (Prob::B_BULK) bulk_g2s(b_hi, prob.b_src(nt, kb), 2 * C::B_BYTES, &full[stage]);
+            if constexpr (A_BULK) bulk_g2s(a_hi, prob.a_src(mt, kb), 2 * C::A_BYTES, &full[stage]);
           }
         }
-        if constexpr (C::ATM) {
+        if constexpr (A_BULK) {
+          (void)a_lo;
+        } else if constexpr (C::ATM) {
           // load_a returned the thread's own A row (a_slot(gt, j) == (gt, j)):
           // row gt = TMEM lane gt
           uint32_t hi[32], lo[32];

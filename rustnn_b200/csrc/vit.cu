@@ -323,6 +323,8 @@ struct rnn_rustvit {
         *bs_qkv = nullptr, *bs_qkv2 = nullptr;
   float *b_img_a = nullptr, *b_img_b = nullptr, *b_img_c = nullptr, *b_img_d = nullptr, *b_c2 = nullptr,
         *b_c2b = nullptr;
+  // packed A image of the last LayerNorm output that feeds a GEMM
+  float* aimg = nullptr;
   const float* x_in = nullptr;  // the batch of the last forward
   float* xkeep = nullptr;
   float* losses = nullptr;  // device [8]
@@ -537,6 +539,12 @@ static int ensure_acts(rnn_rustvit* net, int n) {
   RNN_TRY(dalloc(net, &net->bs_wide2, hmax));
   RNN_TRY(dalloc(net, &net->bs_qkv, 3 * rc));
   RNN_TRY(dalloc(net, &net->bs_qkv2, 3 * rc));
+  {
+    size_t amax = 0;  // ceil(rows / 128) * 128 rows of c columns, hi and lo
+    for (auto* v : {&net->blocks3, &net->blocks4})
+      for (auto& b : *v) amax = std::max(amax, ((size_t)n * b.th * b.th + 127) / 128 * 128 * b.c * 2);
+    RNN_TRY(dalloc(net, &net->aimg, amax));
+  }
   const size_t imgmax = std::max((size_t)n * w * img, (size_t)n * cm * r2);
   RNN_TRY(dalloc(net, &net->b_img_a, imgmax));
   RNN_TRY(dalloc(net, &net->b_img_b, imgmax));
@@ -567,6 +575,20 @@ static int lin_bwd(rnn_rustvit* net, LinL& l, const float* dy, float* dx) {
 static int ln_fwd(rnn_rustvit* net, LNL& l, const float* x, int rows, float* y) {
   l.rows = rows;
   return rnn_layernorm_fwd_dev(net->ctx, x, rows, l.c, P(net, l.g), P(net, l.b), 1e-5f, y, l.xhat, l.invstd);
+}
+// The fused forms (csrc/fused.cu) where the shapes allow them: LayerNorm of
+// x (+ r1) (+ r2) writing the packed A image, and the GEMMs reading it.
+static bool ln_fusable(int c) { return c % 128 == 0 && c <= 512; }
+static int ln_res_fwd(rnn_rustvit* net, LNL& l, const float* x, const float* r1, const float* r2, int rows,
+                      float* sum_out, float* y, float* img) {
+  l.rows = rows;
+  return rnn_layernorm_res_fwd_dev(net->ctx, x, r1, r2, rows, l.c, P(net, l.g), P(net, l.b), 1e-5f, sum_out, y,
+                                   l.xhat, l.invstd, img);
+}
+static int lin_fwd_img(rnn_rustvit* net, LinL& l, const float* img, const float* x, int rows, float* y) {
+  l.x = x;  // the backward's dW reads the row-major input
+  l.rows = rows;
+  return rnn_linear_fwd_packed_dev(net->ctx, img, rows, l.fin, l.fout, P(net, l.w), Popt(net, l.b), y);
 }
 static int ln_bwd(rnn_rustvit* net, LNL& l, const float* dy, float* dx) {
   return rnn_layernorm_bwd_dev(net->ctx, dy, l.xhat, l.invstd, l.rows, l.c, P(net, l.g), dx, Gd(net, l.g),
@@ -664,10 +686,13 @@ static int block_fwd(rnn_rustvit* net, Block& b, const float* x, const float* me
                      uint64_t seed) {
   const int c = b.c, t = b.th * b.th, rows = n * t;
   const size_t rc = (size_t)rows * c, per = (size_t)t * c;
-  RNN_TRY(ln_fwd(net, b.n1, x, rows, b.hb));
+  const bool fuse = ln_fusable(c);
+  if (fuse) RNN_TRY(ln_res_fwd(net, b.n1, x, nullptr, nullptr, rows, nullptr, b.hb, net->aimg));
+  else RNN_TRY(ln_fwd(net, b.n1, x, rows, b.hb));
   // self-attention (attn.rs:387-413)
   SelfAttnL& A = b.attn;
-  RNN_TRY(lin_fwd(net, A.qkv, b.hb, rows, A.ab));
+  if (fuse) RNN_TRY(lin_fwd_img(net, A.qkv, net->aimg, b.hb, rows, A.ab));
+  else RNN_TRY(lin_fwd(net, A.qkv, b.hb, rows, A.ab));
   RNN_TRY(rnn_attn_fwd_dev(net->ctx, n, A.h, A.dh, A.th, A.th, A.th, A.th, 1, A.ab, 3 * c, 0, A.ab, 3 * c, c,
                            2 * c, P(net, A.tau), P(net, A.rel), A.p, A.o));
   RNN_TRY(lin_fwd(net, A.proj, A.o, rows, b.a));
@@ -678,22 +703,36 @@ static int block_fwd(rnn_rustvit* net, Block& b, const float* x, const float* me
   RNN_TRY(rnn_add_dev(net->ctx, b.a, b.tmp, rc));
   RNN_TRY(ls_fwd(net, b.ls1, b.a, rows, b.s1));
   RNN_TRY(dp_fwd(net, b.dp1, b.s1, n, per, train, seed ^ b.idx));
-  RNN_TRY(copy(net, b.y, x, rc));
-  RNN_TRY(rnn_add_dev(net->ctx, b.y, b.s1, rc));
+  if (!fuse) {
+    RNN_TRY(copy(net, b.y, x, rc));
+    RNN_TRY(rnn_add_dev(net->ctx, b.y, b.s1, rc));
+  }
   if (b.has_cross) {
     CrossAttnL& X = b.cross;
-    RNN_TRY(lin_fwd(net, X.wq, b.hb, rows, X.q));
+    // the image still holds LN1's output (no LayerNorm ran since)
+    if (fuse) RNN_TRY(lin_fwd_img(net, X.wq, net->aimg, b.hb, rows, X.q));
+    else RNN_TRY(lin_fwd(net, X.wq, b.hb, rows, X.q));
     RNN_TRY(rnn_attn_fwd_dev(net->ctx, n, X.h, X.dh, X.th, X.th, X.mh, X.mh, 0, X.q, c, 0, mem, 2 * c, 0, c,
                              P(net, X.tau), P(net, X.rel), X.p, X.o));
     RNN_TRY(lin_fwd(net, X.proj, X.o, rows, b.cm));
     RNN_TRY(ls_fwd(net, b.lsm, b.cm, rows, b.s2));
     RNN_TRY(dp_fwd(net, b.dp2, b.s2, n, per, train, seed ^ b.idx ^ 0x5151ULL));
-    RNN_TRY(rnn_add_dev(net->ctx, b.y, b.s2, rc));
+    if (!fuse) RNN_TRY(rnn_add_dev(net->ctx, b.y, b.s2, rc));
   }
-  RNN_TRY(ln_fwd(net, b.n2, b.y, rows, b.h2));
-  // SwiGLU (norm.rs:250-268)
-  RNN_TRY(lin_fwd(net, b.mlp.wg, b.h2, rows, b.mlp.ab));
-  RNN_TRY(rnn_swiglu_act_fwd_dev(net->ctx, b.mlp.ab, rows, b.mlp.h, b.mlp.u));
+  // y = x + s1 (+ s2) joined into the LayerNorm that reads it
+  if (fuse) RNN_TRY(ln_res_fwd(net, b.n2, x, b.s1, b.has_cross ? b.s2 : nullptr, rows, b.y, b.h2, net->aimg));
+  else RNN_TRY(ln_fwd(net, b.n2, b.y, rows, b.h2));
+  // SwiGLU (norm.rs:250-268); fused: the gate in the first GEMM's epilogue
+  if (fuse && b.mlp.h % 16 == 0) {
+    LinL& g = b.mlp.wg;
+    g.x = b.h2;
+    g.rows = rows;
+    RNN_TRY(rnn_swiglu_fwd_dev(net->ctx, b.h2, net->aimg, rows, c, b.mlp.h, P(net, g.w), P(net, g.b), b.mlp.ab,
+                               b.mlp.u));
+  } else {
+    RNN_TRY(lin_fwd(net, b.mlp.wg, b.h2, rows, b.mlp.ab));
+    RNN_TRY(rnn_swiglu_act_fwd_dev(net->ctx, b.mlp.ab, rows, b.mlp.h, b.mlp.u));
+  }
   RNN_TRY(lin_fwd(net, b.mlp.wd, b.mlp.u, rows, b.m));
   RNN_TRY(ls_fwd(net, b.ls2, b.m, rows, b.s3));
   RNN_TRY(dp_fwd(net, b.dp3, b.s3, n, per, train, seed ^ b.idx ^ 0xA2A2ULL));

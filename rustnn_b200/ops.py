@@ -25,7 +25,7 @@ __all__ = [
     "conv2d_wgrad", "batchnorm_forward", "batchnorm_eval", "batchnorm_backward", "relu_back_", "add_",
     "add_relu_", "gap_forward", "gap_backward", "softmax_ce", "sgd_nesterov_", "out_dim", "RnnError",
     "rel_index", "attn_forward", "attn_backward", "layernorm_forward", "layernorm_backward", "linear_forward",
-    "linear_backward", "newton_schulz_", "muon_step_", "adamw_step_", "clip_", "ema_update_",
+    "linear_backward", "layernorm_res_forward", "linear_forward_packed", "swiglu_fused_forward", "newton_schulz_", "muon_step_", "adamw_step_", "clip_", "ema_update_",
     "layerscale_forward", "layerscale_backward", "swiglu_forward", "swiglu_backward", "dwconv3_forward",
     "dwconv3_backward", "seqpool_forward", "seqpool_backward", "droppath_forward_", "droppath_backward_",
     "token_merge", "tok_layout", "taxo_forward_", "taxo_backward", "ce_soft", "kl_distill", "hint_mse",
@@ -287,6 +287,38 @@ def linear_forward(x, rows, fin, fout, w, b=None, ctx=None):
     call("rnn_linear_fwd_dev", _ctx_of(x, ctx), _ptr(x, "x"), rows, fin, fout, _ptr(w, "w"), _opt_ptr(b, "b"),
          _ptr(y, "y"))
     return y
+
+
+def layernorm_res_forward(x, rows, c, gamma, beta, r1=None, r2=None, eps=1e-5, pack=False, ctx=None):
+    """s = x (+ r1) (+ r2) and LayerNorm::forward of s in one pass
+    (vit.rs:160-176 + norm.rs:38); returns (s, y, xhat, invstd, a_image),
+    a_image (the packed A operand of the next GEMM) only when pack."""
+    s = torch.empty_like(x) if r1 is not None else None
+    y, xhat = torch.empty_like(x), torch.empty_like(x)
+    invstd = torch.empty(rows, device=x.device, dtype=torch.float32)
+    img = torch.empty(((rows + 127) // 128) * 128 * c * 2, device=x.device, dtype=torch.float32) if pack else None
+    call("rnn_layernorm_res_fwd_dev", _ctx_of(x, ctx), _ptr(x, "x"), _opt_ptr(r1, "r1"), _opt_ptr(r2, "r2"), rows, c,
+         _ptr(gamma, "gamma"), _ptr(beta, "beta"), eps, _opt_ptr(s, "sum"), _ptr(y, "y"), _ptr(xhat, "xhat"),
+         _ptr(invstd, "invstd"), _opt_ptr(img, "a_image"))
+    return s, y, xhat, invstd, img
+
+
+def linear_forward_packed(a_image, rows, fin, fout, w, b=None, ctx=None):
+    """Linear::forward from the packed A image of x (bias in the epilogue)."""
+    y = torch.empty(rows * fout, device=a_image.device, dtype=torch.float32)
+    call("rnn_linear_fwd_packed_dev", _ctx_of(a_image, ctx), _ptr(a_image, "a_image"), rows, fin, fout,
+         _ptr(w, "w"), _opt_ptr(b, "b"), _ptr(y, "y"))
+    return y
+
+
+def swiglu_fused_forward(x, rows, c, h, wg, bg, a_image=None, ctx=None):
+    """SwiGlu::forward's first GEMM with the gate in its epilogue: (ab, u)."""
+    src = a_image if a_image is not None else x
+    ab = torch.empty(rows * 2 * h, device=src.device, dtype=torch.float32)
+    u = torch.empty(rows * h, device=src.device, dtype=torch.float32)
+    call("rnn_swiglu_fwd_dev", _ctx_of(src, ctx), _opt_ptr(x, "x"), _opt_ptr(a_image, "a_image"), rows, c, h,
+         _ptr(wg, "wg"), _ptr(bg, "bg"), _ptr(ab, "ab"), _ptr(u, "u"))
+    return ab, u
 
 
 def linear_backward(x, dy, rows, fin, fout, w, dw, db=None, ctx=None):
