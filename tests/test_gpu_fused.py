@@ -3,7 +3,7 @@ lists them as identified and not built): the residual add joined into
 LayerNorm, LayerNorm writing the packed A operand of the next GEMM, and the
 SiLU gate in the SwiGLU first GEMM's epilogue.  Each is checked against the
 CPU oracle (bar 1e-4) and against the unfused device sequence, which it
-reproduces bit for bit (the same f32 operations in the same order)."""
+reproduces bit for bit where both run the same summation order."""
 import numpy as np
 import pytest
 
@@ -64,7 +64,8 @@ def test_layernorm_residual_and_packed_linear(ops, rows, c, nres):
     out = ops.linear_forward_packed(img, rows, c, fout, dev(w), dev(bias))
     ref = O.linear_fwd(y_ref, rows, c, fout, w, bias)
     assert rel(host(out), ref) < TOL
-    assert np.array_equal(host(out), host(ops.linear_forward(y, rows, c, fout, dev(w), dev(bias))))
+    # the unfused GEMM may split K for small row counts (another summation order)
+    assert rel(host(out), host(ops.linear_forward(y, rows, c, fout, dev(w), dev(bias)))) < 1e-5
 
 
 @pytest.mark.parametrize("rows,c,h", [(8192, 256, 352), (2048, 384, 512), (200, 64, 48)])
