@@ -71,6 +71,118 @@ struct DenseProb {
   }
 };
 
+// DenseProb on the engine's native interface.  K-major operands keep the
+// per-chunk mapping (8 threads per row, 16-byte loads along K).  An
+// M/N-contiguous operand (A with at, B without bt) is gathered in 4 x 4
+// blocks: a thread loads 4 consecutive rows at each of 4 consecutive K with
+// one 16-byte load per K (a warp covers 512 contiguous bytes) and transposes
+// the block in registers into the 4 rows' K chunks, instead of 16 scalar
+// loads.  For A the thread owns rows 4*(gt % 32) .. +3 in chunks
+// 2*(gt / 32) and +1; for B (tiles of 64 columns and more) block
+// gt + 128*t covers rows 4*(b % (BN/4)) .. +3 in chunk b / (BN/4).  Ragged
+// or unaligned operands fall back to bounds-checked scalar loads.
+template <bool AT, bool BT, int BN>
+struct DenseNative : DenseProb<AT, BT> {
+  using Base = DenseProb<AT, BT>;
+  static constexpr bool B_BULK = false;
+  static constexpr bool B_BLOCKS = !BT && BN >= 64;
+  struct TS {
+    int m0, n0;
+  };
+  __device__ __forceinline__ void tile_begin(TS& ts, int m0, int n0, int) const {
+    ts.m0 = m0;
+    ts.n0 = n0;
+  }
+  static __device__ __forceinline__ void a_slot(int gt, int j, int& r, int& c) {
+    if (!AT) { r = (gt >> 3) + 16 * j; c = gt & 7; }
+    else { r = 4 * (gt & 31) + (j & 3); c = 2 * (gt >> 5) + (j >> 2); }
+  }
+  static __device__ __forceinline__ void b_slot(int gt, int j, int& r, int& c) {
+    if (BT) {
+      const int idx = gt + 128 * j;
+      r = idx >> 3; c = idx & 7;
+    } else if (B_BLOCKS) {
+      const int b = gt + 128 * (j >> 2);
+      r = 4 * (b % (BN / 4)) + (j & 3);
+      c = b / (BN / 4);
+    } else {
+      const int idx = gt + 128 * j;
+      r = idx % BN; c = idx / BN;
+    }
+  }
+  // rows r0..r0+3 of an operand stored [K][rows] (row index contiguous), at
+  // K values k0..k0+3, transposed: out[4*rr + kk] = X[k0 + kk][r0 + rr]
+  static __device__ __forceinline__ void block4(const float* __restrict__ x, int rows, int K, int r0, int k0,
+                                                bool vec, float (&out)[16]) {
+    if (vec && r0 + 3 < rows && k0 + 3 < K) {
+#pragma unroll
+      for (int kk = 0; kk < 4; kk++) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(x + (size_t)(k0 + kk) * rows + r0));
+        out[kk] = t.x; out[4 + kk] = t.y; out[8 + kk] = t.z; out[12 + kk] = t.w;
+      }
+    } else {
+#pragma unroll
+      for (int rr = 0; rr < 4; rr++)
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++)
+          out[4 * rr + kk] =
+              (r0 + rr < rows && k0 + kk < K) ? __ldg(x + (size_t)(k0 + kk) * rows + r0 + rr) : 0.0f;
+    }
+  }
+  __device__ __forceinline__ void load_a(const TS& ts, int kb, int gt, float (&v)[32]) const {
+    if constexpr (!AT) {
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        int r, c;
+        a_slot(gt, j, r, c);
+        float t[4];
+        Base::load_a(ts.m0 + r, kb * BK + 4 * c, t);
+        v[4 * j] = t[0]; v[4 * j + 1] = t[1]; v[4 * j + 2] = t[2]; v[4 * j + 3] = t[3];
+      }
+    } else {
+#pragma unroll
+      for (int jc = 0; jc < 2; jc++) {
+        float blk[16];
+        block4(this->a, this->M, this->K, ts.m0 + 4 * (gt & 31), kb * BK + 4 * (2 * (gt >> 5) + jc), this->a_vec,
+               blk);
+#pragma unroll
+        for (int e = 0; e < 16; e++) v[16 * jc + e] = blk[e];  // j = 4*jc + rr holds row rr's chunk
+      }
+    }
+  }
+  template <int NB>
+  __device__ __forceinline__ void load_b(const TS& ts, int kb, int gt, float (&v)[NB]) const {
+    if constexpr (B_BLOCKS) {
+#pragma unroll
+      for (int t = 0; t < NB / 16; t++) {
+        const int b = gt + 128 * t;
+        float blk[16];
+        block4(this->b, this->N, this->K, ts.n0 + 4 * (b % (BN / 4)), kb * BK + 4 * (b / (BN / 4)), this->b_vec,
+               blk);
+#pragma unroll
+        for (int e = 0; e < 16; e++) v[16 * t + e] = blk[e];
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < NB / 4; j++) {
+        int r, c;
+        b_slot(gt, j, r, c);
+        float t[4];
+        Base::load_b(ts.n0 + r, kb * BK + 4 * c, t);
+        v[4 * j] = t[0]; v[4 * j + 1] = t[1]; v[4 * j + 2] = t[2]; v[4 * j + 3] = t[3];
+      }
+    }
+  }
+  __device__ __forceinline__ const void* b_src(int, int) const { return nullptr; }
+};
+
+template <int BN, bool AT, bool BT>
+static DenseNative<AT, BT, BN> native(const DenseProb<AT, BT>& p) {
+  DenseNative<AT, BT, BN> n;
+  static_cast<DenseProb<AT, BT>&>(n) = p;
+  return n;
+}
+
 template <int BN>
 struct DenseLauncher {
   template <class P>
@@ -85,7 +197,7 @@ struct DenseLauncher {
     RNN_RANGE(prob.a, sizeof(float) * (size_t)prob.M * prob.K);
     RNN_RANGE(prob.b, sizeof(float) * (size_t)prob.N * prob.K);
     RNN_RANGE(prob.c, sizeof(float) * (size_t)prob.M * prob.N);
-    RNN_TRY(launch<BN>(ctx, prob, s));
+    RNN_TRY(launch<BN>(ctx, native<BN>(prob), s));
     if (s.splits > 1)
       RNN_TRY(launch_splitk_reduce(ctx, prob.ws, prob.c, prob.M, prob.N, s.splits, prob.acc != 0,
                                    false));
@@ -101,8 +213,10 @@ static int gemm_typed(rnn_ctx* ctx, int m, int n, int k, const float* a, const f
   DenseProb<AT, BT> p;
   p.a = a; p.b = b; p.c = c; p.ws = nullptr;
   p.M = m; p.N = n; p.K = k; p.acc = acc ? 1 : 0; p.splits = 1;
-  p.a_vec = (k % 4 == 0) && al16(a);
-  p.b_vec = (k % 4 == 0) && al16(b);
+  // 16-byte loads: along K for a K-major operand, along the rows for an
+  // M/N-contiguous one (DenseNative's 4 x 4 blocks)
+  p.a_vec = (AT ? m % 4 == 0 : k % 4 == 0) && al16(a);
+  p.b_vec = (BT ? k % 4 == 0 : n % 4 == 0) && al16(b);
   p.c_vec = (n % 4 == 0) && al16(c);
   const int m_tiles = (m + BM - 1) / BM;
   const int bn = pick_bn(n, m_tiles, ctx->num_sms);
@@ -419,7 +533,7 @@ static int noalloc_run(rnn_ctx* ctx, DenseProb<true, false> p, int splits) {
   Sched s = make_sched(p.M, p.N, p.K, BN, splits);
   p.splits = s.splits;
   p.ws = s.splits > 1 ? static_cast<float*>(ctx->ws) : nullptr;
-  RNN_TRY(launch<BN>(ctx, p, s));
+  RNN_TRY(launch<BN>(ctx, native<BN>(p), s));
   if (s.splits > 1) {
     const size_t total = (size_t)p.M * p.N;
     const unsigned grid = (unsigned)std::min<size_t>((total + 255) / 256, (size_t)ctx->num_sms * 8);
@@ -460,8 +574,8 @@ extern "C" int rnn_gemm_dw_noalloc_dev(int m, int n, int k, const float* a, cons
   DenseProb<true, false> p;
   p.a = a; p.b = b; p.c = c; p.ws = nullptr;
   p.M = m; p.N = n; p.K = k; p.acc = 1; p.splits = 1;
-  p.a_vec = false;
-  p.b_vec = false;
+  p.a_vec = (m % 4 == 0) && ((reinterpret_cast<uintptr_t>(a) & 15) == 0);
+  p.b_vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(b) & 15) == 0);
   p.c_vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(c) & 15) == 0);
   const int bn = pick_bn(n, (m + BM - 1) / BM, ctx.num_sms);
   int splits = pick_splits(m, n, k, bn, ctx.num_sms);

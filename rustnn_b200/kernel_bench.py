@@ -8,6 +8,7 @@
     python -m rustnn_b200.kernel_bench vitstep         # one rustvit Trainer::step (batch 128) after 3 warm-ups,
                                                        # alone between cudaProfilerStart/Stop (ncu
                                                        # --profile-from-start off lists exactly its launches)
+    python -m rustnn_b200.kernel_bench resnetstep --batch 128   # one ResNet-56 W=64 graph step, same way
 
 Prints one line per kernel: time per launch, algorithmic TFLOP/s (2*M*N*K),
 and the minimum HBM bytes / achieved GB/s.  Also the target of the ncu
@@ -208,9 +209,42 @@ def vitstep(args):
              "launches": int(launches)}]
 
 
+def resnetstep(args):
+    """The ResNet-56 W=64 training step (BASELINE config 5's network) at batch
+    args.batch, replayed from a CUDA graph: ten steps timed with CUDA events
+    after four warm-ups, then one step alone inside the profiler range."""
+    import numpy as np
+
+    from . import model
+
+    n = args.batch
+    net = model.ResNet(9, 64, 100, 0)
+    net.use_graph(True)
+    rng = np.random.default_rng(100)
+    u = rng.integers(0, 256, size=n * 3 * 32 * 32).astype(np.float32)
+    x = torch.from_numpy(((u - 127.5) / 73.9).astype(np.float32)).cuda()
+    lab = torch.from_numpy(rng.integers(0, 100, size=n).astype(np.int32)).cuda()
+    for _ in range(4):
+        net.train_step(x, lab)
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(10):
+        net.train_step(x, lab)
+    e1.record(s)
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStart()
+    net.train_step(x, lab)
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    net.close()
+    return [{"kernel": "resnet56_step", "shape": f"batch {n}", "ms": round(e0.elapsed_time(e1) / 10, 3)}]
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["conv", "gemm", "attn", "ln", "muon", "vitstep"])
+    ap.add_argument("what", choices=["conv", "gemm", "attn", "ln", "muon", "vitstep", "resnetstep"])
     ap.add_argument("--cin", type=int, default=64)
     ap.add_argument("--cout", type=int, default=64)
     ap.add_argument("--hw", type=int, default=32)
@@ -221,7 +255,8 @@ def main():
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--dh", type=int, default=32, help="attention head dim (32: BASELINE config 3; 64: rustvit)")
     args = ap.parse_args()
-    rows = {"conv": conv, "gemm": gemm, "attn": attn, "ln": ln, "muon": muon, "vitstep": vitstep}[args.what](args)
+    rows = {"conv": conv, "gemm": gemm, "attn": attn, "ln": ln, "muon": muon, "vitstep": vitstep,
+            "resnetstep": resnetstep}[args.what](args)
     for r in rows:
         print(json.dumps(r))
 
