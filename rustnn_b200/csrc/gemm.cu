@@ -93,17 +93,26 @@ struct DenseNative : DenseProb<AT, BT> {
     ts.m0 = m0;
     ts.n0 = n0;
   }
+  // A thread's 4-row block is stored one row per step, rotated by
+  // (block / 2) % 4: across a warp the rows of one step then differ in row % 8
+  // (8 values), so the 16-byte stores hit all eight positions of the
+  // 128-byte swizzle row (the minimum of four wavefronts per warp store).
+  static __device__ __forceinline__ int rot(int rb) { return (rb >> 1) & 3; }
   static __device__ __forceinline__ void a_slot(int gt, int j, int& r, int& c) {
     if (!AT) { r = (gt >> 3) + 16 * j; c = gt & 7; }
-    else { r = 4 * (gt & 31) + (j & 3); c = 2 * (gt >> 5) + (j >> 2); }
+    else {
+      const int rb = gt & 31;
+      r = 4 * rb + (((j & 3) + rot(rb)) & 3);
+      c = 2 * (gt >> 5) + (j >> 2);
+    }
   }
   static __device__ __forceinline__ void b_slot(int gt, int j, int& r, int& c) {
     if (BT) {
       const int idx = gt + 128 * j;
       r = idx >> 3; c = idx & 7;
     } else if (B_BLOCKS) {
-      const int b = gt + 128 * (j >> 2);
-      r = 4 * (b % (BN / 4)) + (j & 3);
+      const int b = gt + 128 * (j >> 2), rb = b % (BN / 4);
+      r = 4 * rb + (((j & 3) + rot(rb)) & 3);
       c = b / (BN / 4);
     } else {
       const int idx = gt + 128 * j;
@@ -111,22 +120,34 @@ struct DenseNative : DenseProb<AT, BT> {
     }
   }
   // rows r0..r0+3 of an operand stored [K][rows] (row index contiguous), at
-  // K values k0..k0+3, transposed: out[4*rr + kk] = X[k0 + kk][r0 + rr]
+  // K values k0..k0+3, in slot order: out[4*jj + kk] = X[k0 + kk][r0 + ((jj + s) & 3)]
+  // (each loaded float4 rotated by s with two conditional swaps)
   static __device__ __forceinline__ void block4(const float* __restrict__ x, int rows, int K, int r0, int k0,
-                                                bool vec, float (&out)[16]) {
-    if (vec && r0 + 3 < rows && k0 + 3 < K) {
+                                                bool vec, int s, float* __restrict__ out) {
+    const bool full = vec && r0 + 3 < rows && k0 + 3 < K;
 #pragma unroll
-      for (int kk = 0; kk < 4; kk++) {
+    for (int kk = 0; kk < 4; kk++) {
+      float a, b, c, d;
+      if (full) {
         const float4 t = __ldg(reinterpret_cast<const float4*>(x + (size_t)(k0 + kk) * rows + r0));
-        out[kk] = t.x; out[4 + kk] = t.y; out[8 + kk] = t.z; out[12 + kk] = t.w;
+        a = t.x; b = t.y; c = t.z; d = t.w;
+      } else {
+        const bool kin = k0 + kk < K;
+        const float* row = x + (size_t)(k0 + kk) * rows + r0;
+        a = kin && r0 < rows ? __ldg(row) : 0.0f;
+        b = kin && r0 + 1 < rows ? __ldg(row + 1) : 0.0f;
+        c = kin && r0 + 2 < rows ? __ldg(row + 2) : 0.0f;
+        d = kin && r0 + 3 < rows ? __ldg(row + 3) : 0.0f;
       }
-    } else {
-#pragma unroll
-      for (int rr = 0; rr < 4; rr++)
-#pragma unroll
-        for (int kk = 0; kk < 4; kk++)
-          out[4 * rr + kk] =
-              (r0 + rr < rows && k0 + kk < K) ? __ldg(x + (size_t)(k0 + kk) * rows + r0 + rr) : 0.0f;
+      if (s & 2) {
+        const float t0 = a, t1 = b;
+        a = c; b = d; c = t0; d = t1;
+      }
+      if (s & 1) {
+        const float t0 = a;
+        a = b; b = c; c = d; d = t0;
+      }
+      out[kk] = a; out[4 + kk] = b; out[8 + kk] = c; out[12 + kk] = d;
     }
   }
   __device__ __forceinline__ void load_a(const TS& ts, int kb, int gt, float (&v)[32]) const {
@@ -141,13 +162,9 @@ struct DenseNative : DenseProb<AT, BT> {
       }
     } else {
 #pragma unroll
-      for (int jc = 0; jc < 2; jc++) {
-        float blk[16];
+      for (int jc = 0; jc < 2; jc++)
         block4(this->a, this->M, this->K, ts.m0 + 4 * (gt & 31), kb * BK + 4 * (2 * (gt >> 5) + jc), this->a_vec,
-               blk);
-#pragma unroll
-        for (int e = 0; e < 16; e++) v[16 * jc + e] = blk[e];  // j = 4*jc + rr holds row rr's chunk
-      }
+               rot(gt & 31), v + 16 * jc);
     }
   }
   template <int NB>
@@ -156,11 +173,8 @@ struct DenseNative : DenseProb<AT, BT> {
 #pragma unroll
       for (int t = 0; t < NB / 16; t++) {
         const int b = gt + 128 * t;
-        float blk[16];
         block4(this->b, this->N, this->K, ts.n0 + 4 * (b % (BN / 4)), kb * BK + 4 * (b / (BN / 4)), this->b_vec,
-               blk);
-#pragma unroll
-        for (int e = 0; e < 16; e++) v[16 * t + e] = blk[e];
+               rot(b % (BN / 4)), v + 16 * t);
       }
     } else {
 #pragma unroll
