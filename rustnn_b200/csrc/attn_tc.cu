@@ -146,6 +146,43 @@ __device__ __forceinline__ float warp_sum_f(float v) {
   return v;
 }
 
+// The row epilogues give lane l accumulator row l of its warp, and the 32
+// rows of a warp are consecutive rows (stride ld floats) of P, dS, q or the
+// bias table.  A row-per-lane access would make every warp instruction touch
+// 32 lines; these move a 32 x 32 chunk through a padded shared-memory buffer
+// (32 x 33 floats per warp, conflict-free both ways) so each global access is
+// one row's 128 contiguous bytes.
+constexpr int STAGE_LD = 33;
+constexpr int STAGE_WARP_BYTES = 32 * STAGE_LD * 4;
+
+// out[e] = base[lane * ld + c0 + e], e < 32
+__device__ __forceinline__ void stage_load(const float* __restrict__ base, size_t ld, int c0, float* buf, int lane,
+                                           float (&out)[32]) {
+  float t[32];
+#pragma unroll
+  for (int rr = 0; rr < 32; rr++) t[rr] = __ldg(base + rr * ld + c0 + lane);
+#pragma unroll
+  for (int rr = 0; rr < 32; rr++) buf[rr * STAGE_LD + lane] = t[rr];
+  __syncwarp();
+#pragma unroll
+  for (int e = 0; e < 32; e++) out[e] = buf[lane * STAGE_LD + e];
+  __syncwarp();
+}
+
+// base[lane * ld + c0 + e] = v[e] (acc: +=)
+__device__ __forceinline__ void stage_store(float* __restrict__ base, size_t ld, int c0, float* buf, int lane,
+                                            const float (&v)[32], bool acc = false) {
+#pragma unroll
+  for (int e = 0; e < 32; e++) buf[lane * STAGE_LD + e] = v[e];
+  __syncwarp();
+#pragma unroll
+  for (int rr = 0; rr < 32; rr++) {
+    float* p = base + rr * ld + c0 + lane;
+    *p = acc ? *p + buf[rr * STAGE_LD + lane] : buf[rr * STAGE_LD + lane];
+  }
+  __syncwarp();
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------- forward
@@ -157,7 +194,7 @@ __device__ __forceinline__ float warp_sum_f(float v) {
 template <int DH>
 struct AttnScoreProb {
   static constexpr bool B_BULK = false;
-  static constexpr int ROW_EPI_WARP_BYTES = 0;
+  static constexpr int ROW_EPI_WARP_BYTES = STAGE_WARP_BYTES;
   AttnTC a;
   int M, N;
   using TS = PairTS;
@@ -173,61 +210,54 @@ struct AttnScoreProb {
   }
   __device__ __forceinline__ const void* b_src(int, int) const { return nullptr; }
 
-  // z = tau * S + bias for the 32 columns of chunk c (bias is -inf on a
-  // masked diagonal, so z is too)
+  // Two passes over the row in TMEM.  Pass 1: z = tau * S + bias per
+  // 32-column chunk (bias is -inf on a masked diagonal, so z is too), z
+  // written back over the chunk, the running maximum and the sum of
+  // exp(z - max) (rescaled when a chunk raises the maximum).  Pass 2: P from
+  // z.  The warp's 32 rows are queries i0 .. i0+31 of one head, consecutive
+  // rows of the bias table and of P, staged through shared memory.
   template <int BN, bool STACK>
-  __device__ __forceinline__ void logits32(uint32_t taddr, int c, float t, const float* brow, float (&z)[32]) const {
-    float4 b4[8];
-#pragma unroll
-    for (int e = 0; e < 8; e++) b4[e] = ldg4(brow + c * 32 + 4 * e);
-    float v[32];
-    acc_ld32<BN, STACK>(taddr, c, v);
-#pragma unroll
-    for (int e = 0; e < 8; e++) {
-      z[4 * e] = t * v[4 * e] + b4[e].x;
-      z[4 * e + 1] = t * v[4 * e + 1] + b4[e].y;
-      z[4 * e + 2] = t * v[4 * e + 2] + b4[e].z;
-      z[4 * e + 3] = t * v[4 * e + 3] + b4[e].w;
-    }
-  }
-
-  // Two passes over the row in TMEM: the running maximum and the sum of
-  // exp(z - max) (rescaled when a chunk raises the maximum), then P.
-  template <int BN, bool STACK>
-  __device__ __forceinline__ void epi_row(int mt, int, int q, int lane, uint32_t taddr, uint8_t*) const {
+  __device__ __forceinline__ void epi_row(int mt, int, int q, int lane, uint32_t taddr, uint8_t* wsm) const {
     PairTS ts;
     pair_of(a, mt, ts);
-    const int row = q * 32 + lane, hl = row >> 6, i = row & 63, hd = 2 * ts.pr + hl;
+    const int hd = 2 * ts.pr + (q >> 1), i0 = (q & 1) * 32;
     const float t = __ldg(a.tau + hd);
-    const float* brow = a.bias + ((size_t)hd * a.tq + i) * a.tk;
+    float* buf = reinterpret_cast<float*>(wsm);
+    const float* bias0 = a.bias + ((size_t)hd * a.tq + i0) * a.tk;
     const int nch = a.tk / 32;
     float mx = -INFINITY, sum = 0.0f;
 #pragma unroll 1
     for (int c = 0; c < nch; c++) {
-      float z[32];
-      logits32<BN, STACK>(taddr, c, t, brow, z);
-      float cm = z[0];
+      float b[32], v[32];
+      stage_load(bias0, a.tk, c * 32, buf, lane, b);
+      acc_ld32<BN, STACK>(taddr, c, v);
+      uint32_t zu[32];
+      float cm = -INFINITY;
 #pragma unroll
-      for (int e = 1; e < 32; e++) cm = fmaxf(cm, z[e]);
+      for (int e = 0; e < 32; e++) {
+        const float z = t * v[e] + b[e];
+        zu[e] = __float_as_uint(z);
+        cm = fmaxf(cm, z);
+      }
+      tmem_st32(taddr + c * 32, zu);
       if (cm == -INFINITY) continue;  // every key of the chunk masked
       if (cm > mx) {
         sum = mx == -INFINITY ? 0.0f : sum * expf(mx - cm);
         mx = cm;
       }
 #pragma unroll
-      for (int e = 0; e < 32; e++) sum += expf(z[e] - mx);
+      for (int e = 0; e < 32; e++) sum += expf(__uint_as_float(zu[e]) - mx);
     }
+    tmem_wait_st();
     const float inv = 1.0f / sum;
-    float* pg = a.p + ((size_t)(ts.img * a.h + hd) * a.tq + i) * a.tk;
+    float* p0 = a.p + ((size_t)(ts.img * a.h + hd) * a.tq + i0) * a.tk;
 #pragma unroll 1
     for (int c = 0; c < nch; c++) {
       float z[32];
-      logits32<BN, STACK>(taddr, c, t, brow, z);
+      tmem_ld32(taddr + c * 32, z);
 #pragma unroll
-      for (int e = 0; e < 32; e += 4)
-        *reinterpret_cast<float4*>(pg + c * 32 + e) =
-            make_float4(expf(z[e] - mx) * inv, expf(z[e + 1] - mx) * inv, expf(z[e + 2] - mx) * inv,
-                        expf(z[e + 3] - mx) * inv);
+      for (int e = 0; e < 32; e++) z[e] = expf(z[e] - mx) * inv;
+      stage_store(p0, a.tk, c * 32, buf, lane, z);
     }
   }
 };
