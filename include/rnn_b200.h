@@ -338,6 +338,25 @@ int rnn_clip(rnn_ctx *ctx, float *g, size_t n, float max, float *norm_out);  /* 
 int rnn_ema_update(rnn_ctx *ctx, float *e, const float *v, size_t n,
                    float decay, int t);                                      /* optim.rs:270-287 */
 
+/* No reference counterpart (the reference is one process): the SyncBN
+ * exchange of the data-parallel step on its own.  Per-channel forward sums
+ * (sum y, sum y^2; f64, [c][2]) of this rank's y [n,c,hw] (nn.rs:301-322),
+ * published in this rank's mailbox and summed with every peer's in rank order:
+ * mailboxes is a device array of `world` device pointers (peers' mapped
+ * through CUDA IPC by the caller), each mailbox rnn_peer_mailbox_bytes(cmax)
+ * bytes, zeroed before first use: a u64 flag at offset 0, then two slots of
+ * [cmax][2] doubles from offset 128.  seq is this rank's device u64 exchange
+ * counter (starts at 0).  A peer that does not publish within wait_ms sets the
+ * device error word (rnn_ctx_synchronize -> RNN_ERR_DEVICE) and the call
+ * returns with that peer's stale slot in the sums instead of hanging.
+ * hw % 4 == 0; y 16-byte aligned. */
+int rnn_batchnorm_stats_peer_dev(rnn_ctx *ctx, const float *y, int n, int c,
+                                 int hw, int rank, int world,
+                                 void *const *mailboxes,
+                                 unsigned long long *seq, int cmax, int wait_ms,
+                                 double *sums);
+size_t rnn_peer_mailbox_bytes(int cmax);
+
 /* ---- ResNet training step (model.rs, train.rs:684-699) ------------------ */
 /* ResNet::new(depth_n, width, nclass, seed) (model.rs:112-133), with the
  * reference's initialisation drawn from the same xoshiro256++ stream, so

@@ -68,6 +68,8 @@ extern "C" {
     pub fn rnn_batchnorm_fwd_dev(ctx: *mut RnnCtx, y: *const f32, n: c_int, c: c_int, hw: c_int, gamma: *const f32, beta: *const f32, rmean: *mut f32, rvar: *mut f32, mom: f32, eps: f32, relu: c_int, mean: *mut f32, invstd: *mut f32, out: *mut f32) -> c_int;
     pub fn rnn_batchnorm_eval_dev(ctx: *mut RnnCtx, y: *const f32, n: c_int, c: c_int, hw: c_int, gamma: *const f32, beta: *const f32, rmean: *const f32, rvar: *const f32, eps: f32, relu: c_int, out: *mut f32) -> c_int;
     pub fn rnn_batchnorm_bwd_dev(ctx: *mut RnnCtx, dy: *const f32, y: *const f32, n: c_int, c: c_int, hw: c_int, gamma: *const f32, mean: *const f32, invstd: *const f32, relu_out: *const f32, dx: *mut f32, dgamma: *mut f32, dbeta: *mut f32) -> c_int;
+    pub fn rnn_batchnorm_stats_peer_dev(ctx: *mut RnnCtx, y: *const f32, n: c_int, c: c_int, hw: c_int, rank: c_int, world: c_int, mailboxes: *const *mut c_void, seq: *mut u64, cmax: c_int, wait_ms: c_int, sums: *mut f64) -> c_int;
+    pub fn rnn_peer_mailbox_bytes(cmax: c_int) -> usize;
     pub fn rnn_relu_back_dev(ctx: *mut RnnCtx, d: *mut f32, y: *const f32, len: usize) -> c_int;
     pub fn rnn_add_dev(ctx: *mut RnnCtx, a: *mut f32, b: *const f32, len: usize) -> c_int;
     pub fn rnn_add_relu_dev(ctx: *mut RnnCtx, a: *mut f32, b: *const f32, len: usize) -> c_int;

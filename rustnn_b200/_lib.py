@@ -59,6 +59,8 @@ SIGS = {
     "rnn_layernorm_res_fwd_dev": [CTX, FP, FP, FP, I, I, FP, FP, F, FP, FP, FP, FP, FP],
     "rnn_linear_fwd_packed_dev": [CTX, FP, I, I, I, FP, FP, FP],
     "rnn_swiglu_fwd_dev": [CTX, FP, FP, I, I, I, FP, FP, FP, FP],
+    "rnn_batchnorm_stats_peer_dev": [CTX, FP, I, I, I, I, I, P, P, I, I, P],
+    "rnn_peer_mailbox_bytes": [I],
     "rnn_alloc": [CTX, Z, P],
     "rnn_free": [CTX, P],
     "rnn_memcpy_h2d": [CTX, P, P, Z],
@@ -182,7 +184,12 @@ SIGS = {
     "rnn_rustvit_eval_dev": [VIT, FP, FP, I, I, I, I, FP, FP],
     "rnn_rustvit_eval": [VIT, FP, FP, I, I, I, I, FP, FP],
 }
-_RESTYPE = {"rnn_ctx_stream": P, "rnn_launch_count": C.c_ulonglong, "rnn_ckpt_config_hash": C.c_uint64}
+_RESTYPE = {
+    "rnn_ctx_stream": P,
+    "rnn_launch_count": C.c_ulonglong,
+    "rnn_ckpt_config_hash": C.c_uint64,
+    "rnn_peer_mailbox_bytes": C.c_size_t,
+}
 
 
 class RnnError(RuntimeError):

@@ -21,6 +21,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=default",
+         "-Xcompiler", "-ffp-contract=off",
          "--expt-relaxed-constexpr", "-I" + os.path.join(ROOT, "include")]
 
 

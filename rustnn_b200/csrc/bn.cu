@@ -841,3 +841,33 @@ extern "C" int rnn_batchnorm_bwd_dev(rnn_ctx* ctx, const float* dy, const float*
   return bn_bwd_finish(ctx, dy, y, relu_out, n, c, hw, (double)n * hw, sums, gamma, mean, invstd, dgb, dx,
                        dgamma, dbeta, 1.0f);
 }
+
+// The SyncBN exchange on its own (the data-parallel ResNet step runs it inside
+// its statistics kernels): per-channel forward sums of this rank's y, summed
+// with every peer's through the mailboxes in rank order.  For callers that
+// map their peers' device memory themselves (CUDA IPC) and for tests of the
+// exchange on one device.
+extern "C" int rnn_batchnorm_stats_peer_dev(rnn_ctx* ctx, const float* y, int n, int c, int hw, int rank, int world,
+                                            void* const* mailboxes, unsigned long long* seq, int cmax, int wait_ms,
+                                            double* sums) {
+  RNN_REQUIRE(ctx && y && mailboxes && seq && sums, "batchnorm_stats_peer: null argument");
+  RNN_REQUIRE(n > 0 && c > 0 && hw > 0 && world >= 1 && rank >= 0 && rank < world && c <= cmax && wait_ms > 0,
+              "batchnorm_stats_peer: bad arguments (n %d c %d hw %d rank %d world %d cmax %d wait %d ms)", n, c, hw,
+              rank, world, cmax, wait_ms);
+  RNN_REQUIRE(vec4_ok(hw, (size_t)n * c * hw, {y}), "batchnorm_stats_peer: hw %% 4 == 0 and a 16-byte aligned y");
+  RNN_RANGE(mailboxes, sizeof(void*) * world);
+  RNN_RANGE(seq, sizeof(unsigned long long));
+  const int P = bn_parts(n, c, ctx->num_sms);
+  RNN_TRY(ensure_ws(ctx, sizeof(double) * (size_t)c * P * 2));
+  PeerSums ps;
+  ps.rank = rank;
+  ps.world = world;
+  ps.cmax = cmax;
+  ps.mail = reinterpret_cast<char* const*>(mailboxes);
+  ps.seq = seq;
+  ps.dev_error = ctx->dev_error;
+  ps.wait_ns = (unsigned long long)wait_ms * 1000000ull;
+  return bn_fwd_sums(ctx, y, n, c, hw, static_cast<double*>(ctx->ws), sums, &ps, nullptr);
+}
+
+extern "C" size_t rnn_peer_mailbox_bytes(int cmax) { return rnn::peer_mail_bytes(cmax); }

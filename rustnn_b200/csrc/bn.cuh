@@ -24,6 +24,7 @@ struct PeerSums {
   char* const* mail = nullptr;        // device array [world]: mailbox base of every rank (own included)
   unsigned long long* seq = nullptr;  // this rank's exchange counter (device)
   int* dev_error = nullptr;
+  unsigned long long wait_ns = 5000000000ull;  // bound of the wait for a peer's flag
 };
 constexpr size_t PEER_MAIL_HEADER = 128;
 inline size_t peer_mail_bytes(int cmax) { return PEER_MAIL_HEADER + 2 * (size_t)cmax * 2 * sizeof(double); }
@@ -45,8 +46,9 @@ __device__ __forceinline__ unsigned long long gtimer() {
 
 // Cross-rank step of the last CTA (all its threads; `sums` holds this
 // rank's totals): publish them in slot seq&1 of the own mailbox, raise the
-// flag to seq, wait for every peer's flag (bounded: 5 s, then an error bit
-// and garbage instead of a hang), and sum every rank's slot in rank order.
+// flag to seq, wait for every peer's flag (bounded: wait_ns, 5 s in the
+// training step, then an error bit and garbage instead of a hang), and sum
+// every rank's slot in rank order.
 // Two slots suffice: a rank can only publish seq+2 after passing the wait
 // for seq+1, which needs this rank's flag, raised after it read seq.
 __device__ inline void peer_exchange(const PeerSums& ps, double* sums, int C) {
@@ -65,7 +67,7 @@ __device__ inline void peer_exchange(const PeerSums& ps, double* sums, int C) {
     const unsigned long long* flag = reinterpret_cast<const unsigned long long*>(ps.mail[threadIdx.x]);
     const unsigned long long t0 = gtimer();
     while (ld_acquire_sys(flag) < seq) {
-      if (gtimer() - t0 > 5000000000ull) {
+      if (gtimer() - t0 > ps.wait_ns) {
         if (ps.dev_error) atomicOr(ps.dev_error, DEV_ERR_PEER);
         break;
       }

@@ -8,14 +8,30 @@
 // 0x9E3779B97F4A7C15), data.rs:400) and draws every random value the
 // reference draws, in its order; the ops then run over the CTA.  The f32
 // arithmetic uses the round-to-nearest intrinsics operation by operation, as
-// the reference's unfused expressions round.  The reference's logf / cosf /
-// sinf are evaluated in double and rounded to f32.
+// the reference's unfused expressions round.
+//
+// The reference's f32 logf / cosf / sinf are the C library's, and those are
+// not correctly rounded for every argument, so the device takes their results
+// from the C library itself instead of evaluating its own:
+//   * Rng::normal (rng.rs:55-59) is sqrt(-2 ln u1) * cos(TAU u2) with u1, u2
+//     24-bit uniforms k * 2^-24, so ln u1 and cos(TAU u2) each take at most
+//     2^24 values.  Two 64-MB tables, ln_tab[k] = logf(max(k 2^-24, 1e-7)) and
+//     cos_tab[k] = cosf(TAU * k 2^-24) (the f32 product), are computed once
+//     per process and device with the host's logf / cosf and indexed by the
+//     drawn integers.  The sqrt and the products are IEEE-rounded.
+//   * The rotation's cos t / sin t (data.rs:264-266) take an arbitrary f32 t:
+//     the host replays each image's RandAugment draws (a handful of
+//     generator steps per image; the normals with the same C library calls)
+//     and passes cosf(t), sinf(t) of every rotation to the kernel.
+// Both are therefore bit-exact against the reference's libm on this host.
 //
 // mix_batch draws its permutation and lambda on the host from the caller's
 // generator state (a handful of draws per batch) and mixes on the device.
 #include <math.h>
 
 #include <algorithm>
+#include <mutex>
+#include <thread>
 #include <vector>
 
 #include "common.cuh"
@@ -43,14 +59,24 @@ __device__ __forceinline__ float std_of(int c) { return c == 0 ? 0.2673f : (c ==
 // `v.clamp(0.0, 255.0) as u8`
 __device__ __forceinline__ uint8_t clamp_u8(float v) { return (uint8_t)fminf(fmaxf(v, 0.0f), 255.0f); }
 
-// Rng::normal (rng.rs:55-59): sqrt(-2 ln u1) * cos(TAU u2), each step in f32
-__device__ float normal_dev(Rng& r) {
-  float u1 = r.uniform();
-  u1 = fmaxf(u1, 1e-7f);
-  const float u2 = r.uniform();
-  const float l = (float)log((double)u1);
-  const float c = (float)cos((double)__fmul_rn(6.28318530717958647692f, u2));
-  return __fmul_rn(__fsqrt_rn(__fmul_rn(-2.0f, l)), c);
+constexpr int NORMAL_TAB = 1 << 24;  // one entry per 24-bit uniform
+constexpr float TAU = 6.28318530717958647692f;
+
+struct NormalTabs {
+  const float* ln;  // [2^24] logf(max(k 2^-24, 1e-7))
+  const float* cs;  // [2^24] cosf(TAU * k 2^-24)
+};
+
+// Rng::normal (rng.rs:55-59) from the two drawn 24-bit integers:
+// sqrt(-2 ln u1) * cos(TAU u2), each step in f32
+__device__ __forceinline__ float normal_of(const NormalTabs& t, uint32_t k1, uint32_t k2) {
+  return __fmul_rn(__fsqrt_rn(__fmul_rn(-2.0f, __ldg(t.ln + k1))), __ldg(t.cs + k2));
+}
+
+__device__ __forceinline__ float normal_dev(Rng& r, const NormalTabs& t) {
+  const uint32_t k1 = (uint32_t)(r.next_u64() >> 40);
+  const uint32_t k2 = (uint32_t)(r.next_u64() >> 40);
+  return normal_of(t, k1, k2);
 }
 
 // data.rs:105-111
@@ -76,6 +102,7 @@ struct Draws {
   int op[MAX_RA];
   float v[MAX_RA];
   float sign[MAX_RA];
+  float ct[MAX_RA], st[MAX_RA];  // cos t, sin t of a rotation (from the host)
   int dy, dx, flip;
   int erase, y0, y1, x0, x1;
   int nnoise;
@@ -83,13 +110,14 @@ struct Draws {
 
 __global__ void __launch_bounds__(THREADS) make_batch_train_kernel(
     const uint8_t* __restrict__ images, const uint8_t* __restrict__ labels, const uint8_t* __restrict__ coarse,
-    size_t len, const uint32_t* __restrict__ idx, Aug aug, uint64_t seed, float* __restrict__ out,
-    uint32_t* __restrict__ labels_out, uint32_t* __restrict__ coarse_out, int* __restrict__ dev_error) {
+    size_t len, const uint32_t* __restrict__ idx, Aug aug, uint64_t seed, NormalTabs tabs,
+    const float2* __restrict__ rot, float* __restrict__ out, uint32_t* __restrict__ labels_out,
+    uint32_t* __restrict__ coarse_out, int* __restrict__ dev_error) {
   __shared__ uint8_t work[PIX], src[PIX], tmp[PIX];
   __shared__ uint32_t red[3][256];
   __shared__ uint32_t eq_lo[3];
   __shared__ Draws d;
-  extern __shared__ float noise[];  // [2][nnoise_cap]: u1 then u2 of each normal
+  extern __shared__ uint32_t noise[];  // [2][nnoise_cap]: the 24-bit u1 then u2 of each normal
   const int tid = threadIdx.x;
   const int b = blockIdx.x;
   const size_t img = idx[b];
@@ -111,9 +139,12 @@ __global__ void __launch_bounds__(THREADS) make_batch_train_kernel(
     const int nra = aug.ra_mag > 0.0f ? aug.ra_n : 0;
     for (int i = 0; i < nra; i++) {
       d.op[i] = (int)(rng.next_u64() % NOPS);
-      const float n = normal_dev(rng);
+      const float n = normal_dev(rng, tabs);
       d.v[i] = fminf(fmaxf(__fmul_rn(aug.ra_mag, __fadd_rn(1.0f, __fmul_rn(0.5f, n))), 0.0f), 1.0f);
       d.sign[i] = ((rng.next_u64() >> 32) & 1u) ? 1.0f : -1.0f;
+      const float2 cs = rot[(size_t)b * MAX_RA + i];
+      d.ct[i] = cs.x;
+      d.st[i] = cs.y;
     }
     // crop_offset (data.rs:309-318), flip (data.rs:407)
     d.dy = d.dx = 0;
@@ -138,9 +169,8 @@ __global__ void __launch_bounds__(THREADS) make_batch_train_kernel(
       d.erase = cnt > 0;
       d.nnoise = cnt;
       for (int k = 0; k < cnt; k++) {
-        float u1 = rng.uniform();
-        noise[k] = fmaxf(u1, 1e-7f);
-        noise[cnt + k] = rng.uniform();
+        noise[k] = (uint32_t)(rng.next_u64() >> 40);
+        noise[cnt + k] = (uint32_t)(rng.next_u64() >> 40);
       }
     }
   }
@@ -159,14 +189,11 @@ __global__ void __launch_bounds__(THREADS) make_batch_train_kernel(
       if (op == 1) c_ = __fmul_rn(__fmul_rn(sign, 0.3f), v);
       if (op == 2) tx = __fmul_rn(__fmul_rn(sign, 10.0f), v);
       if (op == 3) ty = __fmul_rn(__fmul_rn(sign, 10.0f), v);
-      if (op == 4) {
-        const float t =
-            __fdiv_rn(__fmul_rn(__fmul_rn(__fmul_rn(sign, 30.0f), v), 3.14159265358979323846f), 180.0f);
-        const float ct = (float)cos((double)t), st = (float)sin((double)t);
-        a = ct;
-        bb = -st;
-        c_ = st;
-        dd = ct;
+      if (op == 4) {  // t = sign 30 v pi / 180; cos t and sin t from the host
+        a = d.ct[r];
+        bb = -d.st[r];
+        c_ = d.st[r];
+        dd = d.ct[r];
       }
       for (int i = tid; i < PIX; i += THREADS) src[i] = work[i];
       __syncthreads();
@@ -279,9 +306,7 @@ __global__ void __launch_bounds__(THREADS) make_batch_train_kernel(
     float val;
     if (d.erase && y >= d.y0 && y < d.y1 && x >= d.x0 && x < d.x1) {
       const int k = (c * ny + (y - d.y0)) * nx + (x - d.x0);
-      const float l = (float)log((double)noise[k]);
-      const float cs = (float)cos((double)__fmul_rn(6.28318530717958647692f, noise[d.nnoise + k]));
-      val = __fmul_rn(__fsqrt_rn(__fmul_rn(-2.0f, l)), cs);
+      val = normal_of(tabs, noise[k], noise[d.nnoise + k]);
     } else {
       const int sy = y + d.dy;
       const int sx = (d.flip ? IMG - 1 - x : x) + d.dx;
@@ -334,6 +359,49 @@ float beta_like(float a, Rng& rng) {
   return 1.0f - powf(2.0f * (1.0f - u), 1.0f / a) * 0.5f;
 }
 
+// The Box-Muller tables of one device, computed on first use with the C
+// library's logf / cosf (the functions the reference calls) over every 24-bit
+// uniform, and kept until exit.
+std::mutex g_tab_mu;
+NormalTabs g_tabs[64];
+
+int normal_tables(int device, NormalTabs* out) {
+  RNN_REQUIRE(device >= 0 && device < 64, "make_batch_train: device ordinal %d >= 64", device);
+  std::lock_guard<std::mutex> lock(g_tab_mu);
+  if (!g_tabs[device].ln) {
+    std::vector<float> host(2 * (size_t)NORMAL_TAB);
+    const unsigned nth = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+    std::vector<std::thread> pool;
+    for (unsigned t = 0; t < nth; t++)
+      pool.emplace_back([&host, t, nth] {
+        const size_t lo = (size_t)NORMAL_TAB * t / nth, hi = (size_t)NORMAL_TAB * (t + 1) / nth;
+        for (size_t k = lo; k < hi; k++) {
+          const float u = (float)k * (1.0f / (float)NORMAL_TAB);  // Rng::uniform, exact
+          const float u1 = u < 1e-7f ? 1e-7f : u;
+          const float arg = TAU * u;  // one f32 rounding, as the reference's product
+          host[k] = logf(u1);
+          host[NORMAL_TAB + k] = cosf(arg);
+        }
+      });
+    for (auto& th : pool) th.join();
+    int prev = 0;
+    RNN_CUDA(cudaGetDevice(&prev));
+    RNN_CUDA(cudaSetDevice(device));
+    float* dev = nullptr;
+    cudaError_t e = cudaMalloc(&dev, sizeof(float) * host.size());
+    if (e == cudaSuccess) {
+      e = cudaMemcpy(dev, host.data(), sizeof(float) * host.size(), cudaMemcpyHostToDevice);
+      if (e != cudaSuccess) cudaFree(dev);
+    }
+    cudaSetDevice(prev);
+    RNN_CUDA(e);
+    g_tabs[device].ln = dev;
+    g_tabs[device].cs = dev + NORMAL_TAB;
+  }
+  *out = g_tabs[device];
+  return RNN_OK;
+}
+
 }  // namespace
 
 int make_batch_train(rnn_ctx* ctx, const uint8_t* images, const uint8_t* labels, const uint8_t* coarse,
@@ -351,10 +419,45 @@ int make_batch_train(rnn_ctx* ctx, const uint8_t* images, const uint8_t* labels,
   RNN_RANGE(labels_out, sizeof(uint32_t) * (size_t)bs);
   if (coarse_out) RNN_RANGE(coarse_out, sizeof(uint32_t) * (size_t)bs);
   const int span = erase > 0.0f ? std::min(2 * (erase_side / 2), IMG) : 0;
-  const size_t smem = sizeof(float) * 2 * 3 * (size_t)span * span;
+  const size_t smem = sizeof(uint32_t) * 2 * 3 * (size_t)span * span;
   Aug aug{pad, ra_mag, ra_n, erase, erase_side};
-  make_batch_train_kernel<<<bs, THREADS, smem, ctx->stream>>>(images, labels, coarse, len, idx, aug, seed, out,
-                                                              labels_out, coarse_out, ctx->dev_error);
+  const int nra = ra_mag > 0.0f ? ra_n : 0;
+  NormalTabs tabs{nullptr, nullptr};
+  if (nra > 0 || erase > 0.0f) RNN_TRY(normal_tables(ctx->device, &tabs));
+  // cos t / sin t of every rotation: replay each image's RandAugment draws
+  // (data.rs:297-306, 262-266) with the host's C library, in the order the
+  // kernel draws them
+  std::vector<float2> rot((size_t)bs * MAX_RA, make_float2(1.0f, 0.0f));
+  bool any_rot = false;
+  for (int b = 0; b < bs && nra > 0; b++) {
+    Rng rng(seed ^ ((uint64_t)b * GOLDEN));
+    for (int i = 0; i < nra; i++) {
+      const int op = (int)(rng.next_u64() % NOPS);
+      const float n = rng.normal();
+      float v = ra_mag * (1.0f + 0.5f * n);
+      v = std::min(std::max(v, 0.0f), 1.0f);
+      const float sign = ((rng.next_u64() >> 32) & 1u) ? 1.0f : -1.0f;
+      if (op == 4) {
+        const float t = sign * 30.0f * v * 3.14159265358979323846f / 180.0f;
+        rot[(size_t)b * MAX_RA + i] = make_float2(cosf(t), sinf(t));
+        any_rot = true;
+      }
+    }
+  }
+  const float2* drot = nullptr;
+  if (any_rot) {
+    RNN_TRY(ensure_ws(ctx, sizeof(float2) * rot.size()));
+    RNN_CUDA(cudaMemcpyAsync(ctx->ws, rot.data(), sizeof(float2) * rot.size(), cudaMemcpyHostToDevice,
+                             ctx->stream));
+    drot = static_cast<const float2*>(ctx->ws);
+  } else if (nra > 0) {
+    // no image rotates: the kernel still reads its (unused) slots
+    RNN_TRY(ensure_ws(ctx, sizeof(float2) * rot.size()));
+    RNN_CUDA(cudaMemsetAsync(ctx->ws, 0, sizeof(float2) * rot.size(), ctx->stream));
+    drot = static_cast<const float2*>(ctx->ws);
+  }
+  make_batch_train_kernel<<<bs, THREADS, smem, ctx->stream>>>(images, labels, coarse, len, idx, aug, seed, tabs,
+                                                              drot, out, labels_out, coarse_out, ctx->dev_error);
   RNN_CHECK_LAUNCH();
   return RNN_OK;
 }

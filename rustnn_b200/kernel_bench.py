@@ -10,6 +10,9 @@
                                                        # --profile-from-start off lists exactly its launches)
     python -m rustnn_b200.kernel_bench resnetstep --batch 128   # one ResNet-56 W=64 graph step, same way
 
+--graph times a CUDA-graph replay of the calls instead of back-to-back
+Python calls (device time without the host's per-call cost).
+
 Prints one line per kernel: time per launch, algorithmic TFLOP/s (2*M*N*K),
 and the minimum HBM bytes / achieved GB/s.  Also the target of the ncu
 captures summarised under profiles/.
@@ -24,7 +27,33 @@ import torch
 from . import ops
 
 
+GRAPH = False  # set by --graph
+
+
 def _time(fn, reps):
+    """Seconds per call of fn.  Back-to-back calls from Python by default
+    (what a caller of the Python API sees: small calls are bounded by the
+    host); with --graph the reps calls are captured once into a CUDA graph
+    and the replay is timed (device time, no host launch cost)."""
+    if GRAPH:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()  # binds the context to s, sizes workspaces, sets attributes
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(reps):
+                fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            g.replay()
+            e0.record(s)
+            g.replay()
+            e1.record(s)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps / 1e3
     fn()
     torch.cuda.synchronize()
     s = torch.cuda.current_stream()
@@ -254,7 +283,10 @@ def main():
     ap.add_argument("--which", default="fwd,dgrad,wgrad")
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--dh", type=int, default=32, help="attention head dim (32: BASELINE config 3; 64: rustvit)")
+    ap.add_argument("--graph", action="store_true", help="time a CUDA-graph replay of the calls (device time)")
     args = ap.parse_args()
+    global GRAPH
+    GRAPH = args.graph
     rows = {"conv": conv, "gemm": gemm, "attn": attn, "ln": ln, "muon": muon, "vitstep": vitstep,
             "resnetstep": resnetstep}[args.what](args)
     for r in rows:

@@ -2,11 +2,11 @@
 (oracle/rnn_oracle_data.c): make_batch_train (data.rs:384-412) and mix_batch
 (data.rs:467-491), bit for bit.
 
-The device evaluates the reference's f32 logf / cosf / sinf (erase noise,
-RandAugment magnitudes, rotations) correctly rounded; the oracle runs in the
-same convention here (oracle.cr_math).  How far the C library's
-single-precision functions, which the reference calls, move a batch is
-measured on the CPU in tests/test_oracle_data.py."""
+The oracle runs in its default mode: the C library's f32 logf / cosf / sinf,
+the functions the reference calls (erase noise, RandAugment magnitudes,
+rotations).  The device takes the same functions' results (Box-Muller
+tables over every 24-bit uniform; the rotations' cos / sin from a host
+replay of the draws), so the bytes agree with no correctly-rounded mode."""
 import numpy as np
 import pytest
 
@@ -31,9 +31,8 @@ def both(seed, n, bs, aug):
     images, labels, coarse = dataset(seed, n)
     idx = np.random.default_rng(seed + 1).permutation(n)[:bs].astype(np.uint32)
     s = seed * 1_000_003 + 7
-    with O.cr_math():
-        want, wl, wc = O.make_batch_train(images, labels, coarse, idx, aug.pad, aug.ra_mag, aug.ra_n, aug.erase,
-                                          aug.erase_side, s)
+    want, wl, wc = O.make_batch_train(images, labels, coarse, idx, aug.pad, aug.ra_mag, aug.ra_n, aug.erase,
+                                      aug.erase_side, s)
     dv = lambda a: torch.from_numpy(a).cuda()
     got, gl, gc = data.make_batch_train(dv(images), dv(labels), dv(coarse), dv(idx.view(np.int32)), aug, s)
     torch.cuda.synchronize()
@@ -104,3 +103,24 @@ def test_batch_train_index_outside_dataset():
     got, gl, _ = data.make_batch_train(dv(images), dv(labels), None, dv(ok.view(np.int32)), data.Aug(), 5)
     default_context().synchronize()
     assert np.array_equal(gl.cpu().numpy().view(np.uint32), labels[ok].astype(np.uint32))
+
+
+def test_batch_train_follows_the_c_library_not_correct_rounding():
+    """A batch whose bytes and noise differ between the C library's f32
+    logf / cosf / sinf and correctly-rounded ones (checked on the oracle):
+    the device reproduces the C library's."""
+    from rustnn_b200 import data
+    from rustnn_b200.data import Aug
+
+    aug = Aug(pad=4, ra_mag=1.0, ra_n=4, erase=1.0, erase_side=16)
+    images, labels, coarse = dataset(11, 256)
+    idx = np.arange(256, dtype=np.uint32)
+    args = (images, labels, coarse, idx, aug.pad, aug.ra_mag, aug.ra_n, aug.erase, aug.erase_side, 1234)
+    want = O.make_batch_train(*args)[0]
+    with O.cr_math():
+        cr = O.make_batch_train(*args)[0]
+    assert not np.array_equal(want, cr)
+    dv = lambda a: torch.from_numpy(a).cuda()
+    got = data.make_batch_train(dv(images), dv(labels), dv(coarse), dv(idx.view(np.int32)), aug, 1234)[0]
+    torch.cuda.synchronize()
+    assert np.array_equal(got.cpu().numpy(), want)
