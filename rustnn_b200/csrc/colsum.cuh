@@ -5,16 +5,19 @@
 //
 // The float4 path (c % 4 == 0, 16-byte aligned operands) gives each warp a
 // 128-column strip and a CTA 8 warps over one slab, so a warp reads 512
-// contiguous bytes per row and eight rows are in flight per lane; the
-// partials of the 8 warps are combined in shared memory.  Other shapes take
-// the scalar kernels (one thread per column).
+// contiguous bytes per row and sixteen rows are in flight per lane; the
+// partials of the 8 warps are combined in shared memory.  The final pass
+// runs 32 warps per 128-column strip (few CTAs: its grid is the column
+// strips only), each summing every 32nd partial, then combines the warps in
+// shared memory.  Other shapes take the scalar kernels (one thread per
+// column).
 #pragma once
 
 #include "common.cuh"
 
 namespace rnn {
 
-constexpr int CS_ROWS = 64;  // rows per partial (the callers size `part` as ceil(rows / CS_ROWS) x c)
+constexpr int CS_ROWS = 128;  // rows per partial (the callers size `part` as ceil(rows / CS_ROWS) x c)
 
 // the kernels have internal linkage: each translation unit that includes
 // this header gets its own copy
@@ -62,22 +65,24 @@ __global__ void __launch_bounds__(256) cs_partial4_kernel(const float4* __restri
   }
 }
 
-__global__ void __launch_bounds__(256) cs_final4_kernel(const float4* __restrict__ part, int nb, int c4,
-                                                         float4* __restrict__ out) {
-  __shared__ float4 red[8][32];
+constexpr int CS_FINAL_WARPS = 32;
+
+__global__ void __launch_bounds__(CS_FINAL_WARPS * 32) cs_final4_kernel(const float4* __restrict__ part, int nb,
+                                                                         int c4, float4* __restrict__ out) {
+  __shared__ float4 red[CS_FINAL_WARPS][32];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int j = blockIdx.x * 32 + lane;
   float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   if (j < c4) {
-#pragma unroll 8
-    for (int b = w; b < nb; b += 8) cs_add4(s, __ldg(part + (size_t)b * c4 + j));
+#pragma unroll 4
+    for (int b = w; b < nb; b += CS_FINAL_WARPS) cs_add4(s, __ldg(part + (size_t)b * c4 + j));
   }
   red[w][lane] = s;
   __syncthreads();
   if (w == 0 && j < c4) {
     float4 t = red[0][lane];
 #pragma unroll
-    for (int k = 1; k < 8; k++) cs_add4(t, red[k][lane]);
+    for (int k = 1; k < CS_FINAL_WARPS; k++) cs_add4(t, red[k][lane]);
     float4 o = out[j];
     cs_add4(o, t);
     out[j] = o;
@@ -112,8 +117,8 @@ inline bool cs_aligned(const void* p) { return ((uintptr_t)p & 15) == 0; }
 inline int colsum_final(rnn_ctx* ctx, const float* part, int nb, int c, float* out) {
   if (c % 4 == 0 && cs_aligned(part) && cs_aligned(out)) {
     const int c4 = c / 4;
-    cs_final4_kernel<<<(c4 + 31) / 32, 256, 0, ctx->stream>>>(reinterpret_cast<const float4*>(part), nb, c4,
-                                                              reinterpret_cast<float4*>(out));
+    cs_final4_kernel<<<(c4 + 31) / 32, CS_FINAL_WARPS * 32, 0, ctx->stream>>>(
+        reinterpret_cast<const float4*>(part), nb, c4, reinterpret_cast<float4*>(out));
   } else {
     cs_final_kernel<<<(c + 255) / 256, 256, 0, ctx->stream>>>(part, nb, c, out);
   }

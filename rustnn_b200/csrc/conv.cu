@@ -11,12 +11,49 @@
 // layout [cout][cin][kh][kw] of nn.rs:116.  dgrad handles stride 2 by
 // testing divisibility of (i + pad - kh) by the stride (the transposed
 // convolution of scatter_span, conv.rs:124-165).
+#include <cuda.h>
+
 #include "bn.cuh"
 #include "ew.cuh"
 #include "tc_launch.cuh"
 
 namespace rnn {
 namespace tc {
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (the
+// library does not link libcuda directly).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled_fn() {
+  static const EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<EncodeTiledFn>(p);
+    return static_cast<EncodeTiledFn>(nullptr);
+  }();
+  return fn;
+}
+
+// Tensor map of an NCHW f32 tensor [n][c][h][w] read in boxes of
+// box_w x box_h x box_c pixels of one image (zero fill outside).
+static int encode_nchw_map(CUtensorMap* m, const float* t, int n, int c, int h, int w, int box_w, int box_h,
+                           int box_c) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  RNN_REQUIRE(fn != nullptr, "conv: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[4] = {(cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)c, (cuuint64_t)n};
+  const cuuint64_t strides[3] = {(cuuint64_t)w * 4, (cuuint64_t)h * w * 4, (cuuint64_t)c * h * w * 4};
+  const cuuint32_t box[4] = {(cuuint32_t)box_w, (cuuint32_t)box_h, (cuuint32_t)box_c, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(t), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  RNN_REQUIRE(r == CUDA_SUCCESS, "conv: cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+  return RNN_OK;
+}
 
 struct ConvGeom {
   int n, cin, h, w, cout, stride, pad, oh, ow;
@@ -537,6 +574,12 @@ struct HaloConv3x3 {
   static constexpr int CSTR = PAIRS ? ((HR + 1) / 2) * 2 * HX : HR * HX;  // floats per channel
   static constexpr int HALO_FLOATS = 32 * CSTR;
   static constexpr int HALO_BYTES = 2 * HALO_FLOATS * 4;
+  // 32-wide images: a halo buffer is the dense box [32 channels][HR rows][HX
+  // columns] of the source, filled by one tensor copy (columns -4 .. W+3 and
+  // the rows above and below the image come back as zeros).  16-wide images
+  // store rows in interleaved pairs, which a box copy cannot produce: they
+  // keep the per-thread cp.async.
+  static constexpr bool HALO_TMA = !PAIRS;
   // the producers write the split A tile into tensor memory (tcgen05.st):
   // shared memory then carries only the halo and the B images
   static constexpr bool A_TMEM = HALO_A_TMEM;
@@ -546,6 +589,7 @@ struct HaloConv3x3 {
     if constexpr (PAIRS) return (r >> 1) * (2 * HX) + (x >> 2) * 8 + (r & 1) * 4 + (x & 3);
     return r * HX + x;
   }
+  CUtensorMap tmap;  // src as [n][CS][H][W], boxes of [32][HR][HX] (HALO_TMA)
   const float* src;  // [n][CS][H][W]
   float* out;        // [n][N][H][W]
   const float* bpack;
@@ -575,6 +619,14 @@ struct HaloConv3x3 {
       const float* g = in ? base + ((size_t)c * H + iy) * W + ix : src;
       cp_async16(dst0 + (uint32_t)((c * CSTR + pos(r, xc * 4)) * 4), g, in ? 16u : 0u);
     }
+  }
+  __device__ __forceinline__ void halo_tma(uint32_t halo, int buf, uint64_t* bar, int mt, int cb) const {
+    const int hw = H * W;
+    const int m0 = mt * BM;
+    const int img = m0 / hw, oy0 = (m0 - img * hw) / W;
+    mbar_arrive_expect_tx(bar, (uint32_t)(HALO_FLOATS * 4));
+    // x starts at column -4: -16 bytes, a multiple of 16
+    tma_load_4d(halo + (uint32_t)(buf * HALO_FLOATS * 4), &tmap, -4, oy0 - 1, cb * 32, img, bar);
   }
   __device__ __forceinline__ void load_a_halo(uint32_t halo, int buf, const TS&, int tap, int gt,
                                               float (&v)[32]) const {
@@ -1084,6 +1136,11 @@ static int halo_conv(rnn_ctx* ctx, const float* src, const float* wt, float* out
   p.src = src; p.out = out;
   p.CS = dgrad ? g.cout : g.cin;
   p.H = g.h;
+  if constexpr (HaloConv3x3<BN, W>::HALO_TMA) {
+    RNN_TRY(encode_nchw_map(&p.tmap, src, g.n, p.CS, g.h, W, HaloConv3x3<BN, W>::HX, HaloConv3x3<BN, W>::HR, 32));
+  } else {
+    memset(&p.tmap, 0, sizeof(p.tmap));
+  }
   p.M = g.n * g.h * g.w;
   p.N = dgrad ? g.cin : g.cout;
   p.kblocks = 9 * (p.CS / 32);

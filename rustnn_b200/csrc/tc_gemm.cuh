@@ -81,6 +81,20 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst_smem, const void* src, uin
       : "memory");
 }
 
+// 4-D tiled tensor copy global -> shared through a tensor map (TMA, no
+// multicast); coordinates innermost first, elements outside the tensor
+// (negative included) are filled with zeros.  The innermost coordinate times
+// the element size must be a multiple of 16 bytes.  `tmap` is the generic
+// address of a __grid_constant__ kernel parameter.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst_smem, const void* tmap, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(dst_smem),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 16-byte asynchronous copy global -> shared through L2 (cp.async.cg, not
 // the bulk/TMA engine); src_bytes = 0 zero-fills the 16 bytes and reads
 // nothing.  Completion: cp_async_wait_all() in the issuing thread.
@@ -442,6 +456,11 @@ struct ChunkProb : P {
 //        cp.async the halo of K-block group cb (TAPS consecutive K blocks)
 //        of row tile m_tile into buffer buf; producer thread ptid of npt
 //   void load_a_halo(uint32_t halo, int buf, const TS&, int tap, int gt, float (&v)[32]) const;
+// A HALO problem may set HALO_TMA: one producer thread then fills a halo
+// buffer with a tensor copy instead of every producer issuing cp.async,
+//   void halo_tma(uint32_t halo, int buf, uint64_t* bar, int m_tile, int cb) const;
+//        arrive.expect_tx on bar and start the copy of buffer buf,
+// and the producers wait on that buffer's barrier before reading it.
 template <class P, class = void>
 struct prob_halo {
   static constexpr int value = 0;
@@ -449,6 +468,14 @@ struct prob_halo {
 template <class P>
 struct prob_halo<P, std::void_t<decltype(P::HALO_BYTES)>> {
   static constexpr int value = P::HALO_BYTES;
+};
+template <class P, class = void>
+struct prob_halo_tma {
+  static constexpr bool value = false;
+};
+template <class P>
+struct prob_halo_tma<P, std::void_t<decltype(P::HALO_TMA)>> {
+  static constexpr bool value = P::HALO_TMA;
 };
 // Problems with STATS = true can have the epilogue sum every output column
 // over the rows (f64, per CTA, in shared memory after the halo) and supply
@@ -562,9 +589,10 @@ __device__ __forceinline__ void warp_colsum2(const float (&v)[32], double& s_out
 
 template <int BN, class Prob>
 __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
-    tc3_gemm_kernel(const Prob prob, const Sched sched, int* dev_error) {
+    tc3_gemm_kernel(const __grid_constant__ Prob prob, const Sched sched, int* dev_error) {
   using C = CfgOf<Prob, BN>;
   constexpr bool HALO = prob_halo<Prob>::value > 0;
+  constexpr bool HTMA = HALO && prob_halo_tma<Prob>::value;
   constexpr bool STATS = prob_stats<Prob>::value;
   constexpr bool ROWEPI = prob_rowepi<Prob>::value;
   static_assert(!C::ATM || Prob::B_BULK, "A in tensor memory needs a bulk-copied B");
@@ -585,7 +613,8 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
   uint64_t* acc_empty = acc_full + 2;         // [2] epilogue -> MMA
   uint64_t* drain = acc_empty + 2;            // [1] abort path
   uint64_t* halo_bar = drain + 1;             // [1] all producers: a halo buffer is filled / released
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(halo_bar + 1);
+  uint64_t* halo_full = halo_bar + 1;         // [2] HALO_TMA: the tensor copy of a halo buffer landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(halo_full + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -603,6 +632,8 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
     }
     mbar_init(drain, 1);
     mbar_init(halo_bar, C::PRODUCER_WARPS * 32);
+    mbar_init(&halo_full[0], 1);
+    mbar_init(&halo_full[1], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -634,10 +665,18 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
     auto mt_of = [&](int tile) { return (tile % tiles_mn) % sched.m_tiles; };
     uint32_t it = 0, hc = 0;
     bool ok = true;
+    // HALO_TMA: sequence numbers of the last halo copy started and the last
+    // one waited for (copy s fills buffer s & 1 for the (s >> 1)-th time)
+    int tma_issued = -1, tma_waited = -1;
     if (blockIdx.x < sched.num_tiles) {
-      prob.halo_issue(halo, 0, mt_of(blockIdx.x), 0, ptid, NPT);
+      if constexpr (HTMA) {
+        if (ptid == 0) prob.halo_tma(halo, 0, &halo_full[0], mt_of(blockIdx.x), 0);
+        tma_issued = 0;
+      } else {
+        prob.halo_issue(halo, 0, mt_of(blockIdx.x), 0, ptid, NPT);
+      }
     }
-    cp_async_commit();
+    if constexpr (!HTMA) cp_async_commit();
     for (int tile = blockIdx.x; tile < sched.num_tiles && ok; tile += gridDim.x) {
       const int mn = tile % tiles_mn;
       const int mt = mn % sched.m_tiles, nt = mn / sched.m_tiles;
@@ -646,15 +685,26 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
       for (int kb = 0; kb < sched.kblocks; kb++, it++) {
         const int cb = kb / TAPS, tap = kb - cb * TAPS;
         if (tap == 0) {
-          cp_async_wait_all();
+          if constexpr (!HTMA) cp_async_wait_all();
+          // every producer is done with the buffer the next copy overwrites
           mbar_arrive(halo_bar);
           if (!mbar_wait(halo_bar, hc & 1, abort_flag, dev_error)) { ok = false; break; }
           int ntile = tile, ncb = cb + 1;
           if (ncb * TAPS >= sched.kblocks) { ntile = tile + gridDim.x; ncb = 0; }
-          if (ntile < sched.num_tiles) {
-            prob.halo_issue(halo, (hc + 1) & 1, mt_of(ntile), ncb, ptid, NPT);
+          if constexpr (HTMA) {
+            if (ntile < sched.num_tiles) {
+              if (ptid == 0) prob.halo_tma(halo, (hc + 1) & 1, &halo_full[(hc + 1) & 1], mt_of(ntile), ncb);
+              tma_issued = (int)hc + 1;
+            }
+            // this group's halo (copy hc) has landed
+            if (!mbar_wait(&halo_full[hc & 1], (hc >> 1) & 1, abort_flag, dev_error)) { ok = false; break; }
+            tma_waited = (int)hc;
+          } else {
+            if (ntile < sched.num_tiles) {
+              prob.halo_issue(halo, (hc + 1) & 1, mt_of(ntile), ncb, ptid, NPT);
+            }
+            cp_async_commit();
           }
-          cp_async_commit();
           hc++;
         }
         if ((int)(it % C::GROUPS) != group) continue;
@@ -703,7 +753,20 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
         mbar_arrive(&full[stage]);
       }
     }
-    cp_async_wait_all();
+    if constexpr (HTMA) {
+      // on an abort, let the copies still in flight (at most two) land
+      // before the CTA exits
+      if (!ok && ptid == 0) {
+        for (int sq = tma_waited + 1; sq <= tma_issued; sq++) {
+          const uint32_t a = smem_u32(&halo_full[sq & 1]);
+          const unsigned long long t0 = globaltimer();
+          while (!mbar_try_wait(a, (sq >> 1) & 1) && globaltimer() - t0 < WAIT_TIMEOUT_NS) {
+          }
+        }
+      }
+    } else {
+      cp_async_wait_all();
+    }
    } else {
     // ---------------------------------------------------------- producers
     const int group = warp >> 2;                 // 0 .. GROUPS-1

@@ -9,6 +9,7 @@
                                                        # alone between cudaProfilerStart/Stop (ncu
                                                        # --profile-from-start off lists exactly its launches)
     python -m rustnn_b200.kernel_bench resnetstep --batch 128   # one ResNet-56 W=64 graph step, same way
+    python -m rustnn_b200.kernel_bench data --batch 1024        # batch builder and mixes per call
 
 --graph times a CUDA-graph replay of the calls instead of back-to-back
 Python calls (device time without the host's per-call cost).
@@ -203,6 +204,34 @@ def muon(args):
              "tflops": round(fl / t / 1e12, 2), "gflop": round(fl / 1e9, 2)}]
 
 
+def databatch(args):
+    """data::make_batch_train (data.rs:384-412) and mix_batch (data.rs:467-491)
+    per batch of args.batch images from a resident 50,000-image u8 split:
+    time per call as a caller sees it (the host's draws included)."""
+    import numpy as np
+
+    from . import data
+
+    n, bs = 50_000, args.batch
+    rng = np.random.default_rng(0)
+    images = torch.from_numpy(rng.integers(0, 256, size=n * 3072, dtype=np.uint8)).cuda()
+    labels = torch.from_numpy(rng.integers(0, 100, size=n, dtype=np.uint8)).cuda()
+    idx = torch.from_numpy(rng.permutation(n)[:bs].astype(np.int32)).cuda()
+    out = torch.empty(bs * 3072, device="cuda")
+    lab = torch.empty(bs, dtype=torch.int32, device="cuda")
+    rows = []
+    for tag, aug in (("resnet aug (pad 4, erase 1.0 side 8)", data.Aug(pad=4, erase=1.0, erase_side=8)),
+                     ("randaugment x2 m0.6, erase 0.25", data.Aug(pad=4, ra_mag=0.6, ra_n=2, erase=0.25))):
+        t = _time(lambda: data.make_batch_train(images, labels, None, idx, aug, 7, out=out, labels_out=lab),
+                  args.reps)
+        rows.append({"kernel": "make_batch_train", "shape": f"batch {bs}, {tag}", "ms": round(t * 1e3, 4)})
+    st = np.array([1, 2, 3, 4], dtype=np.uint64)
+    for tag, m, c in (("mixup 0.8", 0.8, 0.0), ("cutmix 1.0", 0.0, 1.0)):
+        t = _time(lambda: data.mix_batch(out, bs, m, c, 0.5, st), args.reps)
+        rows.append({"kernel": "mix_batch", "shape": f"batch {bs}, {tag}", "ms": round(t * 1e3, 4)})
+    return rows
+
+
 def vitstep(args):
     """Trainer::step of the default rustvit (train.rs:346-387) at batch
     args.batch, synthetic data; the timed step runs alone inside the
@@ -273,7 +302,7 @@ def resnetstep(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["conv", "gemm", "attn", "ln", "muon", "vitstep", "resnetstep"])
+    ap.add_argument("what", choices=["conv", "gemm", "attn", "ln", "muon", "vitstep", "resnetstep", "data"])
     ap.add_argument("--cin", type=int, default=64)
     ap.add_argument("--cout", type=int, default=64)
     ap.add_argument("--hw", type=int, default=32)
@@ -288,7 +317,7 @@ def main():
     global GRAPH
     GRAPH = args.graph
     rows = {"conv": conv, "gemm": gemm, "attn": attn, "ln": ln, "muon": muon, "vitstep": vitstep,
-            "resnetstep": resnetstep}[args.what](args)
+            "resnetstep": resnetstep, "data": databatch}[args.what](args)
     for r in rows:
         print(json.dumps(r))
 

@@ -71,3 +71,27 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     code = L.rnn_gemm_dw_noalloc_dev(4096, 1024, 8, p, p, p, None)
     assert code == -1
     assert L.rnn_gemm_dw_noalloc_status(None) == 0
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_noalloc_on_a_second_device_after_the_first():
+    """The entry's per-device state (the scratch array's address, each tile
+    width's shared-memory opt-in) is set up again for device 1 after device
+    0 in the same process."""
+    from rustnn_b200 import _lib
+
+    L = _lib.lib()
+    m, n, k = 768, 256, 8192
+    rng = O.Rng(11)
+    a, b, c0 = rng.rand_vec(k * m), rng.rand_vec(k * n), rng.rand_vec(m * n)
+    want = O.matmul_dw(m, n, k, a, b, c0.copy())
+    for dev in (0, 1):
+        with torch.cuda.device(dev):
+            ad, bd = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+            got = torch.from_numpy(c0).cuda()
+            stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+            code = L.rnn_gemm_dw_noalloc_dev(m, n, k, C.c_void_p(ad.data_ptr()), C.c_void_p(bd.data_ptr()),
+                                             C.c_void_p(got.data_ptr()), stream)
+            assert code == 0, L.rnn_last_error()
+            assert L.rnn_gemm_dw_noalloc_status(stream) == 0, L.rnn_last_error()
+            assert rel(got.cpu().numpy(), want) < TOL, dev
