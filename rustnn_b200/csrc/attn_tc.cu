@@ -514,18 +514,25 @@ __global__ void attn_image_sum_kernel(const float* __restrict__ ds, int n, int p
   }
 }
 
-// drel[h][r] += sum_i dssum[h][i][inv[i][r]], queries ascending.
+// drel[h][r] += sum_i dssum[h][i][inv[i][r]]: one warp per (h, r), lane l
+// sums queries l, l+32, ... in ascending order, then a fixed shuffle tree
+// over the lanes (deterministic; the queries' loads are in flight together
+// instead of one dependent index-then-value pair after another).
 __global__ void attn_drel_gather_kernel(const float* __restrict__ dssum, const int* __restrict__ inv, int h, int tq,
                                         int tk, int nrel, float* __restrict__ drel) {
   const int total = h * nrel;
-  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
+  const int lane = threadIdx.x & 31;
+  const int wstride = (gridDim.x * blockDim.x) >> 5;
+  for (int e = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; e < total; e += wstride) {
     const int hd = e / nrel, r = e - hd * nrel;
     float s = 0.0f;
-    for (int i = 0; i < tq; i++) {
+    for (int i = lane; i < tq; i += 32) {
       const int j = __ldg(inv + (size_t)i * nrel + r);
       if (j >= 0) s += __ldg(dssum + ((size_t)hd * tq + i) * tk + j);
     }
-    drel[e] += s;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_down_sync(0xffffffffu, s, o);
+    if (lane == 0) drel[e] += s;
   }
 }
 
@@ -547,7 +554,8 @@ int attn_drel(rnn_ctx* ctx, const AttnTC& a, const int* inv, float* dssum, float
                                                                                                 dssum);
   RNN_CHECK_LAUNCH();
   const int total = a.h * a.nrel;
-  attn_drel_gather_kernel<<<(total + 127) / 128, 128, 0, ctx->stream>>>(dssum, inv, a.h, a.tq, a.tk, a.nrel, drel);
+  attn_drel_gather_kernel<<<std::min((total + 7) / 8, ctx->num_sms * 8), 256, 0, ctx->stream>>>(
+      dssum, inv, a.h, a.tq, a.tk, a.nrel, drel);
   RNN_CHECK_LAUNCH();
   return RNN_OK;
 }

@@ -152,6 +152,104 @@ __global__ void dw3_dw_partial(const float* __restrict__ dy, const float* __rest
     part[(size_t)i * 10 * c + e] = s;
   }
 }
+// float4 forms (c % 4 == 0, 16-byte aligned tensors): a thread handles four
+// channels of one pixel with 32-bit index arithmetic; each channel's sum
+// runs in the same order as the scalar kernels above.
+__device__ __forceinline__ void fma4(float4& a, const float4 w, const float4 v) {
+  a.x += w.x * v.x;
+  a.y += w.y * v.y;
+  a.z += w.z * v.z;
+  a.w += w.w * v.w;
+}
+__global__ void dw3_fwd4_kernel(const float4* __restrict__ x, int npix, int th, int tw, int c4,
+                                const float4* __restrict__ w, const float4* __restrict__ b, float4* __restrict__ y) {
+  const int total = npix * c4, hw = th * tw;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
+    const int j = e % c4, pix = e / c4;
+    const int img = pix / hw, rem = pix - img * hw;
+    const int oy = rem / tw, ox = rem - oy * tw;
+    float4 acc = __ldg(b + j);
+    for (int ky = 0; ky < 3; ky++) {
+      const int sy = oy + ky - 1;
+      if (sy < 0 || sy >= th) continue;
+      for (int kx = 0; kx < 3; kx++) {
+        const int sx = ox + kx - 1;
+        if (sx < 0 || sx >= tw) continue;
+        fma4(acc, __ldg(w + (ky * 3 + kx) * c4 + j), __ldg(x + (size_t)(img * hw + sy * tw + sx) * c4 + j));
+      }
+    }
+    y[e] = acc;
+  }
+}
+__global__ void dw3_dx4_kernel(const float4* __restrict__ dy, int npix, int th, int tw, int c4,
+                               const float4* __restrict__ w, float4* __restrict__ dx) {
+  const int total = npix * c4, hw = th * tw;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
+    const int j = e % c4, pix = e / c4;
+    const int img = pix / hw, rem = pix - img * hw;
+    const int sy = rem / tw, sx = rem - sy * tw;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int ky = 0; ky < 3; ky++) {
+      const int oy = sy - ky + 1;
+      if (oy < 0 || oy >= th) continue;
+      for (int kx = 0; kx < 3; kx++) {
+        const int ox = sx - kx + 1;
+        if (ox < 0 || ox >= tw) continue;
+        fma4(acc, __ldg(w + (ky * 3 + kx) * c4 + j), __ldg(dy + (size_t)(img * hw + oy * tw + ox) * c4 + j));
+      }
+    }
+    dx[e] = acc;
+  }
+}
+// Per-image partials of dW and dB, part[i][10][c]: a CTA covers 32 channel
+// quads of one image with 8 pixel groups (group g takes pixels g, g+8, ...
+// in order) that accumulate all ten sums at once, then adds the 8 groups in
+// order in shared memory.
+constexpr int DW3_PG = 8;
+__global__ void __launch_bounds__(32 * DW3_PG) dw3_dw_partial4(const float4* __restrict__ dy,
+                                                                 const float4* __restrict__ x, int th, int tw, int c4,
+                                                                 float4* __restrict__ part) {
+  __shared__ float4 red[DW3_PG][10][32];
+  const int q = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int j = blockIdx.x * 32 + q;
+  const int i = blockIdx.y, hw = th * tw;
+  float4 acc[10];
+#pragma unroll
+  for (int t = 0; t < 10; t++) acc[t] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  if (j < c4) {
+    const float4* dyi = dy + (size_t)i * hw * c4 + j;
+    const float4* xi = x + (size_t)i * hw * c4 + j;
+    for (int p = g; p < hw; p += DW3_PG) {
+      const int oy = p / tw, ox = p - oy * tw;
+      const float4 d = __ldg(dyi + (size_t)p * c4);
+      acc[9].x += d.x;
+      acc[9].y += d.y;
+      acc[9].z += d.z;
+      acc[9].w += d.w;
+#pragma unroll
+      for (int t = 0; t < 9; t++) {
+        const int sy = oy + t / 3 - 1, sx = ox + t % 3 - 1;
+        if (sy >= 0 && sy < th && sx >= 0 && sx < tw) fma4(acc[t], d, __ldg(xi + (size_t)(sy * tw + sx) * c4));
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < 10; t++) red[g][t][q] = acc[t];
+  __syncthreads();
+  for (int o = threadIdx.x; o < 10 * 32; o += blockDim.x) {
+    const int t = o >> 5, qq = o & 31, jj = blockIdx.x * 32 + qq;
+    if (jj >= c4) continue;
+    float4 s = red[0][t][qq];
+    for (int gg = 1; gg < DW3_PG; gg++) {
+      const float4 v = red[gg][t][qq];
+      s.x += v.x;
+      s.y += v.y;
+      s.z += v.z;
+      s.w += v.w;
+    }
+    part[((size_t)i * 10 + t) * c4 + jj] = s;
+  }
+}
 __global__ void dw3_dw_final(const float* __restrict__ part, int n, int c, float* __restrict__ dw,
                              float* __restrict__ db) {
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < 10 * c; e += gridDim.x * blockDim.x) {
@@ -499,13 +597,28 @@ extern "C" int rnn_swiglu_act_bwd_dev(rnn_ctx* ctx, const float* du, const float
   return RNN_OK;
 }
 
+// The float4 depthwise kernels need c % 4 == 0, 16-byte aligned tensors and
+// 32-bit element indices.
+static bool dw3_vec_ok(size_t total, int c, std::initializer_list<const void*> ptrs) {
+  if (c % 4 != 0 || total / 4 >= (size_t)INT32_MAX) return false;
+  for (const void* p : ptrs)
+    if (reinterpret_cast<uintptr_t>(p) & 15) return false;
+  return true;
+}
+
 extern "C" int rnn_dwconv3_fwd_dev(rnn_ctx* ctx, const float* x, int n, int th, int tw, int c, const float* w,
                                    const float* b, float* y) {
   RNN_REQUIRE(ctx && x && w && b && y && n >= 0 && th > 0 && tw > 0 && c > 0, "dwconv3_fwd: bad arguments");
   const size_t total = (size_t)n * th * tw * c;
   if (!total) return RNN_OK;
   RNN_RANGE(x, total * 4); RNN_RANGE(y, total * 4); RNN_RANGE(w, (size_t)9 * c * 4); RNN_RANGE(b, (size_t)c * 4);
-  dw3_fwd_kernel<<<gl_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(x, n, th, tw, c, w, b, y);
+  if (dw3_vec_ok(total, c, {x, w, b, y})) {
+    dw3_fwd4_kernel<<<gl_grid(total / 4, ctx->num_sms), 256, 0, ctx->stream>>>(
+        reinterpret_cast<const float4*>(x), n * th * tw, th, tw, c / 4, reinterpret_cast<const float4*>(w),
+        reinterpret_cast<const float4*>(b), reinterpret_cast<float4*>(y));
+  } else {
+    dw3_fwd_kernel<<<gl_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(x, n, th, tw, c, w, b, y);
+  }
   RNN_CHECK_LAUNCH();
   return RNN_OK;
 }
@@ -520,11 +633,24 @@ extern "C" int rnn_dwconv3_bwd_dev(rnn_ctx* ctx, const float* dy, const float* x
   RNN_RANGE(dw, (size_t)9 * c * 4); RNN_RANGE(db, (size_t)c * 4);
   RNN_TRY(ensure_aux(ctx, (size_t)n * 10 * c * 4));
   float* part = static_cast<float*>(ctx->aux);
-  dw3_dw_partial<<<dim3((10 * c + 255) / 256, n), 256, 0, ctx->stream>>>(dy, x, th, tw, c, part);
+  const bool vec = dw3_vec_ok(total, c, {dy, x, w, dx, part});
+  if (vec) {
+    dw3_dw_partial4<<<dim3((c / 4 + 31) / 32, n), 32 * DW3_PG, 0, ctx->stream>>>(
+        reinterpret_cast<const float4*>(dy), reinterpret_cast<const float4*>(x), th, tw, c / 4,
+        reinterpret_cast<float4*>(part));
+  } else {
+    dw3_dw_partial<<<dim3((10 * c + 255) / 256, n), 256, 0, ctx->stream>>>(dy, x, th, tw, c, part);
+  }
   RNN_CHECK_LAUNCH();
   dw3_dw_final<<<(10 * c + 255) / 256, 256, 0, ctx->stream>>>(part, n, c, dw, db);
   RNN_CHECK_LAUNCH();
-  dw3_dx_kernel<<<gl_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(dy, n, th, tw, c, w, dx);
+  if (vec) {
+    dw3_dx4_kernel<<<gl_grid(total / 4, ctx->num_sms), 256, 0, ctx->stream>>>(
+        reinterpret_cast<const float4*>(dy), n * th * tw, th, tw, c / 4, reinterpret_cast<const float4*>(w),
+        reinterpret_cast<float4*>(dx));
+  } else {
+    dw3_dx_kernel<<<gl_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(dy, n, th, tw, c, w, dx);
+  }
   RNN_CHECK_LAUNCH();
   return RNN_OK;
 }
