@@ -49,6 +49,16 @@ int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, in
 // tile width, 32-pixel K blocks); 0 when it would not use one.
 int wgrad_dy_pack_bn(int n, int cout, int k, int oh, int ow, const void* dy);
 }  // namespace tc
+// Backward of LayerNorm (norm.rs:96-135), Linear (linear.rs:66-96) and the
+// depthwise 3x3 (vit.rs DwConv3) as the C entries compute them, except that
+// with acc_dx the input gradient is added into dx (dx += ...) instead of
+// stored: the residual joins of the rustvit backward take it that way.
+int layernorm_bwd(rnn_ctx* ctx, const float* dy, const float* xhat, const float* invstd, int rows, int c,
+                  const float* g, float* dx, float* dg, float* db, bool acc_dx);
+int linear_bwd(rnn_ctx* ctx, const float* x, const float* dy, int rows, int fin, int fout, const float* w, float* dw,
+               float* db, float* dx, bool acc_dx);
+int dwconv3_bwd(rnn_ctx* ctx, const float* dy, const float* x, int n, int th, int tw, int c, const float* w,
+                float* dw, float* db, float* dx, bool acc_dx);
 // Newton-Schulz (optim.rs:124-145) in place on `count` matrices, the
 // matrices of one working shape batched into shared launches (optim.cu)
 int newton_schulz_grouped(rnn_ctx* ctx, int count, float* const* g, const int* rows, const int* cols, int steps);

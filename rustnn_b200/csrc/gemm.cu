@@ -239,8 +239,8 @@ static int gemm_typed(rnn_ctx* ctx, int m, int n, int k, const float* a, const f
   // anyway, so narrow tiles only multiply the re-reads of the A strips (one
   // per column tile) and issue narrower MMAs.  Take 128-column tiles there:
   // rustvit qkv dW (768 x 256 x 16384) 112 -> 53 us, step 12.53 -> 12.03 ms.
-  if (bn < 128 && n >= 128 && pick_splits(m, n, k, bn, ctx->num_sms) > 1 && (long)m * n * k >= (1L << 22))
-    bn = 128;
+  if (bn < 128 && n >= 64 && pick_splits(m, n, k, bn, ctx->num_sms) > 1 && (long)m * n * k >= (1L << 22))
+    bn = n >= 128 ? 128 : 64;
   if (AT && !BT) {  // the matmul_dw layout: RNN_DW_BN=32|64|128|256 forces the tile width (A/B runs)
     const char* e = getenv("RNN_DW_BN");
     const int f = e ? atoi(e) : 0;
@@ -469,11 +469,54 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, float* __rest
   }
 }
 
+// Row-major form over float4 groups (total % 4 == 0, 16-byte aligned): the
+// partials of four splits are loaded together and then added in split order,
+// so every element gets the same sum as in the scalar form.
+__global__ void splitk_reduce4_kernel(const float4* __restrict__ ws, float4* __restrict__ out, size_t total4,
+                                      int splits, int acc) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total4; i += (size_t)gridDim.x * blockDim.x) {
+    float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    int p = 0;
+    for (; p + 4 <= splits; p += 4) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) v[u] = __ldg(ws + (size_t)(p + u) * total4 + i);
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        s.x += v[u].x;
+        s.y += v[u].y;
+        s.z += v[u].z;
+        s.w += v[u].w;
+      }
+    }
+    for (; p < splits; p++) {
+      const float4 v = __ldg(ws + (size_t)p * total4 + i);
+      s.x += v.x;
+      s.y += v.y;
+      s.z += v.z;
+      s.w += v.w;
+    }
+    if (acc) {
+      const float4 o = out[i];
+      s = make_float4(o.x + s.x, o.y + s.y, o.z + s.z, o.w + s.w);
+    }
+    out[i] = s;
+  }
+}
+
 int launch_splitk_reduce(rnn_ctx* ctx, const float* ws, float* out, int rows, int cols, int splits,
                          bool acc, bool transpose) {
   size_t total = (size_t)rows * cols;
   RNN_RANGE(ws, total * splits * sizeof(float));
   RNN_RANGE(out, total * sizeof(float));
+  if (!transpose && total % 4 == 0 && al16(ws) && al16(out)) {
+    const size_t total4 = total / 4;
+    const unsigned g4 = (unsigned)std::max<size_t>(1, std::min<size_t>((total4 + 255) / 256, (size_t)ctx->num_sms * 8));
+    splitk_reduce4_kernel<<<g4, 256, 0, ctx->stream>>>(reinterpret_cast<const float4*>(ws),
+                                                       reinterpret_cast<float4*>(out), total4, splits, acc ? 1 : 0);
+    RNN_CHECK_LAUNCH();
+    return RNN_OK;
+  }
   unsigned grid;
   if (transpose) grid = (unsigned)std::min<size_t>(((rows + 31) / 32) * (size_t)((cols + 31) / 32), 4096);
   else grid = (unsigned)std::min<size_t>((total + 255) / 256, (size_t)ctx->num_sms * 8);

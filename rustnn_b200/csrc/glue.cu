@@ -106,7 +106,7 @@ __global__ void dw3_fwd_kernel(const float* __restrict__ x, int n, int th, int t
 }
 // dx[i, sy, sx, :] = sum over output pixels that read (sy, sx) of w[tap] dy
 __global__ void dw3_dx_kernel(const float* __restrict__ dy, int n, int th, int tw, int c, const float* __restrict__ w,
-                              float* __restrict__ dx) {
+                              float* __restrict__ dx, int accd) {
   const size_t total = (size_t)n * th * tw * c;
   for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
     const int j = (int)(e % c);
@@ -123,7 +123,7 @@ __global__ void dw3_dx_kernel(const float* __restrict__ dy, int n, int th, int t
         acc += w[(ky * 3 + kx) * c + j] * dy[(ibase + (size_t)oy * tw + ox) * c + j];
       }
     }
-    dx[e] = acc;
+    dx[e] = accd ? dx[e] + acc : acc;
   }
 }
 // per-image partials of dW [9][c] and dB [c]: part[i][10][c]
@@ -182,7 +182,7 @@ __global__ void dw3_fwd4_kernel(const float4* __restrict__ x, int npix, int th, 
   }
 }
 __global__ void dw3_dx4_kernel(const float4* __restrict__ dy, int npix, int th, int tw, int c4,
-                               const float4* __restrict__ w, float4* __restrict__ dx) {
+                               const float4* __restrict__ w, float4* __restrict__ dx, int accd) {
   const int total = npix * c4, hw = th * tw;
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
     const int j = e % c4, pix = e / c4;
@@ -197,6 +197,10 @@ __global__ void dw3_dx4_kernel(const float4* __restrict__ dy, int npix, int th, 
         if (ox < 0 || ox >= tw) continue;
         fma4(acc, __ldg(w + (ky * 3 + kx) * c4 + j), __ldg(dy + (size_t)(img * hw + oy * tw + ox) * c4 + j));
       }
+    }
+    if (accd) {
+      const float4 q = dx[e];
+      acc = make_float4(q.x + acc.x, q.y + acc.y, q.z + acc.z, q.w + acc.w);
     }
     dx[e] = acc;
   }
@@ -623,8 +627,8 @@ extern "C" int rnn_dwconv3_fwd_dev(rnn_ctx* ctx, const float* x, int n, int th, 
   return RNN_OK;
 }
 
-extern "C" int rnn_dwconv3_bwd_dev(rnn_ctx* ctx, const float* dy, const float* x, int n, int th, int tw, int c,
-                                   const float* w, float* dw, float* db, float* dx) {
+int rnn::dwconv3_bwd(rnn_ctx* ctx, const float* dy, const float* x, int n, int th, int tw, int c, const float* w,
+                     float* dw, float* db, float* dx, bool acc_dx) {
   RNN_REQUIRE(ctx && dy && x && w && dw && db && dx && n >= 0 && th > 0 && tw > 0 && c > 0,
               "dwconv3_bwd: bad arguments");
   const size_t total = (size_t)n * th * tw * c;
@@ -647,12 +651,17 @@ extern "C" int rnn_dwconv3_bwd_dev(rnn_ctx* ctx, const float* dy, const float* x
   if (vec) {
     dw3_dx4_kernel<<<gl_grid(total / 4, ctx->num_sms), 256, 0, ctx->stream>>>(
         reinterpret_cast<const float4*>(dy), n * th * tw, th, tw, c / 4, reinterpret_cast<const float4*>(w),
-        reinterpret_cast<float4*>(dx));
+        reinterpret_cast<float4*>(dx), acc_dx ? 1 : 0);
   } else {
-    dw3_dx_kernel<<<gl_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(dy, n, th, tw, c, w, dx);
+    dw3_dx_kernel<<<gl_grid(total, ctx->num_sms), 256, 0, ctx->stream>>>(dy, n, th, tw, c, w, dx, acc_dx ? 1 : 0);
   }
   RNN_CHECK_LAUNCH();
   return RNN_OK;
+}
+
+extern "C" int rnn_dwconv3_bwd_dev(rnn_ctx* ctx, const float* dy, const float* x, int n, int th, int tw, int c,
+                                   const float* w, float* dw, float* db, float* dx) {
+  return rnn::dwconv3_bwd(ctx, dy, x, n, th, tw, c, w, dw, db, dx, false);
 }
 
 extern "C" int rnn_seqpool_fwd_dev(rnn_ctx* ctx, const float* x, int n, int t, int c, const float* p, float* z,

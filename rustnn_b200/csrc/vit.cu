@@ -320,7 +320,7 @@ struct rnn_rustvit {
   float *b_rows4 = nullptr, *b_rows4b = nullptr, *b_merge = nullptr, *b_merge2 = nullptr;
   float *b_rows3 = nullptr, *dmem = nullptr, *dmem2 = nullptr;
   float *bs1 = nullptr, *bs2 = nullptr, *bs3 = nullptr, *bs4 = nullptr, *bs_wide = nullptr, *bs_wide2 = nullptr,
-        *bs_qkv = nullptr, *bs_qkv2 = nullptr;
+        *bs_qkv = nullptr;
   float *b_img_a = nullptr, *b_img_b = nullptr, *b_img_c = nullptr, *b_img_d = nullptr, *b_c2 = nullptr,
         *b_c2b = nullptr;
   // packed A image of the last LayerNorm output that feeds a GEMM
@@ -538,7 +538,6 @@ static int ensure_acts(rnn_rustvit* net, int n) {
   RNN_TRY(dalloc(net, &net->bs_wide, hmax));
   RNN_TRY(dalloc(net, &net->bs_wide2, hmax));
   RNN_TRY(dalloc(net, &net->bs_qkv, 3 * rc));
-  RNN_TRY(dalloc(net, &net->bs_qkv2, 3 * rc));
   {
     size_t amax = 0;  // ceil(rows / 128) * 128 rows of c columns, hi and lo
     for (auto* v : {&net->blocks3, &net->blocks4})
@@ -572,6 +571,10 @@ static int lin_bwd(rnn_rustvit* net, LinL& l, const float* dy, float* dx) {
   return rnn_linear_bwd_dev(net->ctx, l.x, dy, l.rows, l.fin, l.fout, P(net, l.w), Gd(net, l.w), Gopt(net, l.b),
                             dx);
 }
+// dx += the Linear input gradient (the GEMM epilogue adds it)
+static int lin_bwd_acc(rnn_rustvit* net, LinL& l, const float* dy, float* dx) {
+  return linear_bwd(net->ctx, l.x, dy, l.rows, l.fin, l.fout, P(net, l.w), Gd(net, l.w), Gopt(net, l.b), dx, true);
+}
 static int ln_fwd(rnn_rustvit* net, LNL& l, const float* x, int rows, float* y) {
   l.rows = rows;
   return rnn_layernorm_fwd_dev(net->ctx, x, rows, l.c, P(net, l.g), P(net, l.b), 1e-5f, y, l.xhat, l.invstd);
@@ -593,6 +596,11 @@ static int lin_fwd_img(rnn_rustvit* net, LinL& l, const float* img, const float*
 static int ln_bwd(rnn_rustvit* net, LNL& l, const float* dy, float* dx) {
   return rnn_layernorm_bwd_dev(net->ctx, dy, l.xhat, l.invstd, l.rows, l.c, P(net, l.g), dx, Gd(net, l.g),
                                Gd(net, l.b));
+}
+// dx += the LayerNorm input gradient (a residual join)
+static int ln_bwd_acc(rnn_rustvit* net, LNL& l, const float* dy, float* dx) {
+  return layernorm_bwd(net->ctx, dy, l.xhat, l.invstd, l.rows, l.c, P(net, l.g), dx, Gd(net, l.g), Gd(net, l.b),
+                       true);
 }
 static int ls_fwd(rnn_rustvit* net, LSL& l, const float* x, int rows, float* y) {
   l.x = x;
@@ -752,8 +760,7 @@ static int block_bwd(rnn_rustvit* net, Block& b, float* dz, const float* mem, fl
   RNN_TRY(lin_bwd(net, b.mlp.wd, t2, net->bs_wide2));  // du [rows, h]
   RNN_TRY(rnn_swiglu_act_bwd_dev(net->ctx, net->bs_wide2, b.mlp.ab, rows, b.mlp.h, net->bs_wide));  // dab
   RNN_TRY(lin_bwd(net, b.mlp.wg, net->bs_wide, t1));  // t1 = dh2
-  RNN_TRY(ln_bwd(net, b.n2, t1, t2));
-  RNN_TRY(rnn_add_dev(net->ctx, dz, t2, rc));  // dz now dy
+  RNN_TRY(ln_bwd_acc(net, b.n2, t1, dz));  // dz now dy
   // dh accumulates the three branches that read LN1's output
   bool dh_set = false;
   if (b.has_cross) {
@@ -776,23 +783,20 @@ static int block_bwd(rnn_rustvit* net, Block& b, float* dz, const float* mem, fl
   // self-attention backward (attn.rs:415-440)
   SelfAttnL& A = b.attn;
   RNN_TRY(lin_bwd(net, A.proj, t2, t1));  // dobuf
+  // dq lands in columns [0, c) of the qkv gradient, dk / dv in [c, 3c):
+  // disjoint, so one zeroed buffer takes both
   RNN_TRY(zero(net, net->bs_qkv, rc * 3));
-  RNN_TRY(zero(net, net->bs_qkv2, rc * 3));
   RNN_TRY(rnn_attn_bwd_dev(net->ctx, n, A.h, A.dh, A.th, A.th, A.th, A.th, A.ab, 3 * c, 0, A.ab, 3 * c, c, 2 * c,
-                           P(net, A.tau), A.p, t1, net->bs_qkv, net->bs_qkv2, Gd(net, A.tau), Gd(net, A.rel)));
-  RNN_TRY(rnn_add_dev(net->ctx, net->bs_qkv, net->bs_qkv2, rc * 3));
+                           P(net, A.tau), A.p, t1, net->bs_qkv, net->bs_qkv, Gd(net, A.tau), Gd(net, A.rel)));
   if (dh_set) {
-    RNN_TRY(lin_bwd(net, A.qkv, net->bs_qkv, t1));
-    RNN_TRY(rnn_add_dev(net->ctx, dh, t1, rc));
+    RNN_TRY(lin_bwd_acc(net, A.qkv, net->bs_qkv, dh));
   } else {
     RNN_TRY(lin_bwd(net, A.qkv, net->bs_qkv, dh));
   }
   // depthwise branch
-  RNN_TRY(rnn_dwconv3_bwd_dev(net->ctx, t4, b.dw.x, n, b.th, b.th, c, P(net, b.dw.w), Gd(net, b.dw.w),
-                              Gd(net, b.dw.b), t1));
-  RNN_TRY(rnn_add_dev(net->ctx, dh, t1, rc));
-  RNN_TRY(ln_bwd(net, b.n1, dh, t1));
-  return rnn_add_dev(net->ctx, dz, t1, rc);
+  RNN_TRY(dwconv3_bwd(net->ctx, t4, b.dw.x, n, b.th, b.th, c, P(net, b.dw.w), Gd(net, b.dw.w), Gd(net, b.dw.b),
+                      dh, true));
+  return ln_bwd_acc(net, b.n1, dh, dz);
 }
 
 // ---- whole network (vit.rs:511-685)

@@ -206,7 +206,7 @@ def test_attention_gradcheck_on_gpu(ops, self_attn):
 # ------------------------------------------------------------------ LayerNorm / Linear
 
 
-@pytest.mark.parametrize("rows,c", [(8192, 256), (2048, 384), (27, 8), (4096, 512)])
+@pytest.mark.parametrize("rows,c", [(8192, 256), (2048, 384), (27, 8), (4096, 512), (100, 128), (1000, 384)])
 def test_layernorm_parity(ops, rows, c):
     rng = O.Rng(rows + c)
     x = (rng.rand_vec(rows * c) * 3 + 1).astype(np.float32)
@@ -216,9 +216,10 @@ def test_layernorm_parity(ops, rows, c):
     y, xh, isd = ops.layernorm_forward(dev(x), rows, c, dev(gm), dev(bt))
     assert rel(host(y), y_ref) < TOL and rel(host(xh), xh_ref) < TOL and rel(host(isd), is_ref) < 1e-6
     dy = rng.rand_vec(rows * c)
-    dg_ref, db_ref = np.zeros(c, np.float32), np.zeros(c, np.float32)
+    # the gradients accumulate (+=) into what the buffers hold
+    dg_ref, db_ref = rng.rand_vec(c), rng.rand_vec(c)
+    dg, db = dev(dg_ref.copy()), dev(db_ref.copy())
     dx_ref = O.layernorm_bwd(dy, xh_ref, is_ref, rows, c, gm, dg_ref, db_ref)
-    dg, db = torch.zeros(c, device="cuda"), torch.zeros(c, device="cuda")
     dx = ops.layernorm_backward(dev(dy), xh, isd, rows, c, dev(gm), dg, db)
     assert rel(host(dx), dx_ref) < TOL and rel(host(dg), dg_ref) < TOL and rel(host(db), db_ref) < TOL
 
