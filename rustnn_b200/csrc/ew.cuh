@@ -59,6 +59,22 @@ int linear_bwd(rnn_ctx* ctx, const float* x, const float* dy, int rows, int fin,
                float* db, float* dx, bool acc_dx);
 int dwconv3_bwd(rnn_ctx* ctx, const float* dy, const float* x, int n, int th, int tw, int c, const float* w,
                 float* dw, float* db, float* dx, bool acc_dx);
+// One launch of an optimiser update over many parameter segments of the flat
+// value / gradient / moment buffers (a table in device memory): segment s
+// covers elements [off, off + n); scale is Muon's update scale and decay the
+// parameter's weight-decay flag.  Per element the arithmetic is that of the
+// single-tensor kernels, so a segmented launch equals one launch per segment.
+struct OptSeg {
+  size_t off, n;
+  float scale;
+  int decay;
+};
+int muon_momentum_segs(rnn_ctx* ctx, float* g, float* m, const OptSeg* segs, int nseg, size_t max_n, float mom);
+int muon_update_segs(rnn_ctx* ctx, float* v, float* g, const OptSeg* segs, int nseg, size_t max_n, float lr,
+                     float wd);
+int adamw_segs(rnn_ctx* ctx, float* v, float* g, float* m, float* v2, const OptSeg* segs, int nseg, size_t max_n,
+               float lr, float wd, float b1, float b2, float eps, int t);
+float muon_scale(int rows, int cols);
 // Newton-Schulz (optim.rs:124-145) in place on `count` matrices, the
 // matrices of one working shape batched into shared launches (optim.cu)
 int newton_schulz_grouped(rnn_ctx* ctx, int count, float* const* g, const int* rows, const int* cols, int steps);

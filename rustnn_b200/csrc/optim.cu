@@ -300,11 +300,81 @@ int muon_momentum(rnn_ctx* ctx, float* g, float* m, size_t n, float mom) {
   return RNN_OK;
 }
 
+float muon_scale(int rows, int cols) { return 0.2f * sqrtf((float)std::max(rows, cols)); }
+
+// Segmented forms: blockIdx.y selects the segment, the x grid strides over it.
+__global__ void muon_mom_seg_kernel(float* __restrict__ g, float* __restrict__ m, const OptSeg* __restrict__ segs,
+                                    float mom) {
+  const OptSeg sg = segs[blockIdx.y];
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < sg.n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t e = sg.off + i;
+    const float mm = mom * m[e] + g[e];
+    m[e] = mm;
+    g[e] += mom * mm;
+  }
+}
+__global__ void muon_update_seg_kernel(float* __restrict__ v, float* __restrict__ g, const OptSeg* __restrict__ segs,
+                                       float lr, float wd) {
+  const OptSeg sg = segs[blockIdx.y];
+  const float w = sg.decay ? wd : 0.0f;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < sg.n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t e = sg.off + i;
+    v[e] -= lr * (sg.scale * g[e] + w * v[e]);
+    g[e] = 0.0f;
+  }
+}
+__global__ void adamw_seg_kernel(float* __restrict__ v, float* __restrict__ g, float* __restrict__ m,
+                                 float* __restrict__ v2, const OptSeg* __restrict__ segs, float lr, float wd, float b1,
+                                 float b2, float eps, float c1, float c2) {
+  const OptSeg sg = segs[blockIdx.y];
+  const float w = sg.decay ? wd : 0.0f;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < sg.n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t e = sg.off + i;
+    const float gg = g[e];
+    const float mm = b1 * m[e] + (1.0f - b1) * gg;
+    const float vv = b2 * v2[e] + (1.0f - b2) * gg * gg;
+    m[e] = mm;
+    v2[e] = vv;
+    v[e] -= lr * ((mm / c1) / (sqrtf(vv / c2) + eps) + w * v[e]);
+    g[e] = 0.0f;
+  }
+}
+
+static dim3 seg_grid(size_t max_n, int nseg, int sms) {
+  const size_t gx = std::max<size_t>(1, std::min<size_t>((max_n + 255) / 256, (size_t)sms * 4));
+  return dim3((unsigned)gx, (unsigned)nseg);
+}
+
+int muon_momentum_segs(rnn_ctx* ctx, float* g, float* m, const OptSeg* segs, int nseg, size_t max_n, float mom) {
+  if (nseg <= 0) return RNN_OK;
+  muon_mom_seg_kernel<<<seg_grid(max_n, nseg, ctx->num_sms), 256, 0, ctx->stream>>>(g, m, segs, mom);
+  RNN_CHECK_LAUNCH();
+  return RNN_OK;
+}
+
+int muon_update_segs(rnn_ctx* ctx, float* v, float* g, const OptSeg* segs, int nseg, size_t max_n, float lr,
+                     float wd) {
+  if (nseg <= 0) return RNN_OK;
+  muon_update_seg_kernel<<<seg_grid(max_n, nseg, ctx->num_sms), 256, 0, ctx->stream>>>(v, g, segs, lr, wd);
+  RNN_CHECK_LAUNCH();
+  return RNN_OK;
+}
+
+int adamw_segs(rnn_ctx* ctx, float* v, float* g, float* m, float* v2, const OptSeg* segs, int nseg, size_t max_n,
+               float lr, float wd, float b1, float b2, float eps, int t) {
+  if (nseg <= 0) return RNN_OK;
+  const float c1 = 1.0f - powf(b1, (float)(t + 1)), c2 = 1.0f - powf(b2, (float)(t + 1));
+  adamw_seg_kernel<<<seg_grid(max_n, nseg, ctx->num_sms), 256, 0, ctx->stream>>>(v, g, m, v2, segs, lr, wd, b1, b2,
+                                                                                 eps, c1, c2);
+  RNN_CHECK_LAUNCH();
+  return RNN_OK;
+}
+
 int muon_update(rnn_ctx* ctx, float* v, float* g, int rows, int cols, float lr, float wd, int decay) {
   const size_t n = (size_t)rows * cols;
   RNN_RANGE(v, n * 4);
   RNN_RANGE(g, n * 4);
-  const float scale = 0.2f * sqrtf((float)std::max(rows, cols));
+  const float scale = muon_scale(rows, cols);
   muon_update_kernel<<<egrid(n, ctx->num_sms), 256, 0, ctx->stream>>>(v, g, n, lr, scale, decay ? wd : 0.0f);
   RNN_CHECK_LAUNCH();
   return RNN_OK;

@@ -304,6 +304,10 @@ struct rnn_rustvit {
   // optimiser state
   int opt_t = 0, ema_t = 0;
   bool ema_ready = false;
+  // step_all's segment tables (device): the Muon matrices, then the AdamW runs
+  rnn::OptSeg* opt_segs = nullptr;
+  int n_mu = 0, n_ad = 0;
+  size_t mu_max = 0, ad_max = 0;
   // activations
   std::vector<void*> allocs;
   int cap = 0;
@@ -1050,53 +1054,67 @@ static bool is_muon(const HostParam& p) { return p.rows > 0 && std::min(p.rows, 
 // the rest (consecutive parameters with the same decay flag in one call).
 static int step_all(rnn_rustvit* net, float lr, float wd) {
   rnn_ctx* ctx = net->ctx;
+  if (!net->opt_segs) {
+    // The segments depend only on the network's layout: built on the first
+    // step.  Muon matrices in for_each_param order; AdamW over runs of
+    // consecutive non-Muon parameters with the same decay flag.
+    std::vector<rnn::OptSeg> mu, ad;
+    size_t run0 = 0, runlen = 0;
+    int rundecay = -1;
+    auto flush = [&]() {
+      if (runlen) {
+        ad.push_back({run0, runlen, 0.0f, rundecay});
+        net->ad_max = std::max(net->ad_max, runlen);
+      }
+      runlen = 0;
+    };
+    for (int id : net->order) {
+      const HostParam& p = net->R.ps[id];
+      const size_t o = net->off[id], len = p.v.size();
+      if (is_muon(p)) {
+        flush();
+        const size_t n = (size_t)p.rows * p.cols;
+        mu.push_back({o, n, rnn::muon_scale(p.rows, p.cols), p.decay ? 1 : 0});
+        net->mu_max = std::max(net->mu_max, n);
+        continue;
+      }
+      const int dec = p.decay ? 1 : 0;
+      if (runlen && (dec != rundecay || run0 + runlen != o)) flush();
+      if (!runlen) {
+        run0 = o;
+        rundecay = dec;
+      }
+      runlen += len;
+    }
+    flush();
+    std::vector<rnn::OptSeg> all(mu);
+    all.insert(all.end(), ad.begin(), ad.end());
+    if (!all.empty()) {
+      RNN_CUDA(cudaMalloc(&net->opt_segs, all.size() * sizeof(rnn::OptSeg)));
+      RNN_CUDA(cudaMemcpy(net->opt_segs, all.data(), all.size() * sizeof(rnn::OptSeg), cudaMemcpyHostToDevice));
+    }
+    net->n_mu = (int)mu.size();
+    net->n_ad = (int)ad.size();
+  }
   // Muon (optim.rs:183-196) per matrix: momentum, Newton-Schulz, update.
   // The matrices are independent, so the momentum of all of them runs
-  // first, then one grouped Newton-Schulz over every gradient, then the
-  // updates.
+  // first (one launch), then one grouped Newton-Schulz over every gradient,
+  // then the updates (one launch); AdamW (optim.rs:205-233) over its runs in
+  // one launch.
+  RNN_TRY(rnn::muon_momentum_segs(ctx, net->G, net->M, net->opt_segs, net->n_mu, net->mu_max, 0.95f));
   std::vector<float*> mg;
   std::vector<int> mr, mc;
   for (int id : net->order) {
     const HostParam& p = net->R.ps[id];
     if (!is_muon(p)) continue;
-    const size_t o = net->off[id];
-    RNN_TRY(rnn::muon_momentum(ctx, net->G + o, net->M + o, (size_t)p.rows * p.cols, 0.95f));
-    mg.push_back(net->G + o);
+    mg.push_back(net->G + net->off[id]);
     mr.push_back(p.rows);
     mc.push_back(p.cols);
   }
   RNN_TRY(rnn::newton_schulz_grouped(ctx, (int)mg.size(), mg.data(), mr.data(), mc.data(), 3));
-  for (int id : net->order) {
-    const HostParam& p = net->R.ps[id];
-    if (!is_muon(p)) continue;
-    const size_t o = net->off[id];
-    RNN_TRY(rnn::muon_update(ctx, net->V + o, net->G + o, p.rows, p.cols, lr, wd, p.decay ? 1 : 0));
-  }
-  size_t run0 = 0, runlen = 0;
-  int rundecay = -1;
-  auto flush = [&]() -> int {
-    if (runlen)
-      RNN_TRY(rnn_adamw_step_dev(ctx, net->V + run0, net->G + run0, net->M + run0, net->V2 + run0, runlen, lr, wd,
-                                 rundecay, 0.9f, 0.999f, 1e-8f, net->opt_t));
-    runlen = 0;
-    return RNN_OK;
-  };
-  for (int id : net->order) {
-    const HostParam& p = net->R.ps[id];
-    const size_t o = net->off[id], len = p.v.size();
-    if (is_muon(p)) {
-      RNN_TRY(flush());
-      continue;
-    }
-    const int dec = p.decay ? 1 : 0;
-    if (runlen && (dec != rundecay || run0 + runlen != o)) RNN_TRY(flush());
-    if (!runlen) {
-      run0 = o;
-      rundecay = dec;
-    }
-    runlen += len;
-  }
-  RNN_TRY(flush());
+  RNN_TRY(rnn::muon_update_segs(ctx, net->V, net->G, net->opt_segs, net->n_mu, net->mu_max, lr, wd));
+  RNN_TRY(rnn::adamw_segs(ctx, net->V, net->G, net->M, net->V2, net->opt_segs + net->n_mu, net->n_ad, net->ad_max, lr,
+                          wd, 0.9f, 0.999f, 1e-8f, net->opt_t));
   net->opt_t++;
   return RNN_OK;
 }
@@ -1196,7 +1214,8 @@ extern "C" int rnn_rustvit_destroy(rnn_rustvit* net) {
   free_acts(net);
   rnn::eval_ws_free(net->eval);
   for (void* p : {(void*)net->V, (void*)net->G, (void*)net->M, (void*)net->V2, (void*)net->E, (void*)net->B,
-                  (void*)net->parent, (void*)net->st_x, (void*)net->st_tf, (void*)net->st_tc, (void*)net->st_hard})
+                  (void*)net->parent, (void*)net->st_x, (void*)net->st_tf, (void*)net->st_tc, (void*)net->st_hard,
+                  (void*)net->opt_segs})
     if (p) cudaFree(p);
   delete net;
   return RNN_OK;
