@@ -325,6 +325,9 @@ struct AttnDSProb {
     const float* pg = a.pin + prow;
     float* dsg = a.ds + prow;
     const int nch = a.tk / 32;
+    // request the whole P row into L2 first (one 128-byte line per chunk, no
+    // registers held), so that the chunk loads below wait on L2, not DRAM
+    for (int c = 0; c < nch; c++) asm volatile("prefetch.global.L2 [%0];" ::"l"(pg + c * 32));
     float dot = 0.0f;
 #pragma unroll 1
     for (int c = 0; c < nch; c++) {

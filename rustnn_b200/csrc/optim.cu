@@ -127,21 +127,66 @@ int newton_schulz(rnn_ctx* ctx, float* g, int rows, int cols, int steps, float* 
 
 // ---- Newton-Schulz over many matrices at once
 //
-// Matrices with one working shape (m = min(rows, cols), n = max) form a
-// group whose items sit back to back in scratch: one launch normalises all
-// of them, each of the three products per iteration is one batched GEMM
-// over the group, and the b A + c AA and a X + T combinations run over the
-// whole group's buffer.  Per item the arithmetic is that of newton_schulz
-// (the same f32 sum-of-squares slices, RED_BLOCKS per item, whose f64 sums
-// are combined by a warp instead of one thread) and the same products.
+// Per item the arithmetic is that of newton_schulz (the same f32
+// sum-of-squares slices, RED_BLOCKS per item, whose f64 sums are combined by
+// a warp instead of one thread) and the same products.
 
-// part[item][b] = f32 sum of squares over block b's slice of item's x
-__global__ void sumsq_items_kernel(const float* __restrict__ x, size_t n, double* __restrict__ part) {
+// Padded classes.  Every matrix's working shape (m, n) is rounded up to
+// (mc, nc), multiples of 128, and matrices of one class are batched; an
+// item's slot holds its X in the top-left m x n corner and zeros elsewhere.
+// The zeros are exact under every step (they add 0 to each real sum: the
+// real K blocks come first and the padding only appends zero blocks; A, AA
+// and T inherit zero rows and columns), so the real block is the same
+// Newton-Schulz iterate.  The gather into the slots, the normalisation and
+// the scatter back are one launch each over all matrices, the two
+// combinations one launch per iteration over all classes; only the GEMMs run
+// per class.  The sum of squares of item i walks its real elements in the
+// same slices as the unpadded form.
+struct NsItem {
+  float* g;           // the matrix (rows x cols), read and written in place
+  int rows, cols;     // as given; tall ones (rows > cols) are transposed
+  int m, n, mc, nc;   // working and padded shapes
+  size_t x;           // float offset of the item's slot in the X / T regions
+};
+
+__global__ void ns_gather_kernel(const NsItem* __restrict__ items, float* __restrict__ xall) {
+  const NsItem it = items[blockIdx.y];
+  const size_t slot = (size_t)it.mc * it.nc;
+  float* x = xall + it.x;
+  const bool tr = it.rows > it.cols;
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < slot; e += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(e / it.nc), c = (int)(e - (size_t)r * it.nc);
+    float v = 0.0f;
+    if (r < it.m && c < it.n) v = tr ? it.g[(size_t)c * it.cols + r] : it.g[(size_t)r * it.n + c];
+    x[e] = v;
+  }
+}
+__global__ void ns_scatter_kernel(const NsItem* __restrict__ items, const float* __restrict__ xall) {
+  const NsItem it = items[blockIdx.y];
+  const size_t real = (size_t)it.m * it.n;
+  const float* x = xall + it.x;
+  const bool tr = it.rows > it.cols;
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < real; e += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(e / it.n), c = (int)(e - (size_t)r * it.n);
+    const float v = x[(size_t)r * it.nc + c];
+    if (tr) it.g[(size_t)c * it.cols + r] = v;
+    else it.g[e] = v;
+  }
+}
+// part[item][b] = f32 sum of squares over block b's slice of the item's
+// real elements (row-major order of the m x n working matrix)
+__global__ void ns_sumsq_slots_kernel(const NsItem* __restrict__ items, const float* __restrict__ xall,
+                                      double* __restrict__ part) {
   __shared__ double sh[256];
-  const float* xi = x + (size_t)blockIdx.y * n;
+  const NsItem it = items[blockIdx.y];
+  const size_t real = (size_t)it.m * it.n;
+  const float* x = xall + it.x;
   float sf = 0.0f;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-    sf += xi[i] * xi[i];
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < real; e += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = e / it.n;
+    const float v = x[r * it.nc + (e - r * it.n)];
+    sf += v * v;
+  }
   sh[threadIdx.x] = (double)sf;
   __syncthreads();
   for (int k = 128; k > 0; k >>= 1) {
@@ -150,10 +195,10 @@ __global__ void sumsq_items_kernel(const float* __restrict__ x, size_t n, double
   }
   if (threadIdx.x == 0) part[(size_t)blockIdx.y * gridDim.x + blockIdx.x] = sh[0];
 }
-
-// x_item *= 1 / (sqrt(sum of its partials) + 1e-7)
-__global__ void ns_scale_items_kernel(float* __restrict__ x, size_t n, const double* __restrict__ part, int nb) {
+__global__ void ns_scale_slots_kernel(const NsItem* __restrict__ items, float* __restrict__ xall,
+                                      const double* __restrict__ part, int nb) {
   __shared__ float inv;
+  const NsItem it = items[blockIdx.y];
   if (threadIdx.x < 32) {  // lane l sums partials l, l+32, ..., then a fixed shuffle tree
     double s = 0.0;
     for (int b = threadIdx.x; b < nb; b += 32) s += part[(size_t)blockIdx.y * nb + b];
@@ -162,65 +207,95 @@ __global__ void ns_scale_items_kernel(float* __restrict__ x, size_t n, const dou
     if (threadIdx.x == 0) inv = 1.0f / (sqrtf((float)s) + 1e-7f);
   }
   __syncthreads();
-  float* xi = x + (size_t)blockIdx.y * n;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-    xi[i] *= inv;
+  float* x = xall + it.x;
+  const size_t slot = (size_t)it.mc * it.nc;
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < slot; e += (size_t)gridDim.x * blockDim.x)
+    x[e] *= inv;
 }
 
 int newton_schulz_grouped(rnn_ctx* ctx, int count, float* const* g, const int* rows, const int* cols, int steps) {
-  // groups by working shape, in first-appearance order
-  std::vector<std::pair<int, int>> shapes;
-  std::vector<std::vector<int>> members;
+  if (count <= 0) return RNN_OK;
+  // classes by padded working shape, in first-appearance order
+  struct Cls {
+    int mc, nc;
+    std::vector<int> members;
+    size_t x, a;  // float offsets of the class's first slot in the X / A regions
+  };
+  std::vector<Cls> cls;
+  auto up = [](int v) { return (v + 127) / 128 * 128; };
   for (int i = 0; i < count; i++) {
-    const int m = std::min(rows[i], cols[i]), n = std::max(rows[i], cols[i]);
-    size_t gi = 0;
-    while (gi < shapes.size() && shapes[gi] != std::make_pair(m, n)) gi++;
-    if (gi == shapes.size()) {
-      shapes.push_back({m, n});
-      members.emplace_back();
-    }
-    members[gi].push_back(i);
+    const int mc = up(std::min(rows[i], cols[i])), nc = up(std::max(rows[i], cols[i]));
+    size_t ci = 0;
+    while (ci < cls.size() && !(cls[ci].mc == mc && cls[ci].nc == nc)) ci++;
+    if (ci == cls.size()) cls.push_back({mc, nc, {}, 0, 0});
+    cls[ci].members.push_back(i);
   }
-  size_t need = 0;
-  for (size_t gi = 0; gi < shapes.size(); gi++) {
-    const size_t m = shapes[gi].first, n = shapes[gi].second, c = members[gi].size();
-    need = std::max(need, c * (2 * m * n + 2 * m * m) * 4 + c * RED_BLOCKS * 8 + 256);
-  }
-  RNN_TRY(ensure_aux(ctx, need));
-  for (size_t gi = 0; gi < shapes.size(); gi++) {
-    const int m = shapes[gi].first, n = shapes[gi].second, cnt = (int)members[gi].size();
-    const size_t mn = (size_t)m * n, mm = (size_t)m * m;
-    float* x = static_cast<float*>(ctx->aux);
-    float* t = x + cnt * mn;
-    float* a = t + cnt * mn;
-    float* aa = a + cnt * mm;
-    double* part = reinterpret_cast<double*>(
-        (reinterpret_cast<uintptr_t>(aa + cnt * mm) + 255) & ~static_cast<uintptr_t>(255));
-    for (int j = 0; j < cnt; j++) {
-      const int i = members[gi][j];
-      if (rows[i] > cols[i]) RNN_TRY(transpose(ctx, g[i], rows[i], cols[i], x + j * mn));
-      else RNN_CUDA(cudaMemcpyAsync(x + j * mn, g[i], mn * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  std::vector<NsItem> items;
+  size_t xf = 0, af = 0, slot_max = 0;
+  for (Cls& c : cls) {
+    c.x = xf;
+    c.a = af;
+    for (int i : c.members) {
+      NsItem it;
+      it.g = g[i];
+      it.rows = rows[i];
+      it.cols = cols[i];
+      it.m = std::min(rows[i], cols[i]);
+      it.n = std::max(rows[i], cols[i]);
+      it.mc = c.mc;
+      it.nc = c.nc;
+      it.x = xf;
+      items.push_back(it);
+      xf += (size_t)c.mc * c.nc;
+      af += (size_t)c.mc * c.mc;
+      slot_max = std::max(slot_max, (size_t)c.mc * c.nc);
+      RNN_RANGE(g[i], sizeof(float) * (size_t)rows[i] * cols[i]);
     }
-    sumsq_items_kernel<<<dim3(RED_BLOCKS, cnt), 256, 0, ctx->stream>>>(x, mn, part);
+  }
+  const int ni = (int)items.size();
+  // aux: X, T [xf], A, AA [af], partials [ni][RED_BLOCKS] (doubles), items
+  const size_t part_off = ((2 * xf + 2 * af) * 4 + 255) / 256 * 256;
+  const size_t items_off = part_off + (size_t)ni * RED_BLOCKS * 8;
+  RNN_TRY(ensure_aux(ctx, items_off + sizeof(NsItem) * ni + 64));
+  char* base = static_cast<char*>(ctx->aux);
+  float* xall = reinterpret_cast<float*>(base);
+  float* tall = xall + xf;
+  float* aall = tall + xf;
+  float* aaall = aall + af;
+  double* part = reinterpret_cast<double*>(base + part_off);
+  NsItem* ditems = reinterpret_cast<NsItem*>(base + items_off);
+  // (staged before cudaMemcpyAsync returns: `items` may go out of scope)
+  RNN_CUDA(cudaMemcpyAsync(ditems, items.data(), sizeof(NsItem) * ni, cudaMemcpyHostToDevice, ctx->stream));
+  const unsigned gx = std::max(1u, egrid(slot_max, ctx->num_sms) / 4);
+  ns_gather_kernel<<<dim3(gx, ni), 256, 0, ctx->stream>>>(ditems, xall);
+  RNN_CHECK_LAUNCH();
+  ns_sumsq_slots_kernel<<<dim3(RED_BLOCKS, ni), 256, 0, ctx->stream>>>(ditems, xall, part);
+  RNN_CHECK_LAUNCH();
+  ns_scale_slots_kernel<<<dim3(gx, ni), 256, 0, ctx->stream>>>(ditems, xall, part, RED_BLOCKS);
+  RNN_CHECK_LAUNCH();
+  for (int st = 0; st < steps; st++) {
+    for (const Cls& c : cls) {  // A = X X^T
+      const size_t mn = (size_t)c.mc * c.nc, mm = (size_t)c.mc * c.mc;
+      RNN_TRY(tc::gemm_batched_dev(ctx, (int)c.members.size(), c.mc, c.mc, c.nc, xall + c.x, mn, false, xall + c.x,
+                                   mn, true, aall + c.a, mm, false));
+    }
+    for (const Cls& c : cls) {  // AA = A A
+      const size_t mm = (size_t)c.mc * c.mc;
+      RNN_TRY(tc::gemm_batched_dev(ctx, (int)c.members.size(), c.mc, c.mc, c.mc, aall + c.a, mm, false, aall + c.a,
+                                   mm, false, aaall + c.a, mm, false));
+    }
+    ns_poly_kernel<<<egrid(af, ctx->num_sms), 256, 0, ctx->stream>>>(aall, aaall, af);
     RNN_CHECK_LAUNCH();
-    const unsigned gx = std::max(1u, egrid(mn, ctx->num_sms) / (unsigned)cnt);
-    ns_scale_items_kernel<<<dim3(gx, cnt), 256, 0, ctx->stream>>>(x, mn, part, RED_BLOCKS);
+    for (const Cls& c : cls) {  // T = B X
+      const size_t mn = (size_t)c.mc * c.nc, mm = (size_t)c.mc * c.mc;
+      RNN_TRY(tc::gemm_batched_dev(ctx, (int)c.members.size(), c.mc, c.nc, c.mc, aall + c.a, mm, false, xall + c.x,
+                                   mn, false, tall + c.x, mn, false));
+    }
+    ns_axpy_kernel<<<egrid(xf, ctx->num_sms), 256, 0, ctx->stream>>>(xall, tall, xf);
     RNN_CHECK_LAUNCH();
-    for (int st = 0; st < steps; st++) {
-      RNN_TRY(tc::gemm_batched_dev(ctx, cnt, m, m, n, x, mn, false, x, mn, true, a, mm, false));   // A = X X^T
-      RNN_TRY(tc::gemm_batched_dev(ctx, cnt, m, m, m, a, mm, false, a, mm, false, aa, mm, false)); // AA = A A
-      ns_poly_kernel<<<egrid(cnt * mm, ctx->num_sms), 256, 0, ctx->stream>>>(a, aa, cnt * mm);
-      RNN_CHECK_LAUNCH();
-      RNN_TRY(tc::gemm_batched_dev(ctx, cnt, m, n, m, a, mm, false, x, mn, false, t, mn, false));  // T = B X
-      ns_axpy_kernel<<<egrid(cnt * mn, ctx->num_sms), 256, 0, ctx->stream>>>(x, t, cnt * mn);
-      RNN_CHECK_LAUNCH();
-    }
-    for (int j = 0; j < cnt; j++) {
-      const int i = members[gi][j];
-      if (rows[i] > cols[i]) RNN_TRY(transpose(ctx, x + j * mn, m, n, g[i]));
-      else RNN_CUDA(cudaMemcpyAsync(g[i], x + j * mn, mn * 4, cudaMemcpyDeviceToDevice, ctx->stream));
-    }
   }
+  ns_scatter_kernel<<<dim3(gx, ni), 256, 0, ctx->stream>>>(ditems, xall);
+  RNN_CHECK_LAUNCH();
   return RNN_OK;
 }
 
