@@ -504,11 +504,55 @@ __global__ void splitk_reduce4_kernel(const float4* __restrict__ ws, float4* __r
   }
 }
 
+// Transposed form for many splits (the convolution weight gradients: 29
+// splits and more): a CTA of 1024 threads covers 8 rows x 32 columns, and
+// four thread groups sum four contiguous ranges of the splits (in order)
+// before group 0 adds the four range sums in order -- each thread's chain
+// of dependent loads is a quarter as long.  Deterministic.
+constexpr int SKR_ROWS = 8, SKR_GROUPS = 4;
+__global__ void __launch_bounds__(256 * SKR_GROUPS) splitk_reduce_t4_kernel(const float* __restrict__ ws,
+                                                                          float* __restrict__ out, int rows,
+                                                                          int cols, int splits, int acc) {
+  __shared__ float red[SKR_GROUPS][SKR_ROWS][33];
+  const int e = threadIdx.x & 255, q = threadIdx.x >> 8;
+  const int rr = e >> 5, cc = e & 31;
+  const int r = blockIdx.x * SKR_ROWS + rr, c = blockIdx.y * 32 + cc;
+  const size_t plane = (size_t)rows * cols;
+  const int per = (splits + SKR_GROUPS - 1) / SKR_GROUPS;
+  const int s0 = q * per, s1 = min(splits, s0 + per);
+  float s = 0.0f;
+  if (r < rows && c < cols) {
+    const float* p = ws + (size_t)r * cols + c;
+#pragma unroll 4
+    for (int sp = s0; sp < s1; sp++) s += __ldg(p + (size_t)sp * plane);
+  }
+  red[q][rr][cc] = s;
+  __syncthreads();
+  if (q == 0) {
+    // write out[c][r]: consecutive threads take consecutive rows of a column
+    const int wc = threadIdx.x >> 3, wr = threadIdx.x & 7;
+    const int orow = blockIdx.x * SKR_ROWS + wr, ocol = blockIdx.y * 32 + wc;
+    if (orow < rows && ocol < cols) {
+      float t = red[0][wr][wc];
+#pragma unroll
+      for (int g = 1; g < SKR_GROUPS; g++) t += red[g][wr][wc];
+      float* o = out + (size_t)ocol * rows + orow;
+      *o = acc ? *o + t : t;
+    }
+  }
+}
+
 int launch_splitk_reduce(rnn_ctx* ctx, const float* ws, float* out, int rows, int cols, int splits,
                          bool acc, bool transpose) {
   size_t total = (size_t)rows * cols;
   RNN_RANGE(ws, total * splits * sizeof(float));
   RNN_RANGE(out, total * sizeof(float));
+  if (transpose && splits >= 8) {
+    const dim3 grid((rows + SKR_ROWS - 1) / SKR_ROWS, (cols + 31) / 32);
+    splitk_reduce_t4_kernel<<<grid, 256 * SKR_GROUPS, 0, ctx->stream>>>(ws, out, rows, cols, splits, acc ? 1 : 0);
+    RNN_CHECK_LAUNCH();
+    return RNN_OK;
+  }
   if (!transpose && total % 4 == 0 && al16(ws) && al16(out)) {
     const size_t total4 = total / 4;
     const unsigned g4 = (unsigned)std::max<size_t>(1, std::min<size_t>((total4 + 255) / 256, (size_t)ctx->num_sms * 8));
