@@ -65,6 +65,73 @@ __global__ void __launch_bounds__(256) cs_partial4_kernel(const float4* __restri
   }
 }
 
+// One-launch form (float4 path): the CTAs of a column strip count
+// themselves in on a device counter after writing their partials; the last
+// one adds the strip's partials in slab order (8 warps: warp w takes slabs
+// w, w+8, ..., then the warps in order), adds into out and resets the
+// counter.  Which CTA finishes last varies, the order of the sums does not.
+constexpr int CS_COUNTER0 = 2, CS_COUNTERS = 14;  // ctx->counters slots 2 .. 15
+template <bool MUL>
+__global__ void __launch_bounds__(256) cs_fused4_kernel(const float4* __restrict__ a, const float4* __restrict__ m,
+                                                         int rows, int c4, float4* __restrict__ part,
+                                                         float4* __restrict__ out, unsigned* __restrict__ counters) {
+  __shared__ float4 red[8][32];
+  __shared__ bool last;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int j = blockIdx.x * 32 + lane;
+  const int r0 = blockIdx.y * CS_ROWS;
+  float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  if (j < c4) {
+#pragma unroll
+    for (int i = 0; i < CS_ROWS / 8; i++) {
+      const int r = r0 + w + 8 * i;
+      if (r < rows) {
+        float4 v = __ldg(a + (size_t)r * c4 + j);
+        if (MUL) {
+          const float4 q = __ldg(m + (size_t)r * c4 + j);
+          v.x *= q.x;
+          v.y *= q.y;
+          v.z *= q.z;
+          v.w *= q.w;
+        }
+        cs_add4(s, v);
+      }
+    }
+  }
+  red[w][lane] = s;
+  __syncthreads();
+  if (w == 0 && j < c4) {
+    float4 t = red[0][lane];
+#pragma unroll
+    for (int k = 1; k < 8; k++) cs_add4(t, red[k][lane]);
+    part[(size_t)blockIdx.y * c4 + j] = t;
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(&counters[blockIdx.x], 1u) == gridDim.y - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  const int nb = gridDim.y;
+  float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  if (j < c4)
+    for (int b = w; b < nb; b += 8) cs_add4(t, __ldcg(part + (size_t)b * c4 + j));
+  __syncthreads();
+  red[w][lane] = t;
+  __syncthreads();
+  if (w == 0) {
+    if (j < c4) {
+      float4 u = red[0][lane];
+#pragma unroll
+      for (int k = 1; k < 8; k++) cs_add4(u, red[k][lane]);
+      float4 o = out[j];
+      cs_add4(o, u);
+      out[j] = o;
+    }
+    if (lane == 0) counters[blockIdx.x] = 0u;
+  }
+}
+
 constexpr int CS_FINAL_WARPS = 32;
 
 __global__ void __launch_bounds__(CS_FINAL_WARPS * 32) cs_final4_kernel(const float4* __restrict__ part, int nb,
@@ -129,6 +196,22 @@ inline int colsum_final(rnn_ctx* ctx, const float* part, int nb, int c, float* o
 // out[j] += sum_r a[r][j] (* m[r][j]); part holds ceil(rows / CS_ROWS) x c floats
 inline int colsum_two_pass(rnn_ctx* ctx, const float* a, const float* m, int rows, int c, float* part, float* out) {
   const int nb = (rows + CS_ROWS - 1) / CS_ROWS;
+  if (c % 4 == 0 && cs_aligned(a) && (!m || cs_aligned(m)) && cs_aligned(part) && cs_aligned(out) &&
+      (c / 4 + 31) / 32 <= CS_COUNTERS) {
+    const int c4 = c / 4;
+    const dim3 grid((c4 + 31) / 32, nb);
+    const float4* a4 = reinterpret_cast<const float4*>(a);
+    const float4* m4 = reinterpret_cast<const float4*>(m);
+    float4* p4 = reinterpret_cast<float4*>(part);
+    float4* o4 = reinterpret_cast<float4*>(out);
+    unsigned* cnt = ctx->counters + CS_COUNTER0;
+    if (m)
+      cs_fused4_kernel<true><<<grid, 256, 0, ctx->stream>>>(a4, m4, rows, c4, p4, o4, cnt);
+    else
+      cs_fused4_kernel<false><<<grid, 256, 0, ctx->stream>>>(a4, m4, rows, c4, p4, o4, cnt);
+    RNN_CHECK_LAUNCH();
+    return RNN_OK;
+  }
   if (c % 4 == 0 && cs_aligned(a) && (!m || cs_aligned(m)) && cs_aligned(part)) {
     const int c4 = c / 4;
     const dim3 grid((c4 + 31) / 32, nb);

@@ -116,7 +116,7 @@ int ensure_pack(rnn_ctx* ctx, size_t bytes);
 int ensure_aux(rnn_ctx* ctx, size_t bytes);
 int ensure_statp(rnn_ctx* ctx, size_t bytes);
 // ctx->counters slots: 0 BatchNorm partial-sum kernels, 1 convolution
-// epilogue statistics
+// epilogue statistics, 2 .. 15 the one-launch column sums (colsum.cuh)
 constexpr int COUNTER_BN = 0, COUNTER_CONV_STATS = 1;
 
 // ---- CUDA-graph replay of a whole training step
