@@ -504,13 +504,12 @@ __global__ void attn_image_sum_kernel(const float* __restrict__ ds, int n, int p
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < per; e += gridDim.x * blockDim.x) {
     float s = 0.0f;
     int k = 0;
-    for (; k + 4 <= n; k += 4) {
-      const float a0 = __ldg(ds + (size_t)k * per + e), a1 = __ldg(ds + (size_t)(k + 1) * per + e);
-      const float a2 = __ldg(ds + (size_t)(k + 2) * per + e), a3 = __ldg(ds + (size_t)(k + 3) * per + e);
-      s += a0;
-      s += a1;
-      s += a2;
-      s += a3;
+    for (; k + 8 <= n; k += 8) {  // eight images' loads in flight, added in order
+      float a[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) a[u] = __ldg(ds + (size_t)(k + u) * per + e);
+#pragma unroll
+      for (int u = 0; u < 8; u++) s += a[u];
     }
     for (; k < n; k++) s += __ldg(ds + (size_t)k * per + e);
     dssum[e] = s;
