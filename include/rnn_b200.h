@@ -543,7 +543,13 @@ int rnn_make_batch_eval_dev(rnn_ctx *ctx, const uint8_t *images,
  * pad, flip, normalise, random erasing with probability `erase` of an
  * erase_side square of normal noise.  Image b draws from
  * Rng::new(seed ^ b * 0x9E3779B97F4A7C15) in the reference's order.
- * out [bs, 3, 32, 32], labels_out / coarse_out (nullable) [bs] u32. */
+ * out [bs, 3, 32, 32], labels_out / coarse_out (nullable) [bs] u32.
+ * The f32 logf / cosf / sinf results are the host C library's, as the
+ * reference's: the first call with erasing or RandAugment on a device builds
+ * two 64-MB Box-Muller tables there from the C library (kept until exit;
+ * make that call before any stream capture), and with RandAugment each call
+ * replays the images' RandAugment draws on the host for the rotations'
+ * cos / sin. */
 int rnn_make_batch_train_dev(rnn_ctx *ctx, const uint8_t *images,
                              const uint8_t *labels, const uint8_t *coarse,
                              size_t len, const uint32_t *idx, int bs, int pad,
