@@ -2,7 +2,7 @@
 // context's stream, and a standalone communicator for the data-parallel
 // gradient sum with failure detection.
 //
-// The reference is one process with host memory only (SURVEY: pool.rs is its
+// The reference is one process with host memory only (pool.rs is its
 // allocator, there is no collective), so none of these has a counterpart in
 // it; they are what a Rust host needs to keep the step's tensors resident on
 // the device and to run the batch-sharded step of train.rs:684-699 on several
