@@ -333,14 +333,15 @@ struct Cfg {
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
   static constexpr int EXTRA = EXTRA_;
   static_assert(EXTRA % 1024 == 0, "EXTRA keeps the barriers 8-byte and the ring 1024-byte aligned");
-  // Narrow tiles (BN <= 64) issue each 8-deep K step as two MMAs of width
-  // 2*BN over the stacked [B_hi; B_lo] image (the lo tile follows the hi
-  // tile in shared memory, so one descriptor covers both): columns [0, BN)
-  // collect A*B_hi = (hi+lo)*B_hi, columns [BN, 2BN) collect A*B_lo, and the
-  // epilogue adds the halves.  Two wide MMAs cost less than three narrow
-  // ones (a 128x64x8 tf32 MMA takes ~86 cycles, a 128x128x8 ~107, measured),
-  // and the fourth product lo*lo comes along for free.
-  static constexpr bool STACK = BN <= 64;
+  // 32-column tiles issue each 8-deep K step as two MMAs of width 2*BN over
+  // the stacked [B_hi; B_lo] image (the lo tile follows the hi tile in
+  // shared memory, so one descriptor covers both): columns [0, BN) collect
+  // A*B_hi = (hi+lo)*B_hi, columns [BN, 2BN) collect A*B_lo, and the
+  // epilogue adds the halves; the fourth product lo*lo comes along.  At 64
+  // columns the three plain MMAs measured faster once the halo kernels' A
+  // side stopped limiting them (64-channel halo fwd/dgrad 0.441 -> 0.419 ms;
+  // the stacked pair reads 4/3 as much B from shared memory per K step).
+  static constexpr bool STACK = BN <= 32;
   static constexpr int ACC_COLS = STACK ? 2 * BN : BN;  // columns per accumulator buffer
   // ATM: the A operand (hi and lo) lives in tensor memory: the producers
   // write it with tcgen05.st and the MMA reads it from there, so shared
