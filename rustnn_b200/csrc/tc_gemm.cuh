@@ -327,21 +327,26 @@ __device__ __forceinline__ void store_split(uint32_t hi_base, uint32_t lo_base, 
 
 // EXTRA: bytes of problem-owned shared memory after the ring (the halo
 // buffers of HALO problems); the ring gets what is left of the budget.
-template <int BN_, int EXTRA_ = 0, bool ATM_ = false>
+template <int BN_, int EXTRA_ = 0, bool ATM_ = false, bool STACKABLE_ = true>
 struct Cfg {
   static constexpr int BN = BN_;
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
   static constexpr int EXTRA = EXTRA_;
   static_assert(EXTRA % 1024 == 0, "EXTRA keeps the barriers 8-byte and the ring 1024-byte aligned");
-  // 32-column tiles issue each 8-deep K step as two MMAs of width 2*BN over
-  // the stacked [B_hi; B_lo] image (the lo tile follows the hi tile in
-  // shared memory, so one descriptor covers both): columns [0, BN) collect
-  // A*B_hi = (hi+lo)*B_hi, columns [BN, 2BN) collect A*B_lo, and the
-  // epilogue adds the halves; the fourth product lo*lo comes along.  At 64
-  // columns the three plain MMAs measured faster once the halo kernels' A
-  // side stopped limiting them (64-channel halo fwd/dgrad 0.441 -> 0.419 ms;
-  // the stacked pair reads 4/3 as much B from shared memory per K step).
-  static constexpr bool STACK = BN <= 32;
+  // Tiles of up to 64 columns issue each 8-deep K step as two MMAs: one of
+  // width 2*BN, A_hi over the stacked [B_hi; B_lo] image (the lo tile follows
+  // the hi tile in shared memory, so one descriptor covers both), and one of
+  // width BN, A_lo over B_hi.  Columns [0, BN) collect hi*B_hi + lo*B_hi,
+  // columns [BN, 2BN) hi*B_lo, and the epilogue adds the halves.  Two MMA
+  // instructions instead of three, and no more B read from shared memory
+  // than the three plain ones.  (An earlier form, lo and hi each over the
+  // whole stacked image, computed the unused lo*lo product and read a third
+  // more B; on the 64-channel halo kernels it measured 5 % slower than three
+  // plain MMAs; this form is 5 % faster than them: 0.419 -> 0.400 ms.)
+  // Problems whose row epilogue reads the accumulator rows themselves
+  // (attention) keep the plain form: stacking doubles their TMEM reads and
+  // they are epilogue-bound (dh-64 score kernel 0.0253 -> 0.0275 ms stacked).
+  static constexpr bool STACK = BN <= 64 && STACKABLE_;
   static constexpr int ACC_COLS = STACK ? 2 * BN : BN;  // columns per accumulator buffer
   // ATM: the A operand (hi and lo) lives in tensor memory: the producers
   // write it with tcgen05.st and the MMA reads it from there, so shared
@@ -542,7 +547,7 @@ struct prob_atm<P, std::void_t<decltype(P::A_TMEM)>> {
 // ------------------------------------------------------------------ kernel
 
 template <class Prob, int BN>
-using CfgOf = Cfg<BN, prob_extra_bn<Prob, BN>::value, prob_atm<Prob>::value>;
+using CfgOf = Cfg<BN, prob_extra_bn<Prob, BN>::value, prob_atm<Prob>::value, !prob_rowepi<Prob>::value>;
 
 // Column sums over the warp's 32 rows: v holds this lane's row; lane l
 // returns (sum, sum of squares) of column l.  Recursive halving: at each of
@@ -893,8 +898,8 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
               // A hi at columns [stage*64, +32), lo at [+32, +64); 8 columns per K step
               const uint32_t tah = tmem_base + C::A_COL0 + stage * 64 + j * 8, tal = tah + 32;
               if constexpr (C::STACK) {
-                mma_tf32_ta(d_tmem, tal, dbh, C::IDESC2, first);  // lo * [hi; lo]
-                mma_tf32_ta(d_tmem, tah, dbh, C::IDESC2, 1u);     // hi * [hi; lo]
+                mma_tf32_ta(d_tmem, tah, dbh, C::IDESC2, first);  // hi * [hi; lo]
+                mma_tf32_ta(d_tmem, tal, dbh, C::IDESC, 1u);      // lo * hi (first BN columns)
               } else {
                 mma_tf32_ta(d_tmem, tal, dbh, C::IDESC, first);  // lo * hi
                 mma_tf32_ta(d_tmem, tah, dbl, C::IDESC, 1u);     // hi * lo
@@ -903,8 +908,8 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
               (void)dah;
               (void)dal;
             } else if constexpr (C::STACK) {
-              mma_tf32(d_tmem, dal, dbh, C::IDESC2, first);  // lo * [hi; lo]
-              mma_tf32(d_tmem, dah, dbh, C::IDESC2, 1u);     // hi * [hi; lo]
+              mma_tf32(d_tmem, dah, dbh, C::IDESC2, first);  // hi * [hi; lo]
+              mma_tf32(d_tmem, dal, dbh, C::IDESC, 1u);      // lo * hi (first BN columns)
               (void)dbl;
             } else {
               mma_tf32(d_tmem, dal, dbh, C::IDESC, first);  // lo * hi
