@@ -39,9 +39,11 @@ static EncodeTiledFn encode_tiled_fn() {
 }
 
 // Tensor map of an NCHW f32 tensor [n][c][h][w] read in boxes of
-// box_w x box_h x box_c pixels of one image (zero fill outside).
+// box_w x box_h x box_c pixels of one image (zero fill outside); with
+// CU_TENSOR_MAP_SWIZZLE_128B (box_w = 32) the 16-byte chunk j of box row r
+// lands at chunk j ^ (r % 8) of its 128-byte row.
 static int encode_nchw_map(CUtensorMap* m, const float* t, int n, int c, int h, int w, int box_w, int box_h,
-                           int box_c) {
+                           int box_c, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
   EncodeTiledFn fn = encode_tiled_fn();
   RNN_REQUIRE(fn != nullptr, "conv: cuTensorMapEncodeTiled unavailable");
   const cuuint64_t dims[4] = {(cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)c, (cuuint64_t)n};
@@ -49,7 +51,7 @@ static int encode_nchw_map(CUtensorMap* m, const float* t, int n, int c, int h, 
   const cuuint32_t box[4] = {(cuuint32_t)box_w, (cuuint32_t)box_h, (cuuint32_t)box_c, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(t), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   RNN_REQUIRE(r == CUDA_SUCCESS, "conv: cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
   return RNN_OK;
@@ -605,7 +607,8 @@ struct HaloConv3x3 {
   };
   __device__ __forceinline__ void tile_begin(TS&, int, int, int) const {}
   static __device__ __forceinline__ void a_slot(int gt, int j, int& r, int& c) { r = gt; c = j; }
-  __device__ __forceinline__ void halo_issue(uint32_t halo, int buf, int mt, int cb, int ptid, int npt) const {
+  __device__ __forceinline__ void halo_issue(uint32_t halo, int buf, int mt, int kbs, int ptid, int npt) const {
+    const int cb = kbs / TAPS;  // 32-channel block
     const int hw = H * W;
     const int m0 = mt * BM;
     const int img = m0 / hw, oy0 = (m0 - img * hw) / W;
@@ -620,7 +623,8 @@ struct HaloConv3x3 {
       cp_async16(dst0 + (uint32_t)((c * CSTR + pos(r, xc * 4)) * 4), g, in ? 16u : 0u);
     }
   }
-  __device__ __forceinline__ void halo_tma(uint32_t halo, int buf, uint64_t* bar, int mt, int cb) const {
+  __device__ __forceinline__ void halo_tma(uint32_t halo, int buf, uint64_t* bar, int mt, int kbs) const {
+    const int cb = kbs / TAPS;  // 32-channel block
     const int hw = H * W;
     const int m0 = mt * BM;
     const int img = m0 / hw, oy0 = (m0 - img * hw) / W;
@@ -867,6 +871,19 @@ struct FastConvWgradPacked : FastConvWgrad<KS> {
   }
 };
 
+// Pixels 4q + kw - 1 .. 4q + kw + 2 of an image row whose pixels 4q .. 4q+3
+// are m, with `left` = pixel 4q - 1 and `right` = pixel 4q + 4 (zero past
+// the row ends): the kw-shifted window of a 3x3 wgrad row.  Selects, not
+// branches: the three kw rows of a (ci, kh) sit in adjacent lanes, so a
+// branch on kw would run all three paths one after another.
+__device__ __forceinline__ void kw_shift4(const float4 m, float left, float right, int kw, float* v) {
+  const bool k0 = kw == 0, k2 = kw == 2;
+  v[0] = k0 ? left : (k2 ? m.y : m.x);
+  v[1] = k0 ? m.x : (k2 ? m.z : m.y);
+  v[2] = k0 ? m.y : (k2 ? m.w : m.z);
+  v[3] = k0 ? m.z : (k2 ? right : m.w);
+}
+
 // wgrad of a 3x3/s1/p1 convolution over W in {8, 16, 32} pixel-wide images
 // (W*H a multiple of 32, so a K block is 32/W whole rows of one image) with
 // A in tensor memory: a producer thread owns one (ci, kh, kw) row and builds
@@ -915,14 +932,73 @@ struct FastConvWgradT : FastConvWgradPacked<3, BN> {
       const int px0 = (4 * q) % W;
       const float left = px0 > 0 ? c[q - (px0 > 0 ? 1 : 0)].w : 0.0f;       // pixel px0 - 1 of the row
       const float right = px0 + 4 < W ? c[q + (px0 + 4 < W ? 1 : 0)].x : 0.0f;  // pixel px0 + 4
-      const float4 m = c[q];
-      if (ts.kw == 1) {
-        v[4 * q] = m.x; v[4 * q + 1] = m.y; v[4 * q + 2] = m.z; v[4 * q + 3] = m.w;
-      } else if (ts.kw == 0) {
-        v[4 * q] = left; v[4 * q + 1] = m.x; v[4 * q + 2] = m.y; v[4 * q + 3] = m.z;
-      } else {
-        v[4 * q] = m.y; v[4 * q + 1] = m.z; v[4 * q + 2] = m.w; v[4 * q + 3] = right;
-      }
+      kw_shift4(c[q], left, right, ts.kw, &v[4 * q]);
+    }
+  }
+};
+
+// wgrad of a 3x3/s1/p1 convolution over 32-wide images (H a multiple of 8)
+// with the input rows staged by tensor copies.  K runs in groups of TAPS = 8
+// K blocks, 8 image rows of one image; one 4-D tensor copy per group brings
+// image rows oy0-1 .. oy0+9 of the (at most 16) channels a 128-row tile
+// touches into shared memory as [16 channels][11 rows][32 columns] of
+// 128-byte rows, 128-byte swizzled, zeros above and below the image and past
+// the last channel.  A producer thread owns one (ci, kh, kw) row, as in
+// FastConvWgradT, and reads its 32 pixels of a K block as eight 16-byte
+// shared loads, shifting by kw - 1 across neighbouring chunks.  Each input
+// row crosses L2 once per group instead of being fetched by every producer
+// warp per K block, and the producers no longer wait on global loads.
+template <int BN>
+struct FastConvWgradHalo : FastConvWgradPacked<3, BN> {
+  static constexpr bool A_TMEM = true;
+  static constexpr int W = 32;
+  static constexpr int TAPS = 8;  // image rows (K blocks) per halo group
+  // rows oy0-1 .. oy0+9 (the last one unused): with 11 rows per channel the
+  // lines one load phase reads, (c, kh..kh+2) and (c+1, 0..2), fall on
+  // distinct swizzle rows (line % 8); with 10, (c, 2) and (c+1, 0) collide
+  static constexpr int HROWS = TAPS + 3;
+  static constexpr int HCH = 16;  // channels a 128-row tile touches, at most
+  static constexpr int BUF_BYTES = HCH * HROWS * W * 4;
+  static_assert(BUF_BYTES % 1024 == 0, "swizzled buffers start on 1024-byte boundaries");
+  static constexpr int HALO_BYTES = 2 * BUF_BYTES;
+  static constexpr bool HALO_TMA = true;
+  CUtensorMap tmap;  // x as [n][cin][H][32], boxes of [16][HROWS][32], 128-byte swizzle
+  struct TS {
+    int line;  // 128-byte row of (channel - first channel of the tile, kh) in a buffer
+    int kw;
+    bool ok;
+  };
+  __device__ __forceinline__ void tile_begin(TS& ts, int m0, int, int gt) const {
+    const int row = m0 + gt;
+    ts.ok = row < this->M;
+    const int r = ts.ok ? row : m0;
+    const int ci = r / 9, kk = r - ci * 9, kh = kk / 3;
+    ts.kw = kk - kh * 3;
+    ts.line = (ci - m0 / 9) * HROWS + kh;
+  }
+  static __device__ __forceinline__ void a_slot(int gt, int j, int& r, int& c) { r = gt; c = j; }
+  __device__ __forceinline__ void halo_tma(uint32_t halo, int buf, uint64_t* bar, int mt, int kbs) const {
+    const int h = this->g.h;
+    const int img = kbs / h, oy0 = kbs - img * h;  // a K block is one image row
+    mbar_arrive_expect_tx(bar, (uint32_t)BUF_BYTES);
+    tma_load_4d(halo + (uint32_t)(buf * BUF_BYTES), &tmap, 0, oy0 - 1, (mt * BM) / 9, img, bar);
+  }
+  __device__ __forceinline__ void load_a_halo(uint32_t halo, int buf, const TS& ts, int tap, int,
+                                              float (&v)[32]) const {
+    const int line = ts.line + tap;
+    const uint32_t a = halo + (uint32_t)(buf * BUF_BYTES + line * 128);
+    float4 c[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) c[q] = ld_shared_v4(a + (uint32_t)((q ^ (line & 7)) << 4));
+    if (!ts.ok) {
+#pragma unroll
+      for (int q = 0; q < 8; q++) c[q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      const float left = q > 0 ? c[q > 0 ? q - 1 : 0].w : 0.0f;   // pixel 4q - 1
+      const float right = q < 7 ? c[q < 7 ? q + 1 : 7].x : 0.0f;  // pixel 4q + 4
+      kw_shift4(c[q], left, right, ts.kw, &v[4 * q]);
     }
   }
 };
@@ -1014,6 +1090,48 @@ static int wgrad_t(rnn_ctx* ctx, const float* x, const float* dy, float* dw, con
   p.x = x; p.dy = dy; p.dw = dw; p.ws = nullptr; p.g = g; p.M = M; p.N = N; p.K = K; p.splits = 1;
   RNN_TRY(wgrad_dy_image<BN>(ctx, p, g, N, K, dy, dy_packed));
   return WgradLauncher<BN>::run(ctx, p, splits);
+}
+
+// 32-wide 3x3 wgrads take the tensor-copy kernel when each split runs at
+// least WGRAD_HALO_MIN_KB K blocks (image rows); shorter splits pay more for
+// the first halo copy and the group barriers than the row loads cost
+// (measured, dY pack included, against FastConvWgradT with the branch-free
+// shift: 64 channels at batch 1024, 1,136 blocks per split, 0.678 -> 0.615
+// ms; 32 channels at batch 128, 88 blocks, 0.0494 -> 0.0507 ms, so the
+// short splits stay on the row loads).  RNN_WGRAD_HALO=0 keeps every call on
+// FastConvWgradT, =1 sends every eligible call to the tensor-copy kernel
+// (A/B runs).
+constexpr int WGRAD_HALO_MIN_KB = 512;
+static bool wgrad_halo_on(int kb_per_split) {
+  const char* v = getenv("RNN_WGRAD_HALO");
+  if (v && v[0]) return v[0] != '0';
+  return kb_per_split >= WGRAD_HALO_MIN_KB;
+}
+
+// The tensor-copy wgrad (FastConvWgradHalo): every split's K range is a
+// whole number of 8-row groups, so the split count from pick_splits is
+// rounded to that.
+template <int BN>
+static int wgrad_halo(rnn_ctx* ctx, const float* x, const float* dy, float* dw, const ConvGeom& g, int M, int N,
+                      int K, int splits, const float* dy_packed) {
+  using P = FastConvWgradHalo<BN>;
+  P p;
+  p.x = x; p.dy = dy; p.dw = dw; p.ws = nullptr; p.g = g; p.M = M; p.N = N; p.K = K; p.splits = 1;
+  RNN_TRY(encode_nchw_map(&p.tmap, x, g.n, g.cin, g.h, P::W, P::W, P::HROWS, P::HCH, CU_TENSOR_MAP_SWIZZLE_128B));
+  RNN_TRY(wgrad_dy_image<BN>(ctx, p, g, N, K, dy, dy_packed));
+  Sched s = make_sched(M, N, K, BN, splits);
+  s.kb_per_split = (s.kb_per_split + P::TAPS - 1) / P::TAPS * P::TAPS;
+  s.splits = (s.kblocks + s.kb_per_split - 1) / s.kb_per_split;
+  s.num_tiles = s.m_tiles * s.n_tiles * s.splits;
+  p.splits = s.splits;
+  if (s.splits > 1) {
+    RNN_TRY(ensure_ws(ctx, sizeof(float) * (size_t)s.splits * M * N));
+    p.ws = static_cast<float*>(ctx->ws);
+    RNN_RANGE(p.ws, sizeof(float) * (size_t)s.splits * M * N);
+  }
+  RNN_TRY(launch<BN>(ctx, p, s));
+  if (s.splits > 1) RNN_TRY(launch_splitk_reduce(ctx, p.ws, dw, M, N, s.splits, true, true));
+  return RNN_OK;
 }
 
 template <int W>
@@ -1372,6 +1490,14 @@ int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, in
     // accumulators fill it, they keep A in shared memory)
     if (k == 3 && stride == 1 && pad == 1 && (h * w) % 32 == 0 && bn <= WGRAD_T_MAX_BN &&
         (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+      if (w == 32 && h % FastConvWgradHalo<64>::TAPS == 0 && bn <= 128 &&
+          wgrad_halo_on(make_sched(M, N, K, bn, splits).kb_per_split)) {
+        switch (bn) {
+          case 32: return wgrad_halo<32>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
+          case 64: return wgrad_halo<64>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
+          default: return wgrad_halo<128>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
+        }
+      }
       if (w == 32) return wgrad_t_bn<32>(ctx, bn, x, dy, dw, g, M, N, K, splits, dy_packed);
       if (w == 16) return wgrad_t_bn<16>(ctx, bn, x, dy, dw, g, M, N, K, splits, dy_packed);
       if (w == 8) return wgrad_t_bn<8>(ctx, bn, x, dy, dw, g, M, N, K, splits, dy_packed);

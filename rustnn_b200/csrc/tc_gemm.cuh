@@ -110,6 +110,11 @@ __device__ __forceinline__ float ld_shared_f32(uint32_t addr) {
   asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
   return v;
 }
+__device__ __forceinline__ float4 ld_shared_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
@@ -458,15 +463,18 @@ struct ChunkProb : P {
 
 // Problems that stage a halo of the gathered operand in shared memory
 // declare HALO_BYTES (both buffers) and TAPS, and supply
-//   void halo_issue(uint32_t halo, int buf, int m_tile, int cb, int ptid, int npt) const;
-//        cp.async the halo of K-block group cb (TAPS consecutive K blocks)
-//        of row tile m_tile into buffer buf; producer thread ptid of npt
+//   void halo_issue(uint32_t halo, int buf, int m_tile, int kbs, int ptid, int npt) const;
+//        cp.async the halo of the K-block group that starts at K block kbs
+//        (TAPS consecutive K blocks) of row tile m_tile into buffer buf;
+//        producer thread ptid of npt
 //   void load_a_halo(uint32_t halo, int buf, const TS&, int tap, int gt, float (&v)[32]) const;
 // A HALO problem may set HALO_TMA: one producer thread then fills a halo
 // buffer with a tensor copy instead of every producer issuing cp.async,
-//   void halo_tma(uint32_t halo, int buf, uint64_t* bar, int m_tile, int cb) const;
+//   void halo_tma(uint32_t halo, int buf, uint64_t* bar, int m_tile, int kbs) const;
 //        arrive.expect_tx on bar and start the copy of buffer buf,
-// and the producers wait on that buffer's barrier before reading it.
+// and the producers wait on that buffer's barrier before reading it.  Under
+// split-K the launcher makes every split's K range a whole number of groups
+// (kb_per_split a multiple of TAPS); groups start at the split's first block.
 template <class P, class = void>
 struct prob_halo {
   static constexpr int value = 0;
@@ -657,18 +665,20 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
   if (warp < C::PRODUCER_WARPS) {
    if constexpr (HALO) {
     // ---------------------------------------------------- halo producers
-    // K runs in groups of TAPS blocks (one 32-channel block, every tap).
-    // All producer threads cp.async the halo of the next group into the
-    // spare buffer while the current one is read, and meet on halo_bar at
-    // every group boundary: it publishes the landed halo and releases the
-    // buffer the next prefetch overwrites.  Groups keep taking K blocks
-    // round-robin as below.  splits == 1 (the launcher guarantees it).
+    // Each tile's K range [kb0, kb1) runs in groups of TAPS blocks from kb0
+    // (the conv fwd/dgrad: one 32-channel block, every tap; the wgrad: TAPS
+    // image rows).  All producer threads fill the halo of the next group
+    // into the spare buffer while the current one is read, and meet on
+    // halo_bar at every group boundary: it publishes the landed halo and
+    // releases the buffer the next prefetch overwrites.  Groups keep taking
+    // K blocks round-robin as below.
     const int group = warp >> 2;
     const int gt = threadIdx.x & (GROUP_THREADS - 1);
     const int ptid = threadIdx.x;
     constexpr int NPT = C::PRODUCER_WARPS * 32;
     constexpr int TAPS = Prob::TAPS;
     auto mt_of = [&](int tile) { return (tile % tiles_mn) % sched.m_tiles; };
+    auto kb0_of = [&](int tile) { return (tile / tiles_mn) * sched.kb_per_split; };
     uint32_t it = 0, hc = 0;
     bool ok = true;
     // HALO_TMA: sequence numbers of the last halo copy started and the last
@@ -676,30 +686,36 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
     int tma_issued = -1, tma_waited = -1;
     if (blockIdx.x < sched.num_tiles) {
       if constexpr (HTMA) {
-        if (ptid == 0) prob.halo_tma(halo, 0, &halo_full[0], mt_of(blockIdx.x), 0);
+        if (ptid == 0) prob.halo_tma(halo, 0, &halo_full[0], mt_of(blockIdx.x), kb0_of(blockIdx.x));
         tma_issued = 0;
       } else {
-        prob.halo_issue(halo, 0, mt_of(blockIdx.x), 0, ptid, NPT);
+        prob.halo_issue(halo, 0, mt_of(blockIdx.x), kb0_of(blockIdx.x), ptid, NPT);
       }
     }
     if constexpr (!HTMA) cp_async_commit();
     for (int tile = blockIdx.x; tile < sched.num_tiles && ok; tile += gridDim.x) {
       const int mn = tile % tiles_mn;
       const int mt = mn % sched.m_tiles, nt = mn / sched.m_tiles;
+      const int kb0 = kb0_of(tile);
+      const int kb1 = kb0 + sched.kb_per_split < sched.kblocks ? kb0 + sched.kb_per_split : sched.kblocks;
       typename Prob::TS ts;
       prob.tile_begin(ts, mt * BM, nt * BN, gt);
-      for (int kb = 0; kb < sched.kblocks; kb++, it++) {
-        const int cb = kb / TAPS, tap = kb - cb * TAPS;
+      for (int kb = kb0; kb < kb1; kb++, it++) {
+        const int tap = (kb - kb0) % TAPS;
         if (tap == 0) {
           if constexpr (!HTMA) cp_async_wait_all();
           // every producer is done with the buffer the next copy overwrites
           mbar_arrive(halo_bar);
           if (!mbar_wait(halo_bar, hc & 1, abort_flag, dev_error)) { ok = false; break; }
-          int ntile = tile, ncb = cb + 1;
-          if (ncb * TAPS >= sched.kblocks) { ntile = tile + gridDim.x; ncb = 0; }
+          // the next group: the rest of this tile's K range, else the next tile's first
+          int ntile = tile, nkbs = kb + TAPS;
+          if (nkbs >= kb1) {
+            ntile = tile + gridDim.x;
+            nkbs = ntile < sched.num_tiles ? kb0_of(ntile) : 0;
+          }
           if constexpr (HTMA) {
             if (ntile < sched.num_tiles) {
-              if (ptid == 0) prob.halo_tma(halo, (hc + 1) & 1, &halo_full[(hc + 1) & 1], mt_of(ntile), ncb);
+              if (ptid == 0) prob.halo_tma(halo, (hc + 1) & 1, &halo_full[(hc + 1) & 1], mt_of(ntile), nkbs);
               tma_issued = (int)hc + 1;
             }
             // this group's halo (copy hc) has landed
@@ -707,7 +723,7 @@ __global__ void __launch_bounds__(CfgOf<Prob, BN>::THREADS, 1)
             tma_waited = (int)hc;
           } else {
             if (ntile < sched.num_tiles) {
-              prob.halo_issue(halo, (hc + 1) & 1, mt_of(ntile), ncb, ptid, NPT);
+              prob.halo_issue(halo, (hc + 1) & 1, mt_of(ntile), nkbs, ptid, NPT);
             }
             cp_async_commit();
           }

@@ -118,6 +118,8 @@ CONVS = [  # (n, cin, h, cout, k, stride, pad)
     (1, 32, 24, 32, 3, 1, 1),    # 24-pixel rows: not a halo width, per-pixel gather path
     (3, 64, 15, 64, 1, 2, 0),    # strided 1x1 dgrad over an odd input: last row/column hit
     (2, 32, 16, 64, 1, 3, 0),    # stride 3: two of every three rows/columns get no gradient
+    (2, 40, 32, 128, 3, 1, 1),   # 32-wide wgrad at 128 columns; 360 rows: a ragged last row tile
+    (2, 16, 32, 256, 3, 1, 1),   # 32-wide wgrad at 256 columns: the per-thread row loads
 ]
 
 
@@ -154,6 +156,24 @@ def test_conv_parity(ops, n, cin, h, cout, k, stride, pad):
     dw_ref = O.conv2d_wgrad(x, dy, n, cin, h, h, cout, k, stride, pad, dw=dw0.copy())
     dw = dev(dw0)
     ops.conv2d_wgrad(dev(x), dev(dy), n, cin, h, h, cout, k, stride, pad, dw=dw)
+    assert rel(host(dw), dw_ref) < TOL
+
+
+@pytest.mark.parametrize("n,cin,cout", [(8, 32, 32), (2, 3, 64), (64, 64, 64), (2, 40, 128), (5, 64, 64)])
+@pytest.mark.parametrize("halo", ["1", "0"])
+def test_conv_wgrad_32wide_both_kernels(ops, monkeypatch, n, cin, cout, halo):
+    """32-wide 3x3 wgrad through the tensor-copy kernel (8-row halo groups,
+    split-K in whole groups) and through the per-thread row loads, at sizes
+    where the default picks the latter."""
+    monkeypatch.setenv("RNN_WGRAD_HALO", halo)
+    h = 32
+    rng = O.Rng(300 + cin + cout + n)
+    x = rng.rand_vec(n * cin * h * h)
+    dy = rng.rand_vec(n * cout * h * h)
+    dw0 = rng.rand_vec(cout * cin * 9)
+    dw_ref = O.conv2d_wgrad(x, dy, n, cin, h, h, cout, 3, 1, 1, dw=dw0.copy())
+    dw = dev(dw0)
+    ops.conv2d_wgrad(dev(x), dev(dy), n, cin, h, h, cout, 3, 1, 1, dw=dw)
     assert rel(host(dw), dw_ref) < TOL
 
 
