@@ -937,34 +937,42 @@ struct FastConvWgradT : FastConvWgradPacked<3, BN> {
   }
 };
 
-// wgrad of a 3x3/s1/p1 convolution over 32-wide images (H a multiple of 8)
-// with the input rows staged by tensor copies.  K runs in groups of TAPS = 8
-// K blocks, 8 image rows of one image; one 4-D tensor copy per group brings
-// image rows oy0-1 .. oy0+9 of the (at most 16) channels a 128-row tile
-// touches into shared memory as [16 channels][11 rows][32 columns] of
-// 128-byte rows, 128-byte swizzled, zeros above and below the image and past
-// the last channel.  A producer thread owns one (ci, kh, kw) row, as in
-// FastConvWgradT, and reads its 32 pixels of a K block as eight 16-byte
-// shared loads, shifting by kw - 1 across neighbouring chunks.  Each input
-// row crosses L2 once per group instead of being fetched by every producer
-// warp per K block, and the producers no longer wait on global loads.
-template <int BN>
+// wgrad of a 3x3/s1/p1 convolution over 32- or 16-wide images with the
+// input rows staged by tensor copies.  A K block is R = 32/W image rows;
+// K runs in groups of TAPS = 8 K blocks, 8R rows of one image (H a multiple
+// of 8R); one 4-D tensor copy per group brings image rows oy0-1 ..
+// oy0+8R+1 of the (at most 16) channels a 128-row tile touches into shared
+// memory as [16 channels][HROWS rows][W columns] of W*4-byte lines,
+// swizzled over the line width (128-byte swizzle at W = 32, 64-byte at
+// W = 16), zeros above and below the image and past the last channel.  A
+// producer thread owns one (ci, kh, kw) row, as in FastConvWgradT, and
+// reads its 32 pixels of a K block as eight 16-byte shared loads, shifting
+// by kw - 1 across neighbouring chunks of each image row.  Each input row
+// crosses L2 once per group instead of being fetched by every producer warp
+// per K block, and the producers no longer wait on global loads.
+template <int BN, int W_ = 32>
 struct FastConvWgradHalo : FastConvWgradPacked<3, BN> {
   static constexpr bool A_TMEM = true;
-  static constexpr int W = 32;
-  static constexpr int TAPS = 8;  // image rows (K blocks) per halo group
-  // rows oy0-1 .. oy0+9 (the last one unused): with 11 rows per channel the
-  // lines one load phase reads, (c, kh..kh+2) and (c+1, 0..2), fall on
-  // distinct swizzle rows (line % 8); with 10, (c, 2) and (c+1, 0) collide
-  static constexpr int HROWS = TAPS + 3;
-  static constexpr int HCH = 16;  // channels a 128-row tile touches, at most
-  static constexpr int BUF_BYTES = HCH * HROWS * W * 4;
+  static constexpr int W = W_;
+  static_assert(W == 32 || W == 16, "tensor-copy wgrad widths");
+  static constexpr int R = 32 / W;            // image rows per K block
+  static constexpr int TAPS = 8;              // K blocks per halo group
+  static constexpr int LINE = W * 4;          // bytes per image row in a buffer
+  static constexpr int CPL = W / 4;           // 16-byte chunks per line
+  // Under either swizzle a line's chunks land on the banks that line % 8
+  // selects; the lines one load phase reads, (c, kh..kh+2) and
+  // (c+1, kh'..kh'+2), are all distinct mod 8 when HROWS % 8 is 3.
+  static constexpr int HROWS = (8 * R + 2 + 5) / 8 * 8 + 3;  // rows oy0-1 .. oy0+8R (+ unused)
+  static_assert(HROWS >= 8 * R + 2 && HROWS % 8 == 3, "halo rows");
+  static constexpr int SWM = W == 32 ? 7 : 3;  // swizzle: chunk ^= (byte offset >> 7) & SWM
+  static constexpr int HCH = 16;               // channels a 128-row tile touches, at most
+  static constexpr int BUF_BYTES = HCH * HROWS * LINE;
   static_assert(BUF_BYTES % 1024 == 0, "swizzled buffers start on 1024-byte boundaries");
   static constexpr int HALO_BYTES = 2 * BUF_BYTES;
   static constexpr bool HALO_TMA = true;
-  CUtensorMap tmap;  // x as [n][cin][H][32], boxes of [16][HROWS][32], 128-byte swizzle
+  CUtensorMap tmap;  // x as [n][cin][H][W], boxes of [16][HROWS][W], swizzled
   struct TS {
-    int line;  // 128-byte row of (channel - first channel of the tile, kh) in a buffer
+    int line;  // line of (channel - first channel of the tile, kh) in a buffer
     int kw;
     bool ok;
   };
@@ -978,26 +986,29 @@ struct FastConvWgradHalo : FastConvWgradPacked<3, BN> {
   }
   static __device__ __forceinline__ void a_slot(int gt, int j, int& r, int& c) { r = gt; c = j; }
   __device__ __forceinline__ void halo_tma(uint32_t halo, int buf, uint64_t* bar, int mt, int kbs) const {
-    const int h = this->g.h;
-    const int img = kbs / h, oy0 = kbs - img * h;  // a K block is one image row
+    const int kbi = this->g.h / R;  // K blocks per image
+    const int img = kbs / kbi, oy0 = (kbs - img * kbi) * R;
     mbar_arrive_expect_tx(bar, (uint32_t)BUF_BYTES);
     tma_load_4d(halo + (uint32_t)(buf * BUF_BYTES), &tmap, 0, oy0 - 1, (mt * BM) / 9, img, bar);
   }
   __device__ __forceinline__ void load_a_halo(uint32_t halo, int buf, const TS& ts, int tap, int,
                                               float (&v)[32]) const {
-    const int line = ts.line + tap;
-    const uint32_t a = halo + (uint32_t)(buf * BUF_BYTES + line * 128);
+    const uint32_t base = halo + (uint32_t)(buf * BUF_BYTES);
     float4 c[8];
 #pragma unroll
-    for (int q = 0; q < 8; q++) c[q] = ld_shared_v4(a + (uint32_t)((q ^ (line & 7)) << 4));
+    for (int q = 0; q < 8; q++) {
+      const uint32_t off = (uint32_t)((ts.line + R * tap + q / CPL) * LINE + (q % CPL) * 16);
+      c[q] = ld_shared_v4(base + (off ^ (((off >> 7) & SWM) << 4)));
+    }
     if (!ts.ok) {
 #pragma unroll
       for (int q = 0; q < 8; q++) c[q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
 #pragma unroll
     for (int q = 0; q < 8; q++) {
-      const float left = q > 0 ? c[q > 0 ? q - 1 : 0].w : 0.0f;   // pixel 4q - 1
-      const float right = q < 7 ? c[q < 7 ? q + 1 : 7].x : 0.0f;  // pixel 4q + 4
+      const int cq = q % CPL;  // chunk within its image row
+      const float left = cq > 0 ? c[q > 0 ? q - 1 : 0].w : 0.0f;          // pixel 4cq - 1 of the row
+      const float right = cq < CPL - 1 ? c[q < 7 ? q + 1 : 7].x : 0.0f;  // pixel 4cq + 4
       kw_shift4(c[q], left, right, ts.kw, &v[4 * q]);
     }
   }
@@ -1092,7 +1103,7 @@ static int wgrad_t(rnn_ctx* ctx, const float* x, const float* dy, float* dw, con
   return WgradLauncher<BN>::run(ctx, p, splits);
 }
 
-// 32-wide 3x3 wgrads take the tensor-copy kernel when each split runs at
+// 32- and 16-wide 3x3 wgrads take the tensor-copy kernel when each split runs at
 // least WGRAD_HALO_MIN_KB K blocks (image rows); shorter splits pay more for
 // the first halo copy and the group barriers than the row loads cost
 // (measured, dY pack included, against FastConvWgradT with the branch-free
@@ -1111,13 +1122,14 @@ static bool wgrad_halo_on(int kb_per_split) {
 // The tensor-copy wgrad (FastConvWgradHalo): every split's K range is a
 // whole number of 8-row groups, so the split count from pick_splits is
 // rounded to that.
-template <int BN>
+template <int BN, int W>
 static int wgrad_halo(rnn_ctx* ctx, const float* x, const float* dy, float* dw, const ConvGeom& g, int M, int N,
                       int K, int splits, const float* dy_packed) {
-  using P = FastConvWgradHalo<BN>;
+  using P = FastConvWgradHalo<BN, W>;
   P p;
   p.x = x; p.dy = dy; p.dw = dw; p.ws = nullptr; p.g = g; p.M = M; p.N = N; p.K = K; p.splits = 1;
-  RNN_TRY(encode_nchw_map(&p.tmap, x, g.n, g.cin, g.h, P::W, P::W, P::HROWS, P::HCH, CU_TENSOR_MAP_SWIZZLE_128B));
+  RNN_TRY(encode_nchw_map(&p.tmap, x, g.n, g.cin, g.h, P::W, P::W, P::HROWS, P::HCH,
+                          W == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B));
   RNN_TRY(wgrad_dy_image<BN>(ctx, p, g, N, K, dy, dy_packed));
   Sched s = make_sched(M, N, K, BN, splits);
   s.kb_per_split = (s.kb_per_split + P::TAPS - 1) / P::TAPS * P::TAPS;
@@ -1490,12 +1502,20 @@ int conv_wgrad(rnn_ctx* ctx, const float* x, const float* dy, int n, int cin, in
     // accumulators fill it, they keep A in shared memory)
     if (k == 3 && stride == 1 && pad == 1 && (h * w) % 32 == 0 && bn <= WGRAD_T_MAX_BN &&
         (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
-      if (w == 32 && h % FastConvWgradHalo<64>::TAPS == 0 && bn <= 128 &&
+      // tensor-copy staging: groups of 8 K blocks (8 * 32/w rows) within one image
+      if ((w == 32 || w == 16) && h % (8 * (32 / w)) == 0 && bn <= 128 &&
           wgrad_halo_on(make_sched(M, N, K, bn, splits).kb_per_split)) {
+        if (w == 32) {
+          switch (bn) {
+            case 32: return wgrad_halo<32, 32>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
+            case 64: return wgrad_halo<64, 32>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
+            default: return wgrad_halo<128, 32>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
+          }
+        }
         switch (bn) {
-          case 32: return wgrad_halo<32>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
-          case 64: return wgrad_halo<64>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
-          default: return wgrad_halo<128>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
+          case 32: return wgrad_halo<32, 16>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
+          case 64: return wgrad_halo<64, 16>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
+          default: return wgrad_halo<128, 16>(ctx, x, dy, dw, g, M, N, K, splits, dy_packed);
         }
       }
       if (w == 32) return wgrad_t_bn<32>(ctx, bn, x, dy, dw, g, M, N, K, splits, dy_packed);

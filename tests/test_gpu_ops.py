@@ -159,14 +159,15 @@ def test_conv_parity(ops, n, cin, h, cout, k, stride, pad):
     assert rel(host(dw), dw_ref) < TOL
 
 
-@pytest.mark.parametrize("n,cin,cout", [(8, 32, 32), (2, 3, 64), (64, 64, 64), (2, 40, 128), (5, 64, 64)])
+@pytest.mark.parametrize("n,cin,h,cout", [(8, 32, 32, 32), (2, 3, 32, 64), (64, 64, 32, 64), (2, 40, 32, 128),
+                                          (5, 64, 32, 64), (4, 64, 16, 128), (3, 40, 16, 64), (2, 128, 16, 128),
+                                          (6, 16, 16, 32)])
 @pytest.mark.parametrize("halo", ["1", "0"])
-def test_conv_wgrad_32wide_both_kernels(ops, monkeypatch, n, cin, cout, halo):
-    """32-wide 3x3 wgrad through the tensor-copy kernel (8-row halo groups,
-    split-K in whole groups) and through the per-thread row loads, at sizes
-    where the default picks the latter."""
+def test_conv_wgrad_both_kernels(ops, monkeypatch, n, cin, h, cout, halo):
+    """32- and 16-wide 3x3 wgrad through the tensor-copy kernel (halo groups
+    of 8 K blocks, split-K in whole groups) and through the per-thread row
+    loads, at sizes where the default picks the latter."""
     monkeypatch.setenv("RNN_WGRAD_HALO", halo)
-    h = 32
     rng = O.Rng(300 + cin + cout + n)
     x = rng.rand_vec(n * cin * h * h)
     dy = rng.rand_vec(n * cout * h * h)
