@@ -515,6 +515,16 @@ int rnn_rustvit_train_step_dev(rnn_rustvit *net, const float *x,
                                const uint32_t *hard, const uint32_t *hardc,
                                int n, float lr, float wd, float clip, float ema,
                                uint64_t drop_seed, float *stats);
+/* Data-parallel Trainer::step.  No counterpart in the reference, whose
+ * step (train.rs:346-387) runs in one process.  comm (borrowed, from
+ * rnn_comm_init on the network's device; NULL detaches) makes every later
+ * train step of this network one rank of a batch-sharded step: each rank
+ * passes its own equal shard (and its own drop_seed); after the forward the
+ * BatchNorm running statistics are averaged over the ranks, after the
+ * backward the flat gradient is (before clip_), so clip_, the optimiser and
+ * the EMA run identically on every rank.  BatchNorm batch statistics stay
+ * per rank; the loss and accuracy in stats are the rank's own shard's. */
+int rnn_rustvit_dp_attach(rnn_rustvit *net, rnn_comm *comm);
 /* Host tier of the step: the batch comes from host memory. */
 int rnn_rustvit_train_step(rnn_rustvit *net, const float *x, const float *tf,
                            const float *tc, const uint32_t *hard,

@@ -167,6 +167,7 @@ extern "C" {
     pub fn rnn_rustvit_forward_dev(net: *mut RnnRustvit, x: *const f32, n: c_int, train: c_int, drop_seed: u64, logits: *mut f32, coarse: *mut f32, e1: *mut f32, e2: *mut f32, h1: *mut f32, h2: *mut f32, feat: *mut f32) -> c_int;
     pub fn rnn_rustvit_backward_dev(net: *mut RnnRustvit, dlogits: *const f32, dcoarse: *const f32, de1: *const f32, de2: *const f32, dh1: *const f32, dh2: *const f32, dhfinal: *const f32) -> c_int;
     pub fn rnn_rustvit_train_step_dev(net: *mut RnnRustvit, x: *const f32, tf: *const f32, tc: *const f32, hard: *const u32, hardc: *const u32, n: c_int, lr: f32, wd: f32, clip: f32, ema: f32, drop_seed: u64, stats: *mut f32) -> c_int;
+    pub fn rnn_rustvit_dp_attach(net: *mut RnnRustvit, comm: *mut RnnComm) -> c_int;
     pub fn rnn_rustvit_train_step(net: *mut RnnRustvit, x: *const f32, tf: *const f32, tc: *const f32, hard: *const u32, hardc: *const u32, n: c_int, lr: f32, wd: f32, clip: f32, ema: f32, drop_seed: u64, stats: *mut f32) -> c_int;
     pub fn rnn_make_batch_eval_dev(ctx: *mut RnnCtx, images: *const u8, labels: *const u8, len: usize, start: usize, bs: c_int, flip: c_int, out: *mut f32, labels_out: *mut u32) -> c_int;
     pub fn rnn_make_batch_train_dev(ctx: *mut RnnCtx, images: *const u8, labels: *const u8, coarse: *const u8, len: usize, idx: *const u32, bs: c_int, pad: c_int, ra_mag: f32, ra_n: c_int, erase: f32, erase_side: c_int, seed: u64, out: *mut f32, labels_out: *mut u32, coarse_out: *mut u32) -> c_int;

@@ -165,6 +165,7 @@ SIGS = {
     "rnn_rustvit_backward_dev": [VIT, FP, FP, FP, FP, FP, FP, FP],
     "rnn_rustvit_train_step_dev": [VIT, FP, FP, FP, FP, FP, I, F, F, F, F, U64, FP],
     "rnn_rustvit_train_step": [VIT, FP, FP, FP, FP, FP, I, F, F, F, F, U64, FP],
+    "rnn_rustvit_dp_attach": [VIT, P],
     "rnn_make_batch_eval_dev": [CTX, FP, FP, Z, Z, I, I, FP, FP],
     "rnn_make_batch_train_dev": [CTX, FP, FP, FP, Z, FP, I, I, F, I, F, I, U64, FP, FP, FP],
     "rnn_mix_batch_dev": [CTX, FP, I, F, F, F, FP, FP, FP],

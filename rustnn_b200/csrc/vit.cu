@@ -290,6 +290,8 @@ struct rnn_rustvit {
   // running statistics (stem_bn, c1, c2, tok_bn: for_each_buffer order)
   float* B = nullptr;
   size_t nb = 0;
+  // data-parallel step (rnn_rustvit_dp_attach): borrowed communicator or null
+  rnn_comm* comm = nullptr;
   // layers
   ConvL stem, memconv, tokconv;
   BNL stem_bn, tok_bn;
@@ -1134,8 +1136,15 @@ static int train_step(rnn_rustvit* net, const float* x, const float* tf, const f
                       const uint32_t* hardc, int n, float lr, float wd, float clip, float ema, uint64_t seed,
                       float* stats) {
   RNN_TRY(forward(net, x, n, true, seed));
+  // data-parallel: every rank leaves the forward with the mean of the
+  // ranks' updated running statistics, so the buffers stay identical
+  if (net->comm) RNN_TRY(rnn_allreduce_grads(net->ctx, net->comm, net->B, net->nb, 1));
   RNN_TRY(build_loss(net, tf, tc, hard, hardc, n));
   RNN_TRY(backward(net, net->g_logits, net->g_coarse, net->g_e1, net->g_e2, net->g_h1, net->g_h2, nullptr));
+  // data-parallel: the mean of the ranks' shard gradients (equal shards: the
+  // gradient of the mean loss over the whole batch) before clip_ and the
+  // optimiser, which then run identically on every rank
+  if (net->comm) RNN_TRY(rnn_allreduce_grads(net->ctx, net->comm, net->G, net->np, 1));
   if (clip > 0.0f) RNN_TRY(rnn_clip_dev(net->ctx, net->G, net->np, clip, net->clip_norm));
   RNN_TRY(step_all(net, lr, wd));
   if (ema > 0.0f) RNN_TRY(ema_update(net, ema));
@@ -1218,6 +1227,12 @@ extern "C" int rnn_rustvit_destroy(rnn_rustvit* net) {
                   (void*)net->opt_segs})
     if (p) cudaFree(p);
   delete net;
+  return RNN_OK;
+}
+
+extern "C" int rnn_rustvit_dp_attach(rnn_rustvit* net, rnn_comm* comm) {
+  RNN_REQUIRE(net, "rustvit_dp_attach: null network");
+  net->comm = comm;
   return RNN_OK;
 }
 

@@ -169,6 +169,14 @@ class RustViT:
         call("rnn_rustvit_backward_dev", self.h, _ptr(g["logits"]), _ptr(g["coarse"]), _ptr(g.get("e1")),
              _ptr(g.get("e2")), _ptr(g.get("h1")), _ptr(g.get("h2")), _ptr(g.get("hfinal")))
 
+    def dp_attach(self, comm):
+        """Makes later train steps one rank of a batch-sharded step over
+        comm (a ``dp.Comm`` on this network's device; None detaches): the
+        gradient and the BatchNorm running statistics are averaged over the
+        ranks inside the step.  The network keeps a borrowed reference."""
+        self._comm = comm
+        call("rnn_rustvit_dp_attach", self.h, comm.h if comm is not None else None)
+
     def train_step(self, x, tf, tc, hard, hardc, lr=6e-4, wd=0.06, clip=1.0, ema=0.9998, drop_seed=0,
                    stats=True):
         """Trainer::step on device inputs; returns (total loss, ce, correct),
