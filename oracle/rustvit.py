@@ -909,6 +909,50 @@ class Trainer:
         return total, ce, correct
 
 
+def dp_step(trainers, shards, lr, wd, seeds):
+    """One batch-sharded Trainer::step over len(trainers) ranks, the
+    semantics of rnn_rustvit_dp_attach (no counterpart in the reference,
+    whose step, train.rs:346-387, runs in one process).  Every trainer holds
+    a network built from the same seed; rank r runs forward, build_loss and
+    backward on shards[r] = (x, labels, n) with drop seed seeds[r] (its
+    BatchNorm layers on its own batch statistics); then the ranks' BatchNorm
+    running statistics and gradients are replaced by their mean (f32 sum in
+    rank order, then the division by the rank count), and every rank runs
+    clip_, Optim::step_all and Ema::update as Trainer.step does.  Returns
+    each rank's (total, ce, correct)."""
+    world = len(trainers)
+    stats = []
+    for tr, (x, labels, n), seed in zip(trainers, shards, seeds):
+        net = tr.net
+        tf, tc, coarse = targets(labels, net.head.parent, net.nc, tr.lc)
+        net.drop_seed = seed
+        out = net.forward(x, n, True)
+        g, total, ce, correct = build_loss(out, tf, tc, labels, coarse, tr.lc, net.nf, net.nc, n)
+        net.backward(g)
+        stats.append((total, ce, correct))
+
+    def mean(arrays):
+        acc = arrays[0].astype(F32).copy()
+        for a in arrays[1:]:
+            acc = (acc + a).astype(F32)
+        return (acc / F32(world)).astype(F32)
+
+    gmean = mean([tr.net.G for tr in trainers])
+    bufs = [list(tr.net.buffers()) for tr in trainers]
+    bmean = [mean([b[i] for b in bufs]) for i in range(len(bufs[0]))]
+    for tr, b in zip(trainers, bufs):
+        net = tr.net
+        net.G[:] = gmean
+        for dst, src in zip(b, bmean):
+            dst[:] = src
+        if tr.clip > 0.0:
+            _L().orc_clip(net.G, net.G.size, tr.clip)
+        tr.opt.step_all(net.plist, lr, wd)
+        if tr.ema is not None:
+            tr.ema.update(net.V)
+    return stats
+
+
 def eval_vit(net: RustViT, images, labels, batch, tta):
     """eval::vit (eval.rs:47-66) over a u8 CHW dataset: the exits are off, each
     batch runs forward with train false, and with tta its logits are averaged

@@ -7,7 +7,9 @@ On one GPU a one-rank communicator must leave the step bit-identical to the
 plain step (the averages are identities).  On two GPUs the ranks, fed
 different shards and drop seeds, must end every step with bit-identical
 parameters, moments, EMA and buffers, different from what either shard
-alone produces.  The two-rank case is skipped when fewer GPUs are visible.
+alone produces, and within 1e-4 (relative Frobenius) of the CPU oracle's
+restatement of the sharded step (oracle.rustvit.dp_step).  The two-rank
+case is skipped when fewer GPUs are visible.
 """
 import multiprocessing as mp
 import os
@@ -16,6 +18,7 @@ import numpy as np
 import pytest
 
 from oracle import oracle as O
+from oracle import rustvit as RV
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -23,6 +26,14 @@ pytestmark = pytest.mark.gpu
 TINY = dict(width=4, cmid=6, dim=8, heads=2, depth3=2, dim4=12, heads4=2, depth4=1, mem_at=[1], droppath=0.2,
             img=16)
 TINY_PARENT = np.array([0, 0, 1, 1, 2, 2], np.uint32)
+TOL = 1e-4
+
+
+def rel(got, want):
+    got = np.asarray(got, np.float64).ravel()
+    want = np.asarray(want, np.float64).ravel()
+    den = np.linalg.norm(want)
+    return float(np.linalg.norm(got - want) / (den if den > 0 else 1.0))
 
 
 def _gpus():
@@ -125,3 +136,15 @@ def test_two_ranks_end_each_step_identical():
     # the shards differ, so the shared parameters are neither rank's own
     assert not np.array_equal(out[0][0][0], out[0][1])
     assert not np.array_equal(out[0][0][0], out[1][1])
+    # the oracle's sharded step on the same shards and seeds
+    trs = [RV.Trainer(RV.RustViT(RV.Cfg(**TINY), TINY_PARENT, 3, 8)) for _ in range(2)]
+    for step in range(2):
+        shards = []
+        for r in range(2):
+            x, labels = _shard(r, 3, step)
+            shards.append((x, labels, 3))
+        RV.dp_step(trs, shards, 6e-4, 0.06, [50 + 7 * r + step for r in range(2)])
+    o = trs[0]
+    want = (o.net.V, o.net.M, o.net.V2, o.ema.w, o.net.buffer_vec())
+    for name, got, w in zip(("params", "m", "v2", "ema", "buffers"), out[0][0], want):
+        assert rel(got, w) < TOL, name

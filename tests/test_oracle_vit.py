@@ -191,3 +191,46 @@ def test_trainer_step_runs():
     moved = np.abs(net.V - v0) > 0
     assert moved.mean() > 0.9
     assert not np.any(net.G)  # the optimiser zeroes every gradient
+
+
+TINY = dict(width=4, cmid=6, dim=8, heads=2, depth3=2, dim4=12, heads4=2, depth4=1, mem_at=[1], droppath=0.2,
+            img=16)
+TINY_PARENT = np.array([0, 0, 1, 1, 2, 2], np.uint32)
+
+
+def _tiny_shard(rank, n, step):
+    rng = O.Rng(1000 + 17 * rank + step)
+    x = rng.rand_vec(n * 3 * 16 * 16)
+    labels = np.array([rng.below(6) for _ in range(n)], np.uint32)
+    return x, labels, n
+
+
+def test_dp_step_one_rank_is_the_trainer_step():
+    """The batch-sharded step's restatement (rnn_rustvit_dp_attach's
+    semantics) at one rank is Trainer.step, bit for bit."""
+    a = RV.Trainer(RV.RustViT(RV.Cfg(**TINY), TINY_PARENT, 3, 8))
+    b = RV.Trainer(RV.RustViT(RV.Cfg(**TINY), TINY_PARENT, 3, 8))
+    for step in range(2):
+        x, labels, n = _tiny_shard(0, 3, step)
+        sa = RV.dp_step([a], [(x, labels, n)], 6e-4, 0.06, [50 + step])
+        sb = b.step(x, labels, n, 6e-4, 0.06, 50 + step)
+        assert sa == [sb]
+        for u, v in ((a.net.V, b.net.V), (a.net.M, b.net.M), (a.net.V2, b.net.V2), (a.ema.w, b.ema.w),
+                     (a.net.buffer_vec(), b.net.buffer_vec())):
+            assert np.array_equal(u, v)
+
+
+def test_dp_step_two_ranks_share_one_update():
+    """Two ranks on different shards: identical parameters, moments, EMA and
+    buffers after each step, and neither equals the step on its shard alone."""
+    ranks = [RV.Trainer(RV.RustViT(RV.Cfg(**TINY), TINY_PARENT, 3, 8)) for _ in range(2)]
+    alone = RV.Trainer(RV.RustViT(RV.Cfg(**TINY), TINY_PARENT, 3, 8))
+    for step in range(2):
+        shards = [_tiny_shard(r, 3, step) for r in range(2)]
+        RV.dp_step(ranks, shards, 6e-4, 0.06, [50 + 7 * r + step for r in range(2)])
+        alone.step(*shards[0][:2], 3, 6e-4, 0.06, 50 + step)
+        r0, r1 = ranks[0].net, ranks[1].net
+        assert np.array_equal(r0.V, r1.V) and np.array_equal(r0.M, r1.M)
+        assert np.array_equal(r0.buffer_vec(), r1.buffer_vec())
+        assert np.array_equal(ranks[0].ema.w, ranks[1].ema.w)
+    assert not np.array_equal(ranks[0].net.V, alone.net.V)
